@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""bench.py -- tpt-spark hot path on B200: batch-1 decode tok/s and prefill tok/s at the
+Llama-3-8B-shape Q4_K_M configuration ("C5"), plus the Q4_K GEMV
+HBM GB/s of configs[0] ("C1").
+
+One JSON line on rank 0.  A "step" is one decode token (one forward pass of the whole model
+at batch 1).  Inputs: a seeded random-init model of the C5 shape written as a GGUF file
+(weights N(0, 0.02), norm gains 1.0 -- no checkpoint exists here) and uniform random prompt
+ids.  The 4.9 GB of weights is far larger than the 126 MB L2, so no L2 flush is needed
+between steps.
+
+  value         decode tok/s, CUDA events over K chained decode graphs (device argmax feeds
+                the next step), max over ranks
+  e2e           the same metric through the C ABI with host buffers (tptc_decode: token id
+                and position copied in, argmax copied out, every step)
+  roofline      decode step vs measured HBM bandwidth (weights + fp16 KV read per token)
+  gemv_c1       C1 Q4_K 4096x4096 GEMV, rotating through 64 weight copies (> 4x L2)
+  prefill       prefill tok/s of the prompt (device time)
+  cpu_baseline  the CPU oracle (restated candle path) on the box's host cores, bounded sample
+
+--impl reference times the CPU oracle on the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    except Exception:
+        return dict(PEAKS_FALLBACK, src="fallback")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=512)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c5_llama8b_q4km")
+    ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default: the config's)")
+    ap.add_argument("--model-dir", default=os.environ.get("TPTC_MODEL_DIR", os.path.join(tempfile.gettempdir(), "tptc_models")))
+    ap.add_argument("--e2e-steps", type=int, default=128)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+PROMPT_LEN = {"c2_llama1b_q4km": 128, "c3_mistral7b_q8_0": 2048, "c4_phi3mini_f16": 1024, "c5_llama8b_q4km": 8192}
+DECODE_LEN = {"c2_llama1b_q4km": 256, "c3_mistral7b_q8_0": 512, "c4_phi3mini_f16": 256, "c5_llama8b_q4km": 1024}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class Dist:
+    """gloo process group for the benchmark's own plumbing (barriers, max over ranks)."""
+
+    def __init__(self):
+        self.rank, self.world, self.local = dist_env()
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def model_file(cfg, model_dir, seed, dist):
+    from tpt_spark_b200 import synth
+
+    os.makedirs(model_dir, exist_ok=True)
+    path = os.path.join(model_dir, f"{cfg.name}_s{seed}.gguf")
+    if dist.local == 0 and not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        synth.write_gguf(tmp, cfg, seed=seed)
+        os.replace(tmp, path)
+    dist.barrier()
+    return path
+
+
+class Clocks:
+    """nvidia-smi samples (200 ms) during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        self.out.flush()
+        rows = []
+        try:
+            for line in open(self.out.name):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def decode_bytes(cfg, kv_len_mean):
+    """Algorithmic HBM bytes of one decode step: every weight matrix once (token_embd: one row
+    unless it is also the output projection), norm gains, and the fp16 K and V of the
+    kv_len positions attended to."""
+    from tpt_spark_b200 import synth
+
+    tot = 0
+    for name, kind, ne in cfg.tensors():
+        n = ne[0] * (ne[1] if len(ne) > 1 else 1)
+        b = synth.type_bytes(cfg.type_of(kind), n)
+        if kind == "token_embd":
+            tot += b if cfg.tied else b // ne[1]
+        else:
+            tot += b
+    tot += int(2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * kv_len_mean)
+    return tot
+
+
+def gemv_c1(torch):
+    """C1: Q4_K [4096 x 4096] GEMV, x ~ N(0,1) quantised to Q8_K inside the kernel."""
+    from tpt_spark_b200 import synth
+    from tpt_spark_b200.kernels import Matrix
+
+    C = synth.GEMV_C1
+    N, K = C["N"], C["K"]
+    copies = 64  # 64 x 9.4 MB = 604 MB > 4x the 126 MB L2
+    w = synth.normal(4242, N * K, C["w_std"])
+    raw = synth.encode(C["type"], w)
+    mats = []
+    for i in range(copies):
+        mats.append(Matrix(C["type"], raw, N, K))
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for m in mats[:8]:
+        m.gemv(x, y, st)
+    torch.cuda.synchronize()
+    iters = 640
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        mats[i % copies].gemv(x, y, st)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / iters
+    algo = mats[0].nbytes + K * 4 + N * 4  # 9,469,952 B: weights + x + y
+    for m in mats:
+        m.close()
+    return algo, us
+
+
+def cpu_baseline(path, cfg, max_seconds=25.0, prompt_len=8):
+    """The oracle (restated candle path) on all host cores: a short prompt, then timed decode
+    steps until max_seconds of CPU work.  Returns (tok/s, steps, cores, sample text)."""
+    from oracle import oracle as O
+
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    m = O.Model(path, max_seq=prompt_len + 64)
+    prompt = list(range(1, prompt_len + 1))
+    lg = m.forward(prompt, 0)
+    tok = O.argmax(lg)
+    pos, n = prompt_len, 0
+    t0 = time.perf_counter()
+    while True:
+        lg = m.forward([tok], pos)
+        tok = O.argmax(lg)
+        pos += 1
+        n += 1
+        el = time.perf_counter() - t0
+        if el > max_seconds or n >= 60:
+            break
+    m.close()
+    sample = (f"{n} greedy decode steps of the full {cfg.name} model after a {prompt_len}-token prompt "
+              f"(kv_len {prompt_len + 1}..{prompt_len + n}), {cores} OpenMP threads")
+    return n / el, n, cores, sample
+
+
+def run_reference(args, dist):
+    from tpt_spark_b200 import synth
+
+    cfg = synth.CONFIGS[args.workload]
+    if dist.rank != 0:
+        return
+    path = model_file(cfg, args.model_dir, args.seed, _Solo())
+    tps, n, cores, sample = cpu_baseline(path, cfg, max_seconds=max(20.0, 2.0 * (args.steps + args.warmup) / 60.0))
+    line = {"metric": "decode tok/s (bs=1)", "value": round(tps, 4), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": n, "warmup": 0, "ms_per_step": round(1000.0 / tps, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": cfg.name, "batch": 1, "decode_tokens": DECODE_LEN[cfg.name]},
+            "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+class _Solo:
+    rank, world, local = 0, 1, 0
+
+    def barrier(self):
+        pass
+
+
+def run_ours(args, dist):
+    import numpy as np
+    import torch
+
+    from tpt_spark_b200 import synth
+    from tpt_spark_b200.engine import CudaEngine
+
+    cfg = synth.CONFIGS[args.workload]
+    torch.cuda.set_device(dist.local)
+    path = model_file(cfg, args.model_dir, args.seed, dist)
+    P = args.prompt if args.prompt is not None else PROMPT_LEN[cfg.name]
+    ctx_len = cfg.context_length
+    eng = CudaEngine(dist.local)
+    info = eng.load(path)
+    rng = np.random.default_rng(1234 + args.seed)
+    prompt = rng.integers(0, cfg.vocab, P).tolist()
+
+    # prefill (device time)
+    eng.kv_reset()
+    lg = eng.prefill(prompt)
+    prefill_ms = eng.last_device_ms()
+    tok = int(np.argmax(lg))
+
+    # decode: warm-up then K timed steps; the window past the prompt is reused when the
+    # context would overflow (the cache is truncated back to the prompt)
+    def run_steps(n, tok):
+        ms = 0.0
+        kv_sum = 0.0
+        done = 0
+        while done < n:
+            room = ctx_len - eng.kv_len()
+            if room <= 0:
+                eng.kv_truncate(P)
+                room = ctx_len - P
+            k = min(n - done, room)
+            kv0 = eng.kv_len()
+            out = eng.decode_greedy(tok, kv0, k)
+            ms += eng.last_device_ms()
+            kv_sum += k * (kv0 + 1 + kv0 + k) / 2.0
+            tok = out[-1]
+            done += k
+        return ms, tok, kv_sum / max(n, 1)
+
+    _, tok, _ = run_steps(args.warmup, tok)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(dist.local) as clk:
+        ms, tok, kv_mean = run_steps(args.steps, tok)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(ms)
+    tps = args.steps / (ms / 1000.0)
+
+    # end to end through the C ABI with host buffers
+    e2e_steps = min(args.e2e_steps, args.steps)
+    eng.kv_truncate(P)
+    pos = P
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        tok = eng.decode(tok, pos, want_logits=False)
+        pos += 1
+    e2e_s = dist.max(time.perf_counter() - t0)
+    e2e_tps = e2e_steps / e2e_s
+
+    pk = peaks()
+    step_bytes = decode_bytes(cfg, kv_mean)
+    ms_step = ms / args.steps
+    achieved = step_bytes / (ms_step / 1000.0) / 1e9
+    gemv_bytes, gemv_us = gemv_c1(torch)
+    gemv_gbs = gemv_bytes / (gemv_us * 1e-6) / 1e9
+    launches_per_step = 5 * cfg.n_layers + 3
+
+    line = {
+        "metric": "decode tok/s (bs=1)", "value": round(tps * dist.world, 3), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "weak" if dist.world > 1 else "strong", "vs_baseline": None, "dtype": "q4_k/q6_k x q8_k int8-dot, f32 accum",
+        "data": "synthetic (seeded random-init GGUF, random prompt ids)",
+        "config": {"workload": cfg.name, "batch": 1, "prompt_tokens": P, "decode_kv_len_mean": round(kv_mean, 1),
+                   "parallelism": "replica" if dist.world > 1 else "single", "l2": "inputs larger than L2 (4.9 GB weights)"},
+        "e2e": {"value": round(e2e_tps * dist.world, 3), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "hbm", "kernel": "decode step (163 launches, CUDA graph)",
+                     "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "algorithmic_bytes": step_bytes, "peak_src": pk["src"]},
+        "gemv_c1": {"bound": "hbm", "kernel": "gemv_kernel Q4_K 4096x4096 (C1)", "us": round(gemv_us, 3),
+                    "achieved": round(gemv_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                    "frac": round(gemv_gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": gemv_bytes},
+        "prefill": {"tokens": P, "ms": round(prefill_ms, 3), "tok_s": round(P / (prefill_ms / 1000.0), 1)},
+        "clocks": clk.summary(),
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    eng.close()
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        v, n, cores, sample = cpu_baseline(path, cfg)
+        line["cpu_baseline"] = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        rank, world, _ = dist_env()
+        if rank == 0:
+            run_reference(args, _Solo())
+        return
+    dist = Dist()
+    try:
+        run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * tptc.h -- C ABI of the B200 (sm_100a) engine for tpt-spark's GGUF Llama/Mistral path.
+ *
+ * The engine replaces the reference's wgpu engine (src-tauri/src/engine/wgpu_engine.rs,
+ * wgpu_loader.rs, wgpu_kvcache.rs, wgpu_ops.rs and the WGSL kernels in shaders/) behind the
+ * LlmEngine trait (src-tauri/src/engine/mod.rs:62-82).  A Rust `engine/cuda_engine.rs`
+ * binds these functions through `extern "C"`; Python binds them through ctypes.
+ *
+ * Conventions
+ *   - Every function that can fail returns int: TPTC_OK (0) or a negative TPTC_ERR_*.
+ *     tptc_last_error(ctx) gives the message of the last failure on that context
+ *     (the anyhow::Error text the Rust side surfaces, commands.rs:59-62,291).
+ *   - The caller owns every host pointer; the library owns all device memory it
+ *     allocates.  Kernel-level test entry points take DEVICE pointers owned by the caller.
+ *   - One host thread drives one context at a time (the reference serialises engine calls
+ *     through EngineHandle = Arc<tokio::Mutex<..>>, engine/mod.rs:95).  Tensor parallelism
+ *     uses one context per GPU, one thread or process per rank.
+ *   - `stream` arguments are cudaStream_t passed as void* (NULL = legacy default stream).
+ */
+#ifndef TPTC_H
+#define TPTC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(TPTC_BUILD)
+#define TPTC_API __attribute__((visibility("default")))
+#else
+#define TPTC_API
+#endif
+
+#define TPTC_OK 0
+#define TPTC_ERR_ARG (-1)         /* invalid argument / shape */
+#define TPTC_ERR_CUDA (-2)        /* CUDA runtime error */
+#define TPTC_ERR_IO (-3)          /* file open / read / mmap failure */
+#define TPTC_ERR_FORMAT (-4)      /* malformed or truncated GGUF */
+#define TPTC_ERR_UNSUPPORTED (-5) /* architecture, tensor type or shape not supported */
+#define TPTC_ERR_STATE (-6)       /* call not valid in the current state (e.g. no model) */
+#define TPTC_ERR_NCCL (-7)        /* NCCL failure */
+#define TPTC_ERR_OOM (-8)         /* device allocation failed or over the configured cap */
+#define TPTC_ERR_CANCELLED (-9)   /* the token callback asked to stop */
+#define TPTC_ERR_TIMEOUT (-10)    /* a bounded device-side wait gave up */
+
+/* GGML tensor type ids (GGUF tensor_info.type). */
+#define TPTC_TYPE_F32 0
+#define TPTC_TYPE_F16 1
+#define TPTC_TYPE_Q8_0 8
+#define TPTC_TYPE_Q4_K 12
+#define TPTC_TYPE_Q6_K 14
+
+typedef struct tptc_ctx tptc_ctx;
+typedef struct tptc_matrix tptc_matrix;
+
+/* ModelInfo (engine/mod.rs:85-92) plus the GgufMeta fields the forward pass uses
+ * (engine/wgpu_loader.rs:41-67). */
+typedef struct {
+    char name[256];
+    char path[1024];
+    uint64_t size_bytes;      /* bytes of tensor data uploaded (wgpu_loader.rs total_bytes) */
+    char backend[64];         /* "cuda-sm100a" or "cuda-sm100a-tpN" */
+    char architecture[32];
+    uint32_t context_length, n_layers, n_heads, n_kv_heads, head_dim, dim, ffn, vocab;
+    float rope_freq_base, rope_scale, rms_eps;
+    uint32_t tied_embeddings;
+    uint32_t tp_rank, tp_size;
+    uint64_t device_bytes;    /* device memory held by this context */
+} tptc_model_info;
+
+/* InferenceParams (engine/mod.rs:35-46) minus the prompt text: the caller tokenises
+ * (tokenizer.json beside the .gguf, wgpu_engine.rs:892-906) and passes ids. */
+typedef struct {
+    uint32_t max_tokens;
+    float temperature;        /* <= 0: greedy (LogitsProcessor with temperature None) */
+    float top_p;              /* >= 1: no nucleus filter */
+    float repeat_penalty;     /* 1: off (candle_engine.rs:87-101) */
+    uint64_t seed;            /* sampling seed (the reference uses LogitsProcessor::new(42, ..)) */
+    int64_t eos_token_id;     /* < 0: never stop on a token (find_eos_token, :908-913) */
+} tptc_infer_params;
+
+/* Called once per generated token with done=0, then once with done=1 (token 0), also on
+ * cancellation -- the TokenEvent protocol of wgpu_engine.rs:297-300,332.  Return non-zero
+ * to cancel; tptc_infer then emits done=1 and returns TPTC_ERR_CANCELLED. */
+typedef int (*tptc_token_cb)(uint32_t token, int done, void* user);
+/* on_progress(done, total) after each tensor upload (wgpu_loader.rs:185). */
+typedef void (*tptc_progress_cb)(uint32_t done, uint32_t total, void* user);
+
+/* ------------------------------------------------------------------ lifecycle */
+
+/* Replaces WgpuEngine::new + GpuContext::try_init (wgpu_engine.rs:52-66,
+ * wgpu_context.rs:22-97).  device: CUDA ordinal.  tp_size 1: single GPU (nccl_uid NULL).
+ * tp_size > 1: nccl_uid points at the 128-byte ncclUniqueId rank 0 made with
+ * tptc_nccl_unique_id and shared with the other ranks. */
+TPTC_API int tptc_create(int device, int tp_rank, int tp_size, const void* nccl_uid, tptc_ctx** out);
+TPTC_API int tptc_nccl_unique_id(void* out128);
+TPTC_API void tptc_destroy(tptc_ctx* ctx);
+TPTC_API const char* tptc_last_error(const tptc_ctx* ctx);
+/* Library version string and the number of CUDA devices (0 without a GPU). */
+TPTC_API const char* tptc_version(void);
+TPTC_API int tptc_device_count(void);
+
+/* LlmEngine::load (mod.rs:66-70) -> load_gguf_to_vram (wgpu_loader.rs:87-201): mmap the
+ * file, parse GGUF v3, check bounds, stream every tensor through pinned staging with
+ * cudaMemcpyAsync, repack to the device layout, build the KV cache and rope table. */
+TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user);
+/* LlmEngine::unload / is_loaded / model_info (mod.rs:71-73, wgpu_engine.rs:126-147). */
+TPTC_API int tptc_unload(tptc_ctx* ctx);
+TPTC_API int tptc_is_loaded(const tptc_ctx* ctx);
+TPTC_API int tptc_get_model_info(const tptc_ctx* ctx, tptc_model_info* out);
+
+/* ------------------------------------------------------------ forward pass */
+
+/* KvCache::reset (wgpu_kvcache.rs:55-58). */
+TPTC_API int tptc_kv_reset(tptc_ctx* ctx);
+/* KvCache::common_prefix_len against the token ids resident in the cache
+ * (wgpu_kvcache.rs:63-69); returns the length (>= 0) or an error. */
+TPTC_API int tptc_kv_prefix_len(const tptc_ctx* ctx, const uint32_t* ids, int n);
+/* Keep only the first n positions of the KV cache (n <= tptc_kv_len): rewinds a turn. */
+TPTC_API int tptc_kv_truncate(tptc_ctx* ctx, int n);
+/* Number of positions resident in the KV cache. */
+TPTC_API int tptc_kv_len(const tptc_ctx* ctx);
+/* The comparison KvCache::common_prefix_len performs (wgpu_kvcache.rs:63-69), on two id
+ * sequences; host-only, needs no device. */
+TPTC_API int tptc_common_prefix_len(const uint32_t* cached, int n_cached, const uint32_t* ids, int n);
+
+/* Batched prefill of ids[0..n) at positions start_pos.. (replaces the per-token prefill
+ * loop of wgpu_engine.rs:252-261 and candle's forward(&input, 0), candle_engine.rs:272-281).
+ * start_pos must equal tptc_kv_len().  last_logits (host, [vocab] f32) may be NULL. */
+TPTC_API int tptc_prefill(tptc_ctx* ctx, const uint32_t* ids, int n, int start_pos, float* last_logits);
+/* One decode step of token `id` at position `pos` (run_forward_pass, wgpu_engine.rs:339-490).
+ * logits (host, [vocab] f32) and argmax (host) may each be NULL. */
+TPTC_API int tptc_decode(tptc_ctx* ctx, uint32_t id, int pos, float* logits, uint32_t* argmax);
+/* n greedy steps chained on the device: the argmax of each step is the next step's token,
+ * starting from `id` at `pos`; out_ids (host, n entries) receives the n argmax tokens. */
+TPTC_API int tptc_decode_greedy(tptc_ctx* ctx, uint32_t id, int pos, int n, uint32_t* out_ids);
+
+/* LlmEngine::infer (mod.rs:76-81, gpu_infer wgpu_engine.rs:165-334) over token ids:
+ * truncation to context_length - max_tokens, prefix reuse, batched prefill, repeat
+ * penalty, greedy or temperature/top-p sampling, EOS / max_tokens / context stops, and
+ * the on_token protocol above. */
+TPTC_API int tptc_infer(tptc_ctx* ctx, const uint32_t* prompt, int n, const tptc_infer_params* params,
+                        tptc_token_cb on_token, void* user);
+/* Device time (CUDA events on the context's stream) of the last tptc_prefill or
+ * tptc_decode_greedy call, in milliseconds. */
+TPTC_API int tptc_last_device_ms(const tptc_ctx* ctx, double* ms);
+/* Wall-clock phases of the last tptc_infer call in milliseconds (wgpu_engine.rs:320-330). */
+TPTC_API int tptc_last_timing(const tptc_ctx* ctx, double* prefill_ms, double* decode_ms, int* n_prompt,
+                              int* n_generated);
+
+/* ------------------------------------------------ kernel-level entry points */
+/* Device pointers owned by the caller.  These expose each hot-path kernel for parity tests
+ * and microbenchmarks; the forward pass uses the same kernels. */
+
+/* Dequantise n elements of raw GGUF blocks (dequant_q4k/q6k/q8/f16.wgsl) to f32. */
+TPTC_API int tptc_dequant(int ggml_type, const void* d_blocks, int64_t n, float* d_out, void* stream);
+/* Q8_K activation blocks (292 B each: f32 d, int8 qs[256], int16 bsums[16]) of x[k]. */
+TPTC_API int tptc_quant_q8k(const float* d_x, int64_t k, void* d_out, void* stream);
+/* Q8_0 activation blocks (34 B each: f16 d, int8 qs[32]) of x[k]. */
+TPTC_API int tptc_quant_q80(const float* d_x, int64_t k, void* d_out, void* stream);
+
+/* A weight matrix [N out x K in] in the device layout the forward pass uses, made from raw
+ * GGUF bytes (host or device pointer; `raw_on_device` says which). */
+TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_device, int N, int K,
+                                tptc_matrix** out);
+TPTC_API void tptc_matrix_destroy(tptc_matrix* m);
+/* Bytes the matrix occupies on the device (the algorithmic bytes of one GEMV over it). */
+TPTC_API int64_t tptc_matrix_bytes(const tptc_matrix* m);
+/* y[N] = W . x with candle QMatMul semantics (x quantised to Q8_K / Q8_0 inside the
+ * kernel; F16 in f32) -- gemm.wgsl + dequant_*.wgsl fused. */
+TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void* stream);
+/* Per (row, super-block) integer sums of the same kernel: isum = sum_j sc_j*dot_j,
+ * msum = sum_j m_j*bsum_j (Q4_K; 0 otherwise); [N, K/256] for k-quants, [N, K/32] Q8_0. */
+TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TPTC_H */

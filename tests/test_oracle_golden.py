@@ -1,0 +1,154 @@
+"""The CPU oracle against gguf-py's block formats (committed golden fixtures) and
+candle's documented arithmetic (properties).  CPU only."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "blocks.npz"))
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("name,t,be", [("q4k", O.Q4_K, 256), ("q6k", O.Q6_K, 256), ("q80", O.Q8_0, 32),
+                                       ("f16", O.F16, 1)])
+def test_dequant_matches_gguf_py_bitwise(name, t, be):
+    ref = GOLD[f"{name}_f32"]
+    got = O.dequant(t, GOLD[f"{name}_raw"], ref.size)
+    np.testing.assert_array_equal(bits(got), bits(ref))
+
+
+def test_q80_quant_matches_gguf_py():
+    x = GOLD["q80_x"]
+    np.testing.assert_array_equal(O.quant_q80(x), GOLD["q80_q"])
+
+
+def test_f16_conversions_match_numpy():
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.standard_normal(20000).astype(np.float32) * 10.0 ** rng.integers(-9, 5, 20000),
+                        np.array([65504, 65519.99, 65520, 1e-8, 2.98e-8, 5.96e-8, -0.0, np.inf, -np.inf], np.float32)])
+    x = x.astype(np.float32)
+    lib = O.lib()
+    got = np.array([lib.or_f2h(float(v)) for v in x], np.uint16)
+    np.testing.assert_array_equal(got, x.astype(np.float16).view(np.uint16))
+    h = np.arange(0, 65536, dtype=np.uint16)
+    h = h[(h & 0x7C00) != 0x7C00]  # finite halves
+    back = np.array([lib.or_h2f(int(v)) for v in h], np.float32)
+    np.testing.assert_array_equal(bits(back), bits(h.view(np.float16).astype(np.float32)))
+
+
+def test_q8k_properties():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal(256 * 8).astype(np.float32)
+    x[256:512] = 0.0
+    x[512 + 17] = -50.0  # negative extreme -> scale sign flips
+    q = O.quant_q8k(x)
+    assert q[1]["d"] == 0 and not q[1]["qs"].any()
+    for b in range(8):
+        blk = x[b * 256:(b + 1) * 256]
+        if not blk.any():
+            continue
+        amax_i = int(np.argmax(np.abs(blk)))
+        iscale = np.float32(-128.0) / blk[amax_i]
+        assert q[b]["qs"][amax_i] == -128
+        np.testing.assert_array_equal(q[b]["bsums"], q[b]["qs"].reshape(16, 16).astype(np.int32).sum(1))
+        assert q[b]["d"] == np.float32(1.0) / iscale
+        # round half away from zero of iscale*x, capped at 127
+        v = np.float32(iscale) * blk
+        r = np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))
+        np.testing.assert_array_equal(q[b]["qs"], np.minimum(r, 127).astype(np.int8))
+
+
+@pytest.mark.parametrize("t", [O.Q4_K, O.Q6_K, O.Q8_0])
+def test_block_dots_equal_integer_math(t):
+    """Per-block integer sums equal a direct numpy restatement from dequantised pieces."""
+    name = {O.Q4_K: "q4k", O.Q6_K: "q6k", O.Q8_0: "q80"}[t]
+    raw = GOLD[f"{name}_raw"]
+    be = 32 if t == O.Q8_0 else 256
+    bb = {O.Q4_K: 144, O.Q6_K: 210, O.Q8_0: 34}[t]
+    nb = 16
+    w = raw[: nb * bb]
+    x = np.random.default_rng(5).standard_normal(nb * be).astype(np.float32)
+    xq = O.quant_for(t, x)
+    isum, msum = O.block_dots(t, w, xq, nb)
+    if t == O.Q8_0:
+        qa = w.reshape(nb, bb)[:, 2:].view(np.int8).astype(np.int64)
+        qb = xq.reshape(nb, 34)[:, 2:].view(np.int8).astype(np.int64)
+        np.testing.assert_array_equal(isum, (qa * qb).sum(1))
+    elif t == O.Q6_K:
+        blk = w.reshape(nb, bb)
+        for b in range(nb):
+            ql = blk[b, :128].astype(np.int64)
+            qh = blk[b, 128:192].astype(np.int64)
+            sc = blk[b, 192:208].view(np.int8).astype(np.int64)
+            q = np.zeros(256, np.int64)
+            for h in range(2):
+                L, H = ql[64 * h:64 * h + 64], qh[32 * h:32 * h + 32]
+                for l in range(32):
+                    q[128 * h + l] = (L[l] & 0xF) | (((H[l] >> 0) & 3) << 4)
+                    q[128 * h + l + 32] = (L[l + 32] & 0xF) | (((H[l] >> 2) & 3) << 4)
+                    q[128 * h + l + 64] = (L[l] >> 4) | (((H[l] >> 4) & 3) << 4)
+                    q[128 * h + l + 96] = (L[l + 32] >> 4) | (((H[l] >> 6) & 3) << 4)
+            q -= 32
+            a = xq[b]["qs"].astype(np.int64)
+            ref = sum(int(sc[j]) * int((q[16 * j:16 * j + 16] * a[16 * j:16 * j + 16]).sum()) for j in range(16))
+            assert isum[b] == ref
+    else:
+        blk = w.reshape(nb, bb)
+        for b in range(nb):
+            s = blk[b, 4:16]
+            sc = [s[j] & 63 if j < 4 else (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4) for j in range(8)]
+            mn = [s[j + 4] & 63 if j < 4 else (s[j + 4] >> 4) | ((s[j] >> 6) << 4) for j in range(8)]
+            qs = blk[b, 16:]
+            q = np.zeros(256, np.int64)
+            for g in range(4):
+                q[64 * g:64 * g + 32] = qs[32 * g:32 * g + 32] & 0xF
+                q[64 * g + 32:64 * g + 64] = qs[32 * g:32 * g + 32] >> 4
+            a = xq[b]["qs"].astype(np.int64)
+            ref_i = sum(int(sc[j]) * int((q[32 * j:32 * j + 32] * a[32 * j:32 * j + 32]).sum()) for j in range(8))
+            ref_m = sum(int(mn[j // 2]) * int(xq[b]["bsums"][j]) for j in range(16))
+            assert isum[b] == ref_i and msum[b] == ref_m
+
+
+@pytest.mark.parametrize("t", [O.Q4_K, O.Q6_K, O.Q8_0, O.F16])
+def test_matmul_close_to_f32_math(t):
+    """candle QMatMul semantics stay within quantisation noise of the f32 product."""
+    from tpt_spark_b200 import synth
+
+    N, K = 64, 1024
+    w = synth.normal(11, N * K, 0.02)
+    raw = synth.encode(t, w)
+    wd = O.dequant(t, raw, N * K).reshape(N, K)
+    x = np.random.default_rng(2).standard_normal(K).astype(np.float32)
+    y = O.matmul(t, raw, N, K, x)[0]
+    ref = wd.astype(np.float64) @ x.astype(np.float64)
+    tol = 1e-5 if t == O.F16 else 0.05
+    assert np.abs(y - ref).max() <= tol * np.abs(ref).max() + 1e-6
+
+
+def test_argmax_ties_last_and_repeat_penalty():
+    lg = np.array([1.0, 3.0, 2.0, 3.0, -1.0], np.float32)
+    assert O.argmax(lg) == 3  # Iterator::max_by keeps the last maximum
+    out = O.repeat_penalty(lg, [1, 1, 4], 2.0)
+    np.testing.assert_array_equal(out, np.array([1.0, 0.75, 2.0, 3.0, -2.0], np.float32))
+    np.testing.assert_array_equal(O.repeat_penalty(lg, [1], 1.0), lg)
+
+
+def test_forward_prefill_equals_incremental(tmp_path):
+    """candle's batched prefill and one-token steps give the same last-position logits."""
+    from tpt_spark_b200 import synth
+
+    p = str(tmp_path / "m.gguf")
+    synth.write_gguf(p, synth.TINY["tiny_q4km"], seed=3)
+    toks = [5, 17, 300, 42, 7, 99]
+    a = O.Model(p)
+    la = a.forward(toks, 0)
+    b = O.Model(p)
+    for i, t in enumerate(toks):
+        lb = b.forward([t], i)
+    # same math; only the attention mask path differs
+    np.testing.assert_allclose(la, lb, rtol=0, atol=1e-4)

@@ -1,0 +1,239 @@
+// attn_decode.cu -- GQA flash-decode over the HBM-resident fp16 KV cache.
+//
+// Replaces the reference's three attention passes (shaders/attention.wgsl:31-58 scores,
+// :73-135 softmax over a materialised scores[heads, ctx] buffer, :152-170 serial P.V),
+// dispatched from engine/wgpu_engine.rs:666-726, for one query position (decode).
+// Semantics follow candle quantized_llama forward_attn: score = (q.k) * (1/sqrt(hd)), no
+// mask for a single query (keys 0..pos), softmax, then P.V; head h reads kv head
+// h / (n_heads / n_kv) (repeat_kv).
+//
+// Layout: per layer K and V caches are [n_kv][max_seq][hd] fp16, so the keys of one kv head
+// at consecutive positions are one contiguous run.  Grid = (n_kv, splits); each CTA streams
+// its share of positions in tiles of 128 (one position per thread for the scores) through
+// a 2-stage shared-memory ring filled by 1-D TMA bulk copies, keeps an online softmax for
+// the group's query heads, and writes (m, l, acc) to scratch.  The last CTA of a kv head
+// (atomic ticket) merges the splits in split order, so the result does not depend on
+// scheduling.
+#include <algorithm>
+
+#include "kernels.h"
+
+namespace tptc {
+
+namespace {
+
+constexpr int kT = 128;        // threads per CTA = positions per tile
+constexpr int kMaxGroup = 8;   // query heads per kv head
+constexpr int kStages = 2;
+
+__global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kStages];
+    __shared__ float red[kMaxGroup][kT / 32];
+    __shared__ float mnew_s[kMaxGroup], alpha_s[kMaxGroup];
+    __shared__ int is_last;
+
+    const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.n_heads / p.n_kv, hd = p.hd;
+    const int tile_elems = kT * hd;
+    __half* kbuf = reinterpret_cast<__half*>(smem);                       // [kStages][kT][hd]
+    __half* vbuf = kbuf + kStages * tile_elems;                           // [kStages][kT][hd]
+    float* qs = reinterpret_cast<float*>(vbuf + kStages * tile_elems);    // [G][hd]
+    float* ps = qs + G * hd;                                              // [G][kT]
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const int kv_len = *p.pos + 1;
+    int per = (kv_len + p.splits - 1) / p.splits;
+    per = (per + kT - 1) / kT * kT;
+    const int t_begin = split * per, t_end = min(kv_len, t_begin + per);
+    const int ntiles = t_end > t_begin ? (t_end - t_begin + kT - 1) / kT : 0;
+
+    for (int i = tid; i < G * hd; i += kT) qs[i] = p.q[(kvh * G) * hd + i];
+    __syncthreads();
+
+    const __half* kh = p.kcache + (int64_t)kvh * p.max_seq * hd;
+    const __half* vh = p.vcache + (int64_t)kvh * p.max_seq * hd;
+    uint64_t policy = 0;
+    auto issue = [&](int tile) {
+        const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
+        const uint32_t bytes = (uint32_t)n * hd * 2;
+        mbar_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(kbuf + s * tile_elems, kh + (int64_t)t0 * hd, bytes, &full[s], policy);
+        bulk_g2s(vbuf + s * tile_elems, vh + (int64_t)t0 * hd, bytes, &full[s], policy);
+    };
+    if (tid == 0) {
+        policy = l2_evict_first_policy();
+        for (int t = 0; t < kStages && t < ntiles; t++) issue(t);
+    }
+
+    float m_run[kMaxGroup], l_run[kMaxGroup], acc[kMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; g++) {
+        m_run[g] = -INFINITY;
+        l_run[g] = 0.f;
+        acc[g] = 0.f;
+    }
+    bool timed_out = false;
+    for (int tile = 0; tile < ntiles; tile++) {
+        const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
+        if (!mbar_wait_bounded(&full[s], (tile / kStages) & 1, p.err)) timed_out = true;
+        if (__syncthreads_or(timed_out)) return;
+        // scores: thread = position; rotate the start column so lanes hit different banks
+        const __half2* krow = reinterpret_cast<const __half2*>(kbuf + s * tile_elems + tid * hd);
+        float sc[kMaxGroup];
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.f;
+        if (tid < n) {
+            const int hp = hd / 2;
+            int jj = tid % hp;
+            for (int j = 0; j < hp; j++, jj = (jj + 1 == hp) ? 0 : jj + 1) {
+                const float2 kv = __half22float2(krow[jj]);
+#pragma unroll
+                for (int g = 0; g < kMaxGroup; g++) {
+                    if (g < G) {
+                        const float2 qv = reinterpret_cast<const float2*>(qs + g * hd)[jj];
+                        sc[g] = fmaf(qv.x, kv.x, sc[g]);
+                        sc[g] = fmaf(qv.y, kv.y, sc[g]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; g++) sc[g] = sc[g] * p.scale;
+        } else {
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; g++) sc[g] = -INFINITY;
+        }
+        // tile max per head
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; g++) {
+            if (g < G) {
+                const float mx = warp_max(sc[g]);
+                if (lane == 0) red[g][warp] = mx;
+            }
+        }
+        __syncthreads();
+        if (tid < G) {
+            float mx = red[tid][0];
+            for (int w = 1; w < kT / 32; w++) mx = fmaxf(mx, red[tid][w]);
+            const float mn = fmaxf(m_run[tid], mx);
+            mnew_s[tid] = mn;
+            alpha_s[tid] = m_run[tid] == -INFINITY ? 0.f : expf(m_run[tid] - mn);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; g++) {
+            if (g < G) {
+                const float pv = tid < n ? expf(sc[g] - mnew_s[g]) : 0.f;
+                ps[g * kT + tid] = pv;
+                const float ls = warp_sum(pv);
+                if (lane == 0) red[g][warp] = ls;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; g++) {
+            if (g < G) {
+                float ls = 0.f;
+                for (int w = 0; w < kT / 32; w++) ls += red[g][w];
+                l_run[g] = l_run[g] * alpha_s[g] + ls;
+                m_run[g] = mnew_s[g];
+                acc[g] *= alpha_s[g];
+            }
+        }
+        // P.V: thread = output dimension
+        if (tid < hd) {
+            const __half* vcol = vbuf + s * tile_elems + tid;
+            for (int t = 0; t < n; t++) {
+                const float v = __half2float(vcol[t * hd]);
+#pragma unroll
+                for (int g = 0; g < kMaxGroup; g++)
+                    if (g < G) acc[g] = fmaf(ps[g * kT + t], v, acc[g]);
+            }
+        }
+        __syncthreads();  // stage s fully consumed
+        if (tid == 0 && tile + kStages < ntiles) {
+            fence_proxy_async_smem();
+            issue(tile + kStages);
+        }
+    }
+
+    // partial results: [kvh][split][g][2 + hd] = (m, l, acc[hd])
+    const int rec = 2 + hd;
+    float* part = p.partial + ((int64_t)kvh * p.splits + split) * G * rec;
+    if (tid < hd) {
+        for (int g = 0; g < G; g++) part[g * rec + 2 + tid] = acc[g];
+    }
+    if (tid == 0) {
+        for (int g = 0; g < G; g++) {
+            part[g * rec] = m_run[g];
+            part[g * rec + 1] = l_run[g];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(&p.counters[kvh], 1) == p.splits - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float* base = p.partial + (int64_t)kvh * p.splits * G * rec;
+    if (tid < hd) {
+        for (int g = 0; g < G; g++) {
+            float M = -INFINITY;
+            for (int s = 0; s < p.splits; s++) M = fmaxf(M, base[(s * G + g) * rec]);
+            float L = 0.f, o = 0.f;
+            for (int s = 0; s < p.splits; s++) {
+                const float* r = base + (s * G + g) * rec;
+                const float w = r[0] == -INFINITY ? 0.f : expf(r[0] - M);
+                L = fmaf(r[1], w, L);
+                o = fmaf(r[2 + tid], w, o);
+            }
+            p.out[(kvh * G + g) * hd + tid] = o / L;
+        }
+    }
+    if (tid == 0) p.counters[kvh] = 0;
+}
+
+size_t attn_smem(int n_heads, int n_kv, int hd) {
+    const int G = n_heads / n_kv;
+    return (size_t)2 * kStages * kT * hd * 2 + (size_t)G * hd * 4 + (size_t)G * kT * 4;
+}
+
+}  // namespace
+
+int attn_decode_splits(int n_kv, int max_seq, int sm_count) {
+    int s = std::max(1, sm_count / n_kv);
+    const int max_useful = (max_seq + kT - 1) / kT;
+    return std::min(s, std::max(1, max_useful));
+}
+
+size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits) {
+    return (size_t)n_kv * splits * (n_heads / n_kv) * (2 + hd);
+}
+
+cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl) {
+    if (p.n_heads % p.n_kv != 0 || p.n_heads / p.n_kv > kMaxGroup || p.hd > kT || p.hd % 2 != 0 || (p.hd * 2) % 16 != 0)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_kv, p.splits);
+    cfg.blockDim = dim3(kT);
+    cfg.dynamicSmemBytes = attn_smem(p.n_heads, p.n_kv, p.hd);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel, p);
+}
+
+cudaError_t attn_init_device() {
+    return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+}  // namespace tptc

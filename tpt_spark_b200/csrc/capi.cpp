@@ -1,0 +1,306 @@
+// capi.cpp -- extern "C" boundary (include/tptc.h).  Every entry point converts C++ state
+// into an int status and keeps the message for tptc_last_error.
+#include <string.h>
+
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "engine.h"
+#include "kernels.h"
+#include "tp.h"
+#include "tptc.h"
+
+using tptc::Engine;
+using tptc::Status;
+
+struct tptc_ctx {
+    Engine* eng = nullptr;
+    std::string err;
+};
+
+struct tptc_matrix {
+    tptc::DevMatrix m;
+    uint8_t* mem = nullptr;
+    int* err = nullptr;
+    int device = 0;
+};
+
+namespace {
+
+thread_local std::string g_err;  // errors without a context (create, kernel-level calls)
+
+int fail(tptc_ctx* c, const Status& s) {
+    if (c) c->err = s.msg;
+    else g_err = s.msg;
+    return s.code;
+}
+
+int fail_code(tptc_ctx* c, int code, const std::string& m) { return fail(c, Status{code, m}); }
+
+int cuda_fail(cudaError_t e, const char* what) {
+    g_err = tptc::cuda_msg(e, what);
+    return TPTC_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+TPTC_API const char* tptc_version(void) { return "tptc 0.1 (sm_100a)"; }
+
+TPTC_API int tptc_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+TPTC_API int tptc_nccl_unique_id(void* out128) {
+    if (!out128) return TPTC_ERR_ARG;
+    return tptc::nccl_unique_id(out128);
+}
+
+TPTC_API int tptc_create(int device, int tp_rank, int tp_size, const void* nccl_uid, tptc_ctx** out) {
+    if (!out) return TPTC_ERR_ARG;
+    *out = nullptr;
+    tptc_ctx* c = new (std::nothrow) tptc_ctx();
+    if (!c) return TPTC_ERR_OOM;
+    c->eng = new (std::nothrow) Engine(device, tp_rank, tp_size);
+    if (!c->eng) {
+        delete c;
+        return TPTC_ERR_OOM;
+    }
+    Status s = c->eng->init(nccl_uid);
+    if (!s.ok()) {
+        g_err = s.msg;
+        delete c->eng;
+        delete c;
+        return s.code;
+    }
+    *out = c;
+    return TPTC_OK;
+}
+
+TPTC_API void tptc_destroy(tptc_ctx* ctx) {
+    if (!ctx) return;
+    delete ctx->eng;
+    delete ctx;
+}
+
+TPTC_API const char* tptc_last_error(const tptc_ctx* ctx) { return ctx ? ctx->err.c_str() : g_err.c_str(); }
+
+TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user) {
+    if (!ctx || !path) return fail_code(ctx, TPTC_ERR_ARG, "null argument");
+    Status s = ctx->eng->load(path, progress, user);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_unload(tptc_ctx* ctx) {
+    if (!ctx) return TPTC_ERR_ARG;
+    ctx->eng->unload();
+    return TPTC_OK;
+}
+
+TPTC_API int tptc_is_loaded(const tptc_ctx* ctx) { return ctx && ctx->eng->loaded() ? 1 : 0; }
+
+TPTC_API int tptc_get_model_info(const tptc_ctx* ctx, tptc_model_info* out) {
+    if (!ctx || !out) return TPTC_ERR_ARG;
+    if (!ctx->eng->loaded()) return TPTC_ERR_STATE;
+    ctx->eng->info(out);
+    return TPTC_OK;
+}
+
+TPTC_API int tptc_kv_reset(tptc_ctx* ctx) {
+    if (!ctx) return TPTC_ERR_ARG;
+    Status s = ctx->eng->kv_reset();
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_kv_truncate(tptc_ctx* ctx, int n) {
+    if (!ctx) return TPTC_ERR_ARG;
+    if (n < 0 || n > ctx->eng->kv_len()) return fail_code(ctx, TPTC_ERR_ARG, "truncate length outside the cache");
+    ctx->eng->kv_truncate(n);
+    return TPTC_OK;
+}
+
+TPTC_API int tptc_kv_prefix_len(const tptc_ctx* ctx, const uint32_t* ids, int n) {
+    if (!ctx || (n > 0 && !ids) || n < 0) return TPTC_ERR_ARG;
+    return ctx->eng->prefix_len(ids, n);
+}
+
+TPTC_API int tptc_kv_len(const tptc_ctx* ctx) { return ctx ? ctx->eng->kv_len() : TPTC_ERR_ARG; }
+
+TPTC_API int tptc_common_prefix_len(const uint32_t* cached, int n_cached, const uint32_t* ids, int n) {
+    if (n_cached < 0 || n < 0 || (n_cached > 0 && !cached) || (n > 0 && !ids)) return TPTC_ERR_ARG;
+    return tptc::common_prefix_len(cached, n_cached, ids, n);
+}
+
+TPTC_API int tptc_prefill(tptc_ctx* ctx, const uint32_t* ids, int n, int start_pos, float* last_logits) {
+    if (!ctx || !ids) return fail_code(ctx, TPTC_ERR_ARG, "null argument");
+    Status s = ctx->eng->prefill(ids, n, start_pos, last_logits);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_decode(tptc_ctx* ctx, uint32_t id, int pos, float* logits, uint32_t* argmax) {
+    if (!ctx) return TPTC_ERR_ARG;
+    Status s = ctx->eng->decode(id, pos, logits, argmax);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_decode_greedy(tptc_ctx* ctx, uint32_t id, int pos, int n, uint32_t* out_ids) {
+    if (!ctx) return TPTC_ERR_ARG;
+    Status s = ctx->eng->decode_greedy(id, pos, n, out_ids);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_infer(tptc_ctx* ctx, const uint32_t* prompt, int n, const tptc_infer_params* params,
+                        tptc_token_cb on_token, void* user) {
+    if (!ctx || !params || (n > 0 && !prompt)) return fail_code(ctx, TPTC_ERR_ARG, "null argument");
+    Status s = ctx->eng->infer(prompt, n, *params, on_token, user);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_last_device_ms(const tptc_ctx* ctx, double* ms) {
+    if (!ctx || !ms) return TPTC_ERR_ARG;
+    *ms = ctx->eng->last_device_ms;
+    return TPTC_OK;
+}
+
+TPTC_API int tptc_last_timing(const tptc_ctx* ctx, double* prefill_ms, double* decode_ms, int* n_prompt,
+                              int* n_generated) {
+    if (!ctx) return TPTC_ERR_ARG;
+    if (prefill_ms) *prefill_ms = ctx->eng->last_prefill_ms;
+    if (decode_ms) *decode_ms = ctx->eng->last_decode_ms;
+    if (n_prompt) *n_prompt = ctx->eng->last_n_prompt;
+    if (n_generated) *n_generated = ctx->eng->last_n_generated;
+    return TPTC_OK;
+}
+
+// ---- kernel-level entry points -----------------------------------------------------------
+
+static bool type_ok(int t) {
+    return t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q8_0 || t == TPTC_TYPE_F16;
+}
+
+TPTC_API int tptc_dequant(int ggml_type, const void* d_blocks, int64_t n, float* d_out, void* stream) {
+    if (!d_blocks || !d_out || n < 0) return TPTC_ERR_ARG;
+    const int64_t be = ggml_type == TPTC_TYPE_Q8_0 ? 32 : (ggml_type == TPTC_TYPE_Q4_K || ggml_type == TPTC_TYPE_Q6_K) ? 256 : 1;
+    if (!(type_ok(ggml_type) || ggml_type == TPTC_TYPE_F32) || n % be) return TPTC_ERR_ARG;
+    cudaError_t e = tptc::launch_dequant_raw(ggml_type, d_blocks, n, d_out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "dequant");
+}
+
+TPTC_API int tptc_quant_q8k(const float* d_x, int64_t k, void* d_out, void* stream) {
+    if (!d_x || !d_out || k < 0 || k % 256) return TPTC_ERR_ARG;
+    cudaError_t e = tptc::launch_quant_q8k(d_x, k, d_out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "quant_q8k");
+}
+
+TPTC_API int tptc_quant_q80(const float* d_x, int64_t k, void* d_out, void* stream) {
+    if (!d_x || !d_out || k < 0 || k % 32) return TPTC_ERR_ARG;
+    cudaError_t e = tptc::launch_quant_q80(d_x, k, d_out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "quant_q80");
+}
+
+TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_device, int N, int K, tptc_matrix** out) {
+    if (!out || !raw || N <= 0 || K <= 0) return TPTC_ERR_ARG;
+    *out = nullptr;
+    if (!type_ok(ggml_type)) {
+        g_err = "unsupported matrix type";
+        return TPTC_ERR_UNSUPPORTED;
+    }
+    if (K % 256) {
+        g_err = "K must be a multiple of 256";
+        return TPTC_ERR_UNSUPPORTED;
+    }
+    tptc_matrix* m = new (std::nothrow) tptc_matrix();
+    if (!m) return TPTC_ERR_OOM;
+    cudaGetDevice(&m->device);
+    cudaError_t ie = tptc::kernels_init_device();
+    if (ie != cudaSuccess) {
+        delete m;
+        return cuda_fail(ie, "kernel setup");
+    }
+    tptc::DevMatrix& d = m->m;
+    d.type = ggml_type;
+    d.N = N;
+    d.K = K;
+    int64_t raw_row;
+    switch (ggml_type) {
+    case TPTC_TYPE_Q4_K: d.main_row_bytes = (int64_t)K / 256 * 144; raw_row = d.main_row_bytes; break;
+    case TPTC_TYPE_Q6_K: d.main_row_bytes = (int64_t)K / 256 * 208; d.d_per_row = K / 256; raw_row = (int64_t)K / 256 * 210; break;
+    case TPTC_TYPE_Q8_0: d.main_row_bytes = K; d.d_per_row = K / 32; raw_row = (int64_t)K / 32 * 34; break;
+    default: d.main_row_bytes = (int64_t)K * 2; raw_row = d.main_row_bytes; break;
+    }
+    const size_t main_bytes = (size_t)d.main_row_bytes * N, d_bytes = (size_t)d.d_per_row * 2 * N;
+    const size_t main_al = (main_bytes + 255) / 256 * 256;
+    cudaError_t e = cudaMalloc(&m->mem, main_al + d_bytes + 256);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_fail(e, "cudaMalloc(matrix)");
+    }
+    d.main = m->mem;
+    d.dplane = d.d_per_row ? reinterpret_cast<uint16_t*>(m->mem + main_al) : nullptr;
+    m->err = reinterpret_cast<int*>(m->mem + main_al + d_bytes);
+    const size_t raw_bytes = (size_t)raw_row * N;
+    const uint8_t* src = static_cast<const uint8_t*>(raw);
+    uint8_t* tmp = nullptr;
+    if (!raw_on_device) {
+        e = cudaMalloc(&tmp, raw_bytes);
+        if (e == cudaSuccess) e = cudaMemcpy(tmp, raw, raw_bytes, cudaMemcpyHostToDevice);
+        src = tmp;
+    }
+    if (e == cudaSuccess) e = cudaMemset(m->err, 0, sizeof(int));
+    if (e == cudaSuccess) e = tptc::launch_repack(src, d, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+        cudaFree(m->mem);
+        delete m;
+        return cuda_fail(e, "matrix upload/repack");
+    }
+    *out = m;
+    return TPTC_OK;
+}
+
+TPTC_API void tptc_matrix_destroy(tptc_matrix* m) {
+    if (!m) return;
+    if (m->mem) cudaFree(m->mem);
+    delete m;
+}
+
+TPTC_API int64_t tptc_matrix_bytes(const tptc_matrix* m) { return m ? m->m.bytes() : -1; }
+
+static tptc::GemvParams matrix_params(const tptc_matrix* m, const float* x) {
+    tptc::GemvParams p = {};
+    p.nseg = 1;
+    p.seg[0] = tptc::GemvSeg{m->m.main, m->m.dplane, m->m.type, m->m.N, m->m.main_row_bytes, m->m.d_per_row, 0};
+    p.K = m->m.K;
+    p.x = x;
+    p.err = m->err;
+    tptc::gemv_prepare(p);
+    return p;
+}
+
+TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void* stream) {
+    if (!m || !d_x || !d_y) return TPTC_ERR_ARG;
+    tptc::GemvParams p = matrix_params(m, d_x);
+    p.out = d_y;
+    cudaError_t e = tptc::gemv_launch(p, tptc::EPI_STORE, static_cast<cudaStream_t>(stream), false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemv");
+}
+
+TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum, void* stream) {
+    if (!m || !d_x || !d_isum) return TPTC_ERR_ARG;
+    if (m->m.type == TPTC_TYPE_F16) return TPTC_ERR_UNSUPPORTED;
+    tptc::GemvParams p = matrix_params(m, d_x);
+    p.isum = d_isum;
+    p.msum = d_msum;
+    cudaError_t e = tptc::gemv_launch(p, tptc::EPI_DOTS, static_cast<cudaStream_t>(stream), false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "block_dots");
+}
+
+}  // extern "C"

@@ -1,0 +1,832 @@
+// engine.cpp -- model load, KV cache, CUDA-graph decode step, prefill and the infer loop.
+#include "engine.h"
+
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <chrono>
+#include <random>
+
+#include "kernels.h"
+#include "prefill.h"
+#include "tp.h"
+
+namespace tptc {
+
+std::string cuda_msg(cudaError_t e, const char* what) {
+    return std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+}
+
+namespace {
+
+Status err(int code, const std::string& m) { return Status{code, m}; }
+
+#define RET_IF(st)            \
+    do {                      \
+        Status _s = (st);     \
+        if (!_s.ok()) return _s; \
+    } while (0)
+
+#define CU(call)                                                                      \
+    do {                                                                              \
+        cudaError_t _e = (call);                                                      \
+        if (_e != cudaSuccess) return Status{TPTC_ERR_CUDA, cuda_msg(_e, #call)};     \
+    } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device layout geometry of a matrix (see gemv.cuh).
+void matrix_geometry(int type, int N, int K, int64_t& main_row, int64_t& d_per_row) {
+    d_per_row = 0;
+    switch (type) {
+    case TPTC_TYPE_Q4_K: main_row = (int64_t)K / QK_K * Q4K_BYTES; break;
+    case TPTC_TYPE_Q6_K: main_row = (int64_t)K / QK_K * Q6K_MAIN; d_per_row = K / QK_K; break;
+    case TPTC_TYPE_Q8_0: main_row = K; d_per_row = K / QK8_0; break;
+    default: main_row = (int64_t)K * 2; break;
+    }
+    (void)N;
+}
+
+int64_t raw_row_bytes(int type, int K) {
+    switch (type) {
+    case TPTC_TYPE_Q4_K: return (int64_t)K / QK_K * Q4K_BYTES;
+    case TPTC_TYPE_Q6_K: return (int64_t)K / QK_K * Q6K_BYTES;
+    case TPTC_TYPE_Q8_0: return (int64_t)K / QK8_0 * Q80_BYTES;
+    case TPTC_TYPE_F16: return (int64_t)K * 2;
+    case TPTC_TYPE_F32: return (int64_t)K * 4;
+    }
+    return 0;
+}
+
+bool matrix_type_ok(int t) {
+    return t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q8_0 || t == TPTC_TYPE_F16;
+}
+
+// Streams host bytes into device memory through two pinned buffers (the reference uploads
+// with wgpu create_buffer_init, wgpu_loader.rs:175; here: mmap -> pinned -> cudaMemcpyAsync).
+struct Stager {
+    static constexpr size_t kChunk = 64ull << 20;
+    uint8_t* pinned[2] = {nullptr, nullptr};
+    uint8_t* dtmp[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    int cur = 0;
+    cudaStream_t st;
+
+    explicit Stager(cudaStream_t s) : st(s) {}
+    ~Stager() {
+        for (int i = 0; i < 2; i++) {
+            if (ev[i]) {
+                cudaEventSynchronize(ev[i]);
+                cudaEventDestroy(ev[i]);
+            }
+            if (pinned[i]) cudaFreeHost(pinned[i]);
+            if (dtmp[i]) cudaFree(dtmp[i]);
+        }
+    }
+    Status init() {
+        for (int i = 0; i < 2; i++) {
+            CU(cudaHostAlloc(&pinned[i], kChunk, cudaHostAllocDefault));
+            CU(cudaMalloc(&dtmp[i], kChunk));
+            CU(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+            CU(cudaEventRecord(ev[i], st));
+        }
+        return {};
+    }
+    // Next free buffer index (waits for its previous transfer).
+    Status acquire(int& i) {
+        i = cur;
+        cur ^= 1;
+        CU(cudaEventSynchronize(ev[i]));
+        return {};
+    }
+    Status release(int i) {
+        CU(cudaEventRecord(ev[i], st));
+        return {};
+    }
+};
+
+// Copy rows [r0, r1) x raw-bytes [c0, c1) of a row-major host tensor into device memory,
+// repacking to the device layout.  Used whole (c0 = 0, c1 = row bytes) on one GPU; the
+// column window selects a K-slice for row-parallel tensor sharding.
+Status upload_rows(Stager& sg, const uint8_t* host, int64_t host_row_bytes, int r0, int r1, int64_t c0, int64_t c1,
+                   const DevMatrix& m) {
+    const int64_t rb = c1 - c0;
+    const bool repack = m.type == TPTC_TYPE_Q6_K || m.type == TPTC_TYPE_Q8_0;
+    int rows_per = (int)std::max<int64_t>(1, (int64_t)Stager::kChunk / rb);
+    for (int r = r0; r < r1; r += rows_per) {
+        const int nr = std::min(rows_per, r1 - r);
+        int b;
+        RET_IF(sg.acquire(b));
+        if (c0 == 0 && rb == host_row_bytes) {
+            memcpy(sg.pinned[b], host + (int64_t)r * host_row_bytes, (size_t)nr * rb);
+        } else {
+            for (int i = 0; i < nr; i++)
+                memcpy(sg.pinned[b] + (int64_t)i * rb, host + (int64_t)(r + i) * host_row_bytes + c0, (size_t)rb);
+        }
+        DevMatrix view = m;
+        view.N = nr;
+        view.main = m.main + (int64_t)(r - r0) * m.main_row_bytes;
+        view.dplane = m.dplane ? m.dplane + (int64_t)(r - r0) * m.d_per_row : nullptr;
+        if (repack) {
+            CU(cudaMemcpyAsync(sg.dtmp[b], sg.pinned[b], (size_t)nr * rb, cudaMemcpyHostToDevice, sg.st));
+            CU(launch_repack(sg.dtmp[b], view, sg.st));
+        } else {
+            CU(cudaMemcpyAsync(view.main, sg.pinned[b], (size_t)nr * rb, cudaMemcpyHostToDevice, sg.st));
+        }
+        RET_IF(sg.release(b));
+    }
+    return {};
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------
+
+Engine::Engine(int device, int tp_rank, int tp_size) : device_(device), tp_rank_(tp_rank), tp_size_(tp_size) {}
+
+Engine::~Engine() {
+    unload();
+    if (stream_) {
+        cudaSetDevice(device_);
+        cudaStreamDestroy(stream_);
+    }
+    if (ev0_) cudaEventDestroy(ev0_);
+    if (ev1_) cudaEventDestroy(ev1_);
+    if (h_tok_) cudaFreeHost(h_tok_);
+    if (h_pos_) cudaFreeHost(h_pos_);
+    if (h_err_) cudaFreeHost(h_err_);
+}
+
+Status Engine::init(const void* nccl_uid) {
+    int n = 0;
+    CU(cudaGetDeviceCount(&n));
+    if (device_ < 0 || device_ >= n) return err(TPTC_ERR_ARG, "device " + std::to_string(device_) + " not present");
+    if (tp_size_ < 1 || tp_rank_ < 0 || tp_rank_ >= tp_size_) return err(TPTC_ERR_ARG, "bad tp rank/size");
+    CU(cudaSetDevice(device_));
+    cudaDeviceProp prop;
+    CU(cudaGetDeviceProperties(&prop, device_));
+    if (prop.major < 10) return err(TPTC_ERR_UNSUPPORTED, std::string("libtptc needs sm_100 (B200); found ") + prop.name);
+    sm_count_ = prop.multiProcessorCount;
+    CU(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    CU(cudaEventCreate(&ev0_));
+    CU(cudaEventCreate(&ev1_));
+    CU(kernels_init_device());
+    CU(cudaHostAlloc(&h_tok_, 64 * sizeof(uint32_t), cudaHostAllocDefault));
+    CU(cudaHostAlloc(&h_pos_, 64 * sizeof(int), cudaHostAllocDefault));
+    CU(cudaHostAlloc(&h_err_, 64 * sizeof(int), cudaHostAllocDefault));
+    const char* e = getenv("TPTC_PDL");
+    pdl_ = !(e && e[0] == '0');
+    if (tp_size_ > 1) {
+        tp_.reset(new Tp());
+        RET_IF(tp_->init(tp_rank_, tp_size_, nccl_uid, stream_));
+    }
+    return {};
+}
+
+void Engine::unload() {
+    if (device_ >= 0) cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (graph_plain_) cudaGraphExecDestroy(graph_plain_);
+    if (graph_chained_) cudaGraphExecDestroy(graph_chained_);
+    graph_plain_ = graph_chained_ = nullptr;
+    if (arena_) cudaFree(arena_);
+    if (rt_) cudaFree(rt_);
+    if (pf_) cudaFree(pf_);
+    arena_ = rt_ = pf_ = nullptr;
+    arena_size_ = rt_size_ = pf_size_ = 0;
+    pf_chunk_ = 0;
+    layers_.clear();
+    cached_tokens_.clear();
+    loaded_ = false;
+    device_bytes_ = 0;
+}
+
+Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
+    if (!stream_) return err(TPTC_ERR_STATE, "context not initialised");
+    CU(cudaSetDevice(device_));
+    unload();
+    GgufFile f;
+    std::string emsg;
+    int rc = f.open(path, emsg);
+    if (rc != TPTC_OK) return err(rc, emsg);
+
+    // ---- metadata (wgpu_loader.rs:305-406; candle_engine.rs:145-165 arch check)
+    ModelMeta m;
+    f.get_str("general.architecture", m.architecture);
+    if (m.architecture != "llama" && m.architecture != "mistral")
+        return err(TPTC_ERR_UNSUPPORTED, "Architecture '" + m.architecture +
+                                             "' is not yet supported. Supported: llama, mistral.");
+    f.get_str("general.name", m.name);
+    const std::string a = m.architecture;
+    uint64_t u;
+    auto getu = [&](const std::string& k, int def) { return f.get_u64(a + "." + k, u) ? (int)u : def; };
+    m.context_length = getu("context_length", 4096);
+    m.n_layers = getu("block_count", 32);
+    m.n_heads = getu("attention.head_count", 32);
+    m.n_kv_heads = getu("attention.head_count_kv", m.n_heads);
+    m.dim = getu("embedding_length", 4096);
+    const GgufTensor* te = f.find("token_embd.weight");
+    if (!te || te->ne.size() != 2) return err(TPTC_ERR_FORMAT, "missing or malformed token_embd.weight");
+    m.vocab = getu("vocab_size", (int)te->ne[1]);
+    float fv;
+    if (f.get_f32(a + ".rope.freq_base", fv)) m.rope_freq_base = fv;
+    if (f.get_f32(a + ".attention.layer_norm_rms_epsilon", fv)) m.rms_eps = fv;
+    {
+        std::string st;
+        float factor = 1.f;
+        f.get_str(a + ".rope.scaling.type", st);
+        f.get_f32(a + ".rope.scaling.factor", factor);
+        if (st == "linear" || st == "longrope") m.rope_scale = std::max(1.f, factor);
+    }
+    if (m.n_heads <= 0 || m.dim % m.n_heads) return err(TPTC_ERR_FORMAT, "embedding_length not divisible by head_count");
+    m.head_dim = m.dim / m.n_heads;
+    {
+        int est = (m.dim * 8 + 2) / 3;
+        est = (est + 255) / 256 * 256;
+        m.ffn = getu("feed_forward_length", est);
+    }
+    if (m.n_kv_heads <= 0 || m.n_heads % m.n_kv_heads) return err(TPTC_ERR_UNSUPPORTED, "head_count not a multiple of head_count_kv");
+    if (m.head_dim % 16 || m.head_dim > 128) return err(TPTC_ERR_UNSUPPORTED, "head_dim must be a multiple of 16 and <= 128");
+    if (m.dim % QK_K || m.ffn % QK_K) return err(TPTC_ERR_UNSUPPORTED, "embedding/ffn sizes must be multiples of 256");
+    if (m.n_kv_heads % tp_size_ || m.ffn % (QK_K * tp_size_))
+        return err(TPTC_ERR_UNSUPPORTED, "model does not shard evenly over tp_size=" + std::to_string(tp_size_));
+    m.tied = f.find("output.weight") == nullptr;
+    meta_ = m;
+    path_ = path;
+    file_bytes_ = f.size;
+
+    const int tp = tp_size_, r = tp_rank_;
+    n_heads_l_ = m.n_heads / tp;
+    n_kv_l_ = m.n_kv_heads / tp;
+    const int hd = m.head_dim, ffn_l = m.ffn / tp, qd_l = n_heads_l_ * hd, kvd_l = n_kv_l_ * hd;
+
+    // ---- tensor plan: name, expected shape, rows/cols this rank keeps
+    struct Plan {
+        std::string name;
+        int N, K;            // full shape
+        int r0, r1;          // rows kept (column parallel)
+        int k0, k1;          // K range kept (row parallel)
+        DevMatrix* mat;      // nullptr for f32 vectors
+        float** vec;
+    };
+    std::vector<Plan> plans;
+    layers_.assign(m.n_layers, LayerWeights{});
+    plans.push_back({"token_embd.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &embd_, nullptr});
+    for (int l = 0; l < m.n_layers; l++) {
+        LayerWeights& L = layers_[l];
+        const std::string p = "blk." + std::to_string(l) + ".";
+        plans.push_back({p + "attn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.attn_norm});
+        plans.push_back({p + "attn_q.weight", m.n_heads * hd, m.dim, r * qd_l, (r + 1) * qd_l, 0, m.dim, &L.q, nullptr});
+        plans.push_back({p + "attn_k.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.k, nullptr});
+        plans.push_back({p + "attn_v.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.v, nullptr});
+        plans.push_back({p + "attn_output.weight", m.dim, m.n_heads * hd, 0, m.dim, r * qd_l, (r + 1) * qd_l, &L.o, nullptr});
+        plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm});
+        plans.push_back({p + "ffn_gate.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.gate, nullptr});
+        plans.push_back({p + "ffn_up.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.up, nullptr});
+        plans.push_back({p + "ffn_down.weight", m.dim, m.ffn, 0, m.dim, r * ffn_l, (r + 1) * ffn_l, &L.down, nullptr});
+    }
+    plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_});
+    if (!m.tied) plans.push_back({"output.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &output_, nullptr});
+
+    // ---- validate and lay out the arena
+    size_t off = 0;
+    std::vector<size_t> offs(plans.size()), doffs(plans.size());
+    std::vector<const GgufTensor*> tens(plans.size());
+    for (size_t i = 0; i < plans.size(); i++) {
+        Plan& p = plans[i];
+        const GgufTensor* t = f.find(p.name);
+        if (!t) return err(TPTC_ERR_FORMAT, "missing tensor '" + p.name + "'");
+        tens[i] = t;
+        const bool vec = p.mat == nullptr;
+        const uint64_t want0 = (uint64_t)p.K, want1 = (uint64_t)p.N;
+        bool shape_ok = vec ? (t->ne.size() == 1 && t->ne[0] == want0)
+                            : (t->ne.size() == 2 && t->ne[0] == want0 && t->ne[1] == want1);
+        if (!shape_ok) return err(TPTC_ERR_FORMAT, "tensor '" + p.name + "' has an unexpected shape");
+        if (vec) {
+            if (t->type != TPTC_TYPE_F32) return err(TPTC_ERR_UNSUPPORTED, "norm tensor '" + p.name + "' must be F32");
+            offs[i] = off;
+            off = align_up(off + (size_t)p.K * 4, 256);
+            continue;
+        }
+        if (!matrix_type_ok((int)t->type))
+            return err(TPTC_ERR_UNSUPPORTED, "tensor '" + p.name + "' has unsupported GGML type " + std::to_string(t->type));
+        DevMatrix& d = *p.mat;
+        d.type = (int)t->type;
+        d.N = p.r1 - p.r0;
+        d.K = p.k1 - p.k0;
+        matrix_geometry(d.type, d.N, d.K, d.main_row_bytes, d.d_per_row);
+        offs[i] = off;
+        off = align_up(off + (size_t)d.main_row_bytes * d.N, 256);
+        doffs[i] = off;
+        off = align_up(off + (size_t)d.d_per_row * 2 * d.N, 256);
+    }
+    arena_size_ = off;
+    cudaError_t ce = cudaMalloc(&arena_, arena_size_);
+    if (ce != cudaSuccess) {
+        arena_ = nullptr;
+        return err(TPTC_ERR_OOM, "weights need " + std::to_string(arena_size_ >> 20) + " MiB: " + cuda_msg(ce, "cudaMalloc"));
+    }
+    device_bytes_ = arena_size_;
+
+    // ---- upload
+    Stager sg(stream_);
+    RET_IF(sg.init());
+    weight_bytes_ = 0;
+    for (size_t i = 0; i < plans.size(); i++) {
+        Plan& p = plans[i];
+        const GgufTensor* t = tens[i];
+        const uint8_t* src = f.tensor_data(*t);
+        if (!p.mat) {
+            *p.vec = reinterpret_cast<float*>(arena_ + offs[i]);
+            DevMatrix tmp;
+            tmp.type = TPTC_TYPE_F32;
+            tmp.N = 1;
+            tmp.K = p.K;
+            tmp.main = arena_ + offs[i];
+            tmp.main_row_bytes = (int64_t)p.K * 4;
+            RET_IF(upload_rows(sg, src, (int64_t)p.K * 4, 0, 1, 0, (int64_t)p.K * 4, tmp));
+            weight_bytes_ += (uint64_t)p.K * 4;
+        } else {
+            DevMatrix& d = *p.mat;
+            d.main = arena_ + offs[i];
+            d.dplane = d.d_per_row ? reinterpret_cast<uint16_t*>(arena_ + doffs[i]) : nullptr;
+            const int64_t rrb = raw_row_bytes(d.type, p.K);
+            const int64_t c0 = raw_row_bytes(d.type, p.k0), c1 = raw_row_bytes(d.type, p.k1);
+            RET_IF(upload_rows(sg, src, rrb, p.r0, p.r1, c0, c1, d));
+            weight_bytes_ += (uint64_t)d.bytes();
+        }
+        if (cb) cb((uint32_t)(i + 1), (uint32_t)plans.size(), user);
+    }
+    if (m.tied) output_ = embd_;
+    CU(cudaStreamSynchronize(stream_));
+    RET_IF(alloc_runtime());
+    loaded_ = true;
+    return {};
+}
+
+Status Engine::alloc_runtime() {
+    const ModelMeta& m = meta_;
+    const int hd = m.head_dim, L = m.n_layers;
+    max_seq_ = m.context_length;
+    attn_splits_ = attn_decode_splits(n_kv_l_, max_seq_, sm_count_);
+    const size_t kv_elems = (size_t)L * 2 * n_kv_l_ * max_seq_ * hd;
+    const int half = hd / 2;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t o_kv = take(kv_elems * 2);
+    const size_t o_cos = take((size_t)max_seq_ * half * 4), o_sin = take((size_t)max_seq_ * half * 4);
+    const size_t o_x = take((size_t)m.dim * 4);
+    const size_t o_q = take((size_t)n_heads_l_ * hd * 4), o_att = take((size_t)n_heads_l_ * hd * 4);
+    const size_t o_h = take((size_t)m.ffn / tp_size_ * 4), o_lg = take((size_t)m.vocab * 4);
+    const size_t o_ti = take(64), o_to = take(64), o_pos = take(64), o_err = take(64);
+    const size_t o_hist = take((size_t)max_seq_ * 4 + 64);
+    const size_t o_part = take(attn_decode_partial_floats(n_heads_l_, n_kv_l_, hd, attn_splits_) * 4);
+    const size_t o_cnt = take((size_t)n_kv_l_ * 4);
+    rt_size_ = off;
+    cudaError_t ce = cudaMalloc(&rt_, rt_size_);
+    if (ce != cudaSuccess) {
+        rt_ = nullptr;
+        return err(TPTC_ERR_OOM, "KV cache / runtime buffers need " + std::to_string(rt_size_ >> 20) +
+                                     " MiB: " + cuda_msg(ce, "cudaMalloc"));
+    }
+    device_bytes_ += rt_size_;
+    CU(cudaMemsetAsync(rt_, 0, rt_size_, stream_));
+    kv_ = reinterpret_cast<__half*>(rt_ + o_kv);
+    rope_cos_ = reinterpret_cast<float*>(rt_ + o_cos);
+    rope_sin_ = reinterpret_cast<float*>(rt_ + o_sin);
+    x_ = reinterpret_cast<float*>(rt_ + o_x);
+    qbuf_ = reinterpret_cast<float*>(rt_ + o_q);
+    attn_ = reinterpret_cast<float*>(rt_ + o_att);
+    h_ = reinterpret_cast<float*>(rt_ + o_h);
+    logits_ = reinterpret_cast<float*>(rt_ + o_lg);
+    tok_in_ = reinterpret_cast<uint32_t*>(rt_ + o_ti);
+    tok_out_ = reinterpret_cast<uint32_t*>(rt_ + o_to);
+    pos_ = reinterpret_cast<int*>(rt_ + o_pos);
+    err_ = reinterpret_cast<int*>(rt_ + o_err);
+    history_ = reinterpret_cast<uint32_t*>(rt_ + o_hist);
+    attn_partial_ = reinterpret_cast<float*>(rt_ + o_part);
+    attn_counters_ = reinterpret_cast<int*>(rt_ + o_cnt);
+
+    // candle quantized_llama precomput_freqs_cis: theta_i = 1/base^(2i/hd) (f32 powf),
+    // angle = pos * theta_i, cos/sin in f32 -- built on the host with the C library's powf,
+    // cosf and sinf (rope.wgsl:37-50 computes the same rotation per dispatch).
+    std::vector<float> c((size_t)max_seq_ * half), s((size_t)max_seq_ * half);
+    for (int p = 0; p < max_seq_; p++) {
+        float pf = (float)p;
+        if (m.rope_scale != 1.f) pf = pf / m.rope_scale;
+        for (int i = 0; i < half; i++) {
+            const float theta = 1.f / powf(m.rope_freq_base, (float)(2 * i) / (float)hd);
+            const float ang = pf * theta;
+            c[(size_t)p * half + i] = cosf(ang);
+            s[(size_t)p * half + i] = sinf(ang);
+        }
+    }
+    CU(cudaMemcpyAsync(rope_cos_, c.data(), c.size() * 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaMemcpyAsync(rope_sin_, s.data(), s.size() * 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaStreamSynchronize(stream_));
+    RET_IF(build_decode_graph(false, &graph_plain_));
+    RET_IF(build_decode_graph(true, &graph_chained_));
+    return {};
+}
+
+// One decode step: embed -> L x (QKV+RoPE+KV write, flash-decode, O+residual,
+// gate/up+SiLU, down+residual) -> norm + lm_head -> argmax.  All positions come from the
+// device scalar pos_, so one captured graph serves every step.
+Status Engine::enqueue_decode(cudaStream_t st, bool chained) {
+    const ModelMeta& m = meta_;
+    const int hd = m.head_dim;
+    const size_t layer_kv = (size_t)2 * n_kv_l_ * max_seq_ * hd;
+    CU(launch_embed_row(embd_, tok_in_, x_, st, false));
+    for (int l = 0; l < m.n_layers; l++) {
+        const LayerWeights& L = layers_[l];
+        __half* kc = kv_ + l * layer_kv;
+        __half* vc = kc + (size_t)n_kv_l_ * max_seq_ * hd;
+        GemvParams p = {};
+        p.K = m.dim;
+        p.err = err_;
+        p.eps = m.rms_eps;
+        // q | k | v with fused RMSNorm, RoPE and KV-cache write
+        p.nseg = 3;
+        const DevMatrix* qkv[3] = {&L.q, &L.k, &L.v};
+        int cta = 0;
+        for (int s = 0; s < 3; s++) {
+            p.seg[s] = GemvSeg{qkv[s]->main, qkv[s]->dplane, qkv[s]->type, qkv[s]->N, qkv[s]->main_row_bytes,
+                               qkv[s]->d_per_row, cta};
+            cta += ceil_div(qkv[s]->N, 8);
+        }
+        p.x = x_;
+        p.norm_w = L.attn_norm;
+        p.out = qbuf_;
+        p.kcache = kc;
+        p.vcache = vc;
+        p.rope_cos = rope_cos_;
+        p.rope_sin = rope_sin_;
+        p.pos = pos_;
+        p.hd = hd;
+        p.max_seq = max_seq_;
+        gemv_prepare(p);
+        CU(gemv_launch(p, EPI_QKV, st, pdl_));
+
+        AttnDecodeParams a = {};
+        a.q = qbuf_;
+        a.kcache = kc;
+        a.vcache = vc;
+        a.pos = pos_;
+        a.out = attn_;
+        a.partial = attn_partial_;
+        a.counters = attn_counters_;
+        a.n_heads = n_heads_l_;
+        a.n_kv = n_kv_l_;
+        a.hd = hd;
+        a.max_seq = max_seq_;
+        a.splits = attn_splits_;
+        a.scale = (float)(1.0 / sqrt((double)hd));
+        a.err = err_;
+        CU(launch_attn_decode(a, st, pdl_));
+
+        GemvParams o = {};
+        o.K = n_heads_l_ * hd;
+        o.err = err_;
+        o.nseg = 1;
+        o.seg[0] = GemvSeg{L.o.main, L.o.dplane, L.o.type, L.o.N, L.o.main_row_bytes, L.o.d_per_row, 0};
+        o.x = attn_;
+        if (tp_) {
+            // row-parallel: partial sums into h-sized scratch, then allreduce into x
+            o.out = tp_->partial(m.dim);
+            gemv_prepare(o);
+            CU(gemv_launch(o, EPI_STORE, st, pdl_));
+            RET_IF(tp_->allreduce_add(o.out, x_, m.dim, st));
+        } else {
+            o.out = x_;
+            gemv_prepare(o);
+            CU(gemv_launch(o, EPI_RESID, st, pdl_));
+        }
+
+        GemvParams g = {};
+        g.K = m.dim;
+        g.err = err_;
+        g.eps = m.rms_eps;
+        g.nseg = 2;
+        g.paired = 1;
+        g.seg[0] = GemvSeg{L.gate.main, L.gate.dplane, L.gate.type, L.gate.N, L.gate.main_row_bytes, L.gate.d_per_row, 0};
+        g.seg[1] = GemvSeg{L.up.main, L.up.dplane, L.up.type, L.up.N, L.up.main_row_bytes, L.up.d_per_row, 0};
+        g.x = x_;
+        g.norm_w = L.ffn_norm;
+        g.out = h_;
+        gemv_prepare(g);
+        CU(gemv_launch(g, EPI_GLU, st, pdl_));
+
+        GemvParams d = {};
+        d.K = m.ffn / tp_size_;
+        d.err = err_;
+        d.nseg = 1;
+        d.seg[0] = GemvSeg{L.down.main, L.down.dplane, L.down.type, L.down.N, L.down.main_row_bytes, L.down.d_per_row, 0};
+        d.x = h_;
+        if (tp_) {
+            d.out = tp_->partial(m.dim);
+            gemv_prepare(d);
+            CU(gemv_launch(d, EPI_STORE, st, pdl_));
+            RET_IF(tp_->allreduce_add(d.out, x_, m.dim, st));
+        } else {
+            d.out = x_;
+            gemv_prepare(d);
+            CU(gemv_launch(d, EPI_RESID, st, pdl_));
+        }
+    }
+    GemvParams h = {};
+    h.K = m.dim;
+    h.err = err_;
+    h.eps = m.rms_eps;
+    h.nseg = 1;
+    h.seg[0] = GemvSeg{output_.main, output_.dplane, output_.type, output_.N, output_.main_row_bytes, output_.d_per_row, 0};
+    h.x = x_;
+    h.norm_w = out_norm_;
+    h.out = logits_;
+    gemv_prepare(h);
+    CU(gemv_launch(h, EPI_STORE, st, pdl_));
+    CU(launch_argmax(logits_, m.vocab, tok_out_, chained ? tok_in_ : nullptr, chained ? pos_ : nullptr,
+                     chained ? history_ : nullptr, st, pdl_));
+    return {};
+}
+
+Status Engine::build_decode_graph(bool chained, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    Status s = enqueue_decode(stream_, chained);
+    cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+    if (!s.ok()) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+    }
+    if (ce != cudaSuccess) return err(TPTC_ERR_CUDA, cuda_msg(ce, "cudaStreamEndCapture"));
+    ce = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return err(TPTC_ERR_CUDA, cuda_msg(ce, "cudaGraphInstantiate"));
+    return {};
+}
+
+Status Engine::check_err() {
+    CU(cudaMemcpyAsync(h_err_, err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    CU(cudaStreamSynchronize(stream_));
+    if (*h_err_ != 0) {
+        const int code = *h_err_;
+        cudaMemsetAsync(err_, 0, sizeof(int), stream_);
+        cudaStreamSynchronize(stream_);
+        return err(code == TPTC_ERR_TIMEOUT ? TPTC_ERR_TIMEOUT : TPTC_ERR_CUDA,
+                   "a device-side bounded wait gave up (status " + std::to_string(code) + ")");
+    }
+    return {};
+}
+
+Status Engine::sync() {
+    CU(cudaStreamSynchronize(stream_));
+    return check_err();
+}
+
+Status Engine::kv_reset() {
+    cached_tokens_.clear();
+    return {};
+}
+
+int common_prefix_len(const uint32_t* cached, int n_cached, const uint32_t* ids, int n) {
+    int i = 0;
+    const int lim = std::min(n, n_cached);
+    while (i < lim && cached[i] == ids[i]) i++;
+    return i;
+}
+
+int Engine::prefix_len(const uint32_t* ids, int n) const {
+    return common_prefix_len(cached_tokens_.data(), (int)cached_tokens_.size(), ids, n);
+}
+
+Status Engine::decode(uint32_t id, int pos, float* logits, uint32_t* argmax) {
+    if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
+    if (id >= (uint32_t)meta_.vocab) return err(TPTC_ERR_ARG, "token id out of range");
+    if (pos < 0 || pos >= max_seq_) return err(TPTC_ERR_ARG, "position outside the context window");
+    if (pos != (int)cached_tokens_.size())
+        return err(TPTC_ERR_ARG, "decode position must equal the KV length (" + std::to_string(cached_tokens_.size()) + ")");
+    CU(cudaSetDevice(device_));
+    h_tok_[0] = id;
+    h_pos_[0] = pos;
+    CU(cudaMemcpyAsync(tok_in_, h_tok_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaMemcpyAsync(pos_, h_pos_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaGraphLaunch(graph_plain_, stream_));
+    if (logits) CU(cudaMemcpyAsync(logits, logits_, (size_t)meta_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    if (argmax) CU(cudaMemcpyAsync(h_tok_ + 1, tok_out_, 4, cudaMemcpyDeviceToHost, stream_));
+    RET_IF(sync());
+    if (argmax) *argmax = h_tok_[1];
+    cached_tokens_.push_back(id);
+    return {};
+}
+
+Status Engine::decode_greedy(uint32_t id, int pos, int n, uint32_t* out_ids) {
+    if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
+    if (n <= 0) return {};
+    if (id >= (uint32_t)meta_.vocab) return err(TPTC_ERR_ARG, "token id out of range");
+    if (pos < 0 || pos + n > max_seq_) return err(TPTC_ERR_ARG, "steps run past the context window");
+    if (pos != (int)cached_tokens_.size()) return err(TPTC_ERR_ARG, "decode position must equal the KV length");
+    CU(cudaSetDevice(device_));
+    h_tok_[0] = id;
+    h_pos_[0] = pos;
+    CU(cudaMemcpyAsync(tok_in_, h_tok_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaMemcpyAsync(pos_, h_pos_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaEventRecord(ev0_, stream_));
+    for (int i = 0; i < n; i++) CU(cudaGraphLaunch(graph_chained_, stream_));
+    CU(cudaEventRecord(ev1_, stream_));
+    std::vector<uint32_t> toks(n);
+    CU(cudaMemcpyAsync(toks.data(), history_ + pos, (size_t)n * 4, cudaMemcpyDeviceToHost, stream_));
+    RET_IF(sync());
+    float ms = 0.f;
+    CU(cudaEventElapsedTime(&ms, ev0_, ev1_));
+    last_device_ms = ms;
+    if (out_ids) memcpy(out_ids, toks.data(), (size_t)n * 4);
+    cached_tokens_.push_back(id);
+    for (int i = 0; i + 1 < n; i++) cached_tokens_.push_back(toks[i]);
+    return {};
+}
+
+Status Engine::prefill(const uint32_t* ids, int n, int start_pos, float* last_logits) {
+    if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
+    if (n <= 0) return err(TPTC_ERR_ARG, "prefill of zero tokens");
+    if (start_pos != (int)cached_tokens_.size())
+        return err(TPTC_ERR_ARG, "start_pos must equal the KV length (" + std::to_string(cached_tokens_.size()) + ")");
+    if (start_pos + n > max_seq_) return err(TPTC_ERR_ARG, "prompt runs past the context window");
+    for (int i = 0; i < n; i++)
+        if (ids[i] >= (uint32_t)meta_.vocab) return err(TPTC_ERR_ARG, "token id out of range");
+    CU(cudaSetDevice(device_));
+    CU(cudaEventRecord(ev0_, stream_));
+    RET_IF(run_prefill_batched(ids, n, start_pos, last_logits));
+    CU(cudaEventRecord(ev1_, stream_));
+    CU(cudaEventSynchronize(ev1_));
+    float ms = 0.f;
+    CU(cudaEventElapsedTime(&ms, ev0_, ev1_));
+    last_device_ms = ms;
+    return {};
+}
+
+// ---- LlmEngine::infer over token ids (wgpu_engine.rs:165-334, candle_engine.rs:205-334)
+
+namespace {
+
+// candle LogitsProcessor with a temperature: softmax(logits / T), optional top-p nucleus,
+// then one draw.  The draw uses std::mt19937_64 seeded from params.seed; candle draws from
+// rand's StdRng, so sampled (non-greedy) streams are not bit-identical to the reference.
+uint32_t sample_host(std::vector<float>& lg, float temperature, float top_p, std::mt19937_64& rng) {
+    const int n = (int)lg.size();
+    if (temperature <= 0.f) {
+        int best = 0;
+        for (int i = 1; i < n; i++)
+            if (!(lg[i] < lg[best])) best = i;
+        return (uint32_t)best;
+    }
+    float mx = -INFINITY;
+    for (float v : lg) mx = std::max(mx, v / temperature);
+    std::vector<float> pr(n);
+    double sum = 0;
+    for (int i = 0; i < n; i++) {
+        pr[i] = expf(lg[i] / temperature - mx);
+        sum += pr[i];
+    }
+    for (auto& v : pr) v = (float)(v / sum);
+    if (top_p > 0.f && top_p < 1.f) {
+        std::vector<int> idx(n);
+        for (int i = 0; i < n; i++) idx[i] = i;
+        std::sort(idx.begin(), idx.end(), [&](int a, int b) { return pr[a] > pr[b]; });
+        float cum = 0.f;
+        for (int i : idx) {
+            if (cum >= top_p) pr[i] = 0.f;
+            cum += pr[i];
+        }
+    }
+    double tot = 0;
+    for (float v : pr) tot += v;
+    std::uniform_real_distribution<double> u(0.0, tot);
+    double r = u(rng), acc = 0;
+    for (int i = 0; i < n; i++) {
+        acc += pr[i];
+        if (r < acc && pr[i] > 0.f) return (uint32_t)i;
+    }
+    for (int i = n - 1; i >= 0; i--)
+        if (pr[i] > 0.f) return (uint32_t)i;
+    return 0;
+}
+
+// candle_engine.rs:87-101 -- every entry of `seen` (duplicates included).
+void repeat_penalty(std::vector<float>& lg, const std::vector<uint32_t>& seen, float penalty) {
+    if (fabsf(penalty - 1.f) < 1.1920929e-7f) return;
+    for (uint32_t id : seen) {
+        if (id < lg.size()) {
+            if (lg[id] >= 0.f) lg[id] /= penalty;
+            else lg[id] *= penalty;
+        }
+    }
+}
+
+}  // namespace
+
+Status Engine::infer(const uint32_t* prompt, int n, const tptc_infer_params& p, tptc_token_cb cb, void* user) {
+    using clk = std::chrono::steady_clock;
+    if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
+    if (!cb) return err(TPTC_ERR_ARG, "on_token callback is required");
+    CU(cudaSetDevice(device_));
+    std::vector<uint32_t> tokens(prompt, prompt + std::max(0, n));
+    for (uint32_t t : tokens)
+        if (t >= (uint32_t)meta_.vocab) return err(TPTC_ERR_ARG, "token id out of range");
+    // truncate from the front (wgpu_engine.rs:188-197)
+    const int max_prompt = std::max(0, meta_.context_length - (int)p.max_tokens);
+    if ((int)tokens.size() > max_prompt) {
+        tokens.erase(tokens.begin(), tokens.begin() + ((int)tokens.size() - max_prompt));
+        cached_tokens_.clear();
+    }
+    if (tokens.empty()) return err(TPTC_ERR_ARG, "prompt is empty after tokenization");
+    // prefix reuse (wgpu_engine.rs:199-206); the last prompt token is always recomputed so
+    // that its logits exist (the reference reads stale logits when the whole prompt hits).
+    int prefix = prefix_len(tokens.data(), (int)tokens.size());
+    if (prefix >= (int)tokens.size()) prefix = (int)tokens.size() - 1;
+    cached_tokens_.resize(prefix);
+
+    const bool greedy = p.temperature <= 0.f;
+    const bool penalty = fabsf(p.repeat_penalty - 1.f) >= 1.1920929e-7f;
+    std::mt19937_64 rng(p.seed);
+    std::vector<float> lg(meta_.vocab);
+
+    auto t0 = clk::now();
+    RET_IF(prefill(tokens.data() + prefix, (int)tokens.size() - prefix, prefix, lg.data()));
+    auto t1 = clk::now();
+    last_prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+    last_n_prompt = (int)tokens.size() - prefix;
+    repeat_penalty(lg, tokens, p.repeat_penalty);
+    uint32_t next = sample_host(lg, p.temperature, p.top_p, rng);
+
+    int pos = (int)tokens.size();
+    uint32_t generated = 0;
+    auto td = clk::now();
+    for (;;) {
+        if (p.eos_token_id >= 0 && next == (uint32_t)p.eos_token_id) break;
+        if (generated >= p.max_tokens) break;
+        if (pos >= meta_.context_length) break;
+        if (cb(next, 0, user) != 0) {
+            cb(0, 1, user);
+            last_decode_ms = std::chrono::duration<double, std::milli>(clk::now() - td).count();
+            last_n_generated = (int)generated;
+            return err(TPTC_ERR_CANCELLED, "inference cancelled by the token callback");
+        }
+        tokens.push_back(next);
+        generated++;
+        if (greedy && !penalty) {
+            uint32_t am;
+            RET_IF(decode(next, pos, nullptr, &am));
+            next = am;
+        } else {
+            RET_IF(decode(next, pos, lg.data(), nullptr));
+            repeat_penalty(lg, tokens, p.repeat_penalty);
+            next = sample_host(lg, p.temperature, p.top_p, rng);
+        }
+        pos++;
+    }
+    last_decode_ms = std::chrono::duration<double, std::milli>(clk::now() - td).count();
+    last_n_generated = (int)generated;
+    cb(0, 1, user);
+    return {};
+}
+
+void Engine::info(tptc_model_info* out) const {
+    memset(out, 0, sizeof(*out));
+    std::string name = meta_.name;
+    {
+        size_t sl = path_.find_last_of('/');
+        std::string stem = sl == std::string::npos ? path_ : path_.substr(sl + 1);
+        size_t dot = stem.rfind('.');
+        if (dot != std::string::npos) stem = stem.substr(0, dot);
+        name = stem.empty() ? name : stem;
+    }
+    strncpy(out->name, name.c_str(), sizeof(out->name) - 1);
+    strncpy(out->path, path_.c_str(), sizeof(out->path) - 1);
+    out->size_bytes = weight_bytes_;
+    std::string be = "cuda-sm100a";
+    if (tp_size_ > 1) be += "-tp" + std::to_string(tp_size_);
+    strncpy(out->backend, be.c_str(), sizeof(out->backend) - 1);
+    strncpy(out->architecture, meta_.architecture.c_str(), sizeof(out->architecture) - 1);
+    out->context_length = meta_.context_length;
+    out->n_layers = meta_.n_layers;
+    out->n_heads = meta_.n_heads;
+    out->n_kv_heads = meta_.n_kv_heads;
+    out->head_dim = meta_.head_dim;
+    out->dim = meta_.dim;
+    out->ffn = meta_.ffn;
+    out->vocab = meta_.vocab;
+    out->rope_freq_base = meta_.rope_freq_base;
+    out->rope_scale = meta_.rope_scale;
+    out->rms_eps = meta_.rms_eps;
+    out->tied_embeddings = meta_.tied ? 1 : 0;
+    out->tp_rank = tp_rank_;
+    out->tp_size = tp_size_;
+    out->device_bytes = device_bytes_ + pf_size_;
+}
+
+}  // namespace tptc

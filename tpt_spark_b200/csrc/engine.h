@@ -1,0 +1,126 @@
+// engine.h -- the CUDA engine behind the C ABI: the counterpart of the reference's WgpuEngine
+// (src-tauri/src/engine/wgpu_engine.rs) + GpuModel + KvCache (wgpu_kvcache.rs) + loader
+// (wgpu_loader.rs), implementing LlmEngine's semantics (engine/mod.rs:62-82).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "gguf.h"
+#include "tptc.h"
+
+namespace tptc {
+
+// GgufMeta (wgpu_loader.rs:41-67), the fields the dense Llama path uses.
+struct ModelMeta {
+    std::string architecture = "llama";
+    std::string name;
+    int context_length = 4096, n_layers = 0, n_heads = 0, n_kv_heads = 0, head_dim = 0, dim = 0, ffn = 0, vocab = 0;
+    float rope_freq_base = 10000.f, rope_scale = 1.f, rms_eps = 1e-5f;
+    bool tied = false;
+};
+
+struct LayerWeights {
+    DevMatrix q, k, v, o, gate, up, down;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+};
+
+struct Tp;  // tensor-parallel communicator (tp.cpp)
+
+// KvCache::common_prefix_len (wgpu_kvcache.rs:63-69): leading ids shared by both sequences.
+int common_prefix_len(const uint32_t* cached, int n_cached, const uint32_t* ids, int n);
+
+class Engine {
+   public:
+    Engine(int device, int tp_rank, int tp_size);
+    ~Engine();
+    Status init(const void* nccl_uid);
+    Status load(const std::string& path, tptc_progress_cb cb, void* user);
+    void unload();
+    bool loaded() const { return loaded_; }
+    void info(tptc_model_info* out) const;
+
+    Status kv_reset();
+    int kv_len() const { return (int)cached_tokens_.size(); }
+    void kv_truncate(int n) { cached_tokens_.resize(n); }
+    int prefix_len(const uint32_t* ids, int n) const;
+
+    Status prefill(const uint32_t* ids, int n, int start_pos, float* last_logits);
+    Status decode(uint32_t id, int pos, float* logits, uint32_t* argmax);
+    Status decode_greedy(uint32_t id, int pos, int n, uint32_t* out_ids);
+    Status infer(const uint32_t* prompt, int n, const tptc_infer_params& p, tptc_token_cb cb, void* user);
+
+    double last_prefill_ms = 0, last_decode_ms = 0, last_device_ms = 0;
+    int last_n_prompt = 0, last_n_generated = 0;
+    std::string last_error;
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+   private:
+    Status alloc_runtime();
+    Status build_decode_graph(bool chained, cudaGraphExec_t* out);
+    Status enqueue_decode(cudaStream_t st, bool chained);
+    Status enqueue_layer_prefill(int l, int n, int start_pos);
+    Status run_prefill_batched(const uint32_t* ids, int n, int start_pos, float* last_logits);
+    Status check_err();
+    Status sync();
+
+    int device_, tp_rank_, tp_size_;
+    int sm_count_ = 148;
+    bool loaded_ = false;
+    bool pdl_ = true;
+    cudaStream_t stream_ = nullptr;
+    ModelMeta meta_;
+    std::string path_;
+    uint64_t file_bytes_ = 0, weight_bytes_ = 0, device_bytes_ = 0;
+
+    // device memory
+    uint8_t* arena_ = nullptr;     // weights
+    size_t arena_size_ = 0;
+    uint8_t* rt_ = nullptr;        // runtime buffers (KV cache, activations, scratch)
+    size_t rt_size_ = 0;
+    std::vector<LayerWeights> layers_;
+    DevMatrix embd_, output_;
+    float* out_norm_ = nullptr;
+    __half* kv_ = nullptr;  // [L][2][n_kv_local][max_seq][hd]
+    int max_seq_ = 0;
+    int n_heads_l_ = 0, n_kv_l_ = 0;  // per-rank heads (TP)
+    float* rope_cos_ = nullptr;
+    float* rope_sin_ = nullptr;
+    float* x_ = nullptr;        // residual stream [dim]
+    float* qbuf_ = nullptr;     // [n_heads_l * hd]
+    float* attn_ = nullptr;     // [n_heads_l * hd]
+    float* h_ = nullptr;        // [ffn_l]
+    float* logits_ = nullptr;   // [vocab]
+    uint32_t* tok_in_ = nullptr;
+    uint32_t* tok_out_ = nullptr;
+    uint32_t* history_ = nullptr;  // [max_seq]
+    int* pos_ = nullptr;
+    int* err_ = nullptr;
+    float* attn_partial_ = nullptr;
+    int* attn_counters_ = nullptr;
+    int attn_splits_ = 1;
+    // prefill buffers (allocated on demand for the chunk size)
+    uint8_t* pf_ = nullptr;
+    size_t pf_size_ = 0;
+    int pf_chunk_ = 0;
+
+    // pinned host staging
+    uint32_t* h_tok_ = nullptr;
+    int* h_pos_ = nullptr;
+    int* h_err_ = nullptr;
+
+    cudaGraphExec_t graph_plain_ = nullptr, graph_chained_ = nullptr;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    std::vector<uint32_t> cached_tokens_;  // KvCache::cached_tokens (wgpu_kvcache.rs:21-23)
+    std::unique_ptr<Tp> tp_;
+};
+
+}  // namespace tptc

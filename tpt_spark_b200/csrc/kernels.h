@@ -1,0 +1,49 @@
+// kernels.h -- host launchers of the small kernels (quant.cu, attn_decode.cu, misc.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gemv.cuh"
+
+namespace tptc {
+
+// quant.cu
+cudaError_t launch_dequant_raw(int type, const void* blocks, int64_t n, float* out, cudaStream_t st);
+cudaError_t launch_quant_q8k(const float* x, int64_t k, void* out, cudaStream_t st);
+cudaError_t launch_quant_q80(const float* x, int64_t k, void* out, cudaStream_t st);
+// Raw GGUF rows [N, K] (device) -> device layout of `m` (main / dplane already allocated).
+cudaError_t launch_repack(const uint8_t* raw, const DevMatrix& m, cudaStream_t st);
+// Device-layout rows [row0, row0+rows) of `m` -> dense f16 [rows, K] (prefill operand).
+cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st);
+
+// attn_decode.cu
+struct AttnDecodeParams {
+    const float* q;        // [n_heads * hd] (rope applied)
+    const __half* kcache;  // this layer, [n_kv][max_seq][hd]
+    const __half* vcache;
+    const int* pos;        // device scalar: the query position (keys 0..pos)
+    float* out;            // [n_heads * hd]
+    float* partial;        // scratch [n_kv][splits][group][2 + hd]
+    int* counters;         // scratch [n_kv], zero between launches
+    int n_heads, n_kv, hd, max_seq, splits;
+    float scale;           // 1/sqrt(hd)
+    int* err;
+};
+int attn_decode_splits(int n_kv, int max_seq, int sm_count);
+size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits);
+cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl);
+
+// misc.cu
+// x[dim] = dequantised row `tok` of token_embd (device layout), token read from *tok_ptr.
+cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl);
+// argmax over logits[n] (ties -> highest index, candle sample_argmax); writes *out_tok;
+// when next_tok/pos are non-null also stores the token as the next step's input and
+// increments *pos (device-chained greedy decode).
+cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_t* next_tok, int* pos,
+                          uint32_t* history, cudaStream_t st, bool pdl);
+
+cudaError_t kernels_init_device();
+
+}  // namespace tptc

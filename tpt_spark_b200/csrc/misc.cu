@@ -1,0 +1,131 @@
+// misc.cu -- token embedding row, on-device argmax, per-device kernel setup.
+#include <algorithm>
+
+#include "kernels.h"
+#include "quant.cuh"
+
+namespace tptc {
+
+cudaError_t attn_init_device();
+cudaError_t prefill_init_device();
+
+namespace {
+
+// candle dequantises token_embd to f32 at load and index_selects a row; here one row is
+// dequantised on the fly (bit-identical values) into the residual stream x.
+// Replaces the reference's whole-table dequant + row copy (wgpu_engine.rs:235-242,364-368).
+__global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok_ptr, float* __restrict__ x) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t row = *tok_ptr;
+    const int K = emb.K;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) {
+        float v;
+        if (emb.type == TPTC_TYPE_Q4_K) {
+            v = q4k_elem(emb.main + row * emb.main_row_bytes + (i / QK_K) * Q4K_BYTES, i % QK_K);
+        } else if (emb.type == TPTC_TYPE_Q6_K) {
+            v = q6k_elem(emb.main + row * emb.main_row_bytes + (i / QK_K) * Q6K_MAIN,
+                         h2f(emb.dplane[row * emb.d_per_row + i / QK_K]), i % QK_K);
+        } else if (emb.type == TPTC_TYPE_Q8_0) {
+            v = __fmul_rn((float)(int8_t)emb.main[row * emb.main_row_bytes + i],
+                          h2f(emb.dplane[row * emb.d_per_row + i / QK8_0]));
+        } else {
+            v = h2f(reinterpret_cast<const uint16_t*>(emb.main + row * emb.main_row_bytes)[i]);
+        }
+        x[i] = v;
+    }
+}
+
+// Greedy pick, candle LogitsProcessor::sample_argmax: Iterator::max_by(f32::total_cmp)
+// returns the LAST of equal maxima, so ties go to the highest index.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, uint32_t* out_tok,
+                                                      uint32_t* next_tok, int* pos, uint32_t* history) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -INFINITY;
+    int bi = -1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = logits[i];
+        if (bi < 0 || v > best || (v == best && i > bi)) {
+            best = v;
+            bi = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (i2 >= 0 && (bi < 0 || v2 > best || (v2 == best && i2 > bi))) {
+            best = v2;
+            bi = i2;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x / 32;
+        best = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : -1;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (i2 >= 0 && (bi < 0 || v2 > best || (v2 == best && i2 > bi))) {
+                best = v2;
+                bi = i2;
+            }
+        }
+        if (lane == 0) {
+            const uint32_t t = bi < 0 ? 0u : (uint32_t)bi;
+            *out_tok = t;
+            if (next_tok) *next_tok = t;
+            if (pos) {
+                if (history) history[*pos] = t;  // token generated after position *pos
+                *pos += 1;
+            }
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::max(1, std::min(16, emb.K / 256)));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, embed_row_kernel, emb, tok_ptr, x);
+}
+
+cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_t* next_tok, int* pos,
+                          uint32_t* history, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(1024);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, n, out_tok, next_tok, pos, history);
+}
+
+cudaError_t kernels_init_device() {
+    cudaError_t e = gemv_init_device();
+    if (e != cudaSuccess) return e;
+    e = attn_init_device();
+    if (e != cudaSuccess) return e;
+    return prefill_init_device();
+}
+
+}  // namespace tptc

@@ -1,0 +1,143 @@
+// quant.cu -- standalone block kernels: dequantisation of raw GGUF blocks (the reference's
+// dequant_q4k/q6k/q8/f16.wgsl entry points, with the GGUF layout of gguf-py rather than the
+// reference's wrong Q4_K nibble split), activation quantisation to Q8_K / Q8_0, the load-time
+// repack into the device layout, and the dense f16 expansion used by the prefill GEMM.
+#include "kernels.h"
+#include "quant.cuh"
+
+namespace tptc {
+
+namespace {
+
+// One thread per element; raw GGUF blocks.
+__global__ void dequant_raw_kernel(int type, const uint8_t* __restrict__ blocks, int64_t n, float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float v;
+    if (type == TPTC_TYPE_Q4_K) {
+        v = q4k_elem(blocks + (i / QK_K) * Q4K_BYTES, (int)(i % QK_K));
+    } else if (type == TPTC_TYPE_Q6_K) {
+        const uint8_t* blk = blocks + (i / QK_K) * Q6K_BYTES;
+        v = q6k_elem(blk, h2f(blk[208] | (blk[209] << 8)), (int)(i % QK_K));
+    } else if (type == TPTC_TYPE_Q8_0) {
+        const uint8_t* blk = blocks + (i / QK8_0) * Q80_BYTES;
+        v = __fmul_rn((float)(int8_t)blk[2 + i % QK8_0], h2f(blk[0] | (blk[1] << 8)));
+    } else if (type == TPTC_TYPE_F16) {
+        v = h2f(reinterpret_cast<const uint16_t*>(blocks)[i]);
+    } else {
+        v = reinterpret_cast<const float*>(blocks)[i];
+    }
+    out[i] = v;
+}
+
+// One warp per 256-element block.
+__global__ void quant_q8k_kernel(const float* __restrict__ x, int64_t nb, BlockQ8K* __restrict__ out) {
+    const int64_t b = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (b >= nb) return;
+    float v[8];
+    const float4* src = reinterpret_cast<const float4*>(x + b * QK_K + lane * 8);
+    const float4 a = src[0], c = src[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    q8k_quant_warp(v, out[b].qs, out[b].bsums, &out[b].d, lane);
+}
+
+// One warp per 32-element block; output 34-byte blocks (f16 d, int8 qs[32]).
+__global__ void quant_q80_kernel(const float* __restrict__ x, int64_t nb, uint8_t* __restrict__ out) {
+    const int64_t b = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (b >= nb) return;
+    float d;
+    const int8_t q = q80_quant_warp(x[b * QK8_0 + lane], d);
+    uint8_t* blk = out + b * Q80_BYTES;
+    blk[2 + lane] = (uint8_t)q;
+    if (lane == 0) {
+        const uint16_t h = f2h(d);
+        blk[0] = (uint8_t)(h & 0xff);
+        blk[1] = (uint8_t)(h >> 8);
+    }
+}
+
+// Repack one super-block (Q6_K) or one 32-block (Q8_0) per thread; Q4_K / F16 copy bytes.
+__global__ void repack_kernel(const uint8_t* __restrict__ raw, int type, int64_t nblocks, uint8_t* __restrict__ main,
+                              uint16_t* __restrict__ dplane) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    if (type == TPTC_TYPE_Q6_K) {
+        const uint8_t* src = raw + b * Q6K_BYTES;
+        uint8_t* dst = main + b * Q6K_MAIN;
+        for (int i = 0; i < Q6K_MAIN; i++) dst[i] = src[i];
+        dplane[b] = (uint16_t)(src[208] | (src[209] << 8));
+    } else if (type == TPTC_TYPE_Q8_0) {
+        const uint8_t* src = raw + b * Q80_BYTES;
+        uint8_t* dst = main + b * 32;
+        for (int i = 0; i < 32; i++) dst[i] = src[2 + i];
+        dplane[b] = (uint16_t)(src[0] | (src[1] << 8));
+    }
+}
+
+// Device layout -> dense f16, one thread per 8 consecutive elements of a row.
+__global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, __half* __restrict__ out) {
+    const int64_t per_row = m.K / 8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= per_row * rows) return;
+    const int r = (int)(i / per_row), k0 = (int)(i % per_row) * 8;
+    const int64_t row = row0 + r;
+    __align__(16) __half v[8];
+    if (m.type == TPTC_TYPE_F16) {
+        *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(m.main + row * m.main_row_bytes + k0 * 2);
+    } else if (m.type == TPTC_TYPE_Q4_K) {
+        const uint8_t* blk = m.main + row * m.main_row_bytes + (k0 / QK_K) * Q4K_BYTES;
+        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q4k_elem(blk, (k0 + j) % QK_K));
+    } else if (m.type == TPTC_TYPE_Q6_K) {
+        const uint8_t* blk = m.main + row * m.main_row_bytes + (k0 / QK_K) * Q6K_MAIN;
+        const float d = h2f(m.dplane[row * m.d_per_row + k0 / QK_K]);
+        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q6k_elem(blk, d, (k0 + j) % QK_K));
+    } else {
+        const int8_t* q = reinterpret_cast<const int8_t*>(m.main + row * m.main_row_bytes + k0);
+        const float d = h2f(m.dplane[row * m.d_per_row + k0 / QK8_0]);
+        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(__fmul_rn((float)q[j], d));
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)r * m.K + k0) = *reinterpret_cast<const uint4*>(v);
+}
+
+}  // namespace
+
+cudaError_t launch_dequant_raw(int type, const void* blocks, int64_t n, float* out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int t = 256;
+    dequant_raw_kernel<<<(unsigned)ceil_div64(n, t), t, 0, st>>>(type, static_cast<const uint8_t*>(blocks), n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_q8k(const float* x, int64_t k, void* out, cudaStream_t st) {
+    const int64_t nb = k / QK_K;
+    if (nb <= 0) return cudaSuccess;
+    quant_q8k_kernel<<<(unsigned)ceil_div64(nb, 8), 256, 0, st>>>(x, nb, static_cast<BlockQ8K*>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_q80(const float* x, int64_t k, void* out, cudaStream_t st) {
+    const int64_t nb = k / QK8_0;
+    if (nb <= 0) return cudaSuccess;
+    quant_q80_kernel<<<(unsigned)ceil_div64(nb, 8), 256, 0, st>>>(x, nb, static_cast<uint8_t*>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack(const uint8_t* raw, const DevMatrix& m, cudaStream_t st) {
+    const int64_t n = (int64_t)m.N * m.K;
+    if (m.type == TPTC_TYPE_Q4_K || m.type == TPTC_TYPE_F16)
+        return cudaMemcpyAsync(m.main, raw, m.main_row_bytes * m.N, cudaMemcpyDeviceToDevice, st);
+    const int64_t nblocks = m.type == TPTC_TYPE_Q6_K ? n / QK_K : n / QK8_0;
+    repack_kernel<<<(unsigned)ceil_div64(nblocks, 256), 256, 0, st>>>(raw, m.type, nblocks, m.main, m.dplane);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st) {
+    const int64_t n = (int64_t)rows * (m.K / 8);
+    if (n <= 0) return cudaSuccess;
+    dequant_rows_f16_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, st>>>(m, row0, rows, out);
+    return cudaGetLastError();
+}
+
+}  // namespace tptc

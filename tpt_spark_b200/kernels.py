@@ -1,0 +1,63 @@
+"""Kernel-level entry points of libtptc over device memory.
+
+Device buffers are passed as raw pointers; tests and the benchmark allocate them with
+torch (plumbing only -- the arithmetic runs in libtptc's kernels).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from ._lib import check, lib
+
+F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+
+
+def _ptr(t) -> int:
+    return t if isinstance(t, int) else t.data_ptr()
+
+
+def dequant(ggml_type: int, d_blocks, n: int, d_out, stream: Optional[int] = None) -> None:
+    check(lib().tptc_dequant(ggml_type, _ptr(d_blocks), n, _ptr(d_out), stream))
+
+
+def quant_q8k(d_x, k: int, d_out, stream: Optional[int] = None) -> None:
+    check(lib().tptc_quant_q8k(_ptr(d_x), k, _ptr(d_out), stream))
+
+
+def quant_q80(d_x, k: int, d_out, stream: Optional[int] = None) -> None:
+    check(lib().tptc_quant_q80(_ptr(d_x), k, _ptr(d_out), stream))
+
+
+class Matrix:
+    """A weight matrix [N x K] in the engine's device layout, made from raw GGUF bytes."""
+
+    def __init__(self, ggml_type: int, raw: np.ndarray, N: int, K: int):
+        raw = np.ascontiguousarray(raw).view(np.uint8)
+        self._h = ctypes.c_void_p()
+        check(lib().tptc_matrix_create(ggml_type, raw.ctypes.data, 0, N, K, ctypes.byref(self._h)))
+        self.type, self.N, self.K = ggml_type, N, K
+
+    @property
+    def nbytes(self) -> int:
+        return lib().tptc_matrix_bytes(self._h)
+
+    def gemv(self, d_x, d_y, stream: Optional[int] = None) -> None:
+        check(lib().tptc_gemv(self._h, _ptr(d_x), _ptr(d_y), stream))
+
+    def block_dots(self, d_x, d_isum, d_msum=None, stream: Optional[int] = None) -> None:
+        check(lib().tptc_block_dots(self._h, _ptr(d_x), _ptr(d_isum), _ptr(d_msum) if d_msum is not None else None,
+                                    stream))
+
+    def close(self):
+        if self._h:
+            lib().tptc_matrix_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

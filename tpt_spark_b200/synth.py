@@ -1,0 +1,289 @@
+"""Synthetic GGUF models for tests and benchmarks.
+
+The benchmark configurations are random-init Llama-architecture decoders: linear weights
+drawn N(0, 0.02) from a seed, RMSNorm gains 1.0, quantised to GGUF Q4_K / Q6_K / Q8_0 or
+stored as F16.  There is no network and no checkpoint, so the files are generated here.
+
+The GGUF v3 container written by :func:`write_gguf` carries the metadata keys that the
+reference reads: ``general.architecture`` and the ``llama.*`` keys of
+src-tauri/src/engine/wgpu_loader.rs:305-406 (context_length, block_count, head_count,
+head_count_kv, embedding_length, vocab_size, rope.freq_base, feed_forward_length,
+layer_norm_rms_epsilon) plus ``llama.rope.dimension_count``, which candle's
+quantized_llama requires.  Tensor names follow llama.cpp (token_embd, blk.N.attn_q, ...),
+dims are stored innermost first ([K, N] for an N x K weight).  Block encoding and the
+random draw run in C (``csrc/synth.c`` -> ``lib/libtptsynth.so``).
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+import os
+import struct
+from typing import Callable, Dict, List, Optional, Tuple
+
+import numpy as np
+
+from ._build import lib_path
+
+F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+ALIGN = 32
+
+
+def type_bytes(t: int, n: int) -> int:
+    be, bb = BLOCK[t]
+    assert n % be == 0, (t, n)
+    return n // be * bb
+
+
+@dataclasses.dataclass(frozen=True)
+class ModelConfig:
+    """Shape and storage types of a synthetic Llama-architecture model."""
+
+    name: str
+    dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    ffn: int
+    vocab: int
+    rope_base: float
+    context_length: int
+    rms_eps: float = 1e-5
+    tied: bool = False
+    default_type: int = Q4_K
+    overrides: Tuple[Tuple[str, int], ...] = ()  # (tensor-kind, type), kinds below
+    embd_type: Optional[int] = None
+    output_type: Optional[int] = None
+    norm_std: float = 0.0  # 0: gains exactly 1.0 (the configs); >0: 1 + N(0, norm_std)
+    weight_std: float = 0.02
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+    def type_of(self, kind: str) -> int:
+        if kind.endswith("norm"):
+            return F32
+        if kind == "token_embd":
+            return self.embd_type if self.embd_type is not None else self.default_type
+        if kind == "output":
+            return self.output_type if self.output_type is not None else self.default_type
+        return dict(self.overrides).get(kind, self.default_type)
+
+    def tensors(self) -> List[Tuple[str, str, List[int]]]:
+        """(name, kind, ne) in file order; ne innermost first."""
+        d, hd = self.dim, self.head_dim
+        out = [("token_embd.weight", "token_embd", [d, self.vocab])]
+        for i in range(self.n_layers):
+            p = f"blk.{i}."
+            out += [
+                (p + "attn_norm.weight", "attn_norm", [d]),
+                (p + "attn_q.weight", "attn_q", [d, self.n_heads * hd]),
+                (p + "attn_k.weight", "attn_k", [d, self.n_kv_heads * hd]),
+                (p + "attn_v.weight", "attn_v", [d, self.n_kv_heads * hd]),
+                (p + "attn_output.weight", "attn_output", [self.n_heads * hd, d]),
+                (p + "ffn_norm.weight", "ffn_norm", [d]),
+                (p + "ffn_gate.weight", "ffn_gate", [d, self.ffn]),
+                (p + "ffn_up.weight", "ffn_up", [d, self.ffn]),
+                (p + "ffn_down.weight", "ffn_down", [self.ffn, d]),
+            ]
+        out.append(("output_norm.weight", "output_norm", [d]))
+        if not self.tied:
+            out.append(("output.weight", "output", [d, self.vocab]))
+        return out
+
+
+Q4_K_M = (("attn_v", Q6_K), ("ffn_down", Q6_K))
+
+# The five benchmark configurations (C1 is a single matrix, see GEMV_C1).
+CONFIGS: Dict[str, ModelConfig] = {
+    "c2_llama1b_q4km": ModelConfig(
+        "c2_llama1b_q4km", dim=2048, n_layers=16, n_heads=32, n_kv_heads=8, ffn=8192,
+        vocab=128256, rope_base=500000.0, context_length=2048, tied=True,
+        overrides=Q4_K_M, embd_type=Q6_K),
+    "c3_mistral7b_q8_0": ModelConfig(
+        "c3_mistral7b_q8_0", dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn=14336,
+        vocab=32000, rope_base=10000.0, context_length=4096, default_type=Q8_0),
+    "c4_phi3mini_f16": ModelConfig(
+        "c4_phi3mini_f16", dim=3072, n_layers=32, n_heads=32, n_kv_heads=32, ffn=8192,
+        vocab=32064, rope_base=10000.0, context_length=4096, default_type=F16),
+    "c5_llama8b_q4km": ModelConfig(
+        "c5_llama8b_q4km", dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, ffn=14336,
+        vocab=128256, rope_base=500000.0, context_length=9216, overrides=Q4_K_M,
+        embd_type=Q4_K, output_type=Q6_K),
+}
+
+# Small models with the same code paths, for parity tests that the CPU oracle finishes
+# in seconds.
+TINY: Dict[str, ModelConfig] = {
+    "tiny_q4km": ModelConfig(
+        "tiny_q4km", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=512,
+        rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
+        output_type=Q6_K, norm_std=0.1),
+    "tiny_q4km_tied": ModelConfig(
+        "tiny_q4km_tied", dim=256, n_layers=2, n_heads=4, n_kv_heads=1, ffn=768, vocab=384,
+        rope_base=500000.0, context_length=512, tied=True, overrides=Q4_K_M, embd_type=Q6_K),
+    "tiny_q8_0": ModelConfig(
+        "tiny_q8_0", dim=256, n_layers=2, n_heads=2, n_kv_heads=2, ffn=512, vocab=320,
+        rope_base=10000.0, context_length=512, default_type=Q8_0, norm_std=0.1),
+    "tiny_f16": ModelConfig(
+        "tiny_f16", dim=768, n_layers=2, n_heads=8, n_kv_heads=8, ffn=512, vocab=320,
+        rope_base=10000.0, context_length=512, default_type=F16, norm_std=0.1),
+}
+
+# C1: one Q4_K matrix [4096 out x 4096 in], W ~ N(0, 0.02), x ~ N(0, 1).
+GEMV_C1 = dict(N=4096, K=4096, type=Q4_K, w_std=0.02, x_std=1.0)
+
+
+def fnv1a64(s: str) -> int:
+    h = 0xCBF29CE484222325
+    for ch in s.encode():
+        h = ((h ^ ch) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+def tensor_seed(name: str, seed: int) -> int:
+    return fnv1a64(name) ^ (seed & 0xFFFFFFFFFFFFFFFF)
+
+
+_lib = None
+
+
+def synth_lib():
+    global _lib
+    if _lib is None:
+        path = lib_path("libtptsynth.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: run tpt_spark_b200._build.build()")
+        L = ctypes.CDLL(path)
+        L.sy_make_tensor.restype = ctypes.c_int64
+        L.sy_make_tensor.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int64, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]
+        L.sy_encode.restype = ctypes.c_int64
+        L.sy_encode.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+        L.sy_fill_normal.restype = None
+        L.sy_fill_normal.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_void_p]
+        _lib = L
+    return _lib
+
+
+def normal(seed: int, n: int, std: float = 1.0, mean: float = 0.0, start: int = 0) -> np.ndarray:
+    x = np.empty(n, np.float32)
+    synth_lib().sy_fill_normal(seed, start, n, mean, std, x.ctypes.data)
+    return x
+
+
+def encode(t: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    out = np.empty(type_bytes(t, x.size), np.uint8)
+    synth_lib().sy_encode(t, x.ctypes.data, x.size, out.ctypes.data)
+    return out
+
+
+def make_tensor(t: int, seed: int, n: int, std: float, mean: float = 0.0) -> np.ndarray:
+    out = np.empty(type_bytes(t, n), np.uint8)
+    scratch = np.empty(n, np.float32)
+    synth_lib().sy_make_tensor(t, seed, n, mean, std, scratch.ctypes.data, out.ctypes.data)
+    return out
+
+
+def _gguf_str(s: str) -> bytes:
+    b = s.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def _kv(key: str, vtype: int, val) -> bytes:
+    out = _gguf_str(key) + struct.pack("<I", vtype)
+    if vtype == 4:
+        out += struct.pack("<I", val)
+    elif vtype == 6:
+        out += struct.pack("<f", val)
+    elif vtype == 8:
+        out += _gguf_str(val)
+    else:
+        raise ValueError(vtype)
+    return out
+
+
+def metadata(cfg: ModelConfig) -> List[bytes]:
+    a = "llama"
+    return [
+        _kv("general.architecture", 8, a),
+        _kv("general.name", 8, cfg.name),
+        _kv("general.alignment", 4, ALIGN),
+        _kv(f"{a}.context_length", 4, cfg.context_length),
+        _kv(f"{a}.embedding_length", 4, cfg.dim),
+        _kv(f"{a}.block_count", 4, cfg.n_layers),
+        _kv(f"{a}.feed_forward_length", 4, cfg.ffn),
+        _kv(f"{a}.attention.head_count", 4, cfg.n_heads),
+        _kv(f"{a}.attention.head_count_kv", 4, cfg.n_kv_heads),
+        _kv(f"{a}.rope.dimension_count", 4, cfg.head_dim),
+        _kv(f"{a}.rope.freq_base", 6, cfg.rope_base),
+        _kv(f"{a}.attention.layer_norm_rms_epsilon", 6, cfg.rms_eps),
+        _kv(f"{a}.vocab_size", 4, cfg.vocab),
+    ]
+
+
+def write_gguf(path: str, cfg: ModelConfig, seed: int = 0,
+               progress: Optional[Callable[[int, int], None]] = None) -> int:
+    """Write the seeded model `cfg` to `path`. Returns the file size in bytes."""
+    tensors = cfg.tensors()
+    infos, offsets, off = [], [], 0
+    for name, kind, ne in tensors:
+        t = cfg.type_of(kind)
+        n = int(np.prod(ne))
+        nbytes = type_bytes(t, n)
+        offsets.append(off)
+        infos.append(_gguf_str(name) + struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", d) for d in ne)
+                     + struct.pack("<I", t) + struct.pack("<Q", off))
+        off += (nbytes + ALIGN - 1) // ALIGN * ALIGN
+    kvs = metadata(cfg)
+    head = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kvs)) + b"".join(kvs) + b"".join(infos)
+    pad = (-len(head)) % ALIGN
+    L = synth_lib()
+    chunk = 1 << 24
+    with open(path, "wb") as f:
+        f.write(head + b"\0" * pad)
+        for i, ((name, kind, ne), o) in enumerate(zip(tensors, offsets)):
+            t = cfg.type_of(kind)
+            n = int(np.prod(ne))
+            be = BLOCK[t][0]
+            row = ne[0]
+            if kind.endswith("norm"):
+                std, mean = cfg.norm_std, 1.0
+            else:
+                std, mean = cfg.weight_std, 0.0
+            s = tensor_seed(name, seed)
+            step = max(row, chunk // row * row)
+            scratch = np.empty(min(step, n), np.float32)
+            done = 0
+            while done < n:
+                m = min(step, n - done)
+                if std == 0.0:
+                    scratch[:m] = mean
+                else:
+                    L.sy_fill_normal(s, done, m, mean, std, scratch.ctypes.data)
+                assert m % be == 0
+                out = np.empty(type_bytes(t, m), np.uint8)
+                L.sy_encode(t, scratch.ctypes.data, m, out.ctypes.data)
+                f.write(out.tobytes())
+                done += m
+            nbytes = type_bytes(t, n)
+            f.write(b"\0" * ((-nbytes) % ALIGN))
+            if progress:
+                progress(i + 1, len(tensors))
+        size = f.tell()
+    return size
+
+
+def tensor_values(cfg: ModelConfig, name: str, seed: int = 0) -> np.ndarray:
+    """The f32 values drawn for tensor `name` before encoding (tests)."""
+    kinds = {n: (k, ne) for n, k, ne in cfg.tensors()}
+    kind, ne = kinds[name]
+    n = int(np.prod(ne))
+    if kind.endswith("norm"):
+        return np.full(n, 1.0, np.float32) if cfg.norm_std == 0 else normal(tensor_seed(name, seed), n, cfg.norm_std, 1.0)
+    return normal(tensor_seed(name, seed), n, cfg.weight_std)
