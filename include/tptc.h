@@ -102,6 +102,11 @@ TPTC_API const char* tptc_last_error(const tptc_ctx* ctx);
 TPTC_API const char* tptc_version(void);
 TPTC_API int tptc_device_count(void);
 
+/* Element type of the KV cache, set before tptc_load_gguf: TPTC_TYPE_F16 (default: half the
+ * bytes per decode step) or TPTC_TYPE_F32 (the precision of the reference's candle path,
+ * wgpu_kvcache.rs:37 also stores f32). */
+TPTC_API int tptc_set_kv_dtype(tptc_ctx* ctx, int ggml_type);
+
 /* LlmEngine::load (mod.rs:66-70) -> load_gguf_to_vram (wgpu_loader.rs:87-201): mmap the
  * file, parse GGUF v3, check bounds, stream every tensor through pinned staging with
  * cudaMemcpyAsync, repack to the device layout, build the KV cache and rope table. */
@@ -149,6 +154,11 @@ TPTC_API int tptc_last_device_ms(const tptc_ctx* ctx, double* ms);
 /* Wall-clock phases of the last tptc_infer call in milliseconds (wgpu_engine.rs:320-330). */
 TPTC_API int tptc_last_timing(const tptc_ctx* ctx, double* prefill_ms, double* decode_ms, int* n_prompt,
                               int* n_generated);
+
+/* Test hook: one decode step (as tptc_decode, outside the CUDA graph) that also copies, for
+ * every layer l, q after RoPE, the attention output and the residual stream into rows 3l,
+ * 3l+1, 3l+2 of trace (host, [3 * n_layers][dim] f32), for layer-by-layer parity checks. */
+TPTC_API int tptc_debug_trace(tptc_ctx* ctx, uint32_t id, int pos, float* trace);
 
 /* ------------------------------------------------ kernel-level entry points */
 /* Device pointers owned by the caller.  These expose each hot-path kernel for parity tests

@@ -60,6 +60,11 @@ typedef struct {
 } or_q8k;
 
 static int g_threads = 1;
+/* Optional per-layer trace of the last position (q after RoPE, attention output, residual
+ * stream after the layer) in rows 3l, 3l+1, 3l+2 -- the layout tptc_debug_trace uses. */
+static float* g_trace = NULL;
+
+void or_set_trace(float* trace) { g_trace = trace; }
 
 void or_set_threads(int n) { g_threads = n > 0 ? n : 1; }
 int or_get_threads(void) { return g_threads; }
@@ -616,6 +621,10 @@ int or_forward(void* p, const uint32_t* tokens, int n, int pos, float* logits, f
                 free(sc);
             }
         }
+        if (g_trace) {
+            memcpy(g_trace + (size_t)(3 * l) * dim, q + (size_t)(n - 1) * qd, sizeof(float) * qd);
+            memcpy(g_trace + (size_t)(3 * l + 1) * dim, att + (size_t)(n - 1) * qd, sizeof(float) * qd);
+        }
         or_matmul(Ty[4], T[4], dim, qd, att, n, tmp);
         for (size_t i = 0; i < (size_t)n * dim; i++) x[i] = tmp[i] + x[i];
         for (int i = 0; i < n; i++) rms_norm(x + (size_t)i * dim, (const float*)T[5], dim, d->rms_eps, xn + (size_t)i * dim);
@@ -627,6 +636,7 @@ int or_forward(void* p, const uint32_t* tokens, int n, int pos, float* logits, f
         }
         or_matmul(Ty[8], T[8], dim, ffn, g, n, tmp);
         for (size_t i = 0; i < (size_t)n * dim; i++) x[i] = tmp[i] + x[i];
+        if (g_trace) memcpy(g_trace + (size_t)(3 * l + 2) * dim, x + (size_t)(n - 1) * dim, sizeof(float) * dim);
     }
     float* last = x + (size_t)(n - 1) * dim;
     rms_norm(last, (const float*)m->t[1], dim, d->rms_eps, xn);

@@ -70,6 +70,8 @@ def lib():
         L.or_argmax.argtypes = [vp, i32]
         L.or_repeat_penalty.restype = None
         L.or_repeat_penalty.argtypes = [vp, i32, vp, i32, ctypes.c_float]
+        L.or_set_trace.restype = None
+        L.or_set_trace.argtypes = [vp]
         L.or_set_threads.restype = None
         L.or_set_threads.argtypes = [i32]
         L.or_rope_table.restype = None
@@ -203,6 +205,17 @@ class Model:
         if rc != 0:
             raise ValueError("oracle forward rejected the input")
         return (logits, hid) if want_hidden else logits
+
+    def forward_trace(self, tokens: Sequence[int], pos: int):
+        """forward() that also returns the per-layer trace [3 * n_layers, dim] of the last
+        position: q after RoPE, attention output, residual stream after the layer."""
+        tr = np.zeros((3 * self.n_layers, self.dim), np.float32)
+        lib().or_set_trace(_p(tr))
+        try:
+            logits = self.forward(tokens, pos)
+        finally:
+            lib().or_set_trace(None)
+        return logits, tr
 
     def greedy(self, prompt: Sequence[int], n_new: int) -> List[int]:
         logits = self.forward(prompt, 0)

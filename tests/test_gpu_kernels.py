@@ -43,10 +43,11 @@ def test_dequant_bitexact_vs_gguf_py(cuda_device, name, t):
 def activations(k, seed):
     rng = np.random.default_rng(seed)
     x = rng.standard_normal(k).astype(np.float32) * rng.choice([1e-3, 1.0, 30.0], k).astype(np.float32)
-    x[:256] = 0.0                       # all-zero block
-    x[256:512] = 0.75                   # constant block
-    x[512:768] = np.float32(-1.0)       # negative constant (max is negative)
-    x[800] = 1e4                        # isolated extreme
+    if k >= 1024:
+        x[:256] = 0.0                   # all-zero block
+        x[256:512] = 0.75               # constant block
+        x[512:768] = np.float32(-1.0)   # negative constant (max is negative)
+        x[800] = 1e4                    # isolated extreme
     return x
 
 

@@ -43,6 +43,7 @@ SIGNATURES = {
     "tptc_last_error": (ctypes.c_char_p, [c_vp]),
     "tptc_version": (ctypes.c_char_p, []),
     "tptc_device_count": (c_int, []),
+    "tptc_set_kv_dtype": (c_int, [c_vp, c_int]),
     "tptc_load_gguf": (c_int, [c_vp, ctypes.c_char_p, PROGRESS_CB, c_vp]),
     "tptc_unload": (c_int, [c_vp]),
     "tptc_is_loaded": (c_int, [c_vp]),
@@ -54,6 +55,7 @@ SIGNATURES = {
     "tptc_common_prefix_len": (c_int, [c_vp, c_int, c_vp, c_int]),
     "tptc_prefill": (c_int, [c_vp, c_vp, c_int, c_int, c_vp]),
     "tptc_decode": (c_int, [c_vp, c_u32, c_int, c_vp, c_vp]),
+    "tptc_debug_trace": (c_int, [c_vp, c_u32, c_int, c_vp]),
     "tptc_decode_greedy": (c_int, [c_vp, c_u32, c_int, c_int, c_vp]),
     "tptc_infer": (c_int, [c_vp, c_vp, c_int, ctypes.POINTER(InferParamsC), TOKEN_CB, c_vp]),
     "tptc_last_device_ms": (c_int, [c_vp, ctypes.POINTER(c_d)]),

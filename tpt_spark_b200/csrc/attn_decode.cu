@@ -1,4 +1,4 @@
-// attn_decode.cu -- GQA flash-decode over the HBM-resident fp16 KV cache.
+// attn_decode.cu -- GQA flash-decode over the HBM-resident KV cache.
 //
 // Replaces the reference's three attention passes (shaders/attention.wgsl:31-58 scores,
 // :73-135 softmax over a materialised scores[heads, ctx] buffer, :152-170 serial P.V),
@@ -7,13 +7,13 @@
 // mask for a single query (keys 0..pos), softmax, then P.V; head h reads kv head
 // h / (n_heads / n_kv) (repeat_kv).
 //
-// Layout: per layer K and V caches are [n_kv][max_seq][hd] fp16, so the keys of one kv head
-// at consecutive positions are one contiguous run.  Grid = (n_kv, splits); each CTA streams
-// its share of positions in tiles of 128 (one position per thread for the scores) through
-// a 2-stage shared-memory ring filled by 1-D TMA bulk copies, keeps an online softmax for
-// the group's query heads, and writes (m, l, acc) to scratch.  The last CTA of a kv head
-// (atomic ticket) merges the splits in split order, so the result does not depend on
-// scheduling.
+// Layout: per layer K and V caches are [n_kv][max_seq][hd], fp16 (default) or f32, so the
+// keys of one kv head at consecutive positions are one contiguous run.  Grid = (n_kv,
+// splits); each CTA streams its share of positions in tiles (one position per thread for
+// the scores, one output dimension per thread for P.V) through a 2-stage shared-memory ring
+// filled by 1-D TMA bulk copies, keeps an online softmax for the group's query heads, and
+// writes (m, l, acc) to scratch.  The last CTA of a kv head (atomic ticket) merges the
+// splits in split order, so the result does not depend on scheduling.
 #include <algorithm>
 
 #include "kernels.h"
@@ -22,24 +22,44 @@ namespace tptc {
 
 namespace {
 
-constexpr int kT = 128;        // threads per CTA = positions per tile
-constexpr int kMaxGroup = 8;   // query heads per kv head
+constexpr int kThreads = 128;
+constexpr int kMaxGroup = 8;  // query heads per kv head
 constexpr int kStages = 2;
 
-__global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
+template <typename KV>
+struct KvTraits;
+template <>
+struct KvTraits<__half> {
+    static constexpr int kTile = 128;  // positions per tile
+    __device__ static float2 pair(const __half* row, int j) {
+        return __half22float2(reinterpret_cast<const __half2*>(row)[j]);
+    }
+    __device__ static float at(const __half* p) { return __half2float(*p); }
+};
+template <>
+struct KvTraits<float> {
+    static constexpr int kTile = 64;
+    __device__ static float2 pair(const float* row, int j) { return reinterpret_cast<const float2*>(row)[j]; }
+    __device__ static float at(const float* p) { return *p; }
+};
+
+template <typename KV>
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
+    using Tr = KvTraits<KV>;
+    constexpr int kT = Tr::kTile;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kStages];
-    __shared__ float red[kMaxGroup][kT / 32];
+    __shared__ float red[kMaxGroup][kThreads / 32];
     __shared__ float mnew_s[kMaxGroup], alpha_s[kMaxGroup];
     __shared__ int is_last;
 
     const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = p.n_heads / p.n_kv, hd = p.hd;
     const int tile_elems = kT * hd;
-    __half* kbuf = reinterpret_cast<__half*>(smem);                       // [kStages][kT][hd]
-    __half* vbuf = kbuf + kStages * tile_elems;                           // [kStages][kT][hd]
-    float* qs = reinterpret_cast<float*>(vbuf + kStages * tile_elems);    // [G][hd]
-    float* ps = qs + G * hd;                                              // [G][kT]
+    KV* kbuf = reinterpret_cast<KV*>(smem);                          // [kStages][kT][hd]
+    KV* vbuf = kbuf + kStages * tile_elems;                          // [kStages][kT][hd]
+    float* qs = reinterpret_cast<float*>(vbuf + kStages * tile_elems);  // [G][hd]
+    float* ps = qs + G * hd;                                         // [G][kT]
 
     if (tid == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
@@ -54,15 +74,15 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
     const int t_begin = split * per, t_end = min(kv_len, t_begin + per);
     const int ntiles = t_end > t_begin ? (t_end - t_begin + kT - 1) / kT : 0;
 
-    for (int i = tid; i < G * hd; i += kT) qs[i] = p.q[(kvh * G) * hd + i];
+    for (int i = tid; i < G * hd; i += kThreads) qs[i] = p.q[(kvh * G) * hd + i];
     __syncthreads();
 
-    const __half* kh = p.kcache + (int64_t)kvh * p.max_seq * hd;
-    const __half* vh = p.vcache + (int64_t)kvh * p.max_seq * hd;
+    const KV* kh = static_cast<const KV*>(p.kcache) + (int64_t)kvh * p.max_seq * hd;
+    const KV* vh = static_cast<const KV*>(p.vcache) + (int64_t)kvh * p.max_seq * hd;
     uint64_t policy = 0;
     auto issue = [&](int tile) {
         const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
-        const uint32_t bytes = (uint32_t)n * hd * 2;
+        const uint32_t bytes = (uint32_t)n * hd * sizeof(KV);
         mbar_expect_tx(&full[s], 2 * bytes);
         bulk_g2s(kbuf + s * tile_elems, kh + (int64_t)t0 * hd, bytes, &full[s], policy);
         bulk_g2s(vbuf + s * tile_elems, vh + (int64_t)t0 * hd, bytes, &full[s], policy);
@@ -84,16 +104,19 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
         const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
         if (!mbar_wait_bounded(&full[s], (tile / kStages) & 1, p.err)) timed_out = true;
         if (__syncthreads_or(timed_out)) return;
-        // scores: thread = position; rotate the start column so lanes hit different banks
-        const __half2* krow = reinterpret_cast<const __half2*>(kbuf + s * tile_elems + tid * hd);
+        // scores: thread = position; the column start rotates with the position so that
+        // neighbouring threads read different shared-memory banks
         float sc[kMaxGroup];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.f;
+        for (int g = 0; g < kMaxGroup; g++) sc[g] = -INFINITY;
         if (tid < n) {
+            const KV* krow = kbuf + s * tile_elems + tid * hd;
             const int hp = hd / 2;
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.f;
             int jj = tid % hp;
             for (int j = 0; j < hp; j++, jj = (jj + 1 == hp) ? 0 : jj + 1) {
-                const float2 kv = __half22float2(krow[jj]);
+                const float2 kv = Tr::pair(krow, jj);
 #pragma unroll
                 for (int g = 0; g < kMaxGroup; g++) {
                     if (g < G) {
@@ -105,9 +128,6 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
             }
 #pragma unroll
             for (int g = 0; g < kMaxGroup; g++) sc[g] = sc[g] * p.scale;
-        } else {
-#pragma unroll
-            for (int g = 0; g < kMaxGroup; g++) sc[g] = -INFINITY;
         }
         // tile max per head
 #pragma unroll
@@ -120,7 +140,7 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
         __syncthreads();
         if (tid < G) {
             float mx = red[tid][0];
-            for (int w = 1; w < kT / 32; w++) mx = fmaxf(mx, red[tid][w]);
+            for (int w = 1; w < kThreads / 32; w++) mx = fmaxf(mx, red[tid][w]);
             const float mn = fmaxf(m_run[tid], mx);
             mnew_s[tid] = mn;
             alpha_s[tid] = m_run[tid] == -INFINITY ? 0.f : expf(m_run[tid] - mn);
@@ -130,7 +150,7 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
         for (int g = 0; g < kMaxGroup; g++) {
             if (g < G) {
                 const float pv = tid < n ? expf(sc[g] - mnew_s[g]) : 0.f;
-                ps[g * kT + tid] = pv;
+                if (tid < kT) ps[g * kT + tid] = pv;
                 const float ls = warp_sum(pv);
                 if (lane == 0) red[g][warp] = ls;
             }
@@ -140,7 +160,7 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
         for (int g = 0; g < kMaxGroup; g++) {
             if (g < G) {
                 float ls = 0.f;
-                for (int w = 0; w < kT / 32; w++) ls += red[g][w];
+                for (int w = 0; w < kThreads / 32; w++) ls += red[g][w];
                 l_run[g] = l_run[g] * alpha_s[g] + ls;
                 m_run[g] = mnew_s[g];
                 acc[g] *= alpha_s[g];
@@ -148,9 +168,9 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
         }
         // P.V: thread = output dimension
         if (tid < hd) {
-            const __half* vcol = vbuf + s * tile_elems + tid;
+            const KV* vcol = vbuf + s * tile_elems + tid;
             for (int t = 0; t < n; t++) {
-                const float v = __half2float(vcol[t * hd]);
+                const float v = Tr::at(vcol + t * hd);
 #pragma unroll
                 for (int g = 0; g < kMaxGroup; g++)
                     if (g < G) acc[g] = fmaf(ps[g * kT + t], v, acc[g]);
@@ -199,16 +219,17 @@ __global__ void __launch_bounds__(kT) attn_decode_kernel(const __grid_constant__
     if (tid == 0) p.counters[kvh] = 0;
 }
 
+template <typename KV>
 size_t attn_smem(int n_heads, int n_kv, int hd) {
-    const int G = n_heads / n_kv;
-    return (size_t)2 * kStages * kT * hd * 2 + (size_t)G * hd * 4 + (size_t)G * kT * 4;
+    const int G = n_heads / n_kv, kT = KvTraits<KV>::kTile;
+    return (size_t)2 * kStages * kT * hd * sizeof(KV) + (size_t)G * hd * 4 + (size_t)G * kT * 4;
 }
 
 }  // namespace
 
 int attn_decode_splits(int n_kv, int max_seq, int sm_count) {
     int s = std::max(1, sm_count / n_kv);
-    const int max_useful = (max_seq + kT - 1) / kT;
+    const int max_useful = (max_seq + 63) / 64;
     return std::min(s, std::max(1, max_useful));
 }
 
@@ -217,23 +238,26 @@ size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits) {
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl) {
-    if (p.n_heads % p.n_kv != 0 || p.n_heads / p.n_kv > kMaxGroup || p.hd > kT || p.hd % 2 != 0 || (p.hd * 2) % 16 != 0)
+    if (p.n_heads % p.n_kv != 0 || p.n_heads / p.n_kv > kMaxGroup || p.hd > kThreads || p.hd % 16 != 0)
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.n_kv, p.splits);
-    cfg.blockDim = dim3(kT);
-    cfg.dynamicSmemBytes = attn_smem(p.n_heads, p.n_kv, p.hd);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = p.kv_f32 ? attn_smem<float>(p.n_heads, p.n_kv, p.hd) : attn_smem<__half>(p.n_heads, p.n_kv, p.hd);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel, p);
+    if (p.kv_f32) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<float>, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<__half>, p);
 }
 
 cudaError_t attn_init_device() {
-    return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
 }
 
 }  // namespace tptc

@@ -92,6 +92,14 @@ TPTC_API void tptc_destroy(tptc_ctx* ctx) {
 
 TPTC_API const char* tptc_last_error(const tptc_ctx* ctx) { return ctx ? ctx->err.c_str() : g_err.c_str(); }
 
+TPTC_API int tptc_set_kv_dtype(tptc_ctx* ctx, int ggml_type) {
+    if (!ctx) return TPTC_ERR_ARG;
+    if (ggml_type != TPTC_TYPE_F16 && ggml_type != TPTC_TYPE_F32)
+        return fail_code(ctx, TPTC_ERR_UNSUPPORTED, "KV cache type must be F16 or F32");
+    Status s = ctx->eng->set_kv_f32(ggml_type == TPTC_TYPE_F32);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
 TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user) {
     if (!ctx || !path) return fail_code(ctx, TPTC_ERR_ARG, "null argument");
     Status s = ctx->eng->load(path, progress, user);
@@ -147,6 +155,12 @@ TPTC_API int tptc_prefill(tptc_ctx* ctx, const uint32_t* ids, int n, int start_p
 TPTC_API int tptc_decode(tptc_ctx* ctx, uint32_t id, int pos, float* logits, uint32_t* argmax) {
     if (!ctx) return TPTC_ERR_ARG;
     Status s = ctx->eng->decode(id, pos, logits, argmax);
+    return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_debug_trace(tptc_ctx* ctx, uint32_t id, int pos, float* trace) {
+    if (!ctx || !trace) return TPTC_ERR_ARG;
+    Status s = ctx->eng->debug_trace(id, pos, trace);
     return s.ok() ? TPTC_OK : fail(ctx, s);
 }
 

@@ -378,7 +378,7 @@ Status Engine::alloc_runtime() {
         off = align_up(off + bytes, 256);
         return o;
     };
-    const size_t o_kv = take(kv_elems * 2);
+    const size_t o_kv = take(kv_elems * kv_elem_bytes());
     const size_t o_cos = take((size_t)max_seq_ * half * 4), o_sin = take((size_t)max_seq_ * half * 4);
     const size_t o_x = take((size_t)m.dim * 4);
     const size_t o_q = take((size_t)n_heads_l_ * hd * 4), o_att = take((size_t)n_heads_l_ * hd * 4);
@@ -396,7 +396,7 @@ Status Engine::alloc_runtime() {
     }
     device_bytes_ += rt_size_;
     CU(cudaMemsetAsync(rt_, 0, rt_size_, stream_));
-    kv_ = reinterpret_cast<__half*>(rt_ + o_kv);
+    kv_ = rt_ + o_kv;
     rope_cos_ = reinterpret_cast<float*>(rt_ + o_cos);
     rope_sin_ = reinterpret_cast<float*>(rt_ + o_sin);
     x_ = reinterpret_cast<float*>(rt_ + o_x);
@@ -437,15 +437,15 @@ Status Engine::alloc_runtime() {
 // One decode step: embed -> L x (QKV+RoPE+KV write, flash-decode, O+residual,
 // gate/up+SiLU, down+residual) -> norm + lm_head -> argmax.  All positions come from the
 // device scalar pos_, so one captured graph serves every step.
-Status Engine::enqueue_decode(cudaStream_t st, bool chained) {
+Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
     const ModelMeta& m = meta_;
     const int hd = m.head_dim;
-    const size_t layer_kv = (size_t)2 * n_kv_l_ * max_seq_ * hd;
+    const size_t layer_kv = (size_t)2 * n_kv_l_ * max_seq_ * hd * kv_elem_bytes();  // bytes
     CU(launch_embed_row(embd_, tok_in_, x_, st, false));
     for (int l = 0; l < m.n_layers; l++) {
         const LayerWeights& L = layers_[l];
-        __half* kc = kv_ + l * layer_kv;
-        __half* vc = kc + (size_t)n_kv_l_ * max_seq_ * hd;
+        uint8_t* kc = kv_ + l * layer_kv;
+        uint8_t* vc = kc + layer_kv / 2;
         GemvParams p = {};
         p.K = m.dim;
         p.err = err_;
@@ -464,6 +464,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained) {
         p.out = qbuf_;
         p.kcache = kc;
         p.vcache = vc;
+        p.kv_f32 = kv_f32_ ? 1 : 0;
         p.rope_cos = rope_cos_;
         p.rope_sin = rope_sin_;
         p.pos = pos_;
@@ -476,6 +477,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained) {
         a.q = qbuf_;
         a.kcache = kc;
         a.vcache = vc;
+        a.kv_f32 = kv_f32_ ? 1 : 0;
         a.pos = pos_;
         a.out = attn_;
         a.partial = attn_partial_;
@@ -536,6 +538,13 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained) {
             d.out = x_;
             gemv_prepare(d);
             CU(gemv_launch(d, EPI_RESID, st, pdl_));
+        }
+        if (trace) {
+            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 0) * m.dim, qbuf_, (size_t)n_heads_l_ * hd * 4,
+                               cudaMemcpyDeviceToHost, st));
+            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 1) * m.dim, attn_, (size_t)n_heads_l_ * hd * 4,
+                               cudaMemcpyDeviceToHost, st));
+            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 2) * m.dim, x_, (size_t)m.dim * 4, cudaMemcpyDeviceToHost, st));
         }
     }
     GemvParams h = {};
@@ -620,6 +629,21 @@ Status Engine::decode(uint32_t id, int pos, float* logits, uint32_t* argmax) {
     if (argmax) CU(cudaMemcpyAsync(h_tok_ + 1, tok_out_, 4, cudaMemcpyDeviceToHost, stream_));
     RET_IF(sync());
     if (argmax) *argmax = h_tok_[1];
+    cached_tokens_.push_back(id);
+    return {};
+}
+
+Status Engine::debug_trace(uint32_t id, int pos, float* trace) {
+    if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
+    if (id >= (uint32_t)meta_.vocab || pos != (int)cached_tokens_.size() || pos >= max_seq_)
+        return err(TPTC_ERR_ARG, "bad token or position");
+    CU(cudaSetDevice(device_));
+    h_tok_[0] = id;
+    h_pos_[0] = pos;
+    CU(cudaMemcpyAsync(tok_in_, h_tok_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaMemcpyAsync(pos_, h_pos_, 4, cudaMemcpyHostToDevice, stream_));
+    RET_IF(enqueue_decode(stream_, false, trace));
+    RET_IF(sync());
     cached_tokens_.push_back(id);
     return {};
 }

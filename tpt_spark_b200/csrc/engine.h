@@ -50,6 +50,13 @@ class Engine {
     Status kv_reset();
     int kv_len() const { return (int)cached_tokens_.size(); }
     void kv_truncate(int n) { cached_tokens_.resize(n); }
+    // KV cache element type, chosen before load: fp16 (default) or f32 (candle's precision).
+    Status set_kv_f32(bool f32) {
+        if (loaded_) return Status{TPTC_ERR_STATE, "the KV cache type must be set before load"};
+        kv_f32_ = f32;
+        return {};
+    }
+    bool kv_f32() const { return kv_f32_; }
     int prefix_len(const uint32_t* ids, int n) const;
 
     Status prefill(const uint32_t* ids, int n, int start_pos, float* last_logits);
@@ -66,7 +73,15 @@ class Engine {
    private:
     Status alloc_runtime();
     Status build_decode_graph(bool chained, cudaGraphExec_t* out);
-    Status enqueue_decode(cudaStream_t st, bool chained);
+    // trace (host, pinned or pageable; null in graphs): per layer l, rows 3l..3l+2 of width
+    // dim receive q (after RoPE), the attention output and the residual stream x.
+    Status enqueue_decode(cudaStream_t st, bool chained, float* trace = nullptr);
+
+   public:
+    // One decode step outside the graph, recording the per-layer trace above (test hook).
+    Status debug_trace(uint32_t id, int pos, float* trace);
+
+   private:
     Status enqueue_layer_prefill(int l, int n, int start_pos);
     Status run_prefill_batched(const uint32_t* ids, int n, int start_pos, float* last_logits);
     Status check_err();
@@ -89,7 +104,9 @@ class Engine {
     std::vector<LayerWeights> layers_;
     DevMatrix embd_, output_;
     float* out_norm_ = nullptr;
-    __half* kv_ = nullptr;  // [L][2][n_kv_local][max_seq][hd]
+    uint8_t* kv_ = nullptr;  // [L][2][n_kv_local][max_seq][hd], fp16 or f32
+    bool kv_f32_ = false;
+    size_t kv_elem_bytes() const { return kv_f32_ ? 4 : 2; }
     int max_seq_ = 0;
     int n_heads_l_ = 0, n_kv_l_ = 0;  // per-rank heads (TP)
     float* rope_cos_ = nullptr;

@@ -416,8 +416,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
                 if (r.seg == 0) {
                     p.out[r.row] = v;
                 } else {
-                    __half* cache = r.seg == 1 ? p.kcache : p.vcache;
-                    cache[((int64_t)head * p.max_seq + pos) * p.hd + d] = __float2half_rn(v);
+                    void* cache = r.seg == 1 ? p.kcache : p.vcache;
+                    const int64_t at = ((int64_t)head * p.max_seq + pos) * p.hd + d;
+                    if (p.kv_f32) static_cast<float*>(cache)[at] = v;
+                    else static_cast<__half*>(cache)[at] = __float2half_rn(v);
                 }
             }
         }

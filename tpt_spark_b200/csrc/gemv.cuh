@@ -56,8 +56,9 @@ struct GemvParams {
     float eps;
     float* out;
     // EPI_QKV
-    __half* kcache;        // this layer's K cache, layout [n_kv][max_seq][hd]
-    __half* vcache;
+    void* kcache;          // this layer's K cache, layout [n_kv][max_seq][hd], fp16 or f32
+    void* vcache;
+    int kv_f32;            // 1: the cache holds f32 (candle's precision), 0: fp16
     const float* rope_cos;  // [max_seq][hd/2]
     const float* rope_sin;
     const int* pos;  // device scalar: position being written

@@ -21,8 +21,9 @@ cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __ha
 // attn_decode.cu
 struct AttnDecodeParams {
     const float* q;        // [n_heads * hd] (rope applied)
-    const __half* kcache;  // this layer, [n_kv][max_seq][hd]
-    const __half* vcache;
+    const void* kcache;    // this layer, [n_kv][max_seq][hd], fp16 (default) or f32
+    const void* vcache;
+    int kv_f32;
     const int* pos;        // device scalar: the query position (keys 0..pos)
     float* out;            // [n_heads * hd]
     float* partial;        // scratch [n_kv][splits][group][2 + hd]

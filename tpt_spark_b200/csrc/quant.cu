@@ -49,13 +49,9 @@ __global__ void quant_q80_kernel(const float* __restrict__ x, int64_t nb, uint8_
     if (b >= nb) return;
     float d;
     const int8_t q = q80_quant_warp(x[b * QK8_0 + lane], d);
-    uint8_t* blk = out + b * Q80_BYTES;
+    uint8_t* blk = out + b * Q80_BYTES;  // 34-byte blocks: 2-byte aligned
     blk[2 + lane] = (uint8_t)q;
-    if (lane == 0) {
-        const uint16_t h = f2h(d);
-        blk[0] = (uint8_t)(h & 0xff);
-        blk[1] = (uint8_t)(h >> 8);
-    }
+    if (lane == 0) *reinterpret_cast<uint16_t*>(blk) = f2h(d);
 }
 
 // Repack one super-block (Q6_K) or one 32-block (Q8_0) per thread; Q4_K / F16 copy bytes.

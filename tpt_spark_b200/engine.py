@@ -79,10 +79,15 @@ class CudaEngine:
     """engine/cuda_engine: the B200 engine behind the LlmEngine API."""
 
     def __init__(self, device: int = 0, tp_rank: int = 0, tp_size: int = 1, nccl_uid: Optional[bytes] = None,
-                 tokenizer=None):
+                 tokenizer=None, kv_dtype: str = "f16"):
+        """kv_dtype: "f16" (default, half the KV bytes per step) or "f32" (candle's precision)."""
         self._ctx = ctypes.c_void_p()
         uid = ctypes.create_string_buffer(nccl_uid, 128) if nccl_uid is not None else None
         check(lib().tptc_create(device, tp_rank, tp_size, uid, ctypes.byref(self._ctx)))
+        if kv_dtype not in ("f16", "f32"):
+            raise ValueError("kv_dtype must be 'f16' or 'f32'")
+        self._check(lib().tptc_set_kv_dtype(self._ctx, 0 if kv_dtype == "f32" else 1))
+        self.kv_dtype = kv_dtype
         self.device = device
         self.tokenizer = tokenizer
         self._info: Optional[ModelInfo] = None
@@ -203,6 +208,13 @@ class CudaEngine:
         self._check(lib().tptc_decode(self._ctx, token, pos, out.ctypes.data if out is not None else None,
                                       ctypes.byref(am)))
         return (out, am.value) if want_logits else am.value
+
+    def debug_trace(self, token: int, pos: int) -> np.ndarray:
+        """Per-layer trace of one decode step: [3 * n_layers, dim] (q, attention, residual)."""
+        self._need_model()
+        tr = np.zeros((3 * self._info.n_layers, self._info.dim), np.float32)
+        self._check(lib().tptc_debug_trace(self._ctx, token, pos, tr.ctypes.data))
+        return tr
 
     def decode_greedy(self, token: int, pos: int, n: int) -> List[int]:
         out = np.empty(n, np.uint32)
