@@ -9,11 +9,12 @@
 //
 // Layout: per layer K and V caches are [n_kv][max_seq][hd], fp16 (default) or f32, so the
 // keys of one kv head at consecutive positions are one contiguous run.  Grid = (n_kv,
-// splits); each CTA streams its share of positions in tiles (one position per thread for
-// the scores, one output dimension per thread for P.V) through a 2-stage shared-memory ring
-// filled by 1-D TMA bulk copies, keeps an online softmax for the group's query heads, and
-// writes (m, l, acc) to scratch.  The last CTA of a kv head (atomic ticket) merges the
-// splits in split order, so the result does not depend on scheduling.
+// splits); each CTA streams its share of positions in 64-position tiles (two threads per
+// position for the scores, one output dimension per thread for P.V) through a 2-stage
+// shared-memory ring filled by 1-D TMA bulk copies, keeps an online softmax for the group's
+// query heads, and writes (m, l, acc) to scratch.  The last CTA of a kv head (atomic
+// ticket) merges the splits in split order, so the result does not depend on scheduling;
+// the merge stages every split's statistics in shared memory with parallel loads.
 #include <algorithm>
 
 #include "kernels.h"
@@ -30,17 +31,19 @@ template <typename KV>
 struct KvTraits;
 template <>
 struct KvTraits<__half> {
-    static constexpr int kTile = 128;  // positions per tile
+    static constexpr int kTile = 64;  // positions per tile (64 KB ring: co-resides with a GEMV CTA)
     __device__ static float2 pair(const __half* row, int j) {
         return __half22float2(reinterpret_cast<const __half2*>(row)[j]);
     }
     __device__ static float at(const __half* p) { return __half2float(*p); }
+    __device__ static void store(__half* p, float v) { *p = __float2half_rn(v); }
 };
 template <>
 struct KvTraits<float> {
     static constexpr int kTile = 64;
     __device__ static float2 pair(const float* row, int j) { return reinterpret_cast<const float2*>(row)[j]; }
     __device__ static float at(const float* p) { return *p; }
+    __device__ static void store(float* p, float v) { *p = v; }
 };
 
 template <typename KV>
@@ -56,10 +59,10 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
     const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = p.n_heads / p.n_kv, hd = p.hd;
     const int tile_elems = kT * hd;
-    KV* kbuf = reinterpret_cast<KV*>(smem);                          // [kStages][kT][hd]
-    KV* vbuf = kbuf + kStages * tile_elems;                          // [kStages][kT][hd]
+    KV* kbuf = reinterpret_cast<KV*>(smem);                             // [kStages][kT][hd]
+    KV* vbuf = kbuf + kStages * tile_elems;                             // [kStages][kT][hd]
     float* qs = reinterpret_cast<float*>(vbuf + kStages * tile_elems);  // [G][hd]
-    float* ps = qs + G * hd;                                         // [G][kT]
+    float* ps = qs + G * hd;                                            // [G][kT]
 
     if (tid == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
@@ -74,7 +77,35 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
     const int t_begin = split * per, t_end = min(kv_len, t_begin + per);
     const int ntiles = t_end > t_begin ? (t_end - t_begin + kT - 1) / kT : 0;
 
-    for (int i = tid; i < G * hd; i += kThreads) qs[i] = p.q[(kvh * G) * hd + i];
+    // RoPE (candle rope_i: interleaved pairs, x0*c - x1*s, x0*s + x1*c) on the group's
+    // queries while they are staged in shared memory
+    const int pos = kv_len - 1, half = hd / 2;
+    const float* cs = p.rope_cos + (int64_t)pos * half;
+    const float* sn = p.rope_sin + (int64_t)pos * half;
+    for (int i = tid; i < G * half; i += kThreads) {
+        const int g = i / half, j = i % half;
+        const float* qg = p.q + (int64_t)(kvh * G + g) * hd;
+        const float q0 = qg[2 * j], q1 = qg[2 * j + 1], c = cs[j], s = sn[j];
+        const float r0 = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
+        const float r1 = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
+        qs[g * hd + 2 * j] = r0;
+        qs[g * hd + 2 * j + 1] = r1;
+        if (p.q_out && split == 0) {
+            p.q_out[(int64_t)(kvh * G + g) * hd + 2 * j] = r0;
+            p.q_out[(int64_t)(kvh * G + g) * hd + 2 * j + 1] = r1;
+        }
+    }
+    // The CTA whose positions include `pos` rotates this step's key and stores it in the cache;
+    // the proxy fence orders those generic stores before its own bulk-copy reads of them.
+    if (pos >= t_begin && pos < t_end) {
+        KV* krow = static_cast<KV*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * hd;
+        for (int j = tid; j < half; j += kThreads) {
+            const float k0 = p.kraw[kvh * hd + 2 * j], k1 = p.kraw[kvh * hd + 2 * j + 1], c = cs[j], s = sn[j];
+            Tr::store(krow + 2 * j, __fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
+            Tr::store(krow + 2 * j + 1, __fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
     __syncthreads();
 
     const KV* kh = static_cast<const KV*>(p.kcache) + (int64_t)kvh * p.max_seq * hd;
@@ -99,23 +130,23 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
         l_run[g] = 0.f;
         acc[g] = 0.f;
     }
+    // scores: two threads per position (kThreads = 2 * kT), each half of the head dimension
+    const int my_pos = tid >> 1, my_half = tid & 1;
+    const int hp = hd / 2, hq = hp / 2;  // half2 pairs per row, per half-row
     bool timed_out = false;
     for (int tile = 0; tile < ntiles; tile++) {
         const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
         if (!mbar_wait_bounded(&full[s], (tile / kStages) & 1, p.err)) timed_out = true;
         if (__syncthreads_or(timed_out)) return;
-        // scores: thread = position; the column start rotates with the position so that
-        // neighbouring threads read different shared-memory banks
         float sc[kMaxGroup];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) sc[g] = -INFINITY;
-        if (tid < n) {
-            const KV* krow = kbuf + s * tile_elems + tid * hd;
-            const int hp = hd / 2;
-#pragma unroll
-            for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.f;
-            int jj = tid % hp;
-            for (int j = 0; j < hp; j++, jj = (jj + 1 == hp) ? 0 : jj + 1) {
+        for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.f;
+        if (my_pos < n) {
+            const KV* krow = kbuf + s * tile_elems + my_pos * hd;
+            // start column rotated by position so neighbouring threads hit different banks
+            int jj = my_half * hq + (my_pos % hq);
+            const int lo = my_half * hq, hi = lo + hq;
+            for (int j = 0; j < hq; j++) {
                 const float2 kv = Tr::pair(krow, jj);
 #pragma unroll
                 for (int g = 0; g < kMaxGroup; g++) {
@@ -125,9 +156,13 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
                         sc[g] = fmaf(qv.y, kv.y, sc[g]);
                     }
                 }
+                jj = (jj + 1 == hi) ? lo : jj + 1;
             }
+        }
 #pragma unroll
-            for (int g = 0; g < kMaxGroup; g++) sc[g] = sc[g] * p.scale;
+        for (int g = 0; g < kMaxGroup; g++) {
+            sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 1);
+            sc[g] = my_pos < n ? sc[g] * p.scale : -INFINITY;
         }
         // tile max per head
 #pragma unroll
@@ -149,9 +184,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
 #pragma unroll
         for (int g = 0; g < kMaxGroup; g++) {
             if (g < G) {
-                const float pv = tid < n ? expf(sc[g] - mnew_s[g]) : 0.f;
-                if (tid < kT) ps[g * kT + tid] = pv;
-                const float ls = warp_sum(pv);
+                const float pv = my_pos < n ? expf(sc[g] - mnew_s[g]) : 0.f;
+                if (my_half == 0) ps[g * kT + my_pos] = pv;
+                const float ls = warp_sum(my_half == 0 ? pv : 0.f);
                 if (lane == 0) red[g][warp] = ls;
             }
         }
@@ -201,19 +236,43 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // merge: stage every split's (m, l) in shared memory with parallel loads, then each
+    // thread reduces one output dimension in split order (deterministic)
     const float* base = p.partial + (int64_t)kvh * p.splits * G * rec;
+    float* wgt = ps;             // reuse: [G][splits] m_s, then weights exp(m_s - M); splits <= kT
+    float* lsp = qs;             // reuse: [G][splits] l_s (splits <= 64 <= hd)
+    float* lsum = mnew_s;        // [G] totals
+    for (int i = tid; i < G * p.splits; i += kThreads) {
+        const int g = i / p.splits, s = i % p.splits;
+        wgt[g * kT + s] = base[(s * G + g) * rec];
+        lsp[g * p.splits + s] = base[(s * G + g) * rec + 1];
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s = 0; s < p.splits; s++) M = fmaxf(M, wgt[tid * kT + s]);
+        float L = 0.f;
+        for (int s = 0; s < p.splits; s++) {
+            const float w = wgt[tid * kT + s] == -INFINITY ? 0.f : expf(wgt[tid * kT + s] - M);
+            wgt[tid * kT + s] = w;
+            L = fmaf(lsp[tid * p.splits + s], w, L);
+        }
+        lsum[tid] = L;
+    }
+    __syncthreads();
     if (tid < hd) {
         for (int g = 0; g < G; g++) {
-            float M = -INFINITY;
-            for (int s = 0; s < p.splits; s++) M = fmaxf(M, base[(s * G + g) * rec]);
-            float L = 0.f, o = 0.f;
-            for (int s = 0; s < p.splits; s++) {
-                const float* r = base + (s * G + g) * rec;
-                const float w = r[0] == -INFINITY ? 0.f : expf(r[0] - M);
-                L = fmaf(r[1], w, L);
-                o = fmaf(r[2 + tid], w, o);
+            float o = 0.f;
+            for (int s0 = 0; s0 < p.splits; s0 += 16) {  // 16 independent loads in flight
+                float v[16];
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    v[k] = s0 + k < p.splits ? base[((s0 + k) * G + g) * rec + 2 + tid] : 0.f;
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    if (s0 + k < p.splits) o = fmaf(v[k], wgt[g * kT + s0 + k], o);
             }
-            p.out[(kvh * G + g) * hd + tid] = o / L;
+            p.out[(kvh * G + g) * hd + tid] = o / lsum[g];
         }
     }
     if (tid == 0) p.counters[kvh] = 0;
@@ -230,7 +289,8 @@ size_t attn_smem(int n_heads, int n_kv, int hd) {
 int attn_decode_splits(int n_kv, int max_seq, int sm_count) {
     int s = std::max(1, sm_count / n_kv);
     const int max_useful = (max_seq + 63) / 64;
-    return std::min(s, std::max(1, max_useful));
+    // the merge stages one weight per split in a 64-entry shared array
+    return std::min(64, std::min(s, std::max(1, max_useful)));
 }
 
 size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits) {

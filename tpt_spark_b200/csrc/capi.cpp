@@ -239,18 +239,11 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
         return cuda_fail(ie, "kernel setup");
     }
     tptc::DevMatrix& d = m->m;
-    d.type = ggml_type;
-    d.N = N;
-    d.K = K;
-    int64_t raw_row;
-    switch (ggml_type) {
-    case TPTC_TYPE_Q4_K: d.main_row_bytes = (int64_t)K / 256 * 144; raw_row = d.main_row_bytes; break;
-    case TPTC_TYPE_Q6_K: d.main_row_bytes = (int64_t)K / 256 * 208; d.d_per_row = K / 256; raw_row = (int64_t)K / 256 * 210; break;
-    case TPTC_TYPE_Q8_0: d.main_row_bytes = K; d.d_per_row = K / 32; raw_row = (int64_t)K / 32 * 34; break;
-    default: d.main_row_bytes = (int64_t)K * 2; raw_row = d.main_row_bytes; break;
-    }
-    const size_t main_bytes = (size_t)d.main_row_bytes * N, d_bytes = (size_t)d.d_per_row * 2 * N;
-    const size_t main_al = (main_bytes + 255) / 256 * 256;
+    d = tptc::dm_geometry(ggml_type, N, K, 0);
+    const int64_t raw_row = ggml_type == TPTC_TYPE_Q6_K ? (int64_t)K / 256 * 210
+                            : ggml_type == TPTC_TYPE_Q8_0 ? (int64_t)K / 32 * 34 : d.main_row_bytes;
+    const size_t main_al = ((size_t)d.main_bytes() + 255) / 256 * 256;
+    const size_t d_bytes = (size_t)d.d_per_row * 2 * d.Npad;
     cudaError_t e = cudaMalloc(&m->mem, main_al + d_bytes + 256);
     if (e != cudaSuccess) {
         delete m;
@@ -267,8 +260,8 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
         if (e == cudaSuccess) e = cudaMemcpy(tmp, raw, raw_bytes, cudaMemcpyHostToDevice);
         src = tmp;
     }
-    if (e == cudaSuccess) e = cudaMemset(m->err, 0, sizeof(int));
-    if (e == cudaSuccess) e = tptc::launch_repack(src, d, 0);
+    if (e == cudaSuccess) e = cudaMemset(m->mem, 0, main_al + d_bytes + 256);
+    if (e == cudaSuccess) e = tptc::launch_repack(src, raw_row, N, 0, d, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (tmp) cudaFree(tmp);
     if (e != cudaSuccess) {
@@ -291,11 +284,14 @@ TPTC_API int64_t tptc_matrix_bytes(const tptc_matrix* m) { return m ? m->m.bytes
 static tptc::GemvParams matrix_params(const tptc_matrix* m, const float* x) {
     tptc::GemvParams p = {};
     p.nseg = 1;
-    p.seg[0] = tptc::GemvSeg{m->m.main, m->m.dplane, m->m.type, m->m.N, m->m.main_row_bytes, m->m.d_per_row, 0};
+    p.seg[0] = tptc::GemvSeg{m->m, 0};
     p.K = m->m.K;
     p.x = x;
     p.err = m->err;
-    tptc::gemv_prepare(p);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    tptc::gemv_prepare(p, sms);
     return p;
 }
 

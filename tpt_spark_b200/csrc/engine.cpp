@@ -36,18 +36,6 @@ Status err(int code, const std::string& m) { return Status{code, m}; }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Device layout geometry of a matrix (see gemv.cuh).
-void matrix_geometry(int type, int N, int K, int64_t& main_row, int64_t& d_per_row) {
-    d_per_row = 0;
-    switch (type) {
-    case TPTC_TYPE_Q4_K: main_row = (int64_t)K / QK_K * Q4K_BYTES; break;
-    case TPTC_TYPE_Q6_K: main_row = (int64_t)K / QK_K * Q6K_MAIN; d_per_row = K / QK_K; break;
-    case TPTC_TYPE_Q8_0: main_row = K; d_per_row = K / QK8_0; break;
-    default: main_row = (int64_t)K * 2; break;
-    }
-    (void)N;
-}
-
 int64_t raw_row_bytes(int type, int K) {
     switch (type) {
     case TPTC_TYPE_Q4_K: return (int64_t)K / QK_K * Q4K_BYTES;
@@ -107,12 +95,12 @@ struct Stager {
 };
 
 // Copy rows [r0, r1) x raw-bytes [c0, c1) of a row-major host tensor into device memory,
-// repacking to the device layout.  Used whole (c0 = 0, c1 = row bytes) on one GPU; the
-// column window selects a K-slice for row-parallel tensor sharding.
+// repacking into the tiled layout as logical rows first_row.. of `m`.  Used whole (c0 = 0,
+// c1 = row bytes) on one GPU; the column window selects a K-slice for row-parallel tensor
+// sharding.  m.type == F32 (norm vectors) is copied as is.
 Status upload_rows(Stager& sg, const uint8_t* host, int64_t host_row_bytes, int r0, int r1, int64_t c0, int64_t c1,
-                   const DevMatrix& m) {
+                   const DevMatrix& m, int first_row) {
     const int64_t rb = c1 - c0;
-    const bool repack = m.type == TPTC_TYPE_Q6_K || m.type == TPTC_TYPE_Q8_0;
     int rows_per = (int)std::max<int64_t>(1, (int64_t)Stager::kChunk / rb);
     for (int r = r0; r < r1; r += rows_per) {
         const int nr = std::min(rows_per, r1 - r);
@@ -124,15 +112,12 @@ Status upload_rows(Stager& sg, const uint8_t* host, int64_t host_row_bytes, int 
             for (int i = 0; i < nr; i++)
                 memcpy(sg.pinned[b] + (int64_t)i * rb, host + (int64_t)(r + i) * host_row_bytes + c0, (size_t)rb);
         }
-        DevMatrix view = m;
-        view.N = nr;
-        view.main = m.main + (int64_t)(r - r0) * m.main_row_bytes;
-        view.dplane = m.dplane ? m.dplane + (int64_t)(r - r0) * m.d_per_row : nullptr;
-        if (repack) {
-            CU(cudaMemcpyAsync(sg.dtmp[b], sg.pinned[b], (size_t)nr * rb, cudaMemcpyHostToDevice, sg.st));
-            CU(launch_repack(sg.dtmp[b], view, sg.st));
+        if (m.type == TPTC_TYPE_F32) {
+            CU(cudaMemcpyAsync(m.main + (int64_t)(r - r0) * rb, sg.pinned[b], (size_t)nr * rb, cudaMemcpyHostToDevice,
+                               sg.st));
         } else {
-            CU(cudaMemcpyAsync(view.main, sg.pinned[b], (size_t)nr * rb, cudaMemcpyHostToDevice, sg.st));
+            CU(cudaMemcpyAsync(sg.dtmp[b], sg.pinned[b], (size_t)nr * rb, cudaMemcpyHostToDevice, sg.st));
+            CU(launch_repack(sg.dtmp[b], rb, nr, first_row + (r - r0), m, sg.st));
         }
         RET_IF(sg.release(b));
     }
@@ -261,7 +246,9 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
     n_kv_l_ = m.n_kv_heads / tp;
     const int hd = m.head_dim, ffn_l = m.ffn / tp, qd_l = n_heads_l_ * hd, kvd_l = n_kv_l_ * hd;
 
-    // ---- tensor plan: name, expected shape, rows/cols this rank keeps
+    // ---- tensor plan: name, expected shape, rows/cols this rank keeps, destination.
+    // gate and up land in one fused gate|up matrix (logical rows [0, ffn_l) and [ffn_l,
+    // 2 ffn_l)), so the decode GEMV streams matching gate and up rows as one tile.
     struct Plan {
         std::string name;
         int N, K;            // full shape
@@ -269,29 +256,31 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         int k0, k1;          // K range kept (row parallel)
         DevMatrix* mat;      // nullptr for f32 vectors
         float** vec;
+        int first_row;       // logical row of r0 in `mat`
+        int glu_rows;        // > 0: `mat` is a fused gate|up matrix of this many rows
     };
     std::vector<Plan> plans;
     layers_.assign(m.n_layers, LayerWeights{});
-    plans.push_back({"token_embd.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &embd_, nullptr});
+    plans.push_back({"token_embd.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &embd_, nullptr, 0, 0});
     for (int l = 0; l < m.n_layers; l++) {
         LayerWeights& L = layers_[l];
         const std::string p = "blk." + std::to_string(l) + ".";
-        plans.push_back({p + "attn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.attn_norm});
-        plans.push_back({p + "attn_q.weight", m.n_heads * hd, m.dim, r * qd_l, (r + 1) * qd_l, 0, m.dim, &L.q, nullptr});
-        plans.push_back({p + "attn_k.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.k, nullptr});
-        plans.push_back({p + "attn_v.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.v, nullptr});
-        plans.push_back({p + "attn_output.weight", m.dim, m.n_heads * hd, 0, m.dim, r * qd_l, (r + 1) * qd_l, &L.o, nullptr});
-        plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm});
-        plans.push_back({p + "ffn_gate.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.gate, nullptr});
-        plans.push_back({p + "ffn_up.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.up, nullptr});
-        plans.push_back({p + "ffn_down.weight", m.dim, m.ffn, 0, m.dim, r * ffn_l, (r + 1) * ffn_l, &L.down, nullptr});
+        plans.push_back({p + "attn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.attn_norm, 0, 0});
+        plans.push_back({p + "attn_q.weight", m.n_heads * hd, m.dim, r * qd_l, (r + 1) * qd_l, 0, m.dim, &L.q, nullptr, 0, 0});
+        plans.push_back({p + "attn_k.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.k, nullptr, 0, 0});
+        plans.push_back({p + "attn_v.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.v, nullptr, 0, 0});
+        plans.push_back({p + "attn_output.weight", m.dim, m.n_heads * hd, 0, m.dim, r * qd_l, (r + 1) * qd_l, &L.o, nullptr, 0, 0});
+        plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm, 0, 0});
+        plans.push_back({p + "ffn_gate.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.glu, nullptr, 0, 2 * ffn_l});
+        plans.push_back({p + "ffn_up.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.glu, nullptr, ffn_l, 2 * ffn_l});
+        plans.push_back({p + "ffn_down.weight", m.dim, m.ffn, 0, m.dim, r * ffn_l, (r + 1) * ffn_l, &L.down, nullptr, 0, 0});
     }
-    plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_});
-    if (!m.tied) plans.push_back({"output.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &output_, nullptr});
+    plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_, 0, 0});
+    if (!m.tied) plans.push_back({"output.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &output_, nullptr, 0, 0});
 
     // ---- validate and lay out the arena
     size_t off = 0;
-    std::vector<size_t> offs(plans.size()), doffs(plans.size());
+    std::vector<size_t> offs(plans.size(), 0), doffs(plans.size(), 0);
     std::vector<const GgufTensor*> tens(plans.size());
     for (size_t i = 0; i < plans.size(); i++) {
         Plan& p = plans[i];
@@ -311,15 +300,17 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         }
         if (!matrix_type_ok((int)t->type))
             return err(TPTC_ERR_UNSUPPORTED, "tensor '" + p.name + "' has unsupported GGML type " + std::to_string(t->type));
+        if (p.glu_rows && p.first_row > 0) {  // second half of a fused gate|up matrix
+            if ((int)t->type != p.mat->type)
+                return err(TPTC_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a GGML type (" + p.name + ")");
+            continue;
+        }
         DevMatrix& d = *p.mat;
-        d.type = (int)t->type;
-        d.N = p.r1 - p.r0;
-        d.K = p.k1 - p.k0;
-        matrix_geometry(d.type, d.N, d.K, d.main_row_bytes, d.d_per_row);
+        d = dm_geometry((int)t->type, p.glu_rows ? p.glu_rows : p.r1 - p.r0, p.k1 - p.k0, p.glu_rows ? 1 : 0);
         offs[i] = off;
-        off = align_up(off + (size_t)d.main_row_bytes * d.N, 256);
+        off = align_up(off + (size_t)d.main_bytes(), 256);
         doffs[i] = off;
-        off = align_up(off + (size_t)d.d_per_row * 2 * d.N, 256);
+        off = align_up(off + (size_t)d.d_per_row * 2 * d.Npad, 256);
     }
     arena_size_ = off;
     cudaError_t ce = cudaMalloc(&arena_, arena_size_);
@@ -328,6 +319,7 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         return err(TPTC_ERR_OOM, "weights need " + std::to_string(arena_size_ >> 20) + " MiB: " + cuda_msg(ce, "cudaMalloc"));
     }
     device_bytes_ = arena_size_;
+    CU(cudaMemsetAsync(arena_, 0, arena_size_, stream_));  // tile padding rows stay zero
 
     // ---- upload
     Stager sg(stream_);
@@ -341,20 +333,19 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
             *p.vec = reinterpret_cast<float*>(arena_ + offs[i]);
             DevMatrix tmp;
             tmp.type = TPTC_TYPE_F32;
-            tmp.N = 1;
-            tmp.K = p.K;
             tmp.main = arena_ + offs[i];
-            tmp.main_row_bytes = (int64_t)p.K * 4;
-            RET_IF(upload_rows(sg, src, (int64_t)p.K * 4, 0, 1, 0, (int64_t)p.K * 4, tmp));
+            RET_IF(upload_rows(sg, src, (int64_t)p.K * 4, 0, 1, 0, (int64_t)p.K * 4, tmp, 0));
             weight_bytes_ += (uint64_t)p.K * 4;
         } else {
             DevMatrix& d = *p.mat;
-            d.main = arena_ + offs[i];
-            d.dplane = d.d_per_row ? reinterpret_cast<uint16_t*>(arena_ + doffs[i]) : nullptr;
+            if (!(p.glu_rows && p.first_row > 0)) {
+                d.main = arena_ + offs[i];
+                d.dplane = d.d_per_row ? reinterpret_cast<uint16_t*>(arena_ + doffs[i]) : nullptr;
+            }
             const int64_t rrb = raw_row_bytes(d.type, p.K);
             const int64_t c0 = raw_row_bytes(d.type, p.k0), c1 = raw_row_bytes(d.type, p.k1);
-            RET_IF(upload_rows(sg, src, rrb, p.r0, p.r1, c0, c1, d));
-            weight_bytes_ += (uint64_t)d.bytes();
+            RET_IF(upload_rows(sg, src, rrb, p.r0, p.r1, c0, c1, d, p.first_row));
+            weight_bytes_ += (uint64_t)(p.r1 - p.r0) * (d.main_row_bytes + d.d_per_row * 2);
         }
         if (cb) cb((uint32_t)(i + 1), (uint32_t)plans.size(), user);
     }
@@ -382,7 +373,8 @@ Status Engine::alloc_runtime() {
     const size_t o_cos = take((size_t)max_seq_ * half * 4), o_sin = take((size_t)max_seq_ * half * 4);
     const size_t o_x = take((size_t)m.dim * 4);
     const size_t o_q = take((size_t)n_heads_l_ * hd * 4), o_att = take((size_t)n_heads_l_ * hd * 4);
-    const size_t o_h = take((size_t)m.ffn / tp_size_ * 4), o_lg = take((size_t)m.vocab * 4);
+    const size_t o_qr = take((size_t)n_heads_l_ * hd * 4), o_kr = take((size_t)n_kv_l_ * hd * 4);
+    const size_t o_h = take((size_t)2 * (m.ffn / tp_size_) * 4), o_lg = take((size_t)m.vocab * 4);
     const size_t o_ti = take(64), o_to = take(64), o_pos = take(64), o_err = take(64);
     const size_t o_hist = take((size_t)max_seq_ * 4 + 64);
     const size_t o_part = take(attn_decode_partial_floats(n_heads_l_, n_kv_l_, hd, attn_splits_) * 4);
@@ -402,6 +394,8 @@ Status Engine::alloc_runtime() {
     x_ = reinterpret_cast<float*>(rt_ + o_x);
     qbuf_ = reinterpret_cast<float*>(rt_ + o_q);
     attn_ = reinterpret_cast<float*>(rt_ + o_att);
+    qrot_ = reinterpret_cast<float*>(rt_ + o_qr);
+    kraw_ = reinterpret_cast<float*>(rt_ + o_kr);
     h_ = reinterpret_cast<float*>(rt_ + o_h);
     logits_ = reinterpret_cast<float*>(rt_ + o_lg);
     tok_in_ = reinterpret_cast<uint32_t*>(rt_ + o_ti);
@@ -450,34 +444,32 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         p.K = m.dim;
         p.err = err_;
         p.eps = m.rms_eps;
-        // q | k | v with fused RMSNorm, RoPE and KV-cache write
+        // q | k | v with fused RMSNorm; v goes straight into the cache, q and k are rotated
+        // by the attention kernel
         p.nseg = 3;
         const DevMatrix* qkv[3] = {&L.q, &L.k, &L.v};
-        int cta = 0;
-        for (int s = 0; s < 3; s++) {
-            p.seg[s] = GemvSeg{qkv[s]->main, qkv[s]->dplane, qkv[s]->type, qkv[s]->N, qkv[s]->main_row_bytes,
-                               qkv[s]->d_per_row, cta};
-            cta += ceil_div(qkv[s]->N, 8);
-        }
+        for (int s = 0; s < 3; s++) p.seg[s] = GemvSeg{*qkv[s], 0};
         p.x = x_;
         p.norm_w = L.attn_norm;
         p.out = qbuf_;
-        p.kcache = kc;
+        p.kraw = kraw_;
         p.vcache = vc;
         p.kv_f32 = kv_f32_ ? 1 : 0;
-        p.rope_cos = rope_cos_;
-        p.rope_sin = rope_sin_;
         p.pos = pos_;
         p.hd = hd;
         p.max_seq = max_seq_;
-        gemv_prepare(p);
+        gemv_prepare(p, sm_count_);
         CU(gemv_launch(p, EPI_QKV, st, pdl_));
 
         AttnDecodeParams a = {};
         a.q = qbuf_;
+        a.kraw = kraw_;
         a.kcache = kc;
         a.vcache = vc;
         a.kv_f32 = kv_f32_ ? 1 : 0;
+        a.rope_cos = rope_cos_;
+        a.rope_sin = rope_sin_;
+        a.q_out = qrot_;
         a.pos = pos_;
         a.out = attn_;
         a.partial = attn_partial_;
@@ -495,17 +487,17 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         o.K = n_heads_l_ * hd;
         o.err = err_;
         o.nseg = 1;
-        o.seg[0] = GemvSeg{L.o.main, L.o.dplane, L.o.type, L.o.N, L.o.main_row_bytes, L.o.d_per_row, 0};
+        o.seg[0] = GemvSeg{L.o, 0};
         o.x = attn_;
         if (tp_) {
             // row-parallel: partial sums into h-sized scratch, then allreduce into x
             o.out = tp_->partial(m.dim);
-            gemv_prepare(o);
+            gemv_prepare(o, sm_count_);
             CU(gemv_launch(o, EPI_STORE, st, pdl_));
             RET_IF(tp_->allreduce_add(o.out, x_, m.dim, st));
         } else {
             o.out = x_;
-            gemv_prepare(o);
+            gemv_prepare(o, sm_count_);
             CU(gemv_launch(o, EPI_RESID, st, pdl_));
         }
 
@@ -513,34 +505,32 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         g.K = m.dim;
         g.err = err_;
         g.eps = m.rms_eps;
-        g.nseg = 2;
-        g.paired = 1;
-        g.seg[0] = GemvSeg{L.gate.main, L.gate.dplane, L.gate.type, L.gate.N, L.gate.main_row_bytes, L.gate.d_per_row, 0};
-        g.seg[1] = GemvSeg{L.up.main, L.up.dplane, L.up.type, L.up.N, L.up.main_row_bytes, L.up.d_per_row, 0};
+        g.nseg = 1;
+        g.seg[0] = GemvSeg{L.glu, 0};
         g.x = x_;
         g.norm_w = L.ffn_norm;
         g.out = h_;
-        gemv_prepare(g);
+        gemv_prepare(g, sm_count_);
         CU(gemv_launch(g, EPI_GLU, st, pdl_));
 
         GemvParams d = {};
         d.K = m.ffn / tp_size_;
         d.err = err_;
         d.nseg = 1;
-        d.seg[0] = GemvSeg{L.down.main, L.down.dplane, L.down.type, L.down.N, L.down.main_row_bytes, L.down.d_per_row, 0};
+        d.seg[0] = GemvSeg{L.down, 0};
         d.x = h_;
         if (tp_) {
             d.out = tp_->partial(m.dim);
-            gemv_prepare(d);
+            gemv_prepare(d, sm_count_);
             CU(gemv_launch(d, EPI_STORE, st, pdl_));
             RET_IF(tp_->allreduce_add(d.out, x_, m.dim, st));
         } else {
             d.out = x_;
-            gemv_prepare(d);
+            gemv_prepare(d, sm_count_);
             CU(gemv_launch(d, EPI_RESID, st, pdl_));
         }
         if (trace) {
-            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 0) * m.dim, qbuf_, (size_t)n_heads_l_ * hd * 4,
+            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 0) * m.dim, qrot_, (size_t)n_heads_l_ * hd * 4,
                                cudaMemcpyDeviceToHost, st));
             CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 1) * m.dim, attn_, (size_t)n_heads_l_ * hd * 4,
                                cudaMemcpyDeviceToHost, st));
@@ -552,11 +542,11 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
     h.err = err_;
     h.eps = m.rms_eps;
     h.nseg = 1;
-    h.seg[0] = GemvSeg{output_.main, output_.dplane, output_.type, output_.N, output_.main_row_bytes, output_.d_per_row, 0};
+    h.seg[0] = GemvSeg{output_, 0};
     h.x = x_;
     h.norm_w = out_norm_;
     h.out = logits_;
-    gemv_prepare(h);
+    gemv_prepare(h, sm_count_);
     CU(gemv_launch(h, EPI_STORE, st, pdl_));
     CU(launch_argmax(logits_, m.vocab, tok_out_, chained ? tok_in_ : nullptr, chained ? pos_ : nullptr,
                      chained ? history_ : nullptr, st, pdl_));

@@ -27,7 +27,8 @@ struct ModelMeta {
 };
 
 struct LayerWeights {
-    DevMatrix q, k, v, o, gate, up, down;
+    DevMatrix q, k, v, o, down;
+    DevMatrix glu;  // fused ffn_gate | ffn_up (gemv.cuh): logical rows [0, ffn) gate, [ffn, 2 ffn) up
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
 };
@@ -112,9 +113,11 @@ class Engine {
     float* rope_cos_ = nullptr;
     float* rope_sin_ = nullptr;
     float* x_ = nullptr;        // residual stream [dim]
-    float* qbuf_ = nullptr;     // [n_heads_l * hd]
+    float* qbuf_ = nullptr;     // [n_heads_l * hd] q before RoPE
+    float* qrot_ = nullptr;     // [n_heads_l * hd] q after RoPE (written by attention, for traces)
+    float* kraw_ = nullptr;     // [n_kv_l * hd] this step's k before RoPE
     float* attn_ = nullptr;     // [n_heads_l * hd]
-    float* h_ = nullptr;        // [ffn_l]
+    float* h_ = nullptr;        // [2 * ffn_l]: gate rows then up rows
     float* logits_ = nullptr;   // [vocab]
     uint32_t* tok_in_ = nullptr;
     uint32_t* tok_out_ = nullptr;

@@ -7,15 +7,21 @@
 // the activation is quantised to Q8_K (Q4_K/Q6_K weights) or Q8_0 (Q8_0 weights) and every
 // super-block contributes (d_w*d_x)*isum - (dmin_w*d_x)*msum from exact integer sums.
 //
-// Kernel structure (one CTA = 8 warps = 8 weight rows):
-//   1. thread 0 starts 1-D TMA bulk copies of the CTA's weight rows, chunk by chunk, into
-//      a shared-memory ring (mbarrier completion, L2 evict-first) -- weights do not depend
-//      on the previous kernel, so this runs before griddepcontrol.wait;
-//   2. griddepcontrol.wait, then the CTA RMS-normalises (optional) and quantises the
-//      activation into shared memory (every CTA computes the same bytes);
-//   3. each warp reduces its row from the ring: dp4a integer dots per sub-block, exact
-//      integer sums across the lanes of a super-block, one f32 FMA per super-block;
-//   4. fused epilogue: store / residual add / RoPE + fp16 KV-cache write / SiLU(gate)*up.
+// Kernel structure: a persistent grid (one CTA per SM), 9 warps per CTA.
+//   - warp 8 (producer) streams the CTA's weight tiles (8 rows x a chunk of super-blocks,
+//     contiguous in the tiled device layout of gemv.cuh) through a ring of shared-memory
+//     stages, one 1-D TMA bulk copy of 13-32 KB per stage (L2 evict-first), gated by
+//     per-stage "empty" mbarriers.  Weights do not depend on the previous kernel, so the
+//     producer starts before griddepcontrol.wait: under programmatic dependent launch the
+//     weight stream of this kernel overlaps the tail of the previous one.
+//   - warps 0-7 (consumers) wait for the previous kernel, RMS-normalise (optional) and
+//     quantise the activation into shared memory once, then each reduces one row of every
+//     tile: dp4a integer dots per sub-block, one f32 FMA per lane item, a warp sum per row.
+//     Each warp releases a stage by arriving on its "empty" barrier.
+//   - every warp writes its own row, no barrier between warps: store / residual add / the
+//     q|k|v projection (q and k unrotated -- the attention kernel applies RoPE -- and v into
+//     the KV cache) / the fused gate|up rows (the down projection forms silu(gate)*up while
+//     quantising its input).
 #include <algorithm>
 
 #include "gemv.cuh"
@@ -25,58 +31,205 @@ namespace tptc {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kMaxStages = 4;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + producer warp
+constexpr int kRingBudget = 100 * 1024;    // shared memory per CTA (two kernels fit per SM)
 
-struct WarpRow {
-    int seg;    // -1: no row for this warp
-    int row;
-    int type;
-    const uint8_t* main;
-    const uint16_t* dplane;
-    int64_t row_bytes;
-    int64_t d_per_row;
-};
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+// Named barrier 2 + i joins consumer warps i and i + 4 only.
+__device__ __forceinline__ void pair_sync(int i) { asm volatile("bar.sync %0, 64;" ::"r"(2 + i) : "memory"); }
 
-__device__ __forceinline__ WarpRow warp_row(const GemvParams& p, int warp) {
-    WarpRow r;
-    int s = 0, row = 0;
-    if (p.paired) {
-        s = warp >> 2;
-        row = blockIdx.x * 4 + (warp & 3);
-    } else {
-        s = 0;
-        while (s + 1 < p.nseg && (int)blockIdx.x >= p.seg[s + 1].cta_begin) s++;
-        row = (blockIdx.x - p.seg[s].cta_begin) * kWarps + warp;
-    }
-    const GemvSeg& g = p.seg[s];
-    r.seg = row < g.N ? s : -1;
-    r.row = row;
-    r.type = g.type;
-    r.main = g.main;
-    r.dplane = g.dplane;
-    r.row_bytes = g.row_bytes;
-    r.d_per_row = g.d_per_row;
-    return r;
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Activation pieces in shared memory.
+// Logical row held in tile row r (0..7) of work unit u, and the segment it belongs to.
+struct UnitRow {
+    int seg;   // -1: padding row (N not a multiple of 8)
+    int row;   // logical row within the segment (for glu: gate row if r < 4, up row otherwise)
+    int out;   // output index (glu: the gate/up pair index)
+};
+
+__device__ __forceinline__ int unit_seg(const GemvParams& p, int u) {
+    int s = 0;
+    while (s + 1 < p.nseg && u >= p.seg[s + 1].unit_begin) s++;
+    return s;
+}
+
+__device__ __forceinline__ UnitRow unit_row(const GemvParams& p, int u, int r) {
+    UnitRow ur;
+    const int s = unit_seg(p, u);
+    const DevMatrix& m = p.seg[s].m;
+    const int t = u - p.seg[s].unit_begin;
+    ur.seg = s;
+    if (m.glu) {
+        const int half = m.N / 2, pr = 4 * t + (r & 3);
+        ur.out = pr;
+        ur.row = r < 4 ? pr : half + pr;
+        if (pr >= half) ur.seg = -1;
+    } else {
+        ur.row = t * kTileRows + r;
+        ur.out = ur.row;
+        if (ur.row >= m.N) ur.seg = -1;
+    }
+    return ur;
+}
+
 struct Act {
     const float* f32;
     const int8_t* q8k;
     const float* q8k_d;
-    const int16_t* q8k_bs;
+    const int16_t* q8k_bs;  // 16 sums of 16 elements per block
+    const int16_t* q8k_ps;  // 8 sums of 32 elements per block (Q4_K sub-blocks)
     const int8_t* q80;
     const float* q80_d;
 };
 
+// Each chunk routine reduces the items [first, first + stride, ...) of one row chunk held in
+// `slot`; `c0` is the chunk's first super-block, `cb` its length in super-blocks.
+//
+// Forward path (DOTS = false): every lane scales its own partial integer sum by the
+// super-block factors, (d_w*d_x)*isum_part - (dmin_w*d_x)*msum_part, so no cross-lane
+// reduction is needed per super-block (the f32 result differs from scaling the full
+// integer sum by float rounding only).  The DOTS test hook reduces the exact per-block
+// integers across the 4 lanes of a super-block.
+
+// All eight 6-bit scales and mins of a Q4_K block from its 12 packed bytes (words s0..s2):
+// bytes of sc_lo/sc_hi are sc[0..3]/sc[4..7], bytes of mn_lo/mn_hi are m[0..3]/m[4..7].
+__device__ __forceinline__ void q4k_unpack_scales(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t& sc_lo,
+                                                  uint32_t& sc_hi, uint32_t& mn_lo, uint32_t& mn_hi) {
+    const uint32_t k6 = 0x3f3f3f3fu, k4 = 0x0f0f0f0fu, k2 = 0x03030303u;
+    sc_lo = s0 & k6;
+    mn_lo = s1 & k6;
+    sc_hi = (s2 & k4) | (((s0 >> 6) & k2) << 4);
+    mn_hi = ((s2 >> 4) & k4) | (((s1 >> 6) & k2) << 4);
+}
+
+__device__ __forceinline__ int byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xff; }
+
+// Q4_K, forward path: lane item = (super-block sb, 64-element group g).
+__device__ __forceinline__ float q4k_item(const uint8_t* slot, const Act& a, int c0, int it) {
+    const int sb = it >> 2, g = it & 3;
+    const uint8_t* blk = slot + sb * Q4K_BYTES;
+    const uint4 hd = *reinterpret_cast<const uint4*>(blk);  // d, dmin, 12 scale bytes
+    const uint4 w0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
+    const int4* xq = reinterpret_cast<const int4*>(a.q8k + (c0 + sb) * QK_K + 64 * g);
+    const int4 x0 = xq[0], x1 = xq[1], x2 = xq[2], x3 = xq[3];
+    const uint32_t m4 = 0x0f0f0f0fu;
+    int lo0 = __dp4a((int)(w0.x & m4), x0.x, 0);
+    int lo1 = __dp4a((int)(w0.y & m4), x0.y, 0);
+    lo0 = __dp4a((int)(w0.z & m4), x0.z, lo0);
+    lo1 = __dp4a((int)(w0.w & m4), x0.w, lo1);
+    lo0 = __dp4a((int)(w1.x & m4), x1.x, lo0);
+    lo1 = __dp4a((int)(w1.y & m4), x1.y, lo1);
+    lo0 = __dp4a((int)(w1.z & m4), x1.z, lo0);
+    lo1 = __dp4a((int)(w1.w & m4), x1.w, lo1);
+    int hi0 = __dp4a((int)((w0.x >> 4) & m4), x2.x, 0);
+    int hi1 = __dp4a((int)((w0.y >> 4) & m4), x2.y, 0);
+    hi0 = __dp4a((int)((w0.z >> 4) & m4), x2.z, hi0);
+    hi1 = __dp4a((int)((w0.w >> 4) & m4), x2.w, hi1);
+    hi0 = __dp4a((int)((w1.x >> 4) & m4), x3.x, hi0);
+    hi1 = __dp4a((int)((w1.y >> 4) & m4), x3.y, hi1);
+    hi0 = __dp4a((int)((w1.z >> 4) & m4), x3.z, hi0);
+    hi1 = __dp4a((int)((w1.w >> 4) & m4), x3.w, hi1);
+    uint32_t sc_lo, sc_hi, mn_lo, mn_hi;
+    q4k_unpack_scales(hd.y, hd.z, hd.w, sc_lo, sc_hi, mn_lo, mn_hi);
+    const uint32_t scw = g < 2 ? sc_lo : sc_hi, mnw = g < 2 ? mn_lo : mn_hi;
+    const int j = (2 * g) & 3;
+    const int sc0 = byte_of(scw, j), sc1 = byte_of(scw, j + 1);
+    const int m0 = byte_of(mnw, j), m1 = byte_of(mnw, j + 1);
+    // pair sums of the 16-element bsums: P[2g], P[2g+1] (sub-blocks 2g and 2g+1)
+    const uint32_t pp = *reinterpret_cast<const uint32_t*>(a.q8k_ps + (c0 + sb) * 8 + 2 * g);
+    const int p0 = (int)(int16_t)(pp & 0xffff), p1 = (int)(int16_t)(pp >> 16);
+    const int isum = sc0 * (lo0 + lo1) + sc1 * (hi0 + hi1);
+    const int msum = m0 * p0 + m1 * p1;
+    const float dx = a.q8k_d[c0 + sb];
+    const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))), dx);
+    const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))), dx);
+    return dd * (float)isum - dm * (float)msum;
+}
+
+// Q6_K, forward path: lane item = (super-block sb, quarter t: half h, 16-column run l0).
+__device__ __forceinline__ float q6k_item(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int it) {
+    const int sb = it >> 2, t = it & 3, h = t >> 1, l0 = (t & 1) * 16;
+    const uint8_t* m = slot + sb * Q6K_MAIN;
+    const uint4 A = *reinterpret_cast<const uint4*>(m + 64 * h + l0);
+    const uint4 B = *reinterpret_cast<const uint4*>(m + 64 * h + 32 + l0);
+    const uint4 H = *reinterpret_cast<const uint4*>(m + 128 + 32 * h + l0);
+    const uint32_t scw = *reinterpret_cast<const uint32_t*>(m + 192 + 8 * h) >> (8 * (l0 >> 4));
+    const uint32_t scw2 = *reinterpret_cast<const uint32_t*>(m + 196 + 8 * h) >> (8 * (l0 >> 4));
+    const int8_t* xb = a.q8k + (c0 + sb) * QK_K + 128 * h + l0;
+    const int4 x1 = *reinterpret_cast<const int4*>(xb);
+    const int4 x2 = *reinterpret_cast<const int4*>(xb + 32);
+    const int4 x3 = *reinterpret_cast<const int4*>(xb + 64);
+    const int4 x4 = *reinterpret_cast<const int4*>(xb + 96);
+    const uint32_t m4 = 0x0f0f0f0fu, m2 = 0x30303030u;
+    int d1 = 0, d2 = 0, d3 = 0, d4 = 0;
+#define Q6K_WORD(Aw, Bw, Hw, X1, X2, X3, X4)                              \
+    d1 = __dp4a((int)(((Aw) & m4) | (((Hw) << 4) & m2)), X1, d1);         \
+    d2 = __dp4a((int)(((Bw) & m4) | (((Hw) << 2) & m2)), X2, d2);         \
+    d3 = __dp4a((int)((((Aw) >> 4) & m4) | ((Hw) & m2)), X3, d3);         \
+    d4 = __dp4a((int)((((Bw) >> 4) & m4) | (((Hw) >> 2) & m2)), X4, d4);
+    Q6K_WORD(A.x, B.x, H.x, x1.x, x2.x, x3.x, x4.x)
+    Q6K_WORD(A.y, B.y, H.y, x1.y, x2.y, x3.y, x4.y)
+    Q6K_WORD(A.z, B.z, H.z, x1.z, x2.z, x3.z, x4.z)
+    Q6K_WORD(A.w, B.w, H.w, x1.w, x2.w, x3.w, x4.w)
+#undef Q6K_WORD
+    // q is stored +32: sum (q-32)*x = sum q*x - 32 * bsum over the 16 elements
+    const int16_t* bs = a.q8k_bs + (c0 + sb) * 16 + 8 * h + (l0 >> 4);
+    d1 -= 32 * (int)bs[0];
+    d2 -= 32 * (int)bs[2];
+    d3 -= 32 * (int)bs[4];
+    d4 -= 32 * (int)bs[6];
+    // scales sc[8h + l0/16 + {0, 2, 4, 6}] (int8)
+    const int s1 = (int)(int8_t)(scw & 0xff), s2 = (int)(int8_t)((scw >> 16) & 0xff);
+    const int s3 = (int)(int8_t)(scw2 & 0xff), s4 = (int)(int8_t)((scw2 >> 16) & 0xff);
+    const int isum = s1 * d1 + s2 * d2 + s3 * d3 + s4 * d4;
+    return __fmul_rn(h2f(drow[c0 + sb]), a.q8k_d[c0 + sb]) * (float)isum;
+}
+
+__device__ __forceinline__ float chunk_q4k_fwd(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int first,
+                                               int stride) {
+    const int items = cb * 4;
+    float acc0 = 0.f, acc1 = 0.f;
+    int base = first;
+    for (; base + stride < items; base += 2 * stride) {  // two independent items in flight
+        const int i0 = base + lane, i1 = base + stride + lane;
+        acc0 += q4k_item(slot, a, c0, i0);
+        if (i1 < items) acc1 += q4k_item(slot, a, c0, i1);
+    }
+    for (; base < items; base += stride) {
+        const int i = base + lane;
+        if (i < items) acc0 += q4k_item(slot, a, c0, i);
+    }
+    return acc0 + acc1;
+}
+
+__device__ __forceinline__ float chunk_q6k_fwd(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int cb,
+                                               int lane, int first, int stride) {
+    const int items = cb * 4;
+    float acc0 = 0.f, acc1 = 0.f;
+    int base = first;
+    for (; base + stride < items; base += 2 * stride) {
+        const int i0 = base + lane, i1 = base + stride + lane;
+        acc0 += q6k_item(slot, drow, a, c0, i0);
+        if (i1 < items) acc1 += q6k_item(slot, drow, a, c0, i1);
+    }
+    for (; base < items; base += stride) {
+        const int i = base + lane;
+        if (i < items) acc0 += q6k_item(slot, drow, a, c0, i);
+    }
+    return acc0 + acc1;
+}
+
 template <bool DOTS>
-__device__ __forceinline__ float chunk_q4k(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int32_t* isum_row,
-                                           int32_t* msum_row) {
+__device__ __forceinline__ float chunk_q4k(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int first,
+                                           int stride, int32_t* isum_row, int32_t* msum_row) {
     float acc = 0.f;
     const int items = cb * 4;
-    for (int base = 0; base < items; base += 32) {
+    for (int base = first; base < items; base += stride) {
         const int it = base + lane;
         const bool valid = it < items;
         const int sb = it >> 2, g = it & 3;
@@ -136,10 +289,10 @@ __device__ __forceinline__ float chunk_q4k(const uint8_t* slot, const Act& a, in
 
 template <bool DOTS>
 __device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int cb,
-                                           int lane, int32_t* isum_row) {
+                                           int lane, int first, int stride, int32_t* isum_row) {
     float acc = 0.f;
     const int items = cb * 4;
-    for (int base = 0; base < items; base += 32) {
+    for (int base = first; base < items; base += stride) {
         const int it = base + lane;
         const bool valid = it < items;
         const int sb = it >> 2, t = it & 3, h = t >> 1, l0 = (t & 1) * 16;
@@ -158,17 +311,17 @@ __device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* 
             const int4 x4 = *reinterpret_cast<const int4*>(xb + 96);
             const uint32_t m4 = 0x0f0f0f0fu, m2 = 0x30303030u;
             int d1 = 0, d2 = 0, d3 = 0, d4 = 0;
-#define Q6K_WORD(Aw, Bw, Hw, X1, X2, X3, X4)                                  \
-    d1 = __dp4a((int)(((Aw) & m4) | (((Hw) << 4) & m2)), X1, d1);             \
-    d2 = __dp4a((int)(((Bw) & m4) | (((Hw) << 2) & m2)), X2, d2);             \
-    d3 = __dp4a((int)((((Aw) >> 4) & m4) | ((Hw) & m2)), X3, d3);             \
+#define Q6K_WORD(Aw, Bw, Hw, X1, X2, X3, X4)                              \
+    d1 = __dp4a((int)(((Aw) & m4) | (((Hw) << 4) & m2)), X1, d1);         \
+    d2 = __dp4a((int)(((Bw) & m4) | (((Hw) << 2) & m2)), X2, d2);         \
+    d3 = __dp4a((int)((((Aw) >> 4) & m4) | ((Hw) & m2)), X3, d3);         \
     d4 = __dp4a((int)((((Bw) >> 4) & m4) | (((Hw) >> 2) & m2)), X4, d4);
             Q6K_WORD(A.x, B.x, H.x, x1.x, x2.x, x3.x, x4.x)
             Q6K_WORD(A.y, B.y, H.y, x1.y, x2.y, x3.y, x4.y)
             Q6K_WORD(A.z, B.z, H.z, x1.z, x2.z, x3.z, x4.z)
             Q6K_WORD(A.w, B.w, H.w, x1.w, x2.w, x3.w, x4.w)
 #undef Q6K_WORD
-            // q stored +32: sum (q-32)*x = sum q*x - 32 * bsum over the 16 elements
+            // q is stored +32: sum (q-32)*x = sum q*x - 32 * bsum over the 16 elements
             const int16_t* bs = a.q8k_bs + (c0 + sb) * 16 + 8 * h + (l0 >> 4);
             d1 -= 32 * (int)bs[0];
             d2 -= 32 * (int)bs[2];
@@ -189,11 +342,13 @@ __device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* 
 
 template <bool DOTS>
 __device__ __forceinline__ float chunk_q80(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int cb,
-                                           int lane, int32_t* isum_row) {
+                                           int lane, int first, int stride, int32_t* isum_row) {
     float acc = 0.f;
     const int nblk = cb * 8;  // 32-element blocks in the chunk
     const int b0 = c0 * 8;
-    for (int b = lane; b < nblk; b += 32) {
+    for (int base = first; base < nblk; base += stride) {
+        const int b = base + lane;
+        if (b >= nblk) continue;
         const uint4 w0 = *reinterpret_cast<const uint4*>(slot + b * 32);
         const uint4 w1 = *reinterpret_cast<const uint4*>(slot + b * 32 + 16);
         const int4* xq = reinterpret_cast<const int4*>(a.q80 + (b0 + b) * 32);
@@ -217,17 +372,20 @@ __device__ __forceinline__ float chunk_q80(const uint8_t* slot, const uint16_t* 
     return acc;
 }
 
-__device__ __forceinline__ float chunk_f16(const uint8_t* slot, const Act& a, int c0, int cb, int lane) {
+__device__ __forceinline__ float chunk_f16(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int first,
+                                           int stride) {
     float acc = 0.f;
     const int units = cb * 32;  // 16-byte units (8 halfs)
     const float* x = a.f32 + c0 * QK_K;
-    for (int u = lane; u < units; u += 32) {
+    for (int base = first; base < units; base += stride) {
+        const int u = base + lane;
+        if (u >= units) continue;
         const uint4 w = *reinterpret_cast<const uint4*>(slot + u * 16);
         const float4 xa = *reinterpret_cast<const float4*>(x + u * 8);
         const float4 xb = *reinterpret_cast<const float4*>(x + u * 8 + 4);
         const __half2* h = reinterpret_cast<const __half2*>(&w);
-        float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]), f2 = __half22float2(h[2]),
-               f3 = __half22float2(h[3]);
+        const float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]), f2 = __half22float2(h[2]),
+                     f3 = __half22float2(h[3]);
         acc = fmaf(f0.x, xa.x, acc);
         acc = fmaf(f0.y, xa.y, acc);
         acc = fmaf(f1.x, xa.z, acc);
@@ -240,53 +398,71 @@ __device__ __forceinline__ float chunk_f16(const uint8_t* slot, const Act& a, in
     return acc;
 }
 
-// Prologue: optional RMSNorm (candle_nn::ops::rms_norm: m = sqrt(sum(x^2)/K + eps),
-// y = x / m * w) and quantisation of the activation into shared memory.
+// Prologue (consumer warps): optional RMSNorm (candle_nn::ops::rms_norm: m = sqrt(sum(x^2)/K
+// + eps), y = x / m * w) and quantisation of the activation into shared memory.
 __device__ void build_activation(const GemvParams& p, uint8_t* smem, float* red) {
     const int K = p.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float m = 1.f;
     const bool norm = p.norm_w != nullptr;
     if (norm) {
         float ss = 0.f;
-        for (int i = tid * 4; i < K; i += kThreads * 4) {
+        for (int i = tid * 4; i < K; i += kConsumers * 4) {
             const float4 v = *reinterpret_cast<const float4*>(p.x + i);
             ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        if (warp == 0) {
-            float v = lane < kWarps ? red[lane] : 0.f;
-            v = warp_sum(v);
-            if (lane == 0) red[kWarps] = v;
-        }
-        __syncthreads();
-        m = sqrtf(__fdiv_rn(red[kWarps], (float)K) + p.eps);
+        consumer_sync();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; w++) tot += red[w];
+        m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
     }
+    // candle Mlp: silu(w1 x) * (w3 x), silu(a) = a / (1 + exp(-a))
+    auto glu = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); };
     auto xval = [&](int i) -> float {
         float v = p.x[i];
+        if (p.glu_in) v = glu(v, p.x[K + i]);
         if (norm) v = __fmul_rn(__fdiv_rn(v, m), p.norm_w[i]);
         return v;
     };
     if (p.act_f32 >= 0) {
         float* dst = reinterpret_cast<float*>(smem + p.act_f32);
-        for (int i = tid; i < K; i += kThreads) dst[i] = xval(i);
+        for (int i = tid; i < K; i += kConsumers) dst[i] = xval(i);
     }
     if (p.act_q8k >= 0) {
         int8_t* qs = reinterpret_cast<int8_t*>(smem + p.act_q8k);
         float* dd = reinterpret_cast<float*>(smem + p.act_q8k_d);
         int16_t* bs = reinterpret_cast<int16_t*>(smem + p.act_q8k_bs);
-        for (int b = warp; b < K / QK_K; b += kWarps) {
+        int16_t* ps = reinterpret_cast<int16_t*>(smem + p.act_q8k_ps);
+        for (int b = warp; b < K / QK_K; b += kConsumerWarps) {
             float v[8];
+            const float4 x0 = *reinterpret_cast<const float4*>(p.x + b * QK_K + lane * 8);
+            const float4 x1 = *reinterpret_cast<const float4*>(p.x + b * QK_K + lane * 8 + 4);
+            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w; v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+            if (p.glu_in) {
+                const float4 u0 = *reinterpret_cast<const float4*>(p.x + K + b * QK_K + lane * 8);
+                const float4 u1 = *reinterpret_cast<const float4*>(p.x + K + b * QK_K + lane * 8 + 4);
+                const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = xval(b * QK_K + lane * 8 + i);
+                for (int i = 0; i < 8; i++) v[i] = glu(v[i], uv[i]);
+            }
+            if (norm) {
+                const float4 w0 = *reinterpret_cast<const float4*>(p.norm_w + b * QK_K + lane * 8);
+                const float4 w1 = *reinterpret_cast<const float4*>(p.norm_w + b * QK_K + lane * 8 + 4);
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], m), wv[i]);
+            }
             q8k_quant_warp(v, qs + b * QK_K, bs + b * 16, dd + b, lane);
+            __syncwarp();
+            if (lane < 8) ps[b * 8 + lane] = (int16_t)((int)bs[b * 16 + 2 * lane] + (int)bs[b * 16 + 2 * lane + 1]);
         }
     }
     if (p.act_q80 >= 0) {
         int8_t* qs = reinterpret_cast<int8_t*>(smem + p.act_q80);
         float* dd = reinterpret_cast<float*>(smem + p.act_q80_d);
-        for (int b = warp; b < K / QK8_0; b += kWarps) {
+        for (int b = warp; b < K / QK8_0; b += kConsumerWarps) {
             float d;
             qs[b * QK8_0 + lane] = q80_quant_warp(xval(b * QK8_0 + lane), d);
             if (lane == 0) dd[b] = h2f(f2h(d));
@@ -295,142 +471,138 @@ __device__ void build_activation(const GemvParams& p, uint8_t* smem, float* red)
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full[kMaxStages];
-    __shared__ float red[2 * kWarps + 2];
-    __shared__ float res[kWarps];
+    __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages];
+    __shared__ float red[kConsumerWarps];
+    __shared__ float glu_up[2][4];
+    int unit_no = 0;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int S = p.stages;
     const int nsb = p.K / QK_K;
     uint8_t* ring = smem + p.act_bytes;
 
-    // Rows and chunking of every warp of this CTA (uniform per warp).
-    const WarpRow wr = warp_row(p, warp);
-
-    // The chunk count is the same for every warp of a CTA: chunk_sb depends on the type,
-    // and a CTA's segments share a chunking class (all quantised or all F16).
-    const int cbs = chunk_sb(p.seg[0].type);
-    const int nchunks = (nsb + cbs - 1) / cbs;
-
     if (tid == 0) {
-        for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
         fence_mbar_init();
     }
     __syncthreads();
 
-    uint64_t policy = 0;
-    auto issue = [&](int c) {
-        const int s = c % S;
-        const int c0 = c * cbs, cb = min(cbs, nsb - c0);
-        uint32_t total = 0;
-        WarpRow rows[kWarps];
-#pragma unroll
-        for (int w = 0; w < kWarps; w++) {
-            rows[w] = warp_row(p, w);
-            if (rows[w].seg >= 0) total += cb * sb_bytes(rows[w].type);
+    if (warp == kConsumerWarps) {
+        // ---------------- producer: one bulk copy per stage (a whole 8-row tile), weights
+        // only, so it runs ahead of griddepcontrol.wait
+        if (lane == 0) {
+            const uint64_t policy = l2_evict_first_policy();
+            int it = 0;
+            for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+                const int s_ = unit_seg(p, u);
+                const DevMatrix& m = p.seg[s_].m;
+                const int sbb = sb_bytes(m.type);
+                const int64_t tile0 = (int64_t)(u - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
+                for (int c = 0; c < p.nchunks; c++, it++) {
+                    const int s = it % S;
+                    if (it >= S && !mbar_wait_bounded(&empty[s], ((it / S) - 1) & 1, p.err)) return;
+                    const int cb = min(p.cbs, nsb - c * p.cbs);
+                    const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
+                    mbar_expect_tx(&full[s], bytes);
+                    bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
+                             &full[s], policy);
+                }
+            }
         }
-        mbar_expect_tx(&full[s], total);
-#pragma unroll
-        for (int w = 0; w < kWarps; w++) {
-            if (rows[w].seg < 0) continue;
-            const int sbb = sb_bytes(rows[w].type);
-            const uint8_t* src = rows[w].main + rows[w].row * rows[w].row_bytes + (int64_t)c0 * sbb;
-            bulk_g2s(ring + (s * kWarps + w) * p.slot_bytes, src, cb * sbb, &full[s], policy);
-        }
-    };
-    if (tid == 0) {
-        policy = l2_evict_first_policy();
-        for (int c = 0; c < S && c < nchunks; c++) issue(c);
+        return;
     }
 
-    // Everything above reads only weights; activations come from the previous kernel.
+    // ---------------- consumers: one warp per tile row
     pdl_wait();
+    // The next kernel may start (and prefetch its weights) only once this one is past its
+    // own wait, so at most two kernels of a chain overlap.
     pdl_launch_dependents();
-
     build_activation(p, smem, red);
-    __syncthreads();
+    consumer_sync();
 
     Act a;
     a.f32 = p.act_f32 >= 0 ? reinterpret_cast<const float*>(smem + p.act_f32) : nullptr;
     a.q8k = p.act_q8k >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act_q8k) : nullptr;
     a.q8k_d = p.act_q8k >= 0 ? reinterpret_cast<const float*>(smem + p.act_q8k_d) : nullptr;
     a.q8k_bs = p.act_q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act_q8k_bs) : nullptr;
+    a.q8k_ps = p.act_q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act_q8k_ps) : nullptr;
     a.q80 = p.act_q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act_q80) : nullptr;
     a.q80_d = p.act_q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act_q80_d) : nullptr;
 
-    const uint16_t* drow = wr.dplane ? wr.dplane + (int64_t)wr.row * wr.d_per_row : nullptr;
-    int32_t* isum_row = nullptr;
-    int32_t* msum_row = nullptr;
-    if (EPI == EPI_DOTS && wr.seg >= 0) {
-        const int per_row = wr.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
-        isum_row = p.isum + (int64_t)wr.row * per_row;
-        msum_row = p.msum ? p.msum + (int64_t)wr.row * per_row : nullptr;
-    }
-
-    float acc = 0.f;
+    int it = 0;
     bool timed_out = false;
-    for (int c = 0; c < nchunks; c++) {
-        const int s = c % S;
-        if (!mbar_wait_bounded(&full[s], (c / S) & 1, p.err)) timed_out = true;
-        if (!timed_out && wr.seg >= 0) {
-            const uint8_t* slot = ring + (s * kWarps + warp) * p.slot_bytes;
-            const int c0 = c * cbs, cb = min(cbs, nsb - c0);
-            switch (wr.type) {
-            case TPTC_TYPE_Q4_K: acc += chunk_q4k<EPI == EPI_DOTS>(slot, a, c0, cb, lane, isum_row, msum_row); break;
-            case TPTC_TYPE_Q6_K: acc += chunk_q6k<EPI == EPI_DOTS>(slot, drow, a, c0, cb, lane, isum_row); break;
-            case TPTC_TYPE_Q8_0: acc += chunk_q80<EPI == EPI_DOTS>(slot, drow, a, c0, cb, lane, isum_row); break;
-            default: acc += chunk_f16(slot, a, c0, cb, lane); break;
-            }
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const UnitRow ur = unit_row(p, u, warp);
+        const DevMatrix& m = p.seg[ur.seg < 0 ? unit_seg(p, u) : ur.seg].m;
+        const int sbb = sb_bytes(m.type);
+        const int prow = (u - p.seg[unit_seg(p, u)].unit_begin) * kTileRows + warp;
+        const uint16_t* drow = m.dplane ? m.dplane + (int64_t)prow * m.d_per_row : nullptr;
+        int32_t* isum_row = nullptr;
+        int32_t* msum_row = nullptr;
+        if (EPI == EPI_DOTS && ur.seg >= 0) {
+            const int per_row = m.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
+            isum_row = p.isum + (int64_t)ur.row * per_row;
+            msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
         }
-        if (__syncthreads_or(timed_out)) return;  // every thread leaves together
-        if (tid == 0 && c + S < nchunks) {
-            fence_proxy_async_smem();
-            issue(c + S);
-        }
-    }
-    if (EPI == EPI_DOTS) return;
-
-    const float y = warp_sum(acc);
-    if (EPI == EPI_STORE) {
-        if (lane == 0 && wr.seg >= 0) p.out[wr.row] = y;
-    } else if (EPI == EPI_RESID) {
-        if (lane == 0 && wr.seg >= 0) p.out[wr.row] += y;
-    } else if (EPI == EPI_QKV) {
-        if (lane == 0) res[warp] = y;
-        __syncthreads();
-        if (tid < kWarps) {
-            const WarpRow r = warp_row(p, tid);
-            if (r.seg >= 0) {
-                const int pos = *p.pos;
-                const int d = r.row % p.hd, head = r.row / p.hd;
-                float v = res[tid];
-                if (r.seg <= 1) {  // q or k: interleaved-pair rotation (rope_i)
-                    const int i = d >> 1;
-                    const float c = p.rope_cos[(int64_t)pos * (p.hd / 2) + i];
-                    const float sn = p.rope_sin[(int64_t)pos * (p.hd / 2) + i];
-                    if ((d & 1) == 0) v = __fsub_rn(__fmul_rn(res[tid], c), __fmul_rn(res[tid + 1], sn));
-                    else v = __fadd_rn(__fmul_rn(res[tid - 1], sn), __fmul_rn(res[tid], c));
-                }
-                if (r.seg == 0) {
-                    p.out[r.row] = v;
-                } else {
-                    void* cache = r.seg == 1 ? p.kcache : p.vcache;
-                    const int64_t at = ((int64_t)head * p.max_seq + pos) * p.hd + d;
-                    if (p.kv_f32) static_cast<float*>(cache)[at] = v;
-                    else static_cast<__half*>(cache)[at] = __float2half_rn(v);
+        float acc = 0.f;
+        for (int c = 0; c < p.nchunks; c++, it++) {
+            const int s = it % S;
+            if (!timed_out && !mbar_wait_bounded(&full[s], (it / S) & 1, p.err)) timed_out = true;
+            if (!timed_out && ur.seg >= 0) {
+                const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
+                const uint8_t* slot = ring + s * p.stage_bytes + warp * cb * sbb;
+                switch (m.type) {
+                case TPTC_TYPE_Q4_K:
+                    if (EPI == EPI_DOTS) chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+                    else acc += chunk_q4k_fwd(slot, a, c0, cb, lane, 0, 32);
+                    break;
+                case TPTC_TYPE_Q6_K:
+                    if (EPI == EPI_DOTS) chunk_q6k<true>(slot, drow, a, c0, cb, lane, 0, 32, isum_row);
+                    else acc += chunk_q6k_fwd(slot, drow, a, c0, cb, lane, 0, 32);
+                    break;
+                case TPTC_TYPE_Q8_0:
+                    acc += chunk_q80<EPI == EPI_DOTS>(slot, drow, a, c0, cb, lane, 0, 32, isum_row);
+                    break;
+                default: acc += chunk_f16(slot, a, c0, cb, lane, 0, 32); break;
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-    } else if (EPI == EPI_GLU) {
-        if (lane == 0) res[warp] = y;
-        __syncthreads();
-        if (tid < 4) {
-            const WarpRow r = warp_row(p, tid);
-            if (r.seg >= 0) {
-                const float g = res[tid], u = res[tid + 4];
-                p.out[r.row] = __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u);
+        if (EPI == EPI_DOTS) continue;
+        const float y = warp_sum(acc);
+        if (EPI == EPI_GLU) {
+            // tile rows 0-3 are gate rows, 4-7 the matching up rows: the up warp hands its
+            // value to the gate warp through shared memory (double-buffered by unit parity,
+            // one two-warp named barrier per unit), which writes silu(gate) * up
+            const int buf = unit_no & 1;
+            if (warp >= 4 && lane == 0) glu_up[buf][warp - 4] = y;
+            pair_sync(warp & 3);
+            if (warp < 4 && lane == 0 && ur.seg >= 0)
+                p.out[ur.out] = __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
+            unit_no++;
+            continue;
+        }
+        if (lane != 0 || ur.seg < 0) continue;
+        if (EPI == EPI_STORE) {
+            p.out[ur.row] = y;
+        } else if (EPI == EPI_RESID) {
+            p.out[ur.out] += y;
+        } else if (EPI == EPI_QKV) {
+            if (ur.seg == 0) {
+                p.out[ur.row] = y;  // q before RoPE
+            } else if (ur.seg == 1) {
+                p.kraw[ur.row] = y;  // k before RoPE
+            } else {
+                const int pos = *p.pos, d = ur.row % p.hd, head = ur.row / p.hd;
+                const int64_t at = ((int64_t)head * p.max_seq + pos) * p.hd + d;
+                if (p.kv_f32) static_cast<float*>(p.vcache)[at] = y;
+                else static_cast<__half*>(p.vcache)[at] = __float2half_rn(y);
             }
         }
     }
@@ -438,15 +610,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
 
 }  // namespace
 
-void gemv_prepare(GemvParams& p) {
+void gemv_prepare(GemvParams& p, int sm_count) {
     bool need_f32 = false, need_q8k = false, need_q80 = false;
-    int slot = 0;
+    int sbb_max = 0;
     for (int s = 0; s < p.nseg; s++) {
-        const int t = p.seg[s].type;
+        const int t = p.seg[s].m.type;
         if (t == TPTC_TYPE_F16) need_f32 = true;
         else if (t == TPTC_TYPE_Q8_0) need_q80 = true;
         else need_q8k = true;
-        slot = std::max(slot, chunk_sb(t) * sb_bytes(t));
+        sbb_max = std::max(sbb_max, sb_bytes(t));
     }
     const int K = p.K;
     int off = 0;
@@ -459,29 +631,35 @@ void gemv_prepare(GemvParams& p) {
     p.act_q8k = need_q8k ? take(K) : -1;
     p.act_q8k_d = need_q8k ? take(K / QK_K * 4) : -1;
     p.act_q8k_bs = need_q8k ? take(K / 16 * 2) : -1;
+    p.act_q8k_ps = need_q8k ? take(K / 32 * 2) : -1;
     p.act_q80 = need_q80 ? take(K) : -1;
     p.act_q80_d = need_q80 ? take(K / QK8_0 * 4) : -1;
     p.act_bytes = (off + 127) / 128 * 128;
-    p.slot_bytes = slot;
-    const int nsb = K / QK_K;
-    const int cbs = chunk_sb(p.seg[0].type);
-    const int nchunks = (nsb + cbs - 1) / cbs;
-    p.stages = std::min(nchunks, 2);
+
+    p.cbs = p.seg[0].m.cbs;
+    p.nchunks = (K / QK_K + p.cbs - 1) / p.cbs;
+    p.stage_bytes = kTileRows * p.cbs * sbb_max;
+    int ub = 0;
+    for (int s = 0; s < p.nseg; s++) {
+        p.seg[s].unit_begin = ub;
+        ub += p.seg[s].m.Npad / kTileRows;
+    }
+    p.units = ub;
+    const int ring = kRingBudget - p.act_bytes;
+    const int S = std::max(2, std::min(kGemvMaxStages, ring / p.stage_bytes));
+    // two persistent CTAs per SM: 16 consumer warps and two producers hide shared-memory
+    // and copy latency better than one
+    p.grid = std::min(p.units, 2 * sm_count);
+    const int needed = ((p.units + p.grid - 1) / p.grid) * p.nchunks;
+    p.stages = std::max(1, std::min(S, needed));
 }
 
-int gemv_grid(const GemvParams& p) {
-    if (p.paired) return ceil_div(p.seg[0].N, 4);
-    int n = 0;
-    for (int s = 0; s < p.nseg; s++) n += ceil_div(p.seg[s].N, kWarps);
-    return n;
-}
-
-size_t gemv_smem(const GemvParams& p) { return (size_t)p.act_bytes + (size_t)p.stages * kWarps * p.slot_bytes; }
+size_t gemv_smem(const GemvParams& p) { return (size_t)p.act_bytes + (size_t)p.stages * p.stage_bytes; }
 
 template <int EPI>
 static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(gemv_grid(p));
+    cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = gemv_smem(p);
     cfg.stream = st;
@@ -493,17 +671,8 @@ static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
     return cudaLaunchKernelEx(&cfg, gemv_kernel<EPI>, p);
 }
 
-cudaError_t gemv_init_device() {
-    const int max_smem = 200 * 1024;
-    cudaError_t e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    return cudaFuncSetAttribute(gemv_kernel<EPI_DOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-}
-
 cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl) {
+    if (p.stages < 1 || p.stages > kGemvMaxStages || p.grid < 1) return cudaErrorInvalidValue;
     switch (epi) {
     case EPI_STORE: return launch_epi<EPI_STORE>(p, st, pdl);
     case EPI_RESID: return launch_epi<EPI_RESID>(p, st, pdl);
@@ -512,6 +681,16 @@ cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl)
     case EPI_DOTS: return launch_epi<EPI_DOTS>(p, st, pdl);
     }
     return cudaErrorInvalidValue;
+}
+
+cudaError_t gemv_init_device() {
+    const int max_smem = 200 * 1024;
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    return cudaFuncSetAttribute(gemv_kernel<EPI_DOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
 
 }  // namespace tptc

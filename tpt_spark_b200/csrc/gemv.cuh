@@ -5,79 +5,123 @@
 
 namespace tptc {
 
-// Device layout of a weight matrix [N out x K in] (K a multiple of 256):
-//   Q4_K  main = GGUF blocks unchanged, 144 B per 256 elements, rows contiguous
-//   Q6_K  main = ql|qh|scales (208 B per 256) ; dplane = f16 d per block [N, K/256]
-//   Q8_0  main = qs (32 B per 32)              ; dplane = f16 d per block [N, K/32]
-//   F16   main = f16 values [N, K]
-// Every main row is a multiple of 16 bytes, so any run of whole super-blocks of a row can
-// be fetched with one 1-D bulk copy.
-struct DevMatrix {
-    int type = 0;
-    int N = 0, K = 0;
-    uint8_t* main = nullptr;
-    uint16_t* dplane = nullptr;
-    int64_t main_row_bytes = 0;  // bytes per row in `main`
-    int64_t d_per_row = 0;       // f16 entries per row in `dplane`
-    int64_t bytes() const { return main_row_bytes * N + d_per_row * 2 * N; }
-};
-
-// Bytes of `main` per 256-element super-block, and super-blocks per pipeline chunk.
+// Bytes of `main` per 256-element super-block, and super-blocks per tile chunk.
 __host__ __device__ inline int sb_bytes(int type) {
     return type == TPTC_TYPE_Q4_K ? 144 : type == TPTC_TYPE_Q6_K ? 208 : type == TPTC_TYPE_Q8_0 ? 256 : 512;
 }
 __host__ __device__ inline int chunk_sb(int type) { return type == TPTC_TYPE_F16 ? 8 : 16; }
 
+constexpr int kTileRows = 8;
+
+// Device layout of a weight matrix [N out x K in] (K a multiple of 256).
+//
+// Per-super-block encoding (256 elements):
+//   Q4_K  144 B: the GGUF block unchanged (d | dmin | scales[12] | qs[128])
+//   Q6_K  208 B: ql | qh | scales          ; dplane = f16 d per super-block [N, K/256]
+//   Q8_0  256 B: qs of eight 32-blocks     ; dplane = f16 d per 32-block   [N, K/32]
+//   F16   512 B: 256 f16 values
+// Tiling of `main`: rows are grouped by 8 (N padded to Npad, zero rows) and each row is cut
+// into chunks of cbs super-blocks; tile (rg, c) = 8 rows x chunk c is one contiguous run of
+// 8 * cb * sbb bytes (cb = cbs, or the remainder for the last chunk), rows in order.  A
+// decode GEMV stage is therefore a single 1-D bulk copy of 13-32 KB, the size the copy
+// engine needs to reach full HBM bandwidth (small copies are bound by a fixed per-copy
+// cost).  glu = 1 marks a fused gate/up matrix: tile rows 0-3 are gate rows 4t..4t+3 and
+// tile rows 4-7 the same up rows, N counts gate + up rows.
+struct DevMatrix {
+    int type = 0;
+    int N = 0, K = 0;  // logical rows (gate + up for glu) and columns
+    int Npad = 0;      // N rounded up to a multiple of 8
+    int cbs = 16;      // super-blocks per chunk
+    int glu = 0;
+    uint8_t* main = nullptr;
+    uint16_t* dplane = nullptr;  // indexed by physical (tile-order) row
+    int64_t main_row_bytes = 0;  // bytes per row in `main` (K / 256 * sbb)
+    int64_t d_per_row = 0;       // f16 entries per row in `dplane`
+    int64_t bytes() const { return main_row_bytes * N + d_per_row * 2 * N; }
+    int64_t main_bytes() const { return main_row_bytes * Npad; }
+};
+
+// Geometry of a matrix in the device layout (pointers left null).
+inline DevMatrix dm_geometry(int type, int N, int K, int glu) {
+    DevMatrix m;
+    m.type = type;
+    m.N = N;
+    m.K = K;
+    m.glu = glu;
+    m.Npad = (N + kTileRows - 1) / kTileRows * kTileRows;
+    m.cbs = chunk_sb(type);
+    m.main_row_bytes = (int64_t)(K / 256) * sb_bytes(type);
+    m.d_per_row = type == TPTC_TYPE_Q6_K ? K / 256 : type == TPTC_TYPE_Q8_0 ? K / 32 : 0;
+    return m;
+}
+
+// Physical row (tile order) of logical row `row`; for a glu matrix rows [0, N/2) are gate
+// rows and [N/2, N) up rows.
+__host__ __device__ inline int dm_phys_row(const DevMatrix& m, int row) {
+    if (!m.glu) return row;
+    const int half = m.N / 2, up = row >= half ? 1 : 0, r = up ? row - half : row;
+    return (r / 4) * 8 + (r % 4) + 4 * up;
+}
+
+// Address of super-block `sb` of physical row `prow`.
+__host__ __device__ inline const uint8_t* dm_block(const DevMatrix& m, int prow, int sb) {
+    const int sbb = sb_bytes(m.type), nsb = m.K / 256;
+    const int c = sb / m.cbs, cb = (nsb - c * m.cbs) < m.cbs ? (nsb - c * m.cbs) : m.cbs;
+    const int64_t tile = (int64_t)(prow / kTileRows) * kTileRows * m.main_row_bytes + (int64_t)c * kTileRows * m.cbs * sbb;
+    return m.main + tile + (int64_t)(prow % kTileRows) * cb * sbb + (int64_t)(sb - c * m.cbs) * sbb;
+}
+
 enum GemvEpi : int {
     EPI_STORE = 0,  // out[row] = y
     EPI_RESID = 1,  // out[row] += y   (residual stream update)
-    EPI_QKV = 2,    // RoPE on q/k rows, q -> out, k/v -> fp16 KV cache at pos
-    EPI_GLU = 3,    // paired gate/up rows: out[row] = silu(gate) * up
+    EPI_QKV = 2,    // q -> out, k -> kraw (RoPE applied by the attention kernel), v -> V cache at pos
+    EPI_GLU = 3,    // fused gate|up matrix: out[logical row] (silu(gate)*up is formed by the consumer)
     EPI_DOTS = 4,   // integer block sums (test hook)
 };
 
+constexpr int kGemvMaxSeg = 3;
+constexpr int kGemvMaxStages = 16;
+
+// One matrix of a (possibly fused) GEMV launch.  A work unit is one 8-row tile group of one
+// segment; units of consecutive segments follow each other.
 struct GemvSeg {
-    const uint8_t* main;
-    const uint16_t* dplane;
-    int type;
-    int N;
-    int64_t row_bytes;
-    int64_t d_per_row;
-    int cta_begin;  // first CTA of this segment (linear mapping)
+    DevMatrix m;
+    int unit_begin;  // filled by gemv_prepare
 };
 
 struct GemvParams {
-    GemvSeg seg[3];
+    GemvSeg seg[kGemvMaxSeg];
     int nseg;
-    int paired;  // 1: CTA b = rows 4b..4b+3 of seg0 (warps 0-3) and seg1 (warps 4-7)
     int K;
     const float* x;       // input activation [K] (f32)
     const float* norm_w;  // RMSNorm gain [K] or nullptr (no norm)
+    int glu_in;           // 1: x holds [gate | up] (2K floats); the input is silu(gate) * up
     float eps;
     float* out;
     // EPI_QKV
-    void* kcache;          // this layer's K cache, layout [n_kv][max_seq][hd], fp16 or f32
-    void* vcache;
-    int kv_f32;            // 1: the cache holds f32 (candle's precision), 0: fp16
-    const float* rope_cos;  // [max_seq][hd/2]
-    const float* rope_sin;
+    void* vcache;  // this layer's V cache, layout [n_kv][max_seq][hd], fp16 or f32
+    int kv_f32;    // 1: the cache holds f32 (candle's precision), 0: fp16
+    float* kraw;   // key rows before RoPE (the attention kernel rotates and caches them)
     const int* pos;  // device scalar: position being written
     int hd;
     int max_seq;
     // EPI_DOTS
     int32_t* isum;
     int32_t* msum;
-    // activation layout in shared memory (byte offsets; -1 = absent)
-    int act_f32, act_q8k, act_q8k_d, act_q8k_bs, act_q80, act_q80_d;
+    // filled by gemv_prepare
+    int units;        // total work units (8-row tile groups)
+    int cbs;          // super-blocks per chunk (same for every segment)
+    int nchunks;      // chunks per row
+    int stages;       // ring depth
+    int stage_bytes;  // bytes per stage (one full tile)
+    int grid;         // CTAs (persistent: units are strided over them)
+    int act_f32, act_q8k, act_q8k_d, act_q8k_bs, act_q8k_ps, act_q80, act_q80_d;  // smem offsets, -1 absent
     int act_bytes;
-    int stages;
-    int slot_bytes;
     int* err;
 };
 
 // Host helpers (gemv.cu).
-void gemv_prepare(GemvParams& p);  // fills activation offsets, stages, slot bytes
-int gemv_grid(const GemvParams& p);
+void gemv_prepare(GemvParams& p, int sm_count = 148);  // work split, ring, activation layout
 size_t gemv_smem(const GemvParams& p);
 cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl);
 cudaError_t gemv_init_device();  // per-device kernel attributes (call once per device)

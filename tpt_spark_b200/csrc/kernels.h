@@ -13,19 +13,26 @@ namespace tptc {
 cudaError_t launch_dequant_raw(int type, const void* blocks, int64_t n, float* out, cudaStream_t st);
 cudaError_t launch_quant_q8k(const float* x, int64_t k, void* out, cudaStream_t st);
 cudaError_t launch_quant_q80(const float* x, int64_t k, void* out, cudaStream_t st);
-// Raw GGUF rows [N, K] (device) -> device layout of `m` (main / dplane already allocated).
-cudaError_t launch_repack(const uint8_t* raw, const DevMatrix& m, cudaStream_t st);
+// nr raw GGUF rows (device, raw_row bytes apart) -> logical rows first_row.. of `m` in the
+// tiled device layout (main / dplane already allocated).
+cudaError_t launch_repack(const uint8_t* raw, int64_t raw_row, int nr, int first_row, const DevMatrix& m,
+                          cudaStream_t st);
 // Device-layout rows [row0, row0+rows) of `m` -> dense f16 [rows, K] (prefill operand).
 cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st);
 
 // attn_decode.cu
 struct AttnDecodeParams {
-    const float* q;        // [n_heads * hd] (rope applied)
-    const void* kcache;    // this layer, [n_kv][max_seq][hd], fp16 (default) or f32
-    const void* vcache;
+    const float* q;        // [n_heads * hd] before RoPE (rotated on load)
+    const float* kraw;     // [n_kv * hd] this position's key before RoPE
+    void* kcache;          // this layer, [n_kv][max_seq][hd], fp16 (default) or f32; the CTA
+                           // owning `pos` writes the rotated key there before reading tiles
+    const void* vcache;    // V at `pos` already written by the QKV GEMV
     int kv_f32;
+    const float* rope_cos;  // [max_seq][hd/2]
+    const float* rope_sin;
     const int* pos;        // device scalar: the query position (keys 0..pos)
     float* out;            // [n_heads * hd]
+    float* q_out;          // optional [n_heads * hd]: rotated q (test trace)
     float* partial;        // scratch [n_kv][splits][group][2 + hd]
     int* counters;         // scratch [n_kv], zero between launches
     int n_heads, n_kv, hd, max_seq, splits;

@@ -17,20 +17,20 @@ namespace {
 __global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok_ptr, float* __restrict__ x) {
     pdl_wait();
     pdl_launch_dependents();
-    const int64_t row = *tok_ptr;
+    const int row = (int)*tok_ptr;  // token_embd is never a fused gate|up matrix: phys row = row
     const int K = emb.K;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) {
+        const uint8_t* blk = dm_block(emb, row, i / QK_K);
+        const int e = i % QK_K;
         float v;
         if (emb.type == TPTC_TYPE_Q4_K) {
-            v = q4k_elem(emb.main + row * emb.main_row_bytes + (i / QK_K) * Q4K_BYTES, i % QK_K);
+            v = q4k_elem(blk, e);
         } else if (emb.type == TPTC_TYPE_Q6_K) {
-            v = q6k_elem(emb.main + row * emb.main_row_bytes + (i / QK_K) * Q6K_MAIN,
-                         h2f(emb.dplane[row * emb.d_per_row + i / QK_K]), i % QK_K);
+            v = q6k_elem(blk, h2f(emb.dplane[(int64_t)row * emb.d_per_row + i / QK_K]), e);
         } else if (emb.type == TPTC_TYPE_Q8_0) {
-            v = __fmul_rn((float)(int8_t)emb.main[row * emb.main_row_bytes + i],
-                          h2f(emb.dplane[row * emb.d_per_row + i / QK8_0]));
+            v = __fmul_rn((float)(int8_t)blk[e], h2f(emb.dplane[(int64_t)row * emb.d_per_row + i / QK8_0]));
         } else {
-            v = h2f(reinterpret_cast<const uint16_t*>(emb.main + row * emb.main_row_bytes)[i]);
+            v = h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
         }
         x[i] = v;
     }
@@ -46,11 +46,23 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     __shared__ int si[32];
     float best = -INFINITY;
     int bi = -1;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = logits[i];
-        if (bi < 0 || v > best || (v == best && i > bi)) {
-            best = v;
-            bi = i;
+    // eight independent loads in flight per thread per round
+    constexpr int U = 8;
+    const int step = blockDim.x * U;
+    for (int base = 0; base < n; base += step) {
+        float v[U];
+#pragma unroll
+        for (int k = 0; k < U; k++) {
+            const int i = base + k * blockDim.x + threadIdx.x;
+            v[k] = i < n ? logits[i] : -INFINITY;
+        }
+#pragma unroll
+        for (int k = 0; k < U; k++) {
+            const int i = base + k * blockDim.x + threadIdx.x;
+            if (i < n && (bi < 0 || v[k] > best || (v[k] == best && i > bi))) {
+                best = v[k];
+                bi = i;
+            }
         }
     }
     for (int o = 16; o > 0; o >>= 1) {

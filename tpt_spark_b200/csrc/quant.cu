@@ -54,44 +54,55 @@ __global__ void quant_q80_kernel(const float* __restrict__ x, int64_t nb, uint8_
     if (lane == 0) *reinterpret_cast<uint16_t*>(blk) = f2h(d);
 }
 
-// Repack one super-block (Q6_K) or one 32-block (Q8_0) per thread; Q4_K / F16 copy bytes.
-__global__ void repack_kernel(const uint8_t* __restrict__ raw, int type, int64_t nblocks, uint8_t* __restrict__ main,
-                              uint16_t* __restrict__ dplane) {
-    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    if (type == TPTC_TYPE_Q6_K) {
-        const uint8_t* src = raw + b * Q6K_BYTES;
-        uint8_t* dst = main + b * Q6K_MAIN;
-        for (int i = 0; i < Q6K_MAIN; i++) dst[i] = src[i];
-        dplane[b] = (uint16_t)(src[208] | (src[209] << 8));
-    } else if (type == TPTC_TYPE_Q8_0) {
-        const uint8_t* src = raw + b * Q80_BYTES;
-        uint8_t* dst = main + b * 32;
-        for (int i = 0; i < 32; i++) dst[i] = src[2 + i];
-        dplane[b] = (uint16_t)(src[0] | (src[1] << 8));
+// Raw GGUF rows -> tiled device layout, one thread per 256-element super-block.  `nr` raw
+// rows (raw_row bytes apart) become logical rows first_row .. first_row + nr - 1 of `m`.
+__global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, int nr, int first_row, DevMatrix m) {
+    const int nsb = m.K / QK_K;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)nr * nsb) return;
+    const int r = (int)(i / nsb), sb = (int)(i % nsb);
+    const int prow = dm_phys_row(m, first_row + r);
+    uint8_t* dst = const_cast<uint8_t*>(dm_block(m, prow, sb));
+    const uint8_t* row = raw + (int64_t)r * raw_row;
+    if (m.type == TPTC_TYPE_Q4_K) {
+        const uint8_t* src = row + (int64_t)sb * Q4K_BYTES;
+        for (int k = 0; k < Q4K_BYTES; k++) dst[k] = src[k];
+    } else if (m.type == TPTC_TYPE_Q6_K) {
+        const uint8_t* src = row + (int64_t)sb * Q6K_BYTES;
+        for (int k = 0; k < Q6K_MAIN; k++) dst[k] = src[k];
+        m.dplane[(int64_t)prow * m.d_per_row + sb] = (uint16_t)(src[208] | (src[209] << 8));
+    } else if (m.type == TPTC_TYPE_Q8_0) {
+        for (int j = 0; j < 8; j++) {
+            const uint8_t* src = row + ((int64_t)sb * 8 + j) * Q80_BYTES;
+            for (int k = 0; k < 32; k++) dst[32 * j + k] = src[2 + k];
+            m.dplane[(int64_t)prow * m.d_per_row + sb * 8 + j] = (uint16_t)(src[0] | (src[1] << 8));
+        }
+    } else {
+        const uint8_t* src = row + (int64_t)sb * 512;
+        for (int k = 0; k < 512; k++) dst[k] = src[k];
     }
 }
 
-// Device layout -> dense f16, one thread per 8 consecutive elements of a row.
+// Device layout -> dense f16 rows [row0, row0 + rows), one thread per 8 consecutive elements.
 __global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, __half* __restrict__ out) {
     const int64_t per_row = m.K / 8;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= per_row * rows) return;
     const int r = (int)(i / per_row), k0 = (int)(i % per_row) * 8;
-    const int64_t row = row0 + r;
+    const int prow = dm_phys_row(m, row0 + r);
+    const uint8_t* blk = dm_block(m, prow, k0 / QK_K);
+    const int e0 = k0 % QK_K;
     __align__(16) __half v[8];
     if (m.type == TPTC_TYPE_F16) {
-        *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(m.main + row * m.main_row_bytes + k0 * 2);
+        *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(blk + e0 * 2);
     } else if (m.type == TPTC_TYPE_Q4_K) {
-        const uint8_t* blk = m.main + row * m.main_row_bytes + (k0 / QK_K) * Q4K_BYTES;
-        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q4k_elem(blk, (k0 + j) % QK_K));
+        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q4k_elem(blk, e0 + j));
     } else if (m.type == TPTC_TYPE_Q6_K) {
-        const uint8_t* blk = m.main + row * m.main_row_bytes + (k0 / QK_K) * Q6K_MAIN;
-        const float d = h2f(m.dplane[row * m.d_per_row + k0 / QK_K]);
-        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q6k_elem(blk, d, (k0 + j) % QK_K));
+        const float d = h2f(m.dplane[(int64_t)prow * m.d_per_row + k0 / QK_K]);
+        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q6k_elem(blk, d, e0 + j));
     } else {
-        const int8_t* q = reinterpret_cast<const int8_t*>(m.main + row * m.main_row_bytes + k0);
-        const float d = h2f(m.dplane[row * m.d_per_row + k0 / QK8_0]);
+        const int8_t* q = reinterpret_cast<const int8_t*>(blk + e0);
+        const float d = h2f(m.dplane[(int64_t)prow * m.d_per_row + k0 / QK8_0]);
         for (int j = 0; j < 8; j++) v[j] = __float2half_rn(__fmul_rn((float)q[j], d));
     }
     *reinterpret_cast<uint4*>(out + (int64_t)r * m.K + k0) = *reinterpret_cast<const uint4*>(v);
@@ -120,12 +131,11 @@ cudaError_t launch_quant_q80(const float* x, int64_t k, void* out, cudaStream_t 
     return cudaGetLastError();
 }
 
-cudaError_t launch_repack(const uint8_t* raw, const DevMatrix& m, cudaStream_t st) {
-    const int64_t n = (int64_t)m.N * m.K;
-    if (m.type == TPTC_TYPE_Q4_K || m.type == TPTC_TYPE_F16)
-        return cudaMemcpyAsync(m.main, raw, m.main_row_bytes * m.N, cudaMemcpyDeviceToDevice, st);
-    const int64_t nblocks = m.type == TPTC_TYPE_Q6_K ? n / QK_K : n / QK8_0;
-    repack_kernel<<<(unsigned)ceil_div64(nblocks, 256), 256, 0, st>>>(raw, m.type, nblocks, m.main, m.dplane);
+cudaError_t launch_repack(const uint8_t* raw, int64_t raw_row, int nr, int first_row, const DevMatrix& m,
+                          cudaStream_t st) {
+    const int64_t n = (int64_t)nr * (m.K / QK_K);
+    if (n <= 0) return cudaSuccess;
+    repack_kernel<<<(unsigned)ceil_div64(n, 128), 128, 0, st>>>(raw, raw_row, nr, first_row, m);
     return cudaGetLastError();
 }
 
