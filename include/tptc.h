@@ -186,6 +186,28 @@ TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void*
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,
                              void* stream);
 
+/* GQA attention of one query position, the decode step of attention.wgsl's three passes
+ * (scores :31-58, softmax :73-135, P.V :152-170; dispatched from wgpu_engine.rs:666-726).
+ *   d_q [n_heads * head_dim], d_kraw [n_kv * head_dim]: q and this position's key before RoPE;
+ *     both are rotated (candle rope_i) with d_rope_cos / d_rope_sin [max_seq][head_dim / 2].
+ *   d_kcache, d_vcache [n_kv][max_seq][head_dim] of kv_type (TPTC_TYPE_F16 or TPTC_TYPE_F32):
+ *     the rotated key is written to d_kcache at position *d_pos; V at *d_pos must be present.
+ *   d_pos: device int p, 0 <= p < max_seq; keys and values 0..p are attended.
+ *   d_out [n_heads * head_dim] = softmax(q.k / sqrt(head_dim)) . V, query head h reading kv
+ *     head h / (n_heads / n_kv).
+ * Limits: n_heads a multiple of n_kv with at most 8 query heads per kv head; head_dim a
+ * multiple of 16, at most 128.  d_workspace holds tptc_attn_decode_workspace_bytes() bytes
+ * (for the current device) and must be zero before its first use; each call leaves it ready
+ * for the next (its split counters return to zero, the partial results are overwritten).  Its
+ * first int receives a nonzero TPTC_ERR_* code if the kernel found p outside [0, max_seq)
+ * (nothing is written then) or a copy wait timed out.  Calls that may overlap on the GPU need
+ * separate workspaces. */
+TPTC_API int64_t tptc_attn_decode_workspace_bytes(int n_heads, int n_kv, int head_dim, int max_seq);
+TPTC_API int tptc_attn_decode(const float* d_q, const float* d_kraw, void* d_kcache, const void* d_vcache,
+                              int kv_type, const float* d_rope_cos, const float* d_rope_sin, const int* d_pos,
+                              int n_heads, int n_kv, int head_dim, int max_seq, float* d_out, void* d_workspace,
+                              int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

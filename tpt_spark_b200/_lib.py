@@ -69,6 +69,9 @@ SIGNATURES = {
     "tptc_matrix_bytes": (c_i64, [c_vp]),
     "tptc_gemv": (c_int, [c_vp, c_vp, c_vp, c_vp]),
     "tptc_block_dots": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "tptc_attn_decode_workspace_bytes": (c_i64, [c_int, c_int, c_int, c_int]),
+    "tptc_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp,
+                                 c_vp, c_i64, c_vp]),
 }
 
 _L = None

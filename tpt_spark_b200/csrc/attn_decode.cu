@@ -72,6 +72,10 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
     pdl_launch_dependents();
 
     const int kv_len = *p.pos + 1;
+    if (kv_len < 1 || kv_len > p.max_seq) {  // position outside the cache: flag it, touch nothing
+        if (tid == 0 && kvh == 0 && split == 0 && p.err) atomicExch(p.err, TPTC_ERR_ARG);
+        return;
+    }
     int per = (kv_len + p.splits - 1) / p.splits;
     per = (per + kT - 1) / kT * kT;
     const int t_begin = split * per, t_end = min(kv_len, t_begin + per);
@@ -297,9 +301,26 @@ size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits) {
     return (size_t)n_kv * splits * (n_heads / n_kv) * (2 + hd);
 }
 
+const char* attn_decode_shape_error(int n_heads, int n_kv, int hd, int max_seq) {
+    if (n_heads <= 0 || n_kv <= 0 || hd <= 0 || max_seq <= 0) return "attention: sizes must be positive";
+    if (n_heads % n_kv != 0) return "attention: n_heads must be a multiple of n_kv";
+    if (n_heads / n_kv > kMaxGroup) return "attention: at most 8 query heads per kv head";
+    if (hd > kThreads || hd % 16 != 0) return "attention: head_dim must be a multiple of 16, at most 128";
+    return nullptr;
+}
+
+AttnScratch attn_scratch_layout(int n_heads, int n_kv, int hd, int max_seq, int sm_count) {
+    AttnScratch s;
+    s.splits = attn_decode_splits(n_kv, max_seq, sm_count);
+    s.err = 0;
+    s.counters = 256;
+    s.partial = s.counters + ((size_t)n_kv * sizeof(int) + 255) / 256 * 256;
+    s.total = s.partial + attn_decode_partial_floats(n_heads, n_kv, hd, s.splits) * sizeof(float);
+    return s;
+}
+
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl) {
-    if (p.n_heads % p.n_kv != 0 || p.n_heads / p.n_kv > kMaxGroup || p.hd > kThreads || p.hd % 16 != 0)
-        return cudaErrorInvalidValue;
+    if (attn_decode_shape_error(p.n_heads, p.n_kv, p.hd, p.max_seq)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.n_kv, p.splits);
     cfg.blockDim = dim3(kThreads);

@@ -303,6 +303,91 @@ TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void*
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemv");
 }
 
+// Kernel attributes of the current device, set once per device (allocates nothing).
+static int ensure_kernels(int* dev_out, int* sms_out) {
+    static std::mutex mu;
+    static bool done[256];
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "device query");
+    if (dev < 0 || dev >= 256) return fail_code(nullptr, TPTC_ERR_UNSUPPORTED, "device ordinal above 255");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!done[dev]) {
+        e = tptc::kernels_init_device();
+        if (e != cudaSuccess) return cuda_fail(e, "kernel setup");
+        done[dev] = true;
+    }
+    *dev_out = dev;
+    *sms_out = sms;
+    return TPTC_OK;
+}
+
+static int attn_args(const float* q, const float* kraw, void* kc, const void* vc, int kv_type, const float* cs,
+                     const float* sn, const int* pos, float* out, int n_heads, int n_kv, int hd, int max_seq) {
+    if (!q || !kraw || !kc || !vc || !cs || !sn || !pos || !out)
+        return fail_code(nullptr, TPTC_ERR_ARG, "attention: null pointer");
+    if (kv_type != TPTC_TYPE_F16 && kv_type != TPTC_TYPE_F32)
+        return fail_code(nullptr, TPTC_ERR_UNSUPPORTED, "attention: kv_type must be TPTC_TYPE_F16 or TPTC_TYPE_F32");
+    if (const char* why = tptc::attn_decode_shape_error(n_heads, n_kv, hd, max_seq))
+        return fail_code(nullptr, TPTC_ERR_ARG, why);
+    return TPTC_OK;
+}
+
+// One attention launch over scratch `ws` laid out by attn_scratch_layout.
+static int attn_launch(const float* q, const float* kraw, void* kc, const void* vc, int kv_type, const float* cs,
+                       const float* sn, const int* pos, float* out, int n_heads, int n_kv, int hd, int max_seq,
+                       uint8_t* ws, const tptc::AttnScratch& L, cudaStream_t st) {
+    tptc::AttnDecodeParams a = {};
+    a.q = q;
+    a.kraw = kraw;
+    a.kcache = kc;
+    a.vcache = vc;
+    a.kv_f32 = kv_type == TPTC_TYPE_F32;
+    a.rope_cos = cs;
+    a.rope_sin = sn;
+    a.pos = pos;
+    a.out = out;
+    a.partial = reinterpret_cast<float*>(ws + L.partial);
+    a.counters = reinterpret_cast<int*>(ws + L.counters);
+    a.err = reinterpret_cast<int*>(ws + L.err);
+    a.n_heads = n_heads;
+    a.n_kv = n_kv;
+    a.hd = hd;
+    a.max_seq = max_seq;
+    a.splits = L.splits;
+    a.scale = 1.0f / sqrtf((float)hd);
+    cudaError_t e = tptc::launch_attn_decode(a, st, false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "attn_decode");
+}
+
+TPTC_API int64_t tptc_attn_decode_workspace_bytes(int n_heads, int n_kv, int head_dim, int max_seq) {
+    if (const char* why = tptc::attn_decode_shape_error(n_heads, n_kv, head_dim, max_seq))
+        return fail_code(nullptr, TPTC_ERR_ARG, why);
+    int dev = 0, sms = 0;
+    if (int rc = ensure_kernels(&dev, &sms)) return rc;
+    return (int64_t)tptc::attn_scratch_layout(n_heads, n_kv, head_dim, max_seq, sms).total;
+}
+
+TPTC_API int tptc_attn_decode(const float* d_q, const float* d_kraw, void* d_kcache, const void* d_vcache, int kv_type,
+                              const float* d_rope_cos, const float* d_rope_sin, const int* d_pos, int n_heads, int n_kv,
+                              int head_dim, int max_seq, float* d_out, void* d_workspace, int64_t workspace_bytes,
+                              void* stream) {
+    if (int rc = attn_args(d_q, d_kraw, d_kcache, d_vcache, kv_type, d_rope_cos, d_rope_sin, d_pos, d_out, n_heads,
+                           n_kv, head_dim, max_seq))
+        return rc;
+    if (!d_workspace) return fail_code(nullptr, TPTC_ERR_ARG, "attention: null workspace");
+    int dev = 0, sms = 0;
+    if (int rc = ensure_kernels(&dev, &sms)) return rc;
+    const tptc::AttnScratch L = tptc::attn_scratch_layout(n_heads, n_kv, head_dim, max_seq, sms);
+    if (workspace_bytes < (int64_t)L.total)
+        return fail_code(nullptr, TPTC_ERR_ARG,
+                         "attention: workspace of " + std::to_string(workspace_bytes) + " bytes, " +
+                             std::to_string(L.total) + " needed");
+    return attn_launch(d_q, d_kraw, d_kcache, d_vcache, kv_type, d_rope_cos, d_rope_sin, d_pos, d_out, n_heads, n_kv,
+                       head_dim, max_seq, static_cast<uint8_t*>(d_workspace), L, static_cast<cudaStream_t>(stream));
+}
+
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum, void* stream) {
     if (!m || !d_x || !d_isum) return TPTC_ERR_ARG;
     if (m->m.type == TPTC_TYPE_F16) return TPTC_ERR_UNSUPPORTED;

@@ -41,6 +41,15 @@ struct AttnDecodeParams {
 };
 int attn_decode_splits(int n_kv, int max_seq, int sm_count);
 size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits);
+// nullptr when the kernel supports the shape, else the reason.
+const char* attn_decode_shape_error(int n_heads, int n_kv, int hd, int max_seq);
+// Scratch of one launch as one buffer (kernel-level entry points): byte offsets of the
+// error word (0), the counters ([n_kv] int, zero between launches) and the partials.
+struct AttnScratch {
+    int splits;
+    size_t counters, err, partial, total;
+};
+AttnScratch attn_scratch_layout(int n_heads, int n_kv, int hd, int max_seq, int sm_count);
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl);
 
 // misc.cu

@@ -61,3 +61,16 @@ class Matrix:
             self.close()
         except Exception:
             pass
+
+
+def attn_decode_workspace_bytes(n_heads: int, n_kv: int, head_dim: int, max_seq: int) -> int:
+    return check(lib().tptc_attn_decode_workspace_bytes(n_heads, n_kv, head_dim, max_seq))
+
+
+def attn_decode(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_cos, d_rope_sin, d_pos, n_heads: int,
+                n_kv: int, head_dim: int, max_seq: int, d_out, d_workspace, workspace_bytes: int,
+                stream: Optional[int] = None) -> None:
+    """One decode-step attention (tptc_attn_decode); every buffer a device pointer or tensor."""
+    check(lib().tptc_attn_decode(_ptr(d_q), _ptr(d_kraw), _ptr(d_kcache), _ptr(d_vcache), kv_type, _ptr(d_rope_cos),
+                                 _ptr(d_rope_sin), _ptr(d_pos), n_heads, n_kv, head_dim, max_seq, _ptr(d_out),
+                                 _ptr(d_workspace), workspace_bytes, stream))
