@@ -36,7 +36,7 @@ def rope(x, c, s):
 
 
 def reference(q, kraw, kc, vc, cs, sn, pos, n_heads, n_kv, hd, kv_dtype):
-    krot = rope(kraw, cs[pos], sn[pos]).to(kv_dtype)
+    krot = rope(kraw.view(n_kv, hd), cs[pos], sn[pos]).to(kv_dtype)
     keys = kc[:, : pos + 1].float().clone()
     keys[:, pos] = krot.float()
     vals = vc[:, : pos + 1].float()
