@@ -72,6 +72,8 @@ SIGNATURES = {
     "tptc_attn_decode_workspace_bytes": (c_i64, [c_int, c_int, c_int, c_int]),
     "tptc_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp,
                                  c_vp, c_i64, c_vp]),
+    "tptc_attn_decode_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
+                                         c_vp, c_vp]),
 }
 
 _L = None

@@ -388,6 +388,28 @@ TPTC_API int tptc_attn_decode(const float* d_q, const float* d_kraw, void* d_kca
                        head_dim, max_seq, static_cast<uint8_t*>(d_workspace), L, static_cast<cudaStream_t>(stream));
 }
 
+TPTC_API int tptc_attn_decode_noalloc(const float* d_q, const float* d_kraw, void* d_kcache, const void* d_vcache,
+                                      int kv_type, const float* d_rope_cos, const float* d_rope_sin, const int* d_pos,
+                                      int n_heads, int n_kv, int head_dim, int max_seq, float* d_out, void* stream) {
+    if (int rc = attn_args(d_q, d_kraw, d_kcache, d_vcache, kv_type, d_rope_cos, d_rope_sin, d_pos, d_out, n_heads,
+                           n_kv, head_dim, max_seq))
+        return rc;
+    int dev = 0, sms = 0;
+    if (int rc = ensure_kernels(&dev, &sms)) return rc;
+    const tptc::AttnScratch L = tptc::attn_scratch_layout(n_heads, n_kv, head_dim, max_seq, sms);
+    if (L.total > tptc::kAttnNoAllocScratchBytes)
+        return fail_code(nullptr, TPTC_ERR_ARG,
+                         "attention (no-alloc): these sizes need " + std::to_string(L.total) +
+                             " bytes of scratch, above the static maximum of " +
+                             std::to_string(tptc::kAttnNoAllocScratchBytes) + " bytes");
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = nullptr;
+    cudaError_t e = tptc::attn_noalloc_scratch(dev, st, &ws);
+    if (e != cudaSuccess) return cuda_fail(e, "attention (no-alloc) scratch set-up");
+    return attn_launch(d_q, d_kraw, d_kcache, d_vcache, kv_type, d_rope_cos, d_rope_sin, d_pos, d_out, n_heads, n_kv,
+                       head_dim, max_seq, ws, L, st);
+}
+
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum, void* stream) {
     if (!m || !d_x || !d_isum) return TPTC_ERR_ARG;
     if (m->m.type == TPTC_TYPE_F16) return TPTC_ERR_UNSUPPORTED;

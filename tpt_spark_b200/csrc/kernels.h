@@ -52,6 +52,12 @@ struct AttnScratch {
 AttnScratch attn_scratch_layout(int n_heads, int n_kv, int hd, int max_seq, int sm_count);
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl);
 
+// attn_noalloc.cu: static per-device scratch of tptc_attn_decode_noalloc (allocates nothing).
+constexpr size_t kAttnNoAllocScratchBytes = size_t(1) << 20;
+// Address of `device`'s static scratch (the current device); the first call per device looks
+// it up and zeroes it on `st` (synchronously).
+cudaError_t attn_noalloc_scratch(int device, cudaStream_t st, uint8_t** out);
+
 // misc.cu
 // x[dim] = dequantised row `tok` of token_embd (device layout), token read from *tok_ptr.
 cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl);

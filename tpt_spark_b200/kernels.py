@@ -74,3 +74,11 @@ def attn_decode(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_cos, d_rop
     check(lib().tptc_attn_decode(_ptr(d_q), _ptr(d_kraw), _ptr(d_kcache), _ptr(d_vcache), kv_type, _ptr(d_rope_cos),
                                  _ptr(d_rope_sin), _ptr(d_pos), n_heads, n_kv, head_dim, max_seq, _ptr(d_out),
                                  _ptr(d_workspace), workspace_bytes, stream))
+
+
+def attn_decode_noalloc(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_cos, d_rope_sin, d_pos, n_heads: int,
+                        n_kv: int, head_dim: int, max_seq: int, d_out, stream: Optional[int] = None) -> None:
+    """tptc_attn_decode_noalloc: as attn_decode, with the library's static scratch (no allocation)."""
+    check(lib().tptc_attn_decode_noalloc(_ptr(d_q), _ptr(d_kraw), _ptr(d_kcache), _ptr(d_vcache), kv_type,
+                                         _ptr(d_rope_cos), _ptr(d_rope_sin), _ptr(d_pos), n_heads, n_kv, head_dim,
+                                         max_seq, _ptr(d_out), stream))
