@@ -195,8 +195,8 @@ TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_
  *   d_pos: device int p, 0 <= p < max_seq; keys and values 0..p are attended.
  *   d_out [n_heads * head_dim] = softmax(q.k / sqrt(head_dim)) . V, query head h reading kv
  *     head h / (n_heads / n_kv).
- * Limits: n_heads a multiple of n_kv with at most 8 query heads per kv head; head_dim a
- * multiple of 16, at most 128.  d_workspace holds tptc_attn_decode_workspace_bytes() bytes
+ * Limits: n_heads a multiple of n_kv with at most 8 query heads per kv head; head_dim 64,
+ * 96 or 128.  d_workspace holds tptc_attn_decode_workspace_bytes() bytes
  * (for the current device) and must be zero before its first use; each call leaves it ready
  * for the next (its split counters return to zero, the partial results are overwritten).  Its
  * first int receives a nonzero TPTC_ERR_* code if the kernel found p outside [0, max_seq)

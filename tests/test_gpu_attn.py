@@ -81,7 +81,9 @@ SHAPES = [
     (8, 1, 128, 512, 300),        # MQA, one kv head
     (12, 4, 64, 1000, 777),       # max_seq not a multiple of the tile
     (24, 8, 96, 700, 63),         # hd 96 (Phi-3 shape), a tile boundary
-    (16, 16, 80, 256, 130),       # MHA, hd 80
+    (16, 16, 64, 256, 130),       # MHA, hd 64
+    (64, 8, 128, 4096, 3000),     # 8 query heads per kv head
+    (16, 8, 64, 2048, 1500),      # 2 query heads per kv head
 ]
 
 

@@ -8,13 +8,21 @@
 // h / (n_heads / n_kv) (repeat_kv).
 //
 // Layout: per layer K and V caches are [n_kv][max_seq][hd], fp16 (default) or f32, so the
-// keys of one kv head at consecutive positions are one contiguous run.  Grid = (n_kv,
-// splits); each CTA streams its share of positions in 64-position tiles (two threads per
-// position for the scores, one output dimension per thread for P.V) through a 2-stage
-// shared-memory ring filled by 1-D TMA bulk copies, keeps an online softmax for the group's
-// query heads, and writes (m, l, acc) to scratch.  The last CTA of a kv head (atomic
-// ticket) merges the splits in split order, so the result does not depend on scheduling;
-// the merge stages every split's statistics in shared memory with parallel loads.
+// keys of one kv head at consecutive positions are one contiguous run.
+//
+// Work split: grid = (n_kv, max_splits).  The kernel reads the position, uses
+// S = min(max_splits, ceil(kv_len / 128)) splits of the keys 0..pos (the CTAs of higher
+// splits exit at once) and gives each split a contiguous range.  A CTA of 8 warps streams
+// its range through a ring of 3-6 stages, each one 1-D TMA bulk copy of 64 K rows and one of
+// 64 V rows (32 of each for f32); the last warp to finish a stage refills it, so no warp is
+// set aside for copies.  Warp w owns rows 8w..8w+7 of every stage and keeps its own online
+// softmax for all query heads of the group: a half-warp handles one row, each of its 16
+// lanes a slice of hd/16 elements with the matching q slice in registers; dot products
+// reduce over the 16 lanes with shuffles, and scores and P.V use packed f32x2 FMAs.  At the
+// end the warps' states are merged in shared memory in warp order.  With S = 1 the CTA
+// writes the output; otherwise it writes (m, l, acc) to scratch and the last CTA of the kv
+// head (atomic ticket) merges the splits in split order, so the result does not depend on
+// scheduling.
 #include <algorithm>
 
 #include "kernels.h"
@@ -23,50 +31,158 @@ namespace tptc {
 
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kMaxGroup = 8;  // query heads per kv head
-constexpr int kStages = 2;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxStages = 6;
+constexpr int kRingBudget = 96 * 1024;  // two CTAs per SM
+constexpr int kMinPerSplit = 128;       // positions per split before another split is used
+constexpr int kMaxSplits = 64;
 
 template <typename KV>
 struct KvTraits;
 template <>
 struct KvTraits<__half> {
-    static constexpr int kTile = 64;  // positions per tile (64 KB ring: co-resides with a GEMV CTA)
-    __device__ static float2 pair(const __half* row, int j) {
-        return __half22float2(reinterpret_cast<const __half2*>(row)[j]);
+    static constexpr int kRows = 64;  // rows of K (and of V) per stage
+    // 2 * N2 consecutive elements at p (p aligned to 4 * N2 bytes when N2 is 4, else 4 bytes)
+    template <int N2>
+    __device__ static void load(const __half* p, float2 (&v)[N2]) {
+        if constexpr (N2 == 4) {
+            const uint4 u = *reinterpret_cast<const uint4*>(p);
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = __half22float2(h[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < N2; i++) v[i] = __half22float2(reinterpret_cast<const __half2*>(p)[i]);
+        }
     }
-    __device__ static float at(const __half* p) { return __half2float(*p); }
     __device__ static void store(__half* p, float v) { *p = __float2half_rn(v); }
 };
 template <>
 struct KvTraits<float> {
-    static constexpr int kTile = 64;
-    __device__ static float2 pair(const float* row, int j) { return reinterpret_cast<const float2*>(row)[j]; }
-    __device__ static float at(const float* p) { return *p; }
+    static constexpr int kRows = 32;
+    template <int N2>
+    __device__ static void load(const float* p, float2 (&v)[N2]) {
+        if constexpr (N2 % 2 == 0) {
+#pragma unroll
+            for (int i = 0; i < N2 / 2; i++) {
+                const float4 f = reinterpret_cast<const float4*>(p)[i];
+                v[2 * i] = make_float2(f.x, f.y);
+                v[2 * i + 1] = make_float2(f.z, f.w);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < N2; i++) v[i] = reinterpret_cast<const float2*>(p)[i];
+        }
+    }
     __device__ static void store(float* p, float v) { *p = v; }
 };
 
-template <typename KV>
-__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
+// 2^x (PTX ex2.approx: a few ulp of relative error; 2^-inf = 0).  Scores are kept in the
+// log2 domain (scaled by log2 e), so softmax weights are 2^(s - m).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// One halving step of a reduce-scatter over lane pairs (lane, lane ^ mask): the lane with
+// the mask bit clear keeps v[0, N) and the other v[N, 2N), each adding its partner's copy.
+template <int N, int GM>
+__device__ __forceinline__ void rs_halve(float (&v)[GM], int mask, bool upper) {
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+        const float send = upper ? v[j] : v[N + j];
+        const float keep = upper ? v[N + j] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+    }
+}
+
+// Sums v[g] (g < GM) over the 16 lanes of a half-warp and returns, in every lane, the sum of
+// head g = l16 / (16 / GM); the 16 / GM lanes of a head hold bit-identical sums.  Costs
+// GM - 1 + 4 - log2(GM) shuffles instead of 4 * GM.
+template <int GM>
+__device__ __forceinline__ float reduce_scatter16(float (&v)[GM], int l16) {
+    if constexpr (GM == 8) {
+        rs_halve<4>(v, 8, l16 & 8);
+        rs_halve<2>(v, 4, l16 & 4);
+        rs_halve<1>(v, 2, l16 & 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    } else if constexpr (GM == 4) {
+        rs_halve<2>(v, 8, l16 & 8);
+        rs_halve<1>(v, 4, l16 & 4);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    } else if constexpr (GM == 2) {
+        rs_halve<1>(v, 8, l16 & 8);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 4);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 8);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 4);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    }
+    return v[0];
+}
+
+// Record of one (split or warp, head) state: m, l, two pad floats, acc[hd] -- hd + 4 floats,
+// a multiple of 16 bytes, so a run of split records is one bulk copy.
+__host__ __device__ constexpr int attn_rec(int hd) { return hd + 4; }
+// Shared memory of the merges (inside the ring): the warp states [kWarps][G][rec]; for the
+// split merge, staging for split records, then weights [G][kMaxSplits] and sums of l [G].
+__host__ __device__ constexpr int attn_weight_bytes(int G) { return (G * kMaxSplits + G) * 4; }
+__host__ __device__ constexpr int attn_merge_bytes(int G, int hd) {
+    return kWarps * G * attn_rec(hd) * 4 > G * attn_rec(hd) * 4 + attn_weight_bytes(G)
+               ? kWarps * G * attn_rec(hd) * 4
+               : G * attn_rec(hd) * 4 + attn_weight_bytes(G);
+}
+
+// Effective split count and this split's key range for kv_len keys.
+struct SplitRange {
+    int S, t_begin, t_end;
+};
+__device__ __forceinline__ SplitRange split_range(int kv_len, int max_splits, int split) {
+    SplitRange r;
+    r.S = min(max_splits, max(1, (kv_len + kMinPerSplit - 1) / kMinPerSplit));
+    int per = (kv_len + r.S - 1) / r.S;
+    per = (per + 15) / 16 * 16;
+    r.t_begin = min(kv_len, split * per);
+    r.t_end = min(kv_len, r.t_begin + per);
+    return r;
+}
+
+// N2: float2 pairs of the head dimension per lane (hd = 32 * N2); GM: most query heads per
+// kv head.
+template <typename KV, int N2, int GM>
+__global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(const __grid_constant__ AttnDecodeParams p) {
     using Tr = KvTraits<KV>;
-    constexpr int kT = Tr::kTile;
+    constexpr int kR = Tr::kRows;
+    constexpr int kRW = kR / kWarps;  // rows per warp per stage
+    constexpr int kIt = kRW / 2;      // two rows (half-warps) per iteration
+    constexpr int DPL = 2 * N2;       // head-dimension elements per lane
+    constexpr int HD = 16 * DPL;
+    constexpr int kStageElems = kR * HD;  // K (or V) elements per stage
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full[kStages];
-    __shared__ float red[kMaxGroup][kThreads / 32];
-    __shared__ float mnew_s[kMaxGroup], alpha_s[kMaxGroup];
-    __shared__ int is_last;
+    __shared__ uint64_t full[kMaxStages], mfull;
+    __shared__ int done_warps[kMaxStages];
+    __shared__ int is_last, abort_s;
 
     const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = p.n_heads / p.n_kv, hd = p.hd;
-    const int tile_elems = kT * hd;
-    KV* kbuf = reinterpret_cast<KV*>(smem);                             // [kStages][kT][hd]
-    KV* vbuf = kbuf + kStages * tile_elems;                             // [kStages][kT][hd]
-    float* qs = reinterpret_cast<float*>(vbuf + kStages * tile_elems);  // [G][hd]
-    float* ps = qs + G * hd;                                            // [G][kT]
+    const int G = p.n_heads / p.n_kv, S_ring = p.stages;
+    KV* ring = reinterpret_cast<KV*>(smem);  // [S_ring][K|V][kR][HD]
+    const int ring_bytes = max(S_ring * 2 * kStageElems * (int)sizeof(KV), attn_merge_bytes(G, HD));
+    float* qs = reinterpret_cast<float*>(smem + ring_bytes);  // [G][HD]
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
+        for (int s = 0; s < S_ring; s++) {
+            mbar_init(&full[s], 1);
+            done_warps[s] = 0;
+        }
+        mbar_init(&mfull, 1);
         fence_mbar_init();
+        abort_s = 0;
     }
     pdl_wait();
     pdl_launch_dependents();
@@ -76,236 +192,358 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const __grid_cons
         if (tid == 0 && kvh == 0 && split == 0 && p.err) atomicExch(p.err, TPTC_ERR_ARG);
         return;
     }
-    int per = (kv_len + p.splits - 1) / p.splits;
-    per = (per + kT - 1) / kT * kT;
-    const int t_begin = split * per, t_end = min(kv_len, t_begin + per);
-    const int ntiles = t_end > t_begin ? (t_end - t_begin + kT - 1) / kT : 0;
+    const SplitRange sr = split_range(kv_len, p.splits, split);
+    if (split >= sr.S) return;
+    const int t_begin = sr.t_begin, t_end = sr.t_end;
+    const int ntiles = (t_end - t_begin + kR - 1) / kR;
+    const int pos = kv_len - 1, half = HD / 2;
+    const bool owner = pos >= t_begin && pos < t_end;  // this CTA writes the new key
+    const int tile_pos = owner ? (pos - t_begin) / kR : -1;
+
+    // Stage s of tile t holds 1-D bulk copies of kR K rows and kR V rows.  Tid 0 fills the
+    // first stages at once -- except the tile holding `pos`, whose key this CTA writes first;
+    // afterwards the last warp to finish a stage refills it (done_warps).
+    const KV* kh = static_cast<const KV*>(p.kcache) + (int64_t)kvh * p.max_seq * HD;
+    const KV* vh = static_cast<const KV*>(p.vcache) + (int64_t)kvh * p.max_seq * HD;
+    auto issue = [&](int t) {
+        const int s = t % S_ring, t0 = t_begin + t * kR, n = min(kR, t_end - t0);
+        const uint32_t bytes = (uint32_t)n * HD * sizeof(KV);
+        KV* kb = ring + (int64_t)s * 2 * kStageElems;
+        const uint64_t policy = l2_evict_first_policy();
+        mbar_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(kb, kh + (int64_t)t0 * HD, bytes, &full[s], policy);
+        bulk_g2s(kb + kStageElems, vh + (int64_t)t0 * HD, bytes, &full[s], policy);
+    };
+    if (tid == 0)
+        for (int t = 0; t < S_ring && t < ntiles; t++)
+            if (t != tile_pos) issue(t);
 
     // RoPE (candle rope_i: interleaved pairs, x0*c - x1*s, x0*s + x1*c) on the group's
-    // queries while they are staged in shared memory
-    const int pos = kv_len - 1, half = hd / 2;
+    // queries, staged in shared memory
     const float* cs = p.rope_cos + (int64_t)pos * half;
     const float* sn = p.rope_sin + (int64_t)pos * half;
     for (int i = tid; i < G * half; i += kThreads) {
         const int g = i / half, j = i % half;
-        const float* qg = p.q + (int64_t)(kvh * G + g) * hd;
+        const float* qg = p.q + (int64_t)(kvh * G + g) * HD;
         const float q0 = qg[2 * j], q1 = qg[2 * j + 1], c = cs[j], s = sn[j];
         const float r0 = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
         const float r1 = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
-        qs[g * hd + 2 * j] = r0;
-        qs[g * hd + 2 * j + 1] = r1;
+        qs[g * HD + 2 * j] = r0;
+        qs[g * HD + 2 * j + 1] = r1;
         if (p.q_out && split == 0) {
-            p.q_out[(int64_t)(kvh * G + g) * hd + 2 * j] = r0;
-            p.q_out[(int64_t)(kvh * G + g) * hd + 2 * j + 1] = r1;
+            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j] = r0;
+            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j + 1] = r1;
         }
     }
-    // The CTA whose positions include `pos` rotates this step's key and stores it in the cache;
-    // the proxy fence orders those generic stores before its own bulk-copy reads of them.
-    if (pos >= t_begin && pos < t_end) {
-        KV* krow = static_cast<KV*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * hd;
+    // The owner rotates this step's key and stores it in the cache; the proxy fence orders
+    // those generic stores before the bulk-copy read of the same row.
+    if (owner) {
+        KV* krow = static_cast<KV*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * HD;
         for (int j = tid; j < half; j += kThreads) {
-            const float k0 = p.kraw[kvh * hd + 2 * j], k1 = p.kraw[kvh * hd + 2 * j + 1], c = cs[j], s = sn[j];
+            const float k0 = p.kraw[kvh * HD + 2 * j], k1 = p.kraw[kvh * HD + 2 * j + 1], c = cs[j], s = sn[j];
             Tr::store(krow + 2 * j, __fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
             Tr::store(krow + 2 * j + 1, __fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
+    if (tid == 0 && tile_pos >= 0 && tile_pos < S_ring) issue(tile_pos);
 
-    const KV* kh = static_cast<const KV*>(p.kcache) + (int64_t)kvh * p.max_seq * hd;
-    const KV* vh = static_cast<const KV*>(p.vcache) + (int64_t)kvh * p.max_seq * hd;
-    uint64_t policy = 0;
-    auto issue = [&](int tile) {
-        const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
-        const uint32_t bytes = (uint32_t)n * hd * sizeof(KV);
-        mbar_expect_tx(&full[s], 2 * bytes);
-        bulk_g2s(kbuf + s * tile_elems, kh + (int64_t)t0 * hd, bytes, &full[s], policy);
-        bulk_g2s(vbuf + s * tile_elems, vh + (int64_t)t0 * hd, bytes, &full[s], policy);
-    };
-    if (tid == 0) {
-        policy = l2_evict_first_policy();
-        for (int t = 0; t < kStages && t < ntiles; t++) issue(t);
-    }
+    const int hw = lane >> 4, l16 = lane & 15;
+    constexpr int LPG = 16 / GM;          // lanes per head after the reduce-scatter
+    const float sl2 = p.scale * 1.4426950408889634f;  // scores in log2 units
+    float2 qv[GM][N2];
+#pragma unroll
+    for (int g = 0; g < GM; g++)
+#pragma unroll
+        for (int j = 0; j < N2; j++)
+            qv[g][j] = g < G ? reinterpret_cast<const float2*>(qs + g * HD + l16 * DPL)[j] : make_float2(0.f, 0.f);
+    // running max and sum of head l16 / LPG (identical in both half-warps), accumulators of
+    // every head over this lane's slice of the head dimension
+    float m_h = -INFINITY, l_h = 0.f;
+    float2 acc[GM][N2];
+#pragma unroll
+    for (int g = 0; g < GM; g++)
+#pragma unroll
+        for (int j = 0; j < N2; j++) acc[g][j] = make_float2(0.f, 0.f);
 
-    float m_run[kMaxGroup], l_run[kMaxGroup], acc[kMaxGroup];
+    bool ok = true;
+    for (int t = 0; t < ntiles; t++) {
+        const int s = t % S_ring, t0 = t_begin + t * kR, n = min(kR, t_end - t0);
+        ok = mbar_wait_bounded(&full[s], (t / S_ring) & 1, p.err);
+        if (!ok) break;
+        const KV* kt = ring + (int64_t)s * 2 * kStageElems;
+        const KV* vt = kt + kStageElems;
+        float sc[kIt];  // score of (row 2i + hw, head l16 / LPG)
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; g++) {
-        m_run[g] = -INFINITY;
-        l_run[g] = 0.f;
-        acc[g] = 0.f;
-    }
-    // scores: two threads per position (kThreads = 2 * kT), each half of the head dimension
-    const int my_pos = tid >> 1, my_half = tid & 1;
-    const int hp = hd / 2, hq = hp / 2;  // half2 pairs per row, per half-row
-    bool timed_out = false;
-    for (int tile = 0; tile < ntiles; tile++) {
-        const int s = tile % kStages, t0 = t_begin + tile * kT, n = min(kT, t_end - t0);
-        if (!mbar_wait_bounded(&full[s], (tile / kStages) & 1, p.err)) timed_out = true;
-        if (__syncthreads_or(timed_out)) return;
-        float sc[kMaxGroup];
+        for (int i = 0; i < kIt; i++) {
+            const int r = warp * kRW + 2 * i + hw;
+            float2 kv[N2];
+            Tr::template load<N2>(kt + r * HD + l16 * DPL, kv);
+            float d[GM];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) sc[g] = 0.f;
-        if (my_pos < n) {
-            const KV* krow = kbuf + s * tile_elems + my_pos * hd;
-            // start column rotated by position so neighbouring threads hit different banks
-            int jj = my_half * hq + (my_pos % hq);
-            const int lo = my_half * hq, hi = lo + hq;
-            for (int j = 0; j < hq; j++) {
-                const float2 kv = Tr::pair(krow, jj);
+            for (int g = 0; g < GM; g++) {
+                float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int g = 0; g < kMaxGroup; g++) {
-                    if (g < G) {
-                        const float2 qv = reinterpret_cast<const float2*>(qs + g * hd)[jj];
-                        sc[g] = fmaf(qv.x, kv.x, sc[g]);
-                        sc[g] = fmaf(qv.y, kv.y, sc[g]);
-                    }
+                for (int j = 0; j < N2; j++) d2 = __ffma2_rn(qv[g][j], kv[j], d2);
+                d[g] = d2.x + d2.y;
+            }
+            const float dot = reduce_scatter16<GM>(d, l16);
+            sc[i] = r < n ? dot * sl2 : -INFINITY;
+        }
+        // online softmax of this warp's rows of the stage
+        float mt = sc[0];
+#pragma unroll
+        for (int i = 1; i < kIt; i++) mt = fmaxf(mt, sc[i]);
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+        const float mn = fmaxf(m_h, mt);
+        const float mu = mn == -INFINITY ? 0.f : mn;
+        const float alpha = ex2(m_h - mu);
+        float ls = 0.f;
+#pragma unroll
+        for (int i = 0; i < kIt; i++) {
+            sc[i] = ex2(sc[i] - mu);
+            ls += sc[i];
+        }
+        ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+        l_h = l_h * alpha + ls;
+        m_h = mn;
+#pragma unroll
+        for (int g = 0; g < GM; g++) {
+            const float a = __shfl_sync(0xffffffffu, alpha, g * LPG);
+            const float2 a2 = make_float2(a, a);
+#pragma unroll
+            for (int j = 0; j < N2; j++) acc[g][j] = __fmul2_rn(acc[g][j], a2);
+        }
+        // P.V
+#pragma unroll
+        for (int i = 0; i < kIt; i++) {
+            const int r = warp * kRW + 2 * i + hw;
+            float pg[GM];
+#pragma unroll
+            for (int g = 0; g < GM; g++) pg[g] = __shfl_sync(0xffffffffu, sc[i], (lane & 16) + g * LPG);
+            float2 vv[N2];
+            if (r < n) {
+                Tr::template load<N2>(vt + r * HD + l16 * DPL, vv);
+            } else {
+#pragma unroll
+                for (int j = 0; j < N2; j++) vv[j] = make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int g = 0; g < GM; g++) {
+                const float2 p2 = make_float2(pg[g], pg[g]);
+#pragma unroll
+                for (int j = 0; j < N2; j++) acc[g][j] = __ffma2_rn(p2, vv[j], acc[g][j]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {  // the last warp done with stage s refills it
+            __threadfence_block();
+            if (atomicAdd(&done_warps[s], 1) == kWarps - 1) {
+                done_warps[s] = 0;
+                __threadfence_block();
+                if (t + S_ring < ntiles) {
+                    fence_proxy_async_smem();
+                    issue(t + S_ring);
                 }
-                jj = (jj + 1 == hi) ? lo : jj + 1;
             }
-        }
-#pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) {
-            sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 1);
-            sc[g] = my_pos < n ? sc[g] * p.scale : -INFINITY;
-        }
-        // tile max per head
-#pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) {
-            if (g < G) {
-                const float mx = warp_max(sc[g]);
-                if (lane == 0) red[g][warp] = mx;
-            }
-        }
-        __syncthreads();
-        if (tid < G) {
-            float mx = red[tid][0];
-            for (int w = 1; w < kThreads / 32; w++) mx = fmaxf(mx, red[tid][w]);
-            const float mn = fmaxf(m_run[tid], mx);
-            mnew_s[tid] = mn;
-            alpha_s[tid] = m_run[tid] == -INFINITY ? 0.f : expf(m_run[tid] - mn);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) {
-            if (g < G) {
-                const float pv = my_pos < n ? expf(sc[g] - mnew_s[g]) : 0.f;
-                if (my_half == 0) ps[g * kT + my_pos] = pv;
-                const float ls = warp_sum(my_half == 0 ? pv : 0.f);
-                if (lane == 0) red[g][warp] = ls;
-            }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) {
-            if (g < G) {
-                float ls = 0.f;
-                for (int w = 0; w < kThreads / 32; w++) ls += red[g][w];
-                l_run[g] = l_run[g] * alpha_s[g] + ls;
-                m_run[g] = mnew_s[g];
-                acc[g] *= alpha_s[g];
-            }
-        }
-        // P.V: thread = output dimension
-        if (tid < hd) {
-            const KV* vcol = vbuf + s * tile_elems + tid;
-            for (int t = 0; t < n; t++) {
-                const float v = Tr::at(vcol + t * hd);
-#pragma unroll
-                for (int g = 0; g < kMaxGroup; g++)
-                    if (g < G) acc[g] = fmaf(ps[g * kT + t], v, acc[g]);
-            }
-        }
-        __syncthreads();  // stage s fully consumed
-        if (tid == 0 && tile + kStages < ntiles) {
-            fence_proxy_async_smem();
-            issue(tile + kStages);
         }
     }
+    if (!ok) abort_s = 1;
 
-    // partial results: [kvh][split][g][2 + hd] = (m, l, acc[hd])
-    const int rec = 2 + hd;
-    float* part = p.partial + ((int64_t)kvh * p.splits + split) * G * rec;
-    if (tid < hd) {
-        for (int g = 0; g < G; g++) part[g * rec + 2 + tid] = acc[g];
-    }
-    if (tid == 0) {
-        for (int g = 0; g < G; g++) {
-            part[g * rec] = m_run[g];
-            part[g * rec + 1] = l_run[g];
+    // the two half-warps saw different rows under the same running max
+#pragma unroll
+    for (int g = 0; g < GM; g++)
+#pragma unroll
+        for (int j = 0; j < N2; j++) {
+            acc[g][j].x += __shfl_xor_sync(0xffffffffu, acc[g][j].x, 16);
+            acc[g][j].y += __shfl_xor_sync(0xffffffffu, acc[g][j].y, 16);
+        }
+
+    __syncthreads();  // every warp is done with the ring: reuse it for the warp states
+    if (abort_s) return;
+    const int rec = attn_rec(HD);
+    float* wst = reinterpret_cast<float*>(smem);  // [warp][G][rec] = (m, l, -, -, acc[HD])
+    if (hw == 0) {
+        const int gh = l16 / LPG;
+        if (l16 % LPG == 0 && gh < G) {
+            wst[(warp * G + gh) * rec] = m_h;
+            wst[(warp * G + gh) * rec + 1] = l_h;
+        }
+#pragma unroll
+        for (int g = 0; g < GM; g++) {
+            if (g >= G) continue;
+            float* w = wst + (warp * G + g) * rec + 4 + l16 * DPL;
+#pragma unroll
+            for (int j = 0; j < N2; j++) {
+                w[2 * j] = acc[g][j].x;
+                w[2 * j + 1] = acc[g][j].y;
+            }
         }
     }
-    __threadfence();
     __syncthreads();
-    if (tid == 0) is_last = atomicAdd(&p.counters[kvh], 1) == p.splits - 1;
+
+    // merge the warps in warp order: the CTA's (M, L, A)
+    const int S = sr.S;
+    float* part = p.partial + ((int64_t)kvh * p.splits + split) * G * rec;
+    for (int idx = tid; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < kWarps; w++) M = fmaxf(M, wst[(w * G + g) * rec]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f, A = 0.f;
+        for (int w = 0; w < kWarps; w++) {
+            const float* ws = wst + (w * G + g) * rec;
+            const float e = ex2(ws[0] - Mu);
+            L = fmaf(ws[1], e, L);
+            A = fmaf(ws[4 + d], e, A);
+        }
+        if (S == 1) {
+            p.out[(kvh * G + g) * HD + d] = A / L;
+        } else {
+            part[g * rec + 4 + d] = A;
+            if (d == 0) {
+                part[g * rec] = M;
+                part[g * rec + 1] = L;
+            }
+        }
+    }
+    if (S == 1) return;
+    __threadfence();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(&p.counters[kvh], 1) == S - 1;
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // merge: stage every split's (m, l) in shared memory with parallel loads, then each
-    // thread reduces one output dimension in split order (deterministic)
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    // merge the splits in split order.  The (m, l) of every (split, head) come in with plain
+    // loads; warp g turns them into weights 2^(m_s - M) and the sum of l; the accumulators
+    // come into shared memory by 1-D bulk copies of as many whole split records as fit.
     const float* base = p.partial + (int64_t)kvh * p.splits * G * rec;
-    float* wgt = ps;             // reuse: [G][splits] m_s, then weights exp(m_s - M); splits <= kT
-    float* lsp = qs;             // reuse: [G][splits] l_s (splits <= 64 <= hd)
-    float* lsum = mnew_s;        // [G] totals
-    for (int i = tid; i < G * p.splits; i += kThreads) {
-        const int g = i / p.splits, s = i % p.splits;
-        wgt[g * kT + s] = base[(s * G + g) * rec];
-        lsp[g * p.splits + s] = base[(s * G + g) * rec + 1];
+    const int stage_bytes = ring_bytes - attn_weight_bytes(G);
+    float* stage = reinterpret_cast<float*>(smem);
+    float* wgt = reinterpret_cast<float*>(smem + stage_bytes);  // [G][kMaxSplits]
+    float* lsum = wgt + G * kMaxSplits;                         // [G]
+    const int Sc = max(1, stage_bytes / (G * rec * 4));          // splits per copy
+    if (tid == 0) {
+        const int n0 = min(Sc, S);
+        fence_proxy_async_smem();  // the warp states were read there
+        mbar_expect_tx(&mfull, (uint32_t)(n0 * G * rec * 4));
+        bulk_g2s(stage, base, (uint32_t)(n0 * G * rec * 4), &mfull, 0);
     }
-    __syncthreads();
-    if (tid < G) {
-        float M = -INFINITY;
-        for (int s = 0; s < p.splits; s++) M = fmaxf(M, wgt[tid * kT + s]);
+    if (warp < G) {
+        const int g = warp;
+        float ms[2], ls2[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int sp = lane + 32 * k;
+            ms[k] = sp < S ? __ldcg(base + (sp * G + g) * rec) : -INFINITY;
+            ls2[k] = sp < S ? __ldcg(base + (sp * G + g) * rec + 1) : 0.f;
+        }
+        const float M = warp_max(fmaxf(ms[0], ms[1]));
+        const float Mu = M == -INFINITY ? 0.f : M;
         float L = 0.f;
-        for (int s = 0; s < p.splits; s++) {
-            const float w = wgt[tid * kT + s] == -INFINITY ? 0.f : expf(wgt[tid * kT + s] - M);
-            wgt[tid * kT + s] = w;
-            L = fmaf(lsp[tid * p.splits + s], w, L);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int sp = lane + 32 * k;
+            const float w = ex2(ms[k] - Mu);
+            if (sp < S) wgt[g * kMaxSplits + sp] = w;
+            L = fmaf(ls2[k], w, L);
         }
-        lsum[tid] = L;
+        L = warp_sum(L);
+        if (lane == 0) lsum[g] = L;
     }
     __syncthreads();
-    if (tid < hd) {
-        for (int g = 0; g < G; g++) {
-            float o = 0.f;
-            for (int s0 = 0; s0 < p.splits; s0 += 16) {  // 16 independent loads in flight
-                float v[16];
+    constexpr int kOut = (GM * HD + kThreads - 1) / kThreads;  // outputs idx = tid + k * kThreads
+    float O[kOut];
 #pragma unroll
-                for (int k = 0; k < 16; k++)
-                    v[k] = s0 + k < p.splits ? base[((s0 + k) * G + g) * rec + 2 + tid] : 0.f;
+    for (int k = 0; k < kOut; k++) O[k] = 0.f;
+    bool mok = true;
+    for (int c0 = 0, ci = 0; c0 < S; c0 += Sc, ci++) {
+        const int n0 = min(Sc, S - c0);
+        if (!mbar_wait_bounded(&mfull, ci & 1, p.err)) mok = false;
+        if (__syncthreads_or(!mok)) return;
 #pragma unroll
-                for (int k = 0; k < 16; k++)
-                    if (s0 + k < p.splits) o = fmaf(v[k], wgt[g * kT + s0 + k], o);
+        for (int k = 0; k < kOut; k++) {
+            const int idx = tid + k * kThreads;
+            if (idx < G * HD) {
+                const int g = idx / HD, d = idx % HD;
+                for (int sp = 0; sp < n0; sp++)
+                    O[k] = fmaf(stage[(sp * G + g) * rec + 4 + d], wgt[g * kMaxSplits + c0 + sp], O[k]);
             }
-            p.out[(kvh * G + g) * hd + tid] = o / lsum[g];
         }
+        __syncthreads();  // staging consumed
+        if (tid == 0 && c0 + Sc < S) {
+            const int n1 = min(Sc, S - c0 - Sc);
+            fence_proxy_async_smem();
+            mbar_expect_tx(&mfull, (uint32_t)(n1 * G * rec * 4));
+            bulk_g2s(stage, base + (int64_t)(c0 + Sc) * G * rec, (uint32_t)(n1 * G * rec * 4), &mfull, 0);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kOut; k++) {
+        const int idx = tid + k * kThreads;
+        if (idx < G * HD) p.out[(kvh * G + idx / HD) * HD + idx % HD] = O[k] / lsum[idx / HD];
     }
     if (tid == 0) p.counters[kvh] = 0;
 }
 
 template <typename KV>
+int attn_stages(int hd) {
+    const int stage = 2 * KvTraits<KV>::kRows * hd * (int)sizeof(KV);
+    return std::max(2, std::min(kMaxStages, kRingBudget / stage));
+}
+
+template <typename KV>
 size_t attn_smem(int n_heads, int n_kv, int hd) {
-    const int G = n_heads / n_kv, kT = KvTraits<KV>::kTile;
-    return (size_t)2 * kStages * kT * hd * sizeof(KV) + (size_t)G * hd * 4 + (size_t)G * kT * 4;
+    const int G = n_heads / n_kv;
+    const size_t ring = (size_t)attn_stages<KV>(hd) * 2 * KvTraits<KV>::kRows * hd * sizeof(KV);
+    const size_t wst = (size_t)attn_merge_bytes(G, hd);
+    return std::max(ring, wst) + (size_t)G * hd * 4;
+}
+
+using KernelFn = void (*)(AttnDecodeParams);
+
+template <typename KV, int GM>
+KernelFn pick_dpl(int hd) {
+    switch (hd) {
+        case 64: return attn_decode_kernel<KV, 2, GM>;
+        case 96: return attn_decode_kernel<KV, 3, GM>;
+        case 128: return attn_decode_kernel<KV, 4, GM>;
+    }
+    return nullptr;
+}
+
+KernelFn pick_kernel(int kv_f32, int hd, int G) {
+    if (kv_f32) {
+        if (G == 1) return pick_dpl<float, 1>(hd);
+        if (G == 2) return pick_dpl<float, 2>(hd);
+        return G <= 4 ? pick_dpl<float, 4>(hd) : pick_dpl<float, 8>(hd);
+    }
+    if (G == 1) return pick_dpl<__half, 1>(hd);
+    if (G == 2) return pick_dpl<__half, 2>(hd);
+    return G <= 4 ? pick_dpl<__half, 4>(hd) : pick_dpl<__half, 8>(hd);
 }
 
 }  // namespace
 
 int attn_decode_splits(int n_kv, int max_seq, int sm_count) {
-    int s = std::max(1, sm_count / n_kv);
-    const int max_useful = (max_seq + 63) / 64;
-    // the merge stages one weight per split in a 64-entry shared array
-    return std::min(64, std::min(s, std::max(1, max_useful)));
+    // two CTAs per SM over all kv heads at long context
+    const int s = std::max(1, (2 * sm_count + n_kv - 1) / n_kv);
+    const int max_useful = std::max(1, (max_seq + kMinPerSplit - 1) / kMinPerSplit);
+    return std::min(kMaxSplits, std::min(s, max_useful));
 }
 
 size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits) {
-    return (size_t)n_kv * splits * (n_heads / n_kv) * (2 + hd);
+    return (size_t)n_kv * splits * (n_heads / n_kv) * attn_rec(hd);
 }
 
 const char* attn_decode_shape_error(int n_heads, int n_kv, int hd, int max_seq) {
     if (n_heads <= 0 || n_kv <= 0 || hd <= 0 || max_seq <= 0) return "attention: sizes must be positive";
     if (n_heads % n_kv != 0) return "attention: n_heads must be a multiple of n_kv";
-    if (n_heads / n_kv > kMaxGroup) return "attention: at most 8 query heads per kv head";
-    if (hd > kThreads || hd % 16 != 0) return "attention: head_dim must be a multiple of 16, at most 128";
+    if (n_heads / n_kv > 8) return "attention: at most 8 query heads per kv head";
+    if (hd != 64 && hd != 96 && hd != 128) return "attention: head_dim must be 64, 96 or 128";
     return nullptr;
 }
 
@@ -319,8 +557,12 @@ AttnScratch attn_scratch_layout(int n_heads, int n_kv, int hd, int max_seq, int 
     return s;
 }
 
-cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool pdl) {
-    if (attn_decode_shape_error(p.n_heads, p.n_kv, p.hd, p.max_seq)) return cudaErrorInvalidValue;
+cudaError_t launch_attn_decode(const AttnDecodeParams& p_in, cudaStream_t st, bool pdl) {
+    if (attn_decode_shape_error(p_in.n_heads, p_in.n_kv, p_in.hd, p_in.max_seq) || p_in.splits < 1 ||
+        p_in.splits > kMaxSplits)
+        return cudaErrorInvalidValue;
+    AttnDecodeParams p = p_in;
+    p.stages = p.kv_f32 ? attn_stages<float>(p.hd) : attn_stages<__half>(p.hd);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.n_kv, p.splits);
     cfg.blockDim = dim3(kThreads);
@@ -331,14 +573,18 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, cudaStream_t st, bool 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (p.kv_f32) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<float>, p);
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<__half>, p);
+    return cudaLaunchKernelEx(&cfg, pick_kernel(p.kv_f32, p.hd, p.n_heads / p.n_kv), p);
 }
 
 cudaError_t attn_init_device() {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    for (int f32 = 0; f32 < 2; f32++)
+        for (int hd : {64, 96, 128})
+            for (int G : {1, 2, 4, 8}) {
+                cudaError_t e = cudaFuncSetAttribute(pick_kernel(f32, hd, G), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     200 * 1024);
+                if (e != cudaSuccess) return e;
+            }
+    return cudaSuccess;
 }
 
 }  // namespace tptc

@@ -232,7 +232,8 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         m.ffn = getu("feed_forward_length", est);
     }
     if (m.n_kv_heads <= 0 || m.n_heads % m.n_kv_heads) return err(TPTC_ERR_UNSUPPORTED, "head_count not a multiple of head_count_kv");
-    if (m.head_dim % 16 || m.head_dim > 128) return err(TPTC_ERR_UNSUPPORTED, "head_dim must be a multiple of 16 and <= 128");
+    if (m.head_dim != 64 && m.head_dim != 96 && m.head_dim != 128)
+        return err(TPTC_ERR_UNSUPPORTED, "head_dim must be 64, 96 or 128");
     if (m.dim % QK_K || m.ffn % QK_K) return err(TPTC_ERR_UNSUPPORTED, "embedding/ffn sizes must be multiples of 256");
     if (m.n_kv_heads % tp_size_ || m.ffn % (QK_K * tp_size_))
         return err(TPTC_ERR_UNSUPPORTED, "model does not shard evenly over tp_size=" + std::to_string(tp_size_));

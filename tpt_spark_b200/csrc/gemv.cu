@@ -40,10 +40,6 @@ __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;"
 // Named barrier 2 + i joins consumer warps i and i + 4 only.
 __device__ __forceinline__ void pair_sync(int i) { asm volatile("bar.sync %0, 64;" ::"r"(2 + i) : "memory"); }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Logical row held in tile row r (0..7) of work unit u, and the segment it belongs to.
 struct UnitRow {
     int seg;   // -1: padding row (N not a multiple of 8)

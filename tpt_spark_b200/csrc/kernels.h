@@ -33,9 +33,12 @@ struct AttnDecodeParams {
     const int* pos;        // device scalar: the query position (keys 0..pos)
     float* out;            // [n_heads * hd]
     float* q_out;          // optional [n_heads * hd]: rotated q (test trace)
-    float* partial;        // scratch [n_kv][splits][group][2 + hd]
+    float* partial;        // scratch [n_kv][splits][group][hd + 4]: m, l, 2 pad, acc
     int* counters;         // scratch [n_kv], zero between launches
-    int n_heads, n_kv, hd, max_seq, splits;
+    int n_heads, n_kv, hd, max_seq;
+    int splits;            // grid splits per kv head (attn_decode_splits); the kernel uses
+                           // min(splits, ceil(kv_len / 128)) of them
+    int stages;            // filled by launch_attn_decode
     float scale;           // 1/sqrt(hd)
     int* err;
 };
