@@ -243,15 +243,13 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
     const int64_t raw_row = ggml_type == TPTC_TYPE_Q6_K ? (int64_t)K / 256 * 210
                             : ggml_type == TPTC_TYPE_Q8_0 ? (int64_t)K / 32 * 34 : d.main_row_bytes;
     const size_t main_al = ((size_t)d.main_bytes() + 255) / 256 * 256;
-    const size_t d_bytes = (size_t)d.d_per_row * 2 * d.Npad;
-    cudaError_t e = cudaMalloc(&m->mem, main_al + d_bytes + 256);
+    cudaError_t e = cudaMalloc(&m->mem, main_al + 256);
     if (e != cudaSuccess) {
         delete m;
         return cuda_fail(e, "cudaMalloc(matrix)");
     }
     d.main = m->mem;
-    d.dplane = d.d_per_row ? reinterpret_cast<uint16_t*>(m->mem + main_al) : nullptr;
-    m->err = reinterpret_cast<int*>(m->mem + main_al + d_bytes);
+    m->err = reinterpret_cast<int*>(m->mem + main_al);
     const size_t raw_bytes = (size_t)raw_row * N;
     const uint8_t* src = static_cast<const uint8_t*>(raw);
     uint8_t* tmp = nullptr;
@@ -260,7 +258,7 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
         if (e == cudaSuccess) e = cudaMemcpy(tmp, raw, raw_bytes, cudaMemcpyHostToDevice);
         src = tmp;
     }
-    if (e == cudaSuccess) e = cudaMemset(m->mem, 0, main_al + d_bytes + 256);
+    if (e == cudaSuccess) e = cudaMemset(m->mem, 0, main_al + 256);
     if (e == cudaSuccess) e = tptc::launch_repack(src, raw_row, N, 0, d, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (tmp) cudaFree(tmp);

@@ -281,7 +281,7 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
 
     // ---- validate and lay out the arena
     size_t off = 0;
-    std::vector<size_t> offs(plans.size(), 0), doffs(plans.size(), 0);
+    std::vector<size_t> offs(plans.size(), 0);
     std::vector<const GgufTensor*> tens(plans.size());
     for (size_t i = 0; i < plans.size(); i++) {
         Plan& p = plans[i];
@@ -310,8 +310,6 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         d = dm_geometry((int)t->type, p.glu_rows ? p.glu_rows : p.r1 - p.r0, p.k1 - p.k0, p.glu_rows ? 1 : 0);
         offs[i] = off;
         off = align_up(off + (size_t)d.main_bytes(), 256);
-        doffs[i] = off;
-        off = align_up(off + (size_t)d.d_per_row * 2 * d.Npad, 256);
     }
     arena_size_ = off;
     cudaError_t ce = cudaMalloc(&arena_, arena_size_);
@@ -341,12 +339,11 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
             DevMatrix& d = *p.mat;
             if (!(p.glu_rows && p.first_row > 0)) {
                 d.main = arena_ + offs[i];
-                d.dplane = d.d_per_row ? reinterpret_cast<uint16_t*>(arena_ + doffs[i]) : nullptr;
             }
             const int64_t rrb = raw_row_bytes(d.type, p.K);
             const int64_t c0 = raw_row_bytes(d.type, p.k0), c1 = raw_row_bytes(d.type, p.k1);
             RET_IF(upload_rows(sg, src, rrb, p.r0, p.r1, c0, c1, d, p.first_row));
-            weight_bytes_ += (uint64_t)(p.r1 - p.r0) * (d.main_row_bytes + d.d_per_row * 2);
+            weight_bytes_ += (uint64_t)(p.r1 - p.r0) * d.main_row_bytes;
         }
         if (cb) cb((uint32_t)(i + 1), (uint32_t)plans.size(), user);
     }

@@ -82,142 +82,117 @@ struct Act {
     const float* q80_d;
 };
 
-// Each chunk routine reduces the items [first, first + stride, ...) of one row chunk held in
-// `slot`; `c0` is the chunk's first super-block, `cb` its length in super-blocks.
-//
-// Forward path (DOTS = false): every lane scales its own partial integer sum by the
-// super-block factors, (d_w*d_x)*isum_part - (dmin_w*d_x)*msum_part, so no cross-lane
-// reduction is needed per super-block (the f32 result differs from scaling the full
-// integer sum by float rounding only).  The DOTS test hook reduces the exact per-block
-// integers across the 4 lanes of a super-block.
-
-// All eight 6-bit scales and mins of a Q4_K block from its 12 packed bytes (words s0..s2):
-// bytes of sc_lo/sc_hi are sc[0..3]/sc[4..7], bytes of mn_lo/mn_hi are m[0..3]/m[4..7].
-__device__ __forceinline__ void q4k_unpack_scales(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t& sc_lo,
-                                                  uint32_t& sc_hi, uint32_t& mn_lo, uint32_t& mn_hi) {
-    const uint32_t k6 = 0x3f3f3f3fu, k4 = 0x0f0f0f0fu, k2 = 0x03030303u;
-    sc_lo = s0 & k6;
-    mn_lo = s1 & k6;
-    sc_hi = (s2 & k4) | (((s0 >> 6) & k2) << 4);
-    mn_hi = ((s2 >> 4) & k4) | (((s1 >> 6) & k2) << 4);
+// dp4a of unsigned bytes (a) with signed bytes (b).
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-__device__ __forceinline__ int byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xff; }
+__device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)((w >> (8 * i)) & 0xff); }
+__device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xff); }
 
-// Q4_K, forward path: lane item = (super-block sb, 64-element group g).
-__device__ __forceinline__ float q4k_item(const uint8_t* slot, const Act& a, int c0, int it) {
-    const int sb = it >> 2, g = it & 3;
+// Forward path (EPI != DOTS).  For Q4_K and Q6_K lane l of a row's warp reduces half
+// super-block l of the chunk (super-block l/2, elements 128*(l%2) .. +128): its quants,
+// scales and activations are read once per 128 elements.  The chunk's Q8_K quants are
+// stored lane-transposed in shared memory (xt_offset): 16-byte vector v of half super-block
+// l sits at (v * nh + l) * 16, nh = 2 * cb, so the 32 lanes read 512 contiguous bytes per
+// load.  Each lane scales its own partial integer sums by the super-block factors,
+// (d_w*d_x)*isum_half - (dmin_w*d_x)*msum_half; the f32 result differs from scaling the
+// whole block's integer sum only by float rounding.  The DOTS test hook keeps the exact
+// per-block integers (chunk_q4k / chunk_q6k below, natural activation layout).
+
+// Byte offset of the 8 Q8_K quants of lane `lane` (elements 8*lane .. +7) of super-block b
+// in the transposed activation layout.
+__host__ __device__ __forceinline__ int xt_offset(int b, int lane, int nsb, int cbs) {
+    const int c = b / cbs, j = b - c * cbs, cbc = min(cbs, nsb - c * cbs), nh = 2 * cbc;
+    const int h = lane >> 4, v = (lane & 15) >> 1;
+    return c * cbs * QK_K + (v * nh + 2 * j + h) * 16 + (lane & 1) * 8;
+}
+
+__device__ __forceinline__ float q4k_half(const uint8_t* slot, const Act& a, int c0, int nh, int lane) {
+    const int sb = lane >> 1, h = lane & 1;
     const uint8_t* blk = slot + sb * Q4K_BYTES;
-    const uint4 hd = *reinterpret_cast<const uint4*>(blk);  // d, dmin, 12 scale bytes
-    const uint4 w0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
-    const uint4 w1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
-    const int4* xq = reinterpret_cast<const int4*>(a.q8k + (c0 + sb) * QK_K + 64 * g);
-    const int4 x0 = xq[0], x1 = xq[1], x2 = xq[2], x3 = xq[3];
-    const uint32_t m4 = 0x0f0f0f0fu;
-    int lo0 = __dp4a((int)(w0.x & m4), x0.x, 0);
-    int lo1 = __dp4a((int)(w0.y & m4), x0.y, 0);
-    lo0 = __dp4a((int)(w0.z & m4), x0.z, lo0);
-    lo1 = __dp4a((int)(w0.w & m4), x0.w, lo1);
-    lo0 = __dp4a((int)(w1.x & m4), x1.x, lo0);
-    lo1 = __dp4a((int)(w1.y & m4), x1.y, lo1);
-    lo0 = __dp4a((int)(w1.z & m4), x1.z, lo0);
-    lo1 = __dp4a((int)(w1.w & m4), x1.w, lo1);
-    int hi0 = __dp4a((int)((w0.x >> 4) & m4), x2.x, 0);
-    int hi1 = __dp4a((int)((w0.y >> 4) & m4), x2.y, 0);
-    hi0 = __dp4a((int)((w0.z >> 4) & m4), x2.z, hi0);
-    hi1 = __dp4a((int)((w0.w >> 4) & m4), x2.w, hi1);
-    hi0 = __dp4a((int)((w1.x >> 4) & m4), x3.x, hi0);
-    hi1 = __dp4a((int)((w1.y >> 4) & m4), x3.y, hi1);
-    hi0 = __dp4a((int)((w1.z >> 4) & m4), x3.z, hi0);
-    hi1 = __dp4a((int)((w1.w >> 4) & m4), x3.w, hi1);
-    uint32_t sc_lo, sc_hi, mn_lo, mn_hi;
-    q4k_unpack_scales(hd.y, hd.z, hd.w, sc_lo, sc_hi, mn_lo, mn_hi);
-    const uint32_t scw = g < 2 ? sc_lo : sc_hi, mnw = g < 2 ? mn_lo : mn_hi;
-    const int j = (2 * g) & 3;
-    const int sc0 = byte_of(scw, j), sc1 = byte_of(scw, j + 1);
-    const int m0 = byte_of(mnw, j), m1 = byte_of(mnw, j + 1);
-    // pair sums of the 16-element bsums: P[2g], P[2g+1] (sub-blocks 2g and 2g+1)
-    const uint32_t pp = *reinterpret_cast<const uint32_t*>(a.q8k_ps + (c0 + sb) * 8 + 2 * g);
-    const int p0 = (int)(int16_t)(pp & 0xffff), p1 = (int)(int16_t)(pp >> 16);
-    const int isum = sc0 * (lo0 + lo1) + sc1 * (hi0 + hi1);
-    const int msum = m0 * p0 + m1 * p1;
+    const uint4 hd = *reinterpret_cast<const uint4*>(blk);  // d, dmin | scales[0..3] | [4..7] | [8..11]
+    const uint4* wq = reinterpret_cast<const uint4*>(blk + 16 + 64 * h);
+    const uint4 w0 = wq[0], w1 = wq[1], w2 = wq[2], w3 = wq[3];
+    const int4* xv = reinterpret_cast<const int4*>(a.q8k + c0 * QK_K) + lane;
+    int4 x[8];
+#pragma unroll
+    for (int v = 0; v < 8; v++) x[v] = xv[v * nh];
+    const uint2 pp = *reinterpret_cast<const uint2*>(a.q8k_ps + (c0 + sb) * 8 + 4 * h);
     const float dx = a.q8k_d[c0 + sb];
+    // sub-blocks 4h, 4h+1 are the low / high nibbles of qs[64h .. +32), 4h+2, 4h+3 of
+    // qs[64h+32 .. +32); high nibbles are dotted in place (16x) and shifted back
+    const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
+    int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    // 16 quant bytes W: low nibbles pair with activations XL, high nibbles with XH
+#define Q4_VEC(W, XL, XH, SL, SH)                                      \
+    SL = dp4a_us(W.x & lo, XL.x, SL); SH = dp4a_us(W.x & hi, XH.x, SH);  \
+    SL = dp4a_us(W.y & lo, XL.y, SL); SH = dp4a_us(W.y & hi, XH.y, SH);  \
+    SL = dp4a_us(W.z & lo, XL.z, SL); SH = dp4a_us(W.z & hi, XH.z, SH);  \
+    SL = dp4a_us(W.w & lo, XL.w, SL); SH = dp4a_us(W.w & hi, XH.w, SH);
+    Q4_VEC(w0, x[0], x[2], s0, s1)
+    Q4_VEC(w1, x[1], x[3], s0, s1)
+    Q4_VEC(w2, x[4], x[6], s2, s3)
+    Q4_VEC(w3, x[5], x[7], s2, s3)
+#undef Q4_VEC
+    s1 >>= 4;
+    s3 >>= 4;
+    const uint32_t k6 = 0x3f3f3f3fu, k4 = 0x0f0f0f0fu, k2 = 0x03030303u;
+    const uint32_t sc = h == 0 ? hd.y & k6 : (hd.w & k4) | (((hd.y >> 6) & k2) << 4);
+    const uint32_t mn = h == 0 ? hd.z & k6 : ((hd.w >> 4) & k4) | (((hd.z >> 6) & k2) << 4);
+    const int isum = ubyte(sc, 0) * s0 + ubyte(sc, 1) * s1 + ubyte(sc, 2) * s2 + ubyte(sc, 3) * s3;
+    const int msum = ubyte(mn, 0) * (int)(int16_t)(pp.x & 0xffff) + ubyte(mn, 1) * (int)(int16_t)(pp.x >> 16) +
+                     ubyte(mn, 2) * (int)(int16_t)(pp.y & 0xffff) + ubyte(mn, 3) * (int)(int16_t)(pp.y >> 16);
     const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))), dx);
     const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))), dx);
     return dd * (float)isum - dm * (float)msum;
 }
 
-// Q6_K, forward path: lane item = (super-block sb, quarter t: half h, 16-column run l0).
-__device__ __forceinline__ float q6k_item(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int it) {
-    const int sb = it >> 2, t = it & 3, h = t >> 1, l0 = (t & 1) * 16;
+__device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int nh,
+                                          int lane) {
+    const int sb = lane >> 1, h = lane & 1;
     const uint8_t* m = slot + sb * Q6K_MAIN;
-    const uint4 A = *reinterpret_cast<const uint4*>(m + 64 * h + l0);
-    const uint4 B = *reinterpret_cast<const uint4*>(m + 64 * h + 32 + l0);
-    const uint4 H = *reinterpret_cast<const uint4*>(m + 128 + 32 * h + l0);
-    const uint32_t scw = *reinterpret_cast<const uint32_t*>(m + 192 + 8 * h) >> (8 * (l0 >> 4));
-    const uint32_t scw2 = *reinterpret_cast<const uint32_t*>(m + 196 + 8 * h) >> (8 * (l0 >> 4));
-    const int8_t* xb = a.q8k + (c0 + sb) * QK_K + 128 * h + l0;
-    const int4 x1 = *reinterpret_cast<const int4*>(xb);
-    const int4 x2 = *reinterpret_cast<const int4*>(xb + 32);
-    const int4 x3 = *reinterpret_cast<const int4*>(xb + 64);
-    const int4 x4 = *reinterpret_cast<const int4*>(xb + 96);
+    const uint4* qa = reinterpret_cast<const uint4*>(m + 64 * h);        // ql[64h .. +32)
+    const uint4* qb = reinterpret_cast<const uint4*>(m + 64 * h + 32);   // ql[64h+32 .. +32)
+    const uint4* qh = reinterpret_cast<const uint4*>(m + 128 + 32 * h);  // qh[32h .. +32)
+    const uint4 A0 = qa[0], A1 = qa[1], B0 = qb[0], B1 = qb[1], H0 = qh[0], H1 = qh[1];
+    const uint2 scw = *reinterpret_cast<const uint2*>(m + 192 + 8 * h);  // int8 scales sc[8h .. +8)
+    const int4* xv = reinterpret_cast<const int4*>(a.q8k + c0 * QK_K) + lane;
+    int4 x[8];
+#pragma unroll
+    for (int v = 0; v < 8; v++) x[v] = xv[v * nh];
+    const uint4 bsw = *reinterpret_cast<const uint4*>(a.q8k_bs + (c0 + sb) * 16 + 8 * h);
+    const float dx = a.q8k_d[c0 + sb];
+    const float dw = h2f(dsec[sb]);
+    // word k of ql/qh holds positions l = 4k..4k+3 of the four 32-element groups
+    // (elements 128h + l, +32, +64, +96; sub-blocks 2*group + k/4)
     const uint32_t m4 = 0x0f0f0f0fu, m2 = 0x30303030u;
-    int d1 = 0, d2 = 0, d3 = 0, d4 = 0;
-#define Q6K_WORD(Aw, Bw, Hw, X1, X2, X3, X4)                              \
-    d1 = __dp4a((int)(((Aw) & m4) | (((Hw) << 4) & m2)), X1, d1);         \
-    d2 = __dp4a((int)(((Bw) & m4) | (((Hw) << 2) & m2)), X2, d2);         \
-    d3 = __dp4a((int)((((Aw) >> 4) & m4) | ((Hw) & m2)), X3, d3);         \
-    d4 = __dp4a((int)((((Bw) >> 4) & m4) | (((Hw) >> 2) & m2)), X4, d4);
-    Q6K_WORD(A.x, B.x, H.x, x1.x, x2.x, x3.x, x4.x)
-    Q6K_WORD(A.y, B.y, H.y, x1.y, x2.y, x3.y, x4.y)
-    Q6K_WORD(A.z, B.z, H.z, x1.z, x2.z, x3.z, x4.z)
-    Q6K_WORD(A.w, B.w, H.w, x1.w, x2.w, x3.w, x4.w)
-#undef Q6K_WORD
-    // q is stored +32: sum (q-32)*x = sum q*x - 32 * bsum over the 16 elements
-    const int16_t* bs = a.q8k_bs + (c0 + sb) * 16 + 8 * h + (l0 >> 4);
-    d1 -= 32 * (int)bs[0];
-    d2 -= 32 * (int)bs[2];
-    d3 -= 32 * (int)bs[4];
-    d4 -= 32 * (int)bs[6];
-    // scales sc[8h + l0/16 + {0, 2, 4, 6}] (int8)
-    const int s1 = (int)(int8_t)(scw & 0xff), s2 = (int)(int8_t)((scw >> 16) & 0xff);
-    const int s3 = (int)(int8_t)(scw2 & 0xff), s4 = (int)(int8_t)((scw2 >> 16) & 0xff);
-    const int isum = s1 * d1 + s2 * d2 + s3 * d3 + s4 * d4;
-    return __fmul_rn(h2f(drow[c0 + sb]), a.q8k_d[c0 + sb]) * (float)isum;
-}
-
-__device__ __forceinline__ float chunk_q4k_fwd(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int first,
-                                               int stride) {
-    const int items = cb * 4;
-    float acc0 = 0.f, acc1 = 0.f;
-    int base = first;
-    for (; base + stride < items; base += 2 * stride) {  // two independent items in flight
-        const int i0 = base + lane, i1 = base + stride + lane;
-        acc0 += q4k_item(slot, a, c0, i0);
-        if (i1 < items) acc1 += q4k_item(slot, a, c0, i1);
+    int t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#define Q6_WORD(Aw, Bw, Hw, X1, X2, X3, X4, T0)                                        \
+    t[T0 + 0] = dp4a_us(((Aw) & m4) | (((Hw) << 4) & m2), X1, t[T0 + 0]);              \
+    t[T0 + 2] = dp4a_us(((Bw) & m4) | (((Hw) << 2) & m2), X2, t[T0 + 2]);              \
+    t[T0 + 4] = dp4a_us((((Aw) >> 4) & m4) | ((Hw) & m2), X3, t[T0 + 4]);              \
+    t[T0 + 6] = dp4a_us((((Bw) >> 4) & m4) | (((Hw) >> 2) & m2), X4, t[T0 + 6]);
+    Q6_WORD(A0.x, B0.x, H0.x, x[0].x, x[2].x, x[4].x, x[6].x, 0)
+    Q6_WORD(A0.y, B0.y, H0.y, x[0].y, x[2].y, x[4].y, x[6].y, 0)
+    Q6_WORD(A0.z, B0.z, H0.z, x[0].z, x[2].z, x[4].z, x[6].z, 0)
+    Q6_WORD(A0.w, B0.w, H0.w, x[0].w, x[2].w, x[4].w, x[6].w, 0)
+    Q6_WORD(A1.x, B1.x, H1.x, x[1].x, x[3].x, x[5].x, x[7].x, 1)
+    Q6_WORD(A1.y, B1.y, H1.y, x[1].y, x[3].y, x[5].y, x[7].y, 1)
+    Q6_WORD(A1.z, B1.z, H1.z, x[1].z, x[3].z, x[5].z, x[7].z, 1)
+    Q6_WORD(A1.w, B1.w, H1.w, x[1].w, x[3].w, x[5].w, x[7].w, 1)
+#undef Q6_WORD
+    // q is stored +32: sum (q-32)*x = sum q*x - 32 * bsum over each 16 elements
+    const uint32_t bw[4] = {bsw.x, bsw.y, bsw.z, bsw.w};
+    int isum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int bs = (int)(int16_t)((bw[i >> 1] >> (16 * (i & 1))) & 0xffff);
+        isum += sbyte(i < 4 ? scw.x : scw.y, i & 3) * (t[i] - 32 * bs);
     }
-    for (; base < items; base += stride) {
-        const int i = base + lane;
-        if (i < items) acc0 += q4k_item(slot, a, c0, i);
-    }
-    return acc0 + acc1;
-}
-
-__device__ __forceinline__ float chunk_q6k_fwd(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int cb,
-                                               int lane, int first, int stride) {
-    const int items = cb * 4;
-    float acc0 = 0.f, acc1 = 0.f;
-    int base = first;
-    for (; base + stride < items; base += 2 * stride) {
-        const int i0 = base + lane, i1 = base + stride + lane;
-        acc0 += q6k_item(slot, drow, a, c0, i0);
-        if (i1 < items) acc1 += q6k_item(slot, drow, a, c0, i1);
-    }
-    for (; base < items; base += stride) {
-        const int i = base + lane;
-        if (i < items) acc0 += q6k_item(slot, drow, a, c0, i);
-    }
-    return acc0 + acc1;
+    return __fmul_rn(dw, dx) * (float)isum;
 }
 
 template <bool DOTS>
@@ -284,7 +259,7 @@ __device__ __forceinline__ float chunk_q4k(const uint8_t* slot, const Act& a, in
 }
 
 template <bool DOTS>
-__device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int cb,
+__device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int cb,
                                            int lane, int first, int stride, int32_t* isum_row) {
     float acc = 0.f;
     const int items = cb * 4;
@@ -324,7 +299,7 @@ __device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* 
             d3 -= 32 * (int)bs[4];
             d4 -= 32 * (int)bs[6];
             isum = (int)sc[0] * d1 + (int)sc[2] * d2 + (int)sc[4] * d3 + (int)sc[6] * d4;
-            if (t == 0 && !DOTS) dd = __fmul_rn(h2f(drow[c0 + sb]), a.q8k_d[c0 + sb]);
+            if (t == 0 && !DOTS) dd = __fmul_rn(h2f(dsec[sb]), a.q8k_d[c0 + sb]);
         }
         isum += __shfl_xor_sync(0xffffffffu, isum, 1);
         isum += __shfl_xor_sync(0xffffffffu, isum, 2);
@@ -336,33 +311,37 @@ __device__ __forceinline__ float chunk_q6k(const uint8_t* slot, const uint16_t* 
     return acc;
 }
 
+// Q8_0: the warp reads the row chunk as consecutive 512-byte runs, lane l taking 16-byte
+// vector l of each (half of 32-block l/2 of the run); the two lanes of a block add their
+// integer sums.  Activations use the natural layout, which gives the same contiguous reads.
 template <bool DOTS>
-__device__ __forceinline__ float chunk_q80(const uint8_t* slot, const uint16_t* drow, const Act& a, int c0, int cb,
-                                           int lane, int first, int stride, int32_t* isum_row) {
+__device__ __forceinline__ float chunk_q80(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int cb,
+                                           int lane, int32_t* isum_row) {
     float acc = 0.f;
-    const int nblk = cb * 8;  // 32-element blocks in the chunk
-    const int b0 = c0 * 8;
-    for (int base = first; base < nblk; base += stride) {
-        const int b = base + lane;
-        if (b >= nblk) continue;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(slot + b * 32);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(slot + b * 32 + 16);
-        const int4* xq = reinterpret_cast<const int4*>(a.q80 + (b0 + b) * 32);
-        const int4 x0 = xq[0], x1 = xq[1];
-        int s = 0;
-        s = __dp4a((int)w0.x, x0.x, s);
-        s = __dp4a((int)w0.y, x0.y, s);
-        s = __dp4a((int)w0.z, x0.z, s);
-        s = __dp4a((int)w0.w, x0.w, s);
-        s = __dp4a((int)w1.x, x1.x, s);
-        s = __dp4a((int)w1.y, x1.y, s);
-        s = __dp4a((int)w1.z, x1.z, s);
-        s = __dp4a((int)w1.w, x1.w, s);
-        if (DOTS) {
-            isum_row[b0 + b] = s;
-        } else {
-            // candle BlockQ8_0::vec_dot: sumi as f32 * d_w * d_x, left to right
-            acc += __fmul_rn(__fmul_rn((float)s, h2f(drow[b0 + b])), a.q80_d[b0 + b]);
+    const int nvec = cb * 16;  // 16-byte vectors in the row chunk
+    const int b0 = c0 * 8;     // first 32-block of the chunk
+    const uint4* w = reinterpret_cast<const uint4*>(slot);
+    const int4* x = reinterpret_cast<const int4*>(a.q80 + c0 * QK_K);
+    for (int i0 = 0; i0 < nvec; i0 += 32) {
+        const int i = i0 + lane;
+        int sum = 0;
+        if (i < nvec) {
+            const uint4 wv = w[i];
+            const int4 xv = x[i];
+            sum = __dp4a((int)wv.x, xv.x, 0);
+            sum = __dp4a((int)wv.y, xv.y, sum);
+            sum = __dp4a((int)wv.z, xv.z, sum);
+            sum = __dp4a((int)wv.w, xv.w, sum);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (i < nvec && (lane & 1) == 0) {
+            const int b = i >> 1;
+            if (DOTS) {
+                isum_row[b0 + b] = sum;
+            } else {
+                // candle BlockQ8_0::vec_dot: sumi as f32 * d_w * d_x, left to right
+                acc += __fmul_rn(__fmul_rn((float)sum, h2f(dsec[b])), a.q80_d[b0 + b]);
+            }
         }
     }
     return acc;
@@ -395,16 +374,51 @@ __device__ __forceinline__ float chunk_f16(const uint8_t* slot, const Act& a, in
 }
 
 // Prologue (consumer warps): optional RMSNorm (candle_nn::ops::rms_norm: m = sqrt(sum(x^2)/K
-// + eps), y = x / m * w) and quantisation of the activation into shared memory.
-__device__ void build_activation(const GemvParams& p, uint8_t* smem, float* red) {
-    const int K = p.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float m = 1.f;
+// + eps), y = x / m * w) and quantisation of the activation into shared memory.  Warp w owns
+// the 256-element blocks w, w + 8, ...; lane l holds elements 8l .. 8l+7 of a block.  Loads
+// go out kActGroup blocks at a time so a warp waits for one L2 round trip per group, not per
+// block; with a norm, the first group's values stay in registers between the two passes.
+constexpr int kActGroup = 2;
+
+__device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(src);
+    const float4 b = *reinterpret_cast<const float4*>(src + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ void build_activation(const GemvParams& p, uint8_t* smem, float* red, bool transposed) {
+    const int K = p.K, nb = K / QK_K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nmine = (nb - warp + kConsumerWarps - 1) / kConsumerWarps;
     const bool norm = p.norm_w != nullptr;
+    // candle Mlp: silu(w1 x) * (w3 x), silu(a) = a / (1 + exp(-a))
+    auto glu = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); };
+    auto load_x = [&](int b, float (&v)[8]) {
+        load8(p.x + b * QK_K + 8 * lane, v);
+        if (p.glu_in) {
+            float u[8];
+            load8(p.x + K + b * QK_K + 8 * lane, u);
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = glu(v[i], u[i]);
+        }
+    };
+    float xr[kActGroup][8];  // the first group, kept from the norm pass
+    float m = 1.f;
     if (norm) {
         float ss = 0.f;
-        for (int i = tid * 4; i < K; i += kConsumers * 4) {
-            const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        for (int g0 = 0; g0 < nmine; g0 += kActGroup) {
+            float t[kActGroup][8];
+#pragma unroll
+            for (int i = 0; i < kActGroup; i++)
+                if (g0 + i < nmine) load_x(warp + kConsumerWarps * (g0 + i), t[i]);
+#pragma unroll
+            for (int i = 0; i < kActGroup; i++)
+                if (g0 + i < nmine) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        ss += t[i][j] * t[i][j];
+                        if (g0 == 0) xr[i][j] = t[i][j];
+                    }
+                }
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
@@ -414,54 +428,46 @@ __device__ void build_activation(const GemvParams& p, uint8_t* smem, float* red)
         for (int w = 0; w < kConsumerWarps; w++) tot += red[w];
         m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
     }
-    // candle Mlp: silu(w1 x) * (w3 x), silu(a) = a / (1 + exp(-a))
-    auto glu = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); };
-    auto xval = [&](int i) -> float {
-        float v = p.x[i];
-        if (p.glu_in) v = glu(v, p.x[K + i]);
-        if (norm) v = __fmul_rn(__fdiv_rn(v, m), p.norm_w[i]);
-        return v;
-    };
-    if (p.act_f32 >= 0) {
-        float* dst = reinterpret_cast<float*>(smem + p.act_f32);
-        for (int i = tid; i < K; i += kConsumers) dst[i] = xval(i);
-    }
-    if (p.act_q8k >= 0) {
-        int8_t* qs = reinterpret_cast<int8_t*>(smem + p.act_q8k);
-        float* dd = reinterpret_cast<float*>(smem + p.act_q8k_d);
-        int16_t* bs = reinterpret_cast<int16_t*>(smem + p.act_q8k_bs);
-        int16_t* ps = reinterpret_cast<int16_t*>(smem + p.act_q8k_ps);
-        for (int b = warp; b < K / QK_K; b += kConsumerWarps) {
-            float v[8];
-            const float4 x0 = *reinterpret_cast<const float4*>(p.x + b * QK_K + lane * 8);
-            const float4 x1 = *reinterpret_cast<const float4*>(p.x + b * QK_K + lane * 8 + 4);
-            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w; v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
-            if (p.glu_in) {
-                const float4 u0 = *reinterpret_cast<const float4*>(p.x + K + b * QK_K + lane * 8);
-                const float4 u1 = *reinterpret_cast<const float4*>(p.x + K + b * QK_K + lane * 8 + 4);
-                const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    for (int g0 = 0; g0 < nmine; g0 += kActGroup) {
+        float t[kActGroup][8], wv[kActGroup][8];
 #pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = glu(v[i], uv[i]);
-            }
-            if (norm) {
-                const float4 w0 = *reinterpret_cast<const float4*>(p.norm_w + b * QK_K + lane * 8);
-                const float4 w1 = *reinterpret_cast<const float4*>(p.norm_w + b * QK_K + lane * 8 + 4);
-                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        for (int i = 0; i < kActGroup; i++) {
+            if (g0 + i >= nmine) continue;
+            const int b = warp + kConsumerWarps * (g0 + i);
+            if (norm && g0 == 0) {
 #pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], m), wv[i]);
+                for (int j = 0; j < 8; j++) t[i][j] = xr[i][j];
+            } else {
+                load_x(b, t[i]);
             }
-            q8k_quant_warp(v, qs + b * QK_K, bs + b * 16, dd + b, lane);
-            __syncwarp();
-            if (lane < 8) ps[b * 8 + lane] = (int16_t)((int)bs[b * 16 + 2 * lane] + (int)bs[b * 16 + 2 * lane + 1]);
+            if (norm) load8(p.norm_w + b * QK_K + 8 * lane, wv[i]);
         }
-    }
-    if (p.act_q80 >= 0) {
-        int8_t* qs = reinterpret_cast<int8_t*>(smem + p.act_q80);
-        float* dd = reinterpret_cast<float*>(smem + p.act_q80_d);
-        for (int b = warp; b < K / QK8_0; b += kConsumerWarps) {
-            float d;
-            qs[b * QK8_0 + lane] = q80_quant_warp(xval(b * QK8_0 + lane), d);
-            if (lane == 0) dd[b] = h2f(f2h(d));
+#pragma unroll
+        for (int i = 0; i < kActGroup; i++) {
+            if (g0 + i >= nmine) continue;
+            const int b = warp + kConsumerWarps * (g0 + i);
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = norm ? __fmul_rn(__fdiv_rn(t[i][j], m), wv[i][j]) : t[i][j];
+            if (p.act_f32 >= 0) {
+                float* dst = reinterpret_cast<float*>(smem + p.act_f32) + b * QK_K + 8 * lane;
+                *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
+            if (p.act_q8k >= 0) {
+                int8_t* qs = reinterpret_cast<int8_t*>(smem + p.act_q8k);
+                int16_t* bs = reinterpret_cast<int16_t*>(smem + p.act_q8k_bs);
+                int16_t* ps = reinterpret_cast<int16_t*>(smem + p.act_q8k_ps);
+                int8_t* my = qs + (transposed ? xt_offset(b, lane, nb, p.cbs) : b * QK_K + 8 * lane);
+                q8k_quant_warp(v, my, bs + b * 16, reinterpret_cast<float*>(smem + p.act_q8k_d) + b, lane);
+                __syncwarp();
+                if (lane < 8) ps[b * 8 + lane] = (int16_t)((int)bs[b * 16 + 2 * lane] + (int)bs[b * 16 + 2 * lane + 1]);
+            }
+            if (p.act_q80 >= 0) {
+                float d;
+                q80_quant_lane8(v, reinterpret_cast<int8_t*>(smem + p.act_q80) + b * QK_K + 8 * lane, d);
+                if ((lane & 3) == 0) reinterpret_cast<float*>(smem + p.act_q80_d)[b * 8 + (lane >> 2)] = h2f(f2h(d));
+            }
         }
     }
 }
@@ -518,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     // The next kernel may start (and prefetch its weights) only once this one is past its
     // own wait, so at most two kernels of a chain overlap.
     pdl_launch_dependents();
-    build_activation(p, smem, red);
+    build_activation(p, smem, red, EPI != EPI_DOTS);
     consumer_sync();
 
     Act a;
@@ -535,9 +541,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
         const UnitRow ur = unit_row(p, u, warp);
         const DevMatrix& m = p.seg[ur.seg < 0 ? unit_seg(p, u) : ur.seg].m;
-        const int sbb = sb_bytes(m.type);
-        const int prow = (u - p.seg[unit_seg(p, u)].unit_begin) * kTileRows + warp;
-        const uint16_t* drow = m.dplane ? m.dplane + (int64_t)prow * m.d_per_row : nullptr;
+        const int sbm = sb_main_bytes(m.type), sbd = sb_d_bytes(m.type);
         int32_t* isum_row = nullptr;
         int32_t* msum_row = nullptr;
         if (EPI == EPI_DOTS && ur.seg >= 0) {
@@ -551,18 +555,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             if (!timed_out && !mbar_wait_bounded(&full[s], (it / S) & 1, p.err)) timed_out = true;
             if (!timed_out && ur.seg >= 0) {
                 const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
-                const uint8_t* slot = ring + s * p.stage_bytes + warp * cb * sbb;
+                const uint8_t* stage = ring + s * p.stage_bytes;
+                const uint8_t* slot = stage + warp * cb * sbm;
+                const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
                 switch (m.type) {
                 case TPTC_TYPE_Q4_K:
                     if (EPI == EPI_DOTS) chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
-                    else acc += chunk_q4k_fwd(slot, a, c0, cb, lane, 0, 32);
+                    else if (lane < 2 * cb) acc += q4k_half(slot, a, c0, 2 * cb, lane);
                     break;
                 case TPTC_TYPE_Q6_K:
-                    if (EPI == EPI_DOTS) chunk_q6k<true>(slot, drow, a, c0, cb, lane, 0, 32, isum_row);
-                    else acc += chunk_q6k_fwd(slot, drow, a, c0, cb, lane, 0, 32);
+                    if (EPI == EPI_DOTS) chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
+                    else if (lane < 2 * cb) acc += q6k_half(slot, dsec, a, c0, 2 * cb, lane);
                     break;
                 case TPTC_TYPE_Q8_0:
-                    acc += chunk_q80<EPI == EPI_DOTS>(slot, drow, a, c0, cb, lane, 0, 32, isum_row);
+                    acc += chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
                     break;
                 default: acc += chunk_f16(slot, a, c0, cb, lane, 0, 32); break;
                 }

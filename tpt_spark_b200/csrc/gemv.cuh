@@ -5,9 +5,16 @@
 
 namespace tptc {
 
-// Bytes of `main` per 256-element super-block, and super-blocks per tile chunk.
+// Bytes per 256-element super-block in the device layout (all of it, GGUF size), the part
+// before a tile's scale section, and its share of that section; super-blocks per chunk.
 __host__ __device__ inline int sb_bytes(int type) {
+    return type == TPTC_TYPE_Q4_K ? 144 : type == TPTC_TYPE_Q6_K ? 210 : type == TPTC_TYPE_Q8_0 ? 272 : 512;
+}
+__host__ __device__ inline int sb_main_bytes(int type) {
     return type == TPTC_TYPE_Q4_K ? 144 : type == TPTC_TYPE_Q6_K ? 208 : type == TPTC_TYPE_Q8_0 ? 256 : 512;
+}
+__host__ __device__ inline int sb_d_bytes(int type) {
+    return type == TPTC_TYPE_Q6_K ? 2 : type == TPTC_TYPE_Q8_0 ? 16 : 0;
 }
 __host__ __device__ inline int chunk_sb(int type) { return type == TPTC_TYPE_F16 ? 8 : 16; }
 
@@ -17,16 +24,18 @@ constexpr int kTileRows = 8;
 //
 // Per-super-block encoding (256 elements):
 //   Q4_K  144 B: the GGUF block unchanged (d | dmin | scales[12] | qs[128])
-//   Q6_K  208 B: ql | qh | scales          ; dplane = f16 d per super-block [N, K/256]
-//   Q8_0  256 B: qs of eight 32-blocks     ; dplane = f16 d per 32-block   [N, K/32]
+//   Q6_K  208 B: ql | qh | scales, plus its f16 d in the tile's scale section
+//   Q8_0  256 B: qs of eight 32-blocks, plus their eight f16 d in the scale section
 //   F16   512 B: 256 f16 values
-// Tiling of `main`: rows are grouped by 8 (N padded to Npad, zero rows) and each row is cut
-// into chunks of cbs super-blocks; tile (rg, c) = 8 rows x chunk c is one contiguous run of
-// 8 * cb * sbb bytes (cb = cbs, or the remainder for the last chunk), rows in order.  A
-// decode GEMV stage is therefore a single 1-D bulk copy of 13-32 KB, the size the copy
-// engine needs to reach full HBM bandwidth (small copies are bound by a fixed per-copy
-// cost).  glu = 1 marks a fused gate/up matrix: tile rows 0-3 are gate rows 4t..4t+3 and
-// tile rows 4-7 the same up rows, N counts gate + up rows.
+// Tiling: rows are grouped by 8 (N padded to Npad, zero rows) and each row is cut into
+// chunks of cbs super-blocks; tile (rg, c) = 8 rows x chunk c is one contiguous run of
+// 8 * cb * sb_bytes (cb = cbs, or the remainder for the last chunk): the 8 rows' quant bytes
+// in row order (cb * sb_main_bytes each), then the scale section (row-major [8][cb] entries
+// of sb_d_bytes).  A decode GEMV stage is therefore a single 1-D bulk copy of 18-35 KB that
+// carries everything its dot products read, the size the copy engine needs to reach full
+// HBM bandwidth (small copies are bound by a fixed per-copy cost).  glu = 1 marks a fused
+// gate/up matrix: tile rows 0-3 are gate rows 4t..4t+3 and tile rows 4-7 the same up rows,
+// N counts gate + up rows.
 struct DevMatrix {
     int type = 0;
     int N = 0, K = 0;  // logical rows (gate + up for glu) and columns
@@ -34,10 +43,8 @@ struct DevMatrix {
     int cbs = 16;      // super-blocks per chunk
     int glu = 0;
     uint8_t* main = nullptr;
-    uint16_t* dplane = nullptr;  // indexed by physical (tile-order) row
-    int64_t main_row_bytes = 0;  // bytes per row in `main` (K / 256 * sbb)
-    int64_t d_per_row = 0;       // f16 entries per row in `dplane`
-    int64_t bytes() const { return main_row_bytes * N + d_per_row * 2 * N; }
+    int64_t main_row_bytes = 0;  // bytes per row (K / 256 * sb_bytes)
+    int64_t bytes() const { return main_row_bytes * N; }
     int64_t main_bytes() const { return main_row_bytes * Npad; }
 };
 
@@ -51,7 +58,6 @@ inline DevMatrix dm_geometry(int type, int N, int K, int glu) {
     m.Npad = (N + kTileRows - 1) / kTileRows * kTileRows;
     m.cbs = chunk_sb(type);
     m.main_row_bytes = (int64_t)(K / 256) * sb_bytes(type);
-    m.d_per_row = type == TPTC_TYPE_Q6_K ? K / 256 : type == TPTC_TYPE_Q8_0 ? K / 32 : 0;
     return m;
 }
 
@@ -63,12 +69,30 @@ __host__ __device__ inline int dm_phys_row(const DevMatrix& m, int row) {
     return (r / 4) * 8 + (r % 4) + 4 * up;
 }
 
-// Address of super-block `sb` of physical row `prow`.
+// Start of the tile holding super-block `sb` of physical row `prow`, its chunk length, and
+// the super-block's index inside the chunk.
+__host__ __device__ inline const uint8_t* dm_tile(const DevMatrix& m, int prow, int sb, int& cb, int& j) {
+    const int nsb = m.K / 256, c = sb / m.cbs;
+    cb = (nsb - c * m.cbs) < m.cbs ? (nsb - c * m.cbs) : m.cbs;
+    j = sb - c * m.cbs;
+    return m.main + (int64_t)(prow / kTileRows) * kTileRows * m.main_row_bytes +
+           (int64_t)c * kTileRows * m.cbs * sb_bytes(m.type);
+}
+
+// Quant bytes of super-block `sb` of physical row `prow`.
 __host__ __device__ inline const uint8_t* dm_block(const DevMatrix& m, int prow, int sb) {
-    const int sbb = sb_bytes(m.type), nsb = m.K / 256;
-    const int c = sb / m.cbs, cb = (nsb - c * m.cbs) < m.cbs ? (nsb - c * m.cbs) : m.cbs;
-    const int64_t tile = (int64_t)(prow / kTileRows) * kTileRows * m.main_row_bytes + (int64_t)c * kTileRows * m.cbs * sbb;
-    return m.main + tile + (int64_t)(prow % kTileRows) * cb * sbb + (int64_t)(sb - c * m.cbs) * sbb;
+    int cb, j;
+    const uint8_t* t = dm_tile(m, prow, sb, cb, j);
+    const int sbm = sb_main_bytes(m.type);
+    return t + (int64_t)((prow % kTileRows) * cb + j) * sbm;
+}
+
+// f16 scales of super-block `sb` of physical row `prow` (Q6_K: 1, Q8_0: 8).
+__host__ __device__ inline const uint16_t* dm_scales(const DevMatrix& m, int prow, int sb) {
+    int cb, j;
+    const uint8_t* t = dm_tile(m, prow, sb, cb, j);
+    return reinterpret_cast<const uint16_t*>(t + (int64_t)kTileRows * cb * sb_main_bytes(m.type) +
+                                             (int64_t)((prow % kTileRows) * cb + j) * sb_d_bytes(m.type));
 }
 
 enum GemvEpi : int {

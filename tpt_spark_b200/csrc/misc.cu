@@ -26,9 +26,9 @@ __global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok
         if (emb.type == TPTC_TYPE_Q4_K) {
             v = q4k_elem(blk, e);
         } else if (emb.type == TPTC_TYPE_Q6_K) {
-            v = q6k_elem(blk, h2f(emb.dplane[(int64_t)row * emb.d_per_row + i / QK_K]), e);
+            v = q6k_elem(blk, h2f(dm_scales(emb, row, i / QK_K)[0]), e);
         } else if (emb.type == TPTC_TYPE_Q8_0) {
-            v = __fmul_rn((float)(int8_t)blk[e], h2f(emb.dplane[(int64_t)row * emb.d_per_row + i / QK8_0]));
+            v = __fmul_rn((float)(int8_t)blk[e], h2f(dm_scales(emb, row, i / QK_K)[e / QK8_0]));
         } else {
             v = h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
         }

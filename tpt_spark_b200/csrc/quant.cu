@@ -39,7 +39,7 @@ __global__ void quant_q8k_kernel(const float* __restrict__ x, int64_t nb, BlockQ
     const float4* src = reinterpret_cast<const float4*>(x + b * QK_K + lane * 8);
     const float4 a = src[0], c = src[1];
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
-    q8k_quant_warp(v, out[b].qs, out[b].bsums, &out[b].d, lane);
+    q8k_quant_warp(v, out[b].qs + 8 * lane, out[b].bsums, &out[b].d, lane);
 }
 
 // One warp per 32-element block; output 34-byte blocks (f16 d, int8 qs[32]).
@@ -70,12 +70,13 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, 
     } else if (m.type == TPTC_TYPE_Q6_K) {
         const uint8_t* src = row + (int64_t)sb * Q6K_BYTES;
         for (int k = 0; k < Q6K_MAIN; k++) dst[k] = src[k];
-        m.dplane[(int64_t)prow * m.d_per_row + sb] = (uint16_t)(src[208] | (src[209] << 8));
+        const_cast<uint16_t*>(dm_scales(m, prow, sb))[0] = (uint16_t)(src[208] | (src[209] << 8));
     } else if (m.type == TPTC_TYPE_Q8_0) {
+        uint16_t* dsc = const_cast<uint16_t*>(dm_scales(m, prow, sb));
         for (int j = 0; j < 8; j++) {
             const uint8_t* src = row + ((int64_t)sb * 8 + j) * Q80_BYTES;
             for (int k = 0; k < 32; k++) dst[32 * j + k] = src[2 + k];
-            m.dplane[(int64_t)prow * m.d_per_row + sb * 8 + j] = (uint16_t)(src[0] | (src[1] << 8));
+            dsc[j] = (uint16_t)(src[0] | (src[1] << 8));
         }
     } else {
         const uint8_t* src = row + (int64_t)sb * 512;
@@ -98,11 +99,11 @@ __global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, __half*
     } else if (m.type == TPTC_TYPE_Q4_K) {
         for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q4k_elem(blk, e0 + j));
     } else if (m.type == TPTC_TYPE_Q6_K) {
-        const float d = h2f(m.dplane[(int64_t)prow * m.d_per_row + k0 / QK_K]);
+        const float d = h2f(dm_scales(m, prow, k0 / QK_K)[0]);
         for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q6k_elem(blk, d, e0 + j));
     } else {
         const int8_t* q = reinterpret_cast<const int8_t*>(blk + e0);
-        const float d = h2f(m.dplane[(int64_t)prow * m.d_per_row + k0 / QK8_0]);
+        const float d = h2f(dm_scales(m, prow, k0 / QK_K)[e0 / QK8_0]);
         for (int j = 0; j < 8; j++) v[j] = __float2half_rn(__fmul_rn((float)q[j], d));
     }
     *reinterpret_cast<uint4*>(out + (int64_t)r * m.K + k0) = *reinterpret_cast<const uint4*>(v);

@@ -15,10 +15,10 @@
 namespace tptc {
 
 // Quantise one 256-element block held in registers across a warp: lane holds x[8*lane ..
-// 8*lane+7].  Writes qs (int8, 8 per lane), returns d via *d_out (lane 0) and the 16
-// bsums (lanes with lane%2==0 own bsum lane/2).  Integer results are bit-exact with
-// candle.
-__device__ __forceinline__ void q8k_quant_warp(const float (&x)[8], int8_t* qs_dst, int16_t* bsums_dst,
+// 8*lane+7].  Writes the lane's 8 int8 quants to qs_lane (4-byte aligned; the caller picks
+// the layout), d via *d_dst (lane 0) and the 16 bsums (lanes with lane%2==0 own bsum
+// lane/2).  Integer results are bit-exact with candle.
+__device__ __forceinline__ void q8k_quant_warp(const float (&x)[8], int8_t* qs_lane, int16_t* bsums_dst,
                                                float* d_dst, int lane) {
     // first index of the largest |x| and its signed value
     float amax = 0.f, vmax = 0.f;
@@ -64,8 +64,8 @@ __device__ __forceinline__ void q8k_quant_warp(const float (&x)[8], int8_t* qs_d
     uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
                   ((uint32_t)(uint8_t)q[7] << 24);
     // 4-byte stores: in a block_q8_K array, qs starts at 4 + 292*b (4-byte aligned only)
-    reinterpret_cast<uint32_t*>(qs_dst)[2 * lane] = w0;
-    reinterpret_cast<uint32_t*>(qs_dst)[2 * lane + 1] = w1;
+    reinterpret_cast<uint32_t*>(qs_lane)[0] = w0;
+    reinterpret_cast<uint32_t*>(qs_lane)[1] = w1;
     int s2 = s + __shfl_xor_sync(0xffffffffu, s, 1);
     if ((lane & 1) == 0) bsums_dst[lane >> 1] = static_cast<int16_t>(s2);
     if (lane == 0) *d_dst = d;
@@ -78,6 +78,25 @@ __device__ __forceinline__ int8_t q80_quant_warp(float x, float& d) {
     d = __fdiv_rn(amax, 127.f);
     float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
     return static_cast<int8_t>(roundf(__fmul_rn(x, id)));
+}
+
+// Q8_0 of eight 32-element blocks held across a warp as in q8k_quant_warp (lane holds
+// elements 8*lane .. +7, so block lane/4): writes the lane's 8 int8 quants to qs_lane and
+// returns the block's f32 scale d (before f16 storage) in every lane of the block.
+__device__ __forceinline__ void q80_quant_lane8(const float (&x)[8], int8_t* qs_lane, float& d) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(x[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    d = __fdiv_rn(amax, 127.f);
+    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+    uint32_t w[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        w[i >> 2] |= (uint32_t)(uint8_t)static_cast<int8_t>(roundf(__fmul_rn(x[i], id))) << (8 * (i & 3));
+    reinterpret_cast<uint32_t*>(qs_lane)[0] = w[0];
+    reinterpret_cast<uint32_t*>(qs_lane)[1] = w[1];
 }
 
 // ---- dequantisation of GGUF blocks (raw layout) ------------------------------------------
