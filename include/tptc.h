@@ -178,8 +178,9 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
 TPTC_API void tptc_matrix_destroy(tptc_matrix* m);
 /* Bytes the matrix occupies on the device (the algorithmic bytes of one GEMV over it). */
 TPTC_API int64_t tptc_matrix_bytes(const tptc_matrix* m);
-/* y[N] = W . x with candle QMatMul semantics (x quantised to Q8_K / Q8_0 inside the
- * kernel; F16 in f32) -- gemm.wgsl + dequant_*.wgsl fused. */
+/* y[N] = W . x with candle QMatMul semantics (x quantised to Q8_K / Q8_0 on the device; F16
+ * in f32) -- gemm.wgsl + dequant_*.wgsl fused.  The matrix holds the scratch of its launches:
+ * calls on the same matrix must not overlap on the GPU. */
 TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void* stream);
 /* Per (row, super-block) integer sums of the same kernel: isum = sum_j sc_j*dot_j,
  * msum = sum_j m_j*bsum_j (Q4_K; 0 otherwise); [N, K/256] for k-quants, [N, K/32] Q8_0. */

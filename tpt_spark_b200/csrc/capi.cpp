@@ -1,5 +1,6 @@
 // capi.cpp -- extern "C" boundary (include/tptc.h).  Every entry point converts C++ state
 // into an int status and keeps the message for tptc_last_error.
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -23,6 +24,7 @@ struct tptc_matrix {
     tptc::DevMatrix m;
     uint8_t* mem = nullptr;
     int* err = nullptr;
+    uint8_t* act = nullptr;  // the prepared activation of this matrix's GEMV launches
     int device = 0;
 };
 
@@ -243,13 +245,15 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
     const int64_t raw_row = ggml_type == TPTC_TYPE_Q6_K ? (int64_t)K / 256 * 210
                             : ggml_type == TPTC_TYPE_Q8_0 ? (int64_t)K / 32 * 34 : d.main_row_bytes;
     const size_t main_al = ((size_t)d.main_bytes() + 255) / 256 * 256;
-    cudaError_t e = cudaMalloc(&m->mem, main_al + 256);
+    const size_t total = main_al + 256 + tptc::gemv_act_bytes_max(K);
+    cudaError_t e = cudaMalloc(&m->mem, total);
     if (e != cudaSuccess) {
         delete m;
         return cuda_fail(e, "cudaMalloc(matrix)");
     }
     d.main = m->mem;
     m->err = reinterpret_cast<int*>(m->mem + main_al);
+    m->act = m->mem + main_al + 256;
     const size_t raw_bytes = (size_t)raw_row * N;
     const uint8_t* src = static_cast<const uint8_t*>(raw);
     uint8_t* tmp = nullptr;
@@ -258,7 +262,7 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
         if (e == cudaSuccess) e = cudaMemcpy(tmp, raw, raw_bytes, cudaMemcpyHostToDevice);
         src = tmp;
     }
-    if (e == cudaSuccess) e = cudaMemset(m->mem, 0, main_al + 256);
+    if (e == cudaSuccess) e = cudaMemset(m->mem, 0, total);
     if (e == cudaSuccess) e = tptc::launch_repack(src, raw_row, N, 0, d, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (tmp) cudaFree(tmp);
@@ -279,6 +283,15 @@ TPTC_API void tptc_matrix_destroy(tptc_matrix* m) {
 
 TPTC_API int64_t tptc_matrix_bytes(const tptc_matrix* m) { return m ? m->m.bytes() : -1; }
 
+// Programmatic dependent launch for kernel-level GEMVs: TPTC_PDL=1 (the engine's switch).
+static bool kernel_pdl() {
+    static const bool on = [] {
+        const char* e = getenv("TPTC_PDL");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 static tptc::GemvParams matrix_params(const tptc_matrix* m, const float* x) {
     tptc::GemvParams p = {};
     p.nseg = 1;
@@ -286,6 +299,7 @@ static tptc::GemvParams matrix_params(const tptc_matrix* m, const float* x) {
     p.K = m->m.K;
     p.x = x;
     p.err = m->err;
+    p.act_global = m->act;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -297,7 +311,7 @@ TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void*
     if (!m || !d_x || !d_y) return TPTC_ERR_ARG;
     tptc::GemvParams p = matrix_params(m, d_x);
     p.out = d_y;
-    cudaError_t e = tptc::gemv_launch(p, tptc::EPI_STORE, static_cast<cudaStream_t>(stream), false);
+    cudaError_t e = tptc::gemv_launch(p, tptc::EPI_STORE, static_cast<cudaStream_t>(stream), kernel_pdl());
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemv");
 }
 

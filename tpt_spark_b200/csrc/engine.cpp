@@ -377,6 +377,8 @@ Status Engine::alloc_runtime() {
     const size_t o_hist = take((size_t)max_seq_ * 4 + 64);
     const size_t o_part = take(attn_decode_partial_floats(n_heads_l_, n_kv_l_, hd, attn_splits_) * 4);
     const size_t o_cnt = take((size_t)n_kv_l_ * 4);
+    const int k_max = std::max(m.dim, std::max(m.ffn / tp_size_, n_heads_l_ * hd));
+    const size_t o_act = take(gemv_act_bytes_max(k_max));
     rt_size_ = off;
     cudaError_t ce = cudaMalloc(&rt_, rt_size_);
     if (ce != cudaSuccess) {
@@ -403,6 +405,7 @@ Status Engine::alloc_runtime() {
     history_ = reinterpret_cast<uint32_t*>(rt_ + o_hist);
     attn_partial_ = reinterpret_cast<float*>(rt_ + o_part);
     attn_counters_ = reinterpret_cast<int*>(rt_ + o_cnt);
+    act_ = rt_ + o_act;
 
     // candle quantized_llama precomput_freqs_cis: theta_i = 1/base^(2i/hd) (f32 powf),
     // angle = pos * theta_i, cos/sin in f32 -- built on the host with the C library's powf,
@@ -441,6 +444,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams p = {};
         p.K = m.dim;
         p.err = err_;
+        p.act_global = act_;
         p.eps = m.rms_eps;
         // q | k | v with fused RMSNorm; v goes straight into the cache, q and k are rotated
         // by the attention kernel
@@ -484,6 +488,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams o = {};
         o.K = n_heads_l_ * hd;
         o.err = err_;
+        o.act_global = act_;
         o.nseg = 1;
         o.seg[0] = GemvSeg{L.o, 0};
         o.x = attn_;
@@ -502,6 +507,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams g = {};
         g.K = m.dim;
         g.err = err_;
+        g.act_global = act_;
         g.eps = m.rms_eps;
         g.nseg = 1;
         g.seg[0] = GemvSeg{L.glu, 0};
@@ -514,6 +520,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams d = {};
         d.K = m.ffn / tp_size_;
         d.err = err_;
+        d.act_global = act_;
         d.nseg = 1;
         d.seg[0] = GemvSeg{L.down, 0};
         d.x = h_;
@@ -538,6 +545,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
     GemvParams h = {};
     h.K = m.dim;
     h.err = err_;
+    h.act_global = act_;
     h.eps = m.rms_eps;
     h.nseg = 1;
     h.seg[0] = GemvSeg{output_, 0};

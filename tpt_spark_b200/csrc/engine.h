@@ -124,6 +124,7 @@ class Engine {
     uint32_t* history_ = nullptr;  // [max_seq]
     int* pos_ = nullptr;
     int* err_ = nullptr;
+    uint8_t* act_ = nullptr;  // prepared GEMV activation (gemv_launch)
     float* attn_partial_ = nullptr;
     int* attn_counters_ = nullptr;
     int attn_splits_ = 1;

@@ -36,6 +36,7 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kRingBudget = 100 * 1024;    // shared memory per CTA (two kernels fit per SM)
 
+
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
 // Named barrier 2 + i joins consumer warps i and i + 4 only.
 __device__ __forceinline__ void pair_sync(int i) { asm volatile("bar.sync %0, 64;" ::"r"(2 + i) : "memory"); }
@@ -373,12 +374,13 @@ __device__ __forceinline__ float chunk_f16(const uint8_t* slot, const Act& a, in
     return acc;
 }
 
-// Prologue (consumer warps): optional RMSNorm (candle_nn::ops::rms_norm: m = sqrt(sum(x^2)/K
-// + eps), y = x / m * w) and quantisation of the activation into shared memory.  Warp w owns
-// the 256-element blocks w, w + 8, ...; lane l holds elements 8l .. 8l+7 of a block.  Loads
-// go out kActGroup blocks at a time so a warp waits for one L2 round trip per group, not per
-// block; with a norm, the first group's values stay in registers between the two passes.
-constexpr int kActGroup = 2;
+// Activation kernel, launched before every GEMV: optional RMSNorm (candle_nn::ops::rms_norm:
+// m = sqrt(sum(x^2)/K + eps), y = x / m * w) and quantisation of the input into
+// p.act_global, laid out exactly as the GEMV's shared-memory activation region, so that
+// each GEMV CTA takes it with one bulk copy instead of quantising the vector itself.  One
+// warp per 256-element block (lane l holds elements 8l .. 8l+7); with a norm every CTA also
+// sums x^2 over the whole vector (each thread a strided set of float4, all in flight).
+constexpr int kActWarps = 8;
 
 __device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
     const float4 a = *reinterpret_cast<const float4*>(src);
@@ -386,97 +388,104 @@ __device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-__device__ void build_activation(const GemvParams& p, uint8_t* smem, float* red, bool transposed) {
+// candle Mlp: silu(w1 x) * (w3 x), silu(a) = a / (1 + exp(-a))
+__device__ __forceinline__ float glu_val(float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); }
+
+__global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_constant__ GemvParams p, int transposed) {
+    __shared__ float red[kActWarps];
     const int K = p.K, nb = K / QK_K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nmine = (nb - warp + kConsumerWarps - 1) / kConsumerWarps;
+    const int b = blockIdx.x * kActWarps + warp;
+    pdl_wait();
+    pdl_launch_dependents();
     const bool norm = p.norm_w != nullptr;
-    // candle Mlp: silu(w1 x) * (w3 x), silu(a) = a / (1 + exp(-a))
-    auto glu = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); };
-    auto load_x = [&](int b, float (&v)[8]) {
+    // every load of the kernel goes out before the first use: this warp's block (and its norm
+    // weights) and, with a norm, this thread's share of the sum of squares
+    float v[8], w8[8];
+    const bool mine = b < nb;
+    if (mine) {
         load8(p.x + b * QK_K + 8 * lane, v);
-        if (p.glu_in) {
-            float u[8];
-            load8(p.x + K + b * QK_K + 8 * lane, u);
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = glu(v[i], u[i]);
-        }
-    };
-    float xr[kActGroup][8];  // the first group, kept from the norm pass
-    float m = 1.f;
+        if (norm) load8(p.norm_w + b * QK_K + 8 * lane, w8);
+    }
     if (norm) {
+        constexpr int kMaxF4 = 8;  // float4 per thread kept in flight (K <= 8192 in one pass)
+        float4 xs[kMaxF4], us[kMaxF4];
         float ss = 0.f;
-        for (int g0 = 0; g0 < nmine; g0 += kActGroup) {
-            float t[kActGroup][8];
+        for (int base = tid * 4; base < K; base += kActWarps * 32 * 4 * kMaxF4) {
 #pragma unroll
-            for (int i = 0; i < kActGroup; i++)
-                if (g0 + i < nmine) load_x(warp + kConsumerWarps * (g0 + i), t[i]);
-#pragma unroll
-            for (int i = 0; i < kActGroup; i++)
-                if (g0 + i < nmine) {
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        ss += t[i][j] * t[i][j];
-                        if (g0 == 0) xr[i][j] = t[i][j];
-                    }
+            for (int j = 0; j < kMaxF4; j++) {
+                const int i = base + j * kActWarps * 32 * 4;
+                if (i < K) {
+                    xs[j] = *reinterpret_cast<const float4*>(p.x + i);
+                    if (p.glu_in) us[j] = *reinterpret_cast<const float4*>(p.x + K + i);
                 }
+            }
+#pragma unroll
+            for (int j = 0; j < kMaxF4; j++) {
+                const int i = base + j * kActWarps * 32 * 4;
+                if (i < K) {
+                    float4 x4 = xs[j];
+                    if (p.glu_in)
+                        x4 = make_float4(glu_val(x4.x, us[j].x), glu_val(x4.y, us[j].y), glu_val(x4.z, us[j].z),
+                                         glu_val(x4.w, us[j].w));
+                    ss += x4.x * x4.x + x4.y * x4.y + x4.z * x4.z + x4.w * x4.w;
+                }
+            }
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
-        consumer_sync();
+        __syncthreads();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; w++) tot += red[w];
-        m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
+        for (int w = 0; w < kActWarps; w++) tot += red[w];
+        const float m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
+        if (mine) {
+            if (p.glu_in) {
+                float u[8];
+                load8(p.x + K + b * QK_K + 8 * lane, u);
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = glu_val(v[i], u[i]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], m), w8[i]);
+        }
+    } else if (mine && p.glu_in) {
+        float u[8];
+        load8(p.x + K + b * QK_K + 8 * lane, u);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = glu_val(v[i], u[i]);
     }
-    for (int g0 = 0; g0 < nmine; g0 += kActGroup) {
-        float t[kActGroup][8], wv[kActGroup][8];
-#pragma unroll
-        for (int i = 0; i < kActGroup; i++) {
-            if (g0 + i >= nmine) continue;
-            const int b = warp + kConsumerWarps * (g0 + i);
-            if (norm && g0 == 0) {
-#pragma unroll
-                for (int j = 0; j < 8; j++) t[i][j] = xr[i][j];
-            } else {
-                load_x(b, t[i]);
-            }
-            if (norm) load8(p.norm_w + b * QK_K + 8 * lane, wv[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < kActGroup; i++) {
-            if (g0 + i >= nmine) continue;
-            const int b = warp + kConsumerWarps * (g0 + i);
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = norm ? __fmul_rn(__fdiv_rn(t[i][j], m), wv[i][j]) : t[i][j];
-            if (p.act_f32 >= 0) {
-                float* dst = reinterpret_cast<float*>(smem + p.act_f32) + b * QK_K + 8 * lane;
-                *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-                *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
-            }
-            if (p.act_q8k >= 0) {
-                int8_t* qs = reinterpret_cast<int8_t*>(smem + p.act_q8k);
-                int16_t* bs = reinterpret_cast<int16_t*>(smem + p.act_q8k_bs);
-                int16_t* ps = reinterpret_cast<int16_t*>(smem + p.act_q8k_ps);
-                int8_t* my = qs + (transposed ? xt_offset(b, lane, nb, p.cbs) : b * QK_K + 8 * lane);
-                q8k_quant_warp(v, my, bs + b * 16, reinterpret_cast<float*>(smem + p.act_q8k_d) + b, lane);
-                __syncwarp();
-                if (lane < 8) ps[b * 8 + lane] = (int16_t)((int)bs[b * 16 + 2 * lane] + (int)bs[b * 16 + 2 * lane + 1]);
-            }
-            if (p.act_q80 >= 0) {
-                float d;
-                q80_quant_lane8(v, reinterpret_cast<int8_t*>(smem + p.act_q80) + b * QK_K + 8 * lane, d);
-                if ((lane & 3) == 0) reinterpret_cast<float*>(smem + p.act_q80_d)[b * 8 + (lane >> 2)] = h2f(f2h(d));
-            }
-        }
+    if (b >= nb) return;
+    uint8_t* out = p.act_global;
+    if (p.act_f32 >= 0) {
+        float4* dst = reinterpret_cast<float4*>(out + p.act_f32 + (size_t)(b * QK_K + 8 * lane) * 4);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    if (p.act_q8k >= 0) {
+        const float(&vv)[1][8] = *reinterpret_cast<const float(*)[1][8]>(&v);
+        uint32_t q[1][2];
+        int s16[1], s32[1];
+        float d[1];
+        q8k_quant_regs<1>(vv, q, s16, s32, d, lane);
+        const int oq = transposed ? xt_offset(b, lane, nb, p.cbs) : b * QK_K + 8 * lane;
+        *reinterpret_cast<uint2*>(out + p.act_q8k + oq) = make_uint2(q[0][0], q[0][1]);
+        if ((lane & 1) == 0) reinterpret_cast<int16_t*>(out + p.act_q8k_bs)[b * 16 + (lane >> 1)] = (int16_t)s16[0];
+        if ((lane & 3) == 0) reinterpret_cast<int16_t*>(out + p.act_q8k_ps)[b * 8 + (lane >> 2)] = (int16_t)s32[0];
+        if (lane == 0) reinterpret_cast<float*>(out + p.act_q8k_d)[b] = d[0];
+    }
+    if (p.act_q80 >= 0) {
+        uint32_t q[2];
+        float d;
+        q80_quant_lane8(v, q, d);
+        *reinterpret_cast<uint2*>(out + p.act_q80 + b * QK_K + 8 * lane) = make_uint2(q[0], q[1]);
+        if ((lane & 3) == 0) reinterpret_cast<float*>(out + p.act_q80_d)[b * 8 + (lane >> 2)] = h2f(f2h(d));
     }
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages];
-    __shared__ float red[kConsumerWarps];
+    __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
     __shared__ float glu_up[2][4];
     int unit_no = 0;
 
@@ -490,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(&actbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -524,8 +534,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     // The next kernel may start (and prefetch its weights) only once this one is past its
     // own wait, so at most two kernels of a chain overlap.
     pdl_launch_dependents();
-    build_activation(p, smem, red, EPI != EPI_DOTS);
-    consumer_sync();
+    // the activation, prepared by act_quant_kernel in this region's layout: one bulk copy
+    if (tid == 0) {
+        mbar_expect_tx(&actbar, (uint32_t)p.act_bytes);
+        bulk_g2s(smem, p.act_global, (uint32_t)p.act_bytes, &actbar, 0);
+    }
+    bool timed_out = !mbar_wait_bounded(&actbar, 0, p.err);
 
     Act a;
     a.f32 = p.act_f32 >= 0 ? reinterpret_cast<const float*>(smem + p.act_f32) : nullptr;
@@ -537,7 +551,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     a.q80_d = p.act_q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act_q80_d) : nullptr;
 
     int it = 0;
-    bool timed_out = false;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
         const UnitRow ur = unit_row(p, u, warp);
         const DevMatrix& m = p.seg[ur.seg < 0 ? unit_seg(p, u) : ur.seg].m;
@@ -674,7 +687,20 @@ static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl) {
-    if (p.stages < 1 || p.stages > kGemvMaxStages || p.grid < 1) return cudaErrorInvalidValue;
+    if (p.stages < 1 || p.stages > kGemvMaxStages || p.grid < 1 || !p.act_global) return cudaErrorInvalidValue;
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((p.K / QK_K + kActWarps - 1) / kActWarps);
+        cfg.blockDim = dim3(kActWarps * 32);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, act_quant_kernel, p, epi == EPI_DOTS ? 0 : 1);
+        if (e != cudaSuccess) return e;
+    }
     switch (epi) {
     case EPI_STORE: return launch_epi<EPI_STORE>(p, st, pdl);
     case EPI_RESID: return launch_epi<EPI_RESID>(p, st, pdl);
@@ -688,6 +714,7 @@ cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl)
 cudaError_t gemv_init_device() {
     const int max_smem = 200 * 1024;
     cudaError_t e;
+
     if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
     if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
     if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;

@@ -141,13 +141,19 @@ struct GemvParams {
     int grid;         // CTAs (persistent: units are strided over them)
     int act_f32, act_q8k, act_q8k_d, act_q8k_bs, act_q8k_ps, act_q80, act_q80_d;  // smem offsets, -1 absent
     int act_bytes;
+    // Device buffer of act_bytes (16-byte aligned) receiving the prepared activation in the
+    // shared-memory layout; written by the quantisation kernel, bulk-copied by every CTA.
+    uint8_t* act_global;
     int* err;
 };
 
 // Host helpers (gemv.cu).
 void gemv_prepare(GemvParams& p, int sm_count = 148);  // work split, ring, activation layout
 size_t gemv_smem(const GemvParams& p);
+// Two launches: the activation kernel (norm + quantisation into p.act_global), then the GEMV.
 cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl);
+// Upper bound of act_bytes for inputs of K elements (buffer sizing).
+inline size_t gemv_act_bytes_max(int K) { return (size_t)K * 7 + 1024; }
 cudaError_t gemv_init_device();  // per-device kernel attributes (call once per device)
 
 }  // namespace tptc

@@ -14,61 +14,72 @@
 
 namespace tptc {
 
-// Quantise one 256-element block held in registers across a warp: lane holds x[8*lane ..
-// 8*lane+7].  Writes the lane's 8 int8 quants to qs_lane (4-byte aligned; the caller picks
-// the layout), d via *d_dst (lane 0) and the 16 bsums (lanes with lane%2==0 own bsum
-// lane/2).  Integer results are bit-exact with candle.
+// Q8_K quantisation of NB 256-element blocks held in registers across a warp: for block k,
+// lane holds x[k][0..7] = elements 8*lane .. 8*lane+7.  Per block the lane receives its 8
+// int8 quants packed in q[k][0..1], the sum of 16 elements s16[k] (bsum lane/2, equal in
+// both lanes of a pair), the sum of 32 elements s32[k] (sub-block lane/4, equal in its 4
+// lanes) and the block scale d[k] (every lane).  The blocks are independent, so their
+// reduction chains overlap.  The largest |x| and its first index come from the hardware
+// warp reductions (non-negative floats order like their bit patterns).  Integer results are
+// bit-exact with candle.
+template <int NB>
+__device__ __forceinline__ void q8k_quant_regs(const float (&x)[NB][8], uint32_t (&q)[NB][2], int (&s16)[NB],
+                                               int (&s32)[NB], float (&d)[NB], int lane) {
+    uint32_t amax_bits[NB];
+#pragma unroll
+    for (int k = 0; k < NB; k++) {
+        uint32_t a = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) a = max(a, __float_as_uint(fabsf(x[k][i])));
+        amax_bits[k] = __reduce_max_sync(0xffffffffu, a);
+    }
+    float vmax[NB];
+#pragma unroll
+    for (int k = 0; k < NB; k++) {
+        uint32_t first = 0xffffffffu;
+        float v = 0.f;
+#pragma unroll
+        for (int i = 7; i >= 0; i--)
+            if (__float_as_uint(fabsf(x[k][i])) == amax_bits[k]) {
+                first = (uint32_t)(lane * 8 + i);
+                v = x[k][i];
+            }
+        const uint32_t imin = __reduce_min_sync(0xffffffffu, first);
+        vmax[k] = __shfl_sync(0xffffffffu, v, (int)(imin >> 3) & 31);
+    }
+#pragma unroll
+    for (int k = 0; k < NB; k++) {
+        int s = 0;
+        q[k][0] = q[k][1] = 0;
+        d[k] = 0.f;
+        if (amax_bits[k] != 0) {
+            const float iscale = __fdiv_rn(-128.f, vmax[k]);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int qi = (int)static_cast<int8_t>(fminf(roundf(__fmul_rn(iscale, x[k][i])), 127.f));
+                q[k][i >> 2] |= (uint32_t)(qi & 0xff) << (8 * (i & 3));
+                s += qi;
+            }
+            d[k] = __fdiv_rn(1.f, iscale);
+        }
+        s16[k] = s + __shfl_xor_sync(0xffffffffu, s, 1);
+        s32[k] = s16[k] + __shfl_xor_sync(0xffffffffu, s16[k], 2);
+    }
+}
+
+// One block into a block_q8_K-style destination: qs_lane = this lane's 8 quants (4-byte
+// aligned), 16 bsums, d.
 __device__ __forceinline__ void q8k_quant_warp(const float (&x)[8], int8_t* qs_lane, int16_t* bsums_dst,
                                                float* d_dst, int lane) {
-    // first index of the largest |x| and its signed value
-    float amax = 0.f, vmax = 0.f;
-    int imax = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        float a = fabsf(x[i]);
-        if (a > amax) {
-            amax = a;
-            vmax = x[i];
-            imax = lane * 8 + i;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float a2 = __shfl_xor_sync(0xffffffffu, amax, o);
-        float v2 = __shfl_xor_sync(0xffffffffu, vmax, o);
-        int i2 = __shfl_xor_sync(0xffffffffu, imax, o);
-        if (a2 > amax || (a2 == amax && i2 < imax)) {
-            amax = a2;
-            vmax = v2;
-            imax = i2;
-        }
-    }
-    int8_t q[8];
-    int s = 0;
-    float d = 0.f;
-    if (amax == 0.f) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) q[i] = 0;
-    } else {
-        float iscale = __fdiv_rn(-128.f, vmax);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float v = roundf(__fmul_rn(iscale, x[i]));
-            q[i] = static_cast<int8_t>(fminf(v, 127.f));
-            s += q[i];
-        }
-        d = __fdiv_rn(1.f, iscale);
-    }
-    uint32_t w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) | ((uint32_t)(uint8_t)q[2] << 16) |
-                  ((uint32_t)(uint8_t)q[3] << 24);
-    uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
-                  ((uint32_t)(uint8_t)q[7] << 24);
-    // 4-byte stores: in a block_q8_K array, qs starts at 4 + 292*b (4-byte aligned only)
-    reinterpret_cast<uint32_t*>(qs_lane)[0] = w0;
-    reinterpret_cast<uint32_t*>(qs_lane)[1] = w1;
-    int s2 = s + __shfl_xor_sync(0xffffffffu, s, 1);
-    if ((lane & 1) == 0) bsums_dst[lane >> 1] = static_cast<int16_t>(s2);
-    if (lane == 0) *d_dst = d;
+    const float(&xx)[1][8] = *reinterpret_cast<const float(*)[1][8]>(&x);
+    uint32_t q[1][2];
+    int s16[1], s32[1];
+    float d[1];
+    q8k_quant_regs<1>(xx, q, s16, s32, d, lane);
+    reinterpret_cast<uint32_t*>(qs_lane)[0] = q[0][0];
+    reinterpret_cast<uint32_t*>(qs_lane)[1] = q[0][1];
+    if ((lane & 1) == 0) bsums_dst[lane >> 1] = static_cast<int16_t>(s16[0]);
+    if (lane == 0) *d_dst = d[0];
 }
 
 // Quantise one 32-element block to Q8_0 across a warp (lane = element).  Returns the
@@ -80,10 +91,10 @@ __device__ __forceinline__ int8_t q80_quant_warp(float x, float& d) {
     return static_cast<int8_t>(roundf(__fmul_rn(x, id)));
 }
 
-// Q8_0 of eight 32-element blocks held across a warp as in q8k_quant_warp (lane holds
-// elements 8*lane .. +7, so block lane/4): writes the lane's 8 int8 quants to qs_lane and
-// returns the block's f32 scale d (before f16 storage) in every lane of the block.
-__device__ __forceinline__ void q80_quant_lane8(const float (&x)[8], int8_t* qs_lane, float& d) {
+// Q8_0 of eight 32-element blocks held across a warp as in q8k_quant_regs (lane holds
+// elements 8*lane .. +7, so block lane/4): the lane's 8 int8 quants packed in q[0..1] and the
+// block's f32 scale d (before f16 storage) in every lane of the block.
+__device__ __forceinline__ void q80_quant_lane8(const float (&x)[8], uint32_t (&q)[2], float& d) {
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(x[i]));
@@ -91,12 +102,10 @@ __device__ __forceinline__ void q80_quant_lane8(const float (&x)[8], int8_t* qs_
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     d = __fdiv_rn(amax, 127.f);
     const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
-    uint32_t w[2] = {0, 0};
+    q[0] = q[1] = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++)
-        w[i >> 2] |= (uint32_t)(uint8_t)static_cast<int8_t>(roundf(__fmul_rn(x[i], id))) << (8 * (i & 3));
-    reinterpret_cast<uint32_t*>(qs_lane)[0] = w[0];
-    reinterpret_cast<uint32_t*>(qs_lane)[1] = w[1];
+        q[i >> 2] |= (uint32_t)(uint8_t)static_cast<int8_t>(roundf(__fmul_rn(x[i], id))) << (8 * (i & 3));
 }
 
 // ---- dequantisation of GGUF blocks (raw layout) ------------------------------------------
