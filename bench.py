@@ -9,14 +9,18 @@ at batch 1).  Inputs: a seeded random-init model of the C5 shape written as a GG
 ids.  The 4.9 GB of weights is far larger than the 126 MB L2, so no L2 flush is needed
 between steps.
 
-  value         decode tok/s, CUDA events over K chained decode graphs (device argmax feeds
-                the next step), max over ranks
-  e2e           the same metric through the C ABI with host buffers (tptc_decode: token id
-                and position copied in, argmax copied out, every step)
-  roofline      decode step vs measured HBM bandwidth (weights + fp16 KV read per token)
-  gemv_c1       C1 Q4_K 4096x4096 GEMV, rotating through 64 weight copies (> 4x L2)
-  prefill       prefill tok/s of the prompt (device time)
-  cpu_baseline  the CPU oracle (restated candle path) on the box's host cores, bounded sample
+  value           decode tok/s, CUDA events over K chained decode graphs (device argmax feeds
+                  the next step), max over ranks
+  e2e             the same metric through the C ABI with host buffers (tptc_decode: token id
+                  and position copied in, argmax copied out, every step)
+  roofline        the dominant decode kernel, the Q4_K GEMV at the C5 ffn gate|up shape
+                  (28672 x 4096, 66 MB) with its activation kernel, timed with CUDA events in
+                  a graph rotating through copies larger than L2; traffic from the committed
+                  ncu summary of the same kernel (profiles/)
+  decode_roofline the whole decode step vs measured HBM bandwidth (weights + fp16 KV / token)
+  gemv_c1         C1 Q4_K 4096x4096 GEMV, rotating through 64 weight copies (> 4x L2)
+  prefill         prefill tok/s of the prompt (device time)
+  cpu_baseline    the CPU oracle (restated candle path) on the box's host cores, bounded sample
 
 --impl reference times the CPU oracle on the same workload (rank 0 only).
 """
@@ -50,7 +54,7 @@ def peaks():
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=512)
+    ap.add_argument("--steps", type=int, default=1024)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c5_llama8b_q4km")
@@ -182,37 +186,52 @@ def decode_bytes(cfg, kv_len_mean):
     return tot
 
 
-def gemv_c1(torch):
-    """C1: Q4_K [4096 x 4096] GEMV, x ~ N(0,1) quantised to Q8_K inside the kernel."""
+def gemv_time(torch, gtype, N, K, w_std=0.02, seed=4242, iters=256):
+    """Average device time of one GEMV launch pair (activation kernel + GEMV, as in the decode
+    step) over a CUDA graph of `iters` launches rotating through weight copies totalling more
+    than 4x the 126 MB L2, timed with CUDA events on the graph's stream."""
     from tpt_spark_b200 import synth
     from tpt_spark_b200.kernels import Matrix
 
-    C = synth.GEMV_C1
-    N, K = C["N"], C["K"]
-    copies = 64  # 64 x 9.4 MB = 604 MB > 4x the 126 MB L2
-    w = synth.normal(4242, N * K, C["w_std"])
-    raw = synth.encode(C["type"], w)
-    mats = []
-    for i in range(copies):
-        mats.append(Matrix(C["type"], raw, N, K))
+    raw = synth.encode(gtype, synth.normal(seed, N * K, w_std))
+    one = synth.type_bytes(gtype, N * K)
+    copies = max(2, min(64, -(-(512 << 20) // one)))
+    mats = [Matrix(gtype, raw, N, K) for _ in range(copies)]
     x = torch.randn(K, device="cuda")
     y = torch.empty(N, device="cuda")
-    st = torch.cuda.current_stream().cuda_stream
-    for m in mats[:8]:
-        m.gemv(x, y, st)
-    torch.cuda.synchronize()
-    iters = 640
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(iters):
-        mats[i % copies].gemv(x, y, st)
-    e1.record()
-    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for m in mats[: min(copies, 8)]:
+            m.gemv(x, y, s.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(iters):
+                mats[i % copies].gemv(x, y, torch.cuda.current_stream().cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / iters
-    algo = mats[0].nbytes + K * 4 + N * 4  # 9,469,952 B: weights + x + y
+    algo = mats[0].nbytes + K * 4 + N * 4  # weights + x + y
+    del g
     for m in mats:
         m.close()
     return algo, us
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded in profiles/<name>.md ("dram_bytes_per_launch: N"), or None."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", name + ".md")):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip().replace(",", ""))
+    except Exception:
+        pass
+    return None
 
 
 def cpu_baseline(path, cfg, max_seconds=25.0, prompt_len=8):
@@ -315,7 +334,10 @@ def run_ours(args, dist):
     dist.barrier()
     torch.cuda.synchronize()
     with Clocks(dist.local) as clk:
+        torch.cuda.profiler.start()  # ncu --profile-from-start off captures only this region
         ms, tok, kv_mean = run_steps(args.steps, tok)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     torch.cuda.synchronize()
     dist.barrier()
     ms = dist.max(ms)
@@ -336,9 +358,15 @@ def run_ours(args, dist):
     step_bytes = decode_bytes(cfg, kv_mean)
     ms_step = ms / args.steps
     achieved = step_bytes / (ms_step / 1000.0) / 1e9
-    gemv_bytes, gemv_us = gemv_c1(torch)
+    launches_per_step = eng.decode_kernels()
+    os.environ.setdefault("TPTC_PDL", "1")  # kernel-level GEMVs chained as in the decode graph
+    from tpt_spark_b200 import synth as _s
+
+    dom_bytes, dom_us = gemv_time(torch, _s.Q4_K, 2 * cfg.ffn, cfg.dim)
+    dom_gbs = dom_bytes / (dom_us * 1e-6) / 1e9
+    C = _s.GEMV_C1
+    gemv_bytes, gemv_us = gemv_time(torch, C["type"], C["N"], C["K"], C["w_std"])
     gemv_gbs = gemv_bytes / (gemv_us * 1e-6) / 1e9
-    launches_per_step = 5 * cfg.n_layers + 3
 
     line = {
         "metric": "decode tok/s (bs=1)", "value": round(tps * dist.world, 3), "unit": "tok/s", "n_gpus": args.gpus,
@@ -349,10 +377,14 @@ def run_ours(args, dist):
                    "parallelism": "replica" if dist.world > 1 else "single", "l2": "inputs larger than L2 (4.9 GB weights)"},
         "e2e": {"value": round(e2e_tps * dist.world, 3), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4},
-        "roofline": {"bound": "hbm", "kernel": "decode step (163 launches, CUDA graph)",
-                     "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                     "algorithmic_bytes": step_bytes, "peak_src": pk["src"]},
+        "roofline": {"bound": "hbm", "kernel": f"act_quant + gemv_kernel, Q4_K {2 * cfg.ffn}x{cfg.dim} (ffn gate|up shape)",
+                     "achieved": round(dom_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(dom_gbs / pk["hbm_gbs"], 4),
+                     "traffic": profile_traffic(f"gemv_q4k_{2 * cfg.ffn}x{cfg.dim}"),
+                     "algorithmic_bytes": dom_bytes, "us_per_launch": round(dom_us, 3), "peak_src": pk["src"]},
+        "decode_roofline": {"bound": "hbm", "kernel": f"decode step ({launches_per_step} launches, CUDA graph)",
+                            "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                            "frac": round(achieved / pk["hbm_gbs"], 4), "algorithmic_bytes": step_bytes},
         "gemv_c1": {"bound": "hbm", "kernel": "gemv_kernel Q4_K 4096x4096 (C1)", "us": round(gemv_us, 3),
                     "achieved": round(gemv_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "frac": round(gemv_gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": gemv_bytes},

@@ -151,6 +151,9 @@ TPTC_API int tptc_infer(tptc_ctx* ctx, const uint32_t* prompt, int n, const tptc
 /* Device time (CUDA events on the context's stream) of the last tptc_prefill or
  * tptc_decode_greedy call, in milliseconds. */
 TPTC_API int tptc_last_device_ms(const tptc_ctx* ctx, double* ms);
+/* Kernel launches in one decode step (the kernel nodes of the step's CUDA graph), or an error
+ * code when no model is loaded. */
+TPTC_API int tptc_decode_kernels(const tptc_ctx* ctx);
 /* Wall-clock phases of the last tptc_infer call in milliseconds (wgpu_engine.rs:320-330). */
 TPTC_API int tptc_last_timing(const tptc_ctx* ctx, double* prefill_ms, double* decode_ms, int* n_prompt,
                               int* n_generated);

@@ -59,6 +59,7 @@ SIGNATURES = {
     "tptc_decode_greedy": (c_int, [c_vp, c_u32, c_int, c_int, c_vp]),
     "tptc_infer": (c_int, [c_vp, c_vp, c_int, ctypes.POINTER(InferParamsC), TOKEN_CB, c_vp]),
     "tptc_last_device_ms": (c_int, [c_vp, ctypes.POINTER(c_d)]),
+    "tptc_decode_kernels": (c_int, [c_vp]),
     "tptc_last_timing": (c_int, [c_vp, ctypes.POINTER(c_d), ctypes.POINTER(c_d), ctypes.POINTER(c_int),
                                  ctypes.POINTER(c_int)]),
     "tptc_dequant": (c_int, [c_int, c_vp, c_i64, c_vp, c_vp]),

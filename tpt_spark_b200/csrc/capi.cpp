@@ -185,6 +185,12 @@ TPTC_API int tptc_last_device_ms(const tptc_ctx* ctx, double* ms) {
     return TPTC_OK;
 }
 
+TPTC_API int tptc_decode_kernels(const tptc_ctx* ctx) {
+    if (!ctx) return TPTC_ERR_ARG;
+    if (!ctx->eng->loaded()) return TPTC_ERR_STATE;
+    return ctx->eng->graph_kernels_;
+}
+
 TPTC_API int tptc_last_timing(const tptc_ctx* ctx, double* prefill_ms, double* decode_ms, int* n_prompt,
                               int* n_generated) {
     if (!ctx) return TPTC_ERR_ARG;

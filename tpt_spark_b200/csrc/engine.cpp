@@ -569,6 +569,17 @@ Status Engine::build_decode_graph(bool chained, cudaGraphExec_t* out) {
         return s;
     }
     if (ce != cudaSuccess) return err(TPTC_ERR_CUDA, cuda_msg(ce, "cudaStreamEndCapture"));
+    size_t nn = 0;
+    if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn) {
+        std::vector<cudaGraphNode_t> nodes(nn);
+        int kernels = 0;
+        if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+            for (size_t i = 0; i < nn; i++) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+            }
+        graph_kernels_ = kernels;
+    }
     ce = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) return err(TPTC_ERR_CUDA, cuda_msg(ce, "cudaGraphInstantiate"));

@@ -66,6 +66,7 @@ class Engine {
     Status infer(const uint32_t* prompt, int n, const tptc_infer_params& p, tptc_token_cb cb, void* user);
 
     double last_prefill_ms = 0, last_decode_ms = 0, last_device_ms = 0;
+    int graph_kernels_ = 0;  // kernel launches in one decode step (nodes of the captured graph)
     int last_n_prompt = 0, last_n_generated = 0;
     std::string last_error;
     int device() const { return device_; }

@@ -168,6 +168,10 @@ class CudaEngine:
                                            ctypes.byref(d)))
         return a.value, b.value, c.value, d.value
 
+    def decode_kernels(self) -> int:
+        """Kernel launches in one decode step (kernel nodes of the step's CUDA graph)."""
+        return self._check(lib().tptc_decode_kernels(self._ctx))
+
     def last_device_ms(self) -> float:
         """CUDA-event time of the last prefill / decode_greedy on the engine's stream."""
         v = ctypes.c_double()
