@@ -25,6 +25,7 @@
 // scheduling.
 #include <algorithm>
 
+#include "act.cuh"
 #include "kernels.h"
 
 namespace tptc {
@@ -153,6 +154,18 @@ __device__ __forceinline__ SplitRange split_range(int kv_len, int max_splits, in
     return r;
 }
 
+// The kv head's outputs (G * HD floats staged at `ob`) as blocks of the next GEMV's prepared
+// activation: warp w quantises block w.  All threads of the CTA call it after a barrier.
+__device__ __forceinline__ void attn_store_act(const AttnDecodeParams& p, const float* ob, int kvh, int G, int HD) {
+    const int nblk = G * HD / 256, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int w = warp; w < nblk; w += kWarps) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = ob[w * 256 + 8 * lane + i];
+        act_store_block(p.act, p.act_transposed, p.act_nb, p.act_out, kvh * nblk + w, v, lane);
+    }
+}
+
 // N2: float2 pairs of the head dimension per lane (hd = 32 * N2); GM: most query heads per
 // kv head.
 template <typename KV, int N2, int GM>
@@ -184,9 +197,9 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
         fence_mbar_init();
         abort_s = 0;
     }
-    pdl_wait();
-    pdl_launch_dependents();
-
+    // Before waiting for the previous kernel (the q|k|v GEMV): the position (set before the
+    // step began) and the key/value rows below it (written by earlier steps) are final, so
+    // the range is known and every tile except the one holding `pos` can be in flight.
     const int kv_len = *p.pos + 1;
     if (kv_len < 1 || kv_len > p.max_seq) {  // position outside the cache: flag it, touch nothing
         if (tid == 0 && kvh == 0 && split == 0 && p.err) atomicExch(p.err, TPTC_ERR_ARG);
@@ -201,8 +214,9 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     const int tile_pos = owner ? (pos - t_begin) / kR : -1;
 
     // Stage s of tile t holds 1-D bulk copies of kR K rows and kR V rows.  Tid 0 fills the
-    // first stages at once -- except the tile holding `pos`, whose key this CTA writes first;
-    // afterwards the last warp to finish a stage refills it (done_warps).
+    // first stages at once -- except the tile holding `pos`, whose value row comes from the
+    // previous kernel and whose key row this CTA writes; afterwards the last warp to finish
+    // a stage refills it (done_warps).
     const KV* kh = static_cast<const KV*>(p.kcache) + (int64_t)kvh * p.max_seq * HD;
     const KV* vh = static_cast<const KV*>(p.vcache) + (int64_t)kvh * p.max_seq * HD;
     auto issue = [&](int t) {
@@ -217,6 +231,9 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     if (tid == 0)
         for (int t = 0; t < S_ring && t < ntiles; t++)
             if (t != tile_pos) issue(t);
+
+    pdl_wait();
+    pdl_launch_dependents();
 
     // RoPE (candle rope_i: interleaved pairs, x0*c - x1*s, x0*s + x1*c) on the group's
     // queries, staged in shared memory
@@ -400,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
         }
         if (S == 1) {
             p.out[(kvh * G + g) * HD + d] = A / L;
+            qs[idx] = A / L;  // q is in registers by now: the buffer stages the outputs
         } else {
             part[g * rec + 4 + d] = A;
             if (d == 0) {
@@ -408,7 +426,13 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
             }
         }
     }
-    if (S == 1) return;
+    if (S == 1) {
+        if (p.act_out) {
+            __syncthreads();
+            attn_store_act(p, qs, kvh, G, HD);
+        }
+        return;
+    }
     __threadfence();
     asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncthreads();
@@ -484,7 +508,15 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
 #pragma unroll
     for (int k = 0; k < kOut; k++) {
         const int idx = tid + k * kThreads;
-        if (idx < G * HD) p.out[(kvh * G + idx / HD) * HD + idx % HD] = O[k] / lsum[idx / HD];
+        if (idx < G * HD) {
+            const float o = O[k] / lsum[idx / HD];
+            p.out[(kvh * G + idx / HD) * HD + idx % HD] = o;
+            qs[idx] = o;
+        }
+    }
+    if (p.act_out) {
+        __syncthreads();
+        attn_store_act(p, qs, kvh, G, HD);
     }
     if (tid == 0) p.counters[kvh] = 0;
 }

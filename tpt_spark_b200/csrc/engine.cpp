@@ -483,7 +483,6 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         a.splits = attn_splits_;
         a.scale = (float)(1.0 / sqrt((double)hd));
         a.err = err_;
-        CU(launch_attn_decode(a, st, pdl_));
 
         GemvParams o = {};
         o.K = n_heads_l_ * hd;
@@ -492,17 +491,34 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         o.nseg = 1;
         o.seg[0] = GemvSeg{L.o, 0};
         o.x = attn_;
+        o.out = tp_ ? tp_->partial(m.dim) : x_;  // row-parallel: partial sums, then allreduce
+        gemv_prepare(o, sm_count_);
+        // the attention kernel writes the o projection's activation itself when every kv
+        // head's output is whole 256-blocks (q8k / q80 / f32 as the o matrix needs)
+        if ((n_heads_l_ / n_kv_l_) * hd % 256 == 0) {
+            a.act_out = act_;
+            a.act = o.act;
+            a.act_transposed = 1;
+            a.act_nb = o.K / 256;
+            o.act_prepared = 1;
+        }
+        CU(launch_attn_decode(a, st, pdl_));
         if (tp_) {
-            // row-parallel: partial sums into h-sized scratch, then allreduce into x
-            o.out = tp_->partial(m.dim);
-            gemv_prepare(o, sm_count_);
             CU(gemv_launch(o, EPI_STORE, st, pdl_));
             RET_IF(tp_->allreduce_add(o.out, x_, m.dim, st));
         } else {
-            o.out = x_;
-            gemv_prepare(o, sm_count_);
             CU(gemv_launch(o, EPI_RESID, st, pdl_));
         }
+
+        GemvParams d = {};
+        d.K = m.ffn / tp_size_;
+        d.err = err_;
+        d.act_global = act_;
+        d.nseg = 1;
+        d.seg[0] = GemvSeg{L.down, 0};
+        d.x = h_;
+        d.out = tp_ ? tp_->partial(m.dim) : x_;  // row-parallel: partial sums, then allreduce
+        gemv_prepare(d, sm_count_);
 
         GemvParams g = {};
         g.K = m.dim;
@@ -516,22 +532,10 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         g.out = h_;
         gemv_prepare(g, sm_count_);
         CU(gemv_launch(g, EPI_GLU, st, pdl_));
-
-        GemvParams d = {};
-        d.K = m.ffn / tp_size_;
-        d.err = err_;
-        d.act_global = act_;
-        d.nseg = 1;
-        d.seg[0] = GemvSeg{L.down, 0};
-        d.x = h_;
         if (tp_) {
-            d.out = tp_->partial(m.dim);
-            gemv_prepare(d, sm_count_);
             CU(gemv_launch(d, EPI_STORE, st, pdl_));
             RET_IF(tp_->allreduce_add(d.out, x_, m.dim, st));
         } else {
-            d.out = x_;
-            gemv_prepare(d, sm_count_);
             CU(gemv_launch(d, EPI_RESID, st, pdl_));
         }
         if (trace) {

@@ -24,8 +24,7 @@
 //     quantising its input).
 #include <algorithm>
 
-#include "gemv.cuh"
-#include "quant.cuh"
+#include "act.cuh"
 
 namespace tptc {
 
@@ -102,14 +101,6 @@ __device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 
 // (d_w*d_x)*isum_half - (dmin_w*d_x)*msum_half; the f32 result differs from scaling the
 // whole block's integer sum only by float rounding.  The DOTS test hook keeps the exact
 // per-block integers (chunk_q4k / chunk_q6k below, natural activation layout).
-
-// Byte offset of the 8 Q8_K quants of lane `lane` (elements 8*lane .. +7) of super-block b
-// in the transposed activation layout.
-__host__ __device__ __forceinline__ int xt_offset(int b, int lane, int nsb, int cbs) {
-    const int c = b / cbs, j = b - c * cbs, cbc = min(cbs, nsb - c * cbs), nh = 2 * cbc;
-    const int h = lane >> 4, v = (lane & 15) >> 1;
-    return c * cbs * QK_K + (v * nh + 2 * j + h) * 16 + (lane & 1) * 8;
-}
 
 __device__ __forceinline__ float q4k_half(const uint8_t* slot, const Act& a, int c0, int nh, int lane) {
     const int sb = lane >> 1, h = lane & 1;
@@ -395,17 +386,15 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
     __shared__ float red[kActWarps];
     const int K = p.K, nb = K / QK_K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = blockIdx.x * kActWarps + warp;
+    const bool norm = p.norm_w != nullptr, mine = b < nb;
+    // the norm weights do not depend on the previous kernel: load them before waiting for it
+    float v[8], w8[8];
+    if (mine && norm) load8(p.norm_w + b * QK_K + 8 * lane, w8);
     pdl_wait();
     pdl_launch_dependents();
-    const bool norm = p.norm_w != nullptr;
-    // every load of the kernel goes out before the first use: this warp's block (and its norm
-    // weights) and, with a norm, this thread's share of the sum of squares
-    float v[8], w8[8];
-    const bool mine = b < nb;
-    if (mine) {
-        load8(p.x + b * QK_K + 8 * lane, v);
-        if (norm) load8(p.norm_w + b * QK_K + 8 * lane, w8);
-    }
+    // then every load of x goes out before the first use: this warp's block and, with a
+    // norm, this thread's share of the sum of squares
+    if (mine) load8(p.x + b * QK_K + 8 * lane, v);
     if (norm) {
         constexpr int kMaxF4 = 8;  // float4 per thread kept in flight (K <= 8192 in one pass)
         float4 xs[kMaxF4], us[kMaxF4];
@@ -455,31 +444,7 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
         for (int i = 0; i < 8; i++) v[i] = glu_val(v[i], u[i]);
     }
     if (b >= nb) return;
-    uint8_t* out = p.act_global;
-    if (p.act_f32 >= 0) {
-        float4* dst = reinterpret_cast<float4*>(out + p.act_f32 + (size_t)(b * QK_K + 8 * lane) * 4);
-        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-    }
-    if (p.act_q8k >= 0) {
-        const float(&vv)[1][8] = *reinterpret_cast<const float(*)[1][8]>(&v);
-        uint32_t q[1][2];
-        int s16[1], s32[1];
-        float d[1];
-        q8k_quant_regs<1>(vv, q, s16, s32, d, lane);
-        const int oq = transposed ? xt_offset(b, lane, nb, p.cbs) : b * QK_K + 8 * lane;
-        *reinterpret_cast<uint2*>(out + p.act_q8k + oq) = make_uint2(q[0][0], q[0][1]);
-        if ((lane & 1) == 0) reinterpret_cast<int16_t*>(out + p.act_q8k_bs)[b * 16 + (lane >> 1)] = (int16_t)s16[0];
-        if ((lane & 3) == 0) reinterpret_cast<int16_t*>(out + p.act_q8k_ps)[b * 8 + (lane >> 2)] = (int16_t)s32[0];
-        if (lane == 0) reinterpret_cast<float*>(out + p.act_q8k_d)[b] = d[0];
-    }
-    if (p.act_q80 >= 0) {
-        uint32_t q[2];
-        float d;
-        q80_quant_lane8(v, q, d);
-        *reinterpret_cast<uint2*>(out + p.act_q80 + b * QK_K + 8 * lane) = make_uint2(q[0], q[1]);
-        if ((lane & 3) == 0) reinterpret_cast<float*>(out + p.act_q80_d)[b * 8 + (lane >> 2)] = h2f(f2h(d));
-    }
+    act_store_block(p.act, transposed, nb, p.act_global, b, v, lane);
 }
 
 template <int EPI>
@@ -492,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int S = p.stages;
     const int nsb = p.K / QK_K;
-    uint8_t* ring = smem + p.act_bytes;
+    uint8_t* ring = smem + p.act.bytes;
 
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
@@ -509,20 +474,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         // only, so it runs ahead of griddepcontrol.wait
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
-            int it = 0;
+            int s = 0, lap = 0;  // ring stage and how many times the ring has wrapped
             for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
                 const int s_ = unit_seg(p, u);
                 const DevMatrix& m = p.seg[s_].m;
                 const int sbb = sb_bytes(m.type);
                 const int64_t tile0 = (int64_t)(u - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
-                for (int c = 0; c < p.nchunks; c++, it++) {
-                    const int s = it % S;
-                    if (it >= S && !mbar_wait_bounded(&empty[s], ((it / S) - 1) & 1, p.err)) return;
+                for (int c = 0; c < p.nchunks; c++) {
+                    if (lap > 0 && !mbar_wait_bounded(&empty[s], (lap - 1) & 1, p.err)) return;
                     const int cb = min(p.cbs, nsb - c * p.cbs);
                     const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
                     mbar_expect_tx(&full[s], bytes);
                     bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
                              &full[s], policy);
+                    if (++s == S) {
+                        s = 0;
+                        lap++;
+                    }
                 }
             }
         }
@@ -536,21 +504,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     pdl_launch_dependents();
     // the activation, prepared by act_quant_kernel in this region's layout: one bulk copy
     if (tid == 0) {
-        mbar_expect_tx(&actbar, (uint32_t)p.act_bytes);
-        bulk_g2s(smem, p.act_global, (uint32_t)p.act_bytes, &actbar, 0);
+        mbar_expect_tx(&actbar, (uint32_t)p.act.bytes);
+        bulk_g2s(smem, p.act_global, (uint32_t)p.act.bytes, &actbar, 0);
     }
     bool timed_out = !mbar_wait_bounded(&actbar, 0, p.err);
 
     Act a;
-    a.f32 = p.act_f32 >= 0 ? reinterpret_cast<const float*>(smem + p.act_f32) : nullptr;
-    a.q8k = p.act_q8k >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act_q8k) : nullptr;
-    a.q8k_d = p.act_q8k >= 0 ? reinterpret_cast<const float*>(smem + p.act_q8k_d) : nullptr;
-    a.q8k_bs = p.act_q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act_q8k_bs) : nullptr;
-    a.q8k_ps = p.act_q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act_q8k_ps) : nullptr;
-    a.q80 = p.act_q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act_q80) : nullptr;
-    a.q80_d = p.act_q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act_q80_d) : nullptr;
+    a.f32 = p.act.f32 >= 0 ? reinterpret_cast<const float*>(smem + p.act.f32) : nullptr;
+    a.q8k = p.act.q8k >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q8k) : nullptr;
+    a.q8k_d = p.act.q8k >= 0 ? reinterpret_cast<const float*>(smem + p.act.q8k_d) : nullptr;
+    a.q8k_bs = p.act.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act.q8k_bs) : nullptr;
+    a.q8k_ps = p.act.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act.q8k_ps) : nullptr;
+    a.q80 = p.act.q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q80) : nullptr;
+    a.q80_d = p.act.q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act.q80_d) : nullptr;
 
-    int it = 0;
+    int s = 0, lap = 0;  // ring stage and its phase parity source
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
         const UnitRow ur = unit_row(p, u, warp);
         const DevMatrix& m = p.seg[ur.seg < 0 ? unit_seg(p, u) : ur.seg].m;
@@ -563,9 +531,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
         }
         float acc = 0.f;
-        for (int c = 0; c < p.nchunks; c++, it++) {
-            const int s = it % S;
-            if (!timed_out && !mbar_wait_bounded(&full[s], (it / S) & 1, p.err)) timed_out = true;
+        for (int c = 0; c < p.nchunks; c++) {
+            if (!timed_out && !mbar_wait_bounded(&full[s], lap & 1, p.err)) timed_out = true;
             if (!timed_out && ur.seg >= 0) {
                 const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
                 const uint8_t* stage = ring + s * p.stage_bytes;
@@ -588,6 +555,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == S) {
+                s = 0;
+                lap++;
+            }
         }
         if (EPI == EPI_DOTS) continue;
         const float y = warp_sum(acc);
@@ -642,14 +613,15 @@ void gemv_prepare(GemvParams& p, int sm_count) {
         off += (bytes + 15) / 16 * 16;
         return o;
     };
-    p.act_f32 = need_f32 ? take(K * 4) : -1;
-    p.act_q8k = need_q8k ? take(K) : -1;
-    p.act_q8k_d = need_q8k ? take(K / QK_K * 4) : -1;
-    p.act_q8k_bs = need_q8k ? take(K / 16 * 2) : -1;
-    p.act_q8k_ps = need_q8k ? take(K / 32 * 2) : -1;
-    p.act_q80 = need_q80 ? take(K) : -1;
-    p.act_q80_d = need_q80 ? take(K / QK8_0 * 4) : -1;
-    p.act_bytes = (off + 127) / 128 * 128;
+    p.act.f32 = need_f32 ? take(K * 4) : -1;
+    p.act.q8k = need_q8k ? take(K) : -1;
+    p.act.q8k_d = need_q8k ? take(K / QK_K * 4) : -1;
+    p.act.q8k_bs = need_q8k ? take(K / 16 * 2) : -1;
+    p.act.q8k_ps = need_q8k ? take(K / 32 * 2) : -1;
+    p.act.q80 = need_q80 ? take(K) : -1;
+    p.act.q80_d = need_q80 ? take(K / QK8_0 * 4) : -1;
+    p.act.bytes = (off + 127) / 128 * 128;
+    p.act.cbs = p.seg[0].m.cbs;
 
     p.cbs = p.seg[0].m.cbs;
     p.nchunks = (K / QK_K + p.cbs - 1) / p.cbs;
@@ -660,7 +632,7 @@ void gemv_prepare(GemvParams& p, int sm_count) {
         ub += p.seg[s].m.Npad / kTileRows;
     }
     p.units = ub;
-    const int ring = kRingBudget - p.act_bytes;
+    const int ring = kRingBudget - p.act.bytes;
     const int S = std::max(2, std::min(kGemvMaxStages, ring / p.stage_bytes));
     // two persistent CTAs per SM: 16 consumer warps and two producers hide shared-memory
     // and copy latency better than one
@@ -669,7 +641,7 @@ void gemv_prepare(GemvParams& p, int sm_count) {
     p.stages = std::max(1, std::min(S, needed));
 }
 
-size_t gemv_smem(const GemvParams& p) { return (size_t)p.act_bytes + (size_t)p.stages * p.stage_bytes; }
+size_t gemv_smem(const GemvParams& p) { return (size_t)p.act.bytes + (size_t)p.stages * p.stage_bytes; }
 
 template <int EPI>
 static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
@@ -688,7 +660,7 @@ static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
 
 cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl) {
     if (p.stages < 1 || p.stages > kGemvMaxStages || p.grid < 1 || !p.act_global) return cudaErrorInvalidValue;
-    {
+    if (!p.act_prepared) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((p.K / QK_K + kActWarps - 1) / kActWarps);
         cfg.blockDim = dim3(kActWarps * 32);

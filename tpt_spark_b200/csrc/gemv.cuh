@@ -103,6 +103,28 @@ enum GemvEpi : int {
     EPI_DOTS = 4,   // integer block sums (test hook)
 };
 
+// Layout of a prepared GEMV activation (the GEMV's shared-memory region, and the global
+// buffer it is bulk-copied from): byte offsets of each part, -1 when absent.
+//   f32           [K] f32                    (F16 weights)
+//   q8k           [K] int8 Q8_K quants       (Q4_K / Q6_K weights), lane-transposed per chunk
+//                 (xt_offset) for the forward kernels, natural order for the DOTS test hook
+//   q8k_d / _bs / _ps  per 256-block scale, 16-element sums [K/16], 32-element sums [K/32]
+//   q80 / q80_d   [K] int8 Q8_0 quants, per 32-block scale (f16-rounded, f32)
+struct ActLayout {
+    int f32, q8k, q8k_d, q8k_bs, q8k_ps, q80, q80_d;
+    int bytes;  // total, a multiple of 128
+    int cbs;    // super-blocks per weight chunk (the transposition period)
+};
+
+// Byte offset of the 8 Q8_K quants of lane `lane` (elements 8*lane .. +7) of 256-block b in
+// the lane-transposed layout: per chunk of cbs blocks, 16-byte vector v of half block h
+// (= 2 * block-in-chunk + half) sits at (v * nh + h) * 16, nh = 2 * blocks in the chunk.
+__host__ __device__ __forceinline__ int xt_offset(int b, int lane, int nsb, int cbs) {
+    const int c = b / cbs, j = b - c * cbs, cbc = (nsb - c * cbs) < cbs ? (nsb - c * cbs) : cbs, nh = 2 * cbc;
+    const int h = lane >> 4, v = (lane & 15) >> 1;
+    return c * cbs * 256 + (v * nh + 2 * j + h) * 16 + (lane & 1) * 8;
+}
+
 constexpr int kGemvMaxSeg = 3;
 constexpr int kGemvMaxStages = 16;
 
@@ -139,11 +161,13 @@ struct GemvParams {
     int stages;       // ring depth
     int stage_bytes;  // bytes per stage (one full tile)
     int grid;         // CTAs (persistent: units are strided over them)
-    int act_f32, act_q8k, act_q8k_d, act_q8k_bs, act_q8k_ps, act_q80, act_q80_d;  // smem offsets, -1 absent
-    int act_bytes;
-    // Device buffer of act_bytes (16-byte aligned) receiving the prepared activation in the
-    // shared-memory layout; written by the quantisation kernel, bulk-copied by every CTA.
+    ActLayout act;  // the activation region at the start of shared memory
+    // Device buffer of act.bytes (16-byte aligned) receiving the prepared activation in the
+    // shared-memory layout, bulk-copied by every CTA.  act_prepared = 0: gemv_launch first
+    // runs the activation kernel on x; 1: the previous kernel already wrote it (for example
+    // the attention kernel for the o projection) and x is not read.
     uint8_t* act_global;
+    int act_prepared;
     int* err;
 };
 

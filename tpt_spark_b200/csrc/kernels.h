@@ -41,6 +41,11 @@ struct AttnDecodeParams {
     int stages;            // filled by launch_attn_decode
     float scale;           // 1/sqrt(hd)
     int* err;
+    // optional: the output also written as the next GEMV's prepared activation (gemv.cuh
+    // ActLayout, act_nb 256-blocks over all heads); requires (n_heads / n_kv) * hd % 256 == 0
+    uint8_t* act_out;
+    ActLayout act;
+    int act_transposed, act_nb;
 };
 int attn_decode_splits(int n_kv, int max_seq, int sm_count);
 size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits);
