@@ -99,6 +99,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return false;
 }
 
+// Bounded wait that yields the issue slot between polls (nanosleep): for a warp whose wait
+// is not on the critical path (a producer waiting for a free ring slot), so that it does not
+// take issue cycles from the warps doing the arithmetic.  Gives up after kWaitPolls polls
+// (at least 4 s of sleep), like mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(64);
+    }
+    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
+    return false;
+}
+
 // 1-D bulk copy global -> shared (TMA engine, no tensor map), completion on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,

@@ -53,6 +53,16 @@ __device__ __forceinline__ int unit_seg(const GemvParams& p, int u) {
     return s;
 }
 
+// Whether units u and u + grid are reduced together (sharing the activation slice): both
+// exist, same Q4_K / Q6_K weights, and the ring holds the pair plus at least one stage to
+// refill meanwhile.  Producer and consumers take the same decision.
+__device__ __forceinline__ bool unit_pair(const GemvParams& p, int u, int epi) {
+    const int u2 = u + gridDim.x;
+    if (epi == EPI_DOTS || u2 >= p.units || p.stages < 3) return false;
+    const int t = p.seg[unit_seg(p, u)].m.type;
+    return t == p.seg[unit_seg(p, u2)].m.type && (t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q6_K);
+}
+
 __device__ __forceinline__ UnitRow unit_row(const GemvParams& p, int u, int r) {
     UnitRow ur;
     const int s = unit_seg(p, u);
@@ -102,18 +112,32 @@ __device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 
 // whole block's integer sum only by float rounding.  The DOTS test hook keeps the exact
 // per-block integers (chunk_q4k / chunk_q6k below, natural activation layout).
 
-__device__ __forceinline__ float q4k_half(const uint8_t* slot, const Act& a, int c0, int nh, int lane) {
+// The lane's slice of a chunk's Q8_K activation (half super-block `lane`): 8 transposed
+// 16-byte vectors of quants, the super-block scale, and 32- (Q4_K) or 16-element (Q6_K) sums.
+struct XHalf {
+    int4 x[8];
+    float dx;
+    uint2 ps;   // pair sums of sub-blocks 4h .. 4h+3 (Q4_K)
+    uint4 bs;   // bsums of the 8 16-element groups (Q6_K)
+};
+
+template <bool Q6>
+__device__ __forceinline__ void load_xhalf(XHalf& xh, const Act& a, int c0, int nh, int lane) {
+    const int sb = lane >> 1, h = lane & 1;
+    const int4* xv = reinterpret_cast<const int4*>(a.q8k + c0 * QK_K) + lane;
+#pragma unroll
+    for (int v = 0; v < 8; v++) xh.x[v] = xv[v * nh];
+    xh.dx = a.q8k_d[c0 + sb];
+    if (Q6) xh.bs = *reinterpret_cast<const uint4*>(a.q8k_bs + (c0 + sb) * 16 + 8 * h);
+    else xh.ps = *reinterpret_cast<const uint2*>(a.q8k_ps + (c0 + sb) * 8 + 4 * h);
+}
+
+__device__ __forceinline__ float q4k_half(const uint8_t* slot, const XHalf& xh, int lane) {
     const int sb = lane >> 1, h = lane & 1;
     const uint8_t* blk = slot + sb * Q4K_BYTES;
     const uint4 hd = *reinterpret_cast<const uint4*>(blk);  // d, dmin | scales[0..3] | [4..7] | [8..11]
     const uint4* wq = reinterpret_cast<const uint4*>(blk + 16 + 64 * h);
     const uint4 w0 = wq[0], w1 = wq[1], w2 = wq[2], w3 = wq[3];
-    const int4* xv = reinterpret_cast<const int4*>(a.q8k + c0 * QK_K) + lane;
-    int4 x[8];
-#pragma unroll
-    for (int v = 0; v < 8; v++) x[v] = xv[v * nh];
-    const uint2 pp = *reinterpret_cast<const uint2*>(a.q8k_ps + (c0 + sb) * 8 + 4 * h);
-    const float dx = a.q8k_d[c0 + sb];
     // sub-blocks 4h, 4h+1 are the low / high nibbles of qs[64h .. +32), 4h+2, 4h+3 of
     // qs[64h+32 .. +32); high nibbles are dotted in place (16x) and shifted back
     const uint32_t lo = 0x0f0f0f0fu, hi = 0xf0f0f0f0u;
@@ -124,10 +148,10 @@ __device__ __forceinline__ float q4k_half(const uint8_t* slot, const Act& a, int
     SL = dp4a_us(W.y & lo, XL.y, SL); SH = dp4a_us(W.y & hi, XH.y, SH);  \
     SL = dp4a_us(W.z & lo, XL.z, SL); SH = dp4a_us(W.z & hi, XH.z, SH);  \
     SL = dp4a_us(W.w & lo, XL.w, SL); SH = dp4a_us(W.w & hi, XH.w, SH);
-    Q4_VEC(w0, x[0], x[2], s0, s1)
-    Q4_VEC(w1, x[1], x[3], s0, s1)
-    Q4_VEC(w2, x[4], x[6], s2, s3)
-    Q4_VEC(w3, x[5], x[7], s2, s3)
+    Q4_VEC(w0, xh.x[0], xh.x[2], s0, s1)
+    Q4_VEC(w1, xh.x[1], xh.x[3], s0, s1)
+    Q4_VEC(w2, xh.x[4], xh.x[6], s2, s3)
+    Q4_VEC(w3, xh.x[5], xh.x[7], s2, s3)
 #undef Q4_VEC
     s1 >>= 4;
     s3 >>= 4;
@@ -135,15 +159,14 @@ __device__ __forceinline__ float q4k_half(const uint8_t* slot, const Act& a, int
     const uint32_t sc = h == 0 ? hd.y & k6 : (hd.w & k4) | (((hd.y >> 6) & k2) << 4);
     const uint32_t mn = h == 0 ? hd.z & k6 : ((hd.w >> 4) & k4) | (((hd.z >> 6) & k2) << 4);
     const int isum = ubyte(sc, 0) * s0 + ubyte(sc, 1) * s1 + ubyte(sc, 2) * s2 + ubyte(sc, 3) * s3;
-    const int msum = ubyte(mn, 0) * (int)(int16_t)(pp.x & 0xffff) + ubyte(mn, 1) * (int)(int16_t)(pp.x >> 16) +
-                     ubyte(mn, 2) * (int)(int16_t)(pp.y & 0xffff) + ubyte(mn, 3) * (int)(int16_t)(pp.y >> 16);
-    const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))), dx);
-    const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))), dx);
+    const int msum = ubyte(mn, 0) * (int)(int16_t)(xh.ps.x & 0xffff) + ubyte(mn, 1) * (int)(int16_t)(xh.ps.x >> 16) +
+                     ubyte(mn, 2) * (int)(int16_t)(xh.ps.y & 0xffff) + ubyte(mn, 3) * (int)(int16_t)(xh.ps.y >> 16);
+    const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))), xh.dx);
+    const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))), xh.dx);
     return dd * (float)isum - dm * (float)msum;
 }
 
-__device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int nh,
-                                          int lane) {
+__device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* dsec, const XHalf& xh, int lane) {
     const int sb = lane >> 1, h = lane & 1;
     const uint8_t* m = slot + sb * Q6K_MAIN;
     const uint4* qa = reinterpret_cast<const uint4*>(m + 64 * h);        // ql[64h .. +32)
@@ -151,12 +174,6 @@ __device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* d
     const uint4* qh = reinterpret_cast<const uint4*>(m + 128 + 32 * h);  // qh[32h .. +32)
     const uint4 A0 = qa[0], A1 = qa[1], B0 = qb[0], B1 = qb[1], H0 = qh[0], H1 = qh[1];
     const uint2 scw = *reinterpret_cast<const uint2*>(m + 192 + 8 * h);  // int8 scales sc[8h .. +8)
-    const int4* xv = reinterpret_cast<const int4*>(a.q8k + c0 * QK_K) + lane;
-    int4 x[8];
-#pragma unroll
-    for (int v = 0; v < 8; v++) x[v] = xv[v * nh];
-    const uint4 bsw = *reinterpret_cast<const uint4*>(a.q8k_bs + (c0 + sb) * 16 + 8 * h);
-    const float dx = a.q8k_d[c0 + sb];
     const float dw = h2f(dsec[sb]);
     // word k of ql/qh holds positions l = 4k..4k+3 of the four 32-element groups
     // (elements 128h + l, +32, +64, +96; sub-blocks 2*group + k/4)
@@ -167,24 +184,24 @@ __device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* d
     t[T0 + 2] = dp4a_us(((Bw) & m4) | (((Hw) << 2) & m2), X2, t[T0 + 2]);              \
     t[T0 + 4] = dp4a_us((((Aw) >> 4) & m4) | ((Hw) & m2), X3, t[T0 + 4]);              \
     t[T0 + 6] = dp4a_us((((Bw) >> 4) & m4) | (((Hw) >> 2) & m2), X4, t[T0 + 6]);
-    Q6_WORD(A0.x, B0.x, H0.x, x[0].x, x[2].x, x[4].x, x[6].x, 0)
-    Q6_WORD(A0.y, B0.y, H0.y, x[0].y, x[2].y, x[4].y, x[6].y, 0)
-    Q6_WORD(A0.z, B0.z, H0.z, x[0].z, x[2].z, x[4].z, x[6].z, 0)
-    Q6_WORD(A0.w, B0.w, H0.w, x[0].w, x[2].w, x[4].w, x[6].w, 0)
-    Q6_WORD(A1.x, B1.x, H1.x, x[1].x, x[3].x, x[5].x, x[7].x, 1)
-    Q6_WORD(A1.y, B1.y, H1.y, x[1].y, x[3].y, x[5].y, x[7].y, 1)
-    Q6_WORD(A1.z, B1.z, H1.z, x[1].z, x[3].z, x[5].z, x[7].z, 1)
-    Q6_WORD(A1.w, B1.w, H1.w, x[1].w, x[3].w, x[5].w, x[7].w, 1)
+    Q6_WORD(A0.x, B0.x, H0.x, xh.x[0].x, xh.x[2].x, xh.x[4].x, xh.x[6].x, 0)
+    Q6_WORD(A0.y, B0.y, H0.y, xh.x[0].y, xh.x[2].y, xh.x[4].y, xh.x[6].y, 0)
+    Q6_WORD(A0.z, B0.z, H0.z, xh.x[0].z, xh.x[2].z, xh.x[4].z, xh.x[6].z, 0)
+    Q6_WORD(A0.w, B0.w, H0.w, xh.x[0].w, xh.x[2].w, xh.x[4].w, xh.x[6].w, 0)
+    Q6_WORD(A1.x, B1.x, H1.x, xh.x[1].x, xh.x[3].x, xh.x[5].x, xh.x[7].x, 1)
+    Q6_WORD(A1.y, B1.y, H1.y, xh.x[1].y, xh.x[3].y, xh.x[5].y, xh.x[7].y, 1)
+    Q6_WORD(A1.z, B1.z, H1.z, xh.x[1].z, xh.x[3].z, xh.x[5].z, xh.x[7].z, 1)
+    Q6_WORD(A1.w, B1.w, H1.w, xh.x[1].w, xh.x[3].w, xh.x[5].w, xh.x[7].w, 1)
 #undef Q6_WORD
     // q is stored +32: sum (q-32)*x = sum q*x - 32 * bsum over each 16 elements
-    const uint32_t bw[4] = {bsw.x, bsw.y, bsw.z, bsw.w};
+    const uint32_t bw[4] = {xh.bs.x, xh.bs.y, xh.bs.z, xh.bs.w};
     int isum = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int bs = (int)(int16_t)((bw[i >> 1] >> (16 * (i & 1))) & 0xffff);
         isum += sbyte(i < 4 ? scw.x : scw.y, i & 3) * (t[i] - 32 * bs);
     }
-    return __fmul_rn(dw, dx) * (float)isum;
+    return __fmul_rn(dw, xh.dx) * (float)isum;
 }
 
 template <bool DOTS>
@@ -475,23 +492,30 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
             int s = 0, lap = 0;  // ring stage and how many times the ring has wrapped
-            for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
-                const int s_ = unit_seg(p, u);
-                const DevMatrix& m = p.seg[s_].m;
-                const int sbb = sb_bytes(m.type);
-                const int64_t tile0 = (int64_t)(u - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
-                for (int c = 0; c < p.nchunks; c++) {
-                    if (lap > 0 && !mbar_wait_bounded(&empty[s], (lap - 1) & 1, p.err)) return;
-                    const int cb = min(p.cbs, nsb - c * p.cbs);
-                    const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
-                    mbar_expect_tx(&full[s], bytes);
-                    bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
-                             &full[s], policy);
-                    if (++s == S) {
-                        s = 0;
-                        lap++;
+            // units in pairs (u, u + grid), chunk by chunk: the order the consumers take them
+            for (int u = blockIdx.x; u < p.units;) {
+                const bool two = unit_pair(p, u, EPI);
+                // a pair goes chunk by chunk alternating its two units; a single unit alone
+                for (int i = 0; i < (two ? 2 : 1) * p.nchunks; i++) {
+                    const int c = two ? i >> 1 : i, k = two ? i & 1 : 0;
+                    {
+                        const int uk = u + k * gridDim.x, s_ = unit_seg(p, uk);
+                        const DevMatrix& m = p.seg[s_].m;
+                        const int sbb = sb_bytes(m.type);
+                        const int64_t tile0 = (int64_t)(uk - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
+                        if (lap > 0 && !mbar_wait_backoff(&empty[s], (lap - 1) & 1, p.err)) return;
+                        const int cb = min(p.cbs, nsb - c * p.cbs);
+                        const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
+                        mbar_expect_tx(&full[s], bytes);
+                        bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
+                                 &full[s], policy);
+                        if (++s == S) {
+                            s = 0;
+                            lap++;
+                        }
                     }
                 }
+                u += (two ? 2 : 1) * gridDim.x;
             }
         }
         return;
@@ -518,49 +542,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     a.q80 = p.act.q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q80) : nullptr;
     a.q80_d = p.act.q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act.q80_d) : nullptr;
 
+    // Units in pairs (u, u + grid): for every chunk the producer fills the pair's two stages
+    // back to back, and a warp reduces its row of both in one pass; with the same weight type
+    // the two dot products share the lane's activation slice (same columns).
     int s = 0, lap = 0;  // ring stage and its phase parity source
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
-        const UnitRow ur = unit_row(p, u, warp);
-        const DevMatrix& m = p.seg[ur.seg < 0 ? unit_seg(p, u) : ur.seg].m;
-        const int sbm = sb_main_bytes(m.type), sbd = sb_d_bytes(m.type);
-        int32_t* isum_row = nullptr;
-        int32_t* msum_row = nullptr;
-        if (EPI == EPI_DOTS && ur.seg >= 0) {
-            const int per_row = m.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
-            isum_row = p.isum + (int64_t)ur.row * per_row;
-            msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
-        }
-        float acc = 0.f;
-        for (int c = 0; c < p.nchunks; c++) {
-            if (!timed_out && !mbar_wait_bounded(&full[s], lap & 1, p.err)) timed_out = true;
-            if (!timed_out && ur.seg >= 0) {
-                const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
-                const uint8_t* stage = ring + s * p.stage_bytes;
-                const uint8_t* slot = stage + warp * cb * sbm;
-                const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
-                switch (m.type) {
-                case TPTC_TYPE_Q4_K:
-                    if (EPI == EPI_DOTS) chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
-                    else if (lane < 2 * cb) acc += q4k_half(slot, a, c0, 2 * cb, lane);
-                    break;
-                case TPTC_TYPE_Q6_K:
-                    if (EPI == EPI_DOTS) chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
-                    else if (lane < 2 * cb) acc += q6k_half(slot, dsec, a, c0, 2 * cb, lane);
-                    break;
-                case TPTC_TYPE_Q8_0:
-                    acc += chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
-                    break;
-                default: acc += chunk_f16(slot, a, c0, cb, lane, 0, 32); break;
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == S) {
-                s = 0;
-                lap++;
-            }
-        }
-        if (EPI == EPI_DOTS) continue;
+    auto epilogue = [&](const UnitRow& ur, float acc) {
+        if (EPI == EPI_DOTS) return;
         const float y = warp_sum(acc);
         if (EPI == EPI_GLU) {
             // tile rows 0-3 are gate rows, 4-7 the matching up rows: the up warp hands its
@@ -572,9 +559,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             if (warp < 4 && lane == 0 && ur.seg >= 0)
                 p.out[ur.out] = __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
             unit_no++;
-            continue;
+            return;
         }
-        if (lane != 0 || ur.seg < 0) continue;
+        if (lane != 0 || ur.seg < 0) return;
         if (EPI == EPI_STORE) {
             p.out[ur.row] = y;
         } else if (EPI == EPI_RESID) {
@@ -591,6 +578,102 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                 else static_cast<__half*>(p.vcache)[at] = __float2half_rn(y);
             }
         }
+    };
+    // one row chunk of one unit on its own (DOTS test hook, mixed types, Q8_0, F16)
+    auto single = [&](const DevMatrix& m, const UnitRow& ur, const uint8_t* stage, int c0, int cb) -> float {
+        if (ur.seg < 0) return 0.f;
+        const int sbm = sb_main_bytes(m.type), sbd = sb_d_bytes(m.type);
+        const uint8_t* slot = stage + warp * cb * sbm;
+        const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
+        int32_t* isum_row = nullptr;
+        int32_t* msum_row = nullptr;
+        if (EPI == EPI_DOTS) {
+            const int per_row = m.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
+            isum_row = p.isum + (int64_t)ur.row * per_row;
+            msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
+        }
+        switch (m.type) {
+        case TPTC_TYPE_Q4_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                return q4k_half(slot, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q6_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                return q6k_half(slot, dsec, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
+        default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
+        }
+    };
+    for (int u = blockIdx.x; u < p.units;) {
+        const int u2 = u + gridDim.x;
+        const bool two = unit_pair(p, u, EPI);
+        const UnitRow ra = unit_row(p, u, warp);
+        const UnitRow rb = unit_row(p, two ? u2 : u, warp);
+        const DevMatrix& ma = p.seg[unit_seg(p, u)].m;
+        const DevMatrix& mb = p.seg[unit_seg(p, two ? u2 : u)].m;
+        const int ty = ma.type;
+        const bool paired = two;
+        float acca = 0.f, accb = 0.f;
+        for (int c = 0; c < p.nchunks; c++) {
+            const int sa = s;
+            if (!timed_out && !mbar_wait_bounded(&full[sa], lap & 1, p.err)) timed_out = true;
+            if (++s == S) {
+                s = 0;
+                lap++;
+            }
+            int sb2 = sa;
+            if (two) {
+                sb2 = s;
+                if (!timed_out && !mbar_wait_bounded(&full[sb2], lap & 1, p.err)) timed_out = true;
+                if (++s == S) {
+                    s = 0;
+                    lap++;
+                }
+            }
+            if (!timed_out) {
+                const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
+                const uint8_t* stA = ring + sa * p.stage_bytes;
+                const uint8_t* stB = ring + sb2 * p.stage_bytes;
+                if (paired) {
+                    if (lane < 2 * cb) {
+                        const int sbm = sb_main_bytes(ty), sbd = sb_d_bytes(ty);
+                        XHalf xh;
+                        if (ty == TPTC_TYPE_Q4_K) {
+                            load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                            acca += q4k_half(stA + warp * cb * sbm, xh, lane);
+                            accb += q4k_half(stB + warp * cb * sbm, xh, lane);
+                        } else {
+                            load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                            const int doff = kTileRows * cb * sbm + warp * cb * sbd;
+                            acca += q6k_half(stA + warp * cb * sbm, reinterpret_cast<const uint16_t*>(stA + doff), xh, lane);
+                            accb += q6k_half(stB + warp * cb * sbm, reinterpret_cast<const uint16_t*>(stB + doff), xh, lane);
+                        }
+                    }
+                } else {
+                    acca += single(ma, ra, stA, c0, cb);
+                    if (two) accb += single(mb, rb, stB, c0, cb);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[sa]);
+                if (two) mbar_arrive(&empty[sb2]);
+            }
+        }
+        epilogue(ra, acca);
+        if (two) epilogue(rb, accb);
+        u += (two ? 2 : 1) * gridDim.x;
     }
 }
 
