@@ -190,6 +190,11 @@ TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void*
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,
                              void* stream);
 
+/* Prefill GEMM on the tensor cores: C[M x N] (f32, row-major) = A[M x K] . B[N x K]^T with A
+ * and B row-major fp16 (16-byte aligned), K a multiple of 64 -- the prompt-wide replacement of
+ * gemm.wgsl's per-token M = 1 products. */
+TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream);
+
 /* GQA attention of one query position, the decode step of attention.wgsl's three passes
  * (scores :31-58, softmax :73-135, P.V :152-170; dispatched from wgpu_engine.rs:666-726).
  *   d_q [n_heads * head_dim], d_kraw [n_kv * head_dim]: q and this position's key before RoPE;

@@ -70,6 +70,7 @@ SIGNATURES = {
     "tptc_matrix_bytes": (c_i64, [c_vp]),
     "tptc_gemv": (c_int, [c_vp, c_vp, c_vp, c_vp]),
     "tptc_block_dots": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "tptc_gemm_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
     "tptc_attn_decode_workspace_bytes": (c_i64, [c_int, c_int, c_int, c_int]),
     "tptc_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp,
                                  c_vp, c_i64, c_vp]),

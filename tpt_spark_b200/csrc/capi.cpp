@@ -9,6 +9,7 @@
 
 #include "engine.h"
 #include "kernels.h"
+#include "prefill.h"
 #include "tp.h"
 #include "tptc.h"
 
@@ -426,6 +427,23 @@ TPTC_API int tptc_attn_decode_noalloc(const float* d_q, const float* d_kraw, voi
     if (e != cudaSuccess) return cuda_fail(e, "attention (no-alloc) scratch set-up");
     return attn_launch(d_q, d_kraw, d_kcache, d_vcache, kv_type, d_rope_cos, d_rope_sin, d_pos, d_out, n_heads, n_kv,
                        head_dim, max_seq, ws, L, st);
+}
+
+TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream) {
+    if (!d_a || !d_b || !d_c || M <= 0 || N <= 0 || K <= 0) return fail_code(nullptr, TPTC_ERR_ARG, "gemm: bad argument");
+    if (K % 64 || (reinterpret_cast<uintptr_t>(d_a) & 15) || (reinterpret_cast<uintptr_t>(d_b) & 15))
+        return fail_code(nullptr, TPTC_ERR_ARG, "gemm: K must be a multiple of 64 and A, B 16-byte aligned");
+    int dev = 0, sms = 0;
+    if (int rc = ensure_kernels(&dev, &sms)) return rc;
+    tptc::GemmTcParams p = {};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.c = d_c;
+    p.ldc = N;
+    cudaError_t e = tptc::gemm_tc(tptc::GEMM_STORE, static_cast<const __half*>(d_a), K, static_cast<const __half*>(d_b),
+                                  K, p, static_cast<cudaStream_t>(stream), false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemm_tc");
 }
 
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum, void* stream) {

@@ -1,0 +1,276 @@
+// gemm_tc.cu -- prefill GEMM on the 5th-generation tensor cores: C[M x N] = A[M x K] . B[N x K]^T
+// with A the prompt's activations (fp16, one row per token) and B a weight matrix (fp16,
+// dequantised from its GGUF blocks), f32 accumulation in tensor memory.
+//
+// Replaces the per-token matmuls of the reference's prefill loop (wgpu_engine.rs:254-261,
+// gemm.wgsl with M = 1 once per token) for a whole prompt.
+//
+// One CTA computes a 128 x 128 tile of C:
+//   - warp 0 (one lane): TMA producer.  Both operands are 2-D tensor maps with 128-byte
+//     swizzle; each pipeline stage is a 128 x 64 tile of A and of B (16 KB each, K-major,
+//     exactly the canonical SWIZZLE_128B operand layout of tcgen05.mma), completion counted
+//     on the stage's "full" mbarrier;
+//   - warp 1: allocates 128 TMEM columns; one lane issues tcgen05.mma (M = 128, N = 128,
+//     K = 16: four per stage, the descriptor start address advancing 32 bytes within the
+//     swizzle atom) and commits each stage to its "empty" mbarrier, so the producer refills it
+//     as soon as the tensor core has read it; the last commit signals the accumulator;
+//   - warps 2-5: epilogue.  Warp w reads TMEM lanes 32 (w % 4) .. +31 (= rows of the tile)
+//     with tcgen05.ld, 32 columns at a time, and writes C (f32 store, residual add, or the
+//     fused gate|up SiLU product in fp16).
+// Every mbarrier wait is bounded (error flag, then the CTA still frees its TMEM and exits).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "prefill.h"
+
+namespace tptc {
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 64, kStages = 4;
+constexpr int kTileBytes = BM * BK * 2;  // one operand tile of a stage (A and B alike)
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 128;
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile with 128-byte swizzle: rows of
+// 128 bytes, 8-row atoms of 1024 bytes (stride byte offset), tile 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);   // start address
+    d |= (uint64_t)1 << 16;                   // leading byte offset (unused with swizzle)
+    d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
+    d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                   // layout: SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: f16 x f16 -> f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t mma_idesc(int M, int N) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns of TMEM: thread t receives lane (base lane + t).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                   const __grid_constant__ GemmTcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kStages], empty[kStages], accum;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int timed_out;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, nk = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&accum, 1);
+        fence_mbar_init();
+        timed_out = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1, p.err)) {
+                    timed_out = 1;
+                    break;
+                }
+                uint8_t* st = smem + s * 2 * kTileBytes;
+                mbar_expect_tx(&full[s], 2 * kTileBytes);
+                tma_load_2d(st, &ta, kb * BK, m0, &full[s]);
+                tma_load_2d(st + kTileBytes, &tb, kb * BK, n0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            const uint32_t idesc = mma_idesc(BM, BN);
+            bool ok = true;
+            for (int kb = 0; kb < nk && ok; kb++) {
+                const int s = kb % kStages;
+                if (!mbar_wait_bounded(&full[s], (kb / kStages) & 1, p.err)) {
+                    ok = false;
+                    timed_out = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(smem + s * 2 * kTileBytes), b = a + kTileBytes;
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++)
+                    mma_f16(tmem, sw128_desc(a + 32 * k), sw128_desc(b + 32 * k), idesc, (kb | k) != 0);
+                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+            }
+            mma_commit(&accum);  // accumulator complete (also after a timeout: no MMA pending)
+        }
+    } else {  // epilogue warps 2..5
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const bool ok = mbar_wait_bounded(&accum, 0, p.err);
+        tc_fence_after();
+        const int row = m0 + 32 * q + lane;
+        if (ok && !timed_out) {
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
+                if (row >= p.M || n0 + c0 >= p.N) continue;
+                const int col = n0 + c0;
+                if (EPI == GEMM_STORE || EPI == GEMM_RESID) {
+                    float* c = p.c + (size_t)row * p.ldc + col;
+                    const int nv = min(32, p.N - col);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        if (j < nv) {
+                            const float v = __uint_as_float(r[j]);
+                            if (EPI == GEMM_RESID) c[j] += v;
+                            else c[j] = v;
+                        }
+                    }
+                } else {  // GEMM_GLU: columns 8t..8t+3 gate, 8t+4..8t+7 up of outputs 4t..4t+3
+                    __half* h = p.h + (size_t)row * p.ldh + col / 2;
+#pragma unroll
+                    for (int t = 0; t < 4; t++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            if (col + 8 * t + 4 + i < p.N) {
+                                const float g = __uint_as_float(r[8 * t + i]), u = __uint_as_float(r[8 * t + 4 + i]);
+                                h[4 * t + i] = __float2half_rn(__fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u));
+                            }
+                        }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+
+cudaError_t get_encode() {
+    std::lock_guard<std::mutex> lk(g_encode_mu);
+    if (g_encode) return cudaSuccess;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return cudaSuccess;
+}
+
+// Row-major fp16 matrix [rows x cols] (leading dimension ld elements) as a 2-D tensor map with
+// a 64 x 128 box and 128-byte swizzle.
+cudaError_t make_map(CUtensorMap* map, const __half* ptr, int rows, int cols, int ld) {
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+constexpr size_t kSmem = (size_t)kStages * 2 * kTileBytes + 1024;
+
+}  // namespace
+
+cudaError_t gemm_tc_init_device() {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GEMM_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem)))
+        return e;
+    if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GEMM_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem)))
+        return e;
+    return cudaFuncSetAttribute(gemm_tc_kernel<GEMM_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+}
+
+cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb, const GemmTcParams& p_in,
+                    cudaStream_t st, bool pdl) {
+    if (p_in.M <= 0 || p_in.N <= 0 || p_in.K <= 0 || p_in.K % BK || lda % 8 || ldb % 8 ||
+        (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
+        return cudaErrorInvalidValue;
+    if (epi == GEMM_GLU && p_in.N % 8) return cudaErrorInvalidValue;
+    CUtensorMap ma, mb;
+    cudaError_t e = make_map(&ma, a, p_in.M, p_in.K, lda);
+    if (e == cudaSuccess) e = make_map(&mb, b, p_in.N, p_in.K, ldb);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p_in.N + BN - 1) / BN, (p_in.M + BM - 1) / BM);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    switch (epi) {
+    case GEMM_STORE: return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<GEMM_STORE>, ma, mb, p_in);
+    case GEMM_RESID: return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<GEMM_RESID>, ma, mb, p_in);
+    case GEMM_GLU: return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<GEMM_GLU>, ma, mb, p_in);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace tptc

@@ -6,7 +6,7 @@
 
 namespace tptc {
 
-cudaError_t prefill_init_device() { return cudaSuccess; }
+cudaError_t prefill_init_device() { return gemm_tc_init_device(); }
 
 // Prompt positions one at a time through the decode graph (the reference's prefill loop,
 // wgpu_engine.rs:254-261); the last step's logits are returned.

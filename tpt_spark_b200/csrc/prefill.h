@@ -4,8 +4,30 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "common.cuh"
+
 namespace tptc {
 
 cudaError_t prefill_init_device();
+
+// ---- tensor-core GEMM (gemm_tc.cu): C[M x N] = A[M x K] . B[N x K]^T, fp16 in, f32 accumulate
+enum GemmEpi : int {
+    GEMM_STORE = 0,  // c[m][n] = acc (f32)
+    GEMM_RESID = 1,  // c[m][n] += acc (f32 residual stream)
+    GEMM_GLU = 2,    // B rows in gate|up tile order (per 8 rows: 4 gate, 4 up): h[m][n/2 ...] =
+                     // silu(gate) * up as fp16
+};
+struct GemmTcParams {
+    int M, N, K;
+    float* c;  // GEMM_STORE / GEMM_RESID, leading dimension ldc
+    int ldc;
+    __half* h;  // GEMM_GLU, leading dimension ldh
+    int ldh;
+    int* err;  // bounded waits that give up set TPTC_ERR_TIMEOUT here
+};
+// A and B 16-byte aligned, lda / ldb multiples of 8 elements, K a multiple of 64.
+cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb, const GemmTcParams& p,
+                    cudaStream_t st, bool pdl);
+cudaError_t gemm_tc_init_device();
 
 }  // namespace tptc

@@ -82,3 +82,8 @@ def attn_decode_noalloc(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_co
     check(lib().tptc_attn_decode_noalloc(_ptr(d_q), _ptr(d_kraw), _ptr(d_kcache), _ptr(d_vcache), kv_type,
                                          _ptr(d_rope_cos), _ptr(d_rope_sin), _ptr(d_pos), n_heads, n_kv, head_dim,
                                          max_seq, _ptr(d_out), stream))
+
+
+def gemm_f16(d_a, d_b, d_c, M: int, N: int, K: int, stream: Optional[int] = None) -> None:
+    """C[M x N] (f32) = A[M x K] . B[N x K]^T on the tensor cores (fp16 row-major A and B)."""
+    check(lib().tptc_gemm_f16(_ptr(d_a), _ptr(d_b), _ptr(d_c), M, N, K, stream))
