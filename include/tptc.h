@@ -106,6 +106,14 @@ TPTC_API int tptc_device_count(void);
  * bytes per decode step) or TPTC_TYPE_F32 (the precision of the reference's candle path,
  * wgpu_kvcache.rs:37 also stores f32). */
 TPTC_API int tptc_set_kv_dtype(tptc_ctx* ctx, int ggml_type);
+/* Prefill path selection (no counterpart in the reference, which prefills token by token on
+ * the GPU, wgpu_engine.rs:252-261, and in one batched forward on the CPU,
+ * candle_engine.rs:272-281).  Prompts of at least min_tokens tokens run batched: dense fp16
+ * weights per layer on the tcgen05 GEMM and causal tensor-core attention, activations in fp16
+ * (logits within fp16 rounding of the integer-dot path).  Shorter prompts, every prompt when
+ * min_tokens <= 0, and every prompt with an f32 KV cache go token by token through the decode
+ * step (bit-identical to decoding them).  Default 16; may be changed at any time. */
+TPTC_API int tptc_set_prefill_gemm_min(tptc_ctx* ctx, int min_tokens);
 
 /* LlmEngine::load (mod.rs:66-70) -> load_gguf_to_vram (wgpu_loader.rs:87-201): mmap the
  * file, parse GGUF v3, check bounds, stream every tensor through pinned staging with
@@ -194,6 +202,17 @@ TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_
  * and B row-major fp16 (16-byte aligned), K a multiple of 64 -- the prompt-wide replacement of
  * gemm.wgsl's per-token M = 1 products. */
 TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream);
+
+/* Causal GQA attention of a prompt chunk on the tensor cores (the prefill replacement of
+ * attention.wgsl's per-token passes, :31-170, run once per prompt token by
+ * wgpu_engine.rs:254-261).  Query rows t = 0..T-1 sit at positions start + t and attend to
+ * cache positions 0 .. start + t (the chunk's own keys already in the cache); head h reads kv
+ * head h / (n_heads / n_kv); scale 1/sqrt(head_dim).  All fp16, device pointers:
+ *   d_q [T][n_heads][head_dim] (rotated), d_kcache / d_vcache [n_kv][max_seq][head_dim],
+ *   d_out [T][n_heads][head_dim].
+ * head_dim 64, 96 or 128; start + T <= max_seq. */
+TPTC_API int tptc_attn_prefill(const void* d_q, const void* d_kcache, const void* d_vcache, void* d_out, int T,
+                               int start, int n_heads, int n_kv, int head_dim, int max_seq, void* stream);
 
 /* GQA attention of one query position, the decode step of attention.wgsl's three passes
  * (scores :31-58, softmax :73-135, P.V :152-170; dispatched from wgpu_engine.rs:666-726).

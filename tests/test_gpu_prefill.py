@@ -1,0 +1,248 @@
+"""Batched prefill on a B200: causal tensor-core attention and the whole prompt forward.
+
+The batched path computes every projection on the tcgen05 GEMM with fp16 operands (weights
+expanded from the quantised blocks, activations rounded to fp16) and f32 accumulation, and the
+attention on fp16 Q/K/V with f32 softmax.  Its numerical reference is therefore a float forward
+of the same model (numpy float64 over the oracle's bit-exact dequantised weights), not candle's
+integer-dot path; the final lm_head of the last token runs with candle's semantics on both
+sides (Q8_K activations, oracle.matmul).  Against the candle oracle itself the difference is
+candle's own 8-bit activation rounding, bounded separately.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+torch = pytest.importorskip("torch")
+
+from tpt_spark_b200 import kernels as K  # noqa: E402
+from tpt_spark_b200._lib import EngineError  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16"]
+
+# fp16 operands (11-bit significands) against a float64 forward: relative error of a few
+# 2^-11 per layer on the hidden state, times the logit scale of the tiny models (|logit| < 3)
+LOGIT_ATOL_FLOAT_REF = 1e-2
+# against candle's 8-bit activation path: that path's own rounding (Q8_K / Q8_0 of every
+# projection input) dominates
+LOGIT_ATOL_ORACLE = 5e-2
+
+
+# ---------------------------------------------------------------- attention kernel
+
+ATTN_SHAPES = [
+    # T, start, n_heads, n_kv, hd, max_seq
+    (64, 0, 32, 8, 128, 256),     # one query tile, the C5 head layout
+    (200, 37, 4, 1, 64, 512),     # ragged chunk after a cached prefix, G = 4
+    (1, 100, 8, 8, 96, 128),      # a single query row (MHA, hd 96: the C4 layout)
+    (130, 0, 8, 8, 96, 256),      # ragged tiles from position 0
+    (512, 1000, 32, 8, 128, 2048),  # long prefix: 24 key tiles per query tile
+]
+
+
+def attn_reference(q, kc, vc, T, start, n_heads, n_kv, hd):
+    """fp32 causal attention of query rows at positions start + t over cache rows 0..start+t."""
+    G = n_heads // n_kv
+    L = start + T
+    qf = q.float().view(T, n_heads, hd).permute(1, 0, 2)            # [H, T, hd]
+    kf = kc[:, :L].float().repeat_interleave(G, dim=0)              # [H, L, hd]
+    vf = vc[:, :L].float().repeat_interleave(G, dim=0)
+    s = qf @ kf.transpose(1, 2) / hd ** 0.5                         # [H, T, L]
+    pos = torch.arange(start, start + T, device=q.device)[:, None]
+    key = torch.arange(L, device=q.device)[None, :]
+    s = s.masked_fill(key > pos, float("-inf"))
+    o = torch.softmax(s, dim=-1) @ vf                               # [H, T, hd]
+    return o.permute(1, 0, 2).reshape(T, n_heads * hd)
+
+
+@pytest.mark.parametrize("shape", ATTN_SHAPES, ids=lambda s: "t%d_s%d_h%d_kv%d_d%d" % s[:5])
+def test_attn_prefill_matches_torch(cuda_device, shape):
+    T, start, H, KV, hd, max_seq = shape
+    g = torch.Generator(device="cpu").manual_seed(T * 31 + start)
+    q = torch.randn(T, H * hd, generator=g).half().to(cuda_device)
+    kc = torch.randn(KV, max_seq, hd, generator=g).half().to(cuda_device)
+    vc = torch.randn(KV, max_seq, hd, generator=g).half().to(cuda_device)
+    out = torch.full((T, H * hd), float("nan"), dtype=torch.half, device=cuda_device)
+    K.attn_prefill(q, kc, vc, out, T, start, H, KV, hd, max_seq)
+    torch.cuda.synchronize()
+    want = attn_reference(q, kc, vc, T, start, H, KV, hd)
+    # probabilities enter P.V as fp16 and the output is stored as fp16 (2^-11 relative each)
+    torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=3e-3)
+
+
+def test_attn_prefill_rejects_bad_arguments(cuda_device):
+    z = torch.zeros(64 * 4 * 64, dtype=torch.half, device=cuda_device)
+    with pytest.raises(EngineError, match="head_dim"):
+        K.attn_prefill(z, z, z, z, 4, 0, 4, 2, 80, 64)
+    with pytest.raises(EngineError, match="bad argument"):
+        K.attn_prefill(z, z, z, z, 4, 62, 4, 2, 64, 64)  # runs past max_seq
+    with pytest.raises(EngineError, match="bad argument"):
+        K.attn_prefill(z, z, z, z, 4, 0, 4, 3, 64, 64)  # heads not a multiple of kv heads
+
+
+# ---------------------------------------------------------------- float forward reference
+
+def _weights(ref):
+    arrs, tys = ref._arrays, ref._types
+    D, F, hd = ref.dim, ref.ffn, ref.head_dim
+
+    def mat(i, N, Kd):
+        return O.dequant(tys[i], arrs[i], N * Kd).reshape(N, Kd).astype(np.float64)
+
+    w = {"emb": mat(0, ref.vocab, D), "out_norm": np.asarray(arrs[1], np.float32).astype(np.float64)}
+    layers = []
+    for l in range(ref.n_layers):
+        b = 3 + 9 * l
+        layers.append(dict(
+            attn_norm=np.asarray(arrs[b], np.float32).astype(np.float64),
+            q=mat(b + 1, ref.n_heads * hd, D), k=mat(b + 2, ref.n_kv_heads * hd, D),
+            v=mat(b + 3, ref.n_kv_heads * hd, D), o=mat(b + 4, D, ref.n_heads * hd),
+            ffn_norm=np.asarray(arrs[b + 5], np.float32).astype(np.float64),
+            gate=mat(b + 6, F, D), up=mat(b + 7, F, D), down=mat(b + 8, D, F)))
+    w["layers"] = layers
+    return w
+
+
+def float_prefill_logits(ref, tokens):
+    """Float64 forward of the prompt; the last position's final norm and lm_head with candle's
+    semantics (oracle.matmul quantises the activation as candle does)."""
+    w = _weights(ref)
+    D, hd, H, KV = ref.dim, ref.head_dim, ref.n_heads, ref.n_kv_heads
+    T, G = len(tokens), H // KV
+    cos, sin = O.rope_table(T, hd, ref.rope_base)
+    cos, sin = cos.astype(np.float64), sin.astype(np.float64)
+
+    def rms(x, g):
+        return x / np.sqrt((x * x).mean(-1, keepdims=True) + ref.rms_eps) * g
+
+    def rope(x, n):  # [T, n*hd], interleaved pairs
+        x = x.reshape(T, n, hd // 2, 2)
+        c, s = cos[:, None, :], sin[:, None, :]
+        r0 = x[..., 0] * c - x[..., 1] * s
+        r1 = x[..., 0] * s + x[..., 1] * c
+        return np.stack([r0, r1], -1).reshape(T, n, hd)
+
+    x = w["emb"][np.asarray(tokens)]
+    mask = np.triu(np.full((T, T), -np.inf), 1)
+    for L in w["layers"]:
+        xn = rms(x, L["attn_norm"])
+        q, k, v = rope(xn @ L["q"].T, H), rope(xn @ L["k"].T, KV), (xn @ L["v"].T).reshape(T, KV, hd)
+        att = np.empty((T, H, hd))
+        for h in range(H):
+            s = q[:, h] @ k[:, h // G].T / np.sqrt(hd) + mask
+            p = np.exp(s - s.max(-1, keepdims=True))
+            att[:, h] = (p / p.sum(-1, keepdims=True)) @ v[:, h // G]
+        x = x + att.reshape(T, H * hd) @ L["o"].T
+        xn = rms(x, L["ffn_norm"])
+        gt, up = xn @ L["gate"].T, xn @ L["up"].T
+        x = x + (gt / (1 + np.exp(-gt)) * up) @ L["down"].T
+    last = rms(x[-1:], w["out_norm"]).astype(np.float32)
+    out_i = 2
+    return O.matmul(ref._types[out_i], ref._arrays[out_i], ref.vocab, D, last)[0]
+
+
+@pytest.fixture(scope="module")
+def engines_f16(tiny_models, cuda_device):
+    from tpt_spark_b200.engine import CudaEngine
+
+    out = {}
+    for name, path in tiny_models.items():
+        e = CudaEngine(0, kv_dtype="f16")
+        e.load(path)
+        e.set_prefill_gemm_min(1)
+        out[name] = e
+    yield out
+    for e in out.values():
+        e.close()
+
+
+def _prompt(ref, n, seed):
+    return [int(t) for t in np.random.default_rng(seed).integers(0, ref.vocab, n)]
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_batched_prefill_matches_float_reference(engines_f16, tiny_models, name):
+    e = engines_f16[name]
+    ref = O.Model(tiny_models[name])
+    for n in (150, 77):
+        e.kv_reset()
+        prompt = _prompt(ref, n, n)
+        lg = e.prefill(prompt)
+        want = float_prefill_logits(ref, prompt)
+        diff = float(np.abs(lg - want).max())
+        print(f"{name} n={n}: max |logit - float64 reference| = {diff:.2e}")
+        assert diff <= LOGIT_ATOL_FLOAT_REF
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_batched_prefill_then_decode_against_oracle(engines_f16, tiny_models, name):
+    """Batched prefill, then 32 teacher-forced decode steps over its KV cache, against candle."""
+    e = engines_f16[name]
+    e.kv_reset()
+    ref = O.Model(tiny_models[name])
+    prompt = _prompt(ref, 100, 5)
+    lg = e.prefill(prompt)
+    lo = ref.forward(prompt, 0)
+    worst = float(np.abs(lg - lo).max())
+    pos = len(prompt)
+    for _ in range(32):
+        tok = O.argmax(lo)
+        g_logits, g_tok = e.decode(tok, pos)
+        lo = ref.forward([tok], pos)
+        d = float(np.abs(g_logits - lo).max())
+        worst = max(worst, d)
+        top2 = np.sort(lo)[-2:]
+        if top2[1] - top2[0] > 2 * d:
+            assert g_tok == O.argmax(lo)
+        pos += 1
+    print(f"{name}: max |logit diff| vs oracle after batched prefill = {worst:.2e}")
+    assert worst <= LOGIT_ATOL_ORACLE
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_prefill_in_pieces_is_bit_identical(engines_f16, tiny_models, name):
+    """A prompt prefilled in two pieces (the second after a cached prefix) gives the same
+    logits bit for bit: GEMM rows are independent and every query row sees the same key
+    tiles in the same order whatever chunk it belongs to."""
+    e = engines_f16[name]
+    ref = O.Model(tiny_models[name])
+    prompt = _prompt(ref, 140, 11)
+    e.kv_reset()
+    whole = e.prefill(prompt)
+    e.kv_reset()
+    e.prefill(prompt[:61])
+    assert e.kv_len() == 61
+    split = e.prefill(prompt[61:], start_pos=61)
+    assert e.kv_len() == 140
+    np.testing.assert_array_equal(split, whole)
+
+
+def test_threshold_and_f32_cache_use_the_token_path(tiny_models, cuda_device):
+    """Below the threshold (and always with an f32 cache) the prompt runs token by token:
+    bit-identical to decoding it."""
+    from tpt_spark_b200.engine import CudaEngine
+
+    path = tiny_models["tiny_q4km"]
+    ref = O.Model(path)
+    prompt = _prompt(ref, 40, 3)
+    for kv, gemm_min in (("f16", 0), ("f16", 41), ("f32", 1)):
+        with CudaEngine(0, kv_dtype=kv) as e:
+            e.load(path)
+            e.set_prefill_gemm_min(gemm_min)
+            lg = e.prefill(prompt)
+            e.kv_reset()
+            for i, t in enumerate(prompt):
+                step, _ = e.decode(t, i)
+            np.testing.assert_array_equal(lg, step)
+    # and at the threshold the batched path is taken (its fp16 numerics differ)
+    with CudaEngine(0, kv_dtype="f16") as e:
+        e.load(path)
+        e.set_prefill_gemm_min(40)
+        lg = e.prefill(prompt)
+        e.kv_reset()
+        for i, t in enumerate(prompt):
+            step, _ = e.decode(t, i)
+        assert not np.array_equal(lg, step)
+        assert float(np.abs(lg - step).max()) <= LOGIT_ATOL_ORACLE

@@ -1,5 +1,6 @@
 // capi.cpp -- extern "C" boundary (include/tptc.h).  Every entry point converts C++ state
 // into an int status and keeps the message for tptc_last_error.
+#include <math.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -101,6 +102,12 @@ TPTC_API int tptc_set_kv_dtype(tptc_ctx* ctx, int ggml_type) {
         return fail_code(ctx, TPTC_ERR_UNSUPPORTED, "KV cache type must be F16 or F32");
     Status s = ctx->eng->set_kv_f32(ggml_type == TPTC_TYPE_F32);
     return s.ok() ? TPTC_OK : fail(ctx, s);
+}
+
+TPTC_API int tptc_set_prefill_gemm_min(tptc_ctx* ctx, int min_tokens) {
+    if (!ctx) return TPTC_ERR_ARG;
+    ctx->eng->set_prefill_gemm_min(min_tokens);
+    return TPTC_OK;
 }
 
 TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user) {
@@ -444,6 +451,31 @@ TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, 
     cudaError_t e = tptc::gemm_tc(tptc::GEMM_STORE, static_cast<const __half*>(d_a), K, static_cast<const __half*>(d_b),
                                   K, p, static_cast<cudaStream_t>(stream), false);
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemm_tc");
+}
+
+TPTC_API int tptc_attn_prefill(const void* d_q, const void* d_kcache, const void* d_vcache, void* d_out, int T,
+                               int start, int n_heads, int n_kv, int head_dim, int max_seq, void* stream) {
+    if (!d_q || !d_kcache || !d_vcache || !d_out || T <= 0 || start < 0 || n_heads <= 0 || n_kv <= 0 ||
+        n_heads % n_kv || max_seq <= 0 || start + T > max_seq)
+        return fail_code(nullptr, TPTC_ERR_ARG, "attn_prefill: bad argument");
+    if (head_dim != 64 && head_dim != 96 && head_dim != 128)
+        return fail_code(nullptr, TPTC_ERR_UNSUPPORTED, "attn_prefill: head_dim must be 64, 96 or 128");
+    int dev = 0, sms = 0;
+    if (int rc = ensure_kernels(&dev, &sms)) return rc;
+    tptc::AttnPrefillParams p = {};
+    p.q = static_cast<const __half*>(d_q);
+    p.kcache = static_cast<const __half*>(d_kcache);
+    p.vcache = static_cast<const __half*>(d_vcache);
+    p.out = static_cast<__half*>(d_out);
+    p.T = T;
+    p.start = start;
+    p.n_heads = n_heads;
+    p.n_kv = n_kv;
+    p.hd = head_dim;
+    p.max_seq = max_seq;
+    p.scale = (float)(1.0 / sqrt((double)head_dim));
+    cudaError_t e = tptc::launch_attn_prefill(p, static_cast<cudaStream_t>(stream), false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "attn_prefill");
 }
 
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum, void* stream) {

@@ -58,6 +58,10 @@ class Engine {
         return {};
     }
     bool kv_f32() const { return kv_f32_; }
+    // Prompts of at least n tokens take the batched tensor-core prefill (fp16 KV cache only);
+    // shorter ones, or all when n <= 0, run token by token through the decode step.
+    void set_prefill_gemm_min(int n) { prefill_gemm_min_ = n; }
+    bool prefill_uses_gemm(int n) const;
     int prefix_len(const uint32_t* ids, int n) const;
 
     Status prefill(const uint32_t* ids, int n, int start_pos, float* last_logits);
@@ -84,7 +88,9 @@ class Engine {
     Status debug_trace(uint32_t id, int pos, float* trace);
 
    private:
-    Status enqueue_layer_prefill(int l, int n, int start_pos);
+    // prefill.cu
+    Status prefill_buffers(int chunk);
+    Status enqueue_prefill_chunk(int T, int start);
     Status run_prefill_batched(const uint32_t* ids, int n, int start_pos, float* last_logits);
     Status check_err();
     Status sync();
@@ -129,10 +135,21 @@ class Engine {
     float* attn_partial_ = nullptr;
     int* attn_counters_ = nullptr;
     int attn_splits_ = 1;
-    // prefill buffers (allocated on demand for the chunk size)
+    // batched prefill: buffers allocated on demand for the chunk size (tokens)
+    static constexpr int kPrefillChunk = 8192;
+    int prefill_gemm_min_ = 16;
     uint8_t* pf_ = nullptr;
     size_t pf_size_ = 0;
     int pf_chunk_ = 0;
+    uint32_t* pf_ids_ = nullptr;  // [T] token ids
+    float* pf_x_ = nullptr;       // [T][dim] residual stream
+    __half* pf_xn_ = nullptr;     // [T][dim] normed activations (GEMM A operand)
+    float* pf_qkv_ = nullptr;     // [T][(n_heads + 2 n_kv) hd] projection output
+    __half* pf_q_ = nullptr;      // [T][n_heads hd] rotated queries
+    __half* pf_o_ = nullptr;      // [T][n_heads hd] attention output
+    __half* pf_h_ = nullptr;      // [T][ffn] silu(gate) * up
+    __half* pf_w_ = nullptr;      // one layer matrix as dense fp16 (GEMM B operand)
+    float* pf_part_ = nullptr;    // [T][dim] row-parallel partial sums (tensor parallel)
 
     // pinned host staging
     uint32_t* h_tok_ = nullptr;

@@ -18,7 +18,10 @@ cudaError_t launch_quant_q80(const float* x, int64_t k, void* out, cudaStream_t 
 cudaError_t launch_repack(const uint8_t* raw, int64_t raw_row, int nr, int first_row, const DevMatrix& m,
                           cudaStream_t st);
 // Device-layout rows [row0, row0+rows) of `m` -> dense f16 [rows, K] (prefill operand).
-cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st);
+// Rows [row0, row0 + rows) of m as dense fp16 rows: logical rows, or with `physical` the
+// device (tile) order -- for a gate|up matrix, 4 gate rows then the 4 matching up rows.
+cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st,
+                                    bool physical = false);
 
 // attn_decode.cu
 struct AttnDecodeParams {

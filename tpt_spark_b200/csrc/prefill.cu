@@ -1,20 +1,316 @@
-// prefill.cu -- prompt processing.
+// prefill.cu -- prompt processing (prefill).
+//
+// Two paths behind Engine::prefill (tptc_prefill):
+//   * batched: the whole chunk of prompt tokens goes through each layer at once -- weights
+//     expanded to dense fp16 per layer, projections on the tcgen05 GEMM (gemm_tc.cu), causal
+//     attention over the chunk on the tensor cores (attn_prefill.cu).  This is candle's batched
+//     `forward(&input, 0)` (candle_engine.rs:272-281) in the form its CUDA backend takes for
+//     batches (dequantise to f16, then a dense matmul), and replaces the reference GPU
+//     engine's token-by-token prefill (wgpu_engine.rs:252-261).  Activations enter the GEMMs
+//     as fp16 (not Q8_K), so the logits differ from the integer-dot decode path by fp16
+//     rounding; the KV cache must be fp16.
+//   * per token: each prompt position through the decode step (bit-identical to decoding the
+//     prompt; the only path for the f32 KV cache and for prompts below the batched threshold).
+#include <algorithm>
 #include <vector>
 
 #include "engine.h"
+#include "kernels.h"
 #include "prefill.h"
+#include "quant.cuh"
+#include "tp.h"
 
 namespace tptc {
 
-cudaError_t prefill_init_device() { return gemm_tc_init_device(); }
+namespace {
 
-// Prompt positions one at a time through the decode graph (the reference's prefill loop,
-// wgpu_engine.rs:254-261); the last step's logits are returned.
+#define PF_RET_IF(st)                \
+    do {                             \
+        Status _s = (st);            \
+        if (!_s.ok()) return _s;     \
+    } while (0)
+
+// x[t][:] = dequantised row ids[t] of token_embd (device layout); one CTA per token.
+__global__ void embed_rows_kernel(DevMatrix emb, const uint32_t* __restrict__ ids, float* __restrict__ x) {
+    const int t = blockIdx.x, row = (int)ids[t], K = emb.K;
+    float* xr = x + (size_t)t * K;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const uint8_t* blk = dm_block(emb, row, i / QK_K);
+        const int e = i % QK_K;
+        float v;
+        if (emb.type == TPTC_TYPE_Q4_K) {
+            v = q4k_elem(blk, e);
+        } else if (emb.type == TPTC_TYPE_Q6_K) {
+            v = q6k_elem(blk, h2f(dm_scales(emb, row, i / QK_K)[0]), e);
+        } else if (emb.type == TPTC_TYPE_Q8_0) {
+            v = __fmul_rn((float)(int8_t)blk[e], h2f(dm_scales(emb, row, i / QK_K)[e / QK8_0]));
+        } else {
+            v = h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
+        }
+        xr[i] = v;
+    }
+}
+
+// out[t][:] = fp16(x[t] / sqrt(mean(x[t]^2) + eps) * w) (candle rms_norm: x / m * alpha);
+// one CTA of 256 threads per token, dim a multiple of 4.
+__global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                          int dim, float eps, __half* __restrict__ out) {
+    __shared__ float red[8];
+    const int t = blockIdx.x;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * dim);
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) {
+        const float4 v = xr[i];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) tot += red[i];
+    const float m = sqrtf(tot / (float)dim + eps);
+    __half2* o2 = reinterpret_cast<__half2*>(out + (size_t)t * dim);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) {
+        const float4 v = xr[i], g = w4[i];
+        o2[2 * i] = __floats2half2_rn(__fdiv_rn(v.x, m) * g.x, __fdiv_rn(v.y, m) * g.y);
+        o2[2 * i + 1] = __floats2half2_rn(__fdiv_rn(v.z, m) * g.z, __fdiv_rn(v.w, m) * g.w);
+    }
+}
+
+// The q|k|v GEMM output row of token t -> RoPE (candle rope_i: interleaved pairs) on q and
+// k, q as fp16 [T][n_heads][hd], k and v into this layer's fp16 cache at position start + t.
+// Same rotation arithmetic as the decode attention kernel.  One CTA per token.
+struct QkvPostParams {
+    const float* qkv;  // [T][(n_heads + 2 n_kv) hd]
+    __half* q;
+    __half* kc;
+    __half* vc;
+    const float* cos;
+    const float* sin;
+    int start, n_heads, n_kv, hd, max_seq;
+};
+__global__ void qkv_post_kernel(const QkvPostParams p) {
+    const int t = blockIdx.x, pos = p.start + t, half = p.hd / 2;
+    const int nq = p.n_heads * p.hd, nk = p.n_kv * p.hd, n = nq + 2 * nk;
+    const float* row = p.qkv + (size_t)t * n;
+    const float* cs = p.cos + (size_t)pos * half;
+    const float* sn = p.sin + (size_t)pos * half;
+    for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const int col = 2 * i;
+        const float2 v = *reinterpret_cast<const float2*>(row + col);
+        if (col < nq + nk) {
+            const int j = (col % p.hd) / 2;
+            const float c = cs[j], s = sn[j];
+            const float r0 = __fsub_rn(__fmul_rn(v.x, c), __fmul_rn(v.y, s));
+            const float r1 = __fadd_rn(__fmul_rn(v.x, s), __fmul_rn(v.y, c));
+            if (col < nq) {
+                *reinterpret_cast<__half2*>(p.q + (size_t)t * nq + col) = __floats2half2_rn(r0, r1);
+            } else {
+                const int kh = (col - nq) / p.hd, e = (col - nq) % p.hd;
+                *reinterpret_cast<__half2*>(p.kc + ((size_t)kh * p.max_seq + pos) * p.hd + e) =
+                    __floats2half2_rn(r0, r1);
+            }
+        } else {
+            const int vh = (col - nq - nk) / p.hd, e = (col - nq - nk) % p.hd;
+            *reinterpret_cast<__half2*>(p.vc + ((size_t)vh * p.max_seq + pos) * p.hd + e) =
+                __floats2half2_rn(v.x, v.y);
+        }
+    }
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+cudaError_t prefill_init_device() {
+    cudaError_t e = gemm_tc_init_device();
+    if (e != cudaSuccess) return e;
+    return attn_prefill_init_device();
+}
+
+// Scratch of the batched path for chunks of up to `chunk` tokens (one allocation).
+Status Engine::prefill_buffers(int chunk) {
+    if (chunk <= pf_chunk_) return {};
+    const ModelMeta& m = meta_;
+    const int hd = m.head_dim, ffn_l = m.ffn / tp_size_;
+    const size_t nq = (size_t)n_heads_l_ * hd, nqkv = nq + 2 * (size_t)n_kv_l_ * hd;
+    const size_t T = (size_t)chunk;
+    const size_t w_elems = std::max({nqkv * m.dim, (size_t)2 * ffn_l * m.dim, (size_t)m.dim * ffn_l,
+                                     (size_t)m.dim * nq});
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = align256(off + bytes);
+        return o;
+    };
+    const size_t o_ids = take(T * 4), o_x = take(T * m.dim * 4), o_xn = take(T * m.dim * 2);
+    const size_t o_qkv = take(T * nqkv * 4), o_q = take(T * nq * 2), o_o = take(T * nq * 2);
+    const size_t o_h = take(T * ffn_l * 2), o_w = take(w_elems * 2);
+    // row-parallel partial sums under tensor parallelism (the decode step's own partial
+    // buffer is baked into its graph and is not resized here)
+    const size_t o_part = tp_ ? take(T * m.dim * 4) : 0;
+    if (pf_) {
+        TPTC_CUDA_RET(cudaStreamSynchronize(stream_));
+        cudaFree(pf_);
+    }
+    pf_ = nullptr;
+    pf_size_ = 0;
+    pf_chunk_ = 0;
+    cudaError_t ce = cudaMalloc(&pf_, off);
+    if (ce != cudaSuccess) {
+        pf_ = nullptr;
+        return Status{TPTC_ERR_OOM, "prefill buffers for " + std::to_string(chunk) + " tokens need " +
+                                        std::to_string(off >> 20) + " MiB: " + cuda_msg(ce, "cudaMalloc")};
+    }
+    pf_size_ = off;
+    pf_chunk_ = chunk;
+    pf_ids_ = reinterpret_cast<uint32_t*>(pf_ + o_ids);
+    pf_x_ = reinterpret_cast<float*>(pf_ + o_x);
+    pf_xn_ = reinterpret_cast<__half*>(pf_ + o_xn);
+    pf_qkv_ = reinterpret_cast<float*>(pf_ + o_qkv);
+    pf_q_ = reinterpret_cast<__half*>(pf_ + o_q);
+    pf_o_ = reinterpret_cast<__half*>(pf_ + o_o);
+    pf_h_ = reinterpret_cast<__half*>(pf_ + o_h);
+    pf_w_ = reinterpret_cast<__half*>(pf_ + o_w);
+    pf_part_ = tp_ ? reinterpret_cast<float*>(pf_ + o_part) : nullptr;
+    return {};
+}
+
+// One chunk of T prompt tokens at positions start .. start + T - 1 (ids already in pf_ids_).
+Status Engine::enqueue_prefill_chunk(int T, int start) {
+    const ModelMeta& m = meta_;
+    const int hd = m.head_dim, dim = m.dim, ffn_l = m.ffn / tp_size_;
+    const int nq = n_heads_l_ * hd, nk = n_kv_l_ * hd, nqkv = nq + 2 * nk;
+    const size_t layer_kv = (size_t)2 * n_kv_l_ * max_seq_ * hd * 2;  // bytes (fp16 cache)
+    cudaStream_t st = stream_;
+    embed_rows_kernel<<<T, 256, 0, st>>>(embd_, pf_ids_, pf_x_);
+    TPTC_CUDA_RET(cudaGetLastError());
+    for (int l = 0; l < m.n_layers; l++) {
+        const LayerWeights& L = layers_[l];
+        __half* kc = reinterpret_cast<__half*>(kv_ + l * layer_kv);
+        __half* vc = reinterpret_cast<__half*>(kv_ + l * layer_kv + layer_kv / 2);
+        // attention block
+        rmsnorm_f16_kernel<<<T, 256, 0, st>>>(pf_x_, L.attn_norm, dim, m.rms_eps, pf_xn_);
+        TPTC_CUDA_RET(cudaGetLastError());
+        TPTC_CUDA_RET(launch_dequant_rows_f16(L.q, 0, nq, pf_w_, st));
+        TPTC_CUDA_RET(launch_dequant_rows_f16(L.k, 0, nk, pf_w_ + (size_t)nq * dim, st));
+        TPTC_CUDA_RET(launch_dequant_rows_f16(L.v, 0, nk, pf_w_ + (size_t)(nq + nk) * dim, st));
+        GemmTcParams g = {};
+        g.M = T;
+        g.N = nqkv;
+        g.K = dim;
+        g.c = pf_qkv_;
+        g.ldc = nqkv;
+        g.err = err_;
+        TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_xn_, dim, pf_w_, dim, g, st, false));
+        QkvPostParams qp = {pf_qkv_, pf_q_, kc, vc, rope_cos_, rope_sin_, start, n_heads_l_, n_kv_l_, hd, max_seq_};
+        qkv_post_kernel<<<T, 256, 0, st>>>(qp);
+        TPTC_CUDA_RET(cudaGetLastError());
+        AttnPrefillParams ap = {};
+        ap.q = pf_q_;
+        ap.kcache = kc;
+        ap.vcache = vc;
+        ap.out = pf_o_;
+        ap.T = T;
+        ap.start = start;
+        ap.n_heads = n_heads_l_;
+        ap.n_kv = n_kv_l_;
+        ap.hd = hd;
+        ap.max_seq = max_seq_;
+        ap.scale = (float)(1.0 / sqrt((double)hd));
+        TPTC_CUDA_RET(launch_attn_prefill(ap, st, false));
+        TPTC_CUDA_RET(launch_dequant_rows_f16(L.o, 0, dim, pf_w_, st));
+        g.N = dim;
+        g.K = nq;
+        g.ldc = dim;
+        if (tp_) {  // row-parallel o: partial sums of every token, then one allreduce
+            g.c = pf_part_;
+            TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_o_, nq, pf_w_, nq, g, st, false));
+            PF_RET_IF(tp_->allreduce_add(g.c, pf_x_, (size_t)T * dim, st));
+        } else {
+            g.c = pf_x_;
+            TPTC_CUDA_RET(gemm_tc(GEMM_RESID, pf_o_, nq, pf_w_, nq, g, st, false));
+        }
+        // feed-forward block: gate|up in the device tile order, silu(gate) * up in the epilogue
+        rmsnorm_f16_kernel<<<T, 256, 0, st>>>(pf_x_, L.ffn_norm, dim, m.rms_eps, pf_xn_);
+        TPTC_CUDA_RET(cudaGetLastError());
+        TPTC_CUDA_RET(launch_dequant_rows_f16(L.glu, 0, 2 * ffn_l, pf_w_, st, true));
+        GemmTcParams gg = {};
+        gg.M = T;
+        gg.N = 2 * ffn_l;
+        gg.K = dim;
+        gg.h = pf_h_;
+        gg.ldh = ffn_l;
+        gg.err = err_;
+        TPTC_CUDA_RET(gemm_tc(GEMM_GLU, pf_xn_, dim, pf_w_, dim, gg, st, false));
+        TPTC_CUDA_RET(launch_dequant_rows_f16(L.down, 0, dim, pf_w_, st));
+        g.N = dim;
+        g.K = ffn_l;
+        g.ldc = dim;
+        if (tp_) {
+            g.c = pf_part_;
+            TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_h_, ffn_l, pf_w_, ffn_l, g, st, false));
+            PF_RET_IF(tp_->allreduce_add(g.c, pf_x_, (size_t)T * dim, st));
+        } else {
+            g.c = pf_x_;
+            TPTC_CUDA_RET(gemm_tc(GEMM_RESID, pf_h_, ffn_l, pf_w_, ffn_l, g, st, false));
+        }
+    }
+    return {};
+}
+
+bool Engine::prefill_uses_gemm(int n) const {
+    if (kv_f32_ || prefill_gemm_min_ <= 0 || n < prefill_gemm_min_) return false;
+    const ModelMeta& m = meta_;
+    const int ffn_l = m.ffn / tp_size_;
+    // GEMM operands: K a multiple of 64, the gate|up tile order whole 8-row groups
+    return m.dim % 64 == 0 && (n_heads_l_ * m.head_dim) % 64 == 0 && ffn_l % 64 == 0 &&
+           (m.head_dim == 64 || m.head_dim == 96 || m.head_dim == 128);
+}
+
 Status Engine::run_prefill_batched(const uint32_t* ids, int n, int start_pos, float* last_logits) {
-    for (int i = 0; i < n; i++) {
-        uint32_t am;
-        Status s = decode(ids[i], start_pos + i, i + 1 == n ? last_logits : nullptr, &am);
-        if (!s.ok()) return s;
+    if (!prefill_uses_gemm(n)) {
+        // Prompt positions one at a time through the decode graph (the reference's prefill
+        // loop, wgpu_engine.rs:254-261); the last step's logits are returned.
+        for (int i = 0; i < n; i++) {
+            uint32_t am;
+            Status s = decode(ids[i], start_pos + i, i + 1 == n ? last_logits : nullptr, &am);
+            if (!s.ok()) return s;
+        }
+        return {};
+    }
+    const int chunk = std::min(n, kPrefillChunk);
+    PF_RET_IF(prefill_buffers(chunk));
+    const ModelMeta& m = meta_;
+    for (int c0 = 0; c0 < n; c0 += chunk) {
+        const int T = std::min(chunk, n - c0);
+        TPTC_CUDA_RET(cudaMemcpyAsync(pf_ids_, ids + c0, (size_t)T * 4, cudaMemcpyHostToDevice, stream_));
+        PF_RET_IF(enqueue_prefill_chunk(T, start_pos + c0));
+        if (c0 + T == n) {
+            // the last token's row -> final norm + lm_head (the decode GEMV)
+            TPTC_CUDA_RET(cudaMemcpyAsync(x_, pf_x_ + (size_t)(T - 1) * m.dim, (size_t)m.dim * 4,
+                                          cudaMemcpyDeviceToDevice, stream_));
+            GemvParams h = {};
+            h.K = m.dim;
+            h.err = err_;
+            h.act_global = act_;
+            h.eps = m.rms_eps;
+            h.nseg = 1;
+            h.seg[0] = GemvSeg{output_, 0};
+            h.x = x_;
+            h.norm_w = out_norm_;
+            h.out = logits_;
+            gemv_prepare(h, sm_count_);
+            TPTC_CUDA_RET(gemv_launch(h, EPI_STORE, stream_, false));
+            if (last_logits)
+                TPTC_CUDA_RET(cudaMemcpyAsync(last_logits, logits_, (size_t)m.vocab * 4, cudaMemcpyDeviceToHost,
+                                              stream_));
+        }
+        // the ids buffer is reused by the next chunk: wait for this one
+        PF_RET_IF(sync());
+        cached_tokens_.insert(cached_tokens_.end(), ids + c0, ids + c0 + T);
     }
     return {};
 }

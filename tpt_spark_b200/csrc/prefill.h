@@ -30,4 +30,23 @@ cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb,
                     cudaStream_t st, bool pdl);
 cudaError_t gemm_tc_init_device();
 
+// ---- causal attention over a prompt chunk (attn_prefill.cu)
+struct AttnPrefillParams {
+    const __half* q;       // [T][n_heads][hd], rotated
+    const __half* kcache;  // this layer's caches [n_kv][max_seq][hd] (fp16), chunk rows written
+    const __half* vcache;
+    __half* out;           // [T][n_heads][hd]
+    int T, start;          // chunk rows are positions start .. start + T - 1
+    int n_heads, n_kv, hd, max_seq;
+    float scale;           // 1/sqrt(hd)
+};
+cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, bool pdl);
+cudaError_t attn_prefill_init_device();
+
+// ---- per-token elementwise steps of a chunk (prefill.cu)
+struct PrefillRope {
+    const float* cos;  // [max_seq][hd/2]
+    const float* sin;
+};
+
 }  // namespace tptc

@@ -85,12 +85,12 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, 
 }
 
 // Device layout -> dense f16 rows [row0, row0 + rows), one thread per 8 consecutive elements.
-__global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, __half* __restrict__ out) {
+__global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, int physical, __half* __restrict__ out) {
     const int64_t per_row = m.K / 8;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= per_row * rows) return;
     const int r = (int)(i / per_row), k0 = (int)(i % per_row) * 8;
-    const int prow = dm_phys_row(m, row0 + r);
+    const int prow = physical ? row0 + r : dm_phys_row(m, row0 + r);
     const uint8_t* blk = dm_block(m, prow, k0 / QK_K);
     const int e0 = k0 % QK_K;
     __align__(16) __half v[8];
@@ -140,10 +140,11 @@ cudaError_t launch_repack(const uint8_t* raw, int64_t raw_row, int nr, int first
     return cudaGetLastError();
 }
 
-cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st) {
+cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st,
+                                    bool physical) {
     const int64_t n = (int64_t)rows * (m.K / 8);
     if (n <= 0) return cudaSuccess;
-    dequant_rows_f16_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, st>>>(m, row0, rows, out);
+    dequant_rows_f16_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, st>>>(m, row0, rows, physical ? 1 : 0, out);
     return cudaGetLastError();
 }
 

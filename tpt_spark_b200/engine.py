@@ -92,6 +92,11 @@ class CudaEngine:
         self.tokenizer = tokenizer
         self._info: Optional[ModelInfo] = None
 
+    def set_prefill_gemm_min(self, min_tokens: int) -> None:
+        """Prompts of at least min_tokens run the batched tensor-core prefill (fp16 KV only);
+        shorter ones, or all when min_tokens <= 0, go token by token (exact decode numerics)."""
+        self._check(lib().tptc_set_prefill_gemm_min(self._ctx, int(min_tokens)))
+
     # -- lifecycle ---------------------------------------------------------------------------
     def close(self):
         if self._ctx:

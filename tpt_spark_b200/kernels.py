@@ -87,3 +87,10 @@ def attn_decode_noalloc(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_co
 def gemm_f16(d_a, d_b, d_c, M: int, N: int, K: int, stream: Optional[int] = None) -> None:
     """C[M x N] (f32) = A[M x K] . B[N x K]^T on the tensor cores (fp16 row-major A and B)."""
     check(lib().tptc_gemm_f16(_ptr(d_a), _ptr(d_b), _ptr(d_c), M, N, K, stream))
+
+
+def attn_prefill(d_q, d_kcache, d_vcache, d_out, T: int, start: int, n_heads: int, n_kv: int, head_dim: int,
+                 max_seq: int, stream: Optional[int] = None) -> None:
+    """Causal GQA attention of T prompt rows at positions start.. over an fp16 KV cache."""
+    check(lib().tptc_attn_prefill(_ptr(d_q), _ptr(d_kcache), _ptr(d_vcache), _ptr(d_out), T, start, n_heads, n_kv,
+                                  head_dim, max_seq, stream))
