@@ -20,6 +20,8 @@ SHAPES = [
     (77, 200, 256),      # ragged M and N
     (1, 128, 512),       # a single token
     (1024, 6144, 4096),  # the C5 q|k|v shape for a 1024-token chunk
+    (64, 130, 64),       # leading dimension not a multiple of 4 (scalar epilogue)
+    (4096, 4096, 512),   # 512 tiles: several per persistent CTA, both accumulators cycling
 ]
 
 

@@ -5,22 +5,28 @@
 // Replaces the per-token matmuls of the reference's prefill loop (wgpu_engine.rs:254-261,
 // gemm.wgsl with M = 1 once per token) for a whole prompt.
 //
-// One CTA computes a 128 x 128 tile of C:
+// A persistent kernel (one CTA per SM, 192 KB of shared memory) walks 128 x 256 tiles of C,
+// M fastest so that concurrent CTAs share the B tiles and the whole A operand stays in L2:
 //   - warp 0 (one lane): TMA producer.  Both operands are 2-D tensor maps with 128-byte
-//     swizzle; each pipeline stage is a 128 x 64 tile of A and of B (16 KB each, K-major,
-//     exactly the canonical SWIZZLE_128B operand layout of tcgen05.mma), completion counted
-//     on the stage's "full" mbarrier;
-//   - warp 1: allocates 128 TMEM columns; one lane issues tcgen05.mma (M = 128, N = 128,
-//     K = 16: four per stage, the descriptor start address advancing 32 bytes within the
-//     swizzle atom) and commits each stage to its "empty" mbarrier, so the producer refills it
-//     as soon as the tensor core has read it; the last commit signals the accumulator;
+//     swizzle; a pipeline stage holds a 128 x 64 tile of A and a 256 x 64 tile of B (16 + 32
+//     KB, K-major, the canonical SWIZZLE_128B operand layout of tcgen05.mma), completion
+//     counted on the stage's "full" mbarrier;
+//   - warp 1: allocates all 512 TMEM columns (two 256-column f32 accumulators); one lane
+//     issues tcgen05.mma (M = 128, N = 256, K = 16: four per stage, the descriptor start
+//     address advancing 32 bytes within the swizzle atom), commits each stage to its "empty"
+//     mbarrier so the producer refills it as soon as the tensor core has read it, and each
+//     finished accumulator to "tfull";
 //   - warps 2-5: epilogue.  Warp w reads TMEM lanes 32 (w % 4) .. +31 (= rows of the tile)
-//     with tcgen05.ld, 32 columns at a time, and writes C (f32 store, residual add, or the
-//     fused gate|up SiLU product in fp16).
-// Every mbarrier wait is bounded (error flag, then the CTA still frees its TMEM and exits).
+//     with tcgen05.ld, 32 columns at a time, hands the accumulator back ("tempty") after its
+//     last read and writes C (f32 store, residual add, or the fused gate|up SiLU product in
+//     fp16) while the tensor core already fills the other accumulator.
+// Every mbarrier wait is bounded: a wait that gives up sets the error word and the CTA's abort
+// flag, the other roles stop at their next wait, the producer waits (bounded) for its copies
+// in flight, the MMA lane for its MMAs, and the CTA frees its TMEM and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "prefill.h"
@@ -29,10 +35,13 @@ namespace tptc {
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, kStages = 4;
-constexpr int kTileBytes = BM * BK * 2;  // one operand tile of a stage (A and B alike)
+constexpr int BM = 128, BN = 256, BK = 64, kStages = 4;
+constexpr int kABytes = BM * BK * 2;  // A tile of a stage (16 KB)
+constexpr int kBBytes = BN * BK * 2;  // B tile of a stage (32 KB)
+constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 128;
+constexpr int kAccCols = BN;             // f32 accumulator columns of one tile
+constexpr int kTmemCols = 2 * kAccCols;  // double-buffered: all 512 columns
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -88,26 +97,104 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Bounded wait that also gives up once another role of the CTA has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
+    *abort_flag = 1;
+    return false;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); }
+
+// Epilogue of 32 accumulator columns (col .. col + 31) of one row.
+template <int EPI>
+__device__ __forceinline__ void store_cols(const GemmTcParams& p, int row, int col, const uint32_t (&r)[32]) {
+    if (row >= p.M || col >= p.N) return;
+    if (EPI == GEMM_STORE || EPI == GEMM_RESID) {
+        float* c = p.c + (size_t)row * p.ldc + col;
+        if (col + 32 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0) {
+            float4* c4 = reinterpret_cast<float4*>(c);
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                v[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            if (EPI == GEMM_RESID) {
+                float4 o[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) o[j] = c4[j];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    v[j].x += o[j].x;
+                    v[j].y += o[j].y;
+                    v[j].z += o[j].z;
+                    v[j].w += o[j].w;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) c4[j] = v[j];
+        } else {
+            const int nv = min(32, p.N - col);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                if (j < nv) {
+                    const float v = __uint_as_float(r[j]);
+                    if (EPI == GEMM_RESID) c[j] += v;
+                    else c[j] = v;
+                }
+            }
+        }
+    } else {  // GEMM_GLU: columns 8t..8t+3 gate, 8t+4..8t+7 up of outputs 4t..4t+3
+        __half* h = p.h + (size_t)row * p.ldh + col / 2;
+        if (col + 32 <= p.N && (p.ldh & 7) == 0 && (reinterpret_cast<uintptr_t>(p.h) & 15) == 0) {
+            __align__(16) __half o[16];
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    o[4 * t + i] = __float2half_rn(silu_mul(__uint_as_float(r[8 * t + i]), __uint_as_float(r[8 * t + 4 + i])));
+            reinterpret_cast<uint4*>(h)[0] = reinterpret_cast<const uint4*>(o)[0];
+            reinterpret_cast<uint4*>(h)[1] = reinterpret_cast<const uint4*>(o)[1];
+        } else {
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (col + 8 * t + 4 + i < p.N)
+                        h[4 * t + i] =
+                            __float2half_rn(silu_mul(__uint_as_float(r[8 * t + i]), __uint_as_float(r[8 * t + 4 + i])));
+        }
+    }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                    const __grid_constant__ GemmTcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[kStages], empty[kStages], accum;
+    __shared__ uint64_t full[kStages], empty[kStages], tfull[2], tempty[2], drain;
     __shared__ uint32_t tmem_slot;
-    __shared__ int timed_out;
+    __shared__ volatile int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, nk = p.K / BK;
+    const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN, tiles = num_m * num_n, nk = p.K / BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&accum, 1);
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(&drain, 1);
         fence_mbar_init();
-        timed_out = 0;
+        abort_flag = 0;
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -124,73 +211,77 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
-            for (int kb = 0; kb < nk; kb++) {
-                const int s = kb % kStages;
-                if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1, p.err)) {
-                    timed_out = 1;
-                    break;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t % num_m) * BM, n0 = (t / num_m) * BN;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * kStageBytes;
+                    mbar_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st, &ta, kb * BK, m0, &full[s]);
+                    tma_load_2d(st + kABytes, &tb, kb * BK, n0, &full[s]);
                 }
-                uint8_t* st = smem + s * 2 * kTileBytes;
-                mbar_expect_tx(&full[s], 2 * kTileBytes);
-                tma_load_2d(st, &ta, kb * BK, m0, &full[s]);
-                tma_load_2d(st + kTileBytes, &tb, kb * BK, n0, &full[s]);
             }
+            // the copies still in flight land before the CTA exits
+            for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; j++)
+                mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, p.err);
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
             const uint32_t idesc = mma_idesc(BM, BN);
+            uint32_t it = 0, tc = 0;
             bool ok = true;
-            for (int kb = 0; kb < nk && ok; kb++) {
-                const int s = kb % kStages;
-                if (!mbar_wait_bounded(&full[s], (kb / kStages) & 1, p.err)) {
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, tc++) {
+                const uint32_t acc = tc & 1, d = tmem + acc * kAccCols;
+                if (tc >= 2 && !wait_or_abort(&tempty[acc], ((tc >> 1) - 1) & 1, p.err, &abort_flag)) {
                     ok = false;
-                    timed_out = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a = smem_u32(smem + s * 2 * kTileBytes), b = a + kTileBytes;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % kStages;
+                    if (!wait_or_abort(&full[s], (it / kStages) & 1, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(smem + s * kStageBytes), b = a + kABytes;
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++)
-                    mma_f16(tmem, sw128_desc(a + 32 * k), sw128_desc(b + 32 * k), idesc, (kb | k) != 0);
-                mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                    for (int k = 0; k < BK / 16; k++)
+                        mma_f16(d, sw128_desc(a + 32 * k), sw128_desc(b + 32 * k), idesc, (kb | k) != 0);
+                    mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                }
+                if (ok) mma_commit(&tfull[acc]);
             }
-            mma_commit(&accum);  // accumulator complete (also after a timeout: no MMA pending)
+            // every MMA issued has completed before TMEM is freed
+            mma_commit(&drain);
+            mbar_wait_bounded(&drain, 0, p.err);
         }
     } else {  // epilogue warps 2..5
         const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const bool ok = mbar_wait_bounded(&accum, 0, p.err);
-        tc_fence_after();
-        const int row = m0 + 32 * q + lane;
-        if (ok && !timed_out) {
+        uint32_t tc = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, tc++) {
+            const uint32_t acc = tc & 1;
+            if (!wait_or_abort(&tfull[acc], (tc >> 1) & 1, p.err, &abort_flag)) break;
+            tc_fence_after();
+            const int m0 = (t % num_m) * BM, n0 = (t / num_m) * BN;
+            const int row = m0 + 32 * q + lane;
+            const uint32_t base = tmem + acc * kAccCols + ((uint32_t)(32 * q) << 16);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
-                if (row >= p.M || n0 + c0 >= p.N) continue;
-                const int col = n0 + c0;
-                if (EPI == GEMM_STORE || EPI == GEMM_RESID) {
-                    float* c = p.c + (size_t)row * p.ldc + col;
-                    const int nv = min(32, p.N - col);
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        if (j < nv) {
-                            const float v = __uint_as_float(r[j]);
-                            if (EPI == GEMM_RESID) c[j] += v;
-                            else c[j] = v;
-                        }
-                    }
-                } else {  // GEMM_GLU: columns 8t..8t+3 gate, 8t+4..8t+7 up of outputs 4t..4t+3
-                    __half* h = p.h + (size_t)row * p.ldh + col / 2;
-#pragma unroll
-                    for (int t = 0; t < 4; t++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            if (col + 8 * t + 4 + i < p.N) {
-                                const float g = __uint_as_float(r[8 * t + i]), u = __uint_as_float(r[8 * t + 4 + i]);
-                                h[4 * t + i] = __float2half_rn(__fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u));
-                            }
-                        }
+                tmem_ld32(base + (uint32_t)c0, r);
+                if (c0 + 32 == BN) {  // accumulator read out: hand it back to the MMA lane
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
                 }
+                store_cols<EPI>(p, row, n0 + c0, r);
             }
         }
     }
@@ -218,13 +309,13 @@ cudaError_t get_encode() {
 }
 
 // Row-major fp16 matrix [rows x cols] (leading dimension ld elements) as a 2-D tensor map with
-// a 64 x 128 box and 128-byte swizzle.
-cudaError_t make_map(CUtensorMap* map, const __half* ptr, int rows, int cols, int ld) {
+// a box of 64 columns x box_rows rows and 128-byte swizzle.
+cudaError_t make_map(CUtensorMap* map, const __half* ptr, int rows, int cols, int ld, int box_rows) {
     cudaError_t e = get_encode();
     if (e != cudaSuccess) return e;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -232,7 +323,23 @@ cudaError_t make_map(CUtensorMap* map, const __half* ptr, int rows, int cols, in
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-constexpr size_t kSmem = (size_t)kStages * 2 * kTileBytes + 1024;
+constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
+// more than half of an SM's shared memory: one CTA per SM, so the 512-column TMEM allocation
+// never waits for another CTA
+static_assert(kSmem > 116 * 1024, "gemm_tc relies on one resident CTA per SM");
+
+int g_sms[64];
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!g_sms[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_sms[dev] = n;
+    }
+    return g_sms[dev];
+}
 
 }  // namespace
 
@@ -252,11 +359,12 @@ cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb,
         return cudaErrorInvalidValue;
     if (epi == GEMM_GLU && p_in.N % 8) return cudaErrorInvalidValue;
     CUtensorMap ma, mb;
-    cudaError_t e = make_map(&ma, a, p_in.M, p_in.K, lda);
-    if (e == cudaSuccess) e = make_map(&mb, b, p_in.N, p_in.K, ldb);
+    cudaError_t e = make_map(&ma, a, p_in.M, p_in.K, lda, BM);
+    if (e == cudaSuccess) e = make_map(&mb, b, p_in.N, p_in.K, ldb, BN);
     if (e != cudaSuccess) return e;
+    const long tiles = (long)((p_in.M + BM - 1) / BM) * ((p_in.N + BN - 1) / BN);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p_in.N + BN - 1) / BN, (p_in.M + BM - 1) / BM);
+    cfg.gridDim = dim3((unsigned)std::min<long>(tiles, sm_count()));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmem;
     cfg.stream = st;
