@@ -46,7 +46,8 @@ def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         d = json.load(open(p))
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "src": "measured"}
     except Exception:
         return dict(PEAKS_FALLBACK, src="fallback")
 
@@ -186,6 +187,16 @@ def decode_bytes(cfg, kv_len_mean):
     return tot
 
 
+def prefill_flops(cfg, P):
+    """Algorithmic FLOPs of a P-token prefill: every linear layer on every token, causal
+    attention (QK^T and PV over positions 0..t for token t), lm_head on the last token."""
+    d, hd, L = cfg.dim, cfg.head_dim, cfg.n_layers
+    nq, nk = cfg.n_heads * hd, cfg.n_kv_heads * hd
+    linear = 2.0 * P * L * (d * (nq + 2 * nk) + nq * d + 3 * d * cfg.ffn)
+    attn = 4.0 * L * cfg.n_heads * hd * P * (P + 1) / 2
+    return linear + attn + 2.0 * d * cfg.vocab
+
+
 def gemv_time(torch, gtype, N, K, w_std=0.02, seed=4242, iters=256):
     """Average device time of one GEMV launch pair (activation kernel + GEMV, as in the decode
     step) over a CUDA graph of `iters` launches rotating through weight copies totalling more
@@ -304,7 +315,9 @@ def run_ours(args, dist):
     rng = np.random.default_rng(1234 + args.seed)
     prompt = rng.integers(0, cfg.vocab, P).tolist()
 
-    # prefill (device time)
+    # prefill (device time): one warm-up pass (buffer allocation, first-touch), then timed
+    eng.kv_reset()
+    eng.prefill(prompt, want_logits=False)
     eng.kv_reset()
     lg = eng.prefill(prompt)
     prefill_ms = eng.last_device_ms()
@@ -355,6 +368,8 @@ def run_ours(args, dist):
     e2e_tps = e2e_steps / e2e_s
 
     pk = peaks()
+    pk.setdefault("bf16_tflops_sustained", pk["bf16_tflops"])
+    pf_flops = prefill_flops(cfg, P)
     step_bytes = decode_bytes(cfg, kv_mean)
     ms_step = ms / args.steps
     achieved = step_bytes / (ms_step / 1000.0) / 1e9
@@ -388,7 +403,12 @@ def run_ours(args, dist):
         "gemv_c1": {"bound": "hbm", "kernel": "gemv_kernel Q4_K 4096x4096 (C1)", "us": round(gemv_us, 3),
                     "achieved": round(gemv_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "frac": round(gemv_gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": gemv_bytes},
-        "prefill": {"tokens": P, "ms": round(prefill_ms, 3), "tok_s": round(P / (prefill_ms / 1000.0), 1)},
+        "prefill": {"tokens": P, "ms": round(prefill_ms, 3), "tok_s": round(P / (prefill_ms / 1000.0), 1),
+                    "path": "batched tcgen05 GEMM + tensor-core causal attention, fp16 operands",
+                    "roofline": {"bound": "tensor", "achieved": round(pf_flops / (prefill_ms * 1e-3) / 1e12, 1),
+                                 "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                                 "frac": round(pf_flops / (prefill_ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
+                                 "algorithmic_flops": pf_flops, "peak_src": pk["src"] + " (sustained bf16)"}},
         "clocks": clk.summary(),
         "gpu_launches": launches_per_step * args.steps,
     }
