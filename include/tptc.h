@@ -96,6 +96,20 @@ typedef void (*tptc_progress_cb)(uint32_t done, uint32_t total, void* user);
  * tptc_nccl_unique_id and shared with the other ranks. */
 TPTC_API int tptc_create(int device, int tp_rank, int tp_size, const void* nccl_uid, tptc_ctx** out);
 TPTC_API int tptc_nccl_unique_id(void* out128);
+
+/* Megatron shard of one weight for rank `rank` of `size` (host only, no device): the rows
+ * [*r0, *r1) and input columns [*k0, *k1) of the full [N x K] matrix the loader keeps.
+ * Column-parallel q / k / v (by heads) and gate / up (by ffn rows); row-parallel o (by the
+ * heads' columns) and down (by ffn columns).  The reference has no tensor parallelism (one
+ * wgpu device, wgpu_engine.rs:62-124); this is the north_star's sharding.  Returns
+ * TPTC_ERR_UNSUPPORTED when the model does not split evenly (kv heads, or whole 256-blocks of
+ * the row-parallel K slices). */
+enum {
+    TPTC_SHARD_Q = 0, TPTC_SHARD_K = 1, TPTC_SHARD_V = 2, TPTC_SHARD_O = 3,
+    TPTC_SHARD_GATE = 4, TPTC_SHARD_UP = 5, TPTC_SHARD_DOWN = 6
+};
+TPTC_API int tptc_tp_shard(int which, int n_heads, int n_kv_heads, int head_dim, int dim, int ffn, int rank, int size,
+                           int* r0, int* r1, int* k0, int* k1);
 TPTC_API void tptc_destroy(tptc_ctx* ctx);
 TPTC_API const char* tptc_last_error(const tptc_ctx* ctx);
 /* Library version string and the number of CUDA devices (0 without a GPU). */

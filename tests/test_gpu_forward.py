@@ -252,3 +252,29 @@ def test_decode_argument_checks(engines):
         e.decode(10**6, 0)  # token out of range
     with pytest.raises(EngineError):
         e.decode(1, 5)  # position != KV length
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_gemv_chain_decode_is_bit_identical(tiny_models, cuda_device, monkeypatch, name):
+    """The GEMV-chain decode step (TPTC_DECODE_CHAIN=1: o, gate|up, down and the next q|k|v in
+    one persistent launch with grid barriers, activations built in every CTA) computes the
+    same bits as one launch per GEMV: same RMSNorm partition, same quantisation, same dots."""
+    from tpt_spark_b200.engine import CudaEngine
+
+    ref = O.Model(tiny_models[name])
+    prompt = [t % ref.vocab for t in PROMPT]
+    outs = []
+    for mode in ("1", "0"):
+        monkeypatch.setenv("TPTC_DECODE_CHAIN", mode)
+        with CudaEngine(0, kv_dtype="f16") as e:
+            e.load(tiny_models[name])
+            lg = [e.prefill(prompt)]
+            tok, pos = O.argmax(lg[0]), len(prompt)
+            for _ in range(16):
+                g, _ = e.decode(tok, pos)
+                lg.append(g)
+                tok, pos = O.argmax(g), pos + 1
+            lg.append(np.asarray(e.decode_greedy(tok, pos, 8), np.float32))
+            outs.append(lg)
+    for a, b in zip(*outs):
+        np.testing.assert_array_equal(a, b)

@@ -104,6 +104,19 @@ TPTC_API int tptc_set_kv_dtype(tptc_ctx* ctx, int ggml_type) {
     return s.ok() ? TPTC_OK : fail(ctx, s);
 }
 
+TPTC_API int tptc_tp_shard(int which, int n_heads, int n_kv_heads, int head_dim, int dim, int ffn, int rank, int size,
+                           int* r0, int* r1, int* k0, int* k1) {
+    if (!r0 || !r1 || !k0 || !k1) return TPTC_ERR_ARG;
+    int a, b, c, d;
+    if (!tptc::tp_shard(which, n_heads, n_kv_heads, head_dim, dim, ffn, rank, size, a, b, c, d))
+        return TPTC_ERR_UNSUPPORTED;
+    *r0 = a;
+    *r1 = b;
+    *k0 = c;
+    *k1 = d;
+    return TPTC_OK;
+}
+
 TPTC_API int tptc_set_prefill_gemm_min(tptc_ctx* ctx, int min_tokens) {
     if (!ctx) return TPTC_ERR_ARG;
     ctx->eng->set_prefill_gemm_min(min_tokens);

@@ -162,6 +162,8 @@ Status Engine::init(const void* nccl_uid) {
     CU(cudaHostAlloc(&h_err_, 64 * sizeof(int), cudaHostAllocDefault));
     const char* e = getenv("TPTC_PDL");
     pdl_ = !(e && e[0] == '0');
+    const char* ch = getenv("TPTC_DECODE_CHAIN");
+    chain_ = ch && ch[0] == '1';
     if (tp_size_ > 1) {
         tp_.reset(new Tp());
         RET_IF(tp_->init(tp_rank_, tp_size_, nccl_uid, stream_));
@@ -235,17 +237,19 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
     if (m.head_dim != 64 && m.head_dim != 96 && m.head_dim != 128)
         return err(TPTC_ERR_UNSUPPORTED, "head_dim must be 64, 96 or 128");
     if (m.dim % QK_K || m.ffn % QK_K) return err(TPTC_ERR_UNSUPPORTED, "embedding/ffn sizes must be multiples of 256");
-    if (m.n_kv_heads % tp_size_ || m.ffn % (QK_K * tp_size_))
-        return err(TPTC_ERR_UNSUPPORTED, "model does not shard evenly over tp_size=" + std::to_string(tp_size_));
+    int sh[7][4];
+    for (int w = 0; w < 7; w++)
+        if (!tp_shard(w, m.n_heads, m.n_kv_heads, m.head_dim, m.dim, m.ffn, tp_rank_, tp_size_, sh[w][0], sh[w][1],
+                      sh[w][2], sh[w][3]))
+            return err(TPTC_ERR_UNSUPPORTED, "model does not shard evenly over tp_size=" + std::to_string(tp_size_));
     m.tied = f.find("output.weight") == nullptr;
     meta_ = m;
     path_ = path;
     file_bytes_ = f.size;
 
-    const int tp = tp_size_, r = tp_rank_;
-    n_heads_l_ = m.n_heads / tp;
-    n_kv_l_ = m.n_kv_heads / tp;
-    const int hd = m.head_dim, ffn_l = m.ffn / tp, qd_l = n_heads_l_ * hd, kvd_l = n_kv_l_ * hd;
+    n_heads_l_ = m.n_heads / tp_size_;
+    n_kv_l_ = m.n_kv_heads / tp_size_;
+    const int hd = m.head_dim, ffn_l = m.ffn / tp_size_;
 
     // ---- tensor plan: name, expected shape, rows/cols this rank keeps, destination.
     // gate and up land in one fused gate|up matrix (logical rows [0, ffn_l) and [ffn_l,
@@ -267,14 +271,18 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         LayerWeights& L = layers_[l];
         const std::string p = "blk." + std::to_string(l) + ".";
         plans.push_back({p + "attn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.attn_norm, 0, 0});
-        plans.push_back({p + "attn_q.weight", m.n_heads * hd, m.dim, r * qd_l, (r + 1) * qd_l, 0, m.dim, &L.q, nullptr, 0, 0});
-        plans.push_back({p + "attn_k.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.k, nullptr, 0, 0});
-        plans.push_back({p + "attn_v.weight", m.n_kv_heads * hd, m.dim, r * kvd_l, (r + 1) * kvd_l, 0, m.dim, &L.v, nullptr, 0, 0});
-        plans.push_back({p + "attn_output.weight", m.dim, m.n_heads * hd, 0, m.dim, r * qd_l, (r + 1) * qd_l, &L.o, nullptr, 0, 0});
+        // rows / K windows from tp_shard (the same plan tptc_tp_shard exposes)
+        auto W = [&](int w, const char* name, int N, int K, DevMatrix* mat, int first_row, int glu_rows) {
+            plans.push_back({p + name, N, K, sh[w][0], sh[w][1], sh[w][2], sh[w][3], mat, nullptr, first_row, glu_rows});
+        };
+        W(TPTC_SHARD_Q, "attn_q.weight", m.n_heads * hd, m.dim, &L.q, 0, 0);
+        W(TPTC_SHARD_K, "attn_k.weight", m.n_kv_heads * hd, m.dim, &L.k, 0, 0);
+        W(TPTC_SHARD_V, "attn_v.weight", m.n_kv_heads * hd, m.dim, &L.v, 0, 0);
+        W(TPTC_SHARD_O, "attn_output.weight", m.dim, m.n_heads * hd, &L.o, 0, 0);
         plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm, 0, 0});
-        plans.push_back({p + "ffn_gate.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.glu, nullptr, 0, 2 * ffn_l});
-        plans.push_back({p + "ffn_up.weight", m.ffn, m.dim, r * ffn_l, (r + 1) * ffn_l, 0, m.dim, &L.glu, nullptr, ffn_l, 2 * ffn_l});
-        plans.push_back({p + "ffn_down.weight", m.dim, m.ffn, 0, m.dim, r * ffn_l, (r + 1) * ffn_l, &L.down, nullptr, 0, 0});
+        W(TPTC_SHARD_GATE, "ffn_gate.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l);
+        W(TPTC_SHARD_UP, "ffn_up.weight", m.ffn, m.dim, &L.glu, ffn_l, 2 * ffn_l);
+        W(TPTC_SHARD_DOWN, "ffn_down.weight", m.dim, m.ffn, &L.down, 0, 0);
     }
     plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_, 0, 0});
     if (!m.tied) plans.push_back({"output.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &output_, nullptr, 0, 0});
@@ -379,6 +387,8 @@ Status Engine::alloc_runtime() {
     const size_t o_cnt = take((size_t)n_kv_l_ * 4);
     const int k_max = std::max(m.dim, std::max(m.ffn / tp_size_, n_heads_l_ * hd));
     const size_t o_act = take(gemv_act_bytes_max(k_max));
+    const size_t o_cbar = take((size_t)(L + 1) * kChainMaxPhases * 4);
+    const size_t o_bval = take((size_t)2 * sm_count_ * 4), o_bidx = take((size_t)2 * sm_count_ * 4);
     rt_size_ = off;
     cudaError_t ce = cudaMalloc(&rt_, rt_size_);
     if (ce != cudaSuccess) {
@@ -406,6 +416,9 @@ Status Engine::alloc_runtime() {
     attn_partial_ = reinterpret_cast<float*>(rt_ + o_part);
     attn_counters_ = reinterpret_cast<int*>(rt_ + o_cnt);
     act_ = rt_ + o_act;
+    chain_bar_ = reinterpret_cast<int*>(rt_ + o_cbar);
+    best_val_ = reinterpret_cast<float*>(rt_ + o_bval);
+    best_idx_ = reinterpret_cast<int*>(rt_ + o_bidx);
 
     // candle quantized_llama precomput_freqs_cis: theta_i = 1/base^(2i/hd) (f32 powf),
     // angle = pos * theta_i, cos/sin in f32 -- built on the host with the C library's powf,
@@ -424,6 +437,9 @@ Status Engine::alloc_runtime() {
     CU(cudaMemcpyAsync(rope_cos_, c.data(), c.size() * 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaMemcpyAsync(rope_sin_, s.data(), s.size() * 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaStreamSynchronize(stream_));
+    // the row-parallel partial buffer is baked into the graphs: allocate it before capture
+    // (cudaMalloc is not allowed while a stream is capturing)
+    if (tp_ && !tp_->partial(m.dim)) return err(TPTC_ERR_OOM, "tensor-parallel partial buffer");
     RET_IF(build_decode_graph(false, &graph_plain_));
     RET_IF(build_decode_graph(true, &graph_chained_));
     return {};
@@ -434,40 +450,81 @@ Status Engine::alloc_runtime() {
 // device scalar pos_, so one captured graph serves every step.
 Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
     const ModelMeta& m = meta_;
-    const int hd = m.head_dim;
+    const int hd = m.head_dim, L = m.n_layers;
     const size_t layer_kv = (size_t)2 * n_kv_l_ * max_seq_ * hd * kv_elem_bytes();  // bytes
-    CU(launch_embed_row(embd_, tok_in_, x_, st, false));
-    for (int l = 0; l < m.n_layers; l++) {
-        const LayerWeights& L = layers_[l];
-        uint8_t* kc = kv_ + l * layer_kv;
-        uint8_t* vc = kc + layer_kv / 2;
+    auto kcache = [&](int l) { return kv_ + l * layer_kv; };
+    auto vcache = [&](int l) { return kv_ + l * layer_kv + layer_kv / 2; };
+    auto base = [&](int K) {
         GemvParams p = {};
-        p.K = m.dim;
+        p.K = K;
         p.err = err_;
         p.act_global = act_;
         p.eps = m.rms_eps;
-        // q | k | v with fused RMSNorm; v goes straight into the cache, q and k are rotated
-        // by the attention kernel
+        p.nseg = 1;
+        return p;
+    };
+    // q | k | v with fused RMSNorm; v goes straight into the cache, q and k are rotated by
+    // the attention kernel
+    auto qkv_params = [&](int l) {
+        const LayerWeights& W = layers_[l];
+        GemvParams p = base(m.dim);
         p.nseg = 3;
-        const DevMatrix* qkv[3] = {&L.q, &L.k, &L.v};
-        for (int s = 0; s < 3; s++) p.seg[s] = GemvSeg{*qkv[s], 0};
+        const DevMatrix* qkv[3] = {&W.q, &W.k, &W.v};
+        for (int i = 0; i < 3; i++) p.seg[i] = GemvSeg{*qkv[i], 0};
         p.x = x_;
-        p.norm_w = L.attn_norm;
+        p.norm_w = W.attn_norm;
         p.out = qbuf_;
         p.kraw = kraw_;
-        p.vcache = vc;
+        p.vcache = vcache(l);
         p.kv_f32 = kv_f32_ ? 1 : 0;
         p.pos = pos_;
         p.hd = hd;
         p.max_seq = max_seq_;
         gemv_prepare(p, sm_count_);
-        CU(gemv_launch(p, EPI_QKV, st, pdl_));
-
+        return p;
+    };
+    auto o_params = [&](int l) {
+        GemvParams p = base(n_heads_l_ * hd);
+        p.seg[0] = GemvSeg{layers_[l].o, 0};
+        p.x = attn_;
+        p.out = tp_ ? tp_->partial(m.dim) : x_;  // row-parallel: partial sums, then allreduce
+        gemv_prepare(p, sm_count_);
+        return p;
+    };
+    auto glu_params = [&](int l) {
+        GemvParams p = base(m.dim);
+        p.seg[0] = GemvSeg{layers_[l].glu, 0};
+        p.x = x_;
+        p.norm_w = layers_[l].ffn_norm;
+        p.out = h_;
+        gemv_prepare(p, sm_count_);
+        return p;
+    };
+    auto down_params = [&](int l) {
+        GemvParams p = base(m.ffn / tp_size_);
+        p.seg[0] = GemvSeg{layers_[l].down, 0};
+        p.x = h_;
+        p.out = tp_ ? tp_->partial(m.dim) : x_;
+        gemv_prepare(p, sm_count_);
+        return p;
+    };
+    auto head_params = [&]() {
+        GemvParams p = base(m.dim);
+        p.seg[0] = GemvSeg{output_, 0};
+        p.x = x_;
+        p.norm_w = out_norm_;
+        p.out = logits_;
+        gemv_prepare(p, sm_count_);
+        return p;
+    };
+    // attention of layer l; when every kv head's output is whole 256-blocks the kernel also
+    // writes the o projection's activation itself (q8k / q80 / f32 as the o matrix needs)
+    auto attn_params = [&](int l, GemvParams& o) {
         AttnDecodeParams a = {};
         a.q = qbuf_;
         a.kraw = kraw_;
-        a.kcache = kc;
-        a.vcache = vc;
+        a.kcache = kcache(l);
+        a.vcache = vcache(l);
         a.kv_f32 = kv_f32_ ? 1 : 0;
         a.rope_cos = rope_cos_;
         a.rope_sin = rope_sin_;
@@ -483,18 +540,6 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         a.splits = attn_splits_;
         a.scale = (float)(1.0 / sqrt((double)hd));
         a.err = err_;
-
-        GemvParams o = {};
-        o.K = n_heads_l_ * hd;
-        o.err = err_;
-        o.act_global = act_;
-        o.nseg = 1;
-        o.seg[0] = GemvSeg{L.o, 0};
-        o.x = attn_;
-        o.out = tp_ ? tp_->partial(m.dim) : x_;  // row-parallel: partial sums, then allreduce
-        gemv_prepare(o, sm_count_);
-        // the attention kernel writes the o projection's activation itself when every kv
-        // head's output is whole 256-blocks (q8k / q80 / f32 as the o matrix needs)
         if ((n_heads_l_ / n_kv_l_) * hd % 256 == 0) {
             a.act_out = act_;
             a.act = o.act;
@@ -502,6 +547,82 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
             a.act_nb = o.K / 256;
             o.act_prepared = 1;
         }
+        return a;
+    };
+    auto trace_layer = [&](int l) -> Status {
+        if (!trace) return {};
+        CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 0) * m.dim, qrot_, (size_t)n_heads_l_ * hd * 4,
+                           cudaMemcpyDeviceToHost, st));
+        CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 1) * m.dim, attn_, (size_t)n_heads_l_ * hd * 4,
+                           cudaMemcpyDeviceToHost, st));
+        CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 2) * m.dim, x_, (size_t)m.dim * 4, cudaMemcpyDeviceToHost, st));
+        return {};
+    };
+
+    bool use_chain = chain_ && !tp_;
+    if (use_chain) {  // the chains with the largest activation / stage (the widest layer, the head)
+        ChainParams t = {};
+        t.ph[0] = o_params(L - 1);
+        t.ph[1] = glu_params(L - 1);
+        t.ph[2] = down_params(L - 1);
+        t.ph[3] = head_params();
+        t.nph = 4;
+        chain_prepare(t, sm_count_);
+        use_chain = chain_fits(t, sm_count_);
+        t.ph[3] = qkv_params(0);
+        chain_prepare(t, sm_count_);
+        use_chain = use_chain && chain_fits(t, sm_count_);
+    }
+    CU(launch_embed_row(embd_, tok_in_, x_, st, false));
+    if (use_chain) {
+        // GEMV chains: [q|k|v(0)], then per layer attention(l) and one chain
+        // [o(l), gate|up(l), down(l), q|k|v(l+1) or lm_head + argmax]
+        ChainParams c0 = {};
+        c0.ph[0] = qkv_params(0);
+        c0.epi[0] = EPI_QKV;
+        c0.nph = 1;
+        c0.bar = chain_bar_;
+        c0.err = err_;
+        chain_prepare(c0, sm_count_);
+        CU(chain_launch(c0, st, pdl_));
+        for (int l = 0; l < L; l++) {
+            GemvParams o = o_params(l);
+            const AttnDecodeParams a = attn_params(l, o);
+            CU(launch_attn_decode(a, st, pdl_));
+            ChainParams c = {};
+            c.ph[0] = o;
+            c.epi[0] = EPI_RESID;
+            c.ph[1] = glu_params(l);
+            c.epi[1] = EPI_GLU;
+            c.ph[2] = down_params(l);
+            c.epi[2] = EPI_RESID;
+            if (l + 1 < L) {
+                c.ph[3] = qkv_params(l + 1);
+                c.epi[3] = EPI_QKV;
+            } else {
+                c.ph[3] = head_params();
+                c.epi[3] = EPI_STORE;
+                c.best_val = best_val_;
+                c.best_idx = best_idx_;
+                c.out_tok = tok_out_;
+                c.next_tok = chained ? tok_in_ : nullptr;
+                c.pos = chained ? pos_ : nullptr;
+                c.history = chained ? history_ : nullptr;
+            }
+            c.nph = 4;
+            c.bar = chain_bar_ + (size_t)(l + 1) * kChainMaxPhases;
+            c.err = err_;
+            chain_prepare(c, sm_count_);
+            CU(chain_launch(c, st, pdl_));
+            RET_IF(trace_layer(l));
+        }
+        return {};
+    }
+    for (int l = 0; l < L; l++) {
+        GemvParams p = qkv_params(l);
+        CU(gemv_launch(p, EPI_QKV, st, pdl_));
+        GemvParams o = o_params(l);
+        const AttnDecodeParams a = attn_params(l, o);
         CU(launch_attn_decode(a, st, pdl_));
         if (tp_) {
             CU(gemv_launch(o, EPI_STORE, st, pdl_));
@@ -509,54 +630,18 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         } else {
             CU(gemv_launch(o, EPI_RESID, st, pdl_));
         }
-
-        GemvParams d = {};
-        d.K = m.ffn / tp_size_;
-        d.err = err_;
-        d.act_global = act_;
-        d.nseg = 1;
-        d.seg[0] = GemvSeg{L.down, 0};
-        d.x = h_;
-        d.out = tp_ ? tp_->partial(m.dim) : x_;  // row-parallel: partial sums, then allreduce
-        gemv_prepare(d, sm_count_);
-
-        GemvParams g = {};
-        g.K = m.dim;
-        g.err = err_;
-        g.act_global = act_;
-        g.eps = m.rms_eps;
-        g.nseg = 1;
-        g.seg[0] = GemvSeg{L.glu, 0};
-        g.x = x_;
-        g.norm_w = L.ffn_norm;
-        g.out = h_;
-        gemv_prepare(g, sm_count_);
+        GemvParams g = glu_params(l);
         CU(gemv_launch(g, EPI_GLU, st, pdl_));
+        GemvParams d = down_params(l);
         if (tp_) {
             CU(gemv_launch(d, EPI_STORE, st, pdl_));
             RET_IF(tp_->allreduce_add(d.out, x_, m.dim, st));
         } else {
             CU(gemv_launch(d, EPI_RESID, st, pdl_));
         }
-        if (trace) {
-            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 0) * m.dim, qrot_, (size_t)n_heads_l_ * hd * 4,
-                               cudaMemcpyDeviceToHost, st));
-            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 1) * m.dim, attn_, (size_t)n_heads_l_ * hd * 4,
-                               cudaMemcpyDeviceToHost, st));
-            CU(cudaMemcpyAsync(trace + (size_t)(l * 3 + 2) * m.dim, x_, (size_t)m.dim * 4, cudaMemcpyDeviceToHost, st));
-        }
+        RET_IF(trace_layer(l));
     }
-    GemvParams h = {};
-    h.K = m.dim;
-    h.err = err_;
-    h.act_global = act_;
-    h.eps = m.rms_eps;
-    h.nseg = 1;
-    h.seg[0] = GemvSeg{output_, 0};
-    h.x = x_;
-    h.norm_w = out_norm_;
-    h.out = logits_;
-    gemv_prepare(h, sm_count_);
+    GemvParams h = head_params();
     CU(gemv_launch(h, EPI_STORE, st, pdl_));
     CU(launch_argmax(logits_, m.vocab, tok_out_, chained ? tok_in_ : nullptr, chained ? pos_ : nullptr,
                      chained ? history_ : nullptr, st, pdl_));
@@ -596,6 +681,8 @@ Status Engine::check_err() {
     if (*h_err_ != 0) {
         const int code = *h_err_;
         cudaMemsetAsync(err_, 0, sizeof(int), stream_);
+        // a chain that gave up leaves its arrival counters mid-count
+        if (chain_bar_) cudaMemsetAsync(chain_bar_, 0, (size_t)(meta_.n_layers + 1) * kChainMaxPhases * 4, stream_);
         cudaStreamSynchronize(stream_);
         return err(code == TPTC_ERR_TIMEOUT ? TPTC_ERR_TIMEOUT : TPTC_ERR_CUDA,
                    "a device-side bounded wait gave up (status " + std::to_string(code) + ")");

@@ -99,6 +99,7 @@ class Engine {
     int sm_count_ = 148;
     bool loaded_ = false;
     bool pdl_ = true;
+    bool chain_ = false;  // single-GPU decode step as GEMV chains (TPTC_DECODE_CHAIN=1; default: one launch per GEMV)
     cudaStream_t stream_ = nullptr;
     ModelMeta meta_;
     std::string path_;
@@ -132,6 +133,9 @@ class Engine {
     int* pos_ = nullptr;
     int* err_ = nullptr;
     uint8_t* act_ = nullptr;  // prepared GEMV activation (gemv_launch)
+    int* chain_bar_ = nullptr;     // [L + 1][kChainMaxPhases] chain arrival counters
+    float* best_val_ = nullptr;    // [2 * SMs] per-CTA argmax partials of the lm_head chain
+    int* best_idx_ = nullptr;
     float* attn_partial_ = nullptr;
     int* attn_counters_ = nullptr;
     int attn_splits_ = 1;

@@ -413,36 +413,26 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
     // norm, this thread's share of the sum of squares
     if (mine) load8(p.x + b * QK_K + 8 * lane, v);
     if (norm) {
-        constexpr int kMaxF4 = 8;  // float4 per thread kept in flight (K <= 8192 in one pass)
-        float4 xs[kMaxF4], us[kMaxF4];
+        static_assert(kActWarps == kNormWarps, "the activation kernel uses the chains' norm partition");
+        // every CTA sums the whole vector in the shared partition (blocks warp, warp + 8, ...)
         float ss = 0.f;
-        for (int base = tid * 4; base < K; base += kActWarps * 32 * 4 * kMaxF4) {
+        for (int bb = warp; bb < nb; bb += kActWarps) {
+            float xv[8];
+            load8(p.x + bb * QK_K + 8 * lane, xv);
+            if (p.glu_in) {
+                float u[8];
+                load8(p.x + K + bb * QK_K + 8 * lane, u);
 #pragma unroll
-            for (int j = 0; j < kMaxF4; j++) {
-                const int i = base + j * kActWarps * 32 * 4;
-                if (i < K) {
-                    xs[j] = *reinterpret_cast<const float4*>(p.x + i);
-                    if (p.glu_in) us[j] = *reinterpret_cast<const float4*>(p.x + K + i);
-                }
+                for (int i = 0; i < 8; i++) xv[i] = glu_val(xv[i], u[i]);
             }
-#pragma unroll
-            for (int j = 0; j < kMaxF4; j++) {
-                const int i = base + j * kActWarps * 32 * 4;
-                if (i < K) {
-                    float4 x4 = xs[j];
-                    if (p.glu_in)
-                        x4 = make_float4(glu_val(x4.x, us[j].x), glu_val(x4.y, us[j].y), glu_val(x4.z, us[j].z),
-                                         glu_val(x4.w, us[j].w));
-                    ss += x4.x * x4.x + x4.y * x4.y + x4.z * x4.z + x4.w * x4.w;
-                }
-            }
+            ss = __fadd_rn(ss, sumsq8(xv));
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kActWarps; w++) tot += red[w];
+        for (int w = 0; w < kActWarps; w++) tot = __fadd_rn(tot, red[w]);
         const float m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
         if (mine) {
             if (p.glu_in) {
@@ -464,88 +454,114 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
     act_store_block(p.act, transposed, nb, p.act_global, b, v, lane);
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
-    __shared__ float glu_up[2][4];
-    int unit_no = 0;
+// A CTA's weight ring: S stages of stage_bytes after the activation region, with their
+// "full" (copy landed) and "empty" (every consumer warp done) mbarriers.  Producer and
+// consumers walk it with the same position (stage s, wrap count lap: parity source).
+struct Ring {
+    uint8_t* base;
+    int stage_bytes, S;
+    uint64_t* full;
+    uint64_t* empty;
+};
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int S = p.stages;
-    const int nsb = p.K / QK_K;
-    uint8_t* ring = smem + p.act.bytes;
-
-    if (tid == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        mbar_init(&actbar, 1);
-        fence_mbar_init();
+// Bounded wait that yields between polls and gives up early once the CTA has aborted.
+__device__ __forceinline__ bool wait_backoff_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        __nanosleep(64);
     }
-    __syncthreads();
+    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
+    *abort_flag = 1;
+    return false;
+}
 
-    if (warp == kConsumerWarps) {
-        // ---------------- producer: one bulk copy per stage (a whole 8-row tile), weights
-        // only, so it runs ahead of griddepcontrol.wait
-        if (lane == 0) {
-            const uint64_t policy = l2_evict_first_policy();
-            int s = 0, lap = 0;  // ring stage and how many times the ring has wrapped
-            // units in pairs (u, u + grid), chunk by chunk: the order the consumers take them
-            for (int u = blockIdx.x; u < p.units;) {
-                const bool two = unit_pair(p, u, EPI);
-                // a pair goes chunk by chunk alternating its two units; a single unit alone
-                for (int i = 0; i < (two ? 2 : 1) * p.nchunks; i++) {
-                    const int c = two ? i >> 1 : i, k = two ? i & 1 : 0;
-                    {
-                        const int uk = u + k * gridDim.x, s_ = unit_seg(p, uk);
-                        const DevMatrix& m = p.seg[s_].m;
-                        const int sbb = sb_bytes(m.type);
-                        const int64_t tile0 = (int64_t)(uk - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
-                        if (lap > 0 && !mbar_wait_backoff(&empty[s], (lap - 1) & 1, p.err)) return;
-                        const int cb = min(p.cbs, nsb - c * p.cbs);
-                        const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
-                        mbar_expect_tx(&full[s], bytes);
-                        bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
-                                 &full[s], policy);
-                        if (++s == S) {
-                            s = 0;
-                            lap++;
-                        }
-                    }
-                }
-                u += (two ? 2 : 1) * gridDim.x;
+__device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
+    *abort_flag = 1;
+    return false;
+}
+
+// Producer lane: the weight tiles of this CTA's units of GEMV p, one bulk copy per stage,
+// in the order the consumers take them -- units in pairs (u, u + grid) chunk by chunk
+// alternating when unit_pair holds, a single unit alone otherwise.  Weights do not depend on
+// any earlier kernel or phase, so this runs ahead of every wait the consumers do.  Returns
+// false once a wait for a free stage gave up (or the CTA aborted).
+__device__ bool produce_units(const GemvParams& p, int epi, const Ring& r, int& s, int& lap, uint64_t policy,
+                              volatile int* abort_flag) {
+    const int nsb = p.K / QK_K;
+    for (int u = blockIdx.x; u < p.units;) {
+        const bool two = unit_pair(p, u, epi);
+        for (int i = 0; i < (two ? 2 : 1) * p.nchunks; i++) {
+            const int c = two ? i >> 1 : i, k = two ? i & 1 : 0;
+            const int uk = u + k * gridDim.x, s_ = unit_seg(p, uk);
+            const DevMatrix& m = p.seg[s_].m;
+            const int sbb = sb_bytes(m.type);
+            const int64_t tile0 = (int64_t)(uk - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
+            if (lap > 0 && !wait_backoff_abort(&r.empty[s], (lap - 1) & 1, p.err, abort_flag)) return false;
+            const int cb = min(p.cbs, nsb - c * p.cbs);
+            const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
+            mbar_expect_tx(&r.full[s], bytes);
+            bulk_g2s(r.base + s * r.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
+                     &r.full[s], policy);
+            if (++s == r.S) {
+                s = 0;
+                lap++;
             }
         }
-        return;
+        u += (two ? 2 : 1) * gridDim.x;
     }
+    return true;
+}
 
-    // ---------------- consumers: one warp per tile row
-    pdl_wait();
-    // The next kernel may start (and prefetch its weights) only once this one is past its
-    // own wait, so at most two kernels of a chain overlap.
-    pdl_launch_dependents();
-    // the activation, prepared by act_quant_kernel in this region's layout: one bulk copy
-    if (tid == 0) {
-        mbar_expect_tx(&actbar, (uint32_t)p.act.bytes);
-        bulk_g2s(smem, p.act_global, (uint32_t)p.act.bytes, &actbar, 0);
-    }
-    bool timed_out = !mbar_wait_bounded(&actbar, 0, p.err);
+// Producer lane, before the CTA may exit: every copy it issued has landed (bounded; the
+// normal path finds them all complete already, the consumers having waited for them).
+__device__ void drain_ring(const Ring& r, int s, int lap) {
+    const int n = lap * r.S + s;  // stages issued
+    for (int j = n > r.S ? n - r.S : 0; j < n; j++) mbar_wait_bounded(&r.full[j % r.S], (j / r.S) & 1, nullptr);
+}
 
+__device__ __forceinline__ Act act_view(const ActLayout& L, const uint8_t* smem) {
     Act a;
-    a.f32 = p.act.f32 >= 0 ? reinterpret_cast<const float*>(smem + p.act.f32) : nullptr;
-    a.q8k = p.act.q8k >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q8k) : nullptr;
-    a.q8k_d = p.act.q8k >= 0 ? reinterpret_cast<const float*>(smem + p.act.q8k_d) : nullptr;
-    a.q8k_bs = p.act.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act.q8k_bs) : nullptr;
-    a.q8k_ps = p.act.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act.q8k_ps) : nullptr;
-    a.q80 = p.act.q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q80) : nullptr;
-    a.q80_d = p.act.q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act.q80_d) : nullptr;
+    a.f32 = L.f32 >= 0 ? reinterpret_cast<const float*>(smem + L.f32) : nullptr;
+    a.q8k = L.q8k >= 0 ? reinterpret_cast<const int8_t*>(smem + L.q8k) : nullptr;
+    a.q8k_d = L.q8k >= 0 ? reinterpret_cast<const float*>(smem + L.q8k_d) : nullptr;
+    a.q8k_bs = L.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + L.q8k_bs) : nullptr;
+    a.q8k_ps = L.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + L.q8k_ps) : nullptr;
+    a.q80 = L.q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + L.q80) : nullptr;
+    a.q80_d = L.q80 >= 0 ? reinterpret_cast<const float*>(smem + L.q80_d) : nullptr;
+    return a;
+}
 
-    // Units in pairs (u, u + grid): for every chunk the producer fills the pair's two stages
-    // back to back, and a warp reduces its row of both in one pass; with the same weight type
-    // the two dot products share the lane's activation slice (same columns).
-    int s = 0, lap = 0;  // ring stage and its phase parity source
+// Running greedy pick of the rows a warp wrote (lane 0): candle sample_argmax keeps the last
+// of equal maxima, so ties go to the higher row.
+struct ArgBest {
+    float v;
+    int i;
+};
+__device__ __forceinline__ void argbest_take(ArgBest& b, float v, int i) {
+    if (b.i < 0 || v > b.v || (v == b.v && i > b.i)) {
+        b.v = v;
+        b.i = i;
+    }
+}
+
+// Consumer warps: this CTA's units of GEMV p from the ring, one warp per tile row.  Units in
+// pairs (u, u + grid): for every chunk the producer filled the pair's two stages back to back
+// and a warp reduces its row of both in one pass; with the same weight type the two dot
+// products share the lane's activation slice (same columns).  Once a wait gives up the warps
+// skip the arithmetic but keep the loop's barriers (the gate|up pair barrier) and stage
+// releases, so every warp leaves together.  `best` (EPI_STORE): argmax of the rows written.
+template <int EPI>
+__device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a, const Ring& r, int& s, int& lap,
+                                              int& unit_no, float (&glu_up)[2][4], ArgBest* best,
+                                              volatile int* abort_flag, bool& timed_out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nsb = p.K / QK_K;
     auto epilogue = [&](const UnitRow& ur, float acc) {
         if (EPI == EPI_DOTS) return;
         const float y = warp_sum(acc);
@@ -556,16 +572,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             const int buf = unit_no & 1;
             if (warp >= 4 && lane == 0) glu_up[buf][warp - 4] = y;
             pair_sync(warp & 3);
-            if (warp < 4 && lane == 0 && ur.seg >= 0)
+            if (warp < 4 && lane == 0 && ur.seg >= 0 && !timed_out)
                 p.out[ur.out] = __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
             unit_no++;
             return;
         }
-        if (lane != 0 || ur.seg < 0) return;
+        if (lane != 0 || ur.seg < 0 || timed_out) return;
         if (EPI == EPI_STORE) {
             p.out[ur.row] = y;
+            if (best) argbest_take(*best, y, ur.row);
         } else if (EPI == EPI_RESID) {
-            p.out[ur.out] += y;
+            p.out[ur.out] = __ldcg(p.out + ur.out) + y;
         } else if (EPI == EPI_QKV) {
             if (ur.seg == 0) {
                 p.out[ur.row] = y;  // q before RoPE
@@ -623,29 +640,28 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         const DevMatrix& ma = p.seg[unit_seg(p, u)].m;
         const DevMatrix& mb = p.seg[unit_seg(p, two ? u2 : u)].m;
         const int ty = ma.type;
-        const bool paired = two;
         float acca = 0.f, accb = 0.f;
         for (int c = 0; c < p.nchunks; c++) {
             const int sa = s;
-            if (!timed_out && !mbar_wait_bounded(&full[sa], lap & 1, p.err)) timed_out = true;
-            if (++s == S) {
+            if (!timed_out && !wait_abort(&r.full[sa], lap & 1, p.err, abort_flag)) timed_out = true;
+            if (++s == r.S) {
                 s = 0;
                 lap++;
             }
             int sb2 = sa;
             if (two) {
                 sb2 = s;
-                if (!timed_out && !mbar_wait_bounded(&full[sb2], lap & 1, p.err)) timed_out = true;
-                if (++s == S) {
+                if (!timed_out && !wait_abort(&r.full[sb2], lap & 1, p.err, abort_flag)) timed_out = true;
+                if (++s == r.S) {
                     s = 0;
                     lap++;
                 }
             }
             if (!timed_out) {
                 const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
-                const uint8_t* stA = ring + sa * p.stage_bytes;
-                const uint8_t* stB = ring + sb2 * p.stage_bytes;
-                if (paired) {
+                const uint8_t* stA = r.base + sa * r.stage_bytes;
+                const uint8_t* stB = r.base + sb2 * r.stage_bytes;
+                if (two) {
                     if (lane < 2 * cb) {
                         const int sbm = sb_main_bytes(ty), sbd = sb_d_bytes(ty);
                         XHalf xh;
@@ -662,19 +678,302 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                     }
                 } else {
                     acca += single(ma, ra, stA, c0, cb);
-                    if (two) accb += single(mb, rb, stB, c0, cb);
                 }
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&empty[sa]);
-                if (two) mbar_arrive(&empty[sb2]);
+                mbar_arrive(&r.empty[sa]);
+                if (two) mbar_arrive(&r.empty[sb2]);
             }
         }
         epilogue(ra, acca);
         if (two) epilogue(rb, accb);
         u += (two ? 2 : 1) * gridDim.x;
     }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
+    __shared__ float glu_up[2][4];
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const Ring r{smem + p.act.bytes, p.stage_bytes, p.stages, full, empty};
+
+    if (tid == 0) {
+        for (int s = 0; s < r.S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        mbar_init(&actbar, 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            int s = 0, lap = 0;
+            produce_units(p, EPI, r, s, lap, l2_evict_first_policy(), &abort_flag);
+            drain_ring(r, s, lap);
+        }
+        return;
+    }
+
+    pdl_wait();
+    // The next kernel may start (and prefetch its weights) only once this one is past its
+    // own wait, so at most two kernels of a chain overlap.
+    pdl_launch_dependents();
+    // the activation, prepared by act_quant_kernel in this region's layout: one bulk copy
+    if (tid == 0) {
+        mbar_expect_tx(&actbar, (uint32_t)p.act.bytes);
+        bulk_g2s(smem, p.act_global, (uint32_t)p.act.bytes, &actbar, 0);
+    }
+    bool timed_out = !wait_abort(&actbar, 0, p.err, &abort_flag);
+    const Act a = act_view(p.act, smem);
+    int s = 0, lap = 0, unit_no = 0;
+    consume_units<EPI>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out);
+}
+
+// ---------------------------------------------------------------- GEMV chains
+//
+// A chain runs several GEMVs of a decode step in one persistent launch (o_proj, gate|up,
+// down, the next layer's q|k|v or the lm_head): between phases every CTA arrives on a global
+// counter and waits (bounded) until all have, then builds the next phase's activation
+// itself from the vector the previous phase completed (RMSNorm + quantisation, the
+// arithmetic of act_quant_kernel).  The producer warp streams weights across the phase
+// boundaries without waiting for them, so the HBM stream does not drain between GEMVs.
+
+__device__ __forceinline__ bool consumer_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kConsumers)
+        : "memory");
+    return r != 0;
+}
+
+// Bounded wait until *ctr >= target (acquire).  Gives up after kWaitPolls polls.
+__device__ __forceinline__ bool spin_count(const int* ctr, int target, int* err, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        if (*abort_flag) return false;
+        if (i > 4096) __nanosleep(64);
+    }
+    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
+    return false;
+}
+
+// Phase activation built by the CTA's consumers from p.x (written before the phase barrier,
+// read through L2): optional RMSNorm with p.norm_w and quantisation into `act` in p.act's
+// layout, with the norm partition and arithmetic of act_quant_kernel (same m, same codes).
+// Vectors of up to 32 blocks are read once and held in registers (one L2 round trip); the
+// norm gains, which no phase writes, are fetched before the caller's barrier (w_pre).
+constexpr int kActHold = 4;  // blocks per warp held in registers
+__device__ __forceinline__ void prefetch_norm(const GemvParams& p, float (&w_pre)[kActHold][8]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = p.K / QK_K;
+    if (!p.norm_w) return;
+#pragma unroll
+    for (int j = 0; j < kActHold; j++) {
+        const int b = warp + j * kConsumerWarps;
+        if (b < nb) load8(p.norm_w + b * QK_K + 8 * lane, w_pre[j]);
+    }
+}
+
+__device__ __forceinline__ void ldcg8(const float* src, float (&v)[8]) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ void build_act_local(const GemvParams& p, uint8_t* act, float* red, const float (&w_pre)[kActHold][8]) {
+    const int K = p.K, nb = K / QK_K, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool norm = p.norm_w != nullptr;
+    float v[kActHold][8];
+    int bi[kActHold];
+#pragma unroll
+    for (int j = 0; j < kActHold; j++) {
+        bi[j] = warp + j * kConsumerWarps;
+        if (bi[j] < nb) ldcg8(p.x + bi[j] * QK_K + 8 * lane, v[j]);
+        else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[j][i] = 0.f;
+        }
+    }
+    float m = 1.f;
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kActHold; j++)
+            if (bi[j] < nb) ss = __fadd_rn(ss, sumsq8(v[j]));
+        for (int b = warp + kActHold * kConsumerWarps; b < nb; b += kConsumerWarps) {  // vectors over 32 blocks
+            float t[8];
+            ldcg8(p.x + b * QK_K + 8 * lane, t);
+            ss = __fadd_rn(ss, sumsq8(t));
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        consumer_sync();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; w++) tot = __fadd_rn(tot, red[w]);
+        m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
+#pragma unroll
+        for (int j = 0; j < kActHold; j++)
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fdiv_rn(v[j][i], m), w_pre[j][i]);
+    }
+    {
+        const int b01[2] = {bi[0], bi[1]}, b23[2] = {bi[2], bi[3]};
+        act_store_blocks<2>(p.act, 1, nb, act, b01, *reinterpret_cast<const float(*)[2][8]>(&v[0]), lane);
+        if (bi[2] < nb) act_store_blocks<2>(p.act, 1, nb, act, b23, *reinterpret_cast<const float(*)[2][8]>(&v[2]), lane);
+    }
+    // blocks beyond the held ones, two at a time
+    for (int b0 = warp + kActHold * kConsumerWarps; b0 < nb; b0 += 2 * kConsumerWarps) {
+        const int bb[2] = {b0, b0 + kConsumerWarps};
+        float t[2][8];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            if (bb[k] < nb) {
+                ldcg8(p.x + bb[k] * QK_K + 8 * lane, t[k]);
+                if (norm) {
+                    float w8[8];
+                    load8(p.norm_w + bb[k] * QK_K + 8 * lane, w8);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) t[k][i] = __fmul_rn(__fdiv_rn(t[k][i], m), w8[i]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) t[k][i] = 0.f;
+            }
+        }
+        act_store_blocks<2>(p.act, 1, nb, act, bb, t, lane);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_constant__ ChainParams c) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
+    __shared__ float glu_up[2][4];
+    __shared__ float red[kConsumerWarps];
+    __shared__ int redi[kConsumerWarps];
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const Ring r{smem + c.act_bytes, c.stage_bytes, c.stages, full, empty};
+
+    if (tid == 0) {
+        for (int s = 0; s < r.S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        mbar_init(&actbar, 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            int s = 0, lap = 0;
+            const uint64_t policy = l2_evict_first_policy();
+            for (int ph = 0; ph < c.nph; ph++)
+                if (!produce_units(c.ph[ph], c.epi[ph], r, s, lap, policy, &abort_flag)) break;
+            drain_ring(r, s, lap);
+        }
+        return;
+    }
+
+    pdl_wait();
+    int s = 0, lap = 0, unit_no = 0;
+    uint32_t actphase = 0;
+    bool timed_out = false;
+    ArgBest best{-INFINITY, -1};
+    for (int ph = 0; ph < c.nph; ph++) {
+        const GemvParams& p = c.ph[ph];
+        if (ph == c.nph - 1) pdl_launch_dependents();
+        float w_pre[kActHold][8];
+        if (!p.act_prepared) prefetch_norm(p, w_pre);
+        if (ph > 0) {  // every CTA has finished the previous phase
+            bool bad = false;
+            if (tid == 0) bad = !spin_count(c.bar + ph - 1, gridDim.x, c.err, &abort_flag);
+            if (consumer_sync_or(bad || abort_flag)) {
+                abort_flag = 1;  // the producer stops at its next wait
+                timed_out = true;
+                break;
+            }
+        }
+        if (p.act_prepared) {  // written by the previous kernel in this layout: one bulk copy
+            if (tid == 0) {
+                mbar_expect_tx(&actbar, (uint32_t)p.act.bytes);
+                bulk_g2s(smem, p.act_global, (uint32_t)p.act.bytes, &actbar, 0);
+            }
+            if (!wait_abort(&actbar, actphase & 1, c.err, &abort_flag)) abort_flag = 1;
+            actphase++;
+        } else {
+            build_act_local(p, smem, red, w_pre);
+        }
+        if (consumer_sync_or(abort_flag)) {
+            abort_flag = 1;
+            timed_out = true;
+            break;
+        }
+        const Act a = act_view(p.act, smem);
+        switch (c.epi[ph]) {
+        case EPI_STORE:
+            consume_units<EPI_STORE>(p, a, r, s, lap, unit_no, glu_up, &best, &abort_flag, timed_out);
+            break;
+        case EPI_RESID:
+            consume_units<EPI_RESID>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out);
+            break;
+        case EPI_QKV: consume_units<EPI_QKV>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out); break;
+        default: consume_units<EPI_GLU>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out); break;
+        }
+        // every warp's writes of this phase, then one arrival for the CTA
+        if (ph == c.nph - 1 && c.out_tok && lane == 0) {
+            red[warp] = best.v;
+            redi[warp] = best.i;
+        }
+        if (consumer_sync_or(abort_flag)) {
+            abort_flag = 1;
+            timed_out = true;
+            break;
+        }
+        if (tid == 0) {
+            if (ph == c.nph - 1 && c.out_tok) {
+                ArgBest b{-INFINITY, -1};
+                for (int w = 0; w < kConsumerWarps; w++)
+                    if (redi[w] >= 0) argbest_take(b, red[w], redi[w]);
+                c.best_val[blockIdx.x] = b.v;
+                c.best_idx[blockIdx.x] = b.i;
+            }
+            __threadfence();
+            const int old = atomicAdd(c.bar + ph, 1);
+            if (ph == c.nph - 1 && old == (int)gridDim.x - 1) {
+                // the last CTA of the last phase: nobody waits on the counters any more
+                __threadfence();
+                if (c.out_tok) {
+                    ArgBest b{-INFINITY, -1};
+                    for (int i = 0; i < (int)gridDim.x; i++) {
+                        const int bi = __ldcg(c.best_idx + i);
+                        if (bi >= 0) argbest_take(b, __ldcg(c.best_val + i), bi);
+                    }
+                    const uint32_t t = b.i < 0 ? 0u : (uint32_t)b.i;
+                    *c.out_tok = t;
+                    if (c.next_tok) *c.next_tok = t;
+                    if (c.pos) {
+                        if (c.history) c.history[*c.pos] = t;  // token generated after position *pos
+                        *c.pos += 1;
+                    }
+                }
+                for (int q = 0; q < c.nph; q++) c.bar[q] = 0;
+            }
+        }
+    }
+    (void)timed_out;
 }
 
 }  // namespace
@@ -766,9 +1065,54 @@ cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl)
     return cudaErrorInvalidValue;
 }
 
+void chain_prepare(ChainParams& c, int sm_count) {
+    int act = 0, stage = 0;
+    for (int i = 0; i < c.nph; i++) {
+        act = std::max(act, c.ph[i].act.bytes);
+        stage = std::max(stage, c.ph[i].stage_bytes);
+    }
+    c.act_bytes = (act + 127) / 128 * 128;
+    c.stage_bytes = stage;
+    c.stages = std::max(2, std::min(kGemvMaxStages, (kRingBudget - c.act_bytes) / stage));
+    c.grid = 2 * sm_count;
+    for (int i = 0; i < c.nph; i++) {
+        // one ring geometry and one grid for every phase (the unit pairing depends on both)
+        c.ph[i].stages = c.stages;
+        c.ph[i].stage_bytes = c.stage_bytes;
+        c.ph[i].grid = c.grid;
+    }
+}
+
+size_t chain_smem(const ChainParams& c) { return (size_t)c.act_bytes + (size_t)c.stages * c.stage_bytes; }
+
+bool chain_fits(const ChainParams& c, int sm_count) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_chain_kernel, kThreads, chain_smem(c)) != cudaSuccess)
+        return false;
+    return n * sm_count >= c.grid;
+}
+
+cudaError_t chain_launch(const ChainParams& c, cudaStream_t st, bool pdl) {
+    if (c.nph < 1 || c.nph > kChainMaxPhases || c.stages < 2 || !c.bar) return cudaErrorInvalidValue;
+    for (int i = 0; i < c.nph; i++)
+        if (c.epi[i] == EPI_DOTS || (c.ph[i].act_prepared && !c.ph[i].act_global)) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = chain_smem(c);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, c);
+}
+
 cudaError_t gemv_init_device() {
     const int max_smem = 200 * 1024;
     cudaError_t e;
+    if ((e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
 
     if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
     if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;

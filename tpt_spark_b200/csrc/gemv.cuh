@@ -171,6 +171,31 @@ struct GemvParams {
     int* err;
 };
 
+// A chain of GEMVs in one persistent launch (gemv.cu gemv_chain_kernel): phases separated
+// by grid-wide arrival counters; each phase's activation is built by every CTA from its x
+// (RMSNorm with norm_w when set, then quantisation), or bulk-copied from act_global when
+// act_prepared.  After the last phase the last CTA to arrive optionally reduces the argmax of
+// the last phase's rows (EPI_STORE, candle sample_argmax ties to the higher index) and
+// resets the counters for the next launch.  Every CTA of the grid must be resident together:
+// the grid is two CTAs per SM, which the shared-memory budget allows.
+constexpr int kChainMaxPhases = 4;
+struct ChainParams {
+    GemvParams ph[kChainMaxPhases];
+    int epi[kChainMaxPhases];  // EPI_STORE / RESID / QKV / GLU
+    int nph;
+    int* bar;  // [kChainMaxPhases] arrival counters, zero at launch (left zero on success)
+    // argmax after the last phase when out_tok != nullptr (same outputs as launch_argmax)
+    float* best_val;  // [grid] per-CTA partials
+    int* best_idx;
+    uint32_t* out_tok;
+    uint32_t* next_tok;
+    int* pos;
+    uint32_t* history;
+    int* err;
+    // filled by chain_prepare
+    int act_bytes, stages, stage_bytes, grid;
+};
+
 // Host helpers (gemv.cu).
 void gemv_prepare(GemvParams& p, int sm_count = 148);  // work split, ring, activation layout
 size_t gemv_smem(const GemvParams& p);
@@ -179,5 +204,11 @@ cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl)
 // Upper bound of act_bytes for inputs of K elements (buffer sizing).
 inline size_t gemv_act_bytes_max(int K) { return (size_t)K * 7 + 1024; }
 cudaError_t gemv_init_device();  // per-device kernel attributes (call once per device)
+// Phases already gemv_prepare'd: common ring geometry and grid (2 CTAs per SM).
+void chain_prepare(ChainParams& c, int sm_count = 148);
+size_t chain_smem(const ChainParams& c);
+// Whether every CTA of the chain's grid can be resident at once (its barriers need that).
+bool chain_fits(const ChainParams& c, int sm_count);
+cudaError_t chain_launch(const ChainParams& c, cudaStream_t st, bool pdl);
 
 }  // namespace tptc

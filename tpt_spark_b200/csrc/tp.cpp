@@ -5,6 +5,7 @@
 // carries PyTorch's own libnccl.so.2, and the first copy loaded wins the symbol names.
 // If a libnccl.so.2 is already resident it is reused; TPTC_NCCL_LIB names another file.
 #include "tp.h"
+#include "tptc.h"
 
 #include <dlfcn.h>
 #include <nccl.h>
@@ -91,6 +92,27 @@ Status Tp::init(int r, int s, const void* uid, cudaStream_t st) {
     if (nr != ncclSuccess) return Status{TPTC_ERR_NCCL, nccl_msg("ncclCommInitRank", nr)};
     comm = c;
     return {};
+}
+
+bool tp_shard(int which, int n_heads, int n_kv_heads, int head_dim, int dim, int ffn, int rank, int size, int& r0,
+              int& r1, int& k0, int& k1) {
+    if (size < 1 || rank < 0 || rank >= size || n_kv_heads <= 0 || n_heads % n_kv_heads) return false;
+    // every rank keeps whole kv heads with their query group, and whole 256-blocks of ffn
+    if (n_kv_heads % size || ffn % (256 * size)) return false;
+    const int qd = n_heads / size * head_dim, kvd = n_kv_heads / size * head_dim, fl = ffn / size;
+    if (size > 1 && qd % 256) return false;  // the o projection's K slice: whole quant blocks
+    r0 = 0;
+    k0 = 0;
+    switch (which) {
+    case TPTC_SHARD_Q: r0 = rank * qd; r1 = r0 + qd; k1 = dim; return true;
+    case TPTC_SHARD_K:
+    case TPTC_SHARD_V: r0 = rank * kvd; r1 = r0 + kvd; k1 = dim; return true;
+    case TPTC_SHARD_O: r1 = dim; k0 = rank * qd; k1 = k0 + qd; return true;
+    case TPTC_SHARD_GATE:
+    case TPTC_SHARD_UP: r0 = rank * fl; r1 = r0 + fl; k1 = dim; return true;
+    case TPTC_SHARD_DOWN: r1 = dim; k0 = rank * fl; k1 = k0 + fl; return true;
+    }
+    return false;
 }
 
 float* Tp::partial(size_t n) {

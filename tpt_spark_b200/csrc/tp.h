@@ -26,4 +26,9 @@ struct Tp {
 
 int nccl_unique_id(void* out128);
 
+// The rows [r0, r1) and input columns [k0, k1) of weight `which` (TPTC_SHARD_*) that rank
+// `rank` of `size` keeps; false when the model does not split evenly.
+bool tp_shard(int which, int n_heads, int n_kv_heads, int head_dim, int dim, int ffn, int rank, int size, int& r0,
+              int& r1, int& k0, int& k1);
+
 }  // namespace tptc

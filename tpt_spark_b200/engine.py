@@ -71,6 +71,19 @@ def nccl_unique_id() -> bytes:
     return buf.raw
 
 
+SHARD_NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def tp_shard(which: str, n_heads: int, n_kv_heads: int, head_dim: int, dim: int, ffn: int, rank: int,
+             size: int) -> Tuple[int, int, int, int]:
+    """(r0, r1, k0, k1): the rows and input columns of weight `which` that TP rank `rank` of
+    `size` keeps (the loader's plan, tptc_tp_shard).  Host only."""
+    v = [ctypes.c_int() for _ in range(4)]
+    check(lib().tptc_tp_shard(SHARD_NAMES.index(which), n_heads, n_kv_heads, head_dim, dim, ffn, rank, size,
+                              *[ctypes.byref(x) for x in v]))
+    return tuple(x.value for x in v)
+
+
 def device_count() -> int:
     return lib().tptc_device_count()
 

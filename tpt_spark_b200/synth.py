@@ -131,6 +131,12 @@ TINY: Dict[str, ModelConfig] = {
     "tiny_f16": ModelConfig(
         "tiny_f16", dim=768, n_layers=2, n_heads=8, n_kv_heads=8, ffn=512, vocab=320,
         rope_base=10000.0, context_length=512, default_type=F16, norm_std=0.1),
+    # splits over 2 tensor-parallel ranks: 4 query heads of 64 (one 256-block of o's K) and
+    # 2 kv heads per rank, 512 ffn rows per rank
+    "tiny_tp_q4km": ModelConfig(
+        "tiny_tp_q4km", dim=512, n_layers=2, n_heads=8, n_kv_heads=4, ffn=1024, vocab=384,
+        rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
+        output_type=Q6_K, norm_std=0.1),
 }
 
 # C1: one Q4_K matrix [4096 out x 4096 in], W ~ N(0, 0.02), x ~ N(0, 1).
