@@ -207,6 +207,10 @@ TPTC_API int64_t tptc_matrix_bytes(const tptc_matrix* m);
  * in f32) -- gemm.wgsl + dequant_*.wgsl fused.  The matrix holds the scratch of its launches:
  * calls on the same matrix must not overlap on the GPU. */
 TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void* stream);
+/* The matrix expanded to dense row-major fp16 [N x K] on the device (the prefill GEMM's B
+ * operand): each value the GGUF dequantisation (dequant_*.wgsl semantics, gguf-py order)
+ * rounded to nearest fp16. */
+TPTC_API int tptc_matrix_dequant_f16(const tptc_matrix* m, void* d_out, void* stream);
 /* Per (row, super-block) integer sums of the same kernel: isum = sum_j sc_j*dot_j,
  * msum = sum_j m_j*bsum_j (Q4_K; 0 otherwise); [N, K/256] for k-quants, [N, K/32] Q8_0. */
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,

@@ -157,3 +157,16 @@ def test_gemv_repeatable(cuda_device):
     m.gemv(x, y1)
     m.gemv(x, y2)
     assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("t,N,K", SHAPES)
+def test_matrix_dequant_f16_bitexact(cuda_device, t, N, K):
+    """The prefill GEMM's B operand: the device-layout matrix expanded to dense fp16 equals the
+    oracle's bit-exact dequantisation rounded to nearest fp16, element for element."""
+    import torch
+
+    raw, m = make_matrix(t, N, K, seed=5)
+    out = torch.full((N, K), float("nan"), dtype=torch.float16, device="cuda")
+    m.dequant_f16(out)
+    want = O.dequant(t, raw, N * K).reshape(N, K).astype(np.float16)
+    np.testing.assert_array_equal(host(out).view(np.uint16), want.view(np.uint16))

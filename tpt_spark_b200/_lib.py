@@ -71,6 +71,7 @@ SIGNATURES = {
     "tptc_matrix_destroy": (None, [c_vp]),
     "tptc_matrix_bytes": (c_i64, [c_vp]),
     "tptc_gemv": (c_int, [c_vp, c_vp, c_vp, c_vp]),
+    "tptc_matrix_dequant_f16": (c_int, [c_vp, c_vp, c_vp]),
     "tptc_block_dots": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp]),
     "tptc_gemm_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
     "tptc_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp]),

@@ -491,6 +491,13 @@ TPTC_API int tptc_attn_prefill(const void* d_q, const void* d_kcache, const void
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "attn_prefill");
 }
 
+TPTC_API int tptc_matrix_dequant_f16(const tptc_matrix* m, void* d_out, void* stream) {
+    if (!m || !d_out) return fail_code(nullptr, TPTC_ERR_ARG, "matrix_dequant_f16: null argument");
+    cudaError_t e = tptc::launch_dequant_rows_f16(m->m, 0, m->m.N, static_cast<__half*>(d_out),
+                                                  static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "dequant_rows_f16");
+}
+
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum, void* stream) {
     if (!m || !d_x || !d_isum) return TPTC_ERR_ARG;
     if (m->m.type == TPTC_TYPE_F16) return TPTC_ERR_UNSUPPORTED;

@@ -84,29 +84,71 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, 
     }
 }
 
-// Device layout -> dense f16 rows [row0, row0 + rows), one thread per 8 consecutive elements.
+// Device layout -> dense f16 rows [row0, row0 + rows), one thread per 32-element group (a
+// Q4_K sub-block, half a Q6_K 16-pair, a Q8_0 block): the group's scales are decoded once,
+// its quant bytes read as 16-byte vectors and the 64 output bytes written as four 16-byte
+// stores.  Values are those of q4k_elem / q6k_elem / the Q8_0 product, rounded to fp16.
 __global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, int physical, __half* __restrict__ out) {
-    const int64_t per_row = m.K / 8;
+    const int64_t per_row = m.K / 32;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= per_row * rows) return;
-    const int r = (int)(i / per_row), k0 = (int)(i % per_row) * 8;
+    const int r = (int)(i / per_row), k0 = (int)(i % per_row) * 32;
     const int prow = physical ? row0 + r : dm_phys_row(m, row0 + r);
-    const uint8_t* blk = dm_block(m, prow, k0 / QK_K);
-    const int e0 = k0 % QK_K;
-    __align__(16) __half v[8];
+    const int sb = k0 / QK_K, e0 = k0 % QK_K, j = e0 / 32;
+    const uint8_t* blk = dm_block(m, prow, sb);
+    __align__(16) __half v[32];
     if (m.type == TPTC_TYPE_F16) {
-        *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(blk + e0 * 2);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            reinterpret_cast<uint4*>(v)[k] = reinterpret_cast<const uint4*>(blk + e0 * 2)[k];
     } else if (m.type == TPTC_TYPE_Q4_K) {
-        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q4k_elem(blk, e0 + j));
+        // sub-block j: low (j even) or high (j odd) nibbles of qs[32 (j/2) .. +32)
+        int sc, mn;
+        q4k_scale_min(blk + 4, j, sc, mn);
+        const float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+        const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)mn);
+        const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + 32 * (j >> 1));
+        const int sh = (j & 1) * 4;
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const uint4 w = qv[k];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int b = 0; b < 16; b++) {
+                const int q = (ww[b >> 2] >> (8 * (b & 3) + sh)) & 0x0f;
+                v[16 * k + b] = __float2half_rn(__fsub_rn(__fmul_rn(ds, (float)q), dm));
+            }
+        }
     } else if (m.type == TPTC_TYPE_Q6_K) {
-        const float d = h2f(dm_scales(m, prow, k0 / QK_K)[0]);
-        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(q6k_elem(blk, d, e0 + j));
+        // elements 128h + 32i + l: ql[64h + 32 (i & 1) + l] nibble (i & 2), qh[32h + l] bits 2i
+        const int h = j >> 2, ii = j & 3;
+        const float d = h2f(dm_scales(m, prow, sb)[0]);
+        const int8_t* scs = reinterpret_cast<const int8_t*>(blk + 192);
+        const float ds0 = __fmul_rn(d, (float)scs[(e0 >> 4)]), ds1 = __fmul_rn(d, (float)scs[(e0 >> 4) + 1]);
+        const uint4* qlv = reinterpret_cast<const uint4*>(blk + 64 * h + 32 * (ii & 1));
+        const uint4* qhv = reinterpret_cast<const uint4*>(blk + 128 + 32 * h);
+        const int lsh = (ii & 2) ? 4 : 0, hsh = 2 * ii;
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const uint4 a = qlv[k], hb = qhv[k];
+            const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, hh[4] = {hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+            for (int b = 0; b < 16; b++) {
+                const int lo = (aa[b >> 2] >> (8 * (b & 3) + lsh)) & 0x0f;
+                const int hi = (hh[b >> 2] >> (8 * (b & 3) + hsh)) & 0x03;
+                const int q = (lo | (hi << 4)) - 32;
+                v[16 * k + b] = __float2half_rn(__fmul_rn(k == 0 ? ds0 : ds1, (float)q));
+            }
+        }
     } else {
         const int8_t* q = reinterpret_cast<const int8_t*>(blk + e0);
-        const float d = h2f(dm_scales(m, prow, k0 / QK_K)[e0 / QK8_0]);
-        for (int j = 0; j < 8; j++) v[j] = __float2half_rn(__fmul_rn((float)q[j], d));
+        const float d = h2f(dm_scales(m, prow, sb)[e0 / QK8_0]);
+#pragma unroll
+        for (int b = 0; b < 32; b++) v[b] = __float2half_rn(__fmul_rn((float)q[b], d));
     }
-    *reinterpret_cast<uint4*>(out + (int64_t)r * m.K + k0) = *reinterpret_cast<const uint4*>(v);
+    uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)r * m.K + k0);
+#pragma unroll
+    for (int k = 0; k < 4; k++) dst[k] = reinterpret_cast<const uint4*>(v)[k];
 }
 
 }  // namespace
@@ -142,9 +184,9 @@ cudaError_t launch_repack(const uint8_t* raw, int64_t raw_row, int nr, int first
 
 cudaError_t launch_dequant_rows_f16(const DevMatrix& m, int row0, int rows, __half* out, cudaStream_t st,
                                     bool physical) {
-    const int64_t n = (int64_t)rows * (m.K / 8);
+    const int64_t n = (int64_t)rows * (m.K / 32);
     if (n <= 0) return cudaSuccess;
-    dequant_rows_f16_kernel<<<(unsigned)ceil_div64(n, 256), 256, 0, st>>>(m, row0, rows, physical ? 1 : 0, out);
+    dequant_rows_f16_kernel<<<(unsigned)ceil_div64(n, 128), 128, 0, st>>>(m, row0, rows, physical ? 1 : 0, out);
     return cudaGetLastError();
 }
 

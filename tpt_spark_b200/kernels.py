@@ -47,6 +47,10 @@ class Matrix:
     def gemv(self, d_x, d_y, stream: Optional[int] = None) -> None:
         check(lib().tptc_gemv(self._h, _ptr(d_x), _ptr(d_y), stream))
 
+    def dequant_f16(self, d_out, stream: Optional[int] = None) -> None:
+        """The matrix as dense row-major fp16 [N x K] (the prefill GEMM operand)."""
+        check(lib().tptc_matrix_dequant_f16(self._h, _ptr(d_out), stream))
+
     def block_dots(self, d_x, d_isum, d_msum=None, stream: Optional[int] = None) -> None:
         check(lib().tptc_block_dots(self._h, _ptr(d_x), _ptr(d_isum), _ptr(d_msum) if d_msum is not None else None,
                                     stream))
