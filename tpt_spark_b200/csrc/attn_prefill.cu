@@ -12,6 +12,7 @@
 // with an online softmax in base 2 in registers (flash-attention, one pass).  Q and the
 // probabilities enter the tensor cores as fp16; the KV cache is fp16.
 #include "prefill.h"
+#include "tcgen05.cuh"
 
 namespace tptc {
 
@@ -218,6 +219,262 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const __grid_con
     }
 }
 
+// ---------------------------------------------------------------- tcgen05 kernel
+
+namespace tc {
+
+constexpr int BM = 128;         // query rows per CTA (TMEM lanes)
+constexpr int BN = 64;          // key positions per tile
+constexpr int kStages = 2;      // K/V ring
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 256;  // S: columns 0..63, O: columns 128..128 + hd
+
+template <int HD>
+struct Lay {
+    static constexpr int kQBytes = BM * HD * 2;   // HD / 64 blocks of [128 rows x 128 B]
+    static constexpr int kKVBytes = BN * HD * 2;  // HD / 64 blocks of [64 rows x 128 B]
+    static constexpr int kPBytes = BM * BN * 2;   // [128 rows x 128 B]
+    // P of tile j may live in the K slot of its stage once S(j) has read it (the slot is
+    // refilled only after P V(j) released the stage) when that slot is large enough
+    static constexpr bool kPInK = kKVBytes >= kPBytes;
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kQBytes;
+    static constexpr int kV = kK + kStages * kKVBytes;
+    static constexpr int kP = kV + kStages * kKVBytes;  // separate P region (kPInK false)
+    static constexpr int kBytes = kP + (kPInK ? 0 : kPBytes);
+    __device__ static constexpr int p_off(int s) { return kPInK ? kK + s * kKVBytes : kP; }
+};
+
+}  // namespace tc
+
+__device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
+    *abort_flag = 1;
+    return false;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(tc::kThreads, 2)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, const __grid_constant__ AttnPrefillParams p) {
+    using L = tc::Lay<HD>;
+    using tc::BM;
+    using tc::BN;
+    constexpr int NC = HD / 64;  // 64-column blocks of a row
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t q_full, kv_full[tc::kStages], kv_empty[tc::kStages], s_full, p_full, o_done, drain;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (latest) query tiles first
+    const int h = blockIdx.y, kvh = h / (p.n_heads / p.n_kv);
+    const int q0 = qt * BM, rows = min(BM, p.T - q0);
+    const int last = p.start + q0 + rows - 1;  // last key position any row of the tile attends to
+    const int nt = last / BN + 1;
+    const int kvrow0 = kvh * p.max_seq;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&q_full, 1);
+        for (int s = 0; s < tc::kStages; s++) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(&s_full, 1);
+        mbar_init(&p_full, 4);  // one arrival per softmax warp
+        mbar_init(&o_done, 1);
+        mbar_init(&drain, 1);
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    if (warp == 1) tmem_alloc(&tmem_slot, tc::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot, tS = tmem, tO = tmem + 128;
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            mbar_expect_tx(&q_full, L::kQBytes);
+#pragma unroll
+            for (int c = 0; c < NC; c++) tma_load_2d(smem + L::kQ + c * BM * 128, &tq, h * HD + c * 64, q0, &q_full);
+            int j = 0;
+            for (; j < nt; j++) {
+                const int s = j & 1;
+                if (j >= tc::kStages && !attn_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err, &abort_flag)) break;
+                mbar_expect_tx(&kv_full[s], 2 * L::kKVBytes);
+#pragma unroll
+                for (int c = 0; c < NC; c++) {
+                    tma_load_2d(smem + L::kK + s * L::kKVBytes + c * BN * 128, &tk, c * 64, kvrow0 + j * BN, &kv_full[s]);
+                    tma_load_2d(smem + L::kV + s * L::kKVBytes + c * BN * 128, &tv, c * 64, kvrow0 + j * BN, &kv_full[s]);
+                }
+            }
+            // the copies still in flight land before the CTA exits
+            mbar_wait_bounded(&q_full, 0, nullptr);
+            for (int jj = j > tc::kStages ? j - tc::kStages : 0; jj < j; jj++)
+                mbar_wait_bounded(&kv_full[jj & 1], (jj >> 1) & 1, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            const uint32_t id_s = mma_idesc(BM, BN), id_o = mma_idesc(BM, HD) | kIdescBMajorMN;
+            auto issue_s = [&](int s) {
+                const uint32_t qa = smem_u32(smem + L::kQ), ka = smem_u32(smem + L::kK + s * L::kKVBytes);
+#pragma unroll
+                for (int c = 0; c < NC; c++)
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_f16(tS, sw128_desc(qa + c * BM * 128 + 32 * kk), sw128_desc(ka + c * BN * 128 + 32 * kk),
+                                id_s, (c | kk) != 0);
+            };
+            auto issue_pv = [&](int j, int s) {
+                const uint32_t pa = smem_u32(smem + L::p_off(s)), va = smem_u32(smem + L::kV + s * L::kKVBytes);
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; kk++)
+                    mma_f16(tO, sw128_desc(pa + 32 * kk), sw128_desc_mn(va + kk * 2048, BN * 128), id_o,
+                            (j | kk) != 0);
+            };
+            bool ok = attn_wait(&q_full, 0, p.err, &abort_flag) && attn_wait(&kv_full[0], 0, p.err, &abort_flag);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
+                mma_commit(&s_full);
+            }
+            for (int j = 0; j < nt && ok; j++) {
+                const int s = j & 1;
+                if (!attn_wait(&p_full, j & 1, p.err, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                issue_pv(j, s);
+                mma_commit(&kv_empty[s]);  // K_j and V_j consumed
+                if (j + 1 < nt) {
+                    const int s1 = (j + 1) & 1;
+                    if (!attn_wait(&kv_full[s1], ((j + 1) >> 1) & 1, p.err, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(s1);
+                    mma_commit(&s_full);
+                }
+            }
+            if (ok) mma_commit(&o_done);
+            // every MMA issued has completed before TMEM is freed
+            mma_commit(&drain);
+            mbar_wait_bounded(&drain, 0, nullptr);
+        }
+    } else {  // warps 2..5: one thread per query row
+        const int qq = warp & 3, r = 32 * qq + lane;
+        const uint32_t loff = (uint32_t)(32 * qq) << 16;
+        const int pos = p.start + q0 + r;
+        const float sl2 = p.scale * 1.4426950408889634f;
+        float m_ref = -INFINITY, l = 0.f;
+        bool ok = true;
+        const int prow_off = (r >> 3) * 1024 + (r & 7) * 128;
+        for (int j = 0; j < nt; j++) {
+            uint8_t* prow = smem + L::p_off(j & 1) + prow_off;
+            if (!attn_wait(&s_full, j & 1, p.err, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sv[BN];
+            tmem_ld32(tS + loff, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_ld32(tS + loff + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+            const int p0 = j * BN;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < BN; k++) {
+                const float x = p0 + k <= pos ? __uint_as_float(sv[k]) * sl2 : -INFINITY;
+                sv[k] = __float_as_uint(x);
+                mt = fmaxf(mt, x);
+            }
+            // the reference max moves only past 2^8 above the current one (P stays <= 256)
+            const bool move = mt > m_ref + 8.f;
+            float alpha = 1.f;
+            if (move) {
+                alpha = fast_exp2(m_ref - mt);
+                l *= alpha;
+                m_ref = mt;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, move)) {
+                // P V of tile j - 1 has completed (s_full of this tile was committed after it)
+#pragma unroll 1
+                for (int c0 = 0; c0 < HD; c0 += 32) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + loff + c0, o);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + loff + c0, o);
+                }
+            }
+            // P = 2^(s - m_ref) as fp16, K-major with 128-byte swizzle: row r's 16-byte chunk
+            // c (keys 8c .. 8c + 7) sits at chunk c ^ (r % 8) of the row
+            float ps = 0.f;
+#pragma unroll
+            for (int c = 0; c < BN / 8; c++) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float a = fast_exp2(__uint_as_float(sv[8 * c + 2 * e]) - m_ref);
+                    const float b = fast_exp2(__uint_as_float(sv[8 * c + 2 * e + 1]) - m_ref);
+                    ps += a + b;
+                    w[e] = pack_half2(a, b);
+                }
+                *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            l += ps;
+            if (j == nt - 1) {
+                // cache rows past the last attended position may hold anything: zero them in
+                // the V tile so that 0 * value cannot turn into NaN
+                uint8_t* sv_base = smem + L::kV + (j & 1) * L::kKVBytes;
+                const int vr0 = last - p0 + 1, nclr = (BN - vr0) * NC * 8;
+                for (int idx = r; idx < nclr; idx += BM) {
+                    const int i = vr0 + idx / (NC * 8), rem = idx % (NC * 8), c = rem >> 3, ch = rem & 7;
+                    *reinterpret_cast<uint4*>(sv_base + c * BN * 128 + (i >> 3) * 1024 + (i & 7) * 128 + ch * 16) =
+                        make_uint4(0, 0, 0, 0);
+                }
+            }
+            fence_proxy_async_smem();  // P (and the cleared V rows) before the tensor core reads them
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full);
+        }
+        if (ok && attn_wait(&o_done, 0, p.err, &abort_flag)) {
+            tc_fence_after();
+            const float il = 1.f / l;
+            __half* orow = p.out + ((size_t)(q0 + r) * p.n_heads + h) * HD;
+#pragma unroll 1
+            for (int c0 = 0; c0 < HD; c0 += 32) {
+                uint32_t o[32];
+                tmem_ld32(tO + loff + c0, o);
+                if (r < rows) {
+                    uint32_t w[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        w[i] = pack_half2(__uint_as_float(o[2 * i]) * il, __uint_as_float(o[2 * i + 1]) * il);
+                    uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tc::kTmemCols);
+    }
+}
+
 template <int HD>
 size_t attn_prefill_smem() {
     return (size_t)(BQ + 4 * BKV) * (HD + 8) * sizeof(__half);
@@ -227,6 +484,12 @@ size_t attn_prefill_smem() {
 
 cudaError_t attn_prefill_init_device() {
     cudaError_t e;
+    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  tc::Lay<64>::kBytes + 1024)))
+        return e;
+    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  tc::Lay<128>::kBytes + 1024)))
+        return e;
     if ((e = cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)attn_prefill_smem<64>())))
         return e;
@@ -237,9 +500,39 @@ cudaError_t attn_prefill_init_device() {
                                 (int)attn_prefill_smem<128>());
 }
 
-cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, bool pdl) {
+namespace {
+
+template <int HD>
+cudaError_t launch_tc(const AttnPrefillParams& p, cudaStream_t st, bool pdl) {
+    CUtensorMap tq, tk, tv;
+    cudaError_t e = make_tmap_f16(&tq, p.q, p.T, (int64_t)p.n_heads * HD, (int64_t)p.n_heads * HD, tc::BM);
+    if (e == cudaSuccess) e = make_tmap_f16(&tk, p.kcache, (int64_t)p.n_kv * p.max_seq, HD, HD, tc::BN);
+    if (e == cudaSuccess) e = make_tmap_f16(&tv, p.vcache, (int64_t)p.n_kv * p.max_seq, HD, HD, tc::BN);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.T + tc::BM - 1) / tc::BM, p.n_heads);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::Lay<HD>::kBytes + 1024;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_prefill_tc_kernel<HD>, tq, tk, tv, p);
+}
+
+}  // namespace
+
+cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, bool pdl, int use_tc) {
     if (p.T <= 0 || p.n_kv <= 0 || p.n_heads % p.n_kv || p.start < 0 || p.start + p.T > p.max_seq)
         return cudaErrorInvalidValue;
+    const uintptr_t align = reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.kcache) |
+                            reinterpret_cast<uintptr_t>(p.vcache);
+    if (use_tc && (align & 15) == 0) {
+        if (p.hd == 64) return launch_tc<64>(p, st, pdl);
+        if (p.hd == 128) return launch_tc<128>(p, st, pdl);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.T + BQ - 1) / BQ, p.n_heads);
     cfg.blockDim = dim3(kThreads);

@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "prefill.h"
+#include "tcgen05.cuh"
 
 namespace tptc {
 
@@ -42,71 +43,6 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 192;
 constexpr int kAccCols = BN;             // f32 accumulator columns of one tile
 constexpr int kTmemCols = 2 * kAccCols;  // double-buffered: all 512 columns
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major operand tile with 128-byte swizzle: rows of
-// 128 bytes, 8-row atoms of 1024 bytes (stride byte offset), tile 1024-byte aligned.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFF);   // start address
-    d |= (uint64_t)1 << 16;                   // leading byte offset (unused with swizzle)
-    d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
-    d |= (uint64_t)1 << 46;                   // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;                   // layout: SWIZZLE_128B
-    return d;
-}
-
-// Instruction descriptor: f16 x f16 -> f32, both K-major, M x N.
-__host__ __device__ constexpr uint32_t mma_idesc(int M, int N) {
-    return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-// 32 lanes x 32 consecutive 32-bit columns of TMEM: thread t receives lane (base lane + t).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Bounded wait that also gives up once another role of the CTA has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-    }
-    if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
-    *abort_flag = 1;
-    return false;
-}
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); }
 
@@ -293,36 +229,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::mutex g_encode_mu;
-
-cudaError_t get_encode() {
-    std::lock_guard<std::mutex> lk(g_encode_mu);
-    if (g_encode) return cudaSuccess;
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess) return e;
-    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    return cudaSuccess;
-}
-
-// Row-major fp16 matrix [rows x cols] (leading dimension ld elements) as a 2-D tensor map with
-// a box of 64 columns x box_rows rows and 128-byte swizzle.
-cudaError_t make_map(CUtensorMap* map, const __half* ptr, int rows, int cols, int ld, int box_rows) {
-    cudaError_t e = get_encode();
-    if (e != cudaSuccess) return e;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
 constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
 // more than half of an SM's shared memory: one CTA per SM, so the 512-column TMEM allocation
 // never waits for another CTA
@@ -343,6 +249,37 @@ int sm_count() {
 
 }  // namespace
 
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+
+cudaError_t get_encode() {
+    std::lock_guard<std::mutex> lk(g_encode_mu);
+    if (g_encode) return cudaSuccess;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t make_tmap_f16(CUtensorMap* map, const __half* ptr, int64_t rows, int64_t cols, int64_t ld,
+                          int box_rows) {
+    cudaError_t e = get_encode();
+    if (e != cudaSuccess) return e;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(ptr), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t gemm_tc_init_device() {
     cudaError_t e;
     if ((e = cudaFuncSetAttribute(gemm_tc_kernel<GEMM_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem)))
@@ -359,8 +296,8 @@ cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb,
         return cudaErrorInvalidValue;
     if (epi == GEMM_GLU && p_in.N % 8) return cudaErrorInvalidValue;
     CUtensorMap ma, mb;
-    cudaError_t e = make_map(&ma, a, p_in.M, p_in.K, lda, BM);
-    if (e == cudaSuccess) e = make_map(&mb, b, p_in.N, p_in.K, ldb, BN);
+    cudaError_t e = make_tmap_f16(&ma, a, p_in.M, p_in.K, lda, BM);
+    if (e == cudaSuccess) e = make_tmap_f16(&mb, b, p_in.N, p_in.K, ldb, BN);
     if (e != cudaSuccess) return e;
     const long tiles = (long)((p_in.M + BM - 1) / BM) * ((p_in.N + BN - 1) / BN);
     cudaLaunchConfig_t cfg = {};

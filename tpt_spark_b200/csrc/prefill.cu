@@ -220,6 +220,7 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         ap.hd = hd;
         ap.max_seq = max_seq_;
         ap.scale = (float)(1.0 / sqrt((double)hd));
+        ap.err = err_;
         TPTC_CUDA_RET(launch_attn_prefill(ap, st, false));
         TPTC_CUDA_RET(launch_dequant_rows_f16(L.o, 0, dim, pf_w_, st));
         g.N = dim;

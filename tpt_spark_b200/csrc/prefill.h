@@ -39,8 +39,11 @@ struct AttnPrefillParams {
     int T, start;          // chunk rows are positions start .. start + T - 1
     int n_heads, n_kv, hd, max_seq;
     float scale;           // 1/sqrt(hd)
+    int* err;              // optional: bounded waits that give up set TPTC_ERR_TIMEOUT here
 };
-cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, bool pdl);
+// head_dim 64 and 128 run on tcgen05 (attn_prefill_tc_kernel), 96 on mma.sync; `use_tc` = 0
+// forces the mma.sync kernel (kernel-level comparisons).
+cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, bool pdl, int use_tc = 1);
 cudaError_t attn_prefill_init_device();
 
 // ---- per-token elementwise steps of a chunk (prefill.cu)
