@@ -773,7 +773,7 @@ __device__ __forceinline__ bool spin_count(const int* ctr, int target, int* err,
 // layout, with the norm partition and arithmetic of act_quant_kernel (same m, same codes).
 // Vectors of up to 32 blocks are read once and held in registers (one L2 round trip); the
 // norm gains, which no phase writes, are fetched before the caller's barrier (w_pre).
-constexpr int kActHold = 4;  // blocks per warp held in registers
+constexpr int kActHold = 2;  // blocks per warp held in registers (K <= 4096 in one pass)
 __device__ __forceinline__ void prefetch_norm(const GemvParams& p, float (&w_pre)[kActHold][8]) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = p.K / QK_K;
     if (!p.norm_w) return;
@@ -790,29 +790,35 @@ __device__ __forceinline__ void ldcg8(const float* src, float (&v)[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// x / m rounded to nearest, given rm = 1 / m rounded to nearest (__frcp_rn): a product and
+// one fused correction step (Markstein's final division step, P. Markstein, IBM J. Res.
+// Dev. 34(1), 1990), correctly rounded for finite operands whose quotient does not
+// underflow.  Replaces one __fdiv_rn per element where a whole vector is divided by the
+// same m; the chain-vs-activation-kernel bit-identity test compares the two on every value.
+__device__ __forceinline__ float div_by(float x, float m, float rm) {
+    const float q = __fmul_rn(x, rm);
+    const float e = __fmaf_rn(-q, m, x);
+    return __fmaf_rn(e, rm, q);
+}
+
 __device__ void build_act_local(const GemvParams& p, uint8_t* act, float* red, const float (&w_pre)[kActHold][8]) {
     const int K = p.K, nb = K / QK_K, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool norm = p.norm_w != nullptr;
+    // this warp's blocks: warp, warp + 8, ... (nbw of them), the first kActHold in registers
+    const int nbw = nb > warp ? (nb - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
     float v[kActHold][8];
-    int bi[kActHold];
 #pragma unroll
-    for (int j = 0; j < kActHold; j++) {
-        bi[j] = warp + j * kConsumerWarps;
-        if (bi[j] < nb) ldcg8(p.x + bi[j] * QK_K + 8 * lane, v[j]);
-        else {
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[j][i] = 0.f;
-        }
-    }
-    float m = 1.f;
+    for (int j = 0; j < kActHold; j++)
+        if (j < nbw) ldcg8(p.x + (warp + j * kConsumerWarps) * QK_K + 8 * lane, v[j]);
+    float m = 1.f, rm = 1.f;
     if (norm) {
         float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < kActHold; j++)
-            if (bi[j] < nb) ss = __fadd_rn(ss, sumsq8(v[j]));
-        for (int b = warp + kActHold * kConsumerWarps; b < nb; b += kConsumerWarps) {  // vectors over 32 blocks
+            if (j < nbw) ss = __fadd_rn(ss, sumsq8(v[j]));
+        for (int j = kActHold; j < nbw; j++) {  // vectors over 32 blocks
             float t[8];
-            ldcg8(p.x + b * QK_K + 8 * lane, t);
+            ldcg8(p.x + (warp + j * kConsumerWarps) * QK_K + 8 * lane, t);
             ss = __fadd_rn(ss, sumsq8(t));
         }
         ss = warp_sum(ss);
@@ -822,19 +828,24 @@ __device__ void build_act_local(const GemvParams& p, uint8_t* act, float* red, c
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; w++) tot = __fadd_rn(tot, red[w]);
         m = sqrtf(__fdiv_rn(tot, (float)K) + p.eps);
+        rm = __frcp_rn(m);
 #pragma unroll
         for (int j = 0; j < kActHold; j++)
+            if (j < nbw)
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fdiv_rn(v[j][i], m), w_pre[j][i]);
+                for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(div_by(v[j][i], m, rm), w_pre[j][i]);
     }
-    {
-        const int b01[2] = {bi[0], bi[1]}, b23[2] = {bi[2], bi[3]};
-        act_store_blocks<2>(p.act, 1, nb, act, b01, *reinterpret_cast<const float(*)[2][8]>(&v[0]), lane);
-        if (bi[2] < nb) act_store_blocks<2>(p.act, 1, nb, act, b23, *reinterpret_cast<const float(*)[2][8]>(&v[2]), lane);
+    // the held blocks, two at a time (a missing partner is skipped by its index)
+#pragma unroll
+    for (int j = 0; j < kActHold; j += 2) {
+        if (j < nbw) {
+            const int bb[2] = {warp + j * kConsumerWarps, j + 1 < nbw ? warp + (j + 1) * kConsumerWarps : nb};
+            act_store_blocks<2>(p.act, 1, nb, act, bb, *reinterpret_cast<const float(*)[2][8]>(&v[j]), lane);
+        }
     }
     // blocks beyond the held ones, two at a time
-    for (int b0 = warp + kActHold * kConsumerWarps; b0 < nb; b0 += 2 * kConsumerWarps) {
-        const int bb[2] = {b0, b0 + kConsumerWarps};
+    for (int j = kActHold; j < nbw; j += 2) {
+        const int bb[2] = {warp + j * kConsumerWarps, j + 1 < nbw ? warp + (j + 1) * kConsumerWarps : nb};
         float t[2][8];
 #pragma unroll
         for (int k = 0; k < 2; k++) {
@@ -844,7 +855,7 @@ __device__ void build_act_local(const GemvParams& p, uint8_t* act, float* red, c
                     float w8[8];
                     load8(p.norm_w + bb[k] * QK_K + 8 * lane, w8);
 #pragma unroll
-                    for (int i = 0; i < 8; i++) t[k][i] = __fmul_rn(__fdiv_rn(t[k][i], m), w8[i]);
+                    for (int i = 0; i < 8; i++) t[k][i] = __fmul_rn(div_by(t[k][i], m, rm), w8[i]);
                 }
             } else {
 #pragma unroll
