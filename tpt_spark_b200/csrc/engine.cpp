@@ -377,11 +377,11 @@ Status Engine::alloc_runtime() {
     };
     const size_t o_kv = take(kv_elems * kv_elem_bytes());
     const size_t o_cos = take((size_t)max_seq_ * half * 4), o_sin = take((size_t)max_seq_ * half * 4);
-    const size_t o_x = take((size_t)m.dim * 4);
+    const size_t o_x = take((size_t)m.dim * 4), o_x2 = take((size_t)m.dim * 4);
     const size_t o_q = take((size_t)n_heads_l_ * hd * 4), o_att = take((size_t)n_heads_l_ * hd * 4);
     const size_t o_qr = take((size_t)n_heads_l_ * hd * 4), o_kr = take((size_t)n_kv_l_ * hd * 4);
     const size_t o_h = take((size_t)2 * (m.ffn / tp_size_) * 4), o_lg = take((size_t)m.vocab * 4);
-    const size_t o_ti = take(64), o_to = take(64), o_pos = take(64), o_err = take(64);
+    const size_t o_ti = take(64), o_to = take(64), o_pos = take(64), o_err = take(64), o_step = take(64);
     const size_t o_hist = take((size_t)max_seq_ * 4 + 64);
     const size_t o_part = take(attn_decode_partial_floats(n_heads_l_, n_kv_l_, hd, attn_splits_) * 4);
     const size_t o_cnt = take((size_t)n_kv_l_ * 4);
@@ -402,6 +402,7 @@ Status Engine::alloc_runtime() {
     rope_cos_ = reinterpret_cast<float*>(rt_ + o_cos);
     rope_sin_ = reinterpret_cast<float*>(rt_ + o_sin);
     x_ = reinterpret_cast<float*>(rt_ + o_x);
+    x2_ = reinterpret_cast<float*>(rt_ + o_x2);
     qbuf_ = reinterpret_cast<float*>(rt_ + o_q);
     attn_ = reinterpret_cast<float*>(rt_ + o_att);
     qrot_ = reinterpret_cast<float*>(rt_ + o_qr);
@@ -412,6 +413,7 @@ Status Engine::alloc_runtime() {
     tok_out_ = reinterpret_cast<uint32_t*>(rt_ + o_to);
     pos_ = reinterpret_cast<int*>(rt_ + o_pos);
     err_ = reinterpret_cast<int*>(rt_ + o_err);
+    step_ = reinterpret_cast<int*>(rt_ + o_step);
     history_ = reinterpret_cast<uint32_t*>(rt_ + o_hist);
     attn_partial_ = reinterpret_cast<float*>(rt_ + o_part);
     attn_counters_ = reinterpret_cast<int*>(rt_ + o_cnt);
@@ -440,6 +442,7 @@ Status Engine::alloc_runtime() {
     // the row-parallel partial buffer is baked into the graphs: allocate it before capture
     // (cudaMalloc is not allowed while a stream is capturing)
     if (tp_ && !tp_->partial(m.dim)) return err(TPTC_ERR_OOM, "tensor-parallel partial buffer");
+    if (tp_) RET_IF(tp_->init_p2p(m.dim, m.n_layers, step_, stream_));
     RET_IF(build_decode_graph(false, &graph_plain_));
     RET_IF(build_decode_graph(true, &graph_chained_));
     return {};
@@ -465,6 +468,19 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
     };
     // q | k | v with fused RMSNorm; v goes straight into the cache, q and k are rotated by
     // the attention kernel
+    // Tensor parallelism: the residual stream alternates between x_ and x2_.  A layer starts
+    // with x in x_; o scatters its partial rows (slot 0) and the gate|up activation gathers
+    // them into x2_; down scatters (slot 1) and the next q|k|v (or the head) activation
+    // gathers them back into x_ (TpLink, gemv.cuh).
+    const TpLink* link = tp_ ? tp_->link_dev : nullptr;
+    auto gather = [&](GemvParams& p, int slot, int use, float* from, float* to) {
+        p.x = from;
+        p.tp = link;
+        p.tp_slot = slot;
+        p.tp_use = use;
+        p.tp_gather = 1;
+        p.x_out = to;
+    };
     auto qkv_params = [&](int l) {
         const LayerWeights& W = layers_[l];
         GemvParams p = base(m.dim);
@@ -472,6 +488,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         const DevMatrix* qkv[3] = {&W.q, &W.k, &W.v};
         for (int i = 0; i < 3; i++) p.seg[i] = GemvSeg{*qkv[i], 0};
         p.x = x_;
+        if (link && l > 0) gather(p, 1, 2 * (l - 1) + 1, x2_, x_);
         p.norm_w = W.attn_norm;
         p.out = qbuf_;
         p.kraw = kraw_;
@@ -487,7 +504,12 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams p = base(n_heads_l_ * hd);
         p.seg[0] = GemvSeg{layers_[l].o, 0};
         p.x = attn_;
-        p.out = tp_ ? tp_->partial(m.dim) : x_;  // row-parallel: partial sums, then allreduce
+        p.out = x_;
+        if (link) {  // row-parallel: partial rows into every rank's inbox
+            p.tp = link;
+            p.tp_slot = 0;
+            p.tp_use = 2 * l;
+        }
         gemv_prepare(p, sm_count_);
         return p;
     };
@@ -495,6 +517,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams p = base(m.dim);
         p.seg[0] = GemvSeg{layers_[l].glu, 0};
         p.x = x_;
+        if (link) gather(p, 0, 2 * l, x_, x2_);
         p.norm_w = layers_[l].ffn_norm;
         p.out = h_;
         gemv_prepare(p, sm_count_);
@@ -504,7 +527,12 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams p = base(m.ffn / tp_size_);
         p.seg[0] = GemvSeg{layers_[l].down, 0};
         p.x = h_;
-        p.out = tp_ ? tp_->partial(m.dim) : x_;
+        p.out = x_;
+        if (link) {
+            p.tp = link;
+            p.tp_slot = 1;
+            p.tp_use = 2 * l + 1;
+        }
         gemv_prepare(p, sm_count_);
         return p;
     };
@@ -512,6 +540,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams p = base(m.dim);
         p.seg[0] = GemvSeg{output_, 0};
         p.x = x_;
+        if (link) gather(p, 1, 2 * (m.n_layers - 1) + 1, x2_, x_);
         p.norm_w = out_norm_;
         p.out = logits_;
         gemv_prepare(p, sm_count_);
@@ -573,7 +602,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         chain_prepare(t, sm_count_);
         use_chain = use_chain && chain_fits(t, sm_count_);
     }
-    CU(launch_embed_row(embd_, tok_in_, x_, st, false));
+    CU(launch_embed_row(embd_, tok_in_, x_, st, false, link ? step_ : nullptr));
     if (use_chain) {
         // GEMV chains: [q|k|v(0)], then per layer attention(l) and one chain
         // [o(l), gate|up(l), down(l), q|k|v(l+1) or lm_head + argmax]
@@ -624,21 +653,11 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         GemvParams o = o_params(l);
         const AttnDecodeParams a = attn_params(l, o);
         CU(launch_attn_decode(a, st, pdl_));
-        if (tp_) {
-            CU(gemv_launch(o, EPI_STORE, st, pdl_));
-            RET_IF(tp_->allreduce_add(o.out, x_, m.dim, st));
-        } else {
-            CU(gemv_launch(o, EPI_RESID, st, pdl_));
-        }
+        CU(gemv_launch(o, EPI_RESID, st, pdl_));  // under TP: scatter to every rank's inbox
         GemvParams g = glu_params(l);
         CU(gemv_launch(g, EPI_GLU, st, pdl_));
         GemvParams d = down_params(l);
-        if (tp_) {
-            CU(gemv_launch(d, EPI_STORE, st, pdl_));
-            RET_IF(tp_->allreduce_add(d.out, x_, m.dim, st));
-        } else {
-            CU(gemv_launch(d, EPI_RESID, st, pdl_));
-        }
+        CU(gemv_launch(d, EPI_RESID, st, pdl_));
         RET_IF(trace_layer(l));
     }
     GemvParams h = head_params();

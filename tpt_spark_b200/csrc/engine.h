@@ -121,6 +121,7 @@ class Engine {
     float* rope_cos_ = nullptr;
     float* rope_sin_ = nullptr;
     float* x_ = nullptr;        // residual stream [dim]
+    float* x2_ = nullptr;       // its second buffer under tensor parallelism (gather target)
     float* qbuf_ = nullptr;     // [n_heads_l * hd] q before RoPE
     float* qrot_ = nullptr;     // [n_heads_l * hd] q after RoPE (written by attention, for traces)
     float* kraw_ = nullptr;     // [n_kv_l * hd] this step's k before RoPE
@@ -132,6 +133,7 @@ class Engine {
     uint32_t* history_ = nullptr;  // [max_seq]
     int* pos_ = nullptr;
     int* err_ = nullptr;
+    int* step_ = nullptr;  // decode steps so far (tensor-parallel reduction epochs)
     uint8_t* act_ = nullptr;  // prepared GEMV activation (gemv_launch)
     int* chain_bar_ = nullptr;     // [L + 1][kChainMaxPhases] chain arrival counters
     float* best_val_ = nullptr;    // [2 * SMs] per-CTA argmax partials of the lm_head chain

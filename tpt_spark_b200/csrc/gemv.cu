@@ -390,6 +390,7 @@ __device__ __forceinline__ float chunk_f16(const uint8_t* slot, const Act& a, in
 // sums x^2 over the whole vector (each thread a strided set of float4, all in flight).
 constexpr int kActWarps = 8;
 
+
 __device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
     const float4 a = *reinterpret_cast<const float4*>(src);
     const float4 b = *reinterpret_cast<const float4*>(src + 4);
@@ -398,6 +399,51 @@ __device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
 
 // candle Mlp: silu(w1 x) * (w3 x), silu(a) = a / (1 + exp(-a))
 __device__ __forceinline__ float glu_val(float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); }
+
+// Epoch of this use of the tensor-parallel slot (TpLink): read after the kernel's
+// griddepcontrol.wait, so the current step's counter is visible.
+__device__ __forceinline__ unsigned int tp_epoch(const GemvParams& p) {
+    const TpLink& t = *p.tp;
+    return (unsigned int)(*reinterpret_cast<volatile const int*>(t.step)) * (unsigned int)t.uses_per_step +
+           (unsigned int)p.tp_use + 1u;
+}
+
+// 8 consecutive input elements at `off`: x, or with tp_gather x plus every rank's partial
+// in rank order.  The partials are 64-bit (value | epoch) words that peers store into this
+// rank's inbox; a word whose epoch is not yet the current one is read again (bounded; a
+// word that never arrives sets TPTC_ERR_TIMEOUT and counts as 0).
+__device__ __forceinline__ void act_in8(const GemvParams& p, int off, float (&v)[8]) {
+    if (!p.tp_gather) {
+        load8(p.x + off, v);
+        return;
+    }
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(p.x + off));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(p.x + off + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    const TpLink& t = *p.tp;
+    const unsigned int e = tp_epoch(p);
+    const unsigned long long* in = t.inbox[t.rank] + (size_t)p.tp_slot * t.size * t.dim + off;
+    for (int r = 0; r < t.size; r++) {
+        const unsigned long long* src = in + (size_t)r * t.dim;
+        unsigned long long w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) ld_volatile_u64x2(src + i, w[i], w[i + 1]);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            uint32_t n = 0;
+            while ((unsigned int)(w[i] >> 32) != e) {
+                if (++n > kWaitPolls) {
+                    if (p.err) atomicExch(p.err, TPTC_ERR_TIMEOUT);
+                    w[i] = (unsigned long long)e << 32;  // value 0
+                    break;
+                }
+                if (n > 64) __nanosleep(32);
+                w[i] = ld_volatile_u64(src + i);
+            }
+            v[i] = __fadd_rn(v[i], __uint_as_float((unsigned int)(w[i] & 0xffffffffu)));
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_constant__ GemvParams p, int transposed) {
     __shared__ float red[kActWarps];
@@ -411,14 +457,19 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
     pdl_launch_dependents();
     // then every load of x goes out before the first use: this warp's block and, with a
     // norm, this thread's share of the sum of squares
-    if (mine) load8(p.x + b * QK_K + 8 * lane, v);
+    if (mine) act_in8(p, b * QK_K + 8 * lane, v);
+    if (mine && p.tp_gather) {  // the reduced residual stream, for the next projection's residual
+        float4* xo = reinterpret_cast<float4*>(p.x_out + b * QK_K + 8 * lane);
+        xo[0] = make_float4(v[0], v[1], v[2], v[3]);
+        xo[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
     if (norm) {
         static_assert(kActWarps == kNormWarps, "the activation kernel uses the chains' norm partition");
         // every CTA sums the whole vector in the shared partition (blocks warp, warp + 8, ...)
         float ss = 0.f;
         for (int bb = warp; bb < nb; bb += kActWarps) {
             float xv[8];
-            load8(p.x + bb * QK_K + 8 * lane, xv);
+            act_in8(p, bb * QK_K + 8 * lane, xv);
             if (p.glu_in) {
                 float u[8];
                 load8(p.x + K + bb * QK_K + 8 * lane, u);
@@ -582,7 +633,14 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
             p.out[ur.row] = y;
             if (best) argbest_take(*best, y, ur.row);
         } else if (EPI == EPI_RESID) {
-            p.out[ur.out] = __ldcg(p.out + ur.out) + y;
+            if (p.tp) {  // this rank's partial row, tagged, into every rank's inbox (peer stores)
+                const TpLink& t = *p.tp;
+                const size_t at = ((size_t)p.tp_slot * t.size + t.rank) * t.dim + ur.out;
+                const unsigned long long w = ((unsigned long long)tp_epoch(p) << 32) | __float_as_uint(y);
+                for (int r = 0; r < t.size; r++) st_volatile_u64(t.inbox[r] + at, w);
+            } else {
+                p.out[ur.out] = __ldcg(p.out + ur.out) + y;
+            }
         } else if (EPI == EPI_QKV) {
             if (ur.seg == 0) {
                 p.out[ur.row] = y;  // q before RoPE

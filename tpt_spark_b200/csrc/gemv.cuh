@@ -128,8 +128,24 @@ __host__ __device__ __forceinline__ int xt_offset(int b, int lane, int nsb, int 
 constexpr int kGemvMaxSeg = 3;
 constexpr int kGemvMaxStages = 16;
 
-// One matrix of a (possibly fused) GEMV launch.  A work unit is one 8-row tile group of one
-// segment; units of consecutive segments follow each other.
+// Tensor-parallel reduction of the row-parallel projections over NVLink peer memory (tp.cpp).
+// Every rank owns an inbox [2 slots][size][dim] of 64-bit words (f32 value | 32-bit epoch);
+// inbox[r] is rank r's, mapped into this process.  A row-parallel GEMV (EPI_RESID with tp
+// set) stores each partial row, tagged with the epoch of this use of the slot, into row
+// block `rank` of slot `tp_slot` of every rank's inbox -- one 64-bit store, so a reader sees
+// a value and its epoch together and needs no separate flag or fence.  The next activation
+// kernel (tp_gather) reads every rank's block, waiting (bounded) on words whose epoch is not
+// yet the current one, and forms x_out = x + sum over ranks in rank order (the same bits on
+// every rank).  Epoch of use u of a step: step * uses_per_step + u + 1, with the step
+// counter advanced by the embedding kernel that opens every step.
+constexpr int kTpMaxRanks = 8;
+struct TpLink {
+    int rank, size, dim;
+    int uses_per_step;  // 2 per layer
+    unsigned long long* inbox[kTpMaxRanks];
+    const int* step;    // this rank's decode step counter
+};
+
 struct GemvSeg {
     DevMatrix m;
     int unit_begin;  // filled by gemv_prepare
@@ -169,6 +185,13 @@ struct GemvParams {
     uint8_t* act_global;
     int act_prepared;
     int* err;
+    // tensor parallelism over peer memory (TpLink): EPI_RESID scatters instead of adding;
+    // the activation kernel gathers (tp_gather) into x_out; tp_use = 2 * layer + slot
+    const TpLink* tp;
+    int tp_slot;
+    int tp_use;
+    int tp_gather;
+    float* x_out;
 };
 
 // A chain of GEMVs in one persistent launch (gemv.cu gemv_chain_kernel): phases separated

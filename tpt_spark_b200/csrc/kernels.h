@@ -71,7 +71,9 @@ cudaError_t attn_noalloc_scratch(int device, cudaStream_t st, uint8_t** out);
 
 // misc.cu
 // x[dim] = dequantised row `tok` of token_embd (device layout), token read from *tok_ptr.
-cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl);
+// `step` (optional): a counter the kernel increments once (the decode step, for TpLink epochs).
+cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl,
+                             int* step = nullptr);
 // argmax over logits[n] (ties -> highest index, candle sample_argmax); writes *out_tok;
 // when next_tok/pos are non-null also stores the token as the next step's input and
 // increments *pos (device-chained greedy decode).

@@ -14,9 +14,11 @@ namespace {
 // candle dequantises token_embd to f32 at load and index_selects a row; here one row is
 // dequantised on the fly (bit-identical values) into the residual stream x.
 // Replaces the reference's whole-table dequant + row copy (wgpu_engine.rs:235-242,364-368).
-__global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok_ptr, float* __restrict__ x) {
+__global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok_ptr, float* __restrict__ x,
+                                 int* step) {
     pdl_wait();
     pdl_launch_dependents();
+    if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;  // opens a decode step (TpLink epochs)
     const int row = (int)*tok_ptr;  // token_embd is never a fused gate|up matrix: phys row = row
     const int K = emb.K;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) {
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 
 }  // namespace
 
-cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl) {
+cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl,
+                             int* step) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::max(1, std::min(16, emb.K / 256)));
     cfg.blockDim = dim3(256);
@@ -115,7 +118,7 @@ cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, floa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, embed_row_kernel, emb, tok_ptr, x);
+    return cudaLaunchKernelEx(&cfg, embed_row_kernel, emb, tok_ptr, x, step);
 }
 
 cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_t* next_tok, int* pos,

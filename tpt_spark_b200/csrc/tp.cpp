@@ -13,6 +13,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <vector>
 
 #include "kernels.h"
 
@@ -27,6 +28,7 @@ struct NcclApi {
     ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -48,7 +50,9 @@ const NcclApi& nccl() {
         api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
         api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
-        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.GetErrorString;
+        api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.GetErrorString &&
+                 api.AllGather;
         if (!api.ok) api.err = "libnccl.so.2 lacks an expected symbol";
     });
     return api;
@@ -75,8 +79,56 @@ int nccl_unique_id(void* out128) {
 }
 
 Tp::~Tp() {
+    for (int r = 0; r < kTpMaxRanks; r++)
+        if (peer_base[r]) cudaIpcCloseMemHandle(peer_base[r]);
+    if (link_dev) cudaFree(link_dev);
+    if (p2p_mem) cudaFree(p2p_mem);
     if (comm && nccl().ok) nccl().CommDestroy(static_cast<ncclComm_t>(comm));
     if (buf) cudaFree(buf);
+}
+
+// Own inbox allocation, its CUDA IPC handle exchanged with every rank over NCCL, the peers'
+// allocations mapped into this process (peer access over NVLink), and the TpLink the
+// kernels read.  Every rank calls it with the same dim and layer count.
+Status Tp::init_p2p(int dim, int n_layers, const int* step, cudaStream_t st) {
+    if (size > kTpMaxRanks) return Status{TPTC_ERR_UNSUPPORTED, "peer-memory reduction supports up to 8 ranks"};
+    const size_t bytes = (size_t)2 * size * dim * sizeof(unsigned long long);
+    TPTC_CUDA_RET(cudaMalloc(&p2p_mem, bytes));
+    TPTC_CUDA_RET(cudaMemsetAsync(p2p_mem, 0, bytes, st));  // epoch 0: no use has that tag
+    cudaIpcMemHandle_t mine;
+    TPTC_CUDA_RET(cudaIpcGetMemHandle(&mine, p2p_mem));
+    void* d_handles = nullptr;
+    TPTC_CUDA_RET(cudaMalloc(&d_handles, sizeof(cudaIpcMemHandle_t) * (size + 1)));
+    uint8_t* d_all = static_cast<uint8_t*>(d_handles) + sizeof(cudaIpcMemHandle_t);
+    TPTC_CUDA_RET(cudaMemcpyAsync(d_handles, &mine, sizeof(mine), cudaMemcpyHostToDevice, st));
+    ncclResult_t nr = nccl().AllGather(d_handles, d_all, sizeof(mine), ncclUint8, static_cast<ncclComm_t>(comm), st);
+    if (nr != ncclSuccess) {
+        cudaFree(d_handles);
+        return Status{TPTC_ERR_NCCL, nccl_msg("ncclAllGather", nr)};
+    }
+    std::vector<cudaIpcMemHandle_t> all(size);
+    cudaError_t ce = cudaMemcpyAsync(all.data(), d_all, sizeof(mine) * size, cudaMemcpyDeviceToHost, st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+    cudaFree(d_handles);
+    TPTC_CUDA_RET(ce);
+    TpLink link = {};
+    link.rank = rank;
+    link.size = size;
+    link.dim = dim;
+    link.uses_per_step = 2 * n_layers;
+    link.step = step;
+    for (int r = 0; r < size; r++) {
+        void* base = p2p_mem;
+        if (r != rank) {
+            TPTC_CUDA_RET(cudaIpcOpenMemHandle(&base, all[r], cudaIpcMemLazyEnablePeerAccess));
+            peer_base[r] = base;
+        }
+        link.inbox[r] = static_cast<unsigned long long*>(base);
+    }
+    TPTC_CUDA_RET(cudaMalloc(&link_dev, sizeof(TpLink)));
+    TPTC_CUDA_RET(cudaMemcpyAsync(link_dev, &link, sizeof(link), cudaMemcpyHostToDevice, st));
+    TPTC_CUDA_RET(cudaStreamSynchronize(st));
+    return {};
 }
 
 Status Tp::init(int r, int s, const void* uid, cudaStream_t st) {

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "gemv.cuh"
 
 namespace tptc {
 
@@ -22,6 +23,11 @@ struct Tp {
     Status allreduce_add(float* part, float* x, size_t n, cudaStream_t st);
     // Sum-allreduce in place.
     Status allreduce(float* buf, size_t n, cudaStream_t st);
+    // Peer-memory reduction of the decode step's row-parallel projections (gemv.cuh TpLink).
+    Status init_p2p(int dim, int n_layers, const int* step, cudaStream_t st);
+    void* p2p_mem = nullptr;                 // own inbox
+    void* peer_base[kTpMaxRanks] = {};       // peers' allocations mapped here
+    TpLink* link_dev = nullptr;              // device copy the kernels read
 };
 
 int nccl_unique_id(void* out128);
