@@ -223,26 +223,22 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_kernel(const __grid_con
 
 namespace tc {
 
-constexpr int BM = 128;         // query rows per CTA (TMEM lanes)
-constexpr int BN = 64;          // key positions per tile
-constexpr int kStages = 2;      // K/V ring
-constexpr int kThreads = 192;
-constexpr int kTmemCols = 256;  // S: columns 0..63, O: columns 128..128 + hd
+constexpr int BM = 128;         // query rows per tile (TMEM lanes); a CTA runs two tiles
+constexpr int BN = 64;          // key positions per K/V tile
+constexpr int kStages = 3;      // K/V ring
+constexpr int kThreads = 320;   // producer, MMA, two softmax warpgroups
+constexpr int kTmemCols = 512;  // S_A 0..63, S_B 64..127, O_A 128.., O_B 256..
 
 template <int HD>
 struct Lay {
-    static constexpr int kQBytes = BM * HD * 2;   // HD / 64 blocks of [128 rows x 128 B]
-    static constexpr int kKVBytes = BN * HD * 2;  // HD / 64 blocks of [64 rows x 128 B]
-    static constexpr int kPBytes = BM * BN * 2;   // [128 rows x 128 B]
-    // P of tile j may live in the K slot of its stage once S(j) has read it (the slot is
-    // refilled only after P V(j) released the stage) when that slot is large enough
-    static constexpr bool kPInK = kKVBytes >= kPBytes;
+    static constexpr int kQBytes = BM * HD * 2;   // one query tile: HD / 64 blocks [128 x 128 B]
+    static constexpr int kKVBytes = BN * HD * 2;  // one K or V tile: HD / 64 blocks [64 x 128 B]
+    static constexpr int kPBytes = BM * BN * 2;   // one P tile [128 x 128 B]
     static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kQBytes;
+    static constexpr int kK = kQ + 2 * kQBytes;
     static constexpr int kV = kK + kStages * kKVBytes;
-    static constexpr int kP = kV + kStages * kKVBytes;  // separate P region (kPInK false)
-    static constexpr int kBytes = kP + (kPInK ? 0 : kPBytes);
-    __device__ static constexpr int p_off(int s) { return kPInK ? kK + s * kKVBytes : kP; }
+    static constexpr int kP = kV + kStages * kKVBytes;
+    static constexpr int kBytes = kP + 2 * kPBytes;
 };
 
 }  // namespace tc
@@ -257,36 +253,49 @@ __device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Two query tiles (A: rows q0 .. q0 + 127, B: the next 128) share every K/V tile: while one
+// tile's warpgroup runs its softmax the tensor core works on the other tile's products.
+// Issue order per key tile j: P V_A(j), S_A(j + 1), P V_B(j), S_B(j + 1); every commit
+// also covers the MMAs issued before it, so when a tile's S(j) lands its P V(j - 1) -- and so
+// its O and its P buffer -- is complete.
 template <int HD>
-__global__ void __launch_bounds__(tc::kThreads, 2)
+__global__ void __launch_bounds__(tc::kThreads, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                            const __grid_constant__ CUtensorMap tv, const __grid_constant__ AttnPrefillParams p) {
     using L = tc::Lay<HD>;
     using tc::BM;
     using tc::BN;
     constexpr int NC = HD / 64;  // 64-column blocks of a row
+    constexpr int S = tc::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t q_full, kv_full[tc::kStages], kv_empty[tc::kStages], s_full, p_full, o_done, drain;
+    __shared__ uint64_t q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_done[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (latest) query tiles first
+    const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (latest) query pairs first
     const int h = blockIdx.y, kvh = h / (p.n_heads / p.n_kv);
-    const int q0 = qt * BM, rows = min(BM, p.T - q0);
-    const int last = p.start + q0 + rows - 1;  // last key position any row of the tile attends to
-    const int nt = last / BN + 1;
+    const int q0 = qt * 2 * BM;
+    int rows[2], nt[2];
+    for (int t = 0; t < 2; t++) {
+        rows[t] = max(0, min(BM, p.T - q0 - t * BM));
+        nt[t] = rows[t] > 0 ? (p.start + q0 + t * BM + rows[t] - 1) / BN + 1 : 0;
+    }
+    const int ntot = max(nt[0], nt[1]);
+    const int last = p.start + q0 + (rows[1] > 0 ? BM + rows[1] : rows[0]) - 1;  // last key the CTA needs
     const int kvrow0 = kvh * p.max_seq;
 
     if (threadIdx.x == 0) {
         mbar_init(&q_full, 1);
-        for (int s = 0; s < tc::kStages; s++) {
+        for (int s = 0; s < S; s++) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(&s_full, 1);
-        mbar_init(&p_full, 4);  // one arrival per softmax warp
-        mbar_init(&o_done, 1);
+        for (int t = 0; t < 2; t++) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&p_full[t], 4);  // one arrival per softmax warp of the tile
+            mbar_init(&o_done[t], 1);
+        }
         mbar_init(&drain, 1);
         fence_mbar_init();
         abort_flag = 0;
@@ -295,19 +304,24 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = tmem_slot, tS = tmem, tO = tmem + 128;
+    const uint32_t tmem = tmem_slot;
     pdl_wait();
     pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
-            mbar_expect_tx(&q_full, L::kQBytes);
+            mbar_expect_tx(&q_full, (rows[1] > 0 ? 2 : 1) * L::kQBytes);
+            for (int t = 0; t < 2; t++) {
+                if (rows[t] == 0) continue;
 #pragma unroll
-            for (int c = 0; c < NC; c++) tma_load_2d(smem + L::kQ + c * BM * 128, &tq, h * HD + c * 64, q0, &q_full);
+                for (int c = 0; c < NC; c++)
+                    tma_load_2d(smem + L::kQ + t * L::kQBytes + c * BM * 128, &tq, h * HD + c * 64, q0 + t * BM,
+                                &q_full);
+            }
             int j = 0;
-            for (; j < nt; j++) {
-                const int s = j & 1;
-                if (j >= tc::kStages && !attn_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err, &abort_flag)) break;
+            for (; j < ntot; j++) {
+                const int s = j % S;
+                if (j >= S && !attn_wait(&kv_empty[s], ((j / S) - 1) & 1, p.err, &abort_flag)) break;
                 mbar_expect_tx(&kv_full[s], 2 * L::kKVBytes);
 #pragma unroll
                 for (int c = 0; c < NC; c++) {
@@ -317,70 +331,77 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
             }
             // the copies still in flight land before the CTA exits
             mbar_wait_bounded(&q_full, 0, nullptr);
-            for (int jj = j > tc::kStages ? j - tc::kStages : 0; jj < j; jj++)
-                mbar_wait_bounded(&kv_full[jj & 1], (jj >> 1) & 1, nullptr);
+            for (int jj = j > S ? j - S : 0; jj < j; jj++) mbar_wait_bounded(&kv_full[jj % S], (jj / S) & 1, nullptr);
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
             const uint32_t id_s = mma_idesc(BM, BN), id_o = mma_idesc(BM, HD) | kIdescBMajorMN;
-            auto issue_s = [&](int s) {
-                const uint32_t qa = smem_u32(smem + L::kQ), ka = smem_u32(smem + L::kK + s * L::kKVBytes);
+            auto issue_s = [&](int t, int j) {
+                const uint32_t qa = smem_u32(smem + L::kQ + t * L::kQBytes);
+                const uint32_t ka = smem_u32(smem + L::kK + (j % S) * L::kKVBytes);
 #pragma unroll
                 for (int c = 0; c < NC; c++)
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        mma_f16(tS, sw128_desc(qa + c * BM * 128 + 32 * kk), sw128_desc(ka + c * BN * 128 + 32 * kk),
-                                id_s, (c | kk) != 0);
+                        mma_f16(tmem + 64 * t, sw128_desc(qa + c * BM * 128 + 32 * kk),
+                                sw128_desc(ka + c * BN * 128 + 32 * kk), id_s, (c | kk) != 0);
+                mma_commit(&s_full[t]);
             };
-            auto issue_pv = [&](int j, int s) {
-                const uint32_t pa = smem_u32(smem + L::p_off(s)), va = smem_u32(smem + L::kV + s * L::kKVBytes);
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t pa = smem_u32(smem + L::kP + t * L::kPBytes);
+                const uint32_t va = smem_u32(smem + L::kV + (j % S) * L::kKVBytes);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++)
-                    mma_f16(tO, sw128_desc(pa + 32 * kk), sw128_desc_mn(va + kk * 2048, BN * 128), id_o,
-                            (j | kk) != 0);
+                    mma_f16(tmem + 128 * (t + 1), sw128_desc(pa + 32 * kk), sw128_desc_mn(va + kk * 2048, BN * 128),
+                            id_o, (j | kk) != 0);
             };
             bool ok = attn_wait(&q_full, 0, p.err, &abort_flag) && attn_wait(&kv_full[0], 0, p.err, &abort_flag);
             if (ok) {
                 tc_fence_after();
-                issue_s(0);
-                mma_commit(&s_full);
+                for (int t = 0; t < 2; t++)
+                    if (nt[t] > 0) issue_s(t, 0);
             }
-            for (int j = 0; j < nt && ok; j++) {
-                const int s = j & 1;
-                if (!attn_wait(&p_full, j & 1, p.err, &abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                issue_pv(j, s);
-                mma_commit(&kv_empty[s]);  // K_j and V_j consumed
-                if (j + 1 < nt) {
-                    const int s1 = (j + 1) & 1;
-                    if (!attn_wait(&kv_full[s1], ((j + 1) >> 1) & 1, p.err, &abort_flag)) {
+            for (int j = 0; j < ntot && ok; j++) {
+                bool next_ready = false;  // K/V tile j + 1 landed (waited for before its first S)
+                for (int t = 0; t < 2 && ok; t++) {
+                    if (j >= nt[t]) continue;
+                    if (!attn_wait(&p_full[t], j & 1, p.err, &abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    issue_s(s1);
-                    mma_commit(&s_full);
+                    issue_pv(t, j);
+                    if (j + 1 < nt[t]) {
+                        if (!next_ready) {
+                            if (!attn_wait(&kv_full[(j + 1) % S], ((j + 1) / S) & 1, p.err, &abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            next_ready = true;
+                        }
+                        issue_s(t, j + 1);
+                    } else {
+                        mma_commit(&o_done[t]);
+                    }
                 }
+                if (ok) mma_commit(&kv_empty[j % S]);  // K_j and V_j consumed by both tiles
             }
-            if (ok) mma_commit(&o_done);
             // every MMA issued has completed before TMEM is freed
             mma_commit(&drain);
             mbar_wait_bounded(&drain, 0, nullptr);
         }
-    } else {  // warps 2..5: one thread per query row
-        const int qq = warp & 3, r = 32 * qq + lane;
+    } else {  // warps 2..5: tile A, warps 6..9: tile B; one thread per query row
+        const int t = (warp - 2) >> 2, qq = warp & 3, r = 32 * qq + lane;
         const uint32_t loff = (uint32_t)(32 * qq) << 16;
-        const int pos = p.start + q0 + r;
+        const uint32_t tS = tmem + 64 * t, tO = tmem + 128 * (t + 1);
+        const int pos = p.start + q0 + t * BM + r;
         const float sl2 = p.scale * 1.4426950408889634f;
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
-        const int prow_off = (r >> 3) * 1024 + (r & 7) * 128;
-        for (int j = 0; j < nt; j++) {
-            uint8_t* prow = smem + L::p_off(j & 1) + prow_off;
-            if (!attn_wait(&s_full, j & 1, p.err, &abort_flag)) {
+        uint8_t* prow = smem + L::kP + t * L::kPBytes + (r >> 3) * 1024 + (r & 7) * 128;
+        for (int j = 0; j < nt[t]; j++) {
+            if (!attn_wait(&s_full[t], j & 1, p.err, &abort_flag)) {
                 ok = false;
                 break;
             }
@@ -405,7 +426,6 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
                 m_ref = mt;
             }
             if (j > 0 && __any_sync(0xffffffffu, move)) {
-                // P V of tile j - 1 has completed (s_full of this tile was committed after it)
 #pragma unroll 1
                 for (int c0 = 0; c0 < HD; c0 += 32) {
                     uint32_t o[32];
@@ -431,31 +451,32 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
                 *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
             l += ps;
-            if (j == nt - 1) {
-                // cache rows past the last attended position may hold anything: zero them in
-                // the V tile so that 0 * value cannot turn into NaN
-                uint8_t* sv_base = smem + L::kV + (j & 1) * L::kKVBytes;
+            if (j == ntot - 1) {
+                // cache rows past the CTA's last attended position may hold anything: zero them
+                // in the V tile so that 0 * value cannot become NaN (both warpgroups write the
+                // same zeros, each before its own P V)
+                uint8_t* vb = smem + L::kV + (j % S) * L::kKVBytes;
                 const int vr0 = last - p0 + 1, nclr = (BN - vr0) * NC * 8;
                 for (int idx = r; idx < nclr; idx += BM) {
                     const int i = vr0 + idx / (NC * 8), rem = idx % (NC * 8), c = rem >> 3, ch = rem & 7;
-                    *reinterpret_cast<uint4*>(sv_base + c * BN * 128 + (i >> 3) * 1024 + (i & 7) * 128 + ch * 16) =
+                    *reinterpret_cast<uint4*>(vb + c * BN * 128 + (i >> 3) * 1024 + (i & 7) * 128 + ch * 16) =
                         make_uint4(0, 0, 0, 0);
                 }
             }
             fence_proxy_async_smem();  // P (and the cleared V rows) before the tensor core reads them
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full);
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        if (ok && attn_wait(&o_done, 0, p.err, &abort_flag)) {
+        if (ok && nt[t] > 0 && attn_wait(&o_done[t], 0, p.err, &abort_flag)) {
             tc_fence_after();
             const float il = 1.f / l;
-            __half* orow = p.out + ((size_t)(q0 + r) * p.n_heads + h) * HD;
+            __half* orow = p.out + ((size_t)(q0 + t * BM + r) * p.n_heads + h) * HD;
 #pragma unroll 1
             for (int c0 = 0; c0 < HD; c0 += 32) {
                 uint32_t o[32];
                 tmem_ld32(tO + loff + c0, o);
-                if (r < rows) {
+                if (r < rows[t]) {
                     uint32_t w[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++)
@@ -510,7 +531,7 @@ cudaError_t launch_tc(const AttnPrefillParams& p, cudaStream_t st, bool pdl) {
     if (e == cudaSuccess) e = make_tmap_f16(&tv, p.vcache, (int64_t)p.n_kv * p.max_seq, HD, HD, tc::BN);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.T + tc::BM - 1) / tc::BM, p.n_heads);
+    cfg.gridDim = dim3((p.T + 2 * tc::BM - 1) / (2 * tc::BM), p.n_heads);
     cfg.blockDim = dim3(tc::kThreads);
     cfg.dynamicSmemBytes = tc::Lay<HD>::kBytes + 1024;
     cfg.stream = st;
