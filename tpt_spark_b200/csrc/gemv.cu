@@ -412,8 +412,9 @@ __device__ __forceinline__ unsigned int tp_epoch(const GemvParams& p) {
 // in rank order.  The partials are 64-bit (value | epoch) words that peers store into this
 // rank's inbox; a word whose epoch is not yet the current one is read again (bounded; a
 // word that never arrives sets TPTC_ERR_TIMEOUT and counts as 0).
+template <bool GATHER>
 __device__ __forceinline__ void act_in8(const GemvParams& p, int off, float (&v)[8]) {
-    if (!p.tp_gather) {
+    if (!GATHER) {
         load8(p.x + off, v);
         return;
     }
@@ -445,8 +446,8 @@ __device__ __forceinline__ void act_in8(const GemvParams& p, int off, float (&v)
     }
 }
 
-__global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_constant__ GemvParams p, int transposed) {
-    __shared__ float red[kActWarps];
+template <bool GATHER>
+__device__ __forceinline__ void act_quant_body(const GemvParams& p, int transposed, float* red) {
     const int K = p.K, nb = K / QK_K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = blockIdx.x * kActWarps + warp;
     const bool norm = p.norm_w != nullptr, mine = b < nb;
@@ -457,19 +458,30 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
     pdl_launch_dependents();
     // then every load of x goes out before the first use: this warp's block and, with a
     // norm, this thread's share of the sum of squares
-    if (mine) act_in8(p, b * QK_K + 8 * lane, v);
-    if (mine && p.tp_gather) {  // the reduced residual stream, for the next projection's residual
+    if (mine) act_in8<GATHER>(p, b * QK_K + 8 * lane, v);
+    if (mine && GATHER) {  // the reduced residual stream, for the next projection's residual
         float4* xo = reinterpret_cast<float4*>(p.x_out + b * QK_K + 8 * lane);
         xo[0] = make_float4(v[0], v[1], v[2], v[3]);
         xo[1] = make_float4(v[4], v[5], v[6], v[7]);
     }
     if (norm) {
         static_assert(kActWarps == kNormWarps, "the activation kernel uses the chains' norm partition");
-        // every CTA sums the whole vector in the shared partition (blocks warp, warp + 8, ...)
+        // every CTA sums the whole vector in the shared partition (blocks warp, warp + 8, ...),
+        // the first kHold blocks of the warp loaded together before any is summed
+        constexpr int kHold = 4;
         float ss = 0.f;
-        for (int bb = warp; bb < nb; bb += kActWarps) {
+        if (!p.glu_in) {
+            float xv[kHold][8];
+#pragma unroll
+            for (int j = 0; j < kHold; j++)
+                if (warp + j * kActWarps < nb) act_in8<GATHER>(p, (warp + j * kActWarps) * QK_K + 8 * lane, xv[j]);
+#pragma unroll
+            for (int j = 0; j < kHold; j++)
+                if (warp + j * kActWarps < nb) ss = __fadd_rn(ss, sumsq8(xv[j]));
+        }
+        for (int bb = p.glu_in ? warp : warp + kHold * kActWarps; bb < nb; bb += kActWarps) {
             float xv[8];
-            act_in8(p, bb * QK_K + 8 * lane, xv);
+            act_in8<GATHER>(p, bb * QK_K + 8 * lane, xv);
             if (p.glu_in) {
                 float u[8];
                 load8(p.x + K + bb * QK_K + 8 * lane, u);
@@ -505,6 +517,15 @@ __global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_
     act_store_block(p.act, transposed, nb, p.act_global, b, v, lane);
 }
 
+// The activation kernel; with tp_gather (tensor parallelism) its input is x plus every rank's
+// partial rows (act_in8), written back as the reduced residual stream.  Two kernels so that
+// each gets its own register allocation.
+template <bool GATHER>
+__global__ void __launch_bounds__(kActWarps * 32) act_quant_kernel(const __grid_constant__ GemvParams p, int transposed) {
+    __shared__ float red[kActWarps];
+    act_quant_body<GATHER>(p, transposed, red);
+}
+
 // A CTA's weight ring: S stages of stage_bytes after the activation region, with their
 // "full" (copy landed) and "empty" (every consumer warp done) mbarriers.  Producer and
 // consumers walk it with the same position (stage s, wrap count lap: parity source).
@@ -519,7 +540,7 @@ struct Ring {
 __device__ __forceinline__ bool wait_backoff_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
     for (uint32_t i = 0; i < kWaitPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
+        if ((i & 15) == 15 && *abort_flag) return false;
         __nanosleep(64);
     }
     if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
@@ -530,7 +551,7 @@ __device__ __forceinline__ bool wait_backoff_abort(uint64_t* bar, uint32_t parit
 __device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
     for (uint32_t i = 0; i < kWaitPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
+        if ((i & 15) == 15 && *abort_flag) return false;
     }
     if (err) atomicExch(err, TPTC_ERR_TIMEOUT);
     *abort_flag = 1;
@@ -569,11 +590,13 @@ __device__ bool produce_units(const GemvParams& p, int epi, const Ring& r, int& 
     return true;
 }
 
-// Producer lane, before the CTA may exit: every copy it issued has landed (bounded; the
-// normal path finds them all complete already, the consumers having waited for them).
-__device__ void drain_ring(const Ring& r, int s, int lap) {
+// Producer lane after an abort, before the CTA may exit: every copy it issued has landed
+// (bounded).  Without an abort the consumers wait for every stage, so the producer returns
+// at once and takes no issue slots from them.
+__device__ void drain_ring(const Ring& r, int s, int lap, volatile int* abort_flag) {
+    if (!*abort_flag) return;
     const int n = lap * r.S + s;  // stages issued
-    for (int j = n > r.S ? n - r.S : 0; j < n; j++) mbar_wait_bounded(&r.full[j % r.S], (j / r.S) & 1, nullptr);
+    for (int j = n > r.S ? n - r.S : 0; j < n; j++) mbar_wait_backoff(&r.full[j % r.S], (j / r.S) & 1, nullptr);
 }
 
 __device__ __forceinline__ Act act_view(const ActLayout& L, const uint8_t* smem) {
@@ -750,35 +773,67 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
     }
 }
 
+// The standalone GEMV (one launch per projection), written out in one body: the ring
+// bookkeeping and the unit loop inline here measured faster than the shared
+// produce_units / consume_units the chain kernel uses.
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
     __shared__ float glu_up[2][4];
-    __shared__ volatile int abort_flag;
+    int unit_no = 0;
+
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const Ring r{smem + p.act.bytes, p.stage_bytes, p.stages, full, empty};
+    const int S = p.stages;
+    const int nsb = p.K / QK_K;
+    uint8_t* ring = smem + p.act.bytes;
 
     if (tid == 0) {
-        for (int s = 0; s < r.S; s++) {
+        for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
         mbar_init(&actbar, 1);
         fence_mbar_init();
-        abort_flag = 0;
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
+        // ---------------- producer: one bulk copy per stage (a whole 8-row tile), weights
+        // only, so it runs ahead of griddepcontrol.wait
         if (lane == 0) {
-            int s = 0, lap = 0;
-            produce_units(p, EPI, r, s, lap, l2_evict_first_policy(), &abort_flag);
-            drain_ring(r, s, lap);
+            const uint64_t policy = l2_evict_first_policy();
+            int s = 0, lap = 0;  // ring stage and how many times the ring has wrapped
+            // units in pairs (u, u + grid), chunk by chunk: the order the consumers take them
+            for (int u = blockIdx.x; u < p.units;) {
+                const bool two = unit_pair(p, u, EPI);
+                // a pair goes chunk by chunk alternating its two units; a single unit alone
+                for (int i = 0; i < (two ? 2 : 1) * p.nchunks; i++) {
+                    const int c = two ? i >> 1 : i, k = two ? i & 1 : 0;
+                    {
+                        const int uk = u + k * gridDim.x, s_ = unit_seg(p, uk);
+                        const DevMatrix& m = p.seg[s_].m;
+                        const int sbb = sb_bytes(m.type);
+                        const int64_t tile0 = (int64_t)(uk - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
+                        if (lap > 0 && !mbar_wait_backoff(&empty[s], (lap - 1) & 1, p.err)) return;
+                        const int cb = min(p.cbs, nsb - c * p.cbs);
+                        const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
+                        mbar_expect_tx(&full[s], bytes);
+                        bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
+                                 &full[s], policy);
+                        if (++s == S) {
+                            s = 0;
+                            lap++;
+                        }
+                    }
+                }
+                u += (two ? 2 : 1) * gridDim.x;
+            }
         }
         return;
     }
 
+    // ---------------- consumers: one warp per tile row
     pdl_wait();
     // The next kernel may start (and prefetch its weights) only once this one is past its
     // own wait, so at most two kernels of a chain overlap.
@@ -788,10 +843,157 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         mbar_expect_tx(&actbar, (uint32_t)p.act.bytes);
         bulk_g2s(smem, p.act_global, (uint32_t)p.act.bytes, &actbar, 0);
     }
-    bool timed_out = !wait_abort(&actbar, 0, p.err, &abort_flag);
-    const Act a = act_view(p.act, smem);
-    int s = 0, lap = 0, unit_no = 0;
-    consume_units<EPI>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out);
+    bool timed_out = !mbar_wait_bounded(&actbar, 0, p.err);
+
+    Act a;
+    a.f32 = p.act.f32 >= 0 ? reinterpret_cast<const float*>(smem + p.act.f32) : nullptr;
+    a.q8k = p.act.q8k >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q8k) : nullptr;
+    a.q8k_d = p.act.q8k >= 0 ? reinterpret_cast<const float*>(smem + p.act.q8k_d) : nullptr;
+    a.q8k_bs = p.act.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act.q8k_bs) : nullptr;
+    a.q8k_ps = p.act.q8k >= 0 ? reinterpret_cast<const int16_t*>(smem + p.act.q8k_ps) : nullptr;
+    a.q80 = p.act.q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + p.act.q80) : nullptr;
+    a.q80_d = p.act.q80 >= 0 ? reinterpret_cast<const float*>(smem + p.act.q80_d) : nullptr;
+
+    // Units in pairs (u, u + grid): for every chunk the producer fills the pair's two stages
+    // back to back, and a warp reduces its row of both in one pass; with the same weight type
+    // the two dot products share the lane's activation slice (same columns).
+    int s = 0, lap = 0;  // ring stage and its phase parity source
+    auto epilogue = [&](const UnitRow& ur, float acc) {
+        if (EPI == EPI_DOTS) return;
+        const float y = warp_sum(acc);
+        if (EPI == EPI_GLU) {
+            // tile rows 0-3 are gate rows, 4-7 the matching up rows: the up warp hands its
+            // value to the gate warp through shared memory (double-buffered by unit parity,
+            // one two-warp named barrier per unit), which writes silu(gate) * up
+            const int buf = unit_no & 1;
+            if (warp >= 4 && lane == 0) glu_up[buf][warp - 4] = y;
+            pair_sync(warp & 3);
+            if (warp < 4 && lane == 0 && ur.seg >= 0)
+                p.out[ur.out] = __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
+            unit_no++;
+            return;
+        }
+        if (lane != 0 || ur.seg < 0) return;
+        if (EPI == EPI_STORE) {
+            p.out[ur.row] = y;
+        } else if (EPI == EPI_RESID) {
+            if (p.tp) {  // this rank's partial row, tagged, into every rank's inbox (peer stores)
+                const TpLink& t = *p.tp;
+                const size_t at = ((size_t)p.tp_slot * t.size + t.rank) * t.dim + ur.out;
+                const unsigned long long w = ((unsigned long long)tp_epoch(p) << 32) | __float_as_uint(y);
+                for (int r = 0; r < t.size; r++) st_volatile_u64(t.inbox[r] + at, w);
+            } else {
+                p.out[ur.out] += y;
+            }
+        } else if (EPI == EPI_QKV) {
+            if (ur.seg == 0) {
+                p.out[ur.row] = y;  // q before RoPE
+            } else if (ur.seg == 1) {
+                p.kraw[ur.row] = y;  // k before RoPE
+            } else {
+                const int pos = *p.pos, d = ur.row % p.hd, head = ur.row / p.hd;
+                const int64_t at = ((int64_t)head * p.max_seq + pos) * p.hd + d;
+                if (p.kv_f32) static_cast<float*>(p.vcache)[at] = y;
+                else static_cast<__half*>(p.vcache)[at] = __float2half_rn(y);
+            }
+        }
+    };
+    // one row chunk of one unit on its own (DOTS test hook, mixed types, Q8_0, F16)
+    auto single = [&](const DevMatrix& m, const UnitRow& ur, const uint8_t* stage, int c0, int cb) -> float {
+        if (ur.seg < 0) return 0.f;
+        const int sbm = sb_main_bytes(m.type), sbd = sb_d_bytes(m.type);
+        const uint8_t* slot = stage + warp * cb * sbm;
+        const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
+        int32_t* isum_row = nullptr;
+        int32_t* msum_row = nullptr;
+        if (EPI == EPI_DOTS) {
+            const int per_row = m.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
+            isum_row = p.isum + (int64_t)ur.row * per_row;
+            msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
+        }
+        switch (m.type) {
+        case TPTC_TYPE_Q4_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                return q4k_half(slot, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q6_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                return q6k_half(slot, dsec, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
+        default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
+        }
+    };
+    for (int u = blockIdx.x; u < p.units;) {
+        const int u2 = u + gridDim.x;
+        const bool two = unit_pair(p, u, EPI);
+        const UnitRow ra = unit_row(p, u, warp);
+        const UnitRow rb = unit_row(p, two ? u2 : u, warp);
+        const DevMatrix& ma = p.seg[unit_seg(p, u)].m;
+        const DevMatrix& mb = p.seg[unit_seg(p, two ? u2 : u)].m;
+        const int ty = ma.type;
+        const bool paired = two;
+        float acca = 0.f, accb = 0.f;
+        for (int c = 0; c < p.nchunks; c++) {
+            const int sa = s;
+            if (!timed_out && !mbar_wait_bounded(&full[sa], lap & 1, p.err)) timed_out = true;
+            if (++s == S) {
+                s = 0;
+                lap++;
+            }
+            int sb2 = sa;
+            if (two) {
+                sb2 = s;
+                if (!timed_out && !mbar_wait_bounded(&full[sb2], lap & 1, p.err)) timed_out = true;
+                if (++s == S) {
+                    s = 0;
+                    lap++;
+                }
+            }
+            if (!timed_out) {
+                const int c0 = c * p.cbs, cb = min(p.cbs, nsb - c0);
+                const uint8_t* stA = ring + sa * p.stage_bytes;
+                const uint8_t* stB = ring + sb2 * p.stage_bytes;
+                if (paired) {
+                    if (lane < 2 * cb) {
+                        const int sbm = sb_main_bytes(ty), sbd = sb_d_bytes(ty);
+                        XHalf xh;
+                        if (ty == TPTC_TYPE_Q4_K) {
+                            load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                            acca += q4k_half(stA + warp * cb * sbm, xh, lane);
+                            accb += q4k_half(stB + warp * cb * sbm, xh, lane);
+                        } else {
+                            load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                            const int doff = kTileRows * cb * sbm + warp * cb * sbd;
+                            acca += q6k_half(stA + warp * cb * sbm, reinterpret_cast<const uint16_t*>(stA + doff), xh, lane);
+                            accb += q6k_half(stB + warp * cb * sbm, reinterpret_cast<const uint16_t*>(stB + doff), xh, lane);
+                        }
+                    }
+                } else {
+                    acca += single(ma, ra, stA, c0, cb);
+                    if (two) accb += single(mb, rb, stB, c0, cb);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[sa]);
+                if (two) mbar_arrive(&empty[sb2]);
+            }
+        }
+        epilogue(ra, acca);
+        if (two) epilogue(rb, accb);
+        u += (two ? 2 : 1) * gridDim.x;
+    }
 }
 
 // ---------------------------------------------------------------- GEMV chains
@@ -951,7 +1153,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
             const uint64_t policy = l2_evict_first_policy();
             for (int ph = 0; ph < c.nph; ph++)
                 if (!produce_units(c.ph[ph], c.epi[ph], r, s, lap, policy, &abort_flag)) break;
-            drain_ring(r, s, lap);
+            drain_ring(r, s, lap, &abort_flag);
         }
         return;
     }
@@ -1121,7 +1323,8 @@ cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl)
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, act_quant_kernel, p, epi == EPI_DOTS ? 0 : 1);
+        cudaError_t e = p.tp_gather ? cudaLaunchKernelEx(&cfg, act_quant_kernel<true>, p, epi == EPI_DOTS ? 0 : 1)
+                                    : cudaLaunchKernelEx(&cfg, act_quant_kernel<false>, p, epi == EPI_DOTS ? 0 : 1);
         if (e != cudaSuccess) return e;
     }
     switch (epi) {
