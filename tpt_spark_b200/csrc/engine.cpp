@@ -439,9 +439,7 @@ Status Engine::alloc_runtime() {
     CU(cudaMemcpyAsync(rope_cos_, c.data(), c.size() * 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaMemcpyAsync(rope_sin_, s.data(), s.size() * 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaStreamSynchronize(stream_));
-    // the row-parallel partial buffer is baked into the graphs: allocate it before capture
-    // (cudaMalloc is not allowed while a stream is capturing)
-    if (tp_ && !tp_->partial(m.dim)) return err(TPTC_ERR_OOM, "tensor-parallel partial buffer");
+    // the peer-memory inboxes are baked into the graphs: map them before capture
     if (tp_) RET_IF(tp_->init_p2p(m.dim, m.n_layers, step_, stream_));
     RET_IF(build_decode_graph(false, &graph_plain_));
     RET_IF(build_decode_graph(true, &graph_chained_));

@@ -84,7 +84,6 @@ Tp::~Tp() {
     if (link_dev) cudaFree(link_dev);
     if (p2p_mem) cudaFree(p2p_mem);
     if (comm && nccl().ok) nccl().CommDestroy(static_cast<ncclComm_t>(comm));
-    if (buf) cudaFree(buf);
 }
 
 // Own inbox allocation, its CUDA IPC handle exchanged with every rank over NCCL, the peers'
@@ -165,17 +164,6 @@ bool tp_shard(int which, int n_heads, int n_kv_heads, int head_dim, int dim, int
     case TPTC_SHARD_DOWN: r1 = dim; k0 = rank * fl; k1 = k0 + fl; return true;
     }
     return false;
-}
-
-float* Tp::partial(size_t n) {
-    if (n > buf_elems) {
-        if (buf) cudaFree(buf);
-        buf = nullptr;
-        buf_elems = 0;
-        if (cudaMalloc(&buf, n * sizeof(float)) != cudaSuccess) return nullptr;
-        buf_elems = n;
-    }
-    return buf;
 }
 
 Status Tp::allreduce(float* b, size_t n, cudaStream_t st) {

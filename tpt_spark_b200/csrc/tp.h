@@ -1,6 +1,6 @@
-// tp.h -- Megatron tensor parallelism over NCCL: one context per GPU, column-parallel
-// q/k/v/gate/up, row-parallel o/down, and a sum-allreduce of the row-parallel output into
-// the replicated residual stream after each row-parallel projection.
+// tp.h -- Megatron tensor parallelism: one context per GPU, column-parallel q/k/v/gate/up,
+// row-parallel o/down.  The decode step reduces the row-parallel outputs over NVLink peer
+// memory (TpLink, gemv.cuh); the batched prefill sum-allreduces them with NCCL.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -13,12 +13,8 @@ namespace tptc {
 struct Tp {
     int rank = 0, size = 1;
     void* comm = nullptr;  // ncclComm_t
-    float* buf = nullptr;  // device scratch for row-parallel partial outputs
-    size_t buf_elems = 0;
     ~Tp();
     Status init(int rank, int size, const void* uid, cudaStream_t st);
-    // Device buffer of at least n floats for a row-parallel partial product.
-    float* partial(size_t n);
     // x[n] += sum over ranks of part[n] (every rank ends with the same x).
     Status allreduce_add(float* part, float* x, size_t n, cudaStream_t st);
     // Sum-allreduce in place.
