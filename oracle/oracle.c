@@ -43,6 +43,7 @@
 #ifdef _OPENMP
 #include <omp.h>
 #endif
+#include <immintrin.h>
 
 #define QK_K 256
 #define QK8_0 32
@@ -68,6 +69,15 @@ void or_set_trace(float* trace) { g_trace = trace; }
 
 void or_set_threads(int n) { g_threads = n > 0 ? n : 1; }
 int or_get_threads(void) { return g_threads; }
+
+/* AVX2 versions of the quantised vec dots (on by default).  They keep candle's
+ * vec_dot_unopt accumulation exactly: its eight int32 lanes aux32[l] collect the products of
+ * elements l (mod 8), which is one 8-lane vector; the per-block float update
+ * sums[l] += d * (float)aux32[l] is the same multiply and add per lane; the lanes are summed
+ * in order at the end.  So both paths return the same bits (tests/test_oracle_golden.py
+ * compares them); the scalar path stays for reference. */
+static int g_simd = 1;
+void or_set_simd(int on) { g_simd = on ? 1 : 0; }
 
 /* ---------------------------------------------------------------- half floats */
 
@@ -335,8 +345,109 @@ int or_block_dots(int type, const void* wrow, const void* xq, int nb, int32_t* i
 
 /* ------------------------------------------------------------------ vec dots */
 
+/* Eight int8 values at p as eight int32 lanes. */
+static inline __m256i ld8_epi32(const int8_t* p) {
+    return _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i*)p));
+}
+
+/* Lanes summed in order 0..7, as the scalar loop does. */
+static inline float sum8_in_order(__m256 v) {
+    float t[8];
+    _mm256_storeu_ps(t, v);
+    float s = 0.f;
+    for (int l = 0; l < 8; l++) s += t[l];
+    return s;
+}
+
+static float vec_dot_q4k_avx2(int n, const uint8_t* w, const or_q8k* y) {
+    __m256 sums = _mm256_setzero_ps();
+    float sumf = 0.f;
+    const __m256i m4 = _mm256_set1_epi8(0x0f);
+    for (int b = 0; b < n / QK_K; b++) {
+        const uint8_t* blk = w + (size_t)b * Q4K_BYTES;
+        uint8_t sc[8], mn[8];
+        q4k_scale_min(blk + 4, sc, mn);
+        const uint8_t* qs = blk + 16;
+        int8_t a[QK_K];
+        for (int g = 0; g < 4; g++) {  /* low nibbles: elements 64g..64g+31, high: +32 */
+            const __m256i q = _mm256_loadu_si256((const __m256i*)(qs + 32 * g));
+            _mm256_storeu_si256((__m256i*)(a + 64 * g), _mm256_and_si256(q, m4));
+            _mm256_storeu_si256((__m256i*)(a + 64 * g + 32), _mm256_and_si256(_mm256_srli_epi16(q, 4), m4));
+        }
+        int32_t sumi = 0;
+        for (int j = 0; j < 16; j++) sumi += (int32_t)y[b].bsums[j] * mn[j / 2];
+        __m256i aux = _mm256_setzero_si256();
+        for (int s8 = 0; s8 < 8; s8++) {
+            const __m256i scale = _mm256_set1_epi32(sc[s8]);
+            for (int k4 = 0; k4 < 4; k4++) {
+                const int idx = 32 * s8 + 8 * k4;
+                const __m256i prod = _mm256_mullo_epi32(ld8_epi32(y[b].qs + idx), ld8_epi32(a + idx));
+                aux = _mm256_add_epi32(aux, _mm256_mullo_epi32(scale, prod));
+            }
+        }
+        const float d = or_h2f(rd16(blk)) * y[b].d;
+        sums = _mm256_add_ps(sums, _mm256_mul_ps(_mm256_set1_ps(d), _mm256_cvtepi32_ps(aux)));
+        const float dmin = or_h2f(rd16(blk + 2)) * y[b].d;
+        sumf -= dmin * (float)sumi;
+    }
+    return sumf + sum8_in_order(sums);
+}
+
+static float vec_dot_q6k_avx2(int n, const uint8_t* w, const or_q8k* y) {
+    __m256 sums = _mm256_setzero_ps();
+    const __m256i m4 = _mm256_set1_epi8(0x0f), m2 = _mm256_set1_epi8(0x03), k32 = _mm256_set1_epi8(32);
+    for (int b = 0; b < n / QK_K; b++) {
+        const uint8_t* blk = w + (size_t)b * Q6K_BYTES;
+        const int8_t* sc = (const int8_t*)(blk + 192);
+        int8_t a[QK_K];
+        for (int h = 0; h < 2; h++) {  /* elements 128h + l, +32, +64, +96 (q6k_val) */
+            const __m256i ql0 = _mm256_loadu_si256((const __m256i*)(blk + 64 * h));
+            const __m256i ql1 = _mm256_loadu_si256((const __m256i*)(blk + 64 * h + 32));
+            const __m256i qh = _mm256_loadu_si256((const __m256i*)(blk + 128 + 32 * h));
+            const __m256i h0 = _mm256_slli_epi16(_mm256_and_si256(qh, m2), 4);
+            const __m256i h1 = _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(qh, 2), m2), 4);
+            const __m256i h2 = _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(qh, 4), m2), 4);
+            const __m256i h3 = _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(qh, 6), m2), 4);
+            const __m256i q1 = _mm256_or_si256(_mm256_and_si256(ql0, m4), h0);
+            const __m256i q2 = _mm256_or_si256(_mm256_and_si256(ql1, m4), h1);
+            const __m256i q3 = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(ql0, 4), m4), h2);
+            const __m256i q4 = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(ql1, 4), m4), h3);
+            _mm256_storeu_si256((__m256i*)(a + 128 * h), _mm256_sub_epi8(q1, k32));
+            _mm256_storeu_si256((__m256i*)(a + 128 * h + 32), _mm256_sub_epi8(q2, k32));
+            _mm256_storeu_si256((__m256i*)(a + 128 * h + 64), _mm256_sub_epi8(q3, k32));
+            _mm256_storeu_si256((__m256i*)(a + 128 * h + 96), _mm256_sub_epi8(q4, k32));
+        }
+        __m256i aux = _mm256_setzero_si256();
+        for (int j = 0; j < QK_K / 16; j++) {
+            const __m256i scale = _mm256_set1_epi32(sc[j]);
+            for (int k2 = 0; k2 < 2; k2++) {
+                const int idx = 16 * j + 8 * k2;
+                const __m256i prod = _mm256_mullo_epi32(ld8_epi32(y[b].qs + idx), ld8_epi32(a + idx));
+                aux = _mm256_add_epi32(aux, _mm256_mullo_epi32(scale, prod));
+            }
+        }
+        const float d = or_h2f(rd16(blk + 208)) * y[b].d;
+        sums = _mm256_add_ps(sums, _mm256_mul_ps(_mm256_set1_ps(d), _mm256_cvtepi32_ps(aux)));
+    }
+    return sum8_in_order(sums);
+}
+
+/* Integer sum of one Q8_0 x Q8_0 block (exact in any order). */
+static inline int32_t q80_block_int_avx2(const uint8_t* blk, const uint8_t* xb) {
+    const __m256i a = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)(blk + 2)));
+    const __m256i b = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)(xb + 2)));
+    const __m256i c = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)(blk + 18)));
+    const __m256i e = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i*)(xb + 18)));
+    __m256i s = _mm256_add_epi32(_mm256_madd_epi16(a, b), _mm256_madd_epi16(c, e));
+    __m128i t = _mm_add_epi32(_mm256_castsi256_si128(s), _mm256_extracti128_si256(s, 1));
+    t = _mm_add_epi32(t, _mm_shuffle_epi32(t, 0x4e));
+    t = _mm_add_epi32(t, _mm_shuffle_epi32(t, 0xb1));
+    return _mm_cvtsi128_si32(t);
+}
+
 /* candle Q4K::vec_dot_unopt order: eight lane sums of d*aux32, mins subtracted from sumf. */
 static float vec_dot_q4k(int n, const uint8_t* w, const or_q8k* y) {
+    if (g_simd) return vec_dot_q4k_avx2(n, w, y);
     float sums[8] = {0}, sumf = 0.f;
     for (int b = 0; b < n / QK_K; b++) {
         const uint8_t* blk = w + (size_t)b * Q4K_BYTES;
@@ -372,6 +483,7 @@ static float vec_dot_q4k(int n, const uint8_t* w, const or_q8k* y) {
 
 /* candle Q6K::vec_dot_unopt order. */
 static float vec_dot_q6k(int n, const uint8_t* w, const or_q8k* y) {
+    if (g_simd) return vec_dot_q6k_avx2(n, w, y);
     float sums[8] = {0};
     for (int b = 0; b < n / QK_K; b++) {
         const uint8_t* blk = w + (size_t)b * Q6K_BYTES;
@@ -401,7 +513,7 @@ static float vec_dot_q80(int n, const uint8_t* w, const uint8_t* xq) {
     for (int b = 0; b < n / QK8_0; b++) {
         const uint8_t* blk = w + (size_t)b * Q80_BYTES;
         const uint8_t* xb = xq + (size_t)b * Q80_BYTES;
-        int32_t si = q80_block_int(blk, xb);
+        int32_t si = g_simd ? q80_block_int_avx2(blk, xb) : q80_block_int(blk, xb);
         sumf += (float)si * or_h2f(rd16(blk)) * or_h2f(rd16(xb));
     }
     return sumf;

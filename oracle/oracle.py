@@ -74,6 +74,8 @@ def lib():
         L.or_set_trace.argtypes = [vp]
         L.or_set_threads.restype = None
         L.or_set_threads.argtypes = [i32]
+        L.or_set_simd.restype = None
+        L.or_set_simd.argtypes = [i32]
         L.or_rope_table.restype = None
         L.or_rope_table.argtypes = [i32, i32, ctypes.c_float, ctypes.c_float, vp, vp]
         L.or_set_threads(os.cpu_count() or 1)
@@ -83,6 +85,11 @@ def lib():
 
 def set_threads(n: int) -> None:
     lib().or_set_threads(int(n))
+
+
+def set_simd(on: bool) -> None:
+    """AVX2 quantised dots (default) or the scalar reference loops; both give the same bits."""
+    lib().or_set_simd(1 if on else 0)
 
 
 def _p(a: np.ndarray):

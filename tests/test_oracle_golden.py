@@ -152,3 +152,38 @@ def test_forward_prefill_equals_incremental(tmp_path):
         lb = b.forward([t], i)
     # same math; only the attention mask path differs
     np.testing.assert_allclose(la, lb, rtol=0, atol=1e-4)
+
+
+@pytest.mark.parametrize("t,N,K", [(O.Q4_K, 48, 4096), (O.Q6_K, 40, 14336), (O.Q8_0, 33, 4096)])
+def test_oracle_simd_dots_match_scalar(t, N, K):
+    """The oracle's AVX2 dots keep candle vec_dot_unopt's lane structure: bit-identical."""
+    from tpt_spark_b200 import synth
+
+    rng = np.random.default_rng(N + K)
+    raw = synth.encode(t, synth.normal(77 + N, N * K, 0.02))
+    x = (rng.standard_normal((3, K)) * rng.choice([0.01, 1.0, 20.0], (3, K))).astype(np.float32)
+    try:
+        O.set_simd(True)
+        fast = O.matmul(t, raw, N, K, x)
+        O.set_simd(False)
+        slow = O.matmul(t, raw, N, K, x)
+    finally:
+        O.set_simd(True)
+    np.testing.assert_array_equal(fast.view(np.uint32), slow.view(np.uint32))
+
+
+def test_oracle_simd_forward_matches_scalar(tmp_path):
+    from tpt_spark_b200 import synth
+
+    path = str(tmp_path / "m.gguf")
+    synth.write_gguf(path, synth.TINY["tiny_q4km"], seed=3)
+    m = O.Model(path)
+    prompt = [5, 17, 300, 2, 9]
+    try:
+        O.set_simd(True)
+        a = m.forward(prompt, 0)
+        O.set_simd(False)
+        b = m.forward(prompt, 0)
+    finally:
+        O.set_simd(True)
+    np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
