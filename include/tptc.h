@@ -128,6 +128,15 @@ TPTC_API int tptc_set_kv_dtype(tptc_ctx* ctx, int ggml_type);
  * min_tokens <= 0, and every prompt with an f32 KV cache go token by token through the decode
  * step (bit-identical to decoding them).  Default 16; may be changed at any time. */
 TPTC_API int tptc_set_prefill_gemm_min(tptc_ctx* ctx, int min_tokens);
+/* How the batched prefill contracts Q4_K / Q6_K / Q8_0 weights: with the fused-dequant GEMM
+ * (blocks expanded to fp16 in shared memory, tptc_gemm_q) or by expanding the matrix to fp16
+ * in HBM first and running the fp16 GEMM.  TPTC_FUSED_AUTO (default) picks per matrix and
+ * chunk with a wave model of both (the fused GEMM wins for short chunks of wide matrices);
+ * NEVER and ALWAYS force one path.  The fused expansion rounds the Q4_K / Q6_K scale product
+ * to fp16 before applying the code, so its weights are within one fp16 rounding of the
+ * two-pass ones (Q8_0: identical). */
+enum { TPTC_FUSED_NEVER = 0, TPTC_FUSED_AUTO = 1, TPTC_FUSED_ALWAYS = 2 };
+TPTC_API int tptc_set_prefill_fused(tptc_ctx* ctx, int mode);
 
 /* LlmEngine::load (mod.rs:66-70) -> load_gguf_to_vram (wgpu_loader.rs:87-201): mmap the
  * file, parse GGUF v3, check bounds, stream every tensor through pinned staging with
@@ -220,6 +229,10 @@ TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_
  * and B row-major fp16 (16-byte aligned), K a multiple of 64 -- the prompt-wide replacement of
  * gemm.wgsl's per-token M = 1 products. */
 TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream);
+/* The prefill GEMM with the weight dequantisation fused in: C[M x N] (f32) = A[M x K] . W^T
+ * with A row-major fp16 (16-byte aligned) and W a Q4_K / Q6_K / Q8_0 matrix (tptc_matrix,
+ * N x K): the quantised blocks reach shared memory by TMA and are expanded there to fp16. */
+TPTC_API int tptc_gemm_q(const tptc_matrix* m, const void* d_a, float* d_c, int M, void* stream);
 
 /* Causal GQA attention of a prompt chunk on the tensor cores (the prefill replacement of
  * attention.wgsl's per-token passes, :31-170, run once per prompt token by

@@ -219,6 +219,42 @@ def test_prefill_in_pieces_is_bit_identical(engines_f16, tiny_models, name):
     np.testing.assert_array_equal(split, whole)
 
 
+@pytest.mark.parametrize("name", ["tiny_q4km", "tiny_q8_0"])
+def test_fused_dequant_prefill_matches_float_reference(tiny_models, cuda_device, name):
+    """Every quantised projection through the fused-dequant GEMM (TPTC_FUSED_ALWAYS): the same
+    float-reference bound as the two-pass path, and close to the two-pass logits (the fused
+    expansion differs from the two-pass one by at most one fp16 rounding of the scale
+    product; Q8_0 weights are identical, so the logits are too)."""
+    from tpt_spark_b200.engine import CudaEngine
+
+    ref = O.Model(tiny_models[name])
+    e = CudaEngine(0, kv_dtype="f16")
+    try:
+        e.load(tiny_models[name])
+        e.set_prefill_gemm_min(1)
+        for n in (150, 33):
+            prompt = _prompt(ref, n, n + 1)
+            e.set_prefill_fused("always")
+            e.kv_reset()
+            fused = e.prefill(prompt)
+            e.set_prefill_fused("never")
+            e.kv_reset()
+            two_pass = e.prefill(prompt)
+            want = float_prefill_logits(ref, prompt)
+            diff = float(np.abs(fused - want).max())
+            print(f"{name} n={n}: fused max |logit - float64 reference| = {diff:.2e}, "
+                  f"vs two-pass {float(np.abs(fused - two_pass).max()):.2e}")
+            assert diff <= LOGIT_ATOL_FLOAT_REF
+            if name == "tiny_q8_0":
+                np.testing.assert_array_equal(fused, two_pass)
+            else:
+                assert float(np.abs(fused - two_pass).max()) <= LOGIT_ATOL_FLOAT_REF
+        with pytest.raises(ValueError):
+            e.set_prefill_fused("sometimes")
+    finally:
+        e.close()
+
+
 def test_threshold_and_f32_cache_use_the_token_path(tiny_models, cuda_device):
     """Below the threshold (and always with an f32 cache) the prompt runs token by token:
     bit-identical to decoding it."""

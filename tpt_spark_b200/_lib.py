@@ -45,6 +45,7 @@ SIGNATURES = {
     "tptc_device_count": (c_int, []),
     "tptc_set_kv_dtype": (c_int, [c_vp, c_int]),
     "tptc_set_prefill_gemm_min": (c_int, [c_vp, c_int]),
+    "tptc_set_prefill_fused": (c_int, [c_vp, c_int]),
     "tptc_tp_shard": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     "tptc_load_gguf": (c_int, [c_vp, ctypes.c_char_p, PROGRESS_CB, c_vp]),
     "tptc_unload": (c_int, [c_vp]),
@@ -74,6 +75,7 @@ SIGNATURES = {
     "tptc_matrix_dequant_f16": (c_int, [c_vp, c_vp, c_vp]),
     "tptc_block_dots": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp]),
     "tptc_gemm_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
+    "tptc_gemm_q": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp]),
     "tptc_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "tptc_attn_decode_workspace_bytes": (c_i64, [c_int, c_int, c_int, c_int]),
     "tptc_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp,

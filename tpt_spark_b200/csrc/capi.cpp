@@ -123,6 +123,14 @@ TPTC_API int tptc_set_prefill_gemm_min(tptc_ctx* ctx, int min_tokens) {
     return TPTC_OK;
 }
 
+TPTC_API int tptc_set_prefill_fused(tptc_ctx* ctx, int mode) {
+    if (!ctx) return TPTC_ERR_ARG;
+    if (mode != TPTC_FUSED_NEVER && mode != TPTC_FUSED_AUTO && mode != TPTC_FUSED_ALWAYS)
+        return fail_code(ctx, TPTC_ERR_ARG, "prefill fused mode must be TPTC_FUSED_NEVER, AUTO or ALWAYS");
+    ctx->eng->set_prefill_fused(mode);
+    return TPTC_OK;
+}
+
 TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user) {
     if (!ctx || !path) return fail_code(ctx, TPTC_ERR_ARG, "null argument");
     Status s = ctx->eng->load(path, progress, user);
@@ -464,6 +472,25 @@ TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, 
     cudaError_t e = tptc::gemm_tc(tptc::GEMM_STORE, static_cast<const __half*>(d_a), K, static_cast<const __half*>(d_b),
                                   K, p, static_cast<cudaStream_t>(stream), false);
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemm_tc");
+}
+
+TPTC_API int tptc_gemm_q(const tptc_matrix* m, const void* d_a, float* d_c, int M, void* stream) {
+    if (!m || !d_a || !d_c || M <= 0) return fail_code(nullptr, TPTC_ERR_ARG, "gemm_q: bad argument");
+    if (!tptc::gemm_q_supported(m->m) || m->m.glu)
+        return fail_code(nullptr, TPTC_ERR_UNSUPPORTED, "gemm_q: Q4_K, Q6_K or Q8_0 matrices only");
+    if (reinterpret_cast<uintptr_t>(d_a) & 15) return fail_code(nullptr, TPTC_ERR_ARG, "gemm_q: A must be 16-byte aligned");
+    int dev = 0, sms = 0;
+    if (int rc = ensure_kernels(&dev, &sms)) return rc;
+    tptc::GemmTcParams p = {};
+    p.M = M;
+    p.N = m->m.N;
+    p.K = m->m.K;
+    p.c = d_c;
+    p.ldc = m->m.N;
+    p.err = m->err;
+    cudaError_t e = tptc::gemm_q(tptc::GEMM_STORE, static_cast<const __half*>(d_a), m->m.K, m->m, p,
+                                 static_cast<cudaStream_t>(stream), false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "gemm_q");
 }
 
 TPTC_API int tptc_attn_prefill(const void* d_q, const void* d_kcache, const void* d_vcache, void* d_out, int T,

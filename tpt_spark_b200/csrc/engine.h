@@ -61,6 +61,9 @@ class Engine {
     // Prompts of at least n tokens take the batched tensor-core prefill (fp16 KV cache only);
     // shorter ones, or all when n <= 0, run token by token through the decode step.
     void set_prefill_gemm_min(int n) { prefill_gemm_min_ = n; }
+    // When the batched prefill contracts quantised weights with the fused-dequant GEMM
+    // (TPTC_FUSED_NEVER / AUTO / ALWAYS) instead of expanding each matrix to fp16 first.
+    void set_prefill_fused(int mode) { prefill_fused_ = mode; }
     bool prefill_uses_gemm(int n) const;
     int prefix_len(const uint32_t* ids, int n) const;
 
@@ -144,6 +147,7 @@ class Engine {
     // batched prefill: buffers allocated on demand for the chunk size (tokens)
     static constexpr int kPrefillChunk = 8192;
     int prefill_gemm_min_ = 16;
+    int prefill_fused_ = TPTC_FUSED_AUTO;
     uint8_t* pf_ = nullptr;
     size_t pf_size_ = 0;
     int pf_chunk_ = 0;

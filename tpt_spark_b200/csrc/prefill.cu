@@ -126,6 +126,7 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 cudaError_t prefill_init_device() {
     cudaError_t e = gemm_tc_init_device();
+    if (e == cudaSuccess) e = gemm_q_init_device();
     if (e != cudaSuccess) return e;
     return attn_prefill_init_device();
 }
@@ -185,6 +186,20 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
     const int nq = n_heads_l_ * hd, nk = n_kv_l_ * hd, nqkv = nq + 2 * nk;
     const size_t layer_kv = (size_t)2 * n_kv_l_ * max_seq_ * hd * 2;  // bytes (fp16 cache)
     cudaStream_t st = stream_;
+    // A quantised weight is contracted by the fused-dequant GEMM (its blocks expanded in shared
+    // memory) where the wave model expects that to be faster (TPTC_FUSED_AUTO) or always
+    // (TPTC_FUSED_ALWAYS); otherwise it is expanded to fp16 in pf_w_ first (one pass over the
+    // matrix) and contracted by gemm_tc.  A gate|up matrix is used in its physical row order
+    // (4 gate rows, then the 4 matching up rows), which the GLU epilogue expects.
+    auto fused = [&](const DevMatrix& w) {
+        if (prefill_fused_ == TPTC_FUSED_NEVER || !gemm_q_supported(w)) return false;
+        return prefill_fused_ == TPTC_FUSED_ALWAYS || gemm_q_preferred(w, T, w.N, sm_count_);
+    };
+    auto matmul = [&](int epi, const __half* a, const DevMatrix& w, const GemmTcParams& g) -> cudaError_t {
+        if (fused(w)) return gemm_q(epi, a, g.K, w, g, st, false);
+        cudaError_t e = launch_dequant_rows_f16(w, 0, g.N, pf_w_, st, w.glu != 0);
+        return e != cudaSuccess ? e : gemm_tc(epi, a, g.K, pf_w_, g.K, g, st, false);
+    };
     embed_rows_kernel<<<T, 256, 0, st>>>(embd_, pf_ids_, pf_x_);
     TPTC_CUDA_RET(cudaGetLastError());
     for (int l = 0; l < m.n_layers; l++) {
@@ -194,9 +209,6 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         // attention block
         rmsnorm_f16_kernel<<<T, 256, 0, st>>>(pf_x_, L.attn_norm, dim, m.rms_eps, pf_xn_);
         TPTC_CUDA_RET(cudaGetLastError());
-        TPTC_CUDA_RET(launch_dequant_rows_f16(L.q, 0, nq, pf_w_, st));
-        TPTC_CUDA_RET(launch_dequant_rows_f16(L.k, 0, nk, pf_w_ + (size_t)nq * dim, st));
-        TPTC_CUDA_RET(launch_dequant_rows_f16(L.v, 0, nk, pf_w_ + (size_t)(nq + nk) * dim, st));
         GemmTcParams g = {};
         g.M = T;
         g.N = nqkv;
@@ -204,7 +216,21 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         g.c = pf_qkv_;
         g.ldc = nqkv;
         g.err = err_;
-        TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_xn_, dim, pf_w_, dim, g, st, false));
+        if (fused(L.q) && fused(L.k) && fused(L.v)) {  // three GEMMs into the column ranges
+            GemmTcParams gq = g;
+            gq.N = nq;
+            TPTC_CUDA_RET(gemm_q(GEMM_STORE, pf_xn_, dim, L.q, gq, st, false));
+            gq.N = nk;
+            gq.c = pf_qkv_ + nq;
+            TPTC_CUDA_RET(gemm_q(GEMM_STORE, pf_xn_, dim, L.k, gq, st, false));
+            gq.c = pf_qkv_ + nq + nk;
+            TPTC_CUDA_RET(gemm_q(GEMM_STORE, pf_xn_, dim, L.v, gq, st, false));
+        } else {
+            TPTC_CUDA_RET(launch_dequant_rows_f16(L.q, 0, nq, pf_w_, st));
+            TPTC_CUDA_RET(launch_dequant_rows_f16(L.k, 0, nk, pf_w_ + (size_t)nq * dim, st));
+            TPTC_CUDA_RET(launch_dequant_rows_f16(L.v, 0, nk, pf_w_ + (size_t)(nq + nk) * dim, st));
+            TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_xn_, dim, pf_w_, dim, g, st, false));
+        }
         QkvPostParams qp = {pf_qkv_, pf_q_, kc, vc, rope_cos_, rope_sin_, start, n_heads_l_, n_kv_l_, hd, max_seq_};
         qkv_post_kernel<<<T, 256, 0, st>>>(qp);
         TPTC_CUDA_RET(cudaGetLastError());
@@ -222,22 +248,20 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         ap.scale = (float)(1.0 / sqrt((double)hd));
         ap.err = err_;
         TPTC_CUDA_RET(launch_attn_prefill(ap, st, false));
-        TPTC_CUDA_RET(launch_dequant_rows_f16(L.o, 0, dim, pf_w_, st));
         g.N = dim;
         g.K = nq;
         g.ldc = dim;
         if (tp_) {  // row-parallel o: partial sums of every token, then one allreduce
             g.c = pf_part_;
-            TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_o_, nq, pf_w_, nq, g, st, false));
+            TPTC_CUDA_RET(matmul(GEMM_STORE, pf_o_, L.o, g));
             PF_RET_IF(tp_->allreduce_add(g.c, pf_x_, (size_t)T * dim, st));
         } else {
             g.c = pf_x_;
-            TPTC_CUDA_RET(gemm_tc(GEMM_RESID, pf_o_, nq, pf_w_, nq, g, st, false));
+            TPTC_CUDA_RET(matmul(GEMM_RESID, pf_o_, L.o, g));
         }
         // feed-forward block: gate|up in the device tile order, silu(gate) * up in the epilogue
         rmsnorm_f16_kernel<<<T, 256, 0, st>>>(pf_x_, L.ffn_norm, dim, m.rms_eps, pf_xn_);
         TPTC_CUDA_RET(cudaGetLastError());
-        TPTC_CUDA_RET(launch_dequant_rows_f16(L.glu, 0, 2 * ffn_l, pf_w_, st, true));
         GemmTcParams gg = {};
         gg.M = T;
         gg.N = 2 * ffn_l;
@@ -245,18 +269,17 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         gg.h = pf_h_;
         gg.ldh = ffn_l;
         gg.err = err_;
-        TPTC_CUDA_RET(gemm_tc(GEMM_GLU, pf_xn_, dim, pf_w_, dim, gg, st, false));
-        TPTC_CUDA_RET(launch_dequant_rows_f16(L.down, 0, dim, pf_w_, st));
+        TPTC_CUDA_RET(matmul(GEMM_GLU, pf_xn_, L.glu, gg));
         g.N = dim;
         g.K = ffn_l;
         g.ldc = dim;
         if (tp_) {
             g.c = pf_part_;
-            TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_h_, ffn_l, pf_w_, ffn_l, g, st, false));
+            TPTC_CUDA_RET(matmul(GEMM_STORE, pf_h_, L.down, g));
             PF_RET_IF(tp_->allreduce_add(g.c, pf_x_, (size_t)T * dim, st));
         } else {
             g.c = pf_x_;
-            TPTC_CUDA_RET(gemm_tc(GEMM_RESID, pf_h_, ffn_l, pf_w_, ffn_l, g, st, false));
+            TPTC_CUDA_RET(matmul(GEMM_RESID, pf_h_, L.down, g));
         }
     }
     return {};

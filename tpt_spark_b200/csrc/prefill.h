@@ -30,6 +30,19 @@ cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb,
                     cudaStream_t st, bool pdl);
 cudaError_t gemm_tc_init_device();
 
+// ---- the same GEMM with the weight dequantisation fused in (gemm_q.cu): B is a Q4_K / Q6_K /
+// Q8_0 matrix in the device layout (its physical rows), N <= its padded rows, K = its K.
+struct DevMatrix;
+bool gemm_q_supported(const DevMatrix& w);
+// Whether the fused GEMM is expected to beat "expand w to fp16, then gemm_tc" for an M x N
+// product on `sms` SMs (a wave model of both with B200-measured step times): the fused kernel
+// re-expands a weight tile for every 128-row block of M, the two-pass path expands the whole
+// matrix once, so the fused one wins for short chunks of wide matrices.
+bool gemm_q_preferred(const DevMatrix& w, int M, int N, int sms);
+cudaError_t gemm_q(int epi, const __half* a, int lda, const DevMatrix& w, const GemmTcParams& p, cudaStream_t st,
+                   bool pdl);
+cudaError_t gemm_q_init_device();
+
 // ---- causal attention over a prompt chunk (attn_prefill.cu)
 struct AttnPrefillParams {
     const __half* q;       // [T][n_heads][hd], rotated

@@ -110,6 +110,16 @@ class CudaEngine:
         shorter ones, or all when min_tokens <= 0, go token by token (exact decode numerics)."""
         self._check(lib().tptc_set_prefill_gemm_min(self._ctx, int(min_tokens)))
 
+    FUSED_MODES = {"never": 0, "auto": 1, "always": 2}
+
+    def set_prefill_fused(self, mode: str) -> None:
+        """How the batched prefill contracts quantised weights: "auto" (default: the
+        fused-dequant GEMM where a wave model expects it to be faster), "always" or "never"
+        (expand each matrix to fp16 first)."""
+        if mode not in self.FUSED_MODES:
+            raise ValueError(f"prefill fused mode must be one of {sorted(self.FUSED_MODES)}")
+        self._check(lib().tptc_set_prefill_fused(self._ctx, self.FUSED_MODES[mode]))
+
     # -- lifecycle ---------------------------------------------------------------------------
     def close(self):
         if self._ctx:

@@ -47,6 +47,10 @@ class Matrix:
     def gemv(self, d_x, d_y, stream: Optional[int] = None) -> None:
         check(lib().tptc_gemv(self._h, _ptr(d_x), _ptr(d_y), stream))
 
+    def gemm(self, d_a, d_c, M: int, stream: Optional[int] = None) -> None:
+        """C[M x N] (f32) = A[M x K] (fp16) . W^T with the dequantisation fused (tptc_gemm_q)."""
+        check(lib().tptc_gemm_q(self._h, _ptr(d_a), _ptr(d_c), M, stream))
+
     def dequant_f16(self, d_out, stream: Optional[int] = None) -> None:
         """The matrix as dense row-major fp16 [N x K] (the prefill GEMM operand)."""
         check(lib().tptc_matrix_dequant_f16(self._h, _ptr(d_out), stream))
