@@ -128,8 +128,9 @@ def test_gemm_q_matches_torch(cuda_device, name, t, shape):
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,t", TYPES)
 def test_gemm_q_bitwise_equals_gemm_of_expanded(cuda_device, name, t):
-    """Same tcgen05 sequence as the fp16 GEMM: identical bits given the expanded matrix
-    (1024 x 6144 x 4096: more tiles than SMs, both accumulators cycling)."""
+    """Same tcgen05 sequence as the fp16 GEMM (128 x 256 tiles, K 16 products in the same
+    order): identical bits given the expanded matrix (1024 x 6144 x 4096 for Q4_K: more tiles
+    than SMs, both accumulators cycling)."""
     from tpt_spark_b200 import kernels as K
 
     M, N, Kd = (1024, 6144, 4096) if t == O.Q4_K else (256, 1024, 4096)

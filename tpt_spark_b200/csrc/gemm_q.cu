@@ -15,7 +15,7 @@
 //     Its own ring runs ahead of the A ring, so the block loads do not wait on the tensor core;
 //   - warps 6-13: dequantisation.  Thread t expands row t of the tile: per 64-column step it
 //     reads the row's codes of the step with 16-byte loads, then writes its 64 fp16 values
-//     into the 128-byte-swizzled K-major layout tcgen05.mma reads (2-stage ring), building
+//     into the 128-byte-swizzled K-major layout tcgen05.mma reads (2- or 3-stage ring), building
 //     each value from its code with fp16 bit arithmetic (byte permute onto 1024 + code, exact
 //     subtraction, one multiply or fused multiply-add with the fp16 scale and offset) -- no
 //     fp32 round trip, no conversion unit;
@@ -42,7 +42,6 @@ namespace tptc {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kBStages = 2;
 constexpr int kABytes = BM * BK * 2;  // 16 KB
 constexpr int kBBytes = BN * BK * 2;  // 32 KB
 constexpr int kThreads = 480;
@@ -53,13 +52,16 @@ constexpr int kDeqThreads = 256;  // one per row of the tile
 constexpr int kDeqWarps = kDeqThreads / 32;
 
 __host__ __device__ constexpr int q_sbm(int type) { return type == TPTC_TYPE_Q4_K ? 144 : type == TPTC_TYPE_Q6_K ? 208 : 256; }
-// Ring depths within 227 KB: Q4_K's 36 KB quantised stages fit three, Q6_K's 52 KB and
-// Q8_0's 64 KB two (Q8_0 then two A stages)
+// Ring depths within 227 KB.  Two quantised stages (8 steps of look-ahead for the W
+// producer); the expanded-B ring decouples the expansion from the tensor core, three stages
+// where they fit (Q4_K's 36 KB quantised stages), else two (Q6_K 52 KB, Q8_0 64 KB, which
+// also leaves Q8_0 two A stages).
 __host__ __device__ constexpr int q_astages(int type) { return type == TPTC_TYPE_Q8_0 ? 2 : 3; }
-__host__ __device__ constexpr int q_qstages(int type) { return type == TPTC_TYPE_Q4_K ? 3 : 2; }
+__host__ __device__ constexpr int q_qstages(int) { return 2; }
+__host__ __device__ constexpr int q_bstages(int type) { return type == TPTC_TYPE_Q4_K ? 3 : 2; }
 __host__ __device__ constexpr size_t q_smem(int type) {
-    return (size_t)q_astages(type) * kABytes + (size_t)q_qstages(type) * BN * q_sbm(type) + (size_t)kBStages * kBBytes +
-           1024;
+    return (size_t)q_astages(type) * kABytes + (size_t)q_qstages(type) * BN * q_sbm(type) +
+           (size_t)q_bstages(type) * kBBytes + 1024;
 }
 static_assert(q_smem(TPTC_TYPE_Q8_0) <= 227 * 1024 - 256 && q_smem(TPTC_TYPE_Q6_K) <= 227 * 1024 - 256 &&
                   q_smem(TPTC_TYPE_Q4_K) <= 227 * 1024 - 256,
@@ -217,13 +219,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kQBytes = BN * SBM;
     constexpr int kAStages = q_astages(QT);
     constexpr int kQStages = q_qstages(QT);
+    constexpr int kBStages = q_bstages(QT);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = sA + kAStages * kABytes;
     uint8_t* sQ = sB + kBStages * kBBytes;
     __shared__ uint64_t a_full[3], a_empty[3], q_full[3], q_empty[3];
-    __shared__ uint64_t b_full[kBStages], b_empty[kBStages], tfull[2], tempty[2], drain;
+    __shared__ uint64_t b_full[3], b_empty[3], tfull[2], tempty[2], drain;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_flag;
     const GemmTcParams& p = q.g;
@@ -487,7 +490,7 @@ bool gemm_q_preferred(const DevMatrix& w, int M, int N, int sms) {
     if (!gemm_q_supported(w) || M <= 0 || N <= 0 || sms <= 0) return false;
     // Both paths walk 128 x 256 tiles, one CTA per SM; per 64-column step a CTA of this kernel
     // takes about 0.9 us (the expansion in shared memory bounds it), one of gemm_tc about
-    // 0.5 us, and the separate expansion of the matrix to fp16 about 0.73 ns per 1000
+    // 0.5 us, and the separate expansion of the matrix to fp16 about 0.7 ns per 1000
     // elements -- B200 measurements over Q4_K / Q6_K / Q8_0 and M = 128 .. 8192.
     const double nk = w.K / 64.0;
     const long tiles = (long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
