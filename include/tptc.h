@@ -228,6 +228,17 @@ TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_
 /* Prefill GEMM on the tensor cores: C[M x N] (f32, row-major) = A[M x K] . B[N x K]^T with A
  * and B row-major fp16 (16-byte aligned), K a multiple of 64 -- the prompt-wide replacement of
  * gemm.wgsl's per-token M = 1 products. */
+/* The engine's next-token selection on the device (infer's sampling step), as a kernel:
+ * logits[vocab] with the repeat penalty applied once per context occurrence (counts[vocab],
+ * candle_engine.rs:87-101; the picked token's count is incremented), then argmax when
+ * temperature <= 0 (ties to the highest index), else softmax(x / temperature), the top-p
+ * nucleus in (0, 1) (candle sample_topp's kept set, computed exactly in fixed point) and one
+ * SplitMix64 draw of (seed, *step) (*step incremented).  scratch: [vocab] floats.  dbg
+ * (nullable): [3] u64 = kept-set cut (fp32 bit pattern of the smallest kept exp(x - max)),
+ * kept mass, total mass, both in units of 2^-40.  counts and step may be null. */
+TPTC_API int tptc_sample(const float* d_logits, int vocab, int* d_counts, float penalty, float temperature,
+                         float top_p, uint64_t seed, int* d_step, float* d_scratch, uint32_t* d_out_tok,
+                         uint64_t* d_dbg, void* stream);
 TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream);
 /* The prefill GEMM with the weight dequantisation fused in: C[M x N] (f32) = A[M x K] . W^T
  * with A row-major fp16 (16-byte aligned) and W a Q4_K / Q6_K / Q8_0 matrix (tptc_matrix,

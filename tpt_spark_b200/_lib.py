@@ -74,6 +74,7 @@ SIGNATURES = {
     "tptc_gemv": (c_int, [c_vp, c_vp, c_vp, c_vp]),
     "tptc_matrix_dequant_f16": (c_int, [c_vp, c_vp, c_vp]),
     "tptc_block_dots": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "tptc_sample": (c_int, [c_vp, c_int, c_vp, c_f, c_f, c_f, c_u64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "tptc_gemm_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
     "tptc_gemm_q": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp]),
     "tptc_attn_prefill": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp]),

@@ -457,6 +457,26 @@ TPTC_API int tptc_attn_decode_noalloc(const float* d_q, const float* d_kraw, voi
                        head_dim, max_seq, ws, L, st);
 }
 
+TPTC_API int tptc_sample(const float* d_logits, int vocab, int* d_counts, float penalty, float temperature,
+                         float top_p, uint64_t seed, int* d_step, float* d_scratch, uint32_t* d_out_tok,
+                         uint64_t* d_dbg, void* stream) {
+    if (!d_logits || vocab <= 0 || !d_scratch || !d_out_tok) return fail_code(nullptr, TPTC_ERR_ARG, "sample: bad argument");
+    tptc::SampleParams s = {};
+    s.logits = d_logits;
+    s.vocab = vocab;
+    s.counts = d_counts;
+    s.penalty = penalty;
+    s.temperature = temperature;
+    s.top_p = top_p;
+    s.seed = seed;
+    s.step = d_step;
+    s.scratch = d_scratch;
+    s.out_tok = d_out_tok;
+    s.dbg = reinterpret_cast<unsigned long long*>(d_dbg);
+    cudaError_t e = tptc::launch_sample(s, static_cast<cudaStream_t>(stream), false);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "sample");
+}
+
 TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream) {
     if (!d_a || !d_b || !d_c || M <= 0 || N <= 0 || K <= 0) return fail_code(nullptr, TPTC_ERR_ARG, "gemm: bad argument");
     if (K % 64 || (reinterpret_cast<uintptr_t>(d_a) & 15) || (reinterpret_cast<uintptr_t>(d_b) & 15))

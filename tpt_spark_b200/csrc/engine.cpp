@@ -6,7 +6,6 @@
 
 #include <algorithm>
 #include <chrono>
-#include <random>
 
 #include "kernels.h"
 #include "prefill.h"
@@ -389,6 +388,7 @@ Status Engine::alloc_runtime() {
     const size_t o_act = take(gemv_act_bytes_max(k_max));
     const size_t o_cbar = take((size_t)(L + 1) * kChainMaxPhases * 4);
     const size_t o_bval = take((size_t)2 * sm_count_ * 4), o_bidx = take((size_t)2 * sm_count_ * 4);
+    const size_t o_scnt = take((size_t)m.vocab * 4), o_sscr = take((size_t)m.vocab * 4), o_sstep = take(64);
     rt_size_ = off;
     cudaError_t ce = cudaMalloc(&rt_, rt_size_);
     if (ce != cudaSuccess) {
@@ -421,6 +421,9 @@ Status Engine::alloc_runtime() {
     chain_bar_ = reinterpret_cast<int*>(rt_ + o_cbar);
     best_val_ = reinterpret_cast<float*>(rt_ + o_bval);
     best_idx_ = reinterpret_cast<int*>(rt_ + o_bidx);
+    sample_counts_ = reinterpret_cast<int*>(rt_ + o_scnt);
+    sample_scratch_ = reinterpret_cast<float*>(rt_ + o_sscr);
+    sample_step_ = reinterpret_cast<int*>(rt_ + o_sstep);
 
     // candle quantized_llama precomput_freqs_cis: theta_i = 1/base^(2i/hd) (f32 powf),
     // angle = pos * theta_i, cos/sin in f32 -- built on the host with the C library's powf,
@@ -748,6 +751,39 @@ Status Engine::decode(uint32_t id, int pos, float* logits, uint32_t* argmax) {
     return {};
 }
 
+Status Engine::sample_reset(const uint32_t* context, int n) {
+    std::vector<int> counts(meta_.vocab, 0);
+    for (int i = 0; i < n; i++)
+        if (context[i] < (uint32_t)meta_.vocab) counts[context[i]]++;
+    CU(cudaMemcpyAsync(sample_counts_, counts.data(), (size_t)meta_.vocab * 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaMemsetAsync(sample_step_, 0, 4, stream_));
+    return sync();
+}
+
+Status Engine::sample_logits(const tptc_infer_params& p, uint32_t* out) {
+    SampleParams s = {};
+    s.logits = logits_;
+    s.vocab = meta_.vocab;
+    s.counts = sample_counts_;
+    s.penalty = p.repeat_penalty;
+    s.temperature = p.temperature;
+    s.top_p = p.top_p;
+    s.seed = p.seed;
+    s.step = sample_step_;
+    s.scratch = sample_scratch_;
+    s.out_tok = tok_out_;
+    CU(launch_sample(s, stream_, false));
+    CU(cudaMemcpyAsync(h_tok_ + 1, tok_out_, 4, cudaMemcpyDeviceToHost, stream_));
+    RET_IF(sync());
+    *out = h_tok_[1];
+    return {};
+}
+
+Status Engine::decode_sample(uint32_t id, int pos, const tptc_infer_params& p, uint32_t* out) {
+    RET_IF(decode(id, pos, nullptr, nullptr));
+    return sample_logits(p, out);
+}
+
 Status Engine::debug_trace(uint32_t id, int pos, float* trace) {
     if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
     if (id >= (uint32_t)meta_.vocab || pos != (int)cached_tokens_.size() || pos >= max_seq_)
@@ -810,64 +846,6 @@ Status Engine::prefill(const uint32_t* ids, int n, int start_pos, float* last_lo
 
 // ---- LlmEngine::infer over token ids (wgpu_engine.rs:165-334, candle_engine.rs:205-334)
 
-namespace {
-
-// candle LogitsProcessor with a temperature: softmax(logits / T), optional top-p nucleus,
-// then one draw.  The draw uses std::mt19937_64 seeded from params.seed; candle draws from
-// rand's StdRng, so sampled (non-greedy) streams are not bit-identical to the reference.
-uint32_t sample_host(std::vector<float>& lg, float temperature, float top_p, std::mt19937_64& rng) {
-    const int n = (int)lg.size();
-    if (temperature <= 0.f) {
-        int best = 0;
-        for (int i = 1; i < n; i++)
-            if (!(lg[i] < lg[best])) best = i;
-        return (uint32_t)best;
-    }
-    float mx = -INFINITY;
-    for (float v : lg) mx = std::max(mx, v / temperature);
-    std::vector<float> pr(n);
-    double sum = 0;
-    for (int i = 0; i < n; i++) {
-        pr[i] = expf(lg[i] / temperature - mx);
-        sum += pr[i];
-    }
-    for (auto& v : pr) v = (float)(v / sum);
-    if (top_p > 0.f && top_p < 1.f) {
-        std::vector<int> idx(n);
-        for (int i = 0; i < n; i++) idx[i] = i;
-        std::sort(idx.begin(), idx.end(), [&](int a, int b) { return pr[a] > pr[b]; });
-        float cum = 0.f;
-        for (int i : idx) {
-            if (cum >= top_p) pr[i] = 0.f;
-            cum += pr[i];
-        }
-    }
-    double tot = 0;
-    for (float v : pr) tot += v;
-    std::uniform_real_distribution<double> u(0.0, tot);
-    double r = u(rng), acc = 0;
-    for (int i = 0; i < n; i++) {
-        acc += pr[i];
-        if (r < acc && pr[i] > 0.f) return (uint32_t)i;
-    }
-    for (int i = n - 1; i >= 0; i--)
-        if (pr[i] > 0.f) return (uint32_t)i;
-    return 0;
-}
-
-// candle_engine.rs:87-101 -- every entry of `seen` (duplicates included).
-void repeat_penalty(std::vector<float>& lg, const std::vector<uint32_t>& seen, float penalty) {
-    if (fabsf(penalty - 1.f) < 1.1920929e-7f) return;
-    for (uint32_t id : seen) {
-        if (id < lg.size()) {
-            if (lg[id] >= 0.f) lg[id] /= penalty;
-            else lg[id] *= penalty;
-        }
-    }
-}
-
-}  // namespace
-
 Status Engine::infer(const uint32_t* prompt, int n, const tptc_infer_params& p, tptc_token_cb cb, void* user) {
     using clk = std::chrono::steady_clock;
     if (!loaded_) return err(TPTC_ERR_STATE, "no model loaded");
@@ -889,18 +867,19 @@ Status Engine::infer(const uint32_t* prompt, int n, const tptc_infer_params& p, 
     if (prefix >= (int)tokens.size()) prefix = (int)tokens.size() - 1;
     cached_tokens_.resize(prefix);
 
+    // next-token selection on the device (sample.cu): the context counts feed the repeat
+    // penalty; greedy without a penalty keeps the argmax inside the decode graph
     const bool greedy = p.temperature <= 0.f;
     const bool penalty = fabsf(p.repeat_penalty - 1.f) >= 1.1920929e-7f;
-    std::mt19937_64 rng(p.seed);
-    std::vector<float> lg(meta_.vocab);
 
     auto t0 = clk::now();
-    RET_IF(prefill(tokens.data() + prefix, (int)tokens.size() - prefix, prefix, lg.data()));
+    RET_IF(prefill(tokens.data() + prefix, (int)tokens.size() - prefix, prefix, nullptr));
+    RET_IF(sample_reset(tokens.data(), (int)tokens.size()));
+    uint32_t next = 0;
+    RET_IF(sample_logits(p, &next));
     auto t1 = clk::now();
     last_prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
     last_n_prompt = (int)tokens.size() - prefix;
-    repeat_penalty(lg, tokens, p.repeat_penalty);
-    uint32_t next = sample_host(lg, p.temperature, p.top_p, rng);
 
     int pos = (int)tokens.size();
     uint32_t generated = 0;
@@ -922,9 +901,8 @@ Status Engine::infer(const uint32_t* prompt, int n, const tptc_infer_params& p, 
             RET_IF(decode(next, pos, nullptr, &am));
             next = am;
         } else {
-            RET_IF(decode(next, pos, lg.data(), nullptr));
-            repeat_penalty(lg, tokens, p.repeat_penalty);
-            next = sample_host(lg, p.temperature, p.top_p, rng);
+            // the sampled token was counted by the kernel; `next` enters the context here
+            RET_IF(decode_sample(next, pos, p, &next));
         }
         pos++;
     }

@@ -70,6 +70,12 @@ class Engine {
     Status prefill(const uint32_t* ids, int n, int start_pos, float* last_logits);
     Status decode(uint32_t id, int pos, float* logits, uint32_t* argmax);
     Status decode_greedy(uint32_t id, int pos, int n, uint32_t* out_ids);
+    // Device next-token selection (sample.cu) over the last logits: sample_reset loads the
+    // context's token counts (repeat penalty) and zeroes the draw counter; sample_logits picks
+    // from logits_ (the kernel counts the pick); decode_sample = decode + sample_logits.
+    Status sample_reset(const uint32_t* context, int n);
+    Status sample_logits(const tptc_infer_params& p, uint32_t* out);
+    Status decode_sample(uint32_t id, int pos, const tptc_infer_params& p, uint32_t* out);
     Status infer(const uint32_t* prompt, int n, const tptc_infer_params& p, tptc_token_cb cb, void* user);
 
     double last_prefill_ms = 0, last_decode_ms = 0, last_device_ms = 0;
@@ -139,6 +145,9 @@ class Engine {
     int* step_ = nullptr;  // decode steps so far (tensor-parallel reduction epochs)
     uint8_t* act_ = nullptr;  // prepared GEMV activation (gemv_launch)
     int* chain_bar_ = nullptr;     // [L + 1][kChainMaxPhases] chain arrival counters
+    int* sample_counts_ = nullptr;     // [vocab] context token counts (repeat penalty)
+    float* sample_scratch_ = nullptr;  // [vocab]
+    int* sample_step_ = nullptr;       // draws so far in this inference
     float* best_val_ = nullptr;    // [2 * SMs] per-CTA argmax partials of the lm_head chain
     int* best_idx_ = nullptr;
     float* attn_partial_ = nullptr;

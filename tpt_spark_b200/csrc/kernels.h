@@ -80,6 +80,27 @@ cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, floa
 cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_t* next_tok, int* pos,
                           uint32_t* history, cudaStream_t st, bool pdl);
 
+// sample.cu: the next token from logits[vocab] on the device (one CTA): repeat penalty over
+// the context counts, then argmax (temperature <= 0) or softmax(x / T), top-p and one seeded draw.
+struct SampleParams {
+    const float* logits;
+    int vocab;
+    int* counts;        // [vocab] occurrences of each token in the context (penalty); the
+                        // sampled token's count is incremented; may be null (no penalty)
+    float penalty;      // 1 = off
+    float temperature;  // <= 0: argmax, ties to the highest index
+    float top_p;        // in (0, 1): nucleus; otherwise every token
+    unsigned long long seed;
+    int* step;          // draw counter (read, then incremented); null = draw 0
+    float* scratch;     // [vocab]
+    uint32_t* out_tok;
+    uint32_t* next_tok;  // optional chaining, as argmax: next decode input, ++pos, history[pos]
+    int* pos;
+    uint32_t* history;
+    unsigned long long* dbg;  // optional [3]: cut pattern, kept mass, total mass (2^-40 units)
+};
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t st, bool pdl);
+
 cudaError_t kernels_init_device();
 
 }  // namespace tptc

@@ -92,6 +92,15 @@ def attn_decode_noalloc(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_co
                                          max_seq, _ptr(d_out), stream))
 
 
+def sample(d_logits, vocab: int, d_counts, penalty: float, temperature: float, top_p: float, seed: int, d_step,
+           d_scratch, d_out, d_dbg=None, stream: Optional[int] = None) -> None:
+    """The engine's device next-token selection (tptc_sample): repeat penalty over d_counts,
+    argmax or softmax(x / T) + top-p + one seeded draw; the token lands in d_out[0]."""
+    check(lib().tptc_sample(_ptr(d_logits), vocab, _ptr(d_counts) if d_counts is not None else None, penalty,
+                            temperature, top_p, seed, _ptr(d_step) if d_step is not None else None, _ptr(d_scratch),
+                            _ptr(d_out), _ptr(d_dbg) if d_dbg is not None else None, stream))
+
+
 def gemm_f16(d_a, d_b, d_c, M: int, N: int, K: int, stream: Optional[int] = None) -> None:
     """C[M x N] (f32) = A[M x K] . B[N x K]^T on the tensor cores (fp16 row-major A and B)."""
     check(lib().tptc_gemm_f16(_ptr(d_a), _ptr(d_b), _ptr(d_c), M, N, K, stream))
