@@ -760,7 +760,7 @@ Status Engine::sample_reset(const uint32_t* context, int n) {
     return sync();
 }
 
-Status Engine::sample_logits(const tptc_infer_params& p, uint32_t* out) {
+Status Engine::enqueue_sample(const tptc_infer_params& p) {
     SampleParams s = {};
     s.logits = logits_;
     s.vocab = meta_.vocab;
@@ -774,14 +774,31 @@ Status Engine::sample_logits(const tptc_infer_params& p, uint32_t* out) {
     s.out_tok = tok_out_;
     CU(launch_sample(s, stream_, false));
     CU(cudaMemcpyAsync(h_tok_ + 1, tok_out_, 4, cudaMemcpyDeviceToHost, stream_));
+    return {};
+}
+
+Status Engine::sample_logits(const tptc_infer_params& p, uint32_t* out) {
+    RET_IF(enqueue_sample(p));
     RET_IF(sync());
     *out = h_tok_[1];
     return {};
 }
 
 Status Engine::decode_sample(uint32_t id, int pos, const tptc_infer_params& p, uint32_t* out) {
-    RET_IF(decode(id, pos, nullptr, nullptr));
-    return sample_logits(p, out);
+    // decode()'s step followed by the selection kernel, one host synchronisation per token
+    if (id >= (uint32_t)meta_.vocab) return err(TPTC_ERR_ARG, "token id out of range");
+    if (pos < 0 || pos >= max_seq_ || pos != (int)cached_tokens_.size())
+        return err(TPTC_ERR_ARG, "decode position must equal the KV length and lie in the context window");
+    h_tok_[0] = id;
+    h_pos_[0] = pos;
+    CU(cudaMemcpyAsync(tok_in_, h_tok_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaMemcpyAsync(pos_, h_pos_, 4, cudaMemcpyHostToDevice, stream_));
+    CU(cudaGraphLaunch(graph_plain_, stream_));
+    RET_IF(enqueue_sample(p));
+    RET_IF(sync());
+    cached_tokens_.push_back(id);
+    *out = h_tok_[1];
+    return {};
 }
 
 Status Engine::debug_trace(uint32_t id, int pos, float* trace) {

@@ -75,6 +75,7 @@ class Engine {
     // from logits_ (the kernel counts the pick); decode_sample = decode + sample_logits.
     Status sample_reset(const uint32_t* context, int n);
     Status sample_logits(const tptc_infer_params& p, uint32_t* out);
+    Status enqueue_sample(const tptc_infer_params& p);  // kernel + token copy, no sync
     Status decode_sample(uint32_t id, int pos, const tptc_infer_params& p, uint32_t* out);
     Status infer(const uint32_t* prompt, int n, const tptc_infer_params& p, tptc_token_cb cb, void* user);
 
