@@ -81,3 +81,23 @@ def test_new_tokens_shorter_than_cached():
 def test_prefix_rejects_bad_args():
     L = _lib.lib()
     assert L.tptc_common_prefix_len(None, 3, None, 0) == -1
+
+
+def test_kernel_entries_reject_bad_arguments_before_any_device_work():
+    """Argument checks of the sampling, fused-GEMM and setting entries run on the host: a bad
+    call fails with TPTC_ERR_ARG (-1) even without a GPU."""
+    L = _lib.lib()
+    assert L.tptc_sample(None, 10, None, 1.0, 0.7, 0.9, 1, None, None, None, None, None) == -1
+    assert L.tptc_sample(None, 0, None, 1.0, 0.7, 0.9, 1, None, None, None, None, None) == -1
+    assert b"sample" in L.tptc_last_error(None)
+    assert L.tptc_gemm_q(None, None, None, 4, None) == -1
+    assert b"gemm_q" in L.tptc_last_error(None)
+    assert L.tptc_set_prefill_fused(None, 1) == -1
+    assert L.tptc_set_prefill_gemm_min(None, 16) == -1
+
+
+def test_profile_cases_usage_without_arguments(capsys):
+    from tpt_spark_b200 import profile_cases
+
+    assert profile_cases.main([]) == 2
+    assert "gemm_q" in capsys.readouterr().out
