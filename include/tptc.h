@@ -279,13 +279,16 @@ TPTC_API int tptc_attn_decode(const float* d_q, const float* d_kraw, void* d_kca
                               int64_t workspace_bytes, void* stream);
 
 /* No counterpart in the reference: tptc_attn_decode for callers that cannot allocate device
- * memory.  Same arguments and results, minus the workspace: the scratch is a static device
+ * memory -- a host whose device memory is all reserved up front by its own pool or another
+ * framework's caching allocator, or a decode loop that must not call cudaMalloc / cudaFree
+ * because they can synchronise the device.  Same arguments and results, minus the workspace: the scratch is a static device
  * array of 1 MiB per device (split counters, error word and split partials; the partials
  * take splits * n_heads * (head_dim + 2) * 4 bytes).  Sizes whose scratch exceeds 1 MiB are
  * rejected with TPTC_ERR_ARG and a message giving both sizes.  The call makes no cudaMalloc,
- * cudaFree or other allocating call.  Its first call on a device looks the array up and
- * zeroes it on `stream`, waiting for that; every launch that does not time out leaves the
- * counters zero again.  The array is shared by all calls on a device: calls that may overlap on the GPU (different
+ * cudaFree or other allocating call.  Its first call on a device does a one-time set-up with
+ * that device current: it looks the array's device address up (cudaGetSymbolAddress) and
+ * zeroes the array on `stream`, waiting for that; make this first call before any stream
+ * capture.  Every launch that does not time out leaves the counters zero again.  The array is shared by all calls on a device: calls that may overlap on the GPU (different
  * streams without ordering, several host threads) race on it and give wrong results, so
  * callers serialise them.  A position outside the cache or a timed-out wait leaves d_out
  * unwritten and is not reported by this call (the error word is internal). */

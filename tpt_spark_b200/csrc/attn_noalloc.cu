@@ -1,5 +1,8 @@
 // attn_noalloc.cu -- scratch for tptc_attn_decode_noalloc, the decode-attention entry point
-// for callers that cannot allocate device memory.  It has no counterpart in the reference.
+// for callers that cannot allocate device memory (a host whose device memory is reserved up
+// front by its own pool or another framework's allocator, or a decode loop that must not call
+// cudaMalloc / cudaFree because they can synchronise the device).  It has no counterpart in
+// the reference.
 //
 // The attention kernel needs scratch for its split partials and per-kv-head split counters
 // (attn_scratch_layout: error word, counters, partials).  Here that scratch is one static
@@ -7,9 +10,10 @@
 // allocating library routine is called on this path.
 //
 // What must start at zero: the split counters (the last CTA of each kv head resets its own
-// counter, so a completed launch leaves them zero again) and the error word.  Set-up zeroes
-// the whole array once per device, ordered on the caller's stream and waited for, before the
-// first launch there.
+// counter, so a completed launch leaves them zero again) and the error word.  Set-up, done by
+// the first call on a device with that device current, looks the array's address up and
+// zeroes the whole array, ordered on the caller's stream and waited for, before the first
+// launch there; that first call belongs before any stream capture.
 //
 // The array is shared by every call on a device.  Calls that may overlap on the GPU (launched
 // on different streams without ordering between them, or from several host threads) race on
