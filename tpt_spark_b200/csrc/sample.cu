@@ -40,6 +40,9 @@ namespace {
 constexpr int kST = 1024;  // threads of the sampling CTA
 constexpr int kWarps = kST / 32;
 constexpr float kFix = 1099511627776.f;  // 2^40: fixed-point scale of the masses (e <= 1)
+// One CTA walks the vocabulary several times, so each pass is bound by load latency: every
+// strided pass keeps kU independent loads in flight per thread.
+constexpr int kU = 8;
 
 __device__ __forceinline__ unsigned long long mass(float e) { return __float2ull_rz(e * kFix); }
 
@@ -137,21 +140,31 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
     // 1-3: penalty, then argmax or x / T and its maximum
     float mx = -INFINITY;
     int mi = -1;
-    for (int i = t; i < V; i += kST) {
-        float x = p.logits[i];
-        if (pen) {
-            const int k = p.counts[i];
-            for (int j = 0; j < k; j++) x = x >= 0.f ? __fdiv_rn(x, p.penalty) : __fmul_rn(x, p.penalty);
+    for (int base = 0; base < V; base += kST * kU) {
+        float xv[kU];
+        int kv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int i = base + u * kST + t;
+            xv[u] = i < V ? p.logits[i] : 0.f;
+            kv[u] = (pen && i < V) ? p.counts[i] : 0;
         }
-        if (greedy) {
-            if (mi < 0 || x > mx || (x == mx && i > mi)) {
-                mx = x;
-                mi = i;
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int i = base + u * kST + t;
+            if (i >= V) break;
+            float x = xv[u];
+            for (int j = 0; j < kv[u]; j++) x = x >= 0.f ? __fdiv_rn(x, p.penalty) : __fmul_rn(x, p.penalty);
+            if (greedy) {
+                if (mi < 0 || x > mx || (x == mx && i > mi)) {
+                    mx = x;
+                    mi = i;
+                }
+            } else {
+                x = __fdiv_rn(x, p.temperature);
+                p.scratch[i] = x;
+                mx = fmaxf(mx, x);
             }
-        } else {
-            x = __fdiv_rn(x, p.temperature);
-            p.scratch[i] = x;
-            mx = fmaxf(mx, x);
         }
     }
     if (greedy) {
@@ -189,12 +202,23 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
         for (int b = t; b < 1024; b += kST) hist[b] = 0;
         __syncthreads();
         unsigned long long s = 0;
-        for (int i = t; i < V; i += kST) {
-            const float e = expf(p.scratch[i] - mx);
-            p.scratch[i] = e;
-            const unsigned long long m = mass(e);
-            s += m;
-            if (m) atomicAdd(&hist[__float_as_uint(e) >> 20], m);
+        for (int base = 0; base < V; base += kST * kU) {
+            float xv[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++) {
+                const int i = base + u * kST + t;
+                xv[u] = i < V ? p.scratch[i] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < kU; u++) {
+                const int i = base + u * kST + t;
+                if (i >= V) break;
+                const float e = expf(xv[u] - mx);
+                p.scratch[i] = e;
+                const unsigned long long m = mass(e);
+                s += m;
+                if (m) atomicAdd(&hist[__float_as_uint(e) >> 20], m);
+            }
         }
         const unsigned long long total = block_sum_u64(s, redu);
         unsigned int cut = 0;  // keep every e whose bit pattern is >= cut
@@ -211,11 +235,19 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
                     for (int b = t; b < 1024; b += kST) hist[b] = 0;
                     __syncthreads();
                     const int shp = 30 - 10 * level, shb = 20 - 10 * level;
-                    for (int i = t; i < V; i += kST) {
-                        const float e = p.scratch[i];
-                        const unsigned int bits = __float_as_uint(e);
-                        const unsigned long long m = mass(e);
-                        if (m && (bits >> shp) == prefix) atomicAdd(&hist[(bits >> shb) & 1023u], m);
+                    for (int base = 0; base < V; base += kST * kU) {
+                        float ev[kU];
+#pragma unroll
+                        for (int u = 0; u < kU; u++) {
+                            const int i = base + u * kST + t;
+                            ev[u] = i < V ? p.scratch[i] : 0.f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < kU; u++) {
+                            const unsigned int bits = __float_as_uint(ev[u]);
+                            const unsigned long long m = mass(ev[u]);
+                            if (m && (bits >> shp) == prefix) atomicAdd(&hist[(bits >> shb) & 1023u], m);
+                        }
                     }
                 }
                 __syncthreads();
@@ -246,58 +278,61 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
                 cut = prefix << (30 - 10 * lv);
             }
         }
-        // 5: kept mass per warp over warp-contiguous index ranges, then the draw
-        const int R = ((V + kWarps - 1) / kWarps + 31) & ~31;
-        const int w0 = warp * R, w1 = min(V, w0 + R);
-        unsigned long long ws = 0;
-        for (int i = w0 + lane; i < w1; i += 32) {
-            const float e = p.scratch[i];
-            if (__float_as_uint(e) >= cut) ws += mass(e);
+        // 5: kept mass per thread over thread-contiguous index ranges (C indices each), an
+        // exclusive scan of those in index order, then the one thread whose range holds the
+        // draw walks it
+        const int C = (V + kST - 1) / kST, c0 = min(V, t * C), c1 = min(V, c0 + C);
+        unsigned long long ts = 0;
+        for (int j0 = c0; j0 < c1; j0 += kU) {
+            float ev[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++) ev[u] = j0 + u < c1 ? p.scratch[j0 + u] : 0.f;
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (j0 + u < c1 && __float_as_uint(ev[u]) >= cut) ts += mass(ev[u]);
         }
-        for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+        // block exclusive scan of ts (thread order = index order)
+        unsigned long long incl = ts;
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
         __syncthreads();
-        if (lane == 0) redu[warp] = ws;
+        if (lane == 31) redu[warp] = incl;
         __syncthreads();
-        if (t == 0) {
-            unsigned long long kept = 0;
-            for (int w = 0; w < kWarps; w++) kept += redu[w];
-            const unsigned long long step = p.step ? (unsigned long long)*p.step : 0ull;
-            const unsigned long long r = __umul64hi(splitmix64(p.seed, step), kept);
-            unsigned long long run = 0;
-            int wsel = kWarps - 1;
-            for (int w = 0; w < kWarps; w++) {
-                if (r < run + redu[w]) {
-                    wsel = w;
-                    break;
-                }
-                run += redu[w];
+        if (warp == 0) {
+            const unsigned long long wv = redu[lane];
+            unsigned long long wi = wv;
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long n = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += n;
             }
-            sh_i[1] = wsel;
-            sh_u[1] = r - run;
-            sh_u[2] = kept;
-            sh_u[3] = total;
-            sh_i[2] = (int)cut;
+            redu[lane] = wi - wv;  // exclusive prefix of the warps
+            if (lane == 31) {
+                const unsigned long long kept = wi;
+                const unsigned long long step = p.step ? (unsigned long long)*p.step : 0ull;
+                sh_u[1] = __umul64hi(splitmix64(p.seed, step), kept);
+                sh_u[2] = kept;
+                sh_u[3] = total;
+                sh_i[2] = (int)cut;
+                sh_i[3] = -1;
+            }
         }
         __syncthreads();
-        tok = -1;
-        if (warp == sh_i[1]) {
+        {
             const unsigned long long r = sh_u[1];
-            unsigned long long base = 0;
-            int found = -1;
-            for (int g = w0; g < w1 && found < 0; g += 32) {
-                const int i = g + lane;
-                const float e = i < w1 ? p.scratch[i] : 0.f;
-                const unsigned long long m = (i < w1 && __float_as_uint(e) >= cut) ? mass(e) : 0ull;
-                unsigned long long incl = m;
-                for (int o = 1; o < 32; o <<= 1) {
-                    const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += n;
+            unsigned long long run = redu[warp] + incl - ts;  // kept mass before this thread's range
+            if (ts && r >= run && r < run + ts) {
+                for (int j = c0; j < c1; j++) {
+                    const float e = p.scratch[j];
+                    const unsigned long long m = __float_as_uint(e) >= cut ? mass(e) : 0ull;
+                    if (m && run + m > r) {
+                        sh_i[3] = j;
+                        break;
+                    }
+                    run += m;
                 }
-                const unsigned ball = __ballot_sync(0xffffffffu, m && base + incl > r);
-                if (ball) found = g + __ffs(ball) - 1;
-                base += __shfl_sync(0xffffffffu, incl, 31);
             }
-            if (lane == 0) sh_i[3] = found;
         }
         __syncthreads();
         tok = sh_i[3];
