@@ -43,6 +43,16 @@ constexpr float kFix = 1099511627776.f;  // 2^40: fixed-point scale of the masse
 // One CTA walks the vocabulary several times, so each pass is bound by load latency: every
 // strided pass keeps kU independent loads in flight per thread.
 constexpr int kU = 8;
+// The radix histograms are kept in kHC copies, warp w adding into copy w % kHC: most tokens'
+// masses fall into a few buckets, and same-address shared atomics from all warps serialise.
+constexpr int kHC = 4;
+
+__device__ __forceinline__ unsigned long long hsum(const unsigned long long* hist, int b) {
+    unsigned long long v = 0;
+#pragma unroll
+    for (int c = 0; c < kHC; c++) v += hist[c * 1024 + b];
+    return v;
+}
 
 __device__ __forceinline__ unsigned long long mass(float e) { return __float2ull_rz(e * kFix); }
 
@@ -84,8 +94,8 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return red[0];
 }
 
-// Level of the radix select: given the buckets' masses hist[1024] (bucket b = the next 10 bits
-// of the pattern) and the mass `above` of everything larger than this level's prefix, the
+// Level of the radix select: given the buckets' masses hist (kHC copies of 1024; bucket b = the
+// next 10 bits of the pattern) and the mass `above` of everything larger than this level's prefix, the
 // bucket in which the running sum from the top reaches `target`, and the mass above it.
 // Returns 1024 when the whole level stays below the target.  Warp 0 only.
 __device__ __forceinline__ int find_bucket(const unsigned long long* hist, unsigned long long above,
@@ -93,7 +103,7 @@ __device__ __forceinline__ int find_bucket(const unsigned long long* hist, unsig
     const int lane = threadIdx.x & 31;
     // lane l owns buckets 1023 - 32 l .. 992 - 32 l (from the top)
     unsigned long long s = 0;
-    for (int j = 0; j < 32; j++) s += hist[1023 - 32 * lane - j];
+    for (int j = 0; j < 32; j++) s += hsum(hist, 1023 - 32 * lane - j);
     unsigned long long incl = s;  // inclusive prefix from the top over lanes
     for (int o = 1; o < 32; o <<= 1) {
         const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
@@ -109,12 +119,13 @@ __device__ __forceinline__ int find_bucket(const unsigned long long* hist, unsig
         unsigned long long run = above + excl;
         for (int j = 0; j < 32; j++) {
             const int b = 1023 - 32 * lane - j;
-            if (run + hist[b] >= target) {
+            const unsigned long long hb = hsum(hist, b);
+            if (run + hb >= target) {
                 found = b;
                 fa = run;
                 break;
             }
-            run += hist[b];
+            run += hb;
         }
     }
     found = __shfl_sync(0xffffffffu, found, l);
@@ -124,7 +135,7 @@ __device__ __forceinline__ int find_bucket(const unsigned long long* hist, unsig
 }
 
 __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
-    __shared__ unsigned long long hist[1024];
+    __shared__ unsigned long long hist[kHC * 1024];
     __shared__ unsigned long long redu[kWarps];
     __shared__ float redf[kWarps];
     __shared__ int redi[kWarps];
@@ -198,8 +209,11 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
         tok = sh_i[0];
     } else {
         mx = block_max(mx, redf);
-        // 3-4: numerators, their fixed-point total and the first radix level (top 10 bits of e)
-        for (int b = t; b < 1024; b += kST) hist[b] = 0;
+        // 3-4: numerators, their fixed-point total and, for a nucleus, the first radix level
+        // (top 10 bits of e)
+        const bool nucleus = p.top_p > 0.f && p.top_p < 1.f;
+        unsigned long long* hw = hist + (warp % kHC) * 1024;
+        for (int b = t; b < kHC * 1024; b += kST) hist[b] = 0;
         __syncthreads();
         unsigned long long s = 0;
         for (int base = 0; base < V; base += kST * kU) {
@@ -217,12 +231,12 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
                 p.scratch[i] = e;
                 const unsigned long long m = mass(e);
                 s += m;
-                if (m) atomicAdd(&hist[__float_as_uint(e) >> 20], m);
+                if (m && nucleus) atomicAdd(&hw[__float_as_uint(e) >> 20], m);
             }
         }
         const unsigned long long total = block_sum_u64(s, redu);
         unsigned int cut = 0;  // keep every e whose bit pattern is >= cut
-        if (p.top_p > 0.f && p.top_p < 1.f) {
+        if (nucleus) {
             // keep iff the strictly larger mass G < top_p * total; for integer G that is
             // G < ceil(top_p * total) (>= 1, so the largest token is always kept)
             const unsigned long long target = (unsigned long long)ceil((double)p.top_p * (double)total);
@@ -232,7 +246,7 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
             for (int level = 0; level < 3; level++) {
                 if (level > 0) {
                     __syncthreads();
-                    for (int b = t; b < 1024; b += kST) hist[b] = 0;
+                    for (int b = t; b < kHC * 1024; b += kST) hist[b] = 0;
                     __syncthreads();
                     const int shp = 30 - 10 * level, shb = 20 - 10 * level;
                     for (int base = 0; base < V; base += kST * kU) {
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
                         for (int u = 0; u < kU; u++) {
                             const unsigned int bits = __float_as_uint(ev[u]);
                             const unsigned long long m = mass(ev[u]);
-                            if (m && (bits >> shp) == prefix) atomicAdd(&hist[(bits >> shb) & 1023u], m);
+                            if (m && (bits >> shp) == prefix) atomicAdd(&hw[(bits >> shb) & 1023u], m);
                         }
                     }
                 }
