@@ -68,7 +68,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="c5_llama8b_q4km")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default: the config's)")
-    ap.add_argument("--model-dir", default=os.environ.get("TPTC_MODEL_DIR", os.path.join(tempfile.gettempdir(), "tptc_models")))
+    ap.add_argument("--model-dir", default=None, help="generated models (default: $TPTC_MODEL_DIR or <tmp>/tptc_models)")
     ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
@@ -118,14 +118,10 @@ class Dist:
 def model_file(cfg, model_dir, seed, dist):
     from tpt_spark_b200 import synth
 
-    os.makedirs(model_dir, exist_ok=True)
-    path = os.path.join(model_dir, f"{cfg.name}_s{seed}.gguf")
-    if dist.local == 0 and not os.path.exists(path):
-        tmp = path + f".tmp{os.getpid()}"
-        synth.write_gguf(tmp, cfg, seed=seed)
-        os.replace(tmp, path)
+    if dist.local == 0:
+        synth.model_file(cfg, model_dir, seed)
     dist.barrier()
-    return path
+    return os.path.join(model_dir, f"{cfg.name}_s{seed}.gguf")
 
 
 class Clocks:
@@ -453,6 +449,10 @@ def run_ours(args, dist):
 
 def main():
     args = parse()
+    if args.model_dir is None:
+        from tpt_spark_b200 import synth
+
+        args.model_dir = synth.default_model_dir()
     if args.impl == "reference":
         rank, world, _ = dist_env()
         if rank == 0:

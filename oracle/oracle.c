@@ -646,10 +646,25 @@ void or_model_destroy(void* p) {
     free(m);
 }
 
+/* Summation order of RMSNorm's sum of squares: 1 (default) is candle's sequential
+ * Iterator::sum; n > 1 sums elements i (mod n) in n partial sums and then adds the partials
+ * in order -- the order a build of the same source with n-wide SIMD reductions would take.
+ * Both are valid f32 evaluations of the same formula; tests use the second to measure how
+ * far a reordering of one reduction moves a model's logits (the floor any reimplementation
+ * that sums in another order can reach). */
+static int g_norm_lanes = 1;
+void or_set_norm_lanes(int n) { g_norm_lanes = n > 1 ? (n > 64 ? 64 : n) : 1; }
+
 /* candle_nn::ops::rms_norm (f32): m = sqrt(sum(x^2)/dim + eps); y = x / m * w. */
 static void rms_norm(const float* x, const float* w, int dim, float eps, float* y) {
     float s = 0.f;
-    for (int i = 0; i < dim; i++) s += x[i] * x[i];
+    if (g_norm_lanes <= 1) {
+        for (int i = 0; i < dim; i++) s += x[i] * x[i];
+    } else {
+        float part[64] = {0.f};
+        for (int i = 0; i < dim; i++) part[i % g_norm_lanes] += x[i] * x[i];
+        for (int l = 0; l < g_norm_lanes; l++) s += part[l];
+    }
     float m = sqrtf(s / (float)dim + eps);
     for (int i = 0; i < dim; i++) y[i] = x[i] / m * w[i];
 }

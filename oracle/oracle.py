@@ -74,6 +74,8 @@ def lib():
         L.or_set_trace.argtypes = [vp]
         L.or_set_threads.restype = None
         L.or_set_threads.argtypes = [i32]
+        L.or_set_norm_lanes.restype = None
+        L.or_set_norm_lanes.argtypes = [i32]
         L.or_set_simd.restype = None
         L.or_set_simd.argtypes = [i32]
         L.or_rope_table.restype = None
@@ -94,6 +96,12 @@ def set_simd(on: bool) -> None:
 
 def _p(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def set_norm_lanes(n: int) -> None:
+    """RMSNorm sum-of-squares order: 1 = candle's sequential sum (default); n > 1 = n
+    interleaved partial sums added in order (an equally valid f32 evaluation)."""
+    lib().or_set_norm_lanes(int(n))
 
 
 def dequant(t: int, raw: np.ndarray, n: int) -> np.ndarray:

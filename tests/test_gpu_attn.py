@@ -50,14 +50,14 @@ def reference(q, kraw, kc, vc, cs, sn, pos, n_heads, n_kv, hd, kv_dtype):
     return out.flatten(), krot
 
 
-def make_case(n_heads, n_kv, hd, max_seq, pos, kv_type, seed, dev):
+def make_case(n_heads, n_kv, hd, max_seq, pos, kv_type, seed, dev, base=10000.0):
     g = torch.Generator(device="cpu").manual_seed(seed)
     kv_dtype = torch.float32 if kv_type == K.F32 else torch.float16
     q = torch.randn(n_heads * hd, generator=g).to(dev)
     kraw = torch.randn(n_kv * hd, generator=g).to(dev)
     kc = torch.randn(n_kv, max_seq, hd, generator=g).to(kv_dtype).to(dev)
     vc = torch.randn(n_kv, max_seq, hd, generator=g).to(kv_dtype).to(dev)
-    cs, sn = rope_tables(max_seq, hd)
+    cs, sn = rope_tables(max_seq, hd, base)
     return q, kraw, kc, vc, cs.to(dev), sn.to(dev), kv_dtype
 
 
@@ -100,6 +100,28 @@ def test_attn_decode_matches_torch(cuda_device, shape, kv_type):
     # the workspace is ready for the next call: error word and split counters zero
     assert int(ws[:4].view(torch.int32)[0]) == 0
     assert int(ws[256:256 + 4 * n_kv].view(torch.int32).abs().sum()) == 0
+
+
+# The configurations' own attention shapes at their longest decode positions, with their RoPE
+# bases: C2 (32/8 heads of 64, base 500000, 384 positions), C3 (32/8 of 128, base 10000, 2560),
+# C4 (32/32 of 96, MHA, base 10000, 1280), C5 (32/8 of 128, base 500000, 9216).
+CONFIG_SHAPES = [
+    (32, 8, 64, 2048, 383, 500000.0),
+    (32, 8, 128, 4096, 2559, 10000.0),
+    (32, 32, 96, 4096, 1279, 10000.0),
+    (32, 8, 128, 9216, 9215, 500000.0),
+    (32, 8, 128, 9216, 8192, 500000.0),
+]
+
+
+@pytest.mark.parametrize("shape", CONFIG_SHAPES, ids=lambda s: "h%d_kv%d_d%d_s%d_p%d_base%d" % s)
+def test_attn_decode_config_shapes(cuda_device, shape):
+    n_heads, n_kv, hd, max_seq, pos, base = shape
+    q, kraw, kc, vc, cs, sn, kv_dtype = make_case(n_heads, n_kv, hd, max_seq, pos, K.F16, 99 + pos, cuda_device, base)
+    want, krot = reference(q, kraw, kc, vc, cs, sn, pos, n_heads, n_kv, hd, kv_dtype)
+    out, _ = run(q, kraw, kc, vc, K.F16, cs, sn, pos, n_heads, n_kv, hd, max_seq)
+    torch.testing.assert_close(out, want, rtol=RTOL, atol=ATOL)
+    assert torch.equal(kc[:, pos], krot)
 
 
 def test_attn_decode_repeatable(cuda_device):

@@ -159,6 +159,56 @@ def test_gemv_repeatable(cuda_device):
     assert torch.equal(y1, y2)
 
 
+# Every matrix shape of the benchmark configurations (BASELINE configs C2-C5), out x in:
+# q/o, k, v, gate (= up), down and the output projection of each.
+CONFIG_MATRICES = {
+    "c2": [(O.Q4_K, 2048, 2048), (O.Q4_K, 512, 2048), (O.Q6_K, 512, 2048), (O.Q4_K, 8192, 2048),
+           (O.Q6_K, 2048, 8192), (O.Q6_K, 128256, 2048)],
+    "c3": [(O.Q8_0, 4096, 4096), (O.Q8_0, 1024, 4096), (O.Q8_0, 14336, 4096), (O.Q8_0, 4096, 14336),
+           (O.Q8_0, 32000, 4096)],
+    "c4": [(O.F16, 3072, 3072), (O.F16, 8192, 3072), (O.F16, 3072, 8192), (O.F16, 32064, 3072)],
+    "c5": [(O.Q4_K, 4096, 4096), (O.Q4_K, 1024, 4096), (O.Q6_K, 1024, 4096), (O.Q4_K, 14336, 4096),
+           (O.Q6_K, 4096, 14336), (O.Q6_K, 128256, 4096)],
+}
+CONFIG_CASES = [(c, t, n, k) for c, ms in CONFIG_MATRICES.items() for (t, n, k) in ms]
+
+
+@pytest.mark.parametrize("cfg,t,N,K", CONFIG_CASES, ids=lambda v: str(v))
+def test_gemv_config_shapes(cuda_device, cfg, t, N, K):
+    """y within 1e-3 relative of the oracle for every row, and the per-block integer sums
+    bit-exact on up to 2048 rows spread over the matrix (first, last and a stride between)."""
+    import torch
+
+    raw, m = make_matrix(t, N, K, seed=N + K)
+    try:
+        x = activations(K, 31)
+        y = torch.empty(N, dtype=torch.float32, device="cuda")
+        m.gemv(dev(x), y)
+        got = host(y)
+        ref = O.matmul(t, raw, N, K, x)[0]
+        scale = np.abs(ref).max()
+        assert np.abs(got - ref).max() <= REL_TOL * scale
+        big = np.abs(ref) > 0.05 * scale
+        assert (np.abs(got - ref)[big] / np.abs(ref[big])).max() < REL_TOL
+        if t == O.F16:
+            return
+        per_row = K // 32 if t == O.Q8_0 else K // 256
+        isum = torch.zeros(N * per_row, dtype=torch.int32, device="cuda")
+        msum = torch.zeros(N * per_row, dtype=torch.int32, device="cuda")
+        m.block_dots(dev(x), isum, msum)
+        gi, gm = host(isum).reshape(N, per_row), host(msum).reshape(N, per_row)
+    finally:
+        m.close()
+    xq = O.quant_for(t, x)
+    bb = {O.Q4_K: 144, O.Q6_K: 210, O.Q8_0: 34}[t]
+    rows = raw.reshape(N, per_row * bb)
+    for r in sorted(set(range(0, N, max(1, N // 2046))) | {N - 1}):
+        ri, rm = O.block_dots(t, rows[r], xq, per_row)
+        np.testing.assert_array_equal(gi[r], ri, err_msg=f"row {r} isum")
+        if t == O.Q4_K:
+            np.testing.assert_array_equal(gm[r], rm, err_msg=f"row {r} msum")
+
+
 @pytest.mark.parametrize("t,N,K", SHAPES)
 def test_matrix_dequant_f16_bitexact(cuda_device, t, N, K):
     """The prefill GEMM's B operand: the device-layout matrix expanded to dense fp16 equals the

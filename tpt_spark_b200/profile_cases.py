@@ -88,12 +88,10 @@ def attn_prefill(T: int) -> None:
     print("ok", float(o[0, 0]))
 
 
-def prefill(P: int, model_dir: str = "/tmp/tptc_models") -> None:
-    """The C5 model (the bench's synthetic GGUF, written on first use): one warm-up prefill of
-    P random token ids, then the same prefill bracketed by cudaProfilerStart / Stop (for
-    ncu --profile-from-start off)."""
-    import os
-
+def prefill(P: int) -> None:
+    """The C5 model (the bench's synthetic GGUF in synth.default_model_dir(), written on first
+    use): one warm-up prefill of P random token ids, then the same prefill bracketed by
+    cudaProfilerStart / Stop (for ncu --profile-from-start off)."""
     import numpy as np
     import torch
 
@@ -101,12 +99,7 @@ def prefill(P: int, model_dir: str = "/tmp/tptc_models") -> None:
     from .engine import CudaEngine
 
     cfg = synth.CONFIGS["c5_llama8b_q4km"]
-    os.makedirs(model_dir, exist_ok=True)
-    path = os.path.join(model_dir, f"{cfg.name}_s0.gguf")
-    if not os.path.exists(path):
-        tmp = path + f".tmp{os.getpid()}"
-        synth.write_gguf(tmp, cfg, seed=0)
-        os.replace(tmp, path)
+    path = synth.model_file(cfg)
     e = CudaEngine(0)
     e.load(path)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, P).tolist()

@@ -285,6 +285,28 @@ def write_gguf(path: str, cfg: ModelConfig, seed: int = 0,
     return size
 
 
+def default_model_dir() -> str:
+    """Where generated benchmark models are kept: $TPTC_MODEL_DIR, else tptc_models under the
+    system temporary directory."""
+    import tempfile
+
+    return os.environ.get("TPTC_MODEL_DIR") or os.path.join(tempfile.gettempdir(), "tptc_models")
+
+
+def model_file(cfg: ModelConfig, model_dir: Optional[str] = None, seed: int = 0) -> str:
+    """Path of the seeded model `cfg` in `model_dir` (default_model_dir()), written first if
+    absent.  The file appears under its final name only once complete (written to a
+    process-private name, then renamed), so concurrent writers never read a partial file."""
+    model_dir = model_dir or default_model_dir()
+    os.makedirs(model_dir, exist_ok=True)
+    path = os.path.join(model_dir, f"{cfg.name}_s{seed}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_gguf(tmp, cfg, seed=seed)
+        os.replace(tmp, path)
+    return path
+
+
 def tensor_values(cfg: ModelConfig, name: str, seed: int = 0) -> np.ndarray:
     """The f32 values drawn for tensor `name` before encoding (tests)."""
     kinds = {n: (k, ne) for n, k, ne in cfg.tensors()}
