@@ -281,21 +281,31 @@ TPTC_API int tptc_attn_decode(const float* d_q, const float* d_kraw, void* d_kca
 /* No counterpart in the reference: tptc_attn_decode for callers that cannot allocate device
  * memory -- a host whose device memory is all reserved up front by its own pool or another
  * framework's caching allocator, or a decode loop that must not call cudaMalloc / cudaFree
- * because they can synchronise the device.  Same arguments and results, minus the workspace: the scratch is a static device
- * array of 1 MiB per device (split counters, error word and split partials; the partials
- * take splits * n_heads * (head_dim + 2) * 4 bytes).  Sizes whose scratch exceeds 1 MiB are
- * rejected with TPTC_ERR_ARG and a message giving both sizes.  The call makes no cudaMalloc,
- * cudaFree or other allocating call.  Its first call on a device does a one-time set-up with
- * that device current: it looks the array's device address up (cudaGetSymbolAddress) and
- * zeroes the array on `stream`, waiting for that; make this first call before any stream
- * capture.  Every launch that does not time out leaves the counters zero again.  The array is shared by all calls on a device: calls that may overlap on the GPU (different
- * streams without ordering, several host threads) race on it and give wrong results, so
- * callers serialise them.  A position outside the cache or a timed-out wait leaves d_out
- * unwritten and is not reported by this call (the error word is internal). */
+ * because they can synchronise the device.  Same arguments and results, minus the
+ * workspace: the scratch is a static device array of 1 MiB per device (split counters, error
+ * word and split partials; the partials take splits * n_heads * (head_dim + 2) * 4 bytes).
+ * Sizes whose scratch exceeds 1 MiB are rejected with TPTC_ERR_ARG and a message giving both
+ * sizes.  The call makes no cudaMalloc, cudaFree or other allocating call.  Its first call on
+ * a device does a one-time set-up with that device current: it looks the array's device
+ * address up (cudaGetSymbolAddress) and zeroes the array on `stream`, waiting for that; make
+ * this first call before any stream capture.  Every call then zeroes the error word and the
+ * split counters on `stream` before its launch, so a launch that was flagged or whose bounded
+ * wait gave up never affects the next call.  The array is shared by all calls on a device:
+ * calls that may overlap on the GPU (different streams without ordering, several host
+ * threads) race on it and give wrong results, so callers serialise them.  A position outside
+ * the cache or a timed-out wait leaves d_out unwritten; tptc_attn_decode_noalloc_status
+ * reports it. */
 TPTC_API int tptc_attn_decode_noalloc(const float* d_q, const float* d_kraw, void* d_kcache, const void* d_vcache,
                                       int kv_type, const float* d_rope_cos, const float* d_rope_sin,
                                       const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
                                       float* d_out, void* stream);
+/* No counterpart in the reference: the outcome of the most recent tptc_attn_decode_noalloc
+ * launch on the current device.  Waits for `stream`, then sets *out_code to the launch's
+ * internal error word: 0 (completed), TPTC_ERR_ARG (its position was outside [0, max_seq),
+ * nothing was written) or TPTC_ERR_TIMEOUT (a bounded wait gave up, d_out is incomplete).  A
+ * nonzero word also re-zeroes the whole static array.  *out_code is 0 when no call has run on
+ * this device.  Allocates nothing. */
+TPTC_API int tptc_attn_decode_noalloc_status(void* stream, int* out_code);
 
 #ifdef __cplusplus
 }

@@ -6,7 +6,11 @@
 - top-p (candle sample_topp: keep every token whose strictly larger probabilities sum below
   top_p): the kernel works on fixed-point masses m = floor(e * 2^40) of e = exp(x - max); the
   test reads back the kernel's e, applies the rule in exact integer arithmetic in numpy and
-  compares the cut, the kept mass and the total;
+  compares the cut, the kept mass and the total; a second restatement follows candle's own
+  walk (stable descending sort, running float64 sum, keep while the sum before is below
+  top_p) and must give the same kept set whenever no two tokens tie at the cut (with a tie at
+  the cut candle keeps only a prefix of the tied tokens in index order, the kernel all);
+- a temperature below 1e-7 is greedy (candle LogitsProcessor::new);
 - the draw: empirical frequencies against the kept masses (statistical bound), never a token
   outside the nucleus, and the same token for the same (seed, step);
 - the engine: infer with a temperature is reproducible for a seed and stays in range.
@@ -101,6 +105,23 @@ def kept_rule(e, top_p):
     return int(np.float32(keep_min).view(np.uint32)), kept, total
 
 
+def candle_topp_kept(e, top_p):
+    """candle sample_topp restated in float64: probabilities e / sum(e), indices sorted by
+    descending probability (stable), a running sum; an index is kept while the sum of the
+    indices before it is below top_p.  Returns (kept mask, the running sum where the walk
+    stopped keeping, i.e. the boundary the decision was taken at)."""
+    e64 = e.astype(np.float64)
+    p = e64 / e64.sum()
+    order = np.argsort(-p, kind="stable")
+    before = np.cumsum(p[order]) - p[order]
+    keep_sorted = before < top_p
+    kept = np.zeros(e.size, bool)
+    kept[order[keep_sorted]] = True
+    n = int(keep_sorted.sum())
+    boundary = before[n] if n < e.size else 1.0
+    return kept, boundary
+
+
 @pytest.mark.parametrize("V,temperature,top_p", [(1000, 1.0, 0.9), (128256, 0.7, 0.9), (128256, 0.7, 0.5),
                                                  (50000, 2.0, 0.99), (4096, 0.3, 1e-6), (4096, 1.0, 1.0)])
 def test_top_p_cut_matches_rule(cuda_device, V, temperature, top_p):
@@ -118,6 +139,20 @@ def test_top_p_cut_matches_rule(cuda_device, V, temperature, top_p):
     assert int(dbg[1]) == kept
     bits = e.view(np.uint32)
     assert bits[tok] >= cut and e[tok] > 0
+    if 0.0 < top_p < 1.0:
+        ck, boundary = candle_topp_kept(e, top_p)
+        cut_val = np.uint32(cut).view(np.float32)
+        tie_at_cut = int((e == cut_val).sum()) > 1
+        if not tie_at_cut and abs(boundary - top_p) > 1e-9:
+            np.testing.assert_array_equal(bits >= cut, ck)
+
+
+def test_tiny_temperature_is_greedy(cuda_device):
+    """candle's LogitsProcessor::new takes a temperature below 1e-7 as none: argmax."""
+    rng = np.random.default_rng(11)
+    lg = (rng.standard_normal(128256) * 3).astype(np.float32)
+    for t in (1e-9, 5e-8, 0.0, -1.0):
+        assert run(lg, None, temperature=t, top_p=0.9, seed=3)[0] == argmax_last(lg)
 
 
 def test_draws_follow_the_kept_masses(cuda_device):

@@ -83,6 +83,7 @@ SIGNATURES = {
                                  c_vp, c_i64, c_vp]),
     "tptc_attn_decode_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
                                          c_vp, c_vp]),
+    "tptc_attn_decode_noalloc_status": (c_int, [c_vp, ctypes.POINTER(c_int)]),
 }
 
 _L = None

@@ -10,10 +10,14 @@
 // allocating library routine is called on this path.
 //
 // What must start at zero: the split counters (the last CTA of each kv head resets its own
-// counter, so a completed launch leaves them zero again) and the error word.  Set-up, done by
-// the first call on a device with that device current, looks the array's address up and
-// zeroes the whole array, ordered on the caller's stream and waited for, before the first
-// launch there; that first call belongs before any stream capture.
+// counter, so a completed launch leaves them zero again, but a launch whose bounded wait gave
+// up may not) and the error word.  Set-up, done by the first call on a device with that
+// device current, looks the array's address up and zeroes the whole array, ordered on the
+// caller's stream and waited for, before the first launch there; that first call belongs
+// before any stream capture.  After that every call zeroes the error word and the counters
+// (the array's head, up to the partials) on its stream before its launch, so a call never
+// inherits a flagged or interrupted launch's state; the partials are always overwritten
+// before they are read.  attn_noalloc_status reads the error word the last launch left.
 //
 // The array is shared by every call on a device.  Calls that may overlap on the GPU (launched
 // on different streams without ordering between them, or from several host threads) race on
@@ -47,6 +51,26 @@ cudaError_t attn_noalloc_scratch(int device, cudaStream_t st, uint8_t** out) {
     }
     *out = g_scratch_ptr[device];
     return cudaSuccess;
+}
+
+cudaError_t attn_noalloc_status(int device, cudaStream_t st, int* code) {
+    *code = 0;
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint8_t* p = g_scratch_ptr[device];
+    if (!p) return cudaSuccess;  // no call on this device yet: nothing was flagged
+    int word = 0;
+    // the error word sits at offset 0 of the scratch (attn_scratch_layout); a 4-byte copy
+    // into this stack variable, ordered after the stream's last launch
+    cudaError_t e = cudaMemcpyAsync(&word, p, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return e;
+    *code = word;
+    if (word != 0) {  // a flagged launch: start the next one from a zeroed array
+        e = cudaMemsetAsync(p, 0, kAttnNoAllocScratchBytes, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    return e;
 }
 
 }  // namespace tptc

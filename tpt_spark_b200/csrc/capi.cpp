@@ -453,8 +453,20 @@ TPTC_API int tptc_attn_decode_noalloc(const float* d_q, const float* d_kraw, voi
     uint8_t* ws = nullptr;
     cudaError_t e = tptc::attn_noalloc_scratch(dev, st, &ws);
     if (e != cudaSuccess) return cuda_fail(e, "attention (no-alloc) scratch set-up");
+    // error word and split counters start every call at zero, whatever the last launch left
+    e = cudaMemsetAsync(ws, 0, L.partial, st);
+    if (e != cudaSuccess) return cuda_fail(e, "attention (no-alloc) scratch reset");
     return attn_launch(d_q, d_kraw, d_kcache, d_vcache, kv_type, d_rope_cos, d_rope_sin, d_pos, d_out, n_heads, n_kv,
                        head_dim, max_seq, ws, L, st);
+}
+
+TPTC_API int tptc_attn_decode_noalloc_status(void* stream, int* out_code) {
+    if (!out_code) return fail_code(nullptr, TPTC_ERR_ARG, "attention (no-alloc) status: null out_code");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    e = tptc::attn_noalloc_status(dev, static_cast<cudaStream_t>(stream), out_code);
+    return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "attention (no-alloc) status");
 }
 
 TPTC_API int tptc_sample(const float* d_logits, int vocab, int* d_counts, float penalty, float temperature,

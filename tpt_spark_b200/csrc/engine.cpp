@@ -886,7 +886,7 @@ Status Engine::infer(const uint32_t* prompt, int n, const tptc_infer_params& p, 
 
     // next-token selection on the device (sample.cu): the context counts feed the repeat
     // penalty; greedy without a penalty keeps the argmax inside the decode graph
-    const bool greedy = p.temperature <= 0.f;
+    const bool greedy = !(p.temperature >= 1e-7f);  // candle: temperature < 1e-7 is argmax
     const bool penalty = fabsf(p.repeat_penalty - 1.f) >= 1.1920929e-7f;
 
     auto t0 = clk::now();

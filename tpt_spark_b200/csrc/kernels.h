@@ -68,6 +68,9 @@ constexpr size_t kAttnNoAllocScratchBytes = size_t(1) << 20;
 // Address of `device`'s static scratch (the current device); the first call per device looks
 // it up and zeroes it on `st` (synchronously).
 cudaError_t attn_noalloc_scratch(int device, cudaStream_t st, uint8_t** out);
+// The error word the last launch on `device`'s static scratch left (0: none), read after
+// `st` finishes; a nonzero word re-zeroes the whole array.
+cudaError_t attn_noalloc_status(int device, cudaStream_t st, int* code);
 
 // misc.cu
 // x[dim] = dequantised row `tok` of token_embd (device layout), token read from *tok_ptr.

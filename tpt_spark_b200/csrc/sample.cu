@@ -12,11 +12,16 @@
 //      occurrence of its token in the context -- the reference's loop over `seen`, duplicates
 //      included, skipped when |penalty - 1| < FLT_EPSILON; the same IEEE operations in the
 //      same order per logit, so bit-identical to the host loop;
-//   2. temperature <= 0: argmax of the penalised logits, ties to the highest index (candle's
+//   2. temperature below 1e-7 (candle's LogitsProcessor::new takes such a temperature as
+//      none): argmax of the penalised logits, ties to the highest index (candle's
 //      sample_argmax keeps the last maximum);
 //   3. otherwise x / temperature, e = exp(x - max) (softmax numerators);
-//   4. top-p in (0, 1): candle's sample_topp keeps, in descending order of probability, every
-//      token whose strictly larger tokens sum to less than top_p.  Here the masses are fixed
+//   4. top-p in (0, 1): candle's sample_topp walks the tokens in descending order of
+//      probability (a stable sort) and keeps each while the sum of those before it is below
+//      top_p.  Here every token whose strictly larger tokens sum to less than top_p is kept:
+//      the same set unless several tokens tie at the cut, where candle keeps only those of
+//      them that come first in index order while its running sum stays below top_p and this
+//      kernel keeps them all.  Here the masses are fixed
 //      point (m = floor(e * 2^40), summed in 64-bit integers, so the result does not depend on
 //      the order of atomics) and the cut is found exactly by a three-level radix select over
 //      the bit patterns of e (10 + 10 + 10 bits, 1024 shared buckets per level): the kept set
@@ -145,7 +150,8 @@ __global__ void __launch_bounds__(kST, 1) sample_kernel(SampleParams p) {
     pdl_launch_dependents();
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, V = p.vocab;
     const bool pen = fabsf(p.penalty - 1.f) >= 1.1920929e-7f && p.counts != nullptr;
-    const bool greedy = !(p.temperature > 0.f);
+    // candle LogitsProcessor::new: a temperature below 1e-7 means none, i.e. argmax
+    const bool greedy = !(p.temperature >= 1e-7f);
     int tok = 0;
 
     // 1-3: penalty, then argmax or x / T and its maximum

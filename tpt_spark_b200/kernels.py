@@ -92,6 +92,14 @@ def attn_decode_noalloc(d_q, d_kraw, d_kcache, d_vcache, kv_type: int, d_rope_co
                                          max_seq, _ptr(d_out), stream))
 
 
+def attn_decode_noalloc_status(stream: Optional[int] = None) -> int:
+    """tptc_attn_decode_noalloc_status: the error word of the last no-alloc attention launch on
+    the current device (0, or a negative TPTC_ERR_* code), after `stream` finishes."""
+    code = ctypes.c_int()
+    check(lib().tptc_attn_decode_noalloc_status(stream, ctypes.byref(code)))
+    return code.value
+
+
 def sample(d_logits, vocab: int, d_counts, penalty: float, temperature: float, top_p: float, seed: int, d_step,
            d_scratch, d_out, d_dbg=None, stream: Optional[int] = None) -> None:
     """The engine's device next-token selection (tptc_sample): repeat penalty over d_counts,
