@@ -26,9 +26,11 @@ between steps.
   cpu_baseline    the CPU oracle (restated candle path) on the box's host cores, bounded sample
 
 With --gpus N > 1 (torchrun, one rank per GPU) the engine is one Megatron tensor-parallel
-job over the N GPUs (column-parallel q/k/v/gate/up, row-parallel o/down, NCCL allreduce after
-each row-parallel projection): value is the tok/s of the one sequence all ranks decode
-together ("scaling": "strong"), decode_roofline compares against the N GPUs' aggregate HBM.
+job over the N GPUs (column-parallel q/k/v/gate/up, row-parallel o/down; in the decode step
+each row-parallel GEMV stores its partial rows into every rank's inbox over NVLink and the
+next activation kernel sums them, the batched prefill all-reduces with NCCL): value is the
+tok/s of the one sequence all ranks decode together ("scaling": "strong"), decode_roofline
+compares against the N GPUs' aggregate HBM.
 
 --impl reference times the CPU oracle on the same workload (rank 0 only).
 """

@@ -74,7 +74,7 @@ typedef struct {
  * (tokenizer.json beside the .gguf, wgpu_engine.rs:892-906) and passes ids. */
 typedef struct {
     uint32_t max_tokens;
-    float temperature;        /* <= 0: greedy (LogitsProcessor with temperature None) */
+    float temperature;        /* below 1e-7: greedy (LogitsProcessor::new takes it as None) */
     float top_p;              /* >= 1: no nucleus filter */
     float repeat_penalty;     /* 1: off (candle_engine.rs:87-101) */
     uint64_t seed;            /* sampling seed (the reference uses LogitsProcessor::new(42, ..)) */
@@ -225,13 +225,10 @@ TPTC_API int tptc_matrix_dequant_f16(const tptc_matrix* m, void* d_out, void* st
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,
                              void* stream);
 
-/* Prefill GEMM on the tensor cores: C[M x N] (f32, row-major) = A[M x K] . B[N x K]^T with A
- * and B row-major fp16 (16-byte aligned), K a multiple of 64 -- the prompt-wide replacement of
- * gemm.wgsl's per-token M = 1 products. */
 /* The engine's next-token selection on the device (infer's sampling step), as a kernel:
  * logits[vocab] with the repeat penalty applied once per context occurrence (counts[vocab],
  * candle_engine.rs:87-101; the picked token's count is incremented), then argmax when
- * temperature <= 0 (ties to the highest index), else softmax(x / temperature), the top-p
+ * temperature is below 1e-7 (ties to the highest index), else softmax(x / temperature), the top-p
  * nucleus in (0, 1) (candle sample_topp's kept set, computed exactly in fixed point) and one
  * SplitMix64 draw of (seed, *step) (*step incremented).  scratch: [vocab] floats.  dbg
  * (nullable): [3] u64 = kept-set cut (fp32 bit pattern of the smallest kept exp(x - max)),
@@ -239,6 +236,9 @@ TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_
 TPTC_API int tptc_sample(const float* d_logits, int vocab, int* d_counts, float penalty, float temperature,
                          float top_p, uint64_t seed, int* d_step, float* d_scratch, uint32_t* d_out_tok,
                          uint64_t* d_dbg, void* stream);
+/* Prefill GEMM on the tensor cores: C[M x N] (f32, row-major) = A[M x K] . B[N x K]^T with A
+ * and B row-major fp16 (16-byte aligned), K a multiple of 64 -- the prompt-wide replacement of
+ * gemm.wgsl's per-token M = 1 products. */
 TPTC_API int tptc_gemm_f16(const void* d_a, const void* d_b, float* d_c, int M, int N, int K, void* stream);
 /* The prefill GEMM with the weight dequantisation fused in: C[M x N] (f32) = A[M x K] . W^T
  * with A row-major fp16 (16-byte aligned) and W a Q4_K / Q6_K / Q8_0 matrix (tptc_matrix,

@@ -84,14 +84,14 @@ cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_
                           uint32_t* history, cudaStream_t st, bool pdl);
 
 // sample.cu: the next token from logits[vocab] on the device (one CTA): repeat penalty over
-// the context counts, then argmax (temperature <= 0) or softmax(x / T), top-p and one seeded draw.
+// the context counts, then argmax (temperature below 1e-7) or softmax(x / T), top-p and one seeded draw.
 struct SampleParams {
     const float* logits;
     int vocab;
     int* counts;        // [vocab] occurrences of each token in the context (penalty); the
                         // sampled token's count is incremented; may be null (no penalty)
     float penalty;      // 1 = off
-    float temperature;  // <= 0: argmax, ties to the highest index
+    float temperature;  // below 1e-7 (candle: no temperature): argmax, ties to the highest index
     float top_p;        // in (0, 1): nucleus; otherwise every token
     unsigned long long seed;
     int* step;          // draw counter (read, then incremented); null = draw 0

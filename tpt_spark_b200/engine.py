@@ -6,8 +6,8 @@ Reference interface (src-tauri/src/engine/mod.rs):
                      repeat_penalty}, defaults 512 / 0.7 / 0.9 / 1.1  :35-59
     LlmEngine::{load, unload, is_loaded, model_info, infer}          :62-82
     ModelInfo {name, path, size_bytes, backend}     :85-92
-The Rust host would bind the same C ABI; this module is what the tests and
-the benchmark drive.  Prompts are token ids (the reference tokenises with tokenizer.json,
+The Rust host binds the same C ABI (tpt_spark_b200/rust/engine/cuda_ffi.rs); this module is
+what the tests and the benchmark drive.  Prompts are token ids (the reference tokenises with tokenizer.json,
 which is not on the numeric path); a string prompt is accepted when a tokenizer is given.
 Errors raise EngineError (the reference returns anyhow::Error).
 """
