@@ -71,7 +71,6 @@ def parse():
     ap.add_argument("--workload", default="c5_llama8b_q4km")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default: the config's)")
     ap.add_argument("--model-dir", default=None, help="generated models (default: $TPTC_MODEL_DIR or <tmp>/tptc_models)")
-    ap.add_argument("--e2e-steps", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args()
@@ -127,52 +126,102 @@ def model_file(cfg, model_dir, seed, dist):
 
 
 class Clocks:
-    """nvidia-smi samples (200 ms) during the timed region."""
+    """SM clock, power and clock-event reasons of the benchmark's GPU, read through NVML every
+    5 ms in a thread (query only) while the timed region runs: `mark(True/False)` brackets the
+    region, and only samples taken inside it count.  Falls back to nvidia-smi at 200 ms when
+    NVML cannot be loaded."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, cuda_index, period_s=0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.rows = []  # (in_region, sm_mhz, max_mhz, watts, reasons)
+        self.inside = False
+        self.stop = threading.Event()
+        self.thread = None
+        self.nvml = None
+        self.handle = None
         self.proc = None
-        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def _open(self):
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(self.cuda_index)
+            try:
+                bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+
+    def _loop(self):
+        n = self.nvml
+        bits = {"hw_slowdown": n.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": n.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": n.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": n.nvmlClocksEventReasonSwPowerCap}
+        mx = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                w = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                r = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.rows.append((self.inside, float(sm), float(mx), w, {k for k, b in bits.items() if r & b}))
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
-                                         stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        self._open()
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
+        else:
+            self.smi = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.cuda_index), f"--query-gpu={q}",
+                                              "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.smi,
+                                             stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
         return self
 
+    def mark(self, inside):
+        self.inside = inside
+
     def __exit__(self, *a):
-        if self.proc:
+        self.stop.set()
+        if self.thread:
+            self.thread.join(2)
+        elif self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(5)
             except Exception:
                 self.proc.kill()
+            for line in open(self.smi.name):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8 and parts[1].replace(".", "").isdigit():
+                    rs = {k for k, v in zip(self.NAMES, parts[4:8]) if v.lower().startswith("active")}
+                    self.rows.append((True, float(parts[1]), float(parts[2]), float(parts[3] or 0), rs))
 
     def summary(self):
-        self.out.flush()
-        rows = []
-        try:
-            for line in open(self.out.name):
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        except Exception:
-            pass
+        rows = [r for r in self.rows if r[0]]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": sorted(set().union(*(r[4] for r in rows))), "samples": len(rows),
+                "power_w_median": round(statistics.median(r[3] for r in rows), 1),
+                "source": "nvml 5 ms" if self.nvml is not None else "nvidia-smi 200 ms"}
 
 
 def decode_bytes(cfg, kv_len_mean):
@@ -251,18 +300,38 @@ def profile_traffic(name):
     return None
 
 
-def cpu_baseline(path, cfg, max_seconds=25.0, prompt_len=8):
-    """The oracle (restated candle path) on all host cores: a short prompt, then timed decode
-    steps until max_seconds of CPU work.  Returns (tok/s, steps, cores, sample text)."""
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_baseline(path, cfg, decode_pos, max_decode_s=20.0, prefill_tokens=64, max_steps=60):
+    """The oracle (restated candle path) on all host cores, on a bounded sample of the GPU arm's
+    workload:
+      prefill  one batched forward of a `prefill_tokens`-token prompt (candle_engine.rs:272-281
+               prefills in one forward) -- the full 8192-token prompt would take minutes here;
+      decode   greedy steps at KV positions decode_pos, decode_pos + 1, ... -- the GPU arm's
+               context length -- for up to max_decode_s seconds or max_steps steps.  The cache
+               positions below decode_pos hold zeros instead of a prefilled prompt (no 8192-token
+               CPU prefill was run), which leaves the work of every step -- the attention over
+               decode_pos + 1 keys and every weight matrix once -- the same as after a real prompt.
+    Returns a dict with both rates, the cores used and a description of the sample."""
     from oracle import oracle as O
 
     cores = os.cpu_count() or 1
     O.set_threads(cores)
-    m = O.Model(path, max_seq=prompt_len + 64)
-    prompt = list(range(1, prompt_len + 1))
+    m = O.Model(path, max_seq=max(decode_pos, prefill_tokens) + max_steps + 8)
+    prompt = list(range(1, prefill_tokens + 1))
+    t0 = time.perf_counter()
     lg = m.forward(prompt, 0)
+    pf_s = time.perf_counter() - t0
     tok = O.argmax(lg)
-    pos, n = prompt_len, 0
+    pos, n = decode_pos, 0
     t0 = time.perf_counter()
     while True:
         lg = m.forward([tok], pos)
@@ -270,12 +339,14 @@ def cpu_baseline(path, cfg, max_seconds=25.0, prompt_len=8):
         pos += 1
         n += 1
         el = time.perf_counter() - t0
-        if el > max_seconds or n >= 60:
+        if el > max_decode_s or n >= max_steps:
             break
     m.close()
-    sample = (f"{n} greedy decode steps of the full {cfg.name} model after a {prompt_len}-token prompt "
-              f"(kv_len {prompt_len + 1}..{prompt_len + n}), {cores} OpenMP threads")
-    return n / el, n, cores, sample
+    sample = (f"{n} greedy decode steps of the full {cfg.name} model at KV lengths {decode_pos + 1}..{decode_pos + n} "
+              f"(positions below {decode_pos} zero-filled, not prefilled), and one {prefill_tokens}-token prefill; "
+              f"{cores} OpenMP threads on {cpu_model()}")
+    return {"decode_tok_s": n / el, "steps": n, "prefill_tok_s": prefill_tokens / pf_s,
+            "prefill_tokens": prefill_tokens, "cores": cores, "cpu": cpu_model(), "sample": sample}
 
 
 def run_reference(args, dist):
@@ -285,14 +356,18 @@ def run_reference(args, dist):
     if dist.rank != 0:
         return
     path = model_file(cfg, args.model_dir, args.seed, _Solo())
-    tps, n, cores, sample = cpu_baseline(path, cfg, max_seconds=max(20.0, 2.0 * (args.steps + args.warmup) / 60.0))
+    P = args.prompt if args.prompt is not None else PROMPT_LEN[cfg.name]
+    cb = cpu_baseline(path, cfg, decode_pos=P + args.warmup)
+    tps = cb["decode_tok_s"]
     line = {"metric": "decode tok/s (bs=1)", "value": round(tps, 4), "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": n, "warmup": 0, "ms_per_step": round(1000.0 / tps, 2), "higher_is_better": True,
+            "steps": cb["steps"], "warmup": 0, "ms_per_step": round(1000.0 / tps, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": cfg.name, "batch": 1, "decode_tokens": DECODE_LEN[cfg.name]},
-            "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+            "config": {"workload": cfg.name, "batch": 1, "prompt_tokens": P, "decode_kv_len_start": P + args.warmup + 1},
+            "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": cb["cores"], "kind": "port",
+                             "sample": cb["sample"], "cpu": cb["cpu"],
+                             "prefill": {"value": round(cb["prefill_tok_s"], 2), "unit": "tok/s",
+                                         "tokens": cb["prefill_tokens"]}},
             "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -330,12 +405,11 @@ def run_ours(args, dist):
     rng = np.random.default_rng(1234 + args.seed)
     prompt = rng.integers(0, cfg.vocab, P).tolist()
 
-    # prefill (device time): one warm-up pass (buffer allocation, first-touch), then timed
-    eng.kv_reset()
-    eng.prefill(prompt, want_logits=False)
+    # The prompt's KV context for the decode steps: one prefill (untimed; it also allocates the
+    # prefill buffers and touches them once).  Decode is timed next, and the timed prefill
+    # comes after it, so the timed decode region never follows a long prefill at full power.
     eng.kv_reset()
     lg = eng.prefill(prompt)
-    prefill_ms = eng.last_device_ms()
     tok = int(np.argmax(lg))
 
     # decode: warm-up then K timed steps; the window past the prompt is reused when the
@@ -359,28 +433,33 @@ def run_ours(args, dist):
         return ms, tok, kv_sum / max(n, 1)
 
     _, tok, _ = run_steps(args.warmup, tok)
+    kv_start, tok_start = eng.kv_len(), tok  # the timed region's first position and token
     dist.barrier()
     torch.cuda.synchronize()
     with Clocks(dist.local) as clk:
+        time.sleep(0.02)  # the sampler is running before the region starts
+        clk.mark(True)
         torch.cuda.profiler.start()  # ncu --profile-from-start off captures only this region
         ms, tok, kv_mean = run_steps(args.steps, tok)
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
+        clk.mark(False)
     torch.cuda.synchronize()
     dist.barrier()
     ms = dist.max(ms)
     tps = args.steps / (ms / 1000.0)  # one sequence decoded by all ranks together
 
-    # end to end through the C ABI with host buffers
-    e2e_steps = min(args.e2e_steps, args.steps)
-    eng.kv_truncate(P)
-    pos = P
+    # end to end through the C ABI with host buffers, over the same steps and positions as the
+    # timed region: each step copies the token id and position in and the argmax out
+    eng.kv_truncate(kv_start)
+    pos, tok = kv_start, tok_start
+    dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
+    for _ in range(args.steps):
         tok = eng.decode(tok, pos, want_logits=False)
         pos += 1
     e2e_s = dist.max(time.perf_counter() - t0)
-    e2e_tps = e2e_steps / e2e_s
+    e2e_tps = args.steps / e2e_s
 
     # the product call with the reference's default chat parameters (InferenceParams::default:
     # temperature 0.7, top-p 0.9, repeat penalty 1.1): tptc_infer, every token selected on the
@@ -391,6 +470,11 @@ def run_ours(args, dist):
     eng.infer(InferenceParams(prompt=prompt, max_tokens=n_sampled, seed=42), lambda ev: None)
     _, dec_ms, _, n_gen = eng.last_timing()
     sampled_tps = n_gen / dist.max(dec_ms / 1000.0) if n_gen else 0.0
+
+    # prefill (device time), after the decode measurements
+    eng.kv_reset()
+    eng.prefill(prompt, want_logits=False)
+    prefill_ms = dist.max(eng.last_device_ms())
 
     pk = peaks()
     pk.setdefault("bf16_tflops_sustained", pk["bf16_tflops"])
@@ -416,7 +500,8 @@ def run_ours(args, dist):
         "config": {"workload": cfg.name, "batch": 1, "prompt_tokens": P, "decode_kv_len_mean": round(kv_mean, 1),
                    "parallelism": f"tp{dist.world}" if dist.world > 1 else "single", "l2": "inputs larger than L2 (4.9 GB weights)"},
         "e2e": {"value": round(e2e_tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                "d2h_bytes_per_step": 4},
+                "d2h_bytes_per_step": 4, "steps": args.steps,
+                "path": "tptc_decode per token (token id and position in, argmax out), same positions as value"},
         "sampled": {"value": round(sampled_tps, 3), "unit": "tok/s", "tokens": n_gen,
                     "params": "temperature 0.7, top-p 0.9, repeat penalty 1.1 (the reference's defaults)",
                     "path": "tptc_infer with host callbacks; penalty, softmax, nucleus and draw on the device"},
@@ -443,8 +528,11 @@ def run_ours(args, dist):
     }
     eng.close()
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        v, n, cores, sample = cpu_baseline(path, cfg)
-        line["cpu_baseline"] = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+        cb = cpu_baseline(path, cfg, decode_pos=kv_start)
+        line["cpu_baseline"] = {"value": round(cb["decode_tok_s"], 4), "unit": "tok/s", "cores": cb["cores"],
+                                "kind": "port", "sample": cb["sample"], "cpu": cb["cpu"],
+                                "prefill": {"value": round(cb["prefill_tok_s"], 2), "unit": "tok/s",
+                                            "tokens": cb["prefill_tokens"]}}
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
 
