@@ -411,6 +411,13 @@ def run_ours(args, dist):
     eng.kv_reset()
     lg = eng.prefill(prompt)
     tok = int(np.argmax(lg))
+    # The 8192-token prefill runs at the 1 kW power cap, and the power limiter keeps the SM
+    # clock lowered for a few hundred ms after it (measured on a B200: 1560 MHz with
+    # sw_power_cap and 2.95 ms per decode step right after the prefill, 1965 MHz and 2.21 ms
+    # from 0.38 s on, at 730 W).  A decode stream does not see that transient in steady state,
+    # so the GPU idles for a second before the warm-up steps.
+    torch.cuda.synchronize()
+    time.sleep(1.0)
 
     # decode: warm-up then K timed steps; the window past the prompt is reused when the
     # context would overflow (the cache is truncated back to the prompt)
