@@ -137,6 +137,12 @@ TPTC_API int tptc_set_prefill_gemm_min(tptc_ctx* ctx, int min_tokens);
  * two-pass ones (Q8_0: identical). */
 enum { TPTC_FUSED_NEVER = 0, TPTC_FUSED_AUTO = 1, TPTC_FUSED_ALWAYS = 2 };
 TPTC_API int tptc_set_prefill_fused(tptc_ctx* ctx, int mode);
+/* Tensor parallelism (no counterpart in the one-device reference): how many reads of a
+ * peer's inbox word a decode kernel makes before it gives up on a rank that does not arrive
+ * (the step then fails with TPTC_ERR_TIMEOUT instead of waiting for ever).  0 (default) keeps
+ * the library's bound of 2^22 reads (seconds); a smaller bound makes a stalled peer show up
+ * sooner.  Set before tptc_load_gguf. */
+TPTC_API int tptc_set_tp_wait_polls(tptc_ctx* ctx, uint32_t polls);
 
 /* LlmEngine::load (mod.rs:66-70) -> load_gguf_to_vram (wgpu_loader.rs:87-201): mmap the
  * file, parse GGUF v3, check bounds, stream every tensor through pinned staging with

@@ -46,6 +46,7 @@ SIGNATURES = {
     "tptc_set_kv_dtype": (c_int, [c_vp, c_int]),
     "tptc_set_prefill_gemm_min": (c_int, [c_vp, c_int]),
     "tptc_set_prefill_fused": (c_int, [c_vp, c_int]),
+    "tptc_set_tp_wait_polls": (c_int, [c_vp, ctypes.c_uint32]),
     "tptc_tp_shard": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     "tptc_load_gguf": (c_int, [c_vp, ctypes.c_char_p, PROGRESS_CB, c_vp]),
     "tptc_unload": (c_int, [c_vp]),

@@ -131,6 +131,12 @@ TPTC_API int tptc_set_prefill_fused(tptc_ctx* ctx, int mode) {
     return TPTC_OK;
 }
 
+TPTC_API int tptc_set_tp_wait_polls(tptc_ctx* ctx, uint32_t polls) {
+    if (!ctx) return TPTC_ERR_ARG;
+    tptc::Status s = ctx->eng->set_tp_wait_polls(polls);
+    return s.ok() ? TPTC_OK : fail_code(ctx, s.code, s.msg);
+}
+
 TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user) {
     if (!ctx || !path) return fail_code(ctx, TPTC_ERR_ARG, "null argument");
     Status s = ctx->eng->load(path, progress, user);

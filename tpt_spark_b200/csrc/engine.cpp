@@ -284,7 +284,19 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         W(TPTC_SHARD_DOWN, "ffn_down.weight", m.dim, m.ffn, &L.down, 0, 0);
     }
     plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_, 0, 0});
-    if (!m.tied) plans.push_back({"output.weight", m.vocab, m.dim, 0, m.vocab, 0, m.dim, &output_, nullptr, 0, 0});
+    // lm_head: vocab-parallel under tensor parallelism when the vocabulary splits evenly (each
+    // rank its rows; with tied embeddings those rows of token_embd, which stays whole for the
+    // embedding lookup), replicated otherwise
+    head_rows_ = m.vocab;
+    head_row0_ = 0;
+    if (tp_size_ > 1 && m.vocab % tp_size_ == 0) {
+        head_rows_ = m.vocab / tp_size_;
+        head_row0_ = tp_rank_ * head_rows_;
+    }
+    const bool head_sliced = head_rows_ < m.vocab;
+    if (!m.tied || head_sliced)
+        plans.push_back({m.tied ? "token_embd.weight" : "output.weight", m.vocab, m.dim, head_row0_,
+                         head_row0_ + head_rows_, 0, m.dim, &output_, nullptr, 0, 0});
 
     // ---- validate and lay out the arena
     size_t off = 0;
@@ -354,7 +366,7 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         }
         if (cb) cb((uint32_t)(i + 1), (uint32_t)plans.size(), user);
     }
-    if (m.tied) output_ = embd_;
+    if (m.tied && !head_sliced) output_ = embd_;
     CU(cudaStreamSynchronize(stream_));
     RET_IF(alloc_runtime());
     loaded_ = true;
@@ -443,7 +455,7 @@ Status Engine::alloc_runtime() {
     CU(cudaMemcpyAsync(rope_sin_, s.data(), s.size() * 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaStreamSynchronize(stream_));
     // the peer-memory inboxes are baked into the graphs: map them before capture
-    if (tp_) RET_IF(tp_->init_p2p(m.dim, m.n_layers, step_, stream_));
+    if (tp_) RET_IF(tp_->init_p2p(m.dim, m.n_layers, step_, tp_wait_polls_, stream_));
     RET_IF(build_decode_graph(false, &graph_plain_));
     RET_IF(build_decode_graph(true, &graph_chained_));
     return {};
@@ -543,7 +555,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         p.x = x_;
         if (link) gather(p, 1, 2 * (m.n_layers - 1) + 1, x2_, x_);
         p.norm_w = out_norm_;
-        p.out = logits_;
+        p.out = logits_ + head_row0_;  // this rank's rows of the vocabulary
         gemv_prepare(p, sm_count_);
         return p;
     };
@@ -663,8 +675,13 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
     }
     GemvParams h = head_params();
     CU(gemv_launch(h, EPI_STORE, st, pdl_));
-    CU(launch_argmax(logits_, m.vocab, tok_out_, chained ? tok_in_ : nullptr, chained ? pos_ : nullptr,
-                     chained ? history_ : nullptr, st, pdl_));
+    if (head_rows_ < m.vocab)  // vocab-parallel: the ranks exchange their best over peer memory
+        CU(launch_argmax_tp(logits_ + head_row0_, head_rows_, head_row0_, link, err_, tok_out_,
+                            chained ? tok_in_ : nullptr, chained ? pos_ : nullptr, chained ? history_ : nullptr, st,
+                            pdl_));
+    else
+        CU(launch_argmax(logits_, m.vocab, tok_out_, chained ? tok_in_ : nullptr, chained ? pos_ : nullptr,
+                         chained ? history_ : nullptr, st, pdl_));
     return {};
 }
 
@@ -743,7 +760,10 @@ Status Engine::decode(uint32_t id, int pos, float* logits, uint32_t* argmax) {
     CU(cudaMemcpyAsync(tok_in_, h_tok_, 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaMemcpyAsync(pos_, h_pos_, 4, cudaMemcpyHostToDevice, stream_));
     CU(cudaGraphLaunch(graph_plain_, stream_));
-    if (logits) CU(cudaMemcpyAsync(logits, logits_, (size_t)meta_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits) {
+        RET_IF(gather_logits());
+        CU(cudaMemcpyAsync(logits, logits_, (size_t)meta_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    }
     if (argmax) CU(cudaMemcpyAsync(h_tok_ + 1, tok_out_, 4, cudaMemcpyDeviceToHost, stream_));
     RET_IF(sync());
     if (argmax) *argmax = h_tok_[1];
@@ -760,7 +780,13 @@ Status Engine::sample_reset(const uint32_t* context, int n) {
     return sync();
 }
 
+Status Engine::gather_logits() {
+    if (!tp_ || head_rows_ == meta_.vocab) return {};
+    return tp_->allgather(logits_, (size_t)head_rows_, stream_);
+}
+
 Status Engine::enqueue_sample(const tptc_infer_params& p) {
+    RET_IF(gather_logits());  // every rank samples the whole vocabulary, the same draw
     SampleParams s = {};
     s.logits = logits_;
     s.vocab = meta_.vocab;

@@ -64,6 +64,12 @@ class Engine {
     // When the batched prefill contracts quantised weights with the fused-dequant GEMM
     // (TPTC_FUSED_NEVER / AUTO / ALWAYS) instead of expanding each matrix to fp16 first.
     void set_prefill_fused(int mode) { prefill_fused_ = mode; }
+    // Reads a tensor-parallel wait makes before it gives up (set before load; 0 = default).
+    Status set_tp_wait_polls(uint32_t polls) {
+        if (loaded_) return Status{TPTC_ERR_STATE, "the wait bound must be set before load"};
+        tp_wait_polls_ = polls;
+        return {};
+    }
     bool prefill_uses_gemm(int n) const;
     int prefix_len(const uint32_t* ids, int n) const;
 
@@ -104,6 +110,9 @@ class Engine {
     Status run_prefill_batched(const uint32_t* ids, int n, int start_pos, float* last_logits);
     Status check_err();
     Status sync();
+    // Under a vocab-parallel lm_head every rank holds the logits of its rows; the full vector
+    // (host copies, sampling) is an NCCL all-gather, made by every rank at the same calls.
+    Status gather_logits();
 
     int device_, tp_rank_, tp_size_;
     int sm_count_ = 148;
@@ -122,6 +131,10 @@ class Engine {
     size_t rt_size_ = 0;
     std::vector<LayerWeights> layers_;
     DevMatrix embd_, output_;
+    // lm_head rows this rank computes: all of them, or under tensor parallelism (vocab a
+    // multiple of the rank count) rows [head_row0_, head_row0_ + head_rows_)
+    int head_row0_ = 0, head_rows_ = 0;
+    uint32_t tp_wait_polls_ = 0;  // bound of the tensor-parallel waits (0: the default)
     float* out_norm_ = nullptr;
     uint8_t* kv_ = nullptr;  // [L][2][n_kv_local][max_seq][hd], fp16 or f32
     bool kv_f32_ = false;

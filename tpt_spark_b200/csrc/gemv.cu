@@ -433,7 +433,9 @@ __device__ __forceinline__ void act_in8(const GemvParams& p, int off, float (&v)
         for (int i = 0; i < 8; i++) {
             uint32_t n = 0;
             while ((unsigned int)(w[i] >> 32) != e) {
-                if (++n > kWaitPolls) {
+                // give up after wait_polls reads, or within 256 once any wait of the step has
+                // (the error word is set: the peer is not coming)
+                if (++n > t.wait_polls || ((n & 255) == 0 && p.err && *reinterpret_cast<volatile int*>(p.err))) {
                     if (p.err) atomicExch(p.err, TPTC_ERR_TIMEOUT);
                     w[i] = (unsigned long long)e << 32;  // value 0
                     break;

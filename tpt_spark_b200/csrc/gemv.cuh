@@ -137,14 +137,21 @@ constexpr int kGemvMaxStages = 16;
 // kernel (tp_gather) reads every rank's block, waiting (bounded) on words whose epoch is not
 // yet the current one, and forms x_out = x + sum over ranks in rank order (the same bits on
 // every rank).  Epoch of use u of a step: step * uses_per_step + u + 1, with the step
-// counter advanced by the embedding kernel that opens every step.
+// counter advanced by the embedding kernel that opens every step.  After the [2][size][dim]
+// reduction slots each inbox holds [size][2] words for the vocab-parallel argmax (each
+// rank's best logit and its index, both tagged with the epoch of use 2 * n_layers).  A wait
+// gives up after wait_polls reads (TPTC_ERR_TIMEOUT): a rank that stops taking steps leaves
+// the others with an error, not a hung GPU.
 constexpr int kTpMaxRanks = 8;
 struct TpLink {
     int rank, size, dim;
-    int uses_per_step;  // 2 per layer
+    int uses_per_step;  // 2 per layer + 1 (the argmax exchange)
     unsigned long long* inbox[kTpMaxRanks];
     const int* step;    // this rank's decode step counter
+    uint32_t wait_polls;
 };
+__host__ __device__ inline size_t tp_inbox_words(int size, int dim) { return (size_t)2 * size * dim + (size_t)2 * size; }
+__host__ __device__ inline size_t tp_argmax_offset(int size, int dim) { return (size_t)2 * size * dim; }
 
 struct GemvSeg {
     DevMatrix m;

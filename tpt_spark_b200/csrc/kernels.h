@@ -82,6 +82,11 @@ cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, floa
 // increments *pos (device-chained greedy decode).
 cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_t* next_tok, int* pos,
                           uint32_t* history, cudaStream_t st, bool pdl);
+// The same over a vocab-parallel lm_head: logits[n] are this rank's rows [row0, row0 + n);
+// the ranks exchange their best (value, index) over the TpLink inboxes and all pick the same
+// token (a peer that never arrives: TPTC_ERR_TIMEOUT in *err after link->wait_polls reads).
+cudaError_t launch_argmax_tp(const float* logits, int n, int row0, const TpLink* link, int* err, uint32_t* out_tok,
+                             uint32_t* next_tok, int* pos, uint32_t* history, cudaStream_t st, bool pdl);
 
 // sample.cu: the next token from logits[vocab] on the device (one CTA): repeat penalty over
 // the context counts, then argmax (temperature below 1e-7) or softmax(x / T), top-p and one seeded draw.

@@ -325,12 +325,14 @@ Status Engine::run_prefill_batched(const uint32_t* ids, int n, int start_pos, fl
             h.seg[0] = GemvSeg{output_, 0};
             h.x = x_;
             h.norm_w = out_norm_;
-            h.out = logits_;
+            h.out = logits_ + head_row0_;
             gemv_prepare(h, sm_count_);
             TPTC_CUDA_RET(gemv_launch(h, EPI_STORE, stream_, false));
-            if (last_logits)
+            if (last_logits) {
+                PF_RET_IF(gather_logits());
                 TPTC_CUDA_RET(cudaMemcpyAsync(last_logits, logits_, (size_t)m.vocab * 4, cudaMemcpyDeviceToHost,
                                               stream_));
+            }
         }
         // the ids buffer is reused by the next chunk: wait for this one
         PF_RET_IF(sync());

@@ -89,9 +89,9 @@ Tp::~Tp() {
 // Own inbox allocation, its CUDA IPC handle exchanged with every rank over NCCL, the peers'
 // allocations mapped into this process (peer access over NVLink), and the TpLink the
 // kernels read.  Every rank calls it with the same dim and layer count.
-Status Tp::init_p2p(int dim, int n_layers, const int* step, cudaStream_t st) {
+Status Tp::init_p2p(int dim, int n_layers, const int* step, uint32_t wait_polls, cudaStream_t st) {
     if (size > kTpMaxRanks) return Status{TPTC_ERR_UNSUPPORTED, "peer-memory reduction supports up to 8 ranks"};
-    const size_t bytes = (size_t)2 * size * dim * sizeof(unsigned long long);
+    const size_t bytes = tp_inbox_words(size, dim) * sizeof(unsigned long long);
     TPTC_CUDA_RET(cudaMalloc(&p2p_mem, bytes));
     TPTC_CUDA_RET(cudaMemsetAsync(p2p_mem, 0, bytes, st));  // epoch 0: no use has that tag
     cudaIpcMemHandle_t mine;
@@ -114,8 +114,9 @@ Status Tp::init_p2p(int dim, int n_layers, const int* step, cudaStream_t st) {
     link.rank = rank;
     link.size = size;
     link.dim = dim;
-    link.uses_per_step = 2 * n_layers;
+    link.uses_per_step = 2 * n_layers + 1;  // o and down of every layer, then the argmax
     link.step = step;
+    link.wait_polls = wait_polls ? wait_polls : kWaitPolls;
     for (int r = 0; r < size; r++) {
         void* base = p2p_mem;
         if (r != rank) {
@@ -169,6 +170,12 @@ bool tp_shard(int which, int n_heads, int n_kv_heads, int head_dim, int dim, int
 Status Tp::allreduce(float* b, size_t n, cudaStream_t st) {
     ncclResult_t nr = nccl().AllReduce(b, b, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm), st);
     if (nr != ncclSuccess) return Status{TPTC_ERR_NCCL, nccl_msg("ncclAllReduce", nr)};
+    return {};
+}
+
+Status Tp::allgather(float* b, size_t count, cudaStream_t st) {
+    ncclResult_t nr = nccl().AllGather(b + (size_t)rank * count, b, count, ncclFloat32, static_cast<ncclComm_t>(comm), st);
+    if (nr != ncclSuccess) return Status{TPTC_ERR_NCCL, nccl_msg("ncclAllGather", nr)};
     return {};
 }
 

@@ -19,8 +19,11 @@ struct Tp {
     Status allreduce_add(float* part, float* x, size_t n, cudaStream_t st);
     // Sum-allreduce in place.
     Status allreduce(float* buf, size_t n, cudaStream_t st);
-    // Peer-memory reduction of the decode step's row-parallel projections (gemv.cuh TpLink).
-    Status init_p2p(int dim, int n_layers, const int* step, cudaStream_t st);
+    // In-place all-gather: rank r's `count` floats at buf + r * count, every rank's after.
+    Status allgather(float* buf, size_t count, cudaStream_t st);
+    // Peer-memory reduction of the decode step's row-parallel projections and the argmax
+    // exchange (gemv.cuh TpLink); wait_polls 0 keeps the library's default wait bound.
+    Status init_p2p(int dim, int n_layers, const int* step, uint32_t wait_polls, cudaStream_t st);
     void* p2p_mem = nullptr;                 // own inbox
     void* peer_base[kTpMaxRanks] = {};       // peers' allocations mapped here
     TpLink* link_dev = nullptr;              // device copy the kernels read

@@ -105,6 +105,11 @@ class CudaEngine:
         self.tokenizer = tokenizer
         self._info: Optional[ModelInfo] = None
 
+    def set_tp_wait_polls(self, polls: int) -> None:
+        """Tensor parallelism: reads of a peer's word before a decode step gives up on a rank
+        that does not arrive (TPTC_ERR_TIMEOUT); 0 = the library default.  Before load."""
+        self._check(lib().tptc_set_tp_wait_polls(self._ctx, int(polls)))
+
     def set_prefill_gemm_min(self, min_tokens: int) -> None:
         """Prompts of at least min_tokens run the batched tensor-core prefill (fp16 KV only);
         shorter ones, or all when min_tokens <= 0, go token by token (exact decode numerics)."""

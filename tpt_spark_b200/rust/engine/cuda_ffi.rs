@@ -114,6 +114,7 @@ extern "C" {
     pub fn tptc_set_kv_dtype(ctx: *mut tptc_ctx, ggml_type: c_int) -> c_int;
     pub fn tptc_set_prefill_gemm_min(ctx: *mut tptc_ctx, min_tokens: c_int) -> c_int;
     pub fn tptc_set_prefill_fused(ctx: *mut tptc_ctx, mode: c_int) -> c_int;
+    pub fn tptc_set_tp_wait_polls(ctx: *mut tptc_ctx, polls: u32) -> c_int;
     pub fn tptc_load_gguf(ctx: *mut tptc_ctx, path: *const c_char, progress: Option<tptc_progress_cb>,
                           user: *mut c_void) -> c_int;
     pub fn tptc_unload(ctx: *mut tptc_ctx) -> c_int;
