@@ -38,6 +38,7 @@ ATTN_SHAPES = [
     (200, 37, 4, 1, 64, 512),     # ragged chunk after a cached prefix, G = 4
     (1, 100, 8, 8, 96, 128),      # a single query row (MHA, hd 96: the C4 layout)
     (130, 0, 8, 8, 96, 256),      # ragged tiles from position 0
+    (300, 700, 32, 32, 96, 1024),  # hd 96 after a long prefix: last head's padding out of bounds
     (512, 1000, 32, 8, 128, 2048),  # long prefix: 24 key tiles per query tile
 ]
 

@@ -258,14 +258,21 @@ __device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, int* e
 // Issue order per key tile j: P V_A(j), S_A(j + 1), P V_B(j), S_B(j + 1); every commit
 // also covers the MMAs issued before it, so when a tile's S(j) lands its P V(j - 1) -- and so
 // its O and its P buffer -- is complete.
-template <int HD>
+// HD is the head dimension, HP the width of the shared-memory and TMEM layout (a multiple of
+// 64).  For HD = 96 the kernel runs the 128-wide layout: the second 64-column TMA box of a
+// K or V row reaches past the tensor's 96 columns and the copy fills those columns with
+// zeros; the Q box of a head then also covers the next head's first 32 values, which meet
+// those zero keys (S is unchanged), P V leaves the padded output columns at zero, and only
+// the HD real columns are written.
+template <int HD, int HP>
 __global__ void __launch_bounds__(tc::kThreads, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                            const __grid_constant__ CUtensorMap tv, const __grid_constant__ AttnPrefillParams p) {
-    using L = tc::Lay<HD>;
+    static_assert(HP % 64 == 0 && HD <= HP && HD % 32 == 0, "layout width");
+    using L = tc::Lay<HP>;
     using tc::BM;
     using tc::BN;
-    constexpr int NC = HD / 64;  // 64-column blocks of a row
+    constexpr int NC = HP / 64;  // 64-column blocks of a (padded) row
     constexpr int S = tc::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -335,7 +342,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            const uint32_t id_s = mma_idesc(BM, BN), id_o = mma_idesc(BM, HD) | kIdescBMajorMN;
+            const uint32_t id_s = mma_idesc(BM, BN), id_o = mma_idesc(BM, HP) | kIdescBMajorMN;
             auto issue_s = [&](int t, int j) {
                 const uint32_t qa = smem_u32(smem + L::kQ + t * L::kQBytes);
                 const uint32_t ka = smem_u32(smem + L::kK + (j % S) * L::kKVBytes);
@@ -505,10 +512,13 @@ size_t attn_prefill_smem() {
 
 cudaError_t attn_prefill_init_device() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<64, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   tc::Lay<64>::kBytes + 1024)))
         return e;
-    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<96, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  tc::Lay<128>::kBytes + 1024)))
+        return e;
+    if ((e = cudaFuncSetAttribute(attn_prefill_tc_kernel<128, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   tc::Lay<128>::kBytes + 1024)))
         return e;
     if ((e = cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -523,7 +533,7 @@ cudaError_t attn_prefill_init_device() {
 
 namespace {
 
-template <int HD>
+template <int HD, int HP>
 cudaError_t launch_tc(const AttnPrefillParams& p, cudaStream_t st, bool pdl) {
     CUtensorMap tq, tk, tv;
     cudaError_t e = make_tmap_f16(&tq, p.q, p.T, (int64_t)p.n_heads * HD, (int64_t)p.n_heads * HD, tc::BM);
@@ -533,14 +543,14 @@ cudaError_t launch_tc(const AttnPrefillParams& p, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.T + 2 * tc::BM - 1) / (2 * tc::BM), p.n_heads);
     cfg.blockDim = dim3(tc::kThreads);
-    cfg.dynamicSmemBytes = tc::Lay<HD>::kBytes + 1024;
+    cfg.dynamicSmemBytes = tc::Lay<HP>::kBytes + 1024;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attn_prefill_tc_kernel<HD>, tq, tk, tv, p);
+    return cudaLaunchKernelEx(&cfg, attn_prefill_tc_kernel<HD, HP>, tq, tk, tv, p);
 }
 
 }  // namespace
@@ -551,8 +561,9 @@ cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, boo
     const uintptr_t align = reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.kcache) |
                             reinterpret_cast<uintptr_t>(p.vcache);
     if (use_tc && (align & 15) == 0) {
-        if (p.hd == 64) return launch_tc<64>(p, st, pdl);
-        if (p.hd == 128) return launch_tc<128>(p, st, pdl);
+        if (p.hd == 64) return launch_tc<64, 64>(p, st, pdl);
+        if (p.hd == 96) return launch_tc<96, 128>(p, st, pdl);
+        if (p.hd == 128) return launch_tc<128, 128>(p, st, pdl);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.T + BQ - 1) / BQ, p.n_heads);

@@ -54,8 +54,8 @@ struct AttnPrefillParams {
     float scale;           // 1/sqrt(hd)
     int* err;              // optional: bounded waits that give up set TPTC_ERR_TIMEOUT here
 };
-// head_dim 64 and 128 run on tcgen05 (attn_prefill_tc_kernel), 96 on mma.sync; `use_tc` = 0
-// forces the mma.sync kernel (kernel-level comparisons).
+// head_dim 64, 96 and 128 run on tcgen05 (attn_prefill_tc_kernel; 96 in the 128-wide layout
+// with zero-filled padding); `use_tc` = 0 forces the mma.sync kernel (kernel-level comparisons).
 cudaError_t launch_attn_prefill(const AttnPrefillParams& p, cudaStream_t st, bool pdl, int use_tc = 1);
 cudaError_t attn_prefill_init_device();
 
