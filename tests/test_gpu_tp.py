@@ -7,7 +7,8 @@ quantised activation code by one; logits are compared teacher-forced within the 
 2e-2.  The lm_head is vocab-parallel: every rank computes its rows, the greedy pick is
 exchanged over peer memory (checked against the argmax of the gathered logits, ties to the
 highest index), and the full logits are an all-gather.  A rank that stops taking steps makes
-the other's next step fail with TPTC_ERR_TIMEOUT within the wait bound, and both recover.
+the other's next step fail with TPTC_ERR_TIMEOUT within the wait bound (and its own late step
+too), and both recover.
 Skipped with fewer than 2 GPUs.
 """
 import time
@@ -125,51 +126,66 @@ def test_tp2_matches_single_gpu(tiny_models):
 def _stall_rank(rank, uid, path, q, ev_stalled, ev_release, barrier):
     """Both ranks decode two steps; rank 1 then skips the third and waits (its context and
     inboxes stay alive, no kernel of it in flight).  Rank 0's third step must fail with
-    TPTC_ERR_TIMEOUT within the bound.  Rank 1 then takes its third step (it finds rank 0's
-    rows of that step in its inbox), both step counters agree again, and a fresh prompt on
-    both ranks gives the logits of a first run.  The wait bound must exceed the skew between
-    the two host processes in a step taken together (they meet at a barrier before each
-    phase)."""
+    TPTC_ERR_TIMEOUT within the bound.  Rank 0 does not stop at the wait that gave up: it runs
+    the rest of the step (every later wait gives up within 256 reads), so its layer-1 rows
+    overwrite its layer-0 rows in rank 1's inbox.  Rank 1's late third step therefore fails
+    with TPTC_ERR_TIMEOUT too -- it never consumes a word of another step, because every
+    word carries its (step, use) epoch -- and both step counters agree again.  A fresh prompt
+    on both ranks then gives the logits of the first run.  The wait bound must exceed the skew
+    between the two host processes in a step taken together (they meet at a barrier before
+    each phase).  Errors are reported before the engine is destroyed: destroying an NCCL
+    communicator waits for the peer's."""
     from tpt_spark_b200.engine import CudaEngine, EngineError
+
+    def step_code(e, tok, pos):
+        t0 = time.perf_counter()
+        try:
+            e.decode(tok, pos, want_logits=False)
+            code = 0
+        except EngineError as ex:
+            code = ex.code
+        return code, time.perf_counter() - t0
 
     try:
         with CudaEngine(rank, tp_rank=rank, tp_size=2, nccl_uid=uid, kv_dtype="f16") as e:
-            e.set_tp_wait_polls(WAIT_POLLS)
-            e.load(path)
-            e.set_prefill_gemm_min(0)
-            barrier.wait(120)
-            first = e.prefill(PROMPT)
-            pos = len(PROMPT)
-            ref = []
-            for t in (5, 6):
-                ref.append(e.decode(t, pos)[0])
-                pos += 1
-            out = {}
-            if rank == 1:
-                ev_stalled.wait(120)  # rank 0 has timed out
-                e.decode(7, pos, want_logits=False)  # catch up: the same step counter again
-                ev_release.set()
-            else:
-                t0 = time.perf_counter()
-                try:
-                    e.decode(7, pos, want_logits=False)
-                    out["code"] = 0
-                except EngineError as ex:
-                    out["code"] = ex.code
-                out["seconds"] = time.perf_counter() - t0
-                ev_stalled.set()
-                ev_release.wait(120)
-            # recovery: both ranks start over on the same prompt
-            barrier.wait(120)
-            e.kv_reset()
-            again = e.prefill(PROMPT)
-            pos = len(PROMPT)
-            redo = []
-            for t in (5, 6):
-                redo.append(e.decode(t, pos)[0])
-                pos += 1
-            out["same"] = bool(np.array_equal(again, first) and all(np.array_equal(a, b) for a, b in zip(redo, ref)))
-            q.put((rank, "ok", out))
+            try:
+                e.set_tp_wait_polls(WAIT_POLLS)
+                e.load(path)
+                e.set_prefill_gemm_min(0)
+                barrier.wait(120)
+                first = e.prefill(PROMPT)
+                pos = len(PROMPT)
+                ref = []
+                for t in (5, 6):
+                    ref.append(e.decode(t, pos)[0])
+                    pos += 1
+                out = {}
+                if rank == 1:
+                    if not ev_stalled.wait(120):
+                        raise RuntimeError("rank 0 did not report its stalled step")
+                    out["code"], out["seconds"] = step_code(e, 7, pos)  # the same step counter again
+                    ev_release.set()
+                else:
+                    out["code"], out["seconds"] = step_code(e, 7, pos)
+                    ev_stalled.set()
+                    if not ev_release.wait(120):
+                        raise RuntimeError("rank 1 did not take its late step")
+                # recovery: both ranks start over on the same prompt
+                barrier.wait(120)
+                e.kv_reset()
+                again = e.prefill(PROMPT)
+                pos = len(PROMPT)
+                redo = []
+                for t in (5, 6):
+                    redo.append(e.decode(t, pos)[0])
+                    pos += 1
+                out["same"] = bool(
+                    np.array_equal(again, first) and all(np.array_equal(a, b) for a, b in zip(redo, ref))
+                )
+                q.put((rank, "ok", out))
+            except Exception as ex:
+                q.put((rank, "error", repr(ex)))
+                barrier.abort()  # the other rank stops waiting at its next barrier
     except Exception as ex:
         q.put((rank, "error", repr(ex)))
 
@@ -183,8 +199,9 @@ def test_tp2_stalled_rank_times_out_and_recovers(tiny_models, monkeypatch):
     uid = nccl_unique_id()
     path = tiny_models["tiny_tp_q4km"]
     got = _spawn(_stall_rank, lambda r: (r, uid, path))
-    r0 = got[0][1]
-    print(f"rank 0's step without rank 1: code {r0['code']} after {r0['seconds']:.3f} s")
-    assert r0["code"] == TIMEOUT
-    assert r0["seconds"] < 10
+    r0, r1 = got[0][1], got[1][1]
+    print(f"rank 0's step without rank 1: code {r0['code']} after {r0['seconds']:.3f} s; "
+          f"rank 1's late step: code {r1['code']} after {r1['seconds']:.3f} s")
+    assert r0["code"] == TIMEOUT and r1["code"] == TIMEOUT
+    assert r0["seconds"] < 10 and r1["seconds"] < 10
     assert got[0][1]["same"] and got[1][1]["same"]
