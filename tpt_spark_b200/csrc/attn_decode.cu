@@ -27,6 +27,7 @@
 
 #include "act.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace tptc {
 
@@ -164,6 +165,141 @@ __device__ __forceinline__ void attn_store_act(const AttnDecodeParams& p, const 
         for (int i = 0; i < 8; i++) v[i] = ob[w * 256 + 8 * lane + i];
         act_store_block(p.act, p.act_transposed, p.act_nb, p.act_out, kvh * nblk + w, v, lane);
     }
+}
+
+// The CTA's end, shared by both decode kernels: the warp states [kWarps][G][rec] are in
+// shared memory (written after a barrier that ended all use of the ring).  Merges them in
+// warp order into the CTA's (M, L, A); with one split writes the output, else the split
+// record, and the last CTA of the kv head (atomic ticket) merges the splits in split order
+// and writes the output (and the next GEMV's activation).
+template <int GM, int HD>
+__device__ __forceinline__ void attn_finish(const AttnDecodeParams& p, uint8_t* smem, float* qs, int ring_bytes,
+                                            const SplitRange& sr, int kvh, int split, int G, uint64_t* mfull_p,
+                                            int* is_last_p) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rec = attn_rec(HD);
+    const float* wst = reinterpret_cast<const float*>(smem);
+    uint64_t& mfull = *mfull_p;
+    int& is_last = *is_last_p;
+    // merge the warps in warp order: the CTA's (M, L, A)
+    const int S = sr.S;
+    float* part = p.partial + ((int64_t)kvh * p.splits + split) * G * rec;
+    for (int idx = tid; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, d = idx % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < kWarps; w++) M = fmaxf(M, wst[(w * G + g) * rec]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f, A = 0.f;
+        for (int w = 0; w < kWarps; w++) {
+            const float* ws = wst + (w * G + g) * rec;
+            const float e = ex2(ws[0] - Mu);
+            L = fmaf(ws[1], e, L);
+            A = fmaf(ws[4 + d], e, A);
+        }
+        if (S == 1) {
+            p.out[(kvh * G + g) * HD + d] = A / L;
+            qs[idx] = A / L;  // q is in registers by now: the buffer stages the outputs
+        } else {
+            part[g * rec + 4 + d] = A;
+            if (d == 0) {
+                part[g * rec] = M;
+                part[g * rec + 1] = L;
+            }
+        }
+    }
+    if (S == 1) {
+        if (p.act_out) {
+            __syncthreads();
+            attn_store_act(p, qs, kvh, G, HD);
+        }
+        return;
+    }
+    __threadfence();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(&p.counters[kvh], 1) == S - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    // merge the splits in split order.  The (m, l) of every (split, head) come in with plain
+    // loads; warp g turns them into weights 2^(m_s - M) and the sum of l; the accumulators
+    // come into shared memory by 1-D bulk copies of as many whole split records as fit.
+    const float* base = p.partial + (int64_t)kvh * p.splits * G * rec;
+    const int stage_bytes = ring_bytes - attn_weight_bytes(G);
+    float* stage = reinterpret_cast<float*>(smem);
+    float* wgt = reinterpret_cast<float*>(smem + stage_bytes);  // [G][kMaxSplits]
+    float* lsum = wgt + G * kMaxSplits;                         // [G]
+    const int Sc = max(1, stage_bytes / (G * rec * 4));          // splits per copy
+    if (tid == 0) {
+        const int n0 = min(Sc, S);
+        fence_proxy_async_smem();  // the warp states were read there
+        mbar_expect_tx(&mfull, (uint32_t)(n0 * G * rec * 4));
+        bulk_g2s(stage, base, (uint32_t)(n0 * G * rec * 4), &mfull, 0);
+    }
+    if (warp < G) {
+        const int g = warp;
+        float ms[2], ls2[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int sp = lane + 32 * k;
+            ms[k] = sp < S ? __ldcg(base + (sp * G + g) * rec) : -INFINITY;
+            ls2[k] = sp < S ? __ldcg(base + (sp * G + g) * rec + 1) : 0.f;
+        }
+        const float M = warp_max(fmaxf(ms[0], ms[1]));
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f;
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int sp = lane + 32 * k;
+            const float w = ex2(ms[k] - Mu);
+            if (sp < S) wgt[g * kMaxSplits + sp] = w;
+            L = fmaf(ls2[k], w, L);
+        }
+        L = warp_sum(L);
+        if (lane == 0) lsum[g] = L;
+    }
+    __syncthreads();
+    constexpr int kOut = (GM * HD + kThreads - 1) / kThreads;  // outputs idx = tid + k * kThreads
+    float O[kOut];
+#pragma unroll
+    for (int k = 0; k < kOut; k++) O[k] = 0.f;
+    bool mok = true;
+    for (int c0 = 0, ci = 0; c0 < S; c0 += Sc, ci++) {
+        const int n0 = min(Sc, S - c0);
+        if (!mbar_wait_bounded(&mfull, ci & 1, p.err)) mok = false;
+        if (__syncthreads_or(!mok)) return;
+#pragma unroll
+        for (int k = 0; k < kOut; k++) {
+            const int idx = tid + k * kThreads;
+            if (idx < G * HD) {
+                const int g = idx / HD, d = idx % HD;
+                for (int sp = 0; sp < n0; sp++)
+                    O[k] = fmaf(stage[(sp * G + g) * rec + 4 + d], wgt[g * kMaxSplits + c0 + sp], O[k]);
+            }
+        }
+        __syncthreads();  // staging consumed
+        if (tid == 0 && c0 + Sc < S) {
+            const int n1 = min(Sc, S - c0 - Sc);
+            fence_proxy_async_smem();
+            mbar_expect_tx(&mfull, (uint32_t)(n1 * G * rec * 4));
+            bulk_g2s(stage, base + (int64_t)(c0 + Sc) * G * rec, (uint32_t)(n1 * G * rec * 4), &mfull, 0);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kOut; k++) {
+        const int idx = tid + k * kThreads;
+        if (idx < G * HD) {
+            const float o = O[k] / lsum[idx / HD];
+            p.out[(kvh * G + idx / HD) * HD + idx % HD] = o;
+            qs[idx] = o;
+        }
+    }
+    if (p.act_out) {
+        __syncthreads();
+        attn_store_act(p, qs, kvh, G, HD);
+    }
+    if (tid == 0) p.counters[kvh] = 0;
 }
 
 // N2: float2 pairs of the head dimension per lane (hd = 32 * N2); GM: most query heads per
@@ -407,125 +543,332 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     }
     __syncthreads();
 
-    // merge the warps in warp order: the CTA's (M, L, A)
-    const int S = sr.S;
-    float* part = p.partial + ((int64_t)kvh * p.splits + split) * G * rec;
-    for (int idx = tid; idx < G * HD; idx += kThreads) {
-        const int g = idx / HD, d = idx % HD;
-        float M = -INFINITY;
-        for (int w = 0; w < kWarps; w++) M = fmaxf(M, wst[(w * G + g) * rec]);
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, A = 0.f;
-        for (int w = 0; w < kWarps; w++) {
-            const float* ws = wst + (w * G + g) * rec;
-            const float e = ex2(ws[0] - Mu);
-            L = fmaf(ws[1], e, L);
-            A = fmaf(ws[4 + d], e, A);
+    attn_finish<GM, HD>(p, smem, qs, ring_bytes, sr, kvh, split, G, &mfull, &is_last);
+}
+
+// ---------------------------------------------------------------------------------------
+// Tensor-core variant for the fp16 cache.  Same split, ring, position ownership and merge as
+// attn_decode_kernel; the products run on mma.sync (m16n8k16, fp16 in, f32 accumulate) with
+// the keys as the M dimension:
+//   S^T[key][head] = K[key][:] . Q^T[:][head]     (A = K rows by ldmatrix, B = Q^T in registers)
+//   O^T[dim][head] += V^T[dim][key] . P^T[key][head]   (A = V^T by ldmatrix.trans, B = P^T)
+// so the n = 8 columns hold up to 8 query heads of the group.  Each stage is a K and a V tile
+// of 64 positions brought by 2-D TMA with 128-byte swizzle (64-column boxes; for head_dim 96
+// the second box's last 32 columns are zero-filled and never read).  Warps 0-3 take the even
+// tiles and warps 4-7 the odd ones, 16 positions each.  Q and P enter the tensor core as a
+// high and a low fp16 part (x = hi + lo to about 22 bits), so scores and weights keep f32
+// precision against the fp16 keys and values.  Softmax is base 2 with a lazily moved
+// reference maximum per head: it moves (and O^T and l are rescaled) only when a score
+// exceeds it by more than 8, so the weights stay below 256.
+namespace tcd {
+constexpr int kKeys = 64;         // positions per stage
+constexpr int kBox = 64 * 128;    // one TMA box: 64 rows x 64 fp16 columns (128 B), swizzled
+}  // namespace tcd
+
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+// (x0, x1) as a high and a low fp16 pair: hi = fp16(x), lo = fp16(x - hi)
+__device__ __forceinline__ void split_half2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 f = __half22float2(h);
+    hi = half2_bits(h);
+    lo = half2_bits(__floats2half2_rn(x0 - f.x, x1 - f.y));
+}
+// Byte offset of (row, column) in a tile of 64-column boxes with 128-byte swizzle: the
+// 16-byte chunk c of a row sits at chunk c ^ (row % 8).
+__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
+    return (uint32_t)((col >> 6) * tcd::kBox + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+template <int HD, int GM>
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_decode_tc_kernel(const __grid_constant__ AttnDecodeParams p, const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv) {
+    constexpr int NB = (HD + 63) / 64;     // TMA boxes per row
+    constexpr int KC = HD / 16;            // k-chunks of the scores = m-tiles of the output
+    constexpr int kTile = NB * tcd::kBox;  // bytes of one K (or V) tile
+    constexpr int kR = tcd::kKeys;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kMaxStages], mfull;
+    __shared__ int done_warps[kMaxStages];
+    __shared__ int is_last, abort_s;
+
+    const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.n_heads / p.n_kv, S_ring = p.stages;
+    const int ring_bytes = max(S_ring * 2 * kTile, attn_merge_bytes(G, HD));
+    float* qs = reinterpret_cast<float*>(smem + ring_bytes);  // [G][HD]
+
+    if (tid == 0) {
+        for (int s = 0; s < S_ring; s++) {
+            mbar_init(&full[s], 1);
+            done_warps[s] = 0;
         }
-        if (S == 1) {
-            p.out[(kvh * G + g) * HD + d] = A / L;
-            qs[idx] = A / L;  // q is in registers by now: the buffer stages the outputs
-        } else {
-            part[g * rec + 4 + d] = A;
-            if (d == 0) {
-                part[g * rec] = M;
-                part[g * rec + 1] = L;
-            }
-        }
+        mbar_init(&mfull, 1);
+        fence_mbar_init();
+        abort_s = 0;
     }
-    if (S == 1) {
-        if (p.act_out) {
-            __syncthreads();
-            attn_store_act(p, qs, kvh, G, HD);
-        }
+    const int kv_len = *p.pos + 1;
+    if (kv_len < 1 || kv_len > p.max_seq) {  // position outside the cache: flag it, touch nothing
+        if (tid == 0 && kvh == 0 && split == 0 && p.err) atomicExch(p.err, TPTC_ERR_ARG);
         return;
     }
-    __threadfence();
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) is_last = atomicAdd(&p.counters[kvh], 1) == S - 1;
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    // merge the splits in split order.  The (m, l) of every (split, head) come in with plain
-    // loads; warp g turns them into weights 2^(m_s - M) and the sum of l; the accumulators
-    // come into shared memory by 1-D bulk copies of as many whole split records as fit.
-    const float* base = p.partial + (int64_t)kvh * p.splits * G * rec;
-    const int stage_bytes = ring_bytes - attn_weight_bytes(G);
-    float* stage = reinterpret_cast<float*>(smem);
-    float* wgt = reinterpret_cast<float*>(smem + stage_bytes);  // [G][kMaxSplits]
-    float* lsum = wgt + G * kMaxSplits;                         // [G]
-    const int Sc = max(1, stage_bytes / (G * rec * 4));          // splits per copy
-    if (tid == 0) {
-        const int n0 = min(Sc, S);
-        fence_proxy_async_smem();  // the warp states were read there
-        mbar_expect_tx(&mfull, (uint32_t)(n0 * G * rec * 4));
-        bulk_g2s(stage, base, (uint32_t)(n0 * G * rec * 4), &mfull, 0);
-    }
-    if (warp < G) {
-        const int g = warp;
-        float ms[2], ls2[2];
+    const SplitRange sr = split_range(kv_len, p.splits, split);
+    if (split >= sr.S) return;
+    const int t_begin = sr.t_begin, t_end = sr.t_end;
+    const int ntiles = (t_end - t_begin + kR - 1) / kR;
+    const int pos = kv_len - 1, half = HD / 2;
+    const bool owner = pos >= t_begin && pos < t_end;
+    const int tile_pos = owner ? (pos - t_begin) / kR : -1;
+    const int row0 = kvh * p.max_seq + t_begin;  // tensor-map row of the split's first key
+
+    // stage s of tile t: K tile then V tile, NB boxes each; rows past the split (or past the
+    // tensor: zero fill) are masked (K) and zeroed (V) by the warps that own them
+    auto issue = [&](int t) {
+        const int s = t % S_ring;
+        uint8_t* kb = smem + s * 2 * kTile;
+        const uint64_t policy = l2_evict_first_policy();
+        mbar_expect_tx(&full[s], 2 * kTile);
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-            const int sp = lane + 32 * k;
-            ms[k] = sp < S ? __ldcg(base + (sp * G + g) * rec) : -INFINITY;
-            ls2[k] = sp < S ? __ldcg(base + (sp * G + g) * rec + 1) : 0.f;
+        for (int b = 0; b < NB; b++) {
+            tma_load_2d_hint(kb + b * tcd::kBox, &tk, b * 64, row0 + t * kR, &full[s], policy);
+            tma_load_2d_hint(kb + kTile + b * tcd::kBox, &tv, b * 64, row0 + t * kR, &full[s], policy);
         }
-        const float M = warp_max(fmaxf(ms[0], ms[1]));
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f;
-#pragma unroll
-        for (int k = 0; k < 2; k++) {
-            const int sp = lane + 32 * k;
-            const float w = ex2(ms[k] - Mu);
-            if (sp < S) wgt[g * kMaxSplits + sp] = w;
-            L = fmaf(ls2[k], w, L);
+    };
+    constexpr int kPreWait = 1;  // tiles issued before the wait (see attn_decode_kernel)
+    if (tid == 0)
+        for (int t = 0; t < kPreWait && t < S_ring && t < ntiles; t++)
+            if (t != tile_pos) issue(t);
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    // RoPE on the group's queries (candle rope_i), staged in shared memory
+    const float* cs = p.rope_cos + (int64_t)pos * half;
+    const float* sn = p.rope_sin + (int64_t)pos * half;
+    for (int i = tid; i < G * half; i += kThreads) {
+        const int g = i / half, j = i % half;
+        const float* qg = p.q + (int64_t)(kvh * G + g) * HD;
+        const float q0 = qg[2 * j], q1 = qg[2 * j + 1], c = cs[j], s = sn[j];
+        const float r0 = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
+        const float r1 = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
+        qs[g * HD + 2 * j] = r0;
+        qs[g * HD + 2 * j + 1] = r1;
+        if (p.q_out && split == 0) {
+            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j] = r0;
+            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j + 1] = r1;
         }
-        L = warp_sum(L);
-        if (lane == 0) lsum[g] = L;
+    }
+    if (owner) {  // this step's key, rotated, into the cache before any read of its tile
+        __half* krow = static_cast<__half*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * HD;
+        for (int j = tid; j < half; j += kThreads) {
+            const float k0 = p.kraw[kvh * HD + 2 * j], k1 = p.kraw[kvh * HD + 2 * j + 1], c = cs[j], s = sn[j];
+            krow[2 * j] = __float2half_rn(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
+            krow[2 * j + 1] = __float2half_rn(__fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
-    constexpr int kOut = (GM * HD + kThreads - 1) / kThreads;  // outputs idx = tid + k * kThreads
-    float O[kOut];
+    if (tid == 0)
+        for (int t = kPreWait; t < S_ring && t < ntiles; t++)
+            if (t != tile_pos) issue(t);
+    if (tid == 0 && tile_pos >= 0 && tile_pos < S_ring) issue(tile_pos);
+
+    const int g8 = lane >> 2, t4 = lane & 3;       // mma fragment coordinates
+    const int grp = warp >> 2, quarter = warp & 3;  // tile parity and 16-position slice
+    // Q^T as the B operand (k = head dimension, n = query head g8), high and low parts
+    uint32_t qh[KC][2], ql[KC][2];
 #pragma unroll
-    for (int k = 0; k < kOut; k++) O[k] = 0.f;
-    bool mok = true;
-    for (int c0 = 0, ci = 0; c0 < S; c0 += Sc, ci++) {
-        const int n0 = min(Sc, S - c0);
-        if (!mbar_wait_bounded(&mfull, ci & 1, p.err)) mok = false;
-        if (__syncthreads_or(!mok)) return;
+    for (int c = 0; c < KC; c++)
 #pragma unroll
-        for (int k = 0; k < kOut; k++) {
-            const int idx = tid + k * kThreads;
-            if (idx < G * HD) {
-                const int g = idx / HD, d = idx % HD;
-                for (int sp = 0; sp < n0; sp++)
-                    O[k] = fmaf(stage[(sp * G + g) * rec + 4 + d], wgt[g * kMaxSplits + c0 + sp], O[k]);
+        for (int e = 0; e < 2; e++) {
+            const int d = 16 * c + 2 * t4 + 8 * e;
+            const float x0 = g8 < G ? qs[g8 * HD + d] : 0.f, x1 = g8 < G ? qs[g8 * HD + d + 1] : 0.f;
+            split_half2(x0, x1, qh[c][e], ql[c][e]);
+        }
+    // ldmatrix row addresses: K (A of the scores) rows r, r + 8 at columns +0 / +8; V (A of
+    // the output, transposed) rows r / r + 8 at columns +0, +8
+    const int krow = 16 * quarter + (lane & 7) + ((lane >> 3) & 1) * 8, kcol = (lane >> 4) * 8;
+    const int vrow = 16 * quarter + (lane & 7) + (lane >> 4) * 8, vcol = ((lane >> 3) & 1) * 8;
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float m_ref[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.f, 0.f};  // heads 2 t4, 2 t4 + 1
+    float o[KC][4];
+#pragma unroll
+    for (int i = 0; i < KC; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+    bool ok = true;
+    for (int t = grp; t < ntiles; t += 2) {
+        const int s = t % S_ring, n = min(kR, t_end - t_begin - t * kR);
+        ok = mbar_wait_bounded(&full[s], (t / S_ring) & 1, p.err);
+        if (!ok) break;
+        uint8_t* kt = smem + s * 2 * kTile;
+        const uint32_t kb = smem_u32(kt), vb = kb + kTile;
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < KC; c++) {
+            uint32_t a[4];
+            ldsm_x4(kb + sw128_off(krow, 16 * c + kcol), a);
+            mma_16816(sacc, a, qh[c][0], qh[c][1]);
+            mma_16816(sacc, a, ql[c][0], ql[c][1]);
+        }
+        // scores (log2 units) of positions r and r + 8 for heads 2 t4, 2 t4 + 1
+        const int r = 16 * quarter + g8;
+        float sc[4];
+        sc[0] = r < n ? sacc[0] * sl2 : -INFINITY;
+        sc[1] = r < n ? sacc[1] * sl2 : -INFINITY;
+        sc[2] = r + 8 < n ? sacc[2] * sl2 : -INFINITY;
+        sc[3] = r + 8 < n ? sacc[3] * sl2 : -INFINITY;
+        float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+        if (__any_sync(0xffffffffu, mx0 > m_ref[0] + 8.f || mx1 > m_ref[1] + 8.f)) {
+#pragma unroll
+            for (int sh = 4; sh < 32; sh <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
+            }
+            const float n0 = fmaxf(m_ref[0], mx0), n1 = fmaxf(m_ref[1], mx1);
+            const float a0 = n0 == -INFINITY ? 1.f : ex2(m_ref[0] - n0);
+            const float a1 = n1 == -INFINITY ? 1.f : ex2(m_ref[1] - n1);
+            m_ref[0] = n0;
+            m_ref[1] = n1;
+            l_part[0] *= a0;
+            l_part[1] *= a1;
+#pragma unroll
+            for (int i = 0; i < KC; i++) {
+                o[i][0] *= a0;
+                o[i][2] *= a0;
+                o[i][1] *= a1;
+                o[i][3] *= a1;
             }
         }
-        __syncthreads();  // staging consumed
-        if (tid == 0 && c0 + Sc < S) {
-            const int n1 = min(Sc, S - c0 - Sc);
-            fence_proxy_async_smem();
-            mbar_expect_tx(&mfull, (uint32_t)(n1 * G * rec * 4));
-            bulk_g2s(stage, base + (int64_t)(c0 + Sc) * G * rec, (uint32_t)(n1 * G * rec * 4), &mfull, 0);
+        const float mu0 = m_ref[0] == -INFINITY ? 0.f : m_ref[0];
+        const float mu1 = m_ref[1] == -INFINITY ? 0.f : m_ref[1];
+        const float pw0 = ex2(sc[0] - mu0), pw1 = ex2(sc[1] - mu1), pw2 = ex2(sc[2] - mu0), pw3 = ex2(sc[3] - mu1);
+        l_part[0] += pw0 + pw2;
+        l_part[1] += pw1 + pw3;
+        // P^T (rows: positions r, r + 8; columns: heads) transposed into B fragments
+        uint32_t ph0, pl0, ph1, pl1;
+        split_half2(pw0, pw1, ph0, pl0);
+        split_half2(pw2, pw3, ph1, pl1);
+        const uint32_t bh0 = movmatrix_trans(ph0), bh1 = movmatrix_trans(ph1);
+        const uint32_t bl0 = movmatrix_trans(pl0), bl1 = movmatrix_trans(pl1);
+        if (16 * quarter + 16 > n) {
+            // V rows of this slice past the range may hold anything: zero them (their weight is 0)
+            uint8_t* vt = kt + kTile;
+            for (int idx = lane; idx < 16 * NB * 8; idx += 32) {
+                const int rr = 16 * quarter + idx / (NB * 8), b = (idx / 8) % NB, ch = idx & 7;
+                if (rr >= n) *reinterpret_cast<uint4*>(vt + b * tcd::kBox + rr * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();  // before the stage is refilled by TMA
+            __syncwarp();
         }
-    }
 #pragma unroll
-    for (int k = 0; k < kOut; k++) {
-        const int idx = tid + k * kThreads;
-        if (idx < G * HD) {
-            const float o = O[k] / lsum[idx / HD];
-            p.out[(kvh * G + idx / HD) * HD + idx % HD] = o;
-            qs[idx] = o;
+        for (int i = 0; i < KC; i++) {
+            uint32_t a[4];
+            ldsm_x4_trans(vb + sw128_off(vrow, 16 * i + vcol), a);
+            mma_16816(o[i], a, bh0, bh1);
+            mma_16816(o[i], a, bl0, bl1);
+        }
+        __syncwarp();
+        if (lane == 0) {  // the last of the tile's four warps refills its stage
+            __threadfence_block();
+            if (atomicAdd(&done_warps[s], 1) == 3) {
+                done_warps[s] = 0;
+                __threadfence_block();
+                if (t + S_ring < ntiles) {
+                    fence_proxy_async_smem();
+                    issue(t + S_ring);
+                }
+            }
         }
     }
-    if (p.act_out) {
-        __syncthreads();
-        attn_store_act(p, qs, kvh, G, HD);
+    if (!ok) abort_s = 1;
+#pragma unroll
+    for (int sh = 4; sh < 32; sh <<= 1) {
+        l_part[0] += __shfl_xor_sync(0xffffffffu, l_part[0], sh);
+        l_part[1] += __shfl_xor_sync(0xffffffffu, l_part[1], sh);
     }
-    if (tid == 0) p.counters[kvh] = 0;
+
+    __syncthreads();  // every warp is done with the ring: reuse it for the warp states
+    if (abort_s) return;
+    const int rec = attn_rec(HD);
+    float* wst = reinterpret_cast<float*>(smem);  // [warp][G][rec] = (m, l, -, -, acc[HD])
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int h = 2 * t4 + e;
+        if (h >= G) continue;
+        float* w = wst + (warp * G + h) * rec;
+        if (g8 == 0) {
+            w[0] = m_ref[e];
+            w[1] = l_part[e];
+        }
+#pragma unroll
+        for (int i = 0; i < KC; i++) {
+            w[4 + 16 * i + g8] = o[i][e];
+            w[4 + 16 * i + g8 + 8] = o[i][2 + e];
+        }
+    }
+    __syncthreads();
+    attn_finish<GM, HD>(p, smem, qs, ring_bytes, sr, kvh, split, G, &mfull, &is_last);
+}
+
+int attn_tc_stages(int hd) {
+    const int stage = 2 * ((hd + 63) / 64) * tcd::kBox;
+    return std::max(2, std::min(kMaxStages, kRingBudget / stage));
+}
+
+size_t attn_tc_smem(int n_heads, int n_kv, int hd) {
+    const int G = n_heads / n_kv;
+    const size_t ring = (size_t)attn_tc_stages(hd) * 2 * ((hd + 63) / 64) * tcd::kBox;
+    return 1024 + std::max(ring, (size_t)attn_merge_bytes(G, hd)) + (size_t)G * hd * 4;
+}
+
+using TcKernelFn = void (*)(AttnDecodeParams, CUtensorMap, CUtensorMap);
+
+template <int GM>
+TcKernelFn pick_tc_hd(int hd) {
+    switch (hd) {
+        case 64: return attn_decode_tc_kernel<64, GM>;
+        case 96: return attn_decode_tc_kernel<96, GM>;
+        case 128: return attn_decode_tc_kernel<128, GM>;
+    }
+    return nullptr;
+}
+
+TcKernelFn pick_tc_kernel(int hd, int G) {
+    if (G == 1) return pick_tc_hd<1>(hd);
+    if (G == 2) return pick_tc_hd<2>(hd);
+    return G <= 4 ? pick_tc_hd<4>(hd) : pick_tc_hd<8>(hd);
 }
 
 template <typename KV>
@@ -602,6 +945,15 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p_in, cudaStream_t st, bo
         return cudaErrorInvalidValue;
     AttnDecodeParams p = p_in;
     p.stages = p.kv_f32 ? attn_stages<float>(p.hd) : attn_stages<__half>(p.hd);
+    const bool tc = !p.kv_f32 && ((reinterpret_cast<uintptr_t>(p.kcache) | reinterpret_cast<uintptr_t>(p.vcache)) & 15) == 0;
+    CUtensorMap tk, tv;
+    if (tc) {
+        p.stages = attn_tc_stages(p.hd);
+        const int64_t rows = (int64_t)p.n_kv * p.max_seq;
+        cudaError_t e = make_tmap_f16(&tk, static_cast<const __half*>(p.kcache), rows, p.hd, p.hd, tcd::kKeys);
+        if (e == cudaSuccess) e = make_tmap_f16(&tv, static_cast<const __half*>(p.vcache), rows, p.hd, p.hd, tcd::kKeys);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.n_kv, p.splits);
     cfg.blockDim = dim3(kThreads);
@@ -612,6 +964,10 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p_in, cudaStream_t st, bo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
+    if (tc) {
+        cfg.dynamicSmemBytes = attn_tc_smem(p.n_heads, p.n_kv, p.hd);
+        return cudaLaunchKernelEx(&cfg, pick_tc_kernel(p.hd, p.n_heads / p.n_kv), p, tk, tv);
+    }
     return cudaLaunchKernelEx(&cfg, pick_kernel(p.kv_f32, p.hd, p.n_heads / p.n_kv), p);
 }
 
@@ -623,6 +979,12 @@ cudaError_t attn_init_device() {
                                                      200 * 1024);
                 if (e != cudaSuccess) return e;
             }
+    for (int hd : {64, 96, 128})
+        for (int G : {1, 2, 4, 8}) {
+            cudaError_t e = cudaFuncSetAttribute(pick_tc_kernel(hd, G), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 200 * 1024);
+            if (e != cudaSuccess) return e;
+        }
     return cudaSuccess;
 }
 
