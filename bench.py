@@ -458,11 +458,15 @@ def run_ours(args, dist):
 
     # end to end through the C ABI with host buffers, over the same steps and positions as the
     # timed region: each step copies the token id and position in and the argmax out
+    # (the window past the prompt wraps back to the prompt where run_steps wrapped it)
     eng.kv_truncate(kv_start)
     pos, tok = kv_start, tok_start
     dist.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
+        if pos >= ctx_len:
+            eng.kv_truncate(P)
+            pos = P
         tok = eng.decode(tok, pos, want_logits=False)
         pos += 1
     e2e_s = dist.max(time.perf_counter() - t0)
