@@ -84,6 +84,8 @@ SHAPES = [
     (16, 16, 64, 256, 130),       # MHA, hd 64
     (64, 8, 128, 4096, 3000),     # 8 query heads per kv head
     (16, 8, 64, 2048, 1500),      # 2 query heads per kv head
+    (32, 32, 128, 8192, 7000),    # MHA at a long context: 11 key tiles per split
+    (32, 32, 96, 8192, 8000),     # hd 96, 13 key tiles per split (the ring reused 4 times)
 ]
 
 

@@ -623,6 +623,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t full[kMaxStages], mfull;
     __shared__ int done_warps[kMaxStages];
+    // issued[s]: the tile whose copies stage s holds or is receiving.  A warp group may run a
+    // tile ahead of the other, and the previous use of a stage belongs to the other group
+    // whenever the ring depth is odd; a parity wait cannot tell phase k + 2 from phase k, so
+    // a consumer first sees its tile issued (its stage's previous phase is then complete).
+    __shared__ volatile int issued[kMaxStages];
     __shared__ int is_last, abort_s;
 
     const int kvh = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -634,6 +639,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int s = 0; s < S_ring; s++) {
             mbar_init(&full[s], 1);
             done_warps[s] = 0;
+            issued[s] = -1;
         }
         mbar_init(&mfull, 1);
         fence_mbar_init();
@@ -665,6 +671,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_load_2d_hint(kb + b * tcd::kBox, &tk, b * 64, row0 + t * kR, &full[s], policy);
             tma_load_2d_hint(kb + kTile + b * tcd::kBox, &tv, b * 64, row0 + t * kR, &full[s], policy);
         }
+        __threadfence_block();
+        issued[s] = t;
     };
     constexpr int kPreWait = 1;  // tiles issued before the wait (see attn_decode_kernel)
     if (tid == 0)
@@ -730,6 +738,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = true;
     for (int t = grp; t < ntiles; t += 2) {
         const int s = t % S_ring, n = min(kR, t_end - t_begin - t * kR);
+        ok = false;
+        for (uint32_t i = 0; i < kWaitPolls; ++i)
+            if (issued[s] == t) {
+                ok = true;
+                break;
+            }
+        if (!ok) {
+            if (p.err) atomicExch(p.err, TPTC_ERR_TIMEOUT);
+            break;
+        }
+        __threadfence_block();
         ok = mbar_wait_bounded(&full[s], (t / S_ring) & 1, p.err);
         if (!ok) break;
         uint8_t* kt = smem + s * 2 * kTile;
