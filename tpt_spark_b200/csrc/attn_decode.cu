@@ -129,6 +129,13 @@ __device__ __forceinline__ float reduce_scatter16(float (&v)[GM], int l16) {
     return v[0];
 }
 
+// 16-byte global -> shared copy through L2 only (cp.async.cg), completed by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Record of one (split or warp, head) state: m, l, two pad floats, acc[hd] -- hd + 4 floats,
 // a multiple of 16 bytes, so a run of split records is one bulk copy.
 __host__ __device__ constexpr int attn_rec(int hd) { return hd + 4; }
@@ -174,33 +181,40 @@ __device__ __forceinline__ void attn_store_act(const AttnDecodeParams& p, const 
 // and writes the output (and the next GEMV's activation).
 template <int GM, int HD>
 __device__ __forceinline__ void attn_finish(const AttnDecodeParams& p, uint8_t* smem, float* qs, int ring_bytes,
-                                            const SplitRange& sr, int kvh, int split, int G, uint64_t* mfull_p,
-                                            int* is_last_p) {
+                                            const SplitRange& sr, int kvh, int split, int G, int* is_last_p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rec = attn_rec(HD);
     const float* wst = reinterpret_cast<const float*>(smem);
-    uint64_t& mfull = *mfull_p;
     int& is_last = *is_last_p;
     // merge the warps in warp order: the CTA's (M, L, A)
     const int S = sr.S;
     float* part = p.partial + ((int64_t)kvh * p.splits + split) * G * rec;
-    for (int idx = tid; idx < G * HD; idx += kThreads) {
-        const int g = idx / HD, d = idx % HD;
+    // thread c handles columns 4c .. 4c + 3 of the group's heads (float4 loads)
+    for (int c = tid; c < G * HD / 4; c += kThreads) {
+        const int g = 4 * c / HD, d = 4 * c % HD;
         float M = -INFINITY;
+#pragma unroll
         for (int w = 0; w < kWarps; w++) M = fmaxf(M, wst[(w * G + g) * rec]);
         const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, A = 0.f;
+        float L = 0.f;
+        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
         for (int w = 0; w < kWarps; w++) {
             const float* ws = wst + (w * G + g) * rec;
             const float e = ex2(ws[0] - Mu);
+            const float4 v = *reinterpret_cast<const float4*>(ws + 4 + d);
             L = fmaf(ws[1], e, L);
-            A = fmaf(ws[4 + d], e, A);
+            A.x = fmaf(v.x, e, A.x);
+            A.y = fmaf(v.y, e, A.y);
+            A.z = fmaf(v.z, e, A.z);
+            A.w = fmaf(v.w, e, A.w);
         }
         if (S == 1) {
-            p.out[(kvh * G + g) * HD + d] = A / L;
-            qs[idx] = A / L;  // q is in registers by now: the buffer stages the outputs
+            const float4 o = make_float4(A.x / L, A.y / L, A.z / L, A.w / L);
+            *reinterpret_cast<float4*>(p.out + (kvh * G + g) * HD + d) = o;
+            *reinterpret_cast<float4*>(qs + 4 * c) = o;  // q is in registers by now: the buffer stages the outputs
         } else {
-            part[g * rec + 4 + d] = A;
+            *reinterpret_cast<float4*>(part + g * rec + 4 + d) = A;
             if (d == 0) {
                 part[g * rec] = M;
                 part[g * rec + 1] = L;
@@ -214,29 +228,34 @@ __device__ __forceinline__ void attn_finish(const AttnDecodeParams& p, uint8_t* 
         }
         return;
     }
-    __threadfence();
-    asm volatile("fence.proxy.async.global;" ::: "memory");
+    // the split ticket: one thread fences after the barrier, which orders the whole CTA's
+    // record stores before the ticket (the pattern of a grid-wide barrier), and the last CTA
+    // fences again before its threads read the other CTAs' records
     __syncthreads();
-    if (tid == 0) is_last = atomicAdd(&p.counters[kvh], 1) == S - 1;
+    if (tid == 0) {
+        __threadfence();
+        is_last = atomicAdd(&p.counters[kvh], 1) == S - 1;
+        if (is_last) __threadfence();
+    }
     __syncthreads();
     if (!is_last) return;
-    __threadfence();
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    // merge the splits in split order.  The (m, l) of every (split, head) come in with plain
-    // loads; warp g turns them into weights 2^(m_s - M) and the sum of l; the accumulators
-    // come into shared memory by 1-D bulk copies of as many whole split records as fit.
+    // merge the splits in split order.  The split records come into shared memory by 16-byte
+    // cp.async copies from every thread (as many whole records as fit, in chunks), all in
+    // flight together; meanwhile warp g reads the (m, l) of every split of head g with plain
+    // loads and turns them into weights 2^(m_s - M) and the sum of l.
     const float* base = p.partial + (int64_t)kvh * p.splits * G * rec;
     const int stage_bytes = ring_bytes - attn_weight_bytes(G);
     float* stage = reinterpret_cast<float*>(smem);
     float* wgt = reinterpret_cast<float*>(smem + stage_bytes);  // [G][kMaxSplits]
     float* lsum = wgt + G * kMaxSplits;                         // [G]
-    const int Sc = max(1, stage_bytes / (G * rec * 4));          // splits per copy
-    if (tid == 0) {
-        const int n0 = min(Sc, S);
-        fence_proxy_async_smem();  // the warp states were read there
-        mbar_expect_tx(&mfull, (uint32_t)(n0 * G * rec * 4));
-        bulk_g2s(stage, base, (uint32_t)(n0 * G * rec * 4), &mfull, 0);
-    }
+    const int Sc = max(1, stage_bytes / (G * rec * 4));          // splits per chunk
+    auto fetch = [&](int c0) {  // records of splits c0 .. c0 + Sc - 1 into the stage
+        const int n16 = min(Sc, S - c0) * G * rec / 4;
+        const float4* src = reinterpret_cast<const float4*>(base + (int64_t)c0 * G * rec);
+        for (int i = tid; i < n16; i += kThreads) cp_async16(stage + 4 * i, src + i);
+        cp_async_commit();
+    };
+    fetch(0);
     if (warp < G) {
         const int g = warp;
         float ms[2], ls2[2];
@@ -259,41 +278,51 @@ __device__ __forceinline__ void attn_finish(const AttnDecodeParams& p, uint8_t* 
         L = warp_sum(L);
         if (lane == 0) lsum[g] = L;
     }
-    __syncthreads();
-    constexpr int kOut = (GM * HD + kThreads - 1) / kThreads;  // outputs idx = tid + k * kThreads
-    float O[kOut];
-#pragma unroll
-    for (int k = 0; k < kOut; k++) O[k] = 0.f;
-    bool mok = true;
-    for (int c0 = 0, ci = 0; c0 < S; c0 += Sc, ci++) {
+    // thread t sums columns 4c .. 4c + 3 (c = t % NC4) over the splits of partition
+    // t / NC4 (splits sp with sp % NP == partition), float4 loads; the partitions' sums are
+    // then added in partition order
+    const int NC4 = G * HD / 4, NP = max(1, kThreads / NC4);
+    const int c4 = tid % NC4, part_i = tid / NC4;
+    float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < S; c0 += Sc) {
         const int n0 = min(Sc, S - c0);
-        if (!mbar_wait_bounded(&mfull, ci & 1, p.err)) mok = false;
-        if (__syncthreads_or(!mok)) return;
-#pragma unroll
-        for (int k = 0; k < kOut; k++) {
-            const int idx = tid + k * kThreads;
-            if (idx < G * HD) {
-                const int g = idx / HD, d = idx % HD;
-                for (int sp = 0; sp < n0; sp++)
-                    O[k] = fmaf(stage[(sp * G + g) * rec + 4 + d], wgt[g * kMaxSplits + c0 + sp], O[k]);
+        cp_async_wait_all();
+        __syncthreads();  // the chunk (and, the first time, the weights) in shared memory
+        if (part_i < NP) {
+            const int g = 4 * c4 / HD, d = 4 * c4 % HD;
+            const float* wv = wgt + g * kMaxSplits + c0;
+            for (int sp = part_i; sp < n0; sp += NP) {
+                const float4 v = *reinterpret_cast<const float4*>(stage + (sp * G + g) * rec + 4 + d);
+                const float w = wv[sp];
+                acc4.x = fmaf(v.x, w, acc4.x);
+                acc4.y = fmaf(v.y, w, acc4.y);
+                acc4.z = fmaf(v.z, w, acc4.z);
+                acc4.w = fmaf(v.w, w, acc4.w);
             }
         }
-        __syncthreads();  // staging consumed
-        if (tid == 0 && c0 + Sc < S) {
-            const int n1 = min(Sc, S - c0 - Sc);
-            fence_proxy_async_smem();
-            mbar_expect_tx(&mfull, (uint32_t)(n1 * G * rec * 4));
-            bulk_g2s(stage, base + (int64_t)(c0 + Sc) * G * rec, (uint32_t)(n1 * G * rec * 4), &mfull, 0);
+        if (c0 + Sc < S) {
+            __syncthreads();  // staging consumed
+            fetch(c0 + Sc);
         }
     }
-#pragma unroll
-    for (int k = 0; k < kOut; k++) {
-        const int idx = tid + k * kThreads;
-        if (idx < G * HD) {
-            const float o = O[k] / lsum[idx / HD];
-            p.out[(kvh * G + idx / HD) * HD + idx % HD] = o;
-            qs[idx] = o;
+    __syncthreads();  // the stage is free: it takes the partitions' sums
+    float4* psum = reinterpret_cast<float4*>(stage);  // [NP][NC4]
+    if (part_i < NP) psum[part_i * NC4 + c4] = acc4;
+    __syncthreads();
+    for (int c = tid; c < NC4; c += kThreads) {
+        float4 o = psum[c];
+        for (int q = 1; q < NP; q++) {
+            const float4 v = psum[q * NC4 + c];
+            o.x += v.x;
+            o.y += v.y;
+            o.z += v.z;
+            o.w += v.w;
         }
+        const int g = 4 * c / HD, d = 4 * c % HD;
+        const float il = 1.f / lsum[g];
+        o = make_float4(o.x * il, o.y * il, o.z * il, o.w * il);
+        *reinterpret_cast<float4*>(p.out + (kvh * G + g) * HD + d) = o;
+        *reinterpret_cast<float4*>(qs + 4 * c) = o;
     }
     if (p.act_out) {
         __syncthreads();
@@ -314,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     constexpr int HD = 16 * DPL;
     constexpr int kStageElems = kR * HD;  // K (or V) elements per stage
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full[kMaxStages], mfull;
+    __shared__ uint64_t full[kMaxStages];
     __shared__ int done_warps[kMaxStages];
     __shared__ int is_last, abort_s;
 
@@ -329,7 +358,6 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
             mbar_init(&full[s], 1);
             done_warps[s] = 0;
         }
-        mbar_init(&mfull, 1);
         fence_mbar_init();
         abort_s = 0;
     }
@@ -543,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     }
     __syncthreads();
 
-    attn_finish<GM, HD>(p, smem, qs, ring_bytes, sr, kvh, split, G, &mfull, &is_last);
+    attn_finish<GM, HD>(p, smem, qs, ring_bytes, sr, kvh, split, G, &is_last);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -621,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     constexpr int kR = tcd::kKeys;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[kMaxStages], mfull;
+    __shared__ uint64_t full[kMaxStages];
     __shared__ int done_warps[kMaxStages];
     // issued[s]: the tile whose copies stage s holds or is receiving.  A warp group may run a
     // tile ahead of the other, and the previous use of a stage belongs to the other group
@@ -641,7 +669,6 @@ __global__ void __launch_bounds__(kThreads, 2)
             done_warps[s] = 0;
             issued[s] = -1;
         }
-        mbar_init(&mfull, 1);
         fence_mbar_init();
         abort_s = 0;
     }
@@ -858,7 +885,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
     }
     __syncthreads();
-    attn_finish<GM, HD>(p, smem, qs, ring_bytes, sr, kvh, split, G, &mfull, &is_last);
+    attn_finish<GM, HD>(p, smem, qs, ring_bytes, sr, kvh, split, G, &is_last);
 }
 
 int attn_tc_stages(int hd) {
@@ -930,8 +957,10 @@ KernelFn pick_kernel(int kv_f32, int hd, int G) {
 }  // namespace
 
 int attn_decode_splits(int n_kv, int max_seq, int sm_count) {
-    // two CTAs per SM over all kv heads at long context
-    const int s = std::max(1, (2 * sm_count + n_kv - 1) / n_kv);
+    // about 1.4 CTAs per SM over all kv heads at long context: at C5 (8 kv heads, 8K keys)
+    // 26 splits stream the keys as fast as 37 (two per SM) and halve the split merge that the
+    // last CTA of each kv head runs alone (measured per kernel with globaltimer stamps)
+    const int s = std::max(1, (7 * sm_count + 5 * n_kv - 1) / (5 * n_kv));
     const int max_useful = std::max(1, (max_seq + kMinPerSplit - 1) / kMinPerSplit);
     return std::min(kMaxSplits, std::min(s, max_useful));
 }
