@@ -228,14 +228,15 @@ __device__ __forceinline__ void attn_finish(const AttnDecodeParams& p, uint8_t* 
         }
         return;
     }
-    // the split ticket: one thread fences after the barrier, which orders the whole CTA's
-    // record stores before the ticket (the pattern of a grid-wide barrier), and the last CTA
-    // fences again before its threads read the other CTAs' records
+    // the split ticket: after the barrier one thread takes it with an acquire-release atomic.
+    // Its release orders the whole CTA's record stores before the ticket (they precede it
+    // through the barrier); in the last CTA its acquire orders every other CTA's records
+    // before the reads that follow the next barrier.
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        is_last = atomicAdd(&p.counters[kvh], 1) == S - 1;
-        if (is_last) __threadfence();
+        int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(p.counters + kvh) : "memory");
+        is_last = prev == S - 1;
     }
     __syncthreads();
     if (!is_last) return;
@@ -625,6 +626,13 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 1-D bulk copy global -> shared without a cache hint; 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 // (x0, x1) as a high and a low fp16 pair: hi = fp16(x), lo = fp16(x - hi)
 __device__ __forceinline__ void split_half2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
@@ -649,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     constexpr int kR = tcd::kKeys;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[kMaxStages];
+    __shared__ uint64_t full[kMaxStages], qbar;
     __shared__ int done_warps[kMaxStages];
     // issued[s]: the tile whose copies stage s holds or is receiving.  A warp group may run a
     // tile ahead of the other, and the previous use of a stage belongs to the other group
@@ -662,6 +670,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int G = p.n_heads / p.n_kv, S_ring = p.stages;
     const int ring_bytes = max(S_ring * 2 * kTile, attn_merge_bytes(G, HD));
     float* qs = reinterpret_cast<float*>(smem + ring_bytes);  // [G][HD]
+    float* csn = qs + G * HD;                                 // cos | sin of position pos
+    float* kr = csn + HD;                                     // the new key before RoPE
 
     if (tid == 0) {
         for (int s = 0; s < S_ring; s++) {
@@ -669,6 +679,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             done_warps[s] = 0;
             issued[s] = -1;
         }
+        mbar_init(&qbar, 1);
         fence_mbar_init();
         abort_s = 0;
     }
@@ -709,13 +720,23 @@ __global__ void __launch_bounds__(kThreads, 2)
     pdl_wait();
     pdl_launch_dependents();
 
-    // RoPE on the group's queries (candle rope_i), staged in shared memory
-    const float* cs = p.rope_cos + (int64_t)pos * half;
-    const float* sn = p.rope_sin + (int64_t)pos * half;
-    for (int i = tid; i < G * half; i += kThreads) {
+    // The group's queries, the RoPE row of `pos` and (owner) the new key come in by bulk
+    // copies issued ahead of the ring's other first tiles: plain loads queued behind a burst of
+    // tile copies took several microseconds.
+    if (tid == 0) {
+        mbar_expect_tx(&qbar, (uint32_t)((G * HD + HD + (owner ? HD : 0)) * 4));
+        bulk_g2s_nohint(qs, p.q + (int64_t)kvh * G * HD, (uint32_t)(G * HD * 4), &qbar);
+        bulk_g2s_nohint(csn, p.rope_cos + (int64_t)pos * half, (uint32_t)(half * 4), &qbar);
+        bulk_g2s_nohint(csn + half, p.rope_sin + (int64_t)pos * half, (uint32_t)(half * 4), &qbar);
+        if (owner) bulk_g2s_nohint(kr, p.kraw + (int64_t)kvh * HD, (uint32_t)(HD * 4), &qbar);
+        for (int t = kPreWait; t < S_ring && t < ntiles; t++)
+            if (t != tile_pos) issue(t);
+    }
+    bool ok = mbar_wait_bounded(&qbar, 0, p.err);
+    // RoPE on the group's queries (candle rope_i), in place
+    for (int i = tid; i < G * half && ok; i += kThreads) {
         const int g = i / half, j = i % half;
-        const float* qg = p.q + (int64_t)(kvh * G + g) * HD;
-        const float q0 = qg[2 * j], q1 = qg[2 * j + 1], c = cs[j], s = sn[j];
+        const float q0 = qs[g * HD + 2 * j], q1 = qs[g * HD + 2 * j + 1], c = csn[j], s = csn[half + j];
         const float r0 = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
         const float r1 = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
         qs[g * HD + 2 * j] = r0;
@@ -725,20 +746,17 @@ __global__ void __launch_bounds__(kThreads, 2)
             p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j + 1] = r1;
         }
     }
-    if (owner) {  // this step's key, rotated, into the cache before any read of its tile
+    if (owner && ok) {  // this step's key, rotated, into the cache before any read of its tile
         __half* krow = static_cast<__half*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * HD;
         for (int j = tid; j < half; j += kThreads) {
-            const float k0 = p.kraw[kvh * HD + 2 * j], k1 = p.kraw[kvh * HD + 2 * j + 1], c = cs[j], s = sn[j];
+            const float k0 = kr[2 * j], k1 = kr[2 * j + 1], c = csn[j], s = csn[half + j];
             krow[2 * j] = __float2half_rn(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
             krow[2 * j + 1] = __float2half_rn(__fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
-    if (tid == 0)
-        for (int t = kPreWait; t < S_ring && t < ntiles; t++)
-            if (t != tile_pos) issue(t);
-    if (tid == 0 && tile_pos >= 0 && tile_pos < S_ring) issue(tile_pos);
+    if (tid == 0 && ok && tile_pos >= 0 && tile_pos < S_ring) issue(tile_pos);
 
     const int g8 = lane >> 2, t4 = lane & 3;       // mma fragment coordinates
     const int grp = warp >> 2, quarter = warp & 3;  // tile parity and 16-position slice
@@ -762,8 +780,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int i = 0; i < KC; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-    bool ok = true;
-    for (int t = grp; t < ntiles; t += 2) {
+    for (int t = grp; t < ntiles && ok; t += 2) {
         const int s = t % S_ring, n = min(kR, t_end - t_begin - t * kR);
         ok = false;
         for (uint32_t i = 0; i < kWaitPolls; ++i)
@@ -896,7 +913,7 @@ int attn_tc_stages(int hd) {
 size_t attn_tc_smem(int n_heads, int n_kv, int hd) {
     const int G = n_heads / n_kv;
     const size_t ring = (size_t)attn_tc_stages(hd) * 2 * ((hd + 63) / 64) * tcd::kBox;
-    return 1024 + std::max(ring, (size_t)attn_merge_bytes(G, hd)) + (size_t)G * hd * 4;
+    return 1024 + std::max(ring, (size_t)attn_merge_bytes(G, hd)) + (size_t)(G + 2) * hd * 4;
 }
 
 using TcKernelFn = void (*)(AttnDecodeParams, CUtensorMap, CUtensorMap);
@@ -993,7 +1010,12 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p_in, cudaStream_t st, bo
         return cudaErrorInvalidValue;
     AttnDecodeParams p = p_in;
     p.stages = p.kv_f32 ? attn_stages<float>(p.hd) : attn_stages<__half>(p.hd);
-    const bool tc = !p.kv_f32 && ((reinterpret_cast<uintptr_t>(p.kcache) | reinterpret_cast<uintptr_t>(p.vcache)) & 15) == 0;
+    // the tensor-core kernel reads the caches by TMA and q, the RoPE rows and the new key by
+    // bulk copies: all 16-byte aligned
+    const uintptr_t align = reinterpret_cast<uintptr_t>(p.kcache) | reinterpret_cast<uintptr_t>(p.vcache) |
+                            reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.kraw) |
+                            reinterpret_cast<uintptr_t>(p.rope_cos) | reinterpret_cast<uintptr_t>(p.rope_sin);
+    const bool tc = !p.kv_f32 && (align & 15) == 0;
     CUtensorMap tk, tv;
     if (tc) {
         p.stages = attn_tc_stages(p.hd);
