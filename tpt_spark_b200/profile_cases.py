@@ -5,6 +5,7 @@ launches the kernel a few times through the library's public entry points and ex
     python -m tpt_spark_b200.profile_cases gemm 1024 28672 4096  # fp16 GEMM, M N K
     python -m tpt_spark_b200.profile_cases gemm_q 2048 14336 4096  # fused-dequant GEMM (Q4_K), M N K
     python -m tpt_spark_b200.profile_cases attn_prefill 4096     # causal prefill attention, T
+    python -m tpt_spark_b200.profile_cases attn_decode 8192      # decode attention (C5 heads), position
     python -m tpt_spark_b200.profile_cases prefill 2048          # C5 batched prefill, prompt tokens
 
 The launch counts are what the summaries under profiles/ select with ncu's -s / -c.
@@ -88,6 +89,33 @@ def attn_prefill(T: int) -> None:
     print("ok", float(o[0, 0]))
 
 
+def attn_decode(pos: int) -> None:
+    """tptc_attn_decode five times at position `pos` (keys 0..pos): 32 query heads over 8 kv
+    heads of 128, fp16 caches of 9216 positions, one of five separate cache pairs per launch
+    (188 MB together, more than L2): the fifth launch reads its keys and values cold."""
+    import torch
+
+    from . import kernels
+
+    H, KV, hd, S = 32, 8, 128, 9216
+    half = hd // 2
+    theta = 500000.0 ** (-torch.arange(half, dtype=torch.float64) * 2 / hd)
+    ang = torch.arange(S, dtype=torch.float64)[:, None] * theta[None, :]
+    cs, sn = ang.cos().float().cuda(), ang.sin().float().cuda()
+    caches = [(torch.randn(KV, S, hd, device="cuda").half(), torch.randn(KV, S, hd, device="cuda").half())
+              for _ in range(5)]
+    q = torch.randn(H * hd, device="cuda")
+    kraw = torch.randn(KV * hd, device="cuda")
+    d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    out = torch.empty(H * hd, device="cuda")
+    nbytes = kernels.attn_decode_workspace_bytes(H, KV, hd, S)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    for kc, vc in caches:
+        kernels.attn_decode(q, kraw, kc, vc, kernels.F16, cs, sn, d_pos, H, KV, hd, S, out, ws, nbytes)
+    torch.cuda.synchronize()
+    print("ok", float(out.abs().sum()))
+
+
 def prefill(P: int) -> None:
     """The C5 model (the bench's synthetic GGUF in synth.default_model_dir(), written on first
     use): one warm-up prefill of P random token ids, then the same prefill bracketed by
@@ -113,7 +141,8 @@ def prefill(P: int) -> None:
     print("prefill ms", e.last_device_ms())
 
 
-CASES = {"gemv": gemv, "gemm": gemm, "gemm_q": gemm_q, "attn_prefill": attn_prefill, "prefill": prefill}
+CASES = {"gemv": gemv, "gemm": gemm, "gemm_q": gemm_q, "attn_prefill": attn_prefill, "attn_decode": attn_decode,
+         "prefill": prefill}
 
 
 def main(argv=None) -> int:
