@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """bench.py -- tpt-spark hot path on B200: batch-1 decode tok/s and prefill tok/s at the
-Llama-3-8B-shape Q4_K_M configuration ("C5"), plus the Q4_K GEMV
-HBM GB/s of configs[0] ("C1").
+Llama-3-8B-shape Q4_K_M configuration (the benchmark configuration "C5"), plus the Q4_K GEMV
+HBM GB/s of configuration "C1" (one 4096x4096 matvec).
 
 One JSON line on rank 0.  A "step" is one decode token (one forward pass of the whole model
 at batch 1).  Inputs: a seeded random-init model of the C5 shape written as a GGUF file

@@ -2,7 +2,7 @@
 
 The default engine is the benchmarked one: fp16 KV cache, batched tensor-core prefill for
 prompts of 16 tokens or more, fused-dequant GEMM on "auto".  Each case runs the full model of
-one configuration (BASELINE configs C2-C5: 16-32 layers, vocab 32k-128k, head_dim 64/96/128,
+one benchmark configuration (C2-C5: 16-32 layers, vocab 32k-128k, head_dim 64/96/128,
 RoPE base 500000 or 10000) against the CPU oracle (the restated candle quantized_llama path of
 src-tauri/src/engine/candle_engine.rs:217-324) on the same seeded GGUF.
 

@@ -159,7 +159,7 @@ def test_gemv_repeatable(cuda_device):
     assert torch.equal(y1, y2)
 
 
-# Every matrix shape of the benchmark configurations (BASELINE configs C2-C5), out x in:
+# Every matrix shape of the benchmark configurations C2-C5, out x in:
 # q/o, k, v, gate (= up), down and the output projection of each.
 CONFIG_MATRICES = {
     "c2": [(O.Q4_K, 2048, 2048), (O.Q4_K, 512, 2048), (O.Q6_K, 512, 2048), (O.Q4_K, 8192, 2048),
