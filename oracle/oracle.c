@@ -12,14 +12,18 @@
  * vec_dot / QMatMul).  candle is pinned in src-tauri/Cargo.lock:316-356 but is not
  * vendored, and no Rust toolchain exists here, so the reference cannot be built.  This
  * file restates candle 0.8.4's published algorithm:
- *   - GGUF block formats Q4_K (144 B / 256), Q6_K (210 B / 256), Q8_0 (34 B / 32), F16;
- *     dequantisation follows the formulas and the evaluation order of gguf-py 0.19
- *     (gguf/quants.py Q8_0 :378-401, Q4_K :475-522, Q6_K :552-572), which the golden
- *     tests pin bit-for-bit;
+ *   - GGUF block formats Q4_K (144 B / 256), Q6_K (210 B / 256), Q8_0 (34 B / 32), F16, and
+ *     Q4_0 (18 B / 32), Q4_1 (20 B / 32), Q5_0 (22 B / 32), Q5_1 (24 B / 32), Q2_K (84 B / 256),
+ *     Q3_K (110 B / 256), Q5_K (176 B / 256); dequantisation follows the formulas and the
+ *     evaluation order of gguf-py 0.19 (gguf/quants.py Q4_0 :241-251, Q4_1 :276-288, Q5_0
+ *     :314-330, Q5_1 :357-375, Q8_0 :378-401, Q2_K :406-428, Q3_K :433-472, Q4_K :475-522,
+ *     Q5_K :527-549, Q6_K :552-572), which the golden tests pin bit-for-bit;
  *   - activation quantisation for the integer dot: Q8_K (BlockQ8K::from_float) for
  *     Q4_K / Q6_K weights, Q8_0 (BlockQ8_0::from_float) for Q8_0 weights; F16 weights
  *     are dequantised to f32 and multiplied in f32 (QMatMul::from_arc);
- *   - vec_dot_q4k_q8k / q6k_q8k / q8_0_q8_0 in candle's scalar accumulation order;
+ *   - vec_dot_q4k_q8k / q5k_q8k / q6k_q8k / q4_0_q8_0 / q5_0_q8_0 / q8_0_q8_0 in candle's
+ *     scalar accumulation order (Q5_K x Q8_K, Q4_0 x Q8_0 and Q5_0 x Q8_0 are the
+ *     k_quants BlockQ5K / BlockQ4_0 / BlockQ5_0 vec_dot_unopt loops);
  *   - the quantized_llama forward: RmsNorm, interleaved RoPE (rope_i) from an f32
  *     cos/sin table, f32 KV concatenation, causal softmax(QK^T/sqrt(d))V, SwiGLU MLP,
  *     residual adds, final norm and the output projection on the last position only.
@@ -50,8 +54,18 @@
 #define Q4K_BYTES 144
 #define Q6K_BYTES 210
 #define Q80_BYTES 34
+#define Q40_BYTES 18
+#define Q41_BYTES 20
+#define Q50_BYTES 22
+#define Q51_BYTES 24
+#define Q2K_BYTES 84
+#define Q3K_BYTES 110
+#define Q5K_BYTES 176
 
-enum { OR_F32 = 0, OR_F16 = 1, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q6_K = 14 };
+enum {
+    OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q5_0 = 6, OR_Q5_1 = 7, OR_Q8_0 = 8,
+    OR_Q2_K = 10, OR_Q3_K = 11, OR_Q4_K = 12, OR_Q5_K = 13, OR_Q6_K = 14
+};
 
 /* block_q8_K layout: f32 d, int8 qs[256], int16 bsums[16] = 292 bytes. */
 typedef struct {
@@ -193,7 +207,133 @@ void or_dequant_f16(const uint16_t* x, int64_t n, float* y) {
     for (int64_t i = 0; i < n; i++) y[i] = or_h2f(x[i]);
 }
 
-int64_t or_type_block_elems(int type) { return type == OR_Q8_0 ? 32 : (type == OR_F16 || type == OR_F32) ? 1 : 256; }
+/* Q5_0 / Q5_1 high bit of element l (0..31) of a block: bit l of the little-endian qh. */
+static inline int q5_hbit(const uint8_t* qh, int l) { return (qh[l >> 3] >> (l & 7)) & 1; }
+
+/* gguf/quants.py Q4_0.dequantize_blocks :241-251: d*(q-8); element l < 16 is the low
+ * nibble of qs[l], element l + 16 its high nibble. */
+void or_dequant_q40(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q40_BYTES;
+        float d = or_h2f(rd16(blk));
+        for (int l = 0; l < 16; l++) {
+            y[b * 32 + l] = d * (float)((blk[2 + l] & 0x0f) - 8);
+            y[b * 32 + 16 + l] = d * (float)((blk[2 + l] >> 4) - 8);
+        }
+    }
+}
+
+/* gguf/quants.py Q4_1.dequantize_blocks :276-288: (d*q) + m. */
+void or_dequant_q41(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q41_BYTES;
+        float d = or_h2f(rd16(blk)), m = or_h2f(rd16(blk + 2));
+        for (int l = 0; l < 16; l++) {
+            y[b * 32 + l] = d * (float)(blk[4 + l] & 0x0f) + m;
+            y[b * 32 + 16 + l] = d * (float)(blk[4 + l] >> 4) + m;
+        }
+    }
+}
+
+/* gguf/quants.py Q5_0.dequantize_blocks :314-330: d*(q-16), q = nibble | hbit << 4. */
+void or_dequant_q50(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q50_BYTES;
+        float d = or_h2f(rd16(blk));
+        const uint8_t* qh = blk + 2;
+        const uint8_t* qs = blk + 6;
+        for (int l = 0; l < 16; l++) {
+            y[b * 32 + l] = d * (float)(((qs[l] & 0x0f) | (q5_hbit(qh, l) << 4)) - 16);
+            y[b * 32 + 16 + l] = d * (float)(((qs[l] >> 4) | (q5_hbit(qh, l + 16) << 4)) - 16);
+        }
+    }
+}
+
+/* gguf/quants.py Q5_1.dequantize_blocks :357-375: (d*q) + m. */
+void or_dequant_q51(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q51_BYTES;
+        float d = or_h2f(rd16(blk)), m = or_h2f(rd16(blk + 2));
+        const uint8_t* qh = blk + 4;
+        const uint8_t* qs = blk + 8;
+        for (int l = 0; l < 16; l++) {
+            y[b * 32 + l] = d * (float)((qs[l] & 0x0f) | (q5_hbit(qh, l) << 4)) + m;
+            y[b * 32 + 16 + l] = d * (float)((qs[l] >> 4) | (q5_hbit(qh, l + 16) << 4)) + m;
+        }
+    }
+}
+
+/* gguf/quants.py Q2_K.dequantize_blocks :406-428 (scales[16] qs[64] d dmin): element
+ * 128h + 32s + l = (qs[32h + l] >> 2s) & 3, group e/16: (d*(sc & 15))*q - (dmin*(sc >> 4)). */
+void or_dequant_q2k(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q2K_BYTES;
+        float d = or_h2f(rd16(blk + 80)), dmin = or_h2f(rd16(blk + 82));
+        for (int e = 0; e < QK_K; e++) {
+            const int h = e >> 7, sh = (e >> 5) & 3, l = e & 31, g = e >> 4;
+            const int q = (blk[16 + 32 * h + l] >> (2 * sh)) & 3;
+            const float dl = d * (float)(blk[g] & 0x0f), ml = dmin * (float)(blk[g] >> 4);
+            y[b * QK_K + e] = dl * (float)q - ml;
+        }
+    }
+}
+
+/* Q3_K 6-bit scale k (0..15), minus 32: low 4 bits from scales[k % 8] (nibble k / 8), high
+ * 2 bits from scales[8 + k % 4] (bits 2 (k / 4)). */
+static inline int q3k_scale(const uint8_t* sc, int k) {
+    const int lo = (sc[k & 7] >> (4 * (k >> 3))) & 0x0f;
+    const int hi = (sc[8 + (k & 3)] >> (2 * (k >> 2))) & 0x03;
+    return (lo | (hi << 4)) - 32;
+}
+
+/* gguf/quants.py Q3_K.dequantize_blocks :433-472 (hmask[32] qs[64] scales[12] d): element
+ * e = 128h + 32s + l: q = ((qs[32h + l] >> 2s) & 3) - 4 * (1 - ((hmask[l] >> (e / 32)) & 1)),
+ * value (d*scale(e / 16))*q. */
+void or_dequant_q3k(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q3K_BYTES;
+        float d = or_h2f(rd16(blk + 108));
+        for (int e = 0; e < QK_K; e++) {
+            const int h = e >> 7, sh = (e >> 5) & 3, l = e & 31;
+            const int ql = (blk[32 + 32 * h + l] >> (2 * sh)) & 3;
+            const int hb = (blk[l] >> (e >> 5)) & 1;
+            const int q = ql - ((hb ^ 1) << 2);
+            const float dl = d * (float)q3k_scale(blk + 96, e >> 4);
+            y[b * QK_K + e] = dl * (float)q;
+        }
+    }
+}
+
+/* Q5_K element value q (0..31) for element e of a block (d dmin scales[12] qh[32] qs[128]). */
+static inline int q5k_val(const uint8_t* blk, int e) {
+    const int g = e >> 6, j = e >> 5, l = e & 31;
+    const uint8_t b = blk[48 + 32 * g + l];
+    const int lo = (j & 1) ? (b >> 4) : (b & 0x0f);
+    return lo | (((blk[16 + l] >> j) & 1) << 4);
+}
+
+/* gguf/quants.py Q5_K.dequantize_blocks :527-549: (d*sc)*q - (dmin*m). */
+void or_dequant_q5k(const uint8_t* blocks, int64_t nb, float* y) {
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * Q5K_BYTES;
+        float d = or_h2f(rd16(blk)), dmin = or_h2f(rd16(blk + 2));
+        uint8_t sc[8], mn[8];
+        q4k_scale_min(blk + 4, sc, mn);
+        for (int e = 0; e < QK_K; e++) {
+            const int j = e >> 5;
+            const float dl = d * (float)sc[j], ml = dmin * (float)mn[j];
+            y[b * QK_K + e] = dl * (float)q5k_val(blk, e) - ml;
+        }
+    }
+}
+
+int64_t or_type_block_elems(int type) {
+    switch (type) {
+    case OR_F32: case OR_F16: return 1;
+    case OR_Q4_0: case OR_Q4_1: case OR_Q5_0: case OR_Q5_1: case OR_Q8_0: return 32;
+    }
+    return 256;
+}
 int64_t or_type_block_bytes(int type) {
     switch (type) {
     case OR_F32: return 4;
@@ -201,6 +341,13 @@ int64_t or_type_block_bytes(int type) {
     case OR_Q8_0: return Q80_BYTES;
     case OR_Q4_K: return Q4K_BYTES;
     case OR_Q6_K: return Q6K_BYTES;
+    case OR_Q4_0: return Q40_BYTES;
+    case OR_Q4_1: return Q41_BYTES;
+    case OR_Q5_0: return Q50_BYTES;
+    case OR_Q5_1: return Q51_BYTES;
+    case OR_Q2_K: return Q2K_BYTES;
+    case OR_Q3_K: return Q3K_BYTES;
+    case OR_Q5_K: return Q5K_BYTES;
     }
     return 0;
 }
@@ -213,6 +360,13 @@ int or_dequant(int type, const void* src, int64_t n, float* y) {
     case OR_Q8_0: or_dequant_q80((const uint8_t*)src, n / 32, y); return 0;
     case OR_Q4_K: or_dequant_q4k((const uint8_t*)src, n / 256, y); return 0;
     case OR_Q6_K: or_dequant_q6k((const uint8_t*)src, n / 256, y); return 0;
+    case OR_Q4_0: or_dequant_q40((const uint8_t*)src, n / 32, y); return 0;
+    case OR_Q4_1: or_dequant_q41((const uint8_t*)src, n / 32, y); return 0;
+    case OR_Q5_0: or_dequant_q50((const uint8_t*)src, n / 32, y); return 0;
+    case OR_Q5_1: or_dequant_q51((const uint8_t*)src, n / 32, y); return 0;
+    case OR_Q2_K: or_dequant_q2k((const uint8_t*)src, n / 256, y); return 0;
+    case OR_Q3_K: or_dequant_q3k((const uint8_t*)src, n / 256, y); return 0;
+    case OR_Q5_K: or_dequant_q5k((const uint8_t*)src, n / 256, y); return 0;
     }
     return -1;
 }
@@ -313,6 +467,41 @@ static inline int32_t q6k_block_int(const uint8_t* blk, const or_q8k* y) {
     return is;
 }
 
+/* Per super-block integer sums of Q5_K x Q8_K (as Q4_K with 5-bit q). */
+static inline void q5k_block_ints(const uint8_t* blk, const or_q8k* y, int32_t* isum, int32_t* msum) {
+    uint8_t sc[8], mn[8];
+    q4k_scale_min(blk + 4, sc, mn);
+    int32_t is = 0, ms = 0;
+    for (int j = 0; j < 8; j++) {
+        int32_t s = 0;
+        for (int l = 0; l < 32; l++) s += (int32_t)q5k_val(blk, 32 * j + l) * y->qs[32 * j + l];
+        is += (int32_t)sc[j] * s;
+    }
+    for (int j = 0; j < 16; j++) ms += (int32_t)y->bsums[j] * mn[j / 2];
+    *isum = is;
+    *msum = ms;
+}
+
+/* candle BlockQ4_0::vec_dot_unopt block sum: sum_j (lo_j - 8) y_j + (hi_j - 8) y_{j+16}. */
+static inline int32_t q40_block_int(const uint8_t* blk, const uint8_t* xb) {
+    const int8_t* y = (const int8_t*)(xb + 2);
+    int32_t s = 0;
+    for (int j = 0; j < 16; j++) s += ((blk[2 + j] & 0x0f) - 8) * y[j] + ((blk[2 + j] >> 4) - 8) * y[j + 16];
+    return s;
+}
+
+/* candle BlockQ5_0::vec_dot_unopt block sum, q = nibble | hbit << 4, minus 16. */
+static inline int32_t q50_block_int(const uint8_t* blk, const uint8_t* xb) {
+    const int8_t* y = (const int8_t*)(xb + 2);
+    const uint8_t* qh = blk + 2;
+    const uint8_t* qs = blk + 6;
+    int32_t s = 0;
+    for (int j = 0; j < 16; j++)
+        s += (((qs[j] & 0x0f) | (q5_hbit(qh, j) << 4)) - 16) * y[j] +
+             (((qs[j] >> 4) | (q5_hbit(qh, j + 16) << 4)) - 16) * y[j + 16];
+    return s;
+}
+
 static inline int32_t q80_block_int(const uint8_t* blk, const uint8_t* xb) {
     const int8_t* a = (const int8_t*)(blk + 2);
     const int8_t* b = (const int8_t*)(xb + 2);
@@ -322,7 +511,8 @@ static inline int32_t q80_block_int(const uint8_t* blk, const uint8_t* xb) {
 }
 
 /* Exported per-block integer sums for one weight row (test hook). msum may be NULL for
- * formats without mins.  xq: or_q8k[] for Q4_K/Q6_K, 34-byte Q8_0 blocks for Q8_0. */
+ * formats without mins.  xq: or_q8k[] for Q4_K/Q5_K/Q6_K, 34-byte Q8_0 blocks for
+ * Q8_0/Q4_0/Q5_0. */
 int or_block_dots(int type, const void* wrow, const void* xq, int nb, int32_t* isum, int32_t* msum) {
     const uint8_t* w = (const uint8_t*)wrow;
     for (int b = 0; b < nb; b++) {
@@ -335,6 +525,16 @@ int or_block_dots(int type, const void* wrow, const void* xq, int nb, int32_t* i
             if (msum) msum[b] = 0;
         } else if (type == OR_Q8_0) {
             isum[b] = q80_block_int(w + (size_t)b * Q80_BYTES, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
+            if (msum) msum[b] = 0;
+        } else if (type == OR_Q5_K) {
+            int32_t m;
+            q5k_block_ints(w + (size_t)b * Q5K_BYTES, (const or_q8k*)xq + b, isum + b, &m);
+            if (msum) msum[b] = m;
+        } else if (type == OR_Q4_0) {
+            isum[b] = q40_block_int(w + (size_t)b * Q40_BYTES, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
+            if (msum) msum[b] = 0;
+        } else if (type == OR_Q5_0) {
+            isum[b] = q50_block_int(w + (size_t)b * Q50_BYTES, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
             if (msum) msum[b] = 0;
         } else {
             return -1;
@@ -519,6 +719,49 @@ static float vec_dot_q80(int n, const uint8_t* w, const uint8_t* xq) {
     return sumf;
 }
 
+/* candle BlockQ5K::vec_dot_unopt: Q4_K's order with q = nibble + 16 * hbit. */
+static float vec_dot_q5k(int n, const uint8_t* w, const or_q8k* y) {
+    float sums[8] = {0}, sumf = 0.f;
+    for (int b = 0; b < n / QK_K; b++) {
+        const uint8_t* blk = w + (size_t)b * Q5K_BYTES;
+        uint8_t sc[8], mn[8];
+        q4k_scale_min(blk + 4, sc, mn);
+        int8_t a[QK_K];
+        for (int e = 0; e < QK_K; e++) a[e] = (int8_t)q5k_val(blk, e);
+        int32_t sumi = 0;
+        for (int j = 0; j < 16; j++) sumi += (int32_t)y[b].bsums[j] * mn[j / 2];
+        int32_t aux32[8] = {0};
+        int idx = 0;
+        for (int s = 0; s < 8; s++) {
+            int32_t scale = sc[s];
+            for (int k4 = 0; k4 < 4; k4++) {
+                for (int l = 0; l < 8; l++) aux32[l] += scale * (int32_t)((int16_t)y[b].qs[idx + l] * (int16_t)a[idx + l]);
+                idx += 8;
+            }
+        }
+        float d = or_h2f(rd16(blk)) * y[b].d;
+        for (int l = 0; l < 8; l++) sums[l] += d * (float)aux32[l];
+        float dmin = or_h2f(rd16(blk + 2)) * y[b].d;
+        sumf -= dmin * (float)sumi;
+    }
+    float s = 0.f;
+    for (int l = 0; l < 8; l++) s += sums[l];
+    return sumf + s;
+}
+
+/* candle BlockQ4_0 / BlockQ5_0 ::vec_dot_unopt: sumf += (float)sumi * d_w * d_x per block. */
+static float vec_dot_q40_q50(int type, int n, const uint8_t* w, const uint8_t* xq) {
+    const size_t bb = type == OR_Q4_0 ? Q40_BYTES : Q50_BYTES;
+    float sumf = 0.f;
+    for (int b = 0; b < n / QK8_0; b++) {
+        const uint8_t* blk = w + (size_t)b * bb;
+        const uint8_t* xb = xq + (size_t)b * Q80_BYTES;
+        int32_t si = type == OR_Q4_0 ? q40_block_int(blk, xb) : q50_block_int(blk, xb);
+        sumf += (float)si * or_h2f(rd16(blk)) * or_h2f(rd16(xb));
+    }
+    return sumf;
+}
+
 static float vec_dot_f32(int n, const float* a, const float* b) {
     float s = 0.f;
     for (int i = 0; i < n; i++) s += a[i] * b[i];
@@ -531,31 +774,36 @@ static float vec_dot_f32(int n, const float* a, const float* b) {
  * quantised to the weight's vec-dot type, then one vec_dot per output element.  F16
  * weights are dequantised to f32 first (QMatMul::from_arc dequantises F16/F32). */
 int or_matmul(int type, const void* W, int N, int K, const float* x, int m, float* y) {
-    if (type == OR_Q4_K || type == OR_Q6_K) {
+    if (type == OR_Q4_K || type == OR_Q5_K || type == OR_Q6_K) {
         if (K % QK_K) return -1;
         or_q8k* xq = (or_q8k*)malloc(sizeof(or_q8k) * (size_t)m * (K / QK_K));
         for (int r = 0; r < m; r++) or_quant_q8k(x + (size_t)r * K, K, xq + (size_t)r * (K / QK_K));
-        size_t rowb = (size_t)(K / QK_K) * (type == OR_Q4_K ? Q4K_BYTES : Q6K_BYTES);
+        size_t rowb = (size_t)(K / QK_K) * (size_t)or_type_block_bytes(type);
 #pragma omp parallel for num_threads(g_threads) schedule(static)
         for (int n = 0; n < N; n++) {
             const uint8_t* wr = (const uint8_t*)W + rowb * n;
             for (int r = 0; r < m; r++) {
                 const or_q8k* xr = xq + (size_t)r * (K / QK_K);
-                y[(size_t)r * N + n] = type == OR_Q4_K ? vec_dot_q4k(K, wr, xr) : vec_dot_q6k(K, wr, xr);
+                y[(size_t)r * N + n] = type == OR_Q4_K   ? vec_dot_q4k(K, wr, xr)
+                                       : type == OR_Q5_K ? vec_dot_q5k(K, wr, xr)
+                                                         : vec_dot_q6k(K, wr, xr);
             }
         }
         free(xq);
         return 0;
     }
-    if (type == OR_Q8_0) {
+    if (type == OR_Q8_0 || type == OR_Q4_0 || type == OR_Q5_0) {
         if (K % QK8_0) return -1;
         size_t xrow = (size_t)(K / QK8_0) * Q80_BYTES;
+        size_t wrow = (size_t)(K / QK8_0) * (size_t)or_type_block_bytes(type);
         uint8_t* xq = (uint8_t*)malloc(xrow * m);
         for (int r = 0; r < m; r++) or_quant_q80(x + (size_t)r * K, K, xq + xrow * r);
 #pragma omp parallel for num_threads(g_threads) schedule(static)
         for (int n = 0; n < N; n++) {
-            const uint8_t* wr = (const uint8_t*)W + xrow * n;
-            for (int r = 0; r < m; r++) y[(size_t)r * N + n] = vec_dot_q80(K, wr, xq + xrow * r);
+            const uint8_t* wr = (const uint8_t*)W + wrow * n;
+            for (int r = 0; r < m; r++)
+                y[(size_t)r * N + n] = type == OR_Q8_0 ? vec_dot_q80(K, wr, xq + xrow * r)
+                                                       : vec_dot_q40_q50(type, K, wr, xq + xrow * r);
         }
         free(xq);
         return 0;

@@ -19,6 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K = 2, 3, 6, 7, 10, 11, 13
 Q8K_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (256,)), ("bsums", "<i2", (16,))])
 assert Q8K_DTYPE.itemsize == 292
 
@@ -127,7 +128,7 @@ def quant_q80(x: np.ndarray) -> np.ndarray:
 
 def quant_for(t: int, x: np.ndarray) -> np.ndarray:
     """Activation quantisation candle applies before the dot with a `t` weight."""
-    return quant_q8k(x) if t in (Q4_K, Q6_K) else quant_q80(x)
+    return quant_q8k(x) if t in (Q4_K, Q5_K, Q6_K) else quant_q80(x)
 
 
 def block_dots(t: int, wrow: np.ndarray, xq: np.ndarray, nb: int):

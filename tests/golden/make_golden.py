@@ -2,7 +2,9 @@
 
 gguf-py 0.19 (the gguf package in this image) implements the GGUF block formats in numpy:
 dequantisation of Q4_K / Q6_K / Q8_0 / F16 (gguf/quants.py :395-401, :505-522, :554-572)
-and quantisation of Q8_0 (:381-393, "bit-exact with ggml-quants.c").  The fixtures store raw
+and of Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q2_K / Q3_K / Q5_K (:241-251, :276-288, :314-330,
+:357-375, :406-428, :433-472, :527-549), and quantisation of Q8_0 (:381-393, "bit-exact with
+ggml-quants.c").  The fixtures store raw
 blocks (random bytes with finite f16 scales, plus hand-made edge blocks) together with
 gguf-py's outputs, so the oracle and the CUDA kernels can be checked against them without
 gguf-py at test time.
@@ -53,6 +55,30 @@ def q80_blocks(rng, nb):
     return b
 
 
+# (name, type, bytes per block, elements per block, byte offsets of f16 scale fields)
+MORE_FORMATS = (
+    ("q40", T.Q4_0, 18, 32, (0,)),
+    ("q41", T.Q4_1, 20, 32, (0, 2)),
+    ("q50", T.Q5_0, 22, 32, (0,)),
+    ("q51", T.Q5_1, 24, 32, (0, 2)),
+    ("q2k", T.Q2_K, 84, 256, (80, 82)),
+    ("q3k", T.Q3_K, 110, 256, (108,)),
+    ("q5k", T.Q5_K, 176, 256, (0, 2)),
+)
+
+
+def more_blocks(rng, nbytes, scale_offs, nb):
+    """Random blocks with finite f16 scales; block 0 all quant bits set, block 1 all clear."""
+    b = rng.integers(0, 256, (nb, nbytes), dtype=np.uint8)
+    keep = np.zeros(nbytes, bool)
+    for o in scale_offs:
+        b[:, o:o + 2] = finite_f16_bytes(rng, nb, -0.1, 0.1)
+        keep[o:o + 2] = True
+    b[0, ~keep] = 0xFF
+    b[1, ~keep] = 0
+    return b
+
+
 def main():
     rng = np.random.default_rng(20261201)
     out = {}
@@ -72,6 +98,13 @@ def main():
     x[96:128] = np.linspace(-127, 127, 32, dtype=np.float32) / 127.0 * 4.0
     out["q80_x"] = x
     out["q80_q"] = Q.quantize(x.reshape(1, -1), T.Q8_0).ravel()
+    # the further formats, from their own generator so that the fixtures above stay as they were
+    rng2 = np.random.default_rng(20261202)
+    for name, qt, nbytes, be, offs in MORE_FORMATS:
+        blocks = more_blocks(rng2, nbytes, offs, 64 if be == 256 else 256)
+        out[f"{name}_raw"] = blocks.ravel()
+        out[f"{name}_f32"] = Q.dequantize(blocks.ravel(), qt).astype(np.float32).ravel()
+        assert out[f"{name}_f32"].size == blocks.shape[0] * be
     np.savez_compressed(os.path.join(HERE, "blocks.npz"), **out)
     print({k: v.shape for k, v in out.items()})
 

@@ -15,7 +15,9 @@ def bits(a):
 
 
 @pytest.mark.parametrize("name,t,be", [("q4k", O.Q4_K, 256), ("q6k", O.Q6_K, 256), ("q80", O.Q8_0, 32),
-                                       ("f16", O.F16, 1)])
+                                       ("f16", O.F16, 1), ("q40", O.Q4_0, 32), ("q41", O.Q4_1, 32),
+                                       ("q50", O.Q5_0, 32), ("q51", O.Q5_1, 32), ("q2k", O.Q2_K, 256),
+                                       ("q3k", O.Q3_K, 256), ("q5k", O.Q5_K, 256)])
 def test_dequant_matches_gguf_py_bitwise(name, t, be):
     ref = GOLD[f"{name}_f32"]
     got = O.dequant(t, GOLD[f"{name}_raw"], ref.size)
@@ -112,6 +114,66 @@ def test_block_dots_equal_integer_math(t):
             ref_i = sum(int(sc[j]) * int((q[32 * j:32 * j + 32] * a[32 * j:32 * j + 32]).sum()) for j in range(8))
             ref_m = sum(int(mn[j // 2]) * int(xq[b]["bsums"][j]) for j in range(16))
             assert isum[b] == ref_i and msum[b] == ref_m
+
+
+def _qvals(t, blk):
+    """The integer quant values of one raw block, restated in numpy from the GGUF layout:
+    Q4_0 / Q5_0 offset-subtracted (32 values), Q5_K unsigned 0..31 (256 values)."""
+    blk = blk.astype(np.int64)
+    if t == O.Q4_0:
+        qs = blk[2:18]
+        return np.concatenate([qs & 0xF, qs >> 4]) - 8
+    if t == O.Q5_0:
+        qh = int(blk[2]) | int(blk[3]) << 8 | int(blk[4]) << 16 | int(blk[5]) << 24
+        qs = blk[6:22]
+        hb = np.array([(qh >> i) & 1 for i in range(32)], np.int64)
+        return np.concatenate([qs & 0xF, qs >> 4]) + 16 * hb - 16
+    qh, qs = blk[16:48], blk[48:176]
+    q = np.zeros(256, np.int64)
+    for g in range(4):
+        q[64 * g:64 * g + 32] = (qs[32 * g:32 * g + 32] & 0xF) | (((qh >> (2 * g)) & 1) << 4)
+        q[64 * g + 32:64 * g + 64] = (qs[32 * g:32 * g + 32] >> 4) | (((qh >> (2 * g + 1)) & 1) << 4)
+    return q
+
+
+@pytest.mark.parametrize("t", [O.Q5_K, O.Q4_0, O.Q5_0])
+def test_block_dots_more_formats(t):
+    """Q5_K x Q8_K and Q4_0 / Q5_0 x Q8_0 per-block integer sums equal numpy integer math."""
+    name, bb, be = {O.Q5_K: ("q5k", 176, 256), O.Q4_0: ("q40", 18, 32), O.Q5_0: ("q50", 22, 32)}[t]
+    nb = 16
+    w = GOLD[f"{name}_raw"][: nb * bb]
+    x = np.random.default_rng(6).standard_normal(nb * be).astype(np.float32)
+    xq = O.quant_for(t, x)
+    isum, msum = O.block_dots(t, w, xq, nb)
+    blk = w.reshape(nb, bb)
+    for b in range(nb):
+        q = _qvals(t, blk[b])
+        if t == O.Q5_K:
+            s = blk[b, 4:16]
+            sc = [s[j] & 63 if j < 4 else (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4) for j in range(8)]
+            mn = [s[j + 4] & 63 if j < 4 else (s[j + 4] >> 4) | ((s[j] >> 6) << 4) for j in range(8)]
+            a = xq[b]["qs"].astype(np.int64)
+            ref_i = sum(int(sc[j]) * int((q[32 * j:32 * j + 32] * a[32 * j:32 * j + 32]).sum()) for j in range(8))
+            ref_m = sum(int(mn[j // 2]) * int(xq[b]["bsums"][j]) for j in range(16))
+            assert isum[b] == ref_i and msum[b] == ref_m
+        else:
+            a = xq.reshape(nb, 34)[b, 2:].view(np.int8).astype(np.int64)
+            assert isum[b] == int((q * a).sum())
+
+
+@pytest.mark.parametrize("t", [O.Q5_K, O.Q4_0, O.Q5_0])
+def test_matmul_more_formats_close_to_f64(t):
+    """QMatMul semantics for the further formats stay within activation-quantisation noise of
+    the f64 product of the dequantised weights (the golden blocks as a weight matrix)."""
+    name, bb, be = {O.Q5_K: ("q5k", 176, 256), O.Q4_0: ("q40", 18, 32), O.Q5_0: ("q50", 22, 32)}[t]
+    raw = GOLD[f"{name}_raw"]
+    K = 1024
+    N = raw.size // bb * be // K
+    wd = O.dequant(t, raw, N * K).reshape(N, K)
+    x = np.random.default_rng(3).standard_normal(K).astype(np.float32)
+    y = O.matmul(t, raw, N, K, x)[0]
+    ref = wd.astype(np.float64) @ x.astype(np.float64)
+    assert np.abs(y - ref).max() <= 0.02 * np.abs(wd).sum(1).max() * np.abs(x).max() / 127 * 4 + 1e-6
 
 
 @pytest.mark.parametrize("t", [O.Q4_K, O.Q6_K, O.Q8_0, O.F16])
