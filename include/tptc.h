@@ -48,8 +48,15 @@ extern "C" {
 /* GGML tensor type ids (GGUF tensor_info.type). */
 #define TPTC_TYPE_F32 0
 #define TPTC_TYPE_F16 1
+#define TPTC_TYPE_Q4_0 2
+#define TPTC_TYPE_Q4_1 3
+#define TPTC_TYPE_Q5_0 6
+#define TPTC_TYPE_Q5_1 7
 #define TPTC_TYPE_Q8_0 8
+#define TPTC_TYPE_Q2_K 10
+#define TPTC_TYPE_Q3_K 11
 #define TPTC_TYPE_Q4_K 12
+#define TPTC_TYPE_Q5_K 13
 #define TPTC_TYPE_Q6_K 14
 
 typedef struct tptc_ctx tptc_ctx;
@@ -204,7 +211,10 @@ TPTC_API int tptc_debug_trace(tptc_ctx* ctx, uint32_t id, int pos, float* trace)
 /* Device pointers owned by the caller.  These expose each hot-path kernel for parity tests
  * and microbenchmarks; the forward pass uses the same kernels. */
 
-/* Dequantise n elements of raw GGUF blocks (dequant_q4k/q6k/q8/f16.wgsl) to f32. */
+/* Dequantise n elements of raw GGUF blocks to f32 (dequant_q4k/q6k/q8/f16.wgsl and the
+ * reference's Q4_0 / Q5_0 / Q5_1 / Q2_K / Q3_K / Q5_K shaders, shaders/dequant_*.wgsl): every
+ * TPTC_TYPE_* above, in gguf-py's layouts and rounding (bit-exact).  n is a multiple of the
+ * type's block (32 or 256 elements). */
 TPTC_API int tptc_dequant(int ggml_type, const void* d_blocks, int64_t n, float* d_out, void* stream);
 /* Q8_K activation blocks (292 B each: f32 d, int8 qs[256], int16 bsums[16]) of x[k]. */
 TPTC_API int tptc_quant_q8k(const float* d_x, int64_t k, void* d_out, void* stream);

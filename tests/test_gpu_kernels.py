@@ -27,7 +27,9 @@ def host(t):
     return t.cpu().numpy()
 
 
-@pytest.mark.parametrize("name,t", [("q4k", O.Q4_K), ("q6k", O.Q6_K), ("q80", O.Q8_0), ("f16", O.F16)])
+@pytest.mark.parametrize("name,t", [("q4k", O.Q4_K), ("q6k", O.Q6_K), ("q80", O.Q8_0), ("f16", O.F16),
+                                    ("q40", O.Q4_0), ("q41", O.Q4_1), ("q50", O.Q5_0), ("q51", O.Q5_1),
+                                    ("q2k", O.Q2_K), ("q3k", O.Q3_K), ("q5k", O.Q5_K)])
 def test_dequant_bitexact_vs_gguf_py(cuda_device, name, t):
     import torch
 

@@ -244,8 +244,13 @@ static bool type_ok(int t) {
 
 TPTC_API int tptc_dequant(int ggml_type, const void* d_blocks, int64_t n, float* d_out, void* stream) {
     if (!d_blocks || !d_out || n < 0) return TPTC_ERR_ARG;
-    const int64_t be = ggml_type == TPTC_TYPE_Q8_0 ? 32 : (ggml_type == TPTC_TYPE_Q4_K || ggml_type == TPTC_TYPE_Q6_K) ? 256 : 1;
-    if (!(type_ok(ggml_type) || ggml_type == TPTC_TYPE_F32) || n % be) return TPTC_ERR_ARG;
+    int64_t be = 0;
+    switch (ggml_type) {
+    case TPTC_TYPE_F32: case TPTC_TYPE_F16: be = 1; break;
+    case TPTC_TYPE_Q4_0: case TPTC_TYPE_Q4_1: case TPTC_TYPE_Q5_0: case TPTC_TYPE_Q5_1: case TPTC_TYPE_Q8_0: be = 32; break;
+    case TPTC_TYPE_Q2_K: case TPTC_TYPE_Q3_K: case TPTC_TYPE_Q4_K: case TPTC_TYPE_Q5_K: case TPTC_TYPE_Q6_K: be = 256; break;
+    }
+    if (be == 0 || n % be) return TPTC_ERR_ARG;
     cudaError_t e = tptc::launch_dequant_raw(ggml_type, d_blocks, n, d_out, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "dequant");
 }

@@ -21,6 +21,13 @@ constexpr int Q4K_BYTES = 144;   // d f16 | dmin f16 | scales[12] | qs[128]
 constexpr int Q6K_BYTES = 210;   // ql[128] | qh[64] | scales[16] int8 | d f16 (GGUF layout)
 constexpr int Q6K_MAIN = 208;    // device layout: ql | qh | scales, d in a separate plane
 constexpr int Q80_BYTES = 34;    // d f16 | qs[32] (GGUF layout); device: qs plane + d plane
+constexpr int Q40_BYTES = 18;    // d f16 | qs[16] (element l < 16: low nibble of qs[l], l + 16: high)
+constexpr int Q41_BYTES = 20;    // d f16 | m f16 | qs[16]
+constexpr int Q50_BYTES = 22;    // d f16 | qh u32 (bit l: 5th bit of element l) | qs[16]
+constexpr int Q51_BYTES = 24;    // d f16 | m f16 | qh u32 | qs[16]
+constexpr int Q2K_BYTES = 84;    // scales[16] (sc | m << 4) | qs[64] (2-bit) | d f16 | dmin f16
+constexpr int Q3K_BYTES = 110;   // hmask[32] | qs[64] (2-bit) | scales[12] (6-bit) | d f16
+constexpr int Q5K_BYTES = 176;   // d f16 | dmin f16 | scales[12] | qh[32] | qs[128]
 
 // block_q8_K: the activation format candle pairs with Q4_K / Q6_K weights (292 bytes).
 struct BlockQ8K {

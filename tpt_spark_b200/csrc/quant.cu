@@ -1,6 +1,6 @@
 // quant.cu -- standalone block kernels: dequantisation of raw GGUF blocks (the reference's
-// dequant_q4k/q6k/q8/f16.wgsl entry points, with the GGUF layout of gguf-py rather than the
-// reference's wrong Q4_K nibble split), activation quantisation to Q8_K / Q8_0, the load-time
+// dequant_q4k/q6k/q8/f16.wgsl entry points and its Q4_0 / Q5_0 / Q5_1 / Q2_K / Q3_K / Q5_K
+// shaders, with the GGUF layouts of gguf-py rather than the reference's wrong nibble splits), activation quantisation to Q8_K / Q8_0, the load-time
 // repack into the device layout, and the dense f16 expansion used by the prefill GEMM.
 #include "kernels.h"
 #include "quant.cuh"
@@ -24,6 +24,20 @@ __global__ void dequant_raw_kernel(int type, const uint8_t* __restrict__ blocks,
         v = __fmul_rn((float)(int8_t)blk[2 + i % QK8_0], h2f(blk[0] | (blk[1] << 8)));
     } else if (type == TPTC_TYPE_F16) {
         v = h2f(reinterpret_cast<const uint16_t*>(blocks)[i]);
+    } else if (type == TPTC_TYPE_Q4_0) {
+        v = q40_elem(blocks + (i / 32) * Q40_BYTES, (int)(i % 32));
+    } else if (type == TPTC_TYPE_Q4_1) {
+        v = q41_elem(blocks + (i / 32) * Q41_BYTES, (int)(i % 32));
+    } else if (type == TPTC_TYPE_Q5_0) {
+        v = q50_elem(blocks + (i / 32) * Q50_BYTES, (int)(i % 32));
+    } else if (type == TPTC_TYPE_Q5_1) {
+        v = q51_elem(blocks + (i / 32) * Q51_BYTES, (int)(i % 32));
+    } else if (type == TPTC_TYPE_Q2_K) {
+        v = q2k_elem(blocks + (i / QK_K) * Q2K_BYTES, (int)(i % QK_K));
+    } else if (type == TPTC_TYPE_Q3_K) {
+        v = q3k_elem(blocks + (i / QK_K) * Q3K_BYTES, (int)(i % QK_K));
+    } else if (type == TPTC_TYPE_Q5_K) {
+        v = q5k_elem(blocks + (i / QK_K) * Q5K_BYTES, (int)(i % QK_K));
     } else {
         v = reinterpret_cast<const float*>(blocks)[i];
     }

@@ -121,6 +121,63 @@ __device__ __forceinline__ float q4k_elem(const uint8_t* blk, int e) {
     return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
 }
 
+// Element e (0..31) of the 32-element formats (gguf-py Q4_0 / Q4_1 / Q5_0 / Q5_1): the
+// 4-bit value is the low nibble of qs[e] for e < 16, the high nibble of qs[e - 16] above;
+// Q5_* add bit e of the little-endian qh word as the 5th bit.  Q4_0: d*(q-8), Q5_0: d*(q-16),
+// Q4_1 / Q5_1: (d*q) + m.
+__device__ __forceinline__ int q4_nibble(const uint8_t* qs, int e) {
+    return e < 16 ? (qs[e] & 0x0f) : (qs[e - 16] >> 4);
+}
+__device__ __forceinline__ int q5_hbit(const uint8_t* qh, int e) { return (qh[e >> 3] >> (e & 7)) & 1; }
+__device__ __forceinline__ float q40_elem(const uint8_t* blk, int e) {
+    return __fmul_rn(h2f(blk[0] | (blk[1] << 8)), (float)(q4_nibble(blk + 2, e) - 8));
+}
+__device__ __forceinline__ float q41_elem(const uint8_t* blk, int e) {
+    return __fadd_rn(__fmul_rn(h2f(blk[0] | (blk[1] << 8)), (float)q4_nibble(blk + 4, e)), h2f(blk[2] | (blk[3] << 8)));
+}
+__device__ __forceinline__ float q50_elem(const uint8_t* blk, int e) {
+    const int q = q4_nibble(blk + 6, e) | (q5_hbit(blk + 2, e) << 4);
+    return __fmul_rn(h2f(blk[0] | (blk[1] << 8)), (float)(q - 16));
+}
+__device__ __forceinline__ float q51_elem(const uint8_t* blk, int e) {
+    const int q = q4_nibble(blk + 8, e) | (q5_hbit(blk + 4, e) << 4);
+    return __fadd_rn(__fmul_rn(h2f(blk[0] | (blk[1] << 8)), (float)q), h2f(blk[2] | (blk[3] << 8)));
+}
+
+// Element e (0..255) of a Q2_K block (gguf-py Q2_K): e = 128h + 32s + l takes bits 2s of
+// qs[32h + l]; the 16-element group e / 16 has scale byte sc | m << 4:
+// (d*sc)*q - (dmin*m).
+__device__ __forceinline__ float q2k_elem(const uint8_t* blk, int e) {
+    const int h = e >> 7, sh = (e >> 5) & 3, l = e & 31, g = e >> 4;
+    const int q = (blk[16 + 32 * h + l] >> (2 * sh)) & 3;
+    const float d = h2f(blk[80] | (blk[81] << 8)), dmin = h2f(blk[82] | (blk[83] << 8));
+    return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)(blk[g] & 0x0f)), (float)q), __fmul_rn(dmin, (float)(blk[g] >> 4)));
+}
+
+// Element e of a Q3_K block (gguf-py Q3_K): 2 low bits as Q2_K, minus 4 where bit e / 32 of
+// hmask[e % 32] is clear; 16-element group scales of 6 bits (low 4 from scales[k % 8], nibble
+// k / 8; high 2 from scales[8 + k % 4], bits 2 (k / 4)) minus 32: (d*scale)*q.
+__device__ __forceinline__ float q3k_elem(const uint8_t* blk, int e) {
+    const int h = e >> 7, sh = (e >> 5) & 3, l = e & 31, k = e >> 4;
+    const int ql = (blk[32 + 32 * h + l] >> (2 * sh)) & 3;
+    const int hb = (blk[l] >> (e >> 5)) & 1;
+    const uint8_t* sc = blk + 96;
+    const int scale = (((sc[k & 7] >> (4 * (k >> 3))) & 0x0f) | (((sc[8 + (k & 3)] >> (2 * (k >> 2))) & 3) << 4)) - 32;
+    return __fmul_rn(__fmul_rn(h2f(blk[108] | (blk[109] << 8)), (float)scale), (float)(ql - ((hb ^ 1) << 2)));
+}
+
+// Element e of a Q5_K block (gguf-py Q5_K): Q4_K's scales and nibbles, plus bit e / 32 of
+// qh[e % 32] as the 5th bit: (d*sc)*q - (dmin*m).
+__device__ __forceinline__ float q5k_elem(const uint8_t* blk, int e) {
+    const int g = e >> 6, j = e >> 5, l = e & 31;
+    int sc, m;
+    q4k_scale_min(blk + 4, j, sc, m);
+    const uint8_t b = blk[48 + 32 * g + l];
+    const int q = ((j & 1) ? (b >> 4) : (b & 0x0f)) | (((blk[16 + l] >> j) & 1) << 4);
+    const float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+    return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+}
+
 // q-32 of element e of a Q6_K block whose ql / qh / scales start at `main`.
 __device__ __forceinline__ int q6k_q(const uint8_t* main, int e) {
     int h = e >> 7, r = e & 127, i = r >> 5, l = r & 31;

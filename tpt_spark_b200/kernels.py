@@ -13,6 +13,7 @@ import numpy as np
 from ._lib import check, lib
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q5_K = 2, 3, 6, 7, 10, 11, 13
 
 
 def _ptr(t) -> int:

@@ -28,8 +28,15 @@ pub const TPTC_ERR_TIMEOUT: c_int = -10;
 
 pub const TPTC_TYPE_F32: c_int = 0;
 pub const TPTC_TYPE_F16: c_int = 1;
+pub const TPTC_TYPE_Q4_0: c_int = 2;
+pub const TPTC_TYPE_Q4_1: c_int = 3;
+pub const TPTC_TYPE_Q5_0: c_int = 6;
+pub const TPTC_TYPE_Q5_1: c_int = 7;
 pub const TPTC_TYPE_Q8_0: c_int = 8;
+pub const TPTC_TYPE_Q2_K: c_int = 10;
+pub const TPTC_TYPE_Q3_K: c_int = 11;
 pub const TPTC_TYPE_Q4_K: c_int = 12;
+pub const TPTC_TYPE_Q5_K: c_int = 13;
 pub const TPTC_TYPE_Q6_K: c_int = 14;
 
 pub const TPTC_SHARD_Q: c_int = 0;
