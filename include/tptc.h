@@ -237,7 +237,8 @@ TPTC_API int tptc_gemv(const tptc_matrix* m, const float* d_x, float* d_y, void*
  * rounded to nearest fp16. */
 TPTC_API int tptc_matrix_dequant_f16(const tptc_matrix* m, void* d_out, void* stream);
 /* Per (row, super-block) integer sums of the same kernel: isum = sum_j sc_j*dot_j,
- * msum = sum_j m_j*bsum_j (Q4_K; 0 otherwise); [N, K/256] for k-quants, [N, K/32] Q8_0. */
+ * msum = sum_j m_j*bsum_j (Q4_K, Q5_K; not written otherwise; d_msum may be NULL);
+ * [N, K/256] for k-quants, [N, K/32] for Q4_0 / Q5_0 / Q8_0 (candle's per-block sumi). */
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,
                              void* stream);
 

@@ -4,8 +4,9 @@
 // 16x16-tiled f32 GEMM with M=1" (shaders/dequant_q4k.wgsl:74-115, dequant_q6k.wgsl:58-92,
 // dequant_q8.wgsl:51-73, dequant_f16.wgsl:30-37, gemm.wgsl:28-70, driven by
 // engine/wgpu_engine.rs:581-605), with candle QMatMul semantics (candle_engine.rs:221,273):
-// the activation is quantised to Q8_K (Q4_K/Q6_K weights) or Q8_0 (Q8_0 weights) and every
-// super-block contributes (d_w*d_x)*isum - (dmin_w*d_x)*msum from exact integer sums.
+// the activation is quantised to Q8_K (Q4_K/Q5_K/Q6_K weights) or Q8_0 (Q4_0/Q5_0/Q8_0 weights)
+// and every super-block (32-block) contributes (d_w*d_x)*isum - (dmin_w*d_x)*msum
+// ((isum*d_w)*d_x) from exact integer sums.
 //
 // Kernel structure: a persistent grid (one CTA per SM), 9 warps per CTA.
 //   - warp 8 (producer) streams the CTA's weight tiles (8 rows x a chunk of super-blocks,
@@ -166,6 +167,45 @@ __device__ __forceinline__ float q4k_half(const uint8_t* slot, const XHalf& xh, 
     return dd * (float)isum - dm * (float)msum;
 }
 
+// Q5_K (the GGUF block unchanged: d | dmin | scales[12] | qh[32] | qs[128]): q4k_half's work
+// split and scales, with the 5th bit of element l of sub-block j (bit j of qh[l]) placed
+// above each nibble before the dot; high nibbles are shifted down first.
+__device__ __forceinline__ float q5k_half(const uint8_t* slot, const XHalf& xh, int lane) {
+    const int sb = lane >> 1, h = lane & 1;
+    const uint8_t* blk = slot + sb * Q5K_BYTES;
+    const uint4 hd = *reinterpret_cast<const uint4*>(blk);
+    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16);  // qh[0..16)
+    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32);  // qh[16..32)
+    const uint4* wq = reinterpret_cast<const uint4*>(blk + 48 + 64 * h);
+    const uint4 w0 = wq[0], w1 = wq[1], w2 = wq[2], w3 = wq[3];
+    const uint32_t lo = 0x0f0f0f0fu, one = 0x01010101u;
+    const int j0 = 4 * h;
+    int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#define Q5_WORD(W, H, XL, XH, SL, SH, JL)                                             \
+    SL = dp4a_us((W & lo) | (((H >> (JL)) & one) << 4), XL, SL);                      \
+    SH = dp4a_us(((W >> 4) & lo) | (((H >> ((JL) + 1)) & one) << 4), XH, SH);
+#define Q5_VEC(W, H, XL, XH, SL, SH, JL)             \
+    Q5_WORD(W.x, H.x, XL.x, XH.x, SL, SH, JL)        \
+    Q5_WORD(W.y, H.y, XL.y, XH.y, SL, SH, JL)        \
+    Q5_WORD(W.z, H.z, XL.z, XH.z, SL, SH, JL)        \
+    Q5_WORD(W.w, H.w, XL.w, XH.w, SL, SH, JL)
+    Q5_VEC(w0, qa, xh.x[0], xh.x[2], s0, s1, j0)
+    Q5_VEC(w1, qb, xh.x[1], xh.x[3], s0, s1, j0)
+    Q5_VEC(w2, qa, xh.x[4], xh.x[6], s2, s3, j0 + 2)
+    Q5_VEC(w3, qb, xh.x[5], xh.x[7], s2, s3, j0 + 2)
+#undef Q5_VEC
+#undef Q5_WORD
+    const uint32_t k6 = 0x3f3f3f3fu, k4 = 0x0f0f0f0fu, k2 = 0x03030303u;
+    const uint32_t sc = h == 0 ? hd.y & k6 : (hd.w & k4) | (((hd.y >> 6) & k2) << 4);
+    const uint32_t mn = h == 0 ? hd.z & k6 : ((hd.w >> 4) & k4) | (((hd.z >> 6) & k2) << 4);
+    const int isum = ubyte(sc, 0) * s0 + ubyte(sc, 1) * s1 + ubyte(sc, 2) * s2 + ubyte(sc, 3) * s3;
+    const int msum = ubyte(mn, 0) * (int)(int16_t)(xh.ps.x & 0xffff) + ubyte(mn, 1) * (int)(int16_t)(xh.ps.x >> 16) +
+                     ubyte(mn, 2) * (int)(int16_t)(xh.ps.y & 0xffff) + ubyte(mn, 3) * (int)(int16_t)(xh.ps.y >> 16);
+    const float dd = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff))), xh.dx);
+    const float dm = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(hd.x >> 16))), xh.dx);
+    return dd * (float)isum - dm * (float)msum;
+}
+
 __device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* dsec, const XHalf& xh, int lane) {
     const int sb = lane >> 1, h = lane & 1;
     const uint8_t* m = slot + sb * Q6K_MAIN;
@@ -258,7 +298,66 @@ __device__ __forceinline__ float chunk_q4k(const uint8_t* slot, const Act& a, in
         if (valid && g == 0) {
             if (DOTS) {
                 isum_row[c0 + sb] = isum;
-                msum_row[c0 + sb] = msum;
+                if (msum_row) msum_row[c0 + sb] = msum;
+            } else {
+                acc += dd * (float)isum - dm * (float)msum;
+            }
+        }
+    }
+    return acc;
+}
+
+// Q5_K in chunk_q4k's item split (natural activation layout; the DOTS test hook).
+template <bool DOTS>
+__device__ __forceinline__ float chunk_q5k(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int first,
+                                           int stride, int32_t* isum_row, int32_t* msum_row) {
+    float acc = 0.f;
+    const int items = cb * 4;
+    for (int base = first; base < items; base += stride) {
+        const int it = base + lane;
+        const bool valid = it < items;
+        const int sb = it >> 2, g = it & 3;
+        int isum = 0, msum = 0;
+        float dd = 0.f, dm = 0.f;
+        if (valid) {
+            const uint8_t* blk = slot + sb * Q5K_BYTES;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(blk + 48 + 32 * g);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(blk + 64 + 32 * g);
+            const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16);
+            const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32);
+            const int4* xq = reinterpret_cast<const int4*>(a.q8k + (c0 + sb) * QK_K + 64 * g);
+            const int4 x0 = xq[0], x1 = xq[1], x2 = xq[2], x3 = xq[3];
+            const uint32_t m4 = 0x0f0f0f0fu, one = 0x01010101u;
+            const int jl = 2 * g, jh = 2 * g + 1;
+            int lo = 0, hi = 0;
+#define Q5_LO(W, H, X) lo = __dp4a((int)((W & m4) | (((H >> jl) & one) << 4)), X, lo);
+#define Q5_HI(W, H, X) hi = __dp4a((int)(((W >> 4) & m4) | (((H >> jh) & one) << 4)), X, hi);
+            Q5_LO(w0.x, qa.x, x0.x) Q5_LO(w0.y, qa.y, x0.y) Q5_LO(w0.z, qa.z, x0.z) Q5_LO(w0.w, qa.w, x0.w)
+            Q5_LO(w1.x, qb.x, x1.x) Q5_LO(w1.y, qb.y, x1.y) Q5_LO(w1.z, qb.z, x1.z) Q5_LO(w1.w, qb.w, x1.w)
+            Q5_HI(w0.x, qa.x, x2.x) Q5_HI(w0.y, qa.y, x2.y) Q5_HI(w0.z, qa.z, x2.z) Q5_HI(w0.w, qa.w, x2.w)
+            Q5_HI(w1.x, qb.x, x3.x) Q5_HI(w1.y, qb.y, x3.y) Q5_HI(w1.z, qb.z, x3.z) Q5_HI(w1.w, qb.w, x3.w)
+#undef Q5_LO
+#undef Q5_HI
+            int sc0, m0, sc1, m1;
+            q4k_scale_min(blk + 4, 2 * g, sc0, m0);
+            q4k_scale_min(blk + 4, 2 * g + 1, sc1, m1);
+            const int16_t* bs = a.q8k_bs + (c0 + sb) * 16 + 4 * g;
+            isum = sc0 * lo + sc1 * hi;
+            msum = m0 * ((int)bs[0] + (int)bs[1]) + m1 * ((int)bs[2] + (int)bs[3]);
+            if (g == 0) {
+                const float dx = a.q8k_d[c0 + sb];
+                dd = __fmul_rn(h2f(blk[0] | (blk[1] << 8)), dx);
+                dm = __fmul_rn(h2f(blk[2] | (blk[3] << 8)), dx);
+            }
+        }
+        isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+        isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+        msum += __shfl_xor_sync(0xffffffffu, msum, 1);
+        msum += __shfl_xor_sync(0xffffffffu, msum, 2);
+        if (valid && g == 0) {
+            if (DOTS) {
+                isum_row[c0 + sb] = isum;
+                if (msum_row) msum_row[c0 + sb] = msum;
             } else {
                 acc += dd * (float)isum - dm * (float)msum;
             }
@@ -352,6 +451,68 @@ __device__ __forceinline__ float chunk_q80(const uint8_t* slot, const uint16_t* 
                 acc += __fmul_rn(__fmul_rn((float)sum, h2f(dsec[b])), a.q80_d[b0 + b]);
             }
         }
+    }
+    return acc;
+}
+
+// Four 1-bit values (bits 0..3 of v) spread to bit 0 of four bytes: bit k lands at 8k
+// through the multiply (shifts 0, 7, 14, 21 give it position k + 7k).
+__device__ __forceinline__ uint32_t spread4(uint32_t v) { return ((v & 0xfu) * 0x00204081u) & 0x01010101u; }
+
+// Q4_0 / Q5_0 (device layout: the eight blocks' 16-byte qs, for Q5_0 then their 4-byte qh;
+// f16 d in the scale section): lane l takes 32-block l of each run of 32 blocks.  Element
+// j < 16 of a block is the low nibble of qs[j] and pairs with activation j, element j + 16
+// its high nibble with activation j + 16; Q5_0 adds bit j (j + 16) of qh as the 5th bit.
+// The block's integer sum is sum(q * x) - off * sum(x) (off = 8 or 16), candle's
+// sum((q - off) * x) exactly; its f32 contribution is candle's (sumi * d_w) * d_x.
+template <bool DOTS, bool Q5>
+__device__ __forceinline__ float chunk_q40(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int cb,
+                                           int lane, int32_t* isum_row) {
+    float acc = 0.f;
+    const int nblk = cb * 8;  // 32-blocks in the row chunk
+    const int b0 = c0 * 8;
+    const uint4* w = reinterpret_cast<const uint4*>(slot);
+    const uint32_t* qhw = reinterpret_cast<const uint32_t*>(slot + cb * 128);
+    const int4* x = reinterpret_cast<const int4*>(a.q80 + c0 * QK_K);
+    const uint32_t lo = 0x0f0f0f0fu;
+    for (int i0 = 0; i0 < nblk; i0 += 32) {
+        const int b = i0 + lane;
+        if (b >= nblk) continue;
+        const uint4 wv = w[b];
+        const int4 xl = x[2 * b], xh = x[2 * b + 1];
+        uint32_t l0 = wv.x & lo, l1 = wv.y & lo, l2 = wv.z & lo, l3 = wv.w & lo;
+        uint32_t h0 = (wv.x >> 4) & lo, h1 = (wv.y >> 4) & lo, h2 = (wv.z >> 4) & lo, h3 = (wv.w >> 4) & lo;
+        if (Q5) {
+            const uint32_t hb = qhw[b];
+            l0 |= spread4(hb) << 4;
+            l1 |= spread4(hb >> 4) << 4;
+            l2 |= spread4(hb >> 8) << 4;
+            l3 |= spread4(hb >> 12) << 4;
+            h0 |= spread4(hb >> 16) << 4;
+            h1 |= spread4(hb >> 20) << 4;
+            h2 |= spread4(hb >> 24) << 4;
+            h3 |= spread4(hb >> 28) << 4;
+        }
+        int s = dp4a_us(l0, xl.x, 0);
+        s = dp4a_us(l1, xl.y, s);
+        s = dp4a_us(l2, xl.z, s);
+        s = dp4a_us(l3, xl.w, s);
+        s = dp4a_us(h0, xh.x, s);
+        s = dp4a_us(h1, xh.y, s);
+        s = dp4a_us(h2, xh.z, s);
+        s = dp4a_us(h3, xh.w, s);
+        const int ones = 0x01010101;
+        int sx = __dp4a(ones, xl.x, 0);
+        sx = __dp4a(ones, xl.y, sx);
+        sx = __dp4a(ones, xl.z, sx);
+        sx = __dp4a(ones, xl.w, sx);
+        sx = __dp4a(ones, xh.x, sx);
+        sx = __dp4a(ones, xh.y, sx);
+        sx = __dp4a(ones, xh.z, sx);
+        sx = __dp4a(ones, xh.w, sx);
+        const int sum = s - (Q5 ? 16 : 8) * sx;
+        if (DOTS) isum_row[b0 + b] = sum;
+        else acc += __fmul_rn(__fmul_rn((float)sum, h2f(dsec[b])), a.q80_d[b0 + b]);
     }
     return acc;
 }
@@ -688,7 +849,7 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
         int32_t* isum_row = nullptr;
         int32_t* msum_row = nullptr;
         if (EPI == EPI_DOTS) {
-            const int per_row = m.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
+            const int per_row = type_q80_family(m.type) ? p.K / QK8_0 : nsb;
             isum_row = p.isum + (int64_t)ur.row * per_row;
             msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
         }
@@ -711,6 +872,17 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
                 return q6k_half(slot, dsec, xh, lane);
             }
             return 0.f;
+        case TPTC_TYPE_Q5_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q5k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                return q5k_half(slot, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
         default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
         }
@@ -909,7 +1081,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         int32_t* isum_row = nullptr;
         int32_t* msum_row = nullptr;
         if (EPI == EPI_DOTS) {
-            const int per_row = m.type == TPTC_TYPE_Q8_0 ? p.K / QK8_0 : nsb;
+            const int per_row = type_q80_family(m.type) ? p.K / QK8_0 : nsb;
             isum_row = p.isum + (int64_t)ur.row * per_row;
             msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
         }
@@ -932,6 +1104,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                 return q6k_half(slot, dsec, xh, lane);
             }
             return 0.f;
+        case TPTC_TYPE_Q5_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q5k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                return q5k_half(slot, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
         default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
         }
@@ -1257,7 +1440,7 @@ void gemv_prepare(GemvParams& p, int sm_count) {
     for (int s = 0; s < p.nseg; s++) {
         const int t = p.seg[s].m.type;
         if (t == TPTC_TYPE_F16) need_f32 = true;
-        else if (t == TPTC_TYPE_Q8_0) need_q80 = true;
+        else if (type_q80_family(t)) need_q80 = true;
         else need_q8k = true;
         sbb_max = std::max(sbb_max, sb_bytes(t));
     }

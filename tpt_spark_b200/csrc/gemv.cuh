@@ -1,4 +1,5 @@
-// gemv.cuh -- batch-1 dequant-fused GEMV (decode) for Q4_K / Q6_K / Q8_0 / F16 weights.
+// gemv.cuh -- batch-1 dequant-fused GEMV (decode) for Q4_K / Q5_K / Q6_K / Q4_0 / Q5_0 / Q8_0 /
+// F16 weights.
 #pragma once
 
 #include "common.cuh"
@@ -7,14 +8,28 @@ namespace tptc {
 
 // Bytes per 256-element super-block in the device layout (all of it, GGUF size), the part
 // before a tile's scale section, and its share of that section; super-blocks per chunk.
-__host__ __device__ inline int sb_bytes(int type) {
-    return type == TPTC_TYPE_Q4_K ? 144 : type == TPTC_TYPE_Q6_K ? 210 : type == TPTC_TYPE_Q8_0 ? 272 : 512;
-}
 __host__ __device__ inline int sb_main_bytes(int type) {
-    return type == TPTC_TYPE_Q4_K ? 144 : type == TPTC_TYPE_Q6_K ? 208 : type == TPTC_TYPE_Q8_0 ? 256 : 512;
+    switch (type) {
+    case TPTC_TYPE_Q4_K: return 144;
+    case TPTC_TYPE_Q5_K: return 176;
+    case TPTC_TYPE_Q6_K: return 208;
+    case TPTC_TYPE_Q4_0: return 128;
+    case TPTC_TYPE_Q5_0: return 160;
+    case TPTC_TYPE_Q8_0: return 256;
+    }
+    return 512;
 }
 __host__ __device__ inline int sb_d_bytes(int type) {
-    return type == TPTC_TYPE_Q6_K ? 2 : type == TPTC_TYPE_Q8_0 ? 16 : 0;
+    switch (type) {
+    case TPTC_TYPE_Q6_K: return 2;
+    case TPTC_TYPE_Q4_0: case TPTC_TYPE_Q5_0: case TPTC_TYPE_Q8_0: return 16;
+    }
+    return 0;
+}
+__host__ __device__ inline int sb_bytes(int type) { return sb_main_bytes(type) + sb_d_bytes(type); }
+// The 32-element formats: eight blocks per super-block, activations quantised to Q8_0.
+__host__ __device__ inline bool type_q80_family(int type) {
+    return type == TPTC_TYPE_Q8_0 || type == TPTC_TYPE_Q4_0 || type == TPTC_TYPE_Q5_0;
 }
 __host__ __device__ inline int chunk_sb(int type) { return type == TPTC_TYPE_F16 ? 8 : 16; }
 
@@ -24,7 +39,10 @@ constexpr int kTileRows = 8;
 //
 // Per-super-block encoding (256 elements):
 //   Q4_K  144 B: the GGUF block unchanged (d | dmin | scales[12] | qs[128])
+//   Q5_K  176 B: the GGUF block unchanged (d | dmin | scales[12] | qh[32] | qs[128])
 //   Q6_K  208 B: ql | qh | scales, plus its f16 d in the tile's scale section
+//   Q4_0  128 B: qs of eight 32-blocks (16 B each), plus their eight f16 d in the scale section
+//   Q5_0  160 B: qs of eight 32-blocks, then their eight 4-byte qh words; d as Q4_0
 //   Q8_0  256 B: qs of eight 32-blocks, plus their eight f16 d in the scale section
 //   F16   512 B: 256 f16 values
 // Tiling: rows are grouped by 8 (N padded to Npad, zero rows) and each row is cut into
@@ -87,7 +105,7 @@ __host__ __device__ inline const uint8_t* dm_block(const DevMatrix& m, int prow,
     return t + (int64_t)((prow % kTileRows) * cb + j) * sbm;
 }
 
-// f16 scales of super-block `sb` of physical row `prow` (Q6_K: 1, Q8_0: 8).
+// f16 scales of super-block `sb` of physical row `prow` (Q6_K: 1, Q4_0 / Q5_0 / Q8_0: 8).
 __host__ __device__ inline const uint16_t* dm_scales(const DevMatrix& m, int prow, int sb) {
     int cb, j;
     const uint8_t* t = dm_tile(m, prow, sb, cb, j);
@@ -106,10 +124,11 @@ enum GemvEpi : int {
 // Layout of a prepared GEMV activation (the GEMV's shared-memory region, and the global
 // buffer it is bulk-copied from): byte offsets of each part, -1 when absent.
 //   f32           [K] f32                    (F16 weights)
-//   q8k           [K] int8 Q8_K quants       (Q4_K / Q6_K weights), lane-transposed per chunk
+//   q8k           [K] int8 Q8_K quants       (Q4_K / Q5_K / Q6_K weights), lane-transposed per chunk
 //                 (xt_offset) for the forward kernels, natural order for the DOTS test hook
 //   q8k_d / _bs / _ps  per 256-block scale, 16-element sums [K/16], 32-element sums [K/32]
-//   q80 / q80_d   [K] int8 Q8_0 quants, per 32-block scale (f16-rounded, f32)
+//   q80 / q80_d   [K] int8 Q8_0 quants, per 32-block scale (f16-rounded, f32) (Q4_0 / Q5_0 /
+//                 Q8_0 weights)
 struct ActLayout {
     int f32, q8k, q8k_d, q8k_bs, q8k_ps, q80, q80_d;
     int bytes;  // total, a multiple of 128

@@ -19,6 +19,13 @@ void ggml_block_info(uint32_t type, uint64_t& elems, uint64_t& bytes) {
     case TPTC_TYPE_Q8_0: elems = 32; bytes = 34; return;
     case TPTC_TYPE_Q4_K: elems = 256; bytes = 144; return;
     case TPTC_TYPE_Q6_K: elems = 256; bytes = 210; return;
+    case TPTC_TYPE_Q4_0: elems = 32; bytes = 18; return;
+    case TPTC_TYPE_Q4_1: elems = 32; bytes = 20; return;
+    case TPTC_TYPE_Q5_0: elems = 32; bytes = 22; return;
+    case TPTC_TYPE_Q5_1: elems = 32; bytes = 24; return;
+    case TPTC_TYPE_Q2_K: elems = 256; bytes = 84; return;
+    case TPTC_TYPE_Q3_K: elems = 256; bytes = 110; return;
+    case TPTC_TYPE_Q5_K: elems = 256; bytes = 176; return;
     default: elems = 0; bytes = 0; return;
     }
 }

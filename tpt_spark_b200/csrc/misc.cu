@@ -21,21 +21,7 @@ __global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok
     if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;  // opens a decode step (TpLink epochs)
     const int row = (int)*tok_ptr;  // token_embd is never a fused gate|up matrix: phys row = row
     const int K = emb.K;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) {
-        const uint8_t* blk = dm_block(emb, row, i / QK_K);
-        const int e = i % QK_K;
-        float v;
-        if (emb.type == TPTC_TYPE_Q4_K) {
-            v = q4k_elem(blk, e);
-        } else if (emb.type == TPTC_TYPE_Q6_K) {
-            v = q6k_elem(blk, h2f(dm_scales(emb, row, i / QK_K)[0]), e);
-        } else if (emb.type == TPTC_TYPE_Q8_0) {
-            v = __fmul_rn((float)(int8_t)blk[e], h2f(dm_scales(emb, row, i / QK_K)[e / QK8_0]));
-        } else {
-            v = h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
-        }
-        x[i] = v;
-    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) x[i] = dm_elem(emb, row, i);
 }
 
 // Greedy pick, candle LogitsProcessor::sample_argmax: Iterator::max_by(f32::total_cmp)

@@ -34,21 +34,7 @@ namespace {
 __global__ void embed_rows_kernel(DevMatrix emb, const uint32_t* __restrict__ ids, float* __restrict__ x) {
     const int t = blockIdx.x, row = (int)ids[t], K = emb.K;
     float* xr = x + (size_t)t * K;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const uint8_t* blk = dm_block(emb, row, i / QK_K);
-        const int e = i % QK_K;
-        float v;
-        if (emb.type == TPTC_TYPE_Q4_K) {
-            v = q4k_elem(blk, e);
-        } else if (emb.type == TPTC_TYPE_Q6_K) {
-            v = q6k_elem(blk, h2f(dm_scales(emb, row, i / QK_K)[0]), e);
-        } else if (emb.type == TPTC_TYPE_Q8_0) {
-            v = __fmul_rn((float)(int8_t)blk[e], h2f(dm_scales(emb, row, i / QK_K)[e / QK8_0]));
-        } else {
-            v = h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
-        }
-        xr[i] = v;
-    }
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xr[i] = dm_elem(emb, row, i);
 }
 
 // out[t][:] = fp16(x[t] / sqrt(mean(x[t]^2) + eps) * w) (candle rms_norm: x / m * alpha);

@@ -92,6 +92,24 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, 
             for (int k = 0; k < 32; k++) dst[32 * j + k] = src[2 + k];
             dsc[j] = (uint16_t)(src[0] | (src[1] << 8));
         }
+    } else if (m.type == TPTC_TYPE_Q5_K) {
+        const uint8_t* src = row + (int64_t)sb * Q5K_BYTES;
+        for (int k = 0; k < Q5K_BYTES; k++) dst[k] = src[k];
+    } else if (m.type == TPTC_TYPE_Q4_0) {
+        uint16_t* dsc = const_cast<uint16_t*>(dm_scales(m, prow, sb));
+        for (int j = 0; j < 8; j++) {
+            const uint8_t* src = row + ((int64_t)sb * 8 + j) * Q40_BYTES;
+            for (int k = 0; k < 16; k++) dst[16 * j + k] = src[2 + k];
+            dsc[j] = (uint16_t)(src[0] | (src[1] << 8));
+        }
+    } else if (m.type == TPTC_TYPE_Q5_0) {
+        uint16_t* dsc = const_cast<uint16_t*>(dm_scales(m, prow, sb));
+        for (int j = 0; j < 8; j++) {
+            const uint8_t* src = row + ((int64_t)sb * 8 + j) * Q50_BYTES;
+            for (int k = 0; k < 16; k++) dst[16 * j + k] = src[6 + k];
+            for (int k = 0; k < 4; k++) dst[128 + 4 * j + k] = src[2 + k];
+            dsc[j] = (uint16_t)(src[0] | (src[1] << 8));
+        }
     } else {
         const uint8_t* src = row + (int64_t)sb * 512;
         for (int k = 0; k < 512; k++) dst[k] = src[k];
@@ -154,11 +172,15 @@ __global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, int phy
                 v[16 * k + b] = __float2half_rn(__fmul_rn(k == 0 ? ds0 : ds1, (float)q));
             }
         }
-    } else {
+    } else if (m.type == TPTC_TYPE_Q8_0) {
         const int8_t* q = reinterpret_cast<const int8_t*>(blk + e0);
         const float d = h2f(dm_scales(m, prow, sb)[e0 / QK8_0]);
 #pragma unroll
         for (int b = 0; b < 32; b++) v[b] = __float2half_rn(__fmul_rn((float)q[b], d));
+    } else {
+        // Q5_K, Q4_0, Q5_0: the element values of dm_elem (one group of 32, rounded to fp16)
+#pragma unroll 8
+        for (int b = 0; b < 32; b++) v[b] = __float2half_rn(dm_elem(m, prow, k0 + b));
     }
     uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)r * m.K + k0);
 #pragma unroll

@@ -11,6 +11,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "gemv.cuh"
 
 namespace tptc {
 
@@ -192,6 +193,30 @@ __device__ __forceinline__ int q6k_q(const uint8_t* main, int e) {
 __device__ __forceinline__ float q6k_elem(const uint8_t* main, float d, int e) {
     const int8_t* sc = reinterpret_cast<const int8_t*>(main + 192);
     return __fmul_rn(__fmul_rn(d, (float)sc[e >> 4]), (float)q6k_q(main, e));
+}
+
+// Element i (0 .. K-1) of physical row `prow` of a matrix in the device layout, with the
+// value (and rounding) of the raw-block dequantisation above.
+__device__ __forceinline__ float dm_elem(const DevMatrix& m, int prow, int i) {
+    const int sb = i / QK_K, e = i % QK_K;
+    const uint8_t* blk = dm_block(m, prow, sb);
+    switch (m.type) {
+    case TPTC_TYPE_Q4_K: return q4k_elem(blk, e);
+    case TPTC_TYPE_Q5_K: return q5k_elem(blk, e);
+    case TPTC_TYPE_Q6_K: return q6k_elem(blk, h2f(dm_scales(m, prow, sb)[0]), e);
+    case TPTC_TYPE_Q8_0:
+        return __fmul_rn((float)(int8_t)blk[e], h2f(dm_scales(m, prow, sb)[e / QK8_0]));
+    case TPTC_TYPE_Q4_0: {
+        const int j = e / QK8_0;
+        return __fmul_rn(h2f(dm_scales(m, prow, sb)[j]), (float)(q4_nibble(blk + 16 * j, e % QK8_0) - 8));
+    }
+    case TPTC_TYPE_Q5_0: {
+        const int j = e / QK8_0, l = e % QK8_0;
+        const int q = q4_nibble(blk + 16 * j, l) | (q5_hbit(blk + 128 + 4 * j, l) << 4);
+        return __fmul_rn(h2f(dm_scales(m, prow, sb)[j]), (float)(q - 16));
+    }
+    }
+    return h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
 }
 
 }  // namespace tptc

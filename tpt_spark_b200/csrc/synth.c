@@ -25,7 +25,7 @@
 #include <stdint.h>
 #include <string.h>
 
-enum { SY_F32 = 0, SY_F16 = 1, SY_Q8_0 = 8, SY_Q4_K = 12, SY_Q6_K = 14 };
+enum { SY_F32 = 0, SY_F16 = 1, SY_Q4_0 = 2, SY_Q5_0 = 6, SY_Q8_0 = 8, SY_Q4_K = 12, SY_Q5_K = 13, SY_Q6_K = 14 };
 
 static inline uint64_t splitmix64(uint64_t x) {
     x += 0x9E3779B97F4A7C15ull;
@@ -143,6 +143,74 @@ static void enc_q4k(const float* x, uint8_t* b) {
         for (int l = 0; l < 32; l++) qs[32 * g + l] = (uint8_t)(q[64 * g + l] | (q[64 * g + 32 + l] << 4));
 }
 
+/* Q4_0 / Q5_0 as gguf-py's quantize_blocks (gguf/quants.py :222-239, :293-312): d = signed
+ * max / -8 (-16), q = trunc(x / d + 8.5 (16.5)) clipped to 0..15 (0..31); element l < 16 in the
+ * low nibble of qs[l], l + 16 in the high nibble, Q5_0's 5th bits in the little-endian qh. */
+static void enc_q40_q50(const float* x, uint8_t* b, int five) {
+    float mx = 0.f, amx = 0.f;
+    for (int j = 0; j < 32; j++)
+        if (fabsf(x[j]) > amx) { amx = fabsf(x[j]); mx = x[j]; }
+    const float d = mx / (five ? -16.f : -8.f), id = d != 0.f ? 1.f / d : 0.f;
+    uint8_t q[32];
+    for (int j = 0; j < 32; j++) q[j] = (uint8_t)clampi((int)truncf(x[j] * id + (five ? 16.5f : 8.5f)), 0, five ? 31 : 15);
+    const uint16_t h = f2h(d);
+    b[0] = (uint8_t)(h & 0xff);
+    b[1] = (uint8_t)(h >> 8);
+    uint8_t* qs = b + (five ? 6 : 2);
+    for (int j = 0; j < 16; j++) qs[j] = (uint8_t)((q[j] & 0x0f) | ((q[j + 16] & 0x0f) << 4));
+    if (five) {
+        uint32_t qh = 0;
+        for (int j = 0; j < 32; j++) qh |= (uint32_t)(q[j] >> 4) << j;
+        memcpy(b + 2, &qh, 4);
+    }
+}
+
+/* Q5_K: enc_q4k with 32 levels (scales (max - min) / 31) and the 5th bits in qh. */
+static void enc_q5k(const float* x, uint8_t* b) {
+    float scales[8], mins[8], max_scale = 0.f, max_min = 0.f;
+    for (int j = 0; j < 8; j++) {
+        float mn = x[32 * j], mx = x[32 * j];
+        for (int l = 1; l < 32; l++) {
+            mn = fminf(mn, x[32 * j + l]);
+            mx = fmaxf(mx, x[32 * j + l]);
+        }
+        if (mn > 0.f) mn = 0.f;
+        scales[j] = (mx - mn) / 31.f;
+        mins[j] = -mn;
+        max_scale = fmaxf(max_scale, scales[j]);
+        max_min = fmaxf(max_min, mins[j]);
+    }
+    uint16_t dh = f2h(max_scale / 63.f), mh = f2h(max_min / 63.f);
+    float d = h2f(dh), dm = h2f(mh);
+    uint8_t sc[8], mq[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = (uint8_t)(d > 0.f ? clampi((int)lroundf(scales[j] / d), 0, 63) : 0);
+        mq[j] = (uint8_t)(dm > 0.f ? clampi((int)lroundf(mins[j] / dm), 0, 63) : 0);
+    }
+    b[0] = (uint8_t)(dh & 0xff);
+    b[1] = (uint8_t)(dh >> 8);
+    b[2] = (uint8_t)(mh & 0xff);
+    b[3] = (uint8_t)(mh >> 8);
+    uint8_t* s = b + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)(sc[j] | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)(mq[j] | ((mq[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 0x0f) | ((mq[j + 4] & 0x0f) << 4));
+    }
+    uint8_t q[256];
+    for (int j = 0; j < 8; j++) {
+        float es = d * (float)sc[j], em = dm * (float)mq[j];
+        for (int l = 0; l < 32; l++) q[32 * j + l] = (uint8_t)(es > 0.f ? clampi((int)lroundf((x[32 * j + l] + em) / es), 0, 31) : 0);
+    }
+    uint8_t* qh = b + 16;
+    uint8_t* qs = b + 48;
+    memset(qh, 0, 32);
+    for (int j = 0; j < 8; j++)
+        for (int l = 0; l < 32; l++) qh[l] |= (uint8_t)((q[32 * j + l] >> 4) << j);
+    for (int g = 0; g < 4; g++)
+        for (int l = 0; l < 32; l++) qs[32 * g + l] = (uint8_t)((q[64 * g + l] & 0x0f) | ((q[64 * g + 32 + l] & 0x0f) << 4));
+}
+
 static void enc_q6k(const float* x, uint8_t* b) {
     float scales[16], max_scale = 0.f, amax_scale = 0.f;
     for (int j = 0; j < 16; j++) {
@@ -190,6 +258,9 @@ int64_t sy_type_bytes(int type, int64_t n) {
     case SY_Q8_0: return n / 32 * 34;
     case SY_Q4_K: return n / 256 * 144;
     case SY_Q6_K: return n / 256 * 210;
+    case SY_Q4_0: return n / 32 * 18;
+    case SY_Q5_0: return n / 32 * 22;
+    case SY_Q5_K: return n / 256 * 176;
     }
     return -1;
 }
@@ -223,6 +294,17 @@ int64_t sy_encode(int type, const float* x, int64_t n, uint8_t* out) {
 #pragma omp parallel for schedule(static)
         for (int64_t i = 0; i < nb; i++) enc_q6k(x + 256 * i, out + 210 * i);
         return nb * 210;
+    case SY_Q4_0:
+    case SY_Q5_0:
+        nb = n / 32;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < nb; i++) enc_q40_q50(x + 32 * i, out + (type == SY_Q5_0 ? 22 : 18) * i, type == SY_Q5_0);
+        return nb * (type == SY_Q5_0 ? 22 : 18);
+    case SY_Q5_K:
+        nb = n / 256;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < nb; i++) enc_q5k(x + 256 * i, out + 176 * i);
+        return nb * 176;
     }
     return -1;
 }

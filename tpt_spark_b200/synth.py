@@ -1,8 +1,8 @@
 """Synthetic GGUF models for tests and benchmarks.
 
 The benchmark configurations are random-init Llama-architecture decoders: linear weights
-drawn N(0, 0.02) from a seed, RMSNorm gains 1.0, quantised to GGUF Q4_K / Q6_K / Q8_0 or
-stored as F16.  There is no network and no checkpoint, so the files are generated here.
+drawn N(0, 0.02) from a seed, RMSNorm gains 1.0, quantised to GGUF Q4_K / Q5_K / Q6_K / Q4_0 /
+Q5_0 / Q8_0 or stored as F16.  There is no network and no checkpoint, so the files are generated here.
 
 The GGUF v3 container written by :func:`write_gguf` carries the metadata keys that the
 reference reads: ``general.architecture`` and the ``llama.*`` keys of
@@ -26,8 +26,11 @@ import numpy as np
 from ._build import lib_path
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
-BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
-TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+Q4_0, Q5_0, Q5_K = 2, 6, 13
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q4_0: (32, 18),
+         Q5_0: (32, 22), Q5_K: (256, 176)}
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q4_0: "Q4_0", Q5_0: "Q5_0",
+              Q5_K: "Q5_K"}
 ALIGN = 32
 
 
@@ -133,6 +136,16 @@ TINY: Dict[str, ModelConfig] = {
         rope_base=10000.0, context_length=512, default_type=F16, norm_std=0.1),
     # splits over 2 tensor-parallel ranks: 4 query heads of 64 (one 256-block of o's K) and
     # 2 kv heads per rank, 512 ffn rows per rank
+    # the further formats: Q5_K_M's mix (Q5_K, with Q6_K attn_v / ffn_down / output) and a
+    # Q4_0 model with Q5_0 attn_v / ffn_down / output (one q|k|v launch over both)
+    "tiny_q5km": ModelConfig(
+        "tiny_q5km", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=448,
+        rope_base=10000.0, context_length=512, default_type=Q5_K, overrides=Q4_K_M, embd_type=Q5_K,
+        output_type=Q6_K, norm_std=0.1),
+    "tiny_q4_0": ModelConfig(
+        "tiny_q4_0", dim=256, n_layers=2, n_heads=4, n_kv_heads=4, ffn=512, vocab=352,
+        rope_base=10000.0, context_length=512, default_type=Q4_0,
+        overrides=(("attn_v", Q5_0), ("ffn_down", Q5_0)), embd_type=Q4_0, output_type=Q5_0, norm_std=0.1),
     "tiny_tp_q4km": ModelConfig(
         "tiny_tp_q4km", dim=512, n_layers=2, n_heads=8, n_kv_heads=4, ffn=1024, vocab=384,
         rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
