@@ -459,8 +459,9 @@ __device__ __forceinline__ float chunk_q80(const uint8_t* slot, const uint16_t* 
 // through the multiply (shifts 0, 7, 14, 21 give it position k + 7k).
 __device__ __forceinline__ uint32_t spread4(uint32_t v) { return ((v & 0xfu) * 0x00204081u) & 0x01010101u; }
 
-// Q4_0 / Q5_0 (device layout: the eight blocks' 16-byte qs, for Q5_0 then their 4-byte qh;
-// f16 d in the scale section): lane l takes 32-block l of each run of 32 blocks.  Element
+// Q4_0 / Q5_0 (device layout per super-block: the eight blocks' 16-byte qs, for Q5_0 then
+// their 4-byte qh words; f16 d in the scale section): lane l takes 32-block l of each run of
+// 32 blocks.  Element
 // j < 16 of a block is the low nibble of qs[j] and pairs with activation j, element j + 16
 // its high nibble with activation j + 16; Q5_0 adds bit j (j + 16) of qh as the 5th bit.
 // The block's integer sum is sum(q * x) - off * sum(x) (off = 8 or 16), candle's
@@ -471,19 +472,18 @@ __device__ __forceinline__ float chunk_q40(const uint8_t* slot, const uint16_t* 
     float acc = 0.f;
     const int nblk = cb * 8;  // 32-blocks in the row chunk
     const int b0 = c0 * 8;
-    const uint4* w = reinterpret_cast<const uint4*>(slot);
-    const uint32_t* qhw = reinterpret_cast<const uint32_t*>(slot + cb * 128);
     const int4* x = reinterpret_cast<const int4*>(a.q80 + c0 * QK_K);
     const uint32_t lo = 0x0f0f0f0fu;
     for (int i0 = 0; i0 < nblk; i0 += 32) {
         const int b = i0 + lane;
         if (b >= nblk) continue;
-        const uint4 wv = w[b];
+        const uint8_t* sbp = slot + (b >> 3) * (Q5 ? 160 : 128);  // the block's super-block
+        const uint4 wv = *reinterpret_cast<const uint4*>(sbp + 16 * (b & 7));
         const int4 xl = x[2 * b], xh = x[2 * b + 1];
         uint32_t l0 = wv.x & lo, l1 = wv.y & lo, l2 = wv.z & lo, l3 = wv.w & lo;
         uint32_t h0 = (wv.x >> 4) & lo, h1 = (wv.y >> 4) & lo, h2 = (wv.z >> 4) & lo, h3 = (wv.w >> 4) & lo;
         if (Q5) {
-            const uint32_t hb = qhw[b];
+            const uint32_t hb = *reinterpret_cast<const uint32_t*>(sbp + 128 + 4 * (b & 7));
             l0 |= spread4(hb) << 4;
             l1 |= spread4(hb >> 4) << 4;
             l2 |= spread4(hb >> 8) << 4;
