@@ -22,6 +22,11 @@ LOGIT_ATOL = 2e-2       # north_star level 3, f32 KV cache (candle's precision)
 LOGIT_ATOL_TIES = 4e-2  # tied Q6_K-embedding model: 8-bit rounding ties at layer 0 (above)
 LOGIT_ATOL_F16KV = 5e-2  # fp16 KV cache: K/V rounded to 11 bits before attention
 TIE_PRONE = {"tiny_q4km_tied"}
+# Greedy paths that pass through near-ties of the oracle's own top two logits (measured on the
+# oracle: tiny_q5km 0.046 at step 31 and 3.2e-4 at step 10, tiny_q4_0 2.3e-5 at step 60): a
+# difference within the logit tolerance can pick the other token there, so these sequences
+# may part only at such a step.
+GREEDY_TIE_PRONE = TIE_PRONE | {"tiny_q5km", "tiny_q4_0"}
 
 
 def atol_for(name):
@@ -132,7 +137,7 @@ def test_greedy_64_identical(engines, tiny_models, name):
     lg = e.prefill(prompt)
     first = O.argmax(lg)
     got = [first] + e.decode_greedy(first, len(prompt), 63)
-    if name not in TIE_PRONE:
+    if name not in GREEDY_TIE_PRONE:
         assert got == want
         return
     # tie-prone model: the sequences may part only where the oracle itself is near a tie
