@@ -21,9 +21,9 @@
  *   - activation quantisation for the integer dot: Q8_K (BlockQ8K::from_float) for
  *     Q4_K / Q6_K weights, Q8_0 (BlockQ8_0::from_float) for Q8_0 weights; F16 weights
  *     are dequantised to f32 and multiplied in f32 (QMatMul::from_arc);
- *   - vec_dot_q4k_q8k / q5k_q8k / q6k_q8k / q4_0_q8_0 / q5_0_q8_0 / q8_0_q8_0 in candle's
- *     scalar accumulation order (Q5_K x Q8_K, Q4_0 x Q8_0 and Q5_0 x Q8_0 are the
- *     k_quants BlockQ5K / BlockQ4_0 / BlockQ5_0 vec_dot_unopt loops);
+ *   - vec_dot_q2k / q3k / q4k / q5k / q6k x q8k and q4_0 / q5_0 / q8_0 x q8_0 in candle's
+ *     scalar accumulation order (the k_quants vec_dot_unopt loops of BlockQ2K, BlockQ3K,
+ *     BlockQ4K, BlockQ5K, BlockQ6K, BlockQ4_0, BlockQ5_0, BlockQ8_0);
  *   - the quantized_llama forward: RmsNorm, interleaved RoPE (rope_i) from an f32
  *     cos/sin table, f32 KV concatenation, causal softmax(QK^T/sqrt(d))V, SwiGLU MLP,
  *     residual adds, final norm and the output projection on the last position only.
@@ -482,6 +482,40 @@ static inline void q5k_block_ints(const uint8_t* blk, const or_q8k* y, int32_t* 
     *msum = ms;
 }
 
+/* Q2_K value q (0..3) of element e, and the 4-bit scale / min of its 16-element group. */
+static inline int q2k_q(const uint8_t* blk, int e) { return (blk[16 + 32 * (e >> 7) + (e & 31)] >> (2 * ((e >> 5) & 3))) & 3; }
+
+/* Per super-block integer sums of Q2_K x Q8_K (candle BlockQ2K::vec_dot_unopt):
+ * isum = sum_g (sc_g & 15) * dot_g, msum = sum_g (sc_g >> 4) * bsum_g over 16-element groups. */
+static inline void q2k_block_ints(const uint8_t* blk, const or_q8k* y, int32_t* isum, int32_t* msum) {
+    int32_t is = 0, ms = 0;
+    for (int g = 0; g < 16; g++) {
+        int32_t s = 0;
+        for (int l = 0; l < 16; l++) s += q2k_q(blk, 16 * g + l) * y->qs[16 * g + l];
+        is += (int32_t)(blk[g] & 0x0f) * s;
+        ms += (int32_t)(blk[g] >> 4) * y->bsums[g];
+    }
+    *isum = is;
+    *msum = ms;
+}
+
+/* Q3_K value q (-4..3) of element e (or_dequant_q3k's q). */
+static inline int q3k_q(const uint8_t* blk, int e) {
+    const int ql = (blk[32 + 32 * (e >> 7) + (e & 31)] >> (2 * ((e >> 5) & 3))) & 3;
+    return ql - ((((blk[e & 31] >> (e >> 5)) & 1) ^ 1) << 2);
+}
+
+/* Per super-block integer sum of Q3_K x Q8_K: sum_g scale_g * dot_g (6-bit scales - 32). */
+static inline int32_t q3k_block_int(const uint8_t* blk, const or_q8k* y) {
+    int32_t is = 0;
+    for (int g = 0; g < 16; g++) {
+        int32_t s = 0;
+        for (int l = 0; l < 16; l++) s += q3k_q(blk, 16 * g + l) * y->qs[16 * g + l];
+        is += q3k_scale(blk + 96, g) * s;
+    }
+    return is;
+}
+
 /* candle BlockQ4_0::vec_dot_unopt block sum: sum_j (lo_j - 8) y_j + (hi_j - 8) y_{j+16}. */
 static inline int32_t q40_block_int(const uint8_t* blk, const uint8_t* xb) {
     const int8_t* y = (const int8_t*)(xb + 2);
@@ -530,6 +564,13 @@ int or_block_dots(int type, const void* wrow, const void* xq, int nb, int32_t* i
             int32_t m;
             q5k_block_ints(w + (size_t)b * Q5K_BYTES, (const or_q8k*)xq + b, isum + b, &m);
             if (msum) msum[b] = m;
+        } else if (type == OR_Q2_K) {
+            int32_t m;
+            q2k_block_ints(w + (size_t)b * Q2K_BYTES, (const or_q8k*)xq + b, isum + b, &m);
+            if (msum) msum[b] = m;
+        } else if (type == OR_Q3_K) {
+            isum[b] = q3k_block_int(w + (size_t)b * Q3K_BYTES, (const or_q8k*)xq + b);
+            if (msum) msum[b] = 0;
         } else if (type == OR_Q4_0) {
             isum[b] = q40_block_int(w + (size_t)b * Q40_BYTES, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
             if (msum) msum[b] = 0;
@@ -749,6 +790,45 @@ static float vec_dot_q5k(int n, const uint8_t* w, const or_q8k* y) {
     return sumf + s;
 }
 
+/* candle BlockQ2K::vec_dot_unopt: sumf += dall * isum - dmin * summs per super-block, with
+ * dall = d_x * d_w and dmin = d_x * dmin_w. */
+static float vec_dot_q2k(int n, const uint8_t* w, const or_q8k* y) {
+    float sumf = 0.f;
+    for (int b = 0; b < n / QK_K; b++) {
+        const uint8_t* blk = w + (size_t)b * Q2K_BYTES;
+        int32_t isum, summs;
+        q2k_block_ints(blk, y + b, &isum, &summs);
+        const float dall = y[b].d * or_h2f(rd16(blk + 80)), dmin = y[b].d * or_h2f(rd16(blk + 82));
+        sumf += dall * (float)isum - dmin * (float)summs;
+    }
+    return sumf;
+}
+
+/* candle BlockQ3K::vec_dot_unopt: Q6_K's order (eight lane sums of d*aux32 over 8-element
+ * groups, each group's products scaled by its 16-element scale). */
+static float vec_dot_q3k(int n, const uint8_t* w, const or_q8k* y) {
+    float sums[8] = {0};
+    for (int b = 0; b < n / QK_K; b++) {
+        const uint8_t* blk = w + (size_t)b * Q3K_BYTES;
+        int8_t a[QK_K];
+        for (int e = 0; e < QK_K; e++) a[e] = (int8_t)q3k_q(blk, e);
+        int32_t aux32[8] = {0};
+        int idx = 0;
+        for (int j = 0; j < QK_K / 16; j++) {
+            const int32_t scale = q3k_scale(blk + 96, j);
+            for (int k2 = 0; k2 < 2; k2++) {
+                for (int l = 0; l < 8; l++) aux32[l] += scale * (int32_t)((int16_t)y[b].qs[idx + l] * (int16_t)a[idx + l]);
+                idx += 8;
+            }
+        }
+        const float d = or_h2f(rd16(blk + 108)) * y[b].d;
+        for (int l = 0; l < 8; l++) sums[l] += d * (float)aux32[l];
+    }
+    float s = 0.f;
+    for (int l = 0; l < 8; l++) s += sums[l];
+    return s;
+}
+
 /* candle BlockQ4_0 / BlockQ5_0 ::vec_dot_unopt: sumf += (float)sumi * d_w * d_x per block. */
 static float vec_dot_q40_q50(int type, int n, const uint8_t* w, const uint8_t* xq) {
     const size_t bb = type == OR_Q4_0 ? Q40_BYTES : Q50_BYTES;
@@ -774,7 +854,7 @@ static float vec_dot_f32(int n, const float* a, const float* b) {
  * quantised to the weight's vec-dot type, then one vec_dot per output element.  F16
  * weights are dequantised to f32 first (QMatMul::from_arc dequantises F16/F32). */
 int or_matmul(int type, const void* W, int N, int K, const float* x, int m, float* y) {
-    if (type == OR_Q4_K || type == OR_Q5_K || type == OR_Q6_K) {
+    if (type == OR_Q4_K || type == OR_Q5_K || type == OR_Q6_K || type == OR_Q2_K || type == OR_Q3_K) {
         if (K % QK_K) return -1;
         or_q8k* xq = (or_q8k*)malloc(sizeof(or_q8k) * (size_t)m * (K / QK_K));
         for (int r = 0; r < m; r++) or_quant_q8k(x + (size_t)r * K, K, xq + (size_t)r * (K / QK_K));
@@ -786,6 +866,8 @@ int or_matmul(int type, const void* W, int N, int K, const float* x, int m, floa
                 const or_q8k* xr = xq + (size_t)r * (K / QK_K);
                 y[(size_t)r * N + n] = type == OR_Q4_K   ? vec_dot_q4k(K, wr, xr)
                                        : type == OR_Q5_K ? vec_dot_q5k(K, wr, xr)
+                                       : type == OR_Q2_K ? vec_dot_q2k(K, wr, xr)
+                                       : type == OR_Q3_K ? vec_dot_q3k(K, wr, xr)
                                                          : vec_dot_q6k(K, wr, xr);
             }
         }

@@ -128,7 +128,7 @@ def quant_q80(x: np.ndarray) -> np.ndarray:
 
 def quant_for(t: int, x: np.ndarray) -> np.ndarray:
     """Activation quantisation candle applies before the dot with a `t` weight."""
-    return quant_q8k(x) if t in (Q4_K, Q5_K, Q6_K) else quant_q80(x)
+    return quant_q8k(x) if t in (Q2_K, Q3_K, Q4_K, Q5_K, Q6_K) else quant_q80(x)
 
 
 def block_dots(t: int, wrow: np.ndarray, xq: np.ndarray, nb: int):

@@ -84,9 +84,10 @@ def test_quant_q80_bitexact(cuda_device):
 SHAPES = [(O.Q4_K, 40, 4096), (O.Q4_K, 8, 256), (O.Q4_K, 1024, 4096), (O.Q4_K, 64, 14336),
           (O.Q6_K, 40, 4096), (O.Q6_K, 24, 14336), (O.Q6_K, 17, 2048), (O.Q8_0, 40, 4096), (O.Q8_0, 16, 14336),
           (O.F16, 40, 4096), (O.F16, 8, 3072), (O.Q5_K, 40, 4096), (O.Q5_K, 24, 14336), (O.Q5_K, 9, 2048),
-          (O.Q4_0, 40, 4096), (O.Q4_0, 16, 14336), (O.Q5_0, 40, 4096), (O.Q5_0, 17, 2048)]
+          (O.Q4_0, 40, 4096), (O.Q4_0, 16, 14336), (O.Q5_0, 40, 4096), (O.Q5_0, 17, 2048),
+          (O.Q2_K, 40, 4096), (O.Q2_K, 24, 14336), (O.Q3_K, 40, 4096), (O.Q3_K, 17, 2048)]
 Q80_FAMILY = (O.Q8_0, O.Q4_0, O.Q5_0)
-BLOCK_BYTES = {O.Q4_K: 144, O.Q5_K: 176, O.Q6_K: 210, O.Q8_0: 34, O.Q4_0: 18, O.Q5_0: 22}
+BLOCK_BYTES = {O.Q4_K: 144, O.Q5_K: 176, O.Q6_K: 210, O.Q8_0: 34, O.Q4_0: 18, O.Q5_0: 22, O.Q2_K: 84, O.Q3_K: 110}
 
 
 def make_matrix(t, N, K, seed=0):
@@ -115,7 +116,7 @@ def test_block_dots_bitexact(cuda_device, t, N, K):
     for r in range(N):
         ri, rm = O.block_dots(t, rows[r], xq, per_row)
         np.testing.assert_array_equal(gi[r], ri, err_msg=f"row {r} isum")
-        if t in (O.Q4_K, O.Q5_K):
+        if t in (O.Q4_K, O.Q5_K, O.Q2_K):
             np.testing.assert_array_equal(gm[r], rm, err_msg=f"row {r} msum")
 
 

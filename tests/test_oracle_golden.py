@@ -161,11 +161,47 @@ def test_block_dots_more_formats(t):
             assert isum[b] == int((q * a).sum())
 
 
-@pytest.mark.parametrize("t", [O.Q5_K, O.Q4_0, O.Q5_0])
+def _q23k(t, blk):
+    """Q2_K / Q3_K integer values (256) and 16-group scales / mins, restated in numpy."""
+    blk = blk.astype(np.int64)
+    e = np.arange(256)
+    h, s, l, g = e >> 7, (e >> 5) & 3, e & 31, e >> 4
+    if t == O.Q2_K:
+        q = (blk[16 + 32 * h + l] >> (2 * s)) & 3
+        return q, blk[:16] & 0xF, blk[:16] >> 4
+    ql = (blk[32 + 32 * h + l] >> (2 * s)) & 3
+    hb = (blk[l] >> (e >> 5)) & 1
+    sc = blk[96:108]
+    k = np.arange(16)
+    scale = (((sc[k & 7] >> (4 * (k >> 3))) & 0xF) | (((sc[8 + (k & 3)] >> (2 * (k >> 2))) & 3) << 4)) - 32
+    return ql - 4 * (1 - hb), scale, None
+
+
+@pytest.mark.parametrize("t", [O.Q2_K, O.Q3_K])
+def test_block_dots_q2k_q3k(t):
+    """Q2_K / Q3_K x Q8_K per-block integer sums equal numpy integer math."""
+    name, bb = {O.Q2_K: ("q2k", 84), O.Q3_K: ("q3k", 110)}[t]
+    nb = 16
+    w = GOLD[f"{name}_raw"][: nb * bb]
+    x = np.random.default_rng(8).standard_normal(nb * 256).astype(np.float32)
+    xq = O.quant_for(t, x)
+    isum, msum = O.block_dots(t, w, xq, nb)
+    blk = w.reshape(nb, bb)
+    for b in range(nb):
+        q, sc, mn = _q23k(t, blk[b])
+        a = xq[b]["qs"].astype(np.int64)
+        ref_i = int(sum(int(sc[j]) * int((q[16 * j:16 * j + 16] * a[16 * j:16 * j + 16]).sum()) for j in range(16)))
+        assert isum[b] == ref_i
+        if t == O.Q2_K:
+            assert msum[b] == int(sum(int(mn[j]) * int(xq[b]["bsums"][j]) for j in range(16)))
+
+
+@pytest.mark.parametrize("t", [O.Q5_K, O.Q4_0, O.Q5_0, O.Q2_K, O.Q3_K])
 def test_matmul_more_formats_close_to_f64(t):
     """QMatMul semantics for the further formats stay within activation-quantisation noise of
     the f64 product of the dequantised weights (the golden blocks as a weight matrix)."""
-    name, bb, be = {O.Q5_K: ("q5k", 176, 256), O.Q4_0: ("q40", 18, 32), O.Q5_0: ("q50", 22, 32)}[t]
+    name, bb, be = {O.Q5_K: ("q5k", 176, 256), O.Q4_0: ("q40", 18, 32), O.Q5_0: ("q50", 22, 32),
+                    O.Q2_K: ("q2k", 84, 256), O.Q3_K: ("q3k", 110, 256)}[t]
     raw = GOLD[f"{name}_raw"]
     K = 1024
     N = raw.size // bb * be // K

@@ -41,6 +41,8 @@ int64_t raw_row_bytes(int type, int K) {
     case TPTC_TYPE_Q6_K: return (int64_t)K / QK_K * Q6K_BYTES;
     case TPTC_TYPE_Q8_0: return (int64_t)K / QK8_0 * Q80_BYTES;
     case TPTC_TYPE_Q5_K: return (int64_t)K / QK_K * Q5K_BYTES;
+    case TPTC_TYPE_Q2_K: return (int64_t)K / QK_K * Q2K_BYTES;
+    case TPTC_TYPE_Q3_K: return (int64_t)K / QK_K * Q3K_BYTES;
     case TPTC_TYPE_Q4_0: return (int64_t)K / QK8_0 * Q40_BYTES;
     case TPTC_TYPE_Q5_0: return (int64_t)K / QK8_0 * Q50_BYTES;
     case TPTC_TYPE_F16: return (int64_t)K * 2;
@@ -50,8 +52,9 @@ int64_t raw_row_bytes(int type, int K) {
 }
 
 bool matrix_type_ok(int t) {
-    return t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q5_K || t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q4_0 ||
-           t == TPTC_TYPE_Q5_0 || t == TPTC_TYPE_Q8_0 || t == TPTC_TYPE_F16;
+    return t == TPTC_TYPE_Q2_K || t == TPTC_TYPE_Q3_K || t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q5_K ||
+           t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q4_0 || t == TPTC_TYPE_Q5_0 || t == TPTC_TYPE_Q8_0 ||
+           t == TPTC_TYPE_F16;
 }
 
 // Streams host bytes into device memory through two pinned buffers (the reference uploads

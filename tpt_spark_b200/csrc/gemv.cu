@@ -244,6 +244,120 @@ __device__ __forceinline__ float q6k_half(const uint8_t* slot, const uint16_t* d
     return __fmul_rn(dw, xh.dx) * (float)isum;
 }
 
+// The lane's half super-block of Q8_K activations in the natural layout (the DOTS test hook):
+// elements 128h .. 128h + 127 of block c0 + lane / 2 are contiguous there.
+__device__ __forceinline__ void load_xhalf_nat(XHalf& xh, const Act& a, int c0, int lane) {
+    const int sb = lane >> 1, h = lane & 1;
+    const int4* xv = reinterpret_cast<const int4*>(a.q8k + (c0 + sb) * QK_K + 128 * h);
+#pragma unroll
+    for (int v = 0; v < 8; v++) xh.x[v] = xv[v];
+    xh.dx = a.q8k_d[c0 + sb];
+    xh.bs = *reinterpret_cast<const uint4*>(a.q8k_bs + (c0 + sb) * 16 + 8 * h);
+}
+
+// 16-element sum i (0..7) of the lane's half from the Q8_K bsums.
+__device__ __forceinline__ int xh_bsum(const XHalf& xh, int i) {
+    const uint32_t w = i < 2 ? xh.bs.x : i < 4 ? xh.bs.y : i < 6 ? xh.bs.z : xh.bs.w;
+    return (int)(int16_t)((w >> (16 * (i & 1))) & 0xffff);
+}
+
+// Q2_K half super-block (device: qs[64] | scales[16]; d, dmin in the scale section).
+// Element 128h + 32s + l is bits 2s of qs[32h + l]; it pairs with activation vector 2s + (l >= 16)
+// and belongs to 16-element group i = 2s + (l >= 16) of the half, scale byte scales[8h + i]
+// (low nibble: scale, high nibble: min).  isum = sum_i sc_i * dot_i, msum = sum_i m_i * bsum_i.
+__device__ __forceinline__ void q2k_half_ints(const uint8_t* slot, const XHalf& xh, int lane, int& isum, int& msum) {
+    const int sb = lane >> 1, h = lane & 1;
+    const uint8_t* m = slot + sb * 80;
+    const uint4 Q0 = *reinterpret_cast<const uint4*>(m + 32 * h), Q1 = *reinterpret_cast<const uint4*>(m + 32 * h + 16);
+    const uint2 scw = *reinterpret_cast<const uint2*>(m + 64 + 8 * h);
+    const uint32_t m3 = 0x03030303u;
+    int t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#define Q2_WORD(W, K, T0)                                                    \
+    t[T0 + 0] = dp4a_us((W) & m3, xh.x[T0 + 0].K, t[T0 + 0]);                \
+    t[T0 + 2] = dp4a_us(((W) >> 2) & m3, xh.x[T0 + 2].K, t[T0 + 2]);         \
+    t[T0 + 4] = dp4a_us(((W) >> 4) & m3, xh.x[T0 + 4].K, t[T0 + 4]);         \
+    t[T0 + 6] = dp4a_us(((W) >> 6) & m3, xh.x[T0 + 6].K, t[T0 + 6]);
+    Q2_WORD(Q0.x, x, 0) Q2_WORD(Q0.y, y, 0) Q2_WORD(Q0.z, z, 0) Q2_WORD(Q0.w, w, 0)
+    Q2_WORD(Q1.x, x, 1) Q2_WORD(Q1.y, y, 1) Q2_WORD(Q1.z, z, 1) Q2_WORD(Q1.w, w, 1)
+#undef Q2_WORD
+    isum = 0;
+    msum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int g = ubyte(i < 4 ? scw.x : scw.y, i & 3);
+        isum += (g & 0x0f) * t[i];
+        msum += (g >> 4) * xh_bsum(xh, i);
+    }
+}
+
+__device__ __forceinline__ float q2k_half(const uint8_t* slot, const uint16_t* dsec, const XHalf& xh, int lane) {
+    int isum, msum;
+    q2k_half_ints(slot, xh, lane, isum, msum);
+    const int sb = lane >> 1;
+    // candle BlockQ2K: dall = d_x * d_w, dmin = d_x * dmin_w; dall * isum - dmin * msum
+    const float dall = __fmul_rn(xh.dx, h2f(dsec[2 * sb])), dmin = __fmul_rn(xh.dx, h2f(dsec[2 * sb + 1]));
+    return dall * (float)isum - dmin * (float)msum;
+}
+
+// Q3_K half super-block (device: hmask[32] | qs[64]; scales[12] and d in a 14-byte scale
+// entry).  Element 128h + 32s + l: q = ((qs[32h + l] >> 2s) & 3) - 4 * (1 - bit (4h + s) of
+// hmask[l]); sum(q * x) over a 16-element group is dot(ql, x) - 4 * (bsum - dot(hbit, x)).
+// Its 6-bit scale k = 8h + i (minus 32) as the raw-block dequantisation decodes it.
+__device__ __forceinline__ int q3k_half_ints(const uint8_t* slot, const uint16_t* dsec, const XHalf& xh, int lane) {
+    const int sb = lane >> 1, h = lane & 1;
+    const uint8_t* m = slot + sb * 96;
+    const uint4 H0 = *reinterpret_cast<const uint4*>(m), H1 = *reinterpret_cast<const uint4*>(m + 16);
+    const uint4 Q0 = *reinterpret_cast<const uint4*>(m + 32 + 32 * h), Q1 = *reinterpret_cast<const uint4*>(m + 48 + 32 * h);
+    const uint8_t* sc = reinterpret_cast<const uint8_t*>(dsec) + sb * 14;
+    const uint32_t m3 = 0x03030303u, one = 0x01010101u;
+    const int hs = 4 * h;
+    int tq[8] = {0, 0, 0, 0, 0, 0, 0, 0}, th[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#define Q3_ONE(W, H, K, T, S)                                                        \
+    tq[T] = dp4a_us(((W) >> (2 * (S))) & m3, xh.x[T].K, tq[T]);                      \
+    th[T] = dp4a_us(((H) >> (hs + (S))) & one, xh.x[T].K, th[T]);
+#define Q3_WORD(W, H, K, T0) \
+    Q3_ONE(W, H, K, T0 + 0, 0) Q3_ONE(W, H, K, T0 + 2, 1) Q3_ONE(W, H, K, T0 + 4, 2) Q3_ONE(W, H, K, T0 + 6, 3)
+    Q3_WORD(Q0.x, H0.x, x, 0) Q3_WORD(Q0.y, H0.y, y, 0) Q3_WORD(Q0.z, H0.z, z, 0) Q3_WORD(Q0.w, H0.w, w, 0)
+    Q3_WORD(Q1.x, H1.x, x, 1) Q3_WORD(Q1.y, H1.y, y, 1) Q3_WORD(Q1.z, H1.z, z, 1) Q3_WORD(Q1.w, H1.w, w, 1)
+#undef Q3_WORD
+#undef Q3_ONE
+    int isum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int k = 8 * h + i;
+        const int scale = (((sc[k & 7] >> (4 * (k >> 3))) & 0x0f) | (((sc[8 + (k & 3)] >> (2 * (k >> 2))) & 3) << 4)) - 32;
+        isum += scale * (tq[i] - 4 * (xh_bsum(xh, i) - th[i]));
+    }
+    return isum;
+}
+
+__device__ __forceinline__ float q3k_half(const uint8_t* slot, const uint16_t* dsec, const XHalf& xh, int lane) {
+    const int isum = q3k_half_ints(slot, dsec, xh, lane);
+    const uint8_t* sc = reinterpret_cast<const uint8_t*>(dsec) + (lane >> 1) * 14;
+    // candle BlockQ3K: d = d_w * d_x, then d * isum
+    return __fmul_rn(h2f(sc[12] | (sc[13] << 8)), xh.dx) * (float)isum;
+}
+
+// DOTS for Q2_K / Q3_K: the two halves' integers of each super-block added, written by its
+// even lane.
+template <int TYPE>
+__device__ __forceinline__ void dots_q23k(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int cb,
+                                          int lane, int32_t* isum_row, int32_t* msum_row) {
+    int isum = 0, msum = 0;
+    if (lane < 2 * cb) {
+        XHalf xh;
+        load_xhalf_nat(xh, a, c0, lane);
+        if (TYPE == TPTC_TYPE_Q2_K) q2k_half_ints(slot, xh, lane, isum, msum);
+        else isum = q3k_half_ints(slot, dsec, xh, lane);
+    }
+    isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+    msum += __shfl_xor_sync(0xffffffffu, msum, 1);
+    if (lane < 2 * cb && (lane & 1) == 0) {
+        isum_row[c0 + (lane >> 1)] = isum;
+        if (msum_row && TYPE == TPTC_TYPE_Q2_K) msum_row[c0 + (lane >> 1)] = msum;
+    }
+}
+
 template <bool DOTS>
 __device__ __forceinline__ float chunk_q4k(const uint8_t* slot, const Act& a, int c0, int cb, int lane, int first,
                                            int stride, int32_t* isum_row, int32_t* msum_row) {
@@ -881,6 +995,17 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
                 return q5k_half(slot, xh, lane);
             }
             return 0.f;
+        case TPTC_TYPE_Q2_K:
+        case TPTC_TYPE_Q3_K:
+            if (EPI == EPI_DOTS) {
+                if (m.type == TPTC_TYPE_Q2_K) dots_q23k<TPTC_TYPE_Q2_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
+                else dots_q23k<TPTC_TYPE_Q3_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                return m.type == TPTC_TYPE_Q2_K ? q2k_half(slot, dsec, xh, lane) : q3k_half(slot, dsec, xh, lane);
+            }
+            return 0.f;
         case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
@@ -1111,6 +1236,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                 XHalf xh;
                 load_xhalf<false>(xh, a, c0, 2 * cb, lane);
                 return q5k_half(slot, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q2_K:
+        case TPTC_TYPE_Q3_K:
+            if (EPI == EPI_DOTS) {
+                if (m.type == TPTC_TYPE_Q2_K) dots_q23k<TPTC_TYPE_Q2_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
+                else dots_q23k<TPTC_TYPE_Q3_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                return m.type == TPTC_TYPE_Q2_K ? q2k_half(slot, dsec, xh, lane) : q3k_half(slot, dsec, xh, lane);
             }
             return 0.f;
         case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);

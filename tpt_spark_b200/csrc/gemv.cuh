@@ -10,6 +10,8 @@ namespace tptc {
 // before a tile's scale section, and its share of that section; super-blocks per chunk.
 __host__ __device__ inline int sb_main_bytes(int type) {
     switch (type) {
+    case TPTC_TYPE_Q2_K: return 80;
+    case TPTC_TYPE_Q3_K: return 96;
     case TPTC_TYPE_Q4_K: return 144;
     case TPTC_TYPE_Q5_K: return 176;
     case TPTC_TYPE_Q6_K: return 208;
@@ -22,6 +24,8 @@ __host__ __device__ inline int sb_main_bytes(int type) {
 __host__ __device__ inline int sb_d_bytes(int type) {
     switch (type) {
     case TPTC_TYPE_Q6_K: return 2;
+    case TPTC_TYPE_Q2_K: return 4;
+    case TPTC_TYPE_Q3_K: return 14;
     case TPTC_TYPE_Q4_0: case TPTC_TYPE_Q5_0: case TPTC_TYPE_Q8_0: return 16;
     }
     return 0;
@@ -38,6 +42,8 @@ constexpr int kTileRows = 8;
 // Device layout of a weight matrix [N out x K in] (K a multiple of 256).
 //
 // Per-super-block encoding (256 elements):
+//   Q2_K   80 B: qs[64] | scales[16], plus its f16 d and dmin in the scale section
+//   Q3_K   96 B: hmask[32] | qs[64], plus its scales[12] and f16 d (14 B) in the scale section
 //   Q4_K  144 B: the GGUF block unchanged (d | dmin | scales[12] | qs[128])
 //   Q5_K  176 B: the GGUF block unchanged (d | dmin | scales[12] | qh[32] | qs[128])
 //   Q6_K  208 B: ql | qh | scales, plus its f16 d in the tile's scale section
@@ -105,7 +111,8 @@ __host__ __device__ inline const uint8_t* dm_block(const DevMatrix& m, int prow,
     return t + (int64_t)((prow % kTileRows) * cb + j) * sbm;
 }
 
-// f16 scales of super-block `sb` of physical row `prow` (Q6_K: 1, Q4_0 / Q5_0 / Q8_0: 8).
+// Scale-section entry of super-block `sb` of physical row `prow` (Q6_K: d; Q2_K: d, dmin;
+// Q3_K: scales[12] then d; Q4_0 / Q5_0 / Q8_0: the eight blocks' d).
 __host__ __device__ inline const uint16_t* dm_scales(const DevMatrix& m, int prow, int sb) {
     int cb, j;
     const uint8_t* t = dm_tile(m, prow, sb, cb, j);

@@ -95,6 +95,17 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, 
     } else if (m.type == TPTC_TYPE_Q5_K) {
         const uint8_t* src = row + (int64_t)sb * Q5K_BYTES;
         for (int k = 0; k < Q5K_BYTES; k++) dst[k] = src[k];
+    } else if (m.type == TPTC_TYPE_Q2_K) {  // scales[16] qs[64] d dmin -> qs | scales, (d, dmin)
+        const uint8_t* src = row + (int64_t)sb * Q2K_BYTES;
+        for (int k = 0; k < 64; k++) dst[k] = src[16 + k];
+        for (int k = 0; k < 16; k++) dst[64 + k] = src[k];
+        uint8_t* dsc = reinterpret_cast<uint8_t*>(const_cast<uint16_t*>(dm_scales(m, prow, sb)));
+        for (int k = 0; k < 4; k++) dsc[k] = src[80 + k];
+    } else if (m.type == TPTC_TYPE_Q3_K) {  // hmask[32] qs[64] | scales[12] d
+        const uint8_t* src = row + (int64_t)sb * Q3K_BYTES;
+        for (int k = 0; k < 96; k++) dst[k] = src[k];
+        uint8_t* dsc = reinterpret_cast<uint8_t*>(const_cast<uint16_t*>(dm_scales(m, prow, sb)));
+        for (int k = 0; k < 14; k++) dsc[k] = src[96 + k];
     } else if (m.type == TPTC_TYPE_Q4_0) {
         uint16_t* dsc = const_cast<uint16_t*>(dm_scales(m, prow, sb));
         for (int j = 0; j < 8; j++) {
@@ -178,7 +189,7 @@ __global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, int phy
 #pragma unroll
         for (int b = 0; b < 32; b++) v[b] = __float2half_rn(__fmul_rn((float)q[b], d));
     } else {
-        // Q5_K, Q4_0, Q5_0: the element values of dm_elem (one group of 32, rounded to fp16)
+        // Q2_K, Q3_K, Q5_K, Q4_0, Q5_0: the element values of dm_elem (one group of 32, rounded to fp16)
 #pragma unroll 8
         for (int b = 0; b < 32; b++) v[b] = __float2half_rn(dm_elem(m, prow, k0 + b));
     }

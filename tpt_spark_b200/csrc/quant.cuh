@@ -206,6 +206,21 @@ __device__ __forceinline__ float dm_elem(const DevMatrix& m, int prow, int i) {
     case TPTC_TYPE_Q6_K: return q6k_elem(blk, h2f(dm_scales(m, prow, sb)[0]), e);
     case TPTC_TYPE_Q8_0:
         return __fmul_rn((float)(int8_t)blk[e], h2f(dm_scales(m, prow, sb)[e / QK8_0]));
+    case TPTC_TYPE_Q2_K: {  // device: qs[64] | scales[16]; d, dmin in the scale section
+        const uint16_t* dd = dm_scales(m, prow, sb);
+        const int q = (blk[32 * (e >> 7) + (e & 31)] >> (2 * ((e >> 5) & 3))) & 3, g = blk[64 + (e >> 4)];
+        return __fsub_rn(__fmul_rn(__fmul_rn(h2f(dd[0]), (float)(g & 0x0f)), (float)q),
+                         __fmul_rn(h2f(dd[1]), (float)(g >> 4)));
+    }
+    case TPTC_TYPE_Q3_K: {  // device: hmask[32] | qs[64]; scales[12] and d in the scale section
+        const uint8_t* sc = reinterpret_cast<const uint8_t*>(dm_scales(m, prow, sb));
+        const int h = e >> 7, sh = (e >> 5) & 3, l = e & 31, k = e >> 4;
+        const int ql = (blk[32 + 32 * h + l] >> (2 * sh)) & 3;
+        const int hb = (blk[l] >> (e >> 5)) & 1;
+        const int scale =
+            (((sc[k & 7] >> (4 * (k >> 3))) & 0x0f) | (((sc[8 + (k & 3)] >> (2 * (k >> 2))) & 3) << 4)) - 32;
+        return __fmul_rn(__fmul_rn(h2f(sc[12] | (sc[13] << 8)), (float)scale), (float)(ql - ((hb ^ 1) << 2)));
+    }
     case TPTC_TYPE_Q4_0: {
         const int j = e / QK8_0;
         return __fmul_rn(h2f(dm_scales(m, prow, sb)[j]), (float)(q4_nibble(blk + 16 * j, e % QK8_0) - 8));

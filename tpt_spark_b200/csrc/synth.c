@@ -25,7 +25,7 @@
 #include <stdint.h>
 #include <string.h>
 
-enum { SY_F32 = 0, SY_F16 = 1, SY_Q4_0 = 2, SY_Q5_0 = 6, SY_Q8_0 = 8, SY_Q4_K = 12, SY_Q5_K = 13, SY_Q6_K = 14 };
+enum { SY_F32 = 0, SY_F16 = 1, SY_Q4_0 = 2, SY_Q5_0 = 6, SY_Q8_0 = 8, SY_Q2_K = 10, SY_Q3_K = 11, SY_Q4_K = 12, SY_Q5_K = 13, SY_Q6_K = 14 };
 
 static inline uint64_t splitmix64(uint64_t x) {
     x += 0x9E3779B97F4A7C15ull;
@@ -211,6 +211,73 @@ static void enc_q5k(const float* x, uint8_t* b) {
         for (int l = 0; l < 32; l++) qs[32 * g + l] = (uint8_t)((q[64 * g + l] & 0x0f) | ((q[64 * g + 32 + l] & 0x0f) << 4));
 }
 
+/* Q2_K (scales[16] qs[64] d dmin): per 16-element group an unsigned 4-bit scale and min over
+ * 2-bit codes, value (d*sc)*q - (dmin*m). */
+static void enc_q2k(const float* x, uint8_t* b) {
+    float sc_f[16], mn_f[16], max_sc = 0.f, max_mn = 0.f;
+    for (int g = 0; g < 16; g++) {
+        float mn = x[16 * g], mx = x[16 * g];
+        for (int l = 1; l < 16; l++) {
+            mn = fminf(mn, x[16 * g + l]);
+            mx = fmaxf(mx, x[16 * g + l]);
+        }
+        if (mn > 0.f) mn = 0.f;
+        sc_f[g] = (mx - mn) / 3.f;
+        mn_f[g] = -mn;
+        max_sc = fmaxf(max_sc, sc_f[g]);
+        max_mn = fmaxf(max_mn, mn_f[g]);
+    }
+    const uint16_t dh = f2h(max_sc / 15.f), mh = f2h(max_mn / 15.f);
+    const float d = h2f(dh), dm = h2f(mh);
+    memset(b, 0, 84);
+    for (int g = 0; g < 16; g++) {
+        const int sc = d > 0.f ? clampi((int)lroundf(sc_f[g] / d), 0, 15) : 0;
+        const int m = dm > 0.f ? clampi((int)lroundf(mn_f[g] / dm), 0, 15) : 0;
+        b[g] = (uint8_t)(sc | (m << 4));
+        const float es = d * (float)sc, em = dm * (float)m;
+        for (int l = 0; l < 16; l++) {
+            const int e = 16 * g + l;
+            const int q = es > 0.f ? clampi((int)lroundf((x[e] + em) / es), 0, 3) : 0;
+            b[16 + 32 * (e >> 7) + (e & 31)] |= (uint8_t)(q << (2 * ((e >> 5) & 3)));
+        }
+    }
+    b[80] = (uint8_t)(dh & 0xff);
+    b[81] = (uint8_t)(dh >> 8);
+    b[82] = (uint8_t)(mh & 0xff);
+    b[83] = (uint8_t)(mh >> 8);
+}
+
+/* Q3_K (hmask[32] qs[64] scales[12] d): per 16-element group a signed 6-bit scale over codes
+ * -4..3 stored as 2 low bits plus the hmask bit (set when the code is >= 0). */
+static void enc_q3k(const float* x, uint8_t* b) {
+    float sc_f[16], amax_sc = 0.f;
+    for (int g = 0; g < 16; g++) {
+        float mx = 0.f, amx = 0.f;
+        for (int l = 0; l < 16; l++)
+            if (fabsf(x[16 * g + l]) > amx) { amx = fabsf(x[16 * g + l]); mx = x[16 * g + l]; }
+        sc_f[g] = mx / -4.f;
+        amax_sc = fmaxf(amax_sc, fabsf(sc_f[g]));
+    }
+    const uint16_t dh = f2h(amax_sc / 31.f);
+    const float d = h2f(dh);
+    memset(b, 0, 110);
+    for (int g = 0; g < 16; g++) {
+        const int sc = d > 0.f ? clampi((int)lroundf(sc_f[g] / d), -32, 31) : 0;
+        const int u = sc + 32;
+        b[96 + (g & 7)] |= (uint8_t)((u & 0x0f) << (4 * (g >> 3)));
+        b[96 + 8 + (g & 3)] |= (uint8_t)(((u >> 4) & 3) << (2 * (g >> 2)));
+        const float es = d * (float)sc;
+        for (int l = 0; l < 16; l++) {
+            const int e = 16 * g + l;
+            const int q = es != 0.f ? clampi((int)lroundf(x[e] / es), -4, 3) : 0;
+            b[32 + 32 * (e >> 7) + (e & 31)] |= (uint8_t)(((q + 4) & 3) << (2 * ((e >> 5) & 3)));
+            if (q >= 0) b[e & 31] |= (uint8_t)(1 << (e >> 5));
+        }
+    }
+    b[108] = (uint8_t)(dh & 0xff);
+    b[109] = (uint8_t)(dh >> 8);
+}
+
 static void enc_q6k(const float* x, uint8_t* b) {
     float scales[16], max_scale = 0.f, amax_scale = 0.f;
     for (int j = 0; j < 16; j++) {
@@ -261,6 +328,8 @@ int64_t sy_type_bytes(int type, int64_t n) {
     case SY_Q4_0: return n / 32 * 18;
     case SY_Q5_0: return n / 32 * 22;
     case SY_Q5_K: return n / 256 * 176;
+    case SY_Q2_K: return n / 256 * 84;
+    case SY_Q3_K: return n / 256 * 110;
     }
     return -1;
 }
@@ -305,6 +374,16 @@ int64_t sy_encode(int type, const float* x, int64_t n, uint8_t* out) {
 #pragma omp parallel for schedule(static)
         for (int64_t i = 0; i < nb; i++) enc_q5k(x + 256 * i, out + 176 * i);
         return nb * 176;
+    case SY_Q2_K:
+        nb = n / 256;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < nb; i++) enc_q2k(x + 256 * i, out + 84 * i);
+        return nb * 84;
+    case SY_Q3_K:
+        nb = n / 256;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < nb; i++) enc_q3k(x + 256 * i, out + 110 * i);
+        return nb * 110;
     }
     return -1;
 }

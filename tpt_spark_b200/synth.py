@@ -26,11 +26,11 @@ import numpy as np
 from ._build import lib_path
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
-Q4_0, Q5_0, Q5_K = 2, 6, 13
+Q4_0, Q5_0, Q5_K, Q2_K, Q3_K = 2, 6, 13, 10, 11
 BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q4_0: (32, 18),
-         Q5_0: (32, 22), Q5_K: (256, 176)}
+         Q5_0: (32, 22), Q5_K: (256, 176), Q2_K: (256, 84), Q3_K: (256, 110)}
 TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q4_0: "Q4_0", Q5_0: "Q5_0",
-              Q5_K: "Q5_K"}
+              Q5_K: "Q5_K", Q2_K: "Q2_K", Q3_K: "Q3_K"}
 ALIGN = 32
 
 
@@ -146,6 +146,11 @@ TINY: Dict[str, ModelConfig] = {
         "tiny_q4_0", dim=256, n_layers=2, n_heads=4, n_kv_heads=4, ffn=512, vocab=352,
         rope_base=10000.0, context_length=512, default_type=Q4_0,
         overrides=(("attn_v", Q5_0), ("ffn_down", Q5_0)), embd_type=Q4_0, output_type=Q5_0, norm_std=0.1),
+    # Q2_K with Q3_K attn_v / ffn_down and a Q4_K output (the mix of llama.cpp's Q2_K files)
+    "tiny_q2k": ModelConfig(
+        "tiny_q2k", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=416,
+        rope_base=10000.0, context_length=512, default_type=Q2_K,
+        overrides=(("attn_v", Q3_K), ("ffn_down", Q3_K)), embd_type=Q2_K, output_type=Q4_K, norm_std=0.1),
     "tiny_tp_q4km": ModelConfig(
         "tiny_tp_q4km", dim=512, n_layers=2, n_heads=8, n_kv_heads=4, ffn=1024, vocab=384,
         rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
