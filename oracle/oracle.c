@@ -915,6 +915,11 @@ typedef struct {
     float rope_base, rms_eps, rope_scale;
     const void** tensors;
     const int* types;
+    /* qwen2 (candle quantized_qwen2): f32 q / k / v biases added after each projection
+     * (biases[3l .. 3l+2], entries NULL when absent, the array NULL for none), and RoPE on
+     * the two halves of each head (candle_nn::rotary_emb::rope) instead of interleaved pairs. */
+    const float** biases;
+    int rope_neox;
 } or_model_desc;
 
 typedef struct {
@@ -926,6 +931,7 @@ typedef struct {
     float* sin_t;
     float* kc;      /* [L, max_seq, n_kv, hd] f32 */
     float* vc;
+    const float** b;  /* copy of desc->biases, or NULL */
     int n_past;
 } or_model;
 
@@ -956,6 +962,11 @@ void* or_model_create(const or_model_desc* desc) {
     memcpy(m->ty, desc->types, sizeof(int) * nt);
     m->d.tensors = m->t;
     m->d.types = m->ty;
+    if (desc->biases) {
+        m->b = (const float**)malloc(sizeof(float*) * 3 * desc->n_layers);
+        memcpy(m->b, desc->biases, sizeof(float*) * 3 * desc->n_layers);
+    }
+    m->d.biases = m->b;
     size_t ne = (size_t)desc->vocab * desc->dim;
     m->embd = (float*)malloc(ne * sizeof(float));
     or_dequant(m->ty[0], m->t[0], (int64_t)ne, m->embd);
@@ -973,6 +984,7 @@ void or_model_destroy(void* p) {
     or_model* m = (or_model*)p;
     if (!m) return;
     free(m->t); free(m->ty); free(m->embd); free(m->cos_t); free(m->sin_t); free(m->kc); free(m->vc);
+    free((void*)m->b);
     free(m);
 }
 
@@ -1008,6 +1020,23 @@ static void rope_i(float* v, int hd, const float* c, const float* s) {
     }
 }
 
+/* candle_nn::rotary_emb::rope on one head vector: element i pairs with i + hd/2. */
+static void rope_neox(float* v, int hd, const float* c, const float* s) {
+    const int half = hd / 2;
+    for (int i = 0; i < half; i++) {
+        float x0 = v[i], x1 = v[i + half];
+        v[i] = x0 * c[i] - x1 * s[i];
+        v[i + half] = x0 * s[i] + x1 * c[i];
+    }
+}
+
+/* y[r][i] += b[i] for n rows of width w (candle's broadcast_add of a projection bias). */
+static void add_bias(float* y, const float* b, int n, int w) {
+    if (!b) return;
+    for (int r = 0; r < n; r++)
+        for (int i = 0; i < w; i++) y[(size_t)r * w + i] += b[i];
+}
+
 /* One forward call: tokens[0..n) at absolute positions pos..pos+n-1, attending the
  * cached positions [0, pos).  Writes the last position's logits [vocab] and, when
  * hidden_out is non-NULL, the final-normed hidden state of the last position [dim].
@@ -1039,13 +1068,24 @@ int or_forward(void* p, const uint32_t* tokens, int n, int pos, float* logits, f
         or_matmul(Ty[1], T[1], qd, dim, xn, n, q);
         or_matmul(Ty[2], T[2], kvd, dim, xn, n, k);
         or_matmul(Ty[3], T[3], kvd, dim, xn, n, v);
+        if (m->b) {
+            add_bias(q, m->b[3 * l], n, qd);
+            add_bias(k, m->b[3 * l + 1], n, kvd);
+            add_bias(v, m->b[3 * l + 2], n, kvd);
+        }
         float* kc = m->kc + (size_t)l * d->max_seq * kvd;
         float* vc = m->vc + (size_t)l * d->max_seq * kvd;
         for (int i = 0; i < n; i++) {
             const float* c = m->cos_t + (size_t)(pos + i) * half;
             const float* s = m->sin_t + (size_t)(pos + i) * half;
-            for (int h = 0; h < nh; h++) rope_i(q + (size_t)i * qd + h * hd, hd, c, s);
-            for (int h = 0; h < nkv; h++) rope_i(k + (size_t)i * kvd + h * hd, hd, c, s);
+            for (int h = 0; h < nh; h++) {
+                if (d->rope_neox) rope_neox(q + (size_t)i * qd + h * hd, hd, c, s);
+                else rope_i(q + (size_t)i * qd + h * hd, hd, c, s);
+            }
+            for (int h = 0; h < nkv; h++) {
+                if (d->rope_neox) rope_neox(k + (size_t)i * kvd + h * hd, hd, c, s);
+                else rope_i(k + (size_t)i * kvd + h * hd, hd, c, s);
+            }
             memcpy(kc + (size_t)(pos + i) * kvd, k + (size_t)i * kvd, sizeof(float) * kvd);
             memcpy(vc + (size_t)(pos + i) * kvd, v + (size_t)i * kvd, sizeof(float) * kvd);
         }

@@ -36,7 +36,8 @@ class _Desc(ctypes.Structure):
                 ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("ffn", ctypes.c_int),
                 ("vocab", ctypes.c_int), ("max_seq", ctypes.c_int), ("rope_base", ctypes.c_float),
                 ("rms_eps", ctypes.c_float), ("rope_scale", ctypes.c_float),
-                ("tensors", ctypes.POINTER(ctypes.c_void_p)), ("types", ctypes.POINTER(ctypes.c_int))]
+                ("tensors", ctypes.POINTER(ctypes.c_void_p)), ("types", ctypes.POINTER(ctypes.c_int)),
+                ("biases", ctypes.POINTER(ctypes.c_void_p)), ("rope_neox", ctypes.c_int)]
 
 
 _L = None
@@ -168,7 +169,8 @@ def repeat_penalty(logits: np.ndarray, seen: Sequence[int], penalty: float) -> n
 
 
 class Model:
-    """candle quantized_llama restated on CPU over a GGUF file (read with gguf-py)."""
+    """candle quantized_llama (architectures llama / mistral) or quantized_qwen2 (qwen2: q / k /
+    v biases, RoPE on head halves) restated on CPU over a GGUF file (read with gguf-py)."""
 
     def __init__(self, path: str, max_seq: Optional[int] = None):
         import gguf
@@ -208,9 +210,17 @@ class Model:
         ptrs = (ctypes.c_void_p * len(order))(*[a.ctypes.data for a in self._arrays])
         tys = (ctypes.c_int * len(order))(*self._types)
         self.max_seq = max_seq or self.context_length
+        self.arch = arch
+        bnames = [f"blk.{i}.attn_{w}.bias" for i in range(self.n_layers) for w in ("q", "k", "v")]
+        self._biases = [np.ascontiguousarray(tensors[n].data, np.float32) if n in tensors else None for n in bnames]
+        barr = None
+        if any(b is not None for b in self._biases):
+            barr = (ctypes.c_void_p * len(bnames))(*[b.ctypes.data if b is not None else None for b in self._biases])
         d = _Desc(self.n_layers, self.dim, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.vocab,
-                  self.max_seq, self.rope_base, self.rms_eps, 1.0, ptrs, tys)
-        self._keep = (ptrs, tys)
+                  self.max_seq, self.rope_base, self.rms_eps, 1.0, ptrs, tys,
+                  ctypes.cast(barr, ctypes.POINTER(ctypes.c_void_p)) if barr is not None else None,
+                  1 if arch == "qwen2" else 0)
+        self._keep = (ptrs, tys, barr)
         self.h = lib().or_model_create(ctypes.byref(d))
 
     def forward(self, tokens: Sequence[int], pos: int, want_hidden: bool = False):

@@ -61,7 +61,7 @@ def engines_f16kv(tiny_models, cuda_device):
         e.close()
 
 
-MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k"]
+MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2"]
 
 
 @pytest.mark.parametrize("name", MODELS)

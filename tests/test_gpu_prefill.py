@@ -20,7 +20,7 @@ from tpt_spark_b200._lib import EngineError  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k"]
+MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2"]
 
 # fp16 operands (11-bit significands) against a float64 forward: relative error of a few
 # 2^-11 per layer on the hidden state, times the logit scale of the tiny models (|logit| < 3)
@@ -118,18 +118,33 @@ def float_prefill_logits(ref, tokens):
     def rms(x, g):
         return x / np.sqrt((x * x).mean(-1, keepdims=True) + ref.rms_eps) * g
 
-    def rope(x, n):  # [T, n*hd], interleaved pairs
-        x = x.reshape(T, n, hd // 2, 2)
+    neox = getattr(ref, "arch", "llama") == "qwen2"
+
+    def rope(x, n):  # [T, n*hd]: interleaved pairs (rope_i), or the head's two halves (qwen2)
         c, s = cos[:, None, :], sin[:, None, :]
+        if neox:
+            x = x.reshape(T, n, 2, hd // 2)
+            r0 = x[:, :, 0] * c - x[:, :, 1] * s
+            r1 = x[:, :, 0] * s + x[:, :, 1] * c
+            return np.concatenate([r0, r1], -1).reshape(T, n, hd)
+        x = x.reshape(T, n, hd // 2, 2)
         r0 = x[..., 0] * c - x[..., 1] * s
         r1 = x[..., 0] * s + x[..., 1] * c
         return np.stack([r0, r1], -1).reshape(T, n, hd)
 
+    biases = getattr(ref, "_biases", None) or [None] * (3 * ref.n_layers)
+
+    def bias(i):
+        b = biases[i]
+        return 0.0 if b is None else b.astype(np.float64)
+
     x = w["emb"][np.asarray(tokens)]
     mask = np.triu(np.full((T, T), -np.inf), 1)
-    for L in w["layers"]:
+    for li, L in enumerate(w["layers"]):
         xn = rms(x, L["attn_norm"])
-        q, k, v = rope(xn @ L["q"].T, H), rope(xn @ L["k"].T, KV), (xn @ L["v"].T).reshape(T, KV, hd)
+        q = rope(xn @ L["q"].T + bias(3 * li), H)
+        k = rope(xn @ L["k"].T + bias(3 * li + 1), KV)
+        v = (xn @ L["v"].T + bias(3 * li + 2)).reshape(T, KV, hd)
         att = np.empty((T, H, hd))
         for h in range(H):
             s = q[:, h] @ k[:, h // G].T / np.sqrt(hd) + mask

@@ -236,12 +236,13 @@ def test_argmax_ties_last_and_repeat_penalty():
     np.testing.assert_array_equal(O.repeat_penalty(lg, [1], 1.0), lg)
 
 
-def test_forward_prefill_equals_incremental(tmp_path):
+@pytest.mark.parametrize("name", ["tiny_q4km", "tiny_qwen2"])
+def test_forward_prefill_equals_incremental(tmp_path, name):
     """candle's batched prefill and one-token steps give the same last-position logits."""
     from tpt_spark_b200 import synth
 
     p = str(tmp_path / "m.gguf")
-    synth.write_gguf(p, synth.TINY["tiny_q4km"], seed=3)
+    synth.write_gguf(p, synth.TINY[name], seed=3)
     toks = [5, 17, 300, 42, 7, 99]
     a = O.Model(p)
     la = a.forward(toks, 0)
@@ -250,6 +251,25 @@ def test_forward_prefill_equals_incremental(tmp_path):
         lb = b.forward([t], i)
     # same math; only the attention mask path differs
     np.testing.assert_allclose(la, lb, rtol=0, atol=1e-4)
+
+
+def test_qwen2_oracle_uses_bias_and_half_rope(tmp_path):
+    """The qwen2 path is not the llama path: zeroing the biases or switching the RoPE pairing
+    changes the logits (the restatement reads both)."""
+    from tpt_spark_b200 import synth
+
+    import dataclasses
+
+    cfg = synth.TINY["tiny_qwen2"]
+    p, p0, pl = (str(tmp_path / f) for f in ("q.gguf", "q0.gguf", "ql.gguf"))
+    synth.write_gguf(p, cfg, seed=1)
+    synth.write_gguf(p0, dataclasses.replace(cfg, bias_std=0.0), seed=1)  # zero biases
+    synth.write_gguf(pl, dataclasses.replace(cfg, arch="llama"), seed=1)  # rope_i pairs, same weights
+    toks = [5, 17, 300, 42]
+    base = O.Model(p).forward(toks, 0)
+    assert O.Model(p).arch == "qwen2"
+    assert np.abs(O.Model(p0).forward(toks, 0) - base).max() > 1e-3
+    assert np.abs(O.Model(pl).forward(toks, 0) - base).max() > 1e-3
 
 
 @pytest.mark.parametrize("t,N,K", [(O.Q4_K, 48, 4096), (O.Q6_K, 40, 14336), (O.Q8_0, 33, 4096)])

@@ -404,21 +404,23 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     pdl_wait();
     pdl_launch_dependents();
 
-    // RoPE (candle rope_i: interleaved pairs, x0*c - x1*s, x0*s + x1*c) on the group's
-    // queries, staged in shared memory
+    // RoPE (candle rope_i: interleaved pairs, x0*c - x1*s, x0*s + x1*c; with rope_neox the
+    // pairs are elements j and j + hd/2, candle rope) on the group's queries, staged in
+    // shared memory
     const float* cs = p.rope_cos + (int64_t)pos * half;
     const float* sn = p.rope_sin + (int64_t)pos * half;
     for (int i = tid; i < G * half; i += kThreads) {
         const int g = i / half, j = i % half;
         const float* qg = p.q + (int64_t)(kvh * G + g) * HD;
-        const float q0 = qg[2 * j], q1 = qg[2 * j + 1], c = cs[j], s = sn[j];
+        const int ia = p.rope_neox ? j : 2 * j, ib = p.rope_neox ? j + half : 2 * j + 1;  // the rotated pair
+        const float q0 = qg[ia], q1 = qg[ib], c = cs[j], s = sn[j];
         const float r0 = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
         const float r1 = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
-        qs[g * HD + 2 * j] = r0;
-        qs[g * HD + 2 * j + 1] = r1;
+        qs[g * HD + ia] = r0;
+        qs[g * HD + ib] = r1;
         if (p.q_out && split == 0) {
-            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j] = r0;
-            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j + 1] = r1;
+            p.q_out[(int64_t)(kvh * G + g) * HD + ia] = r0;
+            p.q_out[(int64_t)(kvh * G + g) * HD + ib] = r1;
         }
     }
     // The owner rotates this step's key and stores it in the cache; the proxy fence orders
@@ -426,9 +428,10 @@ __global__ void __launch_bounds__(kThreads, GM <= 4 ? 2 : 1) attn_decode_kernel(
     if (owner) {
         KV* krow = static_cast<KV*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * HD;
         for (int j = tid; j < half; j += kThreads) {
-            const float k0 = p.kraw[kvh * HD + 2 * j], k1 = p.kraw[kvh * HD + 2 * j + 1], c = cs[j], s = sn[j];
-            Tr::store(krow + 2 * j, __fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
-            Tr::store(krow + 2 * j + 1, __fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
+            const int ia = p.rope_neox ? j : 2 * j, ib = p.rope_neox ? j + half : 2 * j + 1;
+            const float k0 = p.kraw[kvh * HD + ia], k1 = p.kraw[kvh * HD + ib], c = cs[j], s = sn[j];
+            Tr::store(krow + ia, __fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
+            Tr::store(krow + ib, __fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
     }
@@ -733,25 +736,27 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (t != tile_pos) issue(t);
     }
     bool ok = mbar_wait_bounded(&qbar, 0, p.err);
-    // RoPE on the group's queries (candle rope_i), in place
+    // RoPE on the group's queries (candle rope_i, or rope with rope_neox), in place
     for (int i = tid; i < G * half && ok; i += kThreads) {
         const int g = i / half, j = i % half;
-        const float q0 = qs[g * HD + 2 * j], q1 = qs[g * HD + 2 * j + 1], c = csn[j], s = csn[half + j];
+        const int ia = p.rope_neox ? j : 2 * j, ib = p.rope_neox ? j + half : 2 * j + 1;  // the rotated pair
+        const float q0 = qs[g * HD + ia], q1 = qs[g * HD + ib], c = csn[j], s = csn[half + j];
         const float r0 = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
         const float r1 = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
-        qs[g * HD + 2 * j] = r0;
-        qs[g * HD + 2 * j + 1] = r1;
+        qs[g * HD + ia] = r0;
+        qs[g * HD + ib] = r1;
         if (p.q_out && split == 0) {
-            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j] = r0;
-            p.q_out[(int64_t)(kvh * G + g) * HD + 2 * j + 1] = r1;
+            p.q_out[(int64_t)(kvh * G + g) * HD + ia] = r0;
+            p.q_out[(int64_t)(kvh * G + g) * HD + ib] = r1;
         }
     }
     if (owner && ok) {  // this step's key, rotated, into the cache before any read of its tile
         __half* krow = static_cast<__half*>(p.kcache) + ((int64_t)kvh * p.max_seq + pos) * HD;
         for (int j = tid; j < half; j += kThreads) {
-            const float k0 = kr[2 * j], k1 = kr[2 * j + 1], c = csn[j], s = csn[half + j];
-            krow[2 * j] = __float2half_rn(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
-            krow[2 * j + 1] = __float2half_rn(__fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
+            const int ia = p.rope_neox ? j : 2 * j, ib = p.rope_neox ? j + half : 2 * j + 1;
+            const float k0 = kr[ia], k1 = kr[ib], c = csn[j], s = csn[half + j];
+            krow[ia] = __float2half_rn(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
+            krow[ib] = __float2half_rn(__fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
         }
         asm volatile("fence.proxy.async.global;" ::: "memory");
     }

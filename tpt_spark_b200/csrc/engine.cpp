@@ -204,12 +204,15 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
     int rc = f.open(path, emsg);
     if (rc != TPTC_OK) return err(rc, emsg);
 
-    // ---- metadata (wgpu_loader.rs:305-406; candle_engine.rs:145-165 arch check)
+    // ---- metadata (wgpu_loader.rs:305-406; candle_engine.rs:145-165 arch check).  qwen2 is
+    // llama's forward with q / k / v biases and RoPE on head halves (candle quantized_qwen2;
+    // the reference runs it on its wgpu path, wgpu_loader.rs:270, bias_add.wgsl).
     ModelMeta m;
     f.get_str("general.architecture", m.architecture);
-    if (m.architecture != "llama" && m.architecture != "mistral")
+    if (m.architecture != "llama" && m.architecture != "mistral" && m.architecture != "qwen2")
         return err(TPTC_ERR_UNSUPPORTED, "Architecture '" + m.architecture +
-                                             "' is not yet supported. Supported: llama, mistral.");
+                                             "' is not yet supported. Supported: llama, mistral, qwen2.");
+    m.rope_neox = m.architecture == "qwen2";
     f.get_str("general.name", m.name);
     const std::string a = m.architecture;
     uint64_t u;
@@ -249,6 +252,7 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
                       sh[w][2], sh[w][3]))
             return err(TPTC_ERR_UNSUPPORTED, "model does not shard evenly over tp_size=" + std::to_string(tp_size_));
     m.tied = f.find("output.weight") == nullptr;
+    m.qkv_bias = f.find("blk.0.attn_q.bias") != nullptr;
     meta_ = m;
     path_ = path;
     file_bytes_ = f.size;
@@ -284,6 +288,14 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         W(TPTC_SHARD_Q, "attn_q.weight", m.n_heads * hd, m.dim, &L.q, 0, 0);
         W(TPTC_SHARD_K, "attn_k.weight", m.n_kv_heads * hd, m.dim, &L.k, 0, 0);
         W(TPTC_SHARD_V, "attn_v.weight", m.n_kv_heads * hd, m.dim, &L.v, 0, 0);
+        if (m.qkv_bias) {  // f32 vectors: this rank keeps the rows of its weight window
+            auto B = [&](int w, const char* name, int N, float** dst) {
+                plans.push_back({p + name, 1, N, 0, 1, sh[w][0], sh[w][1], nullptr, dst, 0, 0});
+            };
+            B(TPTC_SHARD_Q, "attn_q.bias", m.n_heads * hd, &L.bq);
+            B(TPTC_SHARD_K, "attn_k.bias", m.n_kv_heads * hd, &L.bk);
+            B(TPTC_SHARD_V, "attn_v.bias", m.n_kv_heads * hd, &L.bv);
+        }
         W(TPTC_SHARD_O, "attn_output.weight", m.dim, m.n_heads * hd, &L.o, 0, 0);
         plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm, 0, 0});
         W(TPTC_SHARD_GATE, "ffn_gate.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l);
@@ -320,9 +332,9 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
                             : (t->ne.size() == 2 && t->ne[0] == want0 && t->ne[1] == want1);
         if (!shape_ok) return err(TPTC_ERR_FORMAT, "tensor '" + p.name + "' has an unexpected shape");
         if (vec) {
-            if (t->type != TPTC_TYPE_F32) return err(TPTC_ERR_UNSUPPORTED, "norm tensor '" + p.name + "' must be F32");
+            if (t->type != TPTC_TYPE_F32) return err(TPTC_ERR_UNSUPPORTED, "vector tensor '" + p.name + "' must be F32");
             offs[i] = off;
-            off = align_up(off + (size_t)p.K * 4, 256);
+            off = align_up(off + (size_t)(p.k1 - p.k0) * 4, 256);
             continue;
         }
         if (!matrix_type_ok((int)t->type))
@@ -359,8 +371,8 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
             DevMatrix tmp;
             tmp.type = TPTC_TYPE_F32;
             tmp.main = arena_ + offs[i];
-            RET_IF(upload_rows(sg, src, (int64_t)p.K * 4, 0, 1, 0, (int64_t)p.K * 4, tmp, 0));
-            weight_bytes_ += (uint64_t)p.K * 4;
+            RET_IF(upload_rows(sg, src, (int64_t)p.K * 4, 0, 1, (int64_t)p.k0 * 4, (int64_t)p.k1 * 4, tmp, 0));
+            weight_bytes_ += (uint64_t)(p.k1 - p.k0) * 4;
         } else {
             DevMatrix& d = *p.mat;
             if (!(p.glu_rows && p.first_row > 0)) {
@@ -517,6 +529,9 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         p.pos = pos_;
         p.hd = hd;
         p.max_seq = max_seq_;
+        p.bias[0] = W.bq;
+        p.bias[1] = W.bk;
+        p.bias[2] = W.bv;
         gemv_prepare(p, sm_count_);
         return p;
     };
@@ -589,6 +604,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         a.splits = attn_splits_;
         a.scale = (float)(1.0 / sqrt((double)hd));
         a.err = err_;
+        a.rope_neox = m.rope_neox ? 1 : 0;
         if ((n_heads_l_ / n_kv_l_) * hd % 256 == 0) {
             a.act_out = act_;
             a.act = o.act;

@@ -24,6 +24,8 @@ struct ModelMeta {
     int context_length = 4096, n_layers = 0, n_heads = 0, n_kv_heads = 0, head_dim = 0, dim = 0, ffn = 0, vocab = 0;
     float rope_freq_base = 10000.f, rope_scale = 1.f, rms_eps = 1e-5f;
     bool tied = false;
+    bool rope_neox = false;  // qwen2: RoPE pairs element i with i + head_dim / 2 (candle rope)
+    bool qkv_bias = false;   // qwen2: f32 attn_q / attn_k / attn_v biases
 };
 
 struct LayerWeights {
@@ -31,6 +33,9 @@ struct LayerWeights {
     DevMatrix glu;  // fused ffn_gate | ffn_up (gemv.cuh): logical rows [0, ffn) gate, [ffn, 2 ffn) up
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
+    float* bq = nullptr;  // this rank's rows of the q / k / v biases (qwen2), or nullptr
+    float* bk = nullptr;
+    float* bv = nullptr;
 };
 
 struct Tp;  // tensor-parallel communicator (tp.cpp)

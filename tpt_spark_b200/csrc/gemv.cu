@@ -942,15 +942,17 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
                 p.out[ur.out] = __ldcg(p.out + ur.out) + y;
             }
         } else if (EPI == EPI_QKV) {
+            const float* bias = p.bias[ur.seg];
+            const float yb = bias ? __fadd_rn(y, bias[ur.row]) : y;  // candle QLinear: matmul, then + bias
             if (ur.seg == 0) {
-                p.out[ur.row] = y;  // q before RoPE
+                p.out[ur.row] = yb;  // q before RoPE
             } else if (ur.seg == 1) {
-                p.kraw[ur.row] = y;  // k before RoPE
+                p.kraw[ur.row] = yb;  // k before RoPE
             } else {
                 const int pos = *p.pos, d = ur.row % p.hd, head = ur.row / p.hd;
                 const int64_t at = ((int64_t)head * p.max_seq + pos) * p.hd + d;
-                if (p.kv_f32) static_cast<float*>(p.vcache)[at] = y;
-                else static_cast<__half*>(p.vcache)[at] = __float2half_rn(y);
+                if (p.kv_f32) static_cast<float*>(p.vcache)[at] = yb;
+                else static_cast<__half*>(p.vcache)[at] = __float2half_rn(yb);
             }
         }
     };
@@ -1185,15 +1187,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                 p.out[ur.out] += y;
             }
         } else if (EPI == EPI_QKV) {
+            const float* bias = p.bias[ur.seg];
+            const float yb = bias ? __fadd_rn(y, bias[ur.row]) : y;  // candle QLinear: matmul, then + bias
             if (ur.seg == 0) {
-                p.out[ur.row] = y;  // q before RoPE
+                p.out[ur.row] = yb;  // q before RoPE
             } else if (ur.seg == 1) {
-                p.kraw[ur.row] = y;  // k before RoPE
+                p.kraw[ur.row] = yb;  // k before RoPE
             } else {
                 const int pos = *p.pos, d = ur.row % p.hd, head = ur.row / p.hd;
                 const int64_t at = ((int64_t)head * p.max_seq + pos) * p.hd + d;
-                if (p.kv_f32) static_cast<float*>(p.vcache)[at] = y;
-                else static_cast<__half*>(p.vcache)[at] = __float2half_rn(y);
+                if (p.kv_f32) static_cast<float*>(p.vcache)[at] = yb;
+                else static_cast<__half*>(p.vcache)[at] = __float2half_rn(yb);
             }
         }
     };

@@ -200,6 +200,7 @@ struct GemvParams {
     const int* pos;  // device scalar: position being written
     int hd;
     int max_seq;
+    const float* bias[kGemvMaxSeg];  // optional per-segment row biases (qwen2 q / k / v), added in f32
     // EPI_DOTS
     int32_t* isum;
     int32_t* msum;

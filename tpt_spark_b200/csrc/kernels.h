@@ -49,6 +49,7 @@ struct AttnDecodeParams {
     uint8_t* act_out;
     ActLayout act;
     int act_transposed, act_nb;
+    int rope_neox;  // 1: RoPE pairs element i with i + hd/2 (candle rope, qwen2); 0: rope_i pairs
 };
 int attn_decode_splits(int n_kv, int max_seq, int sm_count);
 size_t attn_decode_partial_floats(int n_heads, int n_kv, int hd, int splits);

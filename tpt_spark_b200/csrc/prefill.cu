@@ -76,33 +76,47 @@ struct QkvPostParams {
     const float* cos;
     const float* sin;
     int start, n_heads, n_kv, hd, max_seq;
+    const float* bq;  // optional q / k / v biases (qwen2), added in f32 before RoPE
+    const float* bk;
+    const float* bv;
+    int neox;         // 1: RoPE pairs element j with j + hd/2 (candle rope), 0: 2j with 2j+1 (rope_i)
 };
+// Per token: the q and k heads rotated pair by pair (q -> fp16 for the attention GEMMs, k ->
+// the fp16 cache) and v copied to the cache, each value plus its bias when there is one.
 __global__ void qkv_post_kernel(const QkvPostParams p) {
     const int t = blockIdx.x, pos = p.start + t, half = p.hd / 2;
     const int nq = p.n_heads * p.hd, nk = p.n_kv * p.hd, n = nq + 2 * nk;
     const float* row = p.qkv + (size_t)t * n;
     const float* cs = p.cos + (size_t)pos * half;
     const float* sn = p.sin + (size_t)pos * half;
-    for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
-        const int col = 2 * i;
-        const float2 v = *reinterpret_cast<const float2*>(row + col);
-        if (col < nq + nk) {
-            const int j = (col % p.hd) / 2;
-            const float c = cs[j], s = sn[j];
-            const float r0 = __fsub_rn(__fmul_rn(v.x, c), __fmul_rn(v.y, s));
-            const float r1 = __fadd_rn(__fmul_rn(v.x, s), __fmul_rn(v.y, c));
-            if (col < nq) {
-                *reinterpret_cast<__half2*>(p.q + (size_t)t * nq + col) = __floats2half2_rn(r0, r1);
-            } else {
-                const int kh = (col - nq) / p.hd, e = (col - nq) % p.hd;
-                *reinterpret_cast<__half2*>(p.kc + ((size_t)kh * p.max_seq + pos) * p.hd + e) =
-                    __floats2half2_rn(r0, r1);
-            }
-        } else {
-            const int vh = (col - nq - nk) / p.hd, e = (col - nq - nk) % p.hd;
-            *reinterpret_cast<__half2*>(p.vc + ((size_t)vh * p.max_seq + pos) * p.hd + e) =
-                __floats2half2_rn(v.x, v.y);
+    for (int i = threadIdx.x; i < (p.n_heads + p.n_kv) * half; i += blockDim.x) {
+        const int head = i / half, j = i % half;
+        const int e0 = p.neox ? j : 2 * j, e1 = p.neox ? j + half : 2 * j + 1;  // within the head
+        const int col = head * p.hd;  // the head's first column in [q | k]
+        float x0 = row[col + e0], x1 = row[col + e1];
+        const float* b = head < p.n_heads ? (p.bq ? p.bq + col : nullptr) : (p.bk ? p.bk + (col - nq) : nullptr);
+        if (b) {
+            x0 = __fadd_rn(x0, b[e0]);
+            x1 = __fadd_rn(x1, b[e1]);
         }
+        const float c = cs[j], s = sn[j];
+        const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        if (head < p.n_heads) {
+            __half* dq = p.q + (size_t)t * nq + col;
+            dq[e0] = __float2half_rn(r0);
+            dq[e1] = __float2half_rn(r1);
+        } else {
+            __half* dk = p.kc + ((size_t)(head - p.n_heads) * p.max_seq + pos) * p.hd;
+            dk[e0] = __float2half_rn(r0);
+            dk[e1] = __float2half_rn(r1);
+        }
+    }
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+        float v = row[nq + nk + i];
+        if (p.bv) v = __fadd_rn(v, p.bv[i]);
+        const int vh = i / p.hd, e = i % p.hd;
+        p.vc[((size_t)vh * p.max_seq + pos) * p.hd + e] = __float2half_rn(v);
     }
 }
 
@@ -217,7 +231,8 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
             TPTC_CUDA_RET(launch_dequant_rows_f16(L.v, 0, nk, pf_w_ + (size_t)(nq + nk) * dim, st));
             TPTC_CUDA_RET(gemm_tc(GEMM_STORE, pf_xn_, dim, pf_w_, dim, g, st, false));
         }
-        QkvPostParams qp = {pf_qkv_, pf_q_, kc, vc, rope_cos_, rope_sin_, start, n_heads_l_, n_kv_l_, hd, max_seq_};
+        QkvPostParams qp = {pf_qkv_, pf_q_, kc, vc, rope_cos_, rope_sin_, start, n_heads_l_, n_kv_l_, hd, max_seq_,
+                            L.bq, L.bk, L.bv, meta_.rope_neox ? 1 : 0};
         qkv_post_kernel<<<T, 256, 0, st>>>(qp);
         TPTC_CUDA_RET(cudaGetLastError());
         AttnPrefillParams ap = {};

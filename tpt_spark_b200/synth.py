@@ -61,13 +61,16 @@ class ModelConfig:
     output_type: Optional[int] = None
     norm_std: float = 0.0  # 0: gains exactly 1.0 (the configs); >0: 1 + N(0, norm_std)
     weight_std: float = 0.02
+    arch: str = "llama"     # general.architecture; "qwen2" rotates head halves (NEOX)
+    qkv_bias: bool = False  # f32 attn_q / attn_k / attn_v biases, N(0, bias_std)
+    bias_std: float = 0.1
 
     @property
     def head_dim(self) -> int:
         return self.dim // self.n_heads
 
     def type_of(self, kind: str) -> int:
-        if kind.endswith("norm"):
+        if kind.endswith("norm") or kind == "bias":
             return F32
         if kind == "token_embd":
             return self.embd_type if self.embd_type is not None else self.default_type
@@ -86,6 +89,12 @@ class ModelConfig:
                 (p + "attn_q.weight", "attn_q", [d, self.n_heads * hd]),
                 (p + "attn_k.weight", "attn_k", [d, self.n_kv_heads * hd]),
                 (p + "attn_v.weight", "attn_v", [d, self.n_kv_heads * hd]),
+            ]
+            if self.qkv_bias:
+                out += [(p + "attn_q.bias", "bias", [self.n_heads * hd]),
+                        (p + "attn_k.bias", "bias", [self.n_kv_heads * hd]),
+                        (p + "attn_v.bias", "bias", [self.n_kv_heads * hd])]
+            out += [
                 (p + "attn_output.weight", "attn_output", [self.n_heads * hd, d]),
                 (p + "ffn_norm.weight", "ffn_norm", [d]),
                 (p + "ffn_gate.weight", "ffn_gate", [d, self.ffn]),
@@ -151,6 +160,11 @@ TINY: Dict[str, ModelConfig] = {
         "tiny_q2k", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=416,
         rope_base=10000.0, context_length=512, default_type=Q2_K,
         overrides=(("attn_v", Q3_K), ("ffn_down", Q3_K)), embd_type=Q2_K, output_type=Q4_K, norm_std=0.1),
+    # qwen2 (candle quantized_qwen2): q / k / v biases, RoPE on head halves, tied embeddings
+    "tiny_qwen2": ModelConfig(
+        "tiny_qwen2", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=384,
+        rope_base=1000000.0, context_length=512, tied=True, overrides=Q4_K_M, embd_type=Q4_K,
+        norm_std=0.1, arch="qwen2", qkv_bias=True),
     "tiny_tp_q4km": ModelConfig(
         "tiny_tp_q4km", dim=512, n_layers=2, n_heads=8, n_kv_heads=4, ffn=1024, vocab=384,
         rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
@@ -233,7 +247,7 @@ def _kv(key: str, vtype: int, val) -> bytes:
 
 
 def metadata(cfg: ModelConfig) -> List[bytes]:
-    a = "llama"
+    a = cfg.arch
     return [
         _kv("general.architecture", 8, a),
         _kv("general.name", 8, cfg.name),
@@ -278,6 +292,8 @@ def write_gguf(path: str, cfg: ModelConfig, seed: int = 0,
             row = ne[0]
             if kind.endswith("norm"):
                 std, mean = cfg.norm_std, 1.0
+            elif kind == "bias":
+                std, mean = cfg.bias_std, 0.0
             else:
                 std, mean = cfg.weight_std, 0.0
             s = tensor_seed(name, seed)
