@@ -169,8 +169,9 @@ def repeat_penalty(logits: np.ndarray, seen: Sequence[int], penalty: float) -> n
 
 
 class Model:
-    """candle quantized_llama (architectures llama / mistral) or quantized_qwen2 (qwen2: q / k /
-    v biases, RoPE on head halves) restated on CPU over a GGUF file (read with gguf-py)."""
+    """candle quantized_llama (architectures llama / mistral), quantized_qwen2 (qwen2: q / k / v
+    biases, RoPE on head halves) or quantized_phi3 (phi3: fused attn_qkv and ffn_up, RoPE on head
+    halves) restated on CPU over a GGUF file (read with gguf-py)."""
 
     def __init__(self, path: str, max_seq: Optional[int] = None):
         import gguf
@@ -204,8 +205,27 @@ class Model:
         for i in range(self.n_layers):
             order += [f"blk.{i}.{n}.weight" for n in ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
                                                        "ffn_norm", "ffn_gate", "ffn_up", "ffn_down")]
-        self._arrays = [np.ascontiguousarray(tensors[n].data) for n in order]
-        self._types = [int(tensors[n].tensor_type) for n in order]
+        # phi3 (candle quantized_phi3): attn_qkv rows are q | k | v and ffn_up rows gate | up; the
+        # fused matmul is row by row the separate ones, so the row blocks stand in for them
+        hd = self.dim // self.n_heads
+        nq, nkv = self.n_heads * hd, self.n_kv_heads * hd
+        blocks = {}
+        for i in range(self.n_layers):
+            p = f"blk.{i}."
+            if p + "attn_qkv.weight" in tensors:
+                t = tensors[p + "attn_qkv.weight"]
+                for n, (r0, r1) in (("attn_q", (0, nq)), ("attn_k", (nq, nq + nkv)), ("attn_v", (nq + nkv, nq + 2 * nkv))):
+                    blocks[p + n + ".weight"] = (np.ascontiguousarray(t.data[r0:r1]), int(t.tensor_type))
+            if p + "ffn_gate.weight" not in tensors:
+                t = tensors[p + "ffn_up.weight"]
+                blocks[p + "ffn_gate.weight"] = (np.ascontiguousarray(t.data[:self.ffn]), int(t.tensor_type))
+                blocks[p + "ffn_up.weight"] = (np.ascontiguousarray(t.data[self.ffn:]), int(t.tensor_type))
+
+        def get(n):
+            return blocks[n] if n in blocks else (np.ascontiguousarray(tensors[n].data), int(tensors[n].tensor_type))
+
+        self._arrays = [get(n)[0] for n in order]
+        self._types = [get(n)[1] for n in order]
         self.types = dict(zip(order, self._types))
         ptrs = (ctypes.c_void_p * len(order))(*[a.ctypes.data for a in self._arrays])
         tys = (ctypes.c_int * len(order))(*self._types)
@@ -219,7 +239,7 @@ class Model:
         d = _Desc(self.n_layers, self.dim, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.vocab,
                   self.max_seq, self.rope_base, self.rms_eps, 1.0, ptrs, tys,
                   ctypes.cast(barr, ctypes.POINTER(ctypes.c_void_p)) if barr is not None else None,
-                  1 if arch == "qwen2" else 0)
+                  1 if arch in ("qwen2", "phi3") else 0)
         self._keep = (ptrs, tys, barr)
         self.h = lib().or_model_create(ctypes.byref(d))
 

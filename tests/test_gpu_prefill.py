@@ -20,7 +20,8 @@ from tpt_spark_b200._lib import EngineError  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2"]
+MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2",
+          "tiny_phi3"]
 
 # fp16 operands (11-bit significands) against a float64 forward: relative error of a few
 # 2^-11 per layer on the hidden state, times the logit scale of the tiny models (|logit| < 3)
@@ -118,7 +119,7 @@ def float_prefill_logits(ref, tokens):
     def rms(x, g):
         return x / np.sqrt((x * x).mean(-1, keepdims=True) + ref.rms_eps) * g
 
-    neox = getattr(ref, "arch", "llama") == "qwen2"
+    neox = getattr(ref, "arch", "llama") in ("qwen2", "phi3")
 
     def rope(x, n):  # [T, n*hd]: interleaved pairs (rope_i), or the head's two halves (qwen2)
         c, s = cos[:, None, :], sin[:, None, :]

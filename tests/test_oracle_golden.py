@@ -236,7 +236,7 @@ def test_argmax_ties_last_and_repeat_penalty():
     np.testing.assert_array_equal(O.repeat_penalty(lg, [1], 1.0), lg)
 
 
-@pytest.mark.parametrize("name", ["tiny_q4km", "tiny_qwen2"])
+@pytest.mark.parametrize("name", ["tiny_q4km", "tiny_qwen2", "tiny_phi3"])
 def test_forward_prefill_equals_incremental(tmp_path, name):
     """candle's batched prefill and one-token steps give the same last-position logits."""
     from tpt_spark_b200 import synth

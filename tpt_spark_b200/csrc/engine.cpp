@@ -207,12 +207,15 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
     // ---- metadata (wgpu_loader.rs:305-406; candle_engine.rs:145-165 arch check).  qwen2 is
     // llama's forward with q / k / v biases and RoPE on head halves (candle quantized_qwen2;
     // the reference runs it on its wgpu path, wgpu_loader.rs:270, bias_add.wgsl).
+    // phi3 (candle quantized_phi3): one fused attn_qkv tensor (rows q | k | v, the reference's
+    // wgpu_engine.rs:385-397) and one fused ffn_up tensor (rows gate | up), RoPE on head halves.
     ModelMeta m;
     f.get_str("general.architecture", m.architecture);
-    if (m.architecture != "llama" && m.architecture != "mistral" && m.architecture != "qwen2")
+    if (m.architecture != "llama" && m.architecture != "mistral" && m.architecture != "qwen2" &&
+        m.architecture != "phi3")
         return err(TPTC_ERR_UNSUPPORTED, "Architecture '" + m.architecture +
-                                             "' is not yet supported. Supported: llama, mistral, qwen2.");
-    m.rope_neox = m.architecture == "qwen2";
+                                             "' is not yet supported. Supported: llama, mistral, qwen2, phi3.");
+    m.rope_neox = m.architecture == "qwen2" || m.architecture == "phi3";
     f.get_str("general.name", m.name);
     const std::string a = m.architecture;
     uint64_t u;
@@ -253,6 +256,8 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
             return err(TPTC_ERR_UNSUPPORTED, "model does not shard evenly over tp_size=" + std::to_string(tp_size_));
     m.tied = f.find("output.weight") == nullptr;
     m.qkv_bias = f.find("blk.0.attn_q.bias") != nullptr;
+    m.fused_qkv = f.find("blk.0.attn_qkv.weight") != nullptr;
+    m.fused_gate_up = f.find("blk.0.ffn_gate.weight") == nullptr && f.find("blk.0.ffn_up.weight") != nullptr;
     meta_ = m;
     path_ = path;
     file_bytes_ = f.size;
@@ -281,13 +286,23 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         LayerWeights& L = layers_[l];
         const std::string p = "blk." + std::to_string(l) + ".";
         plans.push_back({p + "attn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.attn_norm, 0, 0});
-        // rows / K windows from tp_shard (the same plan tptc_tp_shard exposes)
-        auto W = [&](int w, const char* name, int N, int K, DevMatrix* mat, int first_row, int glu_rows) {
-            plans.push_back({p + name, N, K, sh[w][0], sh[w][1], sh[w][2], sh[w][3], mat, nullptr, first_row, glu_rows});
+        // rows / K windows from tp_shard (the same plan tptc_tp_shard exposes); a fused tensor
+        // (phi3 attn_qkv, ffn_up) is read as its row blocks, `row_off` rows into it
+        auto W = [&](int w, const char* name, int N, int K, DevMatrix* mat, int first_row, int glu_rows,
+                     int row_off = 0, int fused_rows = 0) {
+            plans.push_back({p + name, fused_rows ? fused_rows : N, K, row_off + sh[w][0], row_off + sh[w][1], sh[w][2],
+                             sh[w][3], mat, nullptr, first_row, glu_rows});
         };
-        W(TPTC_SHARD_Q, "attn_q.weight", m.n_heads * hd, m.dim, &L.q, 0, 0);
-        W(TPTC_SHARD_K, "attn_k.weight", m.n_kv_heads * hd, m.dim, &L.k, 0, 0);
-        W(TPTC_SHARD_V, "attn_v.weight", m.n_kv_heads * hd, m.dim, &L.v, 0, 0);
+        const int nq = m.n_heads * hd, nkv = m.n_kv_heads * hd;
+        if (m.fused_qkv) {
+            W(TPTC_SHARD_Q, "attn_qkv.weight", nq, m.dim, &L.q, 0, 0, 0, nq + 2 * nkv);
+            W(TPTC_SHARD_K, "attn_qkv.weight", nkv, m.dim, &L.k, 0, 0, nq, nq + 2 * nkv);
+            W(TPTC_SHARD_V, "attn_qkv.weight", nkv, m.dim, &L.v, 0, 0, nq + nkv, nq + 2 * nkv);
+        } else {
+            W(TPTC_SHARD_Q, "attn_q.weight", nq, m.dim, &L.q, 0, 0);
+            W(TPTC_SHARD_K, "attn_k.weight", nkv, m.dim, &L.k, 0, 0);
+            W(TPTC_SHARD_V, "attn_v.weight", nkv, m.dim, &L.v, 0, 0);
+        }
         if (m.qkv_bias) {  // f32 vectors: this rank keeps the rows of its weight window
             auto B = [&](int w, const char* name, int N, float** dst) {
                 plans.push_back({p + name, 1, N, 0, 1, sh[w][0], sh[w][1], nullptr, dst, 0, 0});
@@ -298,8 +313,13 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         }
         W(TPTC_SHARD_O, "attn_output.weight", m.dim, m.n_heads * hd, &L.o, 0, 0);
         plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm, 0, 0});
-        W(TPTC_SHARD_GATE, "ffn_gate.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l);
-        W(TPTC_SHARD_UP, "ffn_up.weight", m.ffn, m.dim, &L.glu, ffn_l, 2 * ffn_l);
+        if (m.fused_gate_up) {  // ffn_up rows [0, ffn) gate, [ffn, 2 ffn) up
+            W(TPTC_SHARD_GATE, "ffn_up.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l, 0, 2 * m.ffn);
+            W(TPTC_SHARD_UP, "ffn_up.weight", m.ffn, m.dim, &L.glu, ffn_l, 2 * ffn_l, m.ffn, 2 * m.ffn);
+        } else {
+            W(TPTC_SHARD_GATE, "ffn_gate.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l);
+            W(TPTC_SHARD_UP, "ffn_up.weight", m.ffn, m.dim, &L.glu, ffn_l, 2 * ffn_l);
+        }
         W(TPTC_SHARD_DOWN, "ffn_down.weight", m.dim, m.ffn, &L.down, 0, 0);
     }
     plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_, 0, 0});

@@ -26,6 +26,8 @@ struct ModelMeta {
     bool tied = false;
     bool rope_neox = false;  // qwen2: RoPE pairs element i with i + head_dim / 2 (candle rope)
     bool qkv_bias = false;   // qwen2: f32 attn_q / attn_k / attn_v biases
+    bool fused_qkv = false;      // phi3: one attn_qkv tensor, rows q | k | v
+    bool fused_gate_up = false;  // phi3: one ffn_up tensor, rows gate | up
 };
 
 struct LayerWeights {

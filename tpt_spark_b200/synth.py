@@ -61,7 +61,8 @@ class ModelConfig:
     output_type: Optional[int] = None
     norm_std: float = 0.0  # 0: gains exactly 1.0 (the configs); >0: 1 + N(0, norm_std)
     weight_std: float = 0.02
-    arch: str = "llama"     # general.architecture; "qwen2" rotates head halves (NEOX)
+    arch: str = "llama"     # general.architecture; "qwen2" / "phi3" rotate head halves (NEOX);
+                            # "phi3" stores attn_qkv (rows q | k | v) and ffn_up (rows gate | up) fused
     qkv_bias: bool = False  # f32 attn_q / attn_k / attn_v biases, N(0, bias_std)
     bias_std: float = 0.1
 
@@ -84,23 +85,27 @@ class ModelConfig:
         out = [("token_embd.weight", "token_embd", [d, self.vocab])]
         for i in range(self.n_layers):
             p = f"blk.{i}."
-            out += [
-                (p + "attn_norm.weight", "attn_norm", [d]),
-                (p + "attn_q.weight", "attn_q", [d, self.n_heads * hd]),
-                (p + "attn_k.weight", "attn_k", [d, self.n_kv_heads * hd]),
-                (p + "attn_v.weight", "attn_v", [d, self.n_kv_heads * hd]),
-            ]
+            out += [(p + "attn_norm.weight", "attn_norm", [d])]
+            if self.arch == "phi3":
+                out += [(p + "attn_qkv.weight", "attn_qkv", [d, (self.n_heads + 2 * self.n_kv_heads) * hd])]
+            else:
+                out += [
+                    (p + "attn_q.weight", "attn_q", [d, self.n_heads * hd]),
+                    (p + "attn_k.weight", "attn_k", [d, self.n_kv_heads * hd]),
+                    (p + "attn_v.weight", "attn_v", [d, self.n_kv_heads * hd]),
+                ]
             if self.qkv_bias:
                 out += [(p + "attn_q.bias", "bias", [self.n_heads * hd]),
                         (p + "attn_k.bias", "bias", [self.n_kv_heads * hd]),
                         (p + "attn_v.bias", "bias", [self.n_kv_heads * hd])]
-            out += [
-                (p + "attn_output.weight", "attn_output", [self.n_heads * hd, d]),
-                (p + "ffn_norm.weight", "ffn_norm", [d]),
-                (p + "ffn_gate.weight", "ffn_gate", [d, self.ffn]),
-                (p + "ffn_up.weight", "ffn_up", [d, self.ffn]),
-                (p + "ffn_down.weight", "ffn_down", [self.ffn, d]),
-            ]
+            out += [(p + "attn_output.weight", "attn_output", [self.n_heads * hd, d]),
+                    (p + "ffn_norm.weight", "ffn_norm", [d])]
+            if self.arch == "phi3":
+                out += [(p + "ffn_up.weight", "ffn_up", [d, 2 * self.ffn])]
+            else:
+                out += [(p + "ffn_gate.weight", "ffn_gate", [d, self.ffn]),
+                        (p + "ffn_up.weight", "ffn_up", [d, self.ffn])]
+            out += [(p + "ffn_down.weight", "ffn_down", [self.ffn, d])]
         out.append(("output_norm.weight", "output_norm", [d]))
         if not self.tied:
             out.append(("output.weight", "output", [d, self.vocab]))
@@ -165,6 +170,11 @@ TINY: Dict[str, ModelConfig] = {
         "tiny_qwen2", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=384,
         rope_base=1000000.0, context_length=512, tied=True, overrides=Q4_K_M, embd_type=Q4_K,
         norm_std=0.1, arch="qwen2", qkv_bias=True),
+    # phi3 (candle quantized_phi3): fused attn_qkv and ffn_up, RoPE on head halves, head_dim 96
+    "tiny_phi3": ModelConfig(
+        "tiny_phi3", dim=768, n_layers=2, n_heads=8, n_kv_heads=8, ffn=512, vocab=352,
+        rope_base=10000.0, context_length=512, default_type=Q4_K, embd_type=Q4_K, output_type=Q6_K,
+        norm_std=0.1, arch="phi3"),
     "tiny_tp_q4km": ModelConfig(
         "tiny_tp_q4km", dim=512, n_layers=2, n_heads=8, n_kv_heads=4, ffn=1024, vocab=384,
         rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
