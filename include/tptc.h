@@ -156,7 +156,8 @@ TPTC_API int tptc_set_tp_wait_polls(tptc_ctx* ctx, uint32_t polls);
  * cudaMemcpyAsync, repack to the device layout, build the KV cache and rope table.
  * Architectures llama, mistral, qwen2 (q / k / v biases, RoPE on head halves) and phi3 (fused
  * attn_qkv and ffn_up, RoPE on head halves); weight types
- * F16, Q8_0, Q4_0, Q5_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K; anything else TPTC_ERR_UNSUPPORTED. */
+ * F16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K; anything else
+ * TPTC_ERR_UNSUPPORTED. */
 TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user);
 /* LlmEngine::unload / is_loaded / model_info (mod.rs:71-73, wgpu_engine.rs:126-147). */
 TPTC_API int tptc_unload(tptc_ctx* ctx);

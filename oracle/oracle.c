@@ -516,6 +516,32 @@ static inline int32_t q3k_block_int(const uint8_t* blk, const or_q8k* y) {
     return is;
 }
 
+/* Q4_1 / Q5_1 unsigned code of element l (0..31) of a block (d m [qh] qs layout). */
+static inline int q41_code(const uint8_t* blk, int l) {
+    const uint8_t* qs = blk + 4;
+    return l < 16 ? (qs[l] & 0x0f) : (qs[l - 16] >> 4);
+}
+static inline int q51_code(const uint8_t* blk, int l) {
+    const uint8_t* qs = blk + 8;
+    return (l < 16 ? (qs[l] & 0x0f) : (qs[l - 16] >> 4)) | (q5_hbit(blk + 4, l) << 4);
+}
+
+/* candle BlockQ4_1 / BlockQ5_1 ::vec_dot_unopt block sum against a Q8_1 block: sum_l q_l y_l.
+ * candle's Q8_1 quants and d equal Q8_0's (d = amax/127, q = round(x/d)), so the Q8_0 block
+ * stands in; its s = f16(f16(sum y) * d) is formed in q81_s. */
+static inline int32_t q41_q51_block_int(int type, const uint8_t* blk, const uint8_t* xb) {
+    const int8_t* y = (const int8_t*)(xb + 2);
+    int32_t s = 0;
+    for (int l = 0; l < 32; l++) s += (type == OR_Q4_1 ? q41_code(blk, l) : q51_code(blk, l)) * y[l];
+    return s;
+}
+static inline float q81_s(const uint8_t* xb) {
+    const int8_t* y = (const int8_t*)(xb + 2);
+    int32_t sum = 0;
+    for (int l = 0; l < 32; l++) sum += y[l];
+    return or_h2f(or_f2h(or_h2f(or_f2h((float)sum)) * or_h2f(rd16(xb))));
+}
+
 /* candle BlockQ4_0::vec_dot_unopt block sum: sum_j (lo_j - 8) y_j + (hi_j - 8) y_{j+16}. */
 static inline int32_t q40_block_int(const uint8_t* blk, const uint8_t* xb) {
     const int8_t* y = (const int8_t*)(xb + 2);
@@ -573,6 +599,10 @@ int or_block_dots(int type, const void* wrow, const void* xq, int nb, int32_t* i
             if (msum) msum[b] = 0;
         } else if (type == OR_Q4_0) {
             isum[b] = q40_block_int(w + (size_t)b * Q40_BYTES, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
+            if (msum) msum[b] = 0;
+        } else if (type == OR_Q4_1 || type == OR_Q5_1) {
+            const size_t bb = type == OR_Q4_1 ? Q41_BYTES : Q51_BYTES;
+            isum[b] = q41_q51_block_int(type, w + (size_t)b * bb, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
             if (msum) msum[b] = 0;
         } else if (type == OR_Q5_0) {
             isum[b] = q50_block_int(w + (size_t)b * Q50_BYTES, (const uint8_t*)xq + (size_t)b * Q80_BYTES);
@@ -842,6 +872,19 @@ static float vec_dot_q40_q50(int type, int n, const uint8_t* w, const uint8_t* x
     return sumf;
 }
 
+/* candle BlockQ4_1 / BlockQ5_1 ::vec_dot_unopt: sumf += sumi * d_w * d_x + m_w * s_x per block. */
+static float vec_dot_q41_q51(int type, int n, const uint8_t* w, const uint8_t* xq) {
+    const size_t bb = type == OR_Q4_1 ? Q41_BYTES : Q51_BYTES;
+    float sumf = 0.f;
+    for (int b = 0; b < n / QK8_0; b++) {
+        const uint8_t* blk = w + (size_t)b * bb;
+        const uint8_t* xb = xq + (size_t)b * Q80_BYTES;
+        const int32_t si = q41_q51_block_int(type, blk, xb);
+        sumf += (float)si * or_h2f(rd16(blk)) * or_h2f(rd16(xb)) + or_h2f(rd16(blk + 2)) * q81_s(xb);
+    }
+    return sumf;
+}
+
 static float vec_dot_f32(int n, const float* a, const float* b) {
     float s = 0.f;
     for (int i = 0; i < n; i++) s += a[i] * b[i];
@@ -874,7 +917,7 @@ int or_matmul(int type, const void* W, int N, int K, const float* x, int m, floa
         free(xq);
         return 0;
     }
-    if (type == OR_Q8_0 || type == OR_Q4_0 || type == OR_Q5_0) {
+    if (type == OR_Q8_0 || type == OR_Q4_0 || type == OR_Q5_0 || type == OR_Q4_1 || type == OR_Q5_1) {
         if (K % QK8_0) return -1;
         size_t xrow = (size_t)(K / QK8_0) * Q80_BYTES;
         size_t wrow = (size_t)(K / QK8_0) * (size_t)or_type_block_bytes(type);
@@ -884,8 +927,9 @@ int or_matmul(int type, const void* W, int N, int K, const float* x, int m, floa
         for (int n = 0; n < N; n++) {
             const uint8_t* wr = (const uint8_t*)W + wrow * n;
             for (int r = 0; r < m; r++)
-                y[(size_t)r * N + n] = type == OR_Q8_0 ? vec_dot_q80(K, wr, xq + xrow * r)
-                                                       : vec_dot_q40_q50(type, K, wr, xq + xrow * r);
+                y[(size_t)r * N + n] = type == OR_Q8_0                      ? vec_dot_q80(K, wr, xq + xrow * r)
+                                       : (type == OR_Q4_1 || type == OR_Q5_1) ? vec_dot_q41_q51(type, K, wr, xq + xrow * r)
+                                                                              : vec_dot_q40_q50(type, K, wr, xq + xrow * r);
         }
         free(xq);
         return 0;

@@ -85,9 +85,11 @@ SHAPES = [(O.Q4_K, 40, 4096), (O.Q4_K, 8, 256), (O.Q4_K, 1024, 4096), (O.Q4_K, 6
           (O.Q6_K, 40, 4096), (O.Q6_K, 24, 14336), (O.Q6_K, 17, 2048), (O.Q8_0, 40, 4096), (O.Q8_0, 16, 14336),
           (O.F16, 40, 4096), (O.F16, 8, 3072), (O.Q5_K, 40, 4096), (O.Q5_K, 24, 14336), (O.Q5_K, 9, 2048),
           (O.Q4_0, 40, 4096), (O.Q4_0, 16, 14336), (O.Q5_0, 40, 4096), (O.Q5_0, 17, 2048),
-          (O.Q2_K, 40, 4096), (O.Q2_K, 24, 14336), (O.Q3_K, 40, 4096), (O.Q3_K, 17, 2048)]
-Q80_FAMILY = (O.Q8_0, O.Q4_0, O.Q5_0)
-BLOCK_BYTES = {O.Q4_K: 144, O.Q5_K: 176, O.Q6_K: 210, O.Q8_0: 34, O.Q4_0: 18, O.Q5_0: 22, O.Q2_K: 84, O.Q3_K: 110}
+          (O.Q2_K, 40, 4096), (O.Q2_K, 24, 14336), (O.Q3_K, 40, 4096), (O.Q3_K, 17, 2048),
+          (O.Q4_1, 40, 4096), (O.Q4_1, 9, 14336), (O.Q5_1, 40, 4096), (O.Q5_1, 17, 2048)]
+Q80_FAMILY = (O.Q8_0, O.Q4_0, O.Q5_0, O.Q4_1, O.Q5_1)
+BLOCK_BYTES = {O.Q4_K: 144, O.Q5_K: 176, O.Q6_K: 210, O.Q8_0: 34, O.Q4_0: 18, O.Q5_0: 22, O.Q2_K: 84, O.Q3_K: 110,
+               O.Q4_1: 20, O.Q5_1: 24}
 
 
 def make_matrix(t, N, K, seed=0):

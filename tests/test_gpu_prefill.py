@@ -21,7 +21,7 @@ from tpt_spark_b200._lib import EngineError  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2",
-          "tiny_phi3"]
+          "tiny_phi3", "tiny_q4_1"]
 
 # fp16 operands (11-bit significands) against a float64 forward: relative error of a few
 # 2^-11 per layer on the hidden state, times the logit scale of the tiny models (|logit| < 3)

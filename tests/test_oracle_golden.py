@@ -196,12 +196,13 @@ def test_block_dots_q2k_q3k(t):
             assert msum[b] == int(sum(int(mn[j]) * int(xq[b]["bsums"][j]) for j in range(16)))
 
 
-@pytest.mark.parametrize("t", [O.Q5_K, O.Q4_0, O.Q5_0, O.Q2_K, O.Q3_K])
+@pytest.mark.parametrize("t", [O.Q5_K, O.Q4_0, O.Q5_0, O.Q2_K, O.Q3_K, O.Q4_1, O.Q5_1])
 def test_matmul_more_formats_close_to_f64(t):
     """QMatMul semantics for the further formats stay within activation-quantisation noise of
     the f64 product of the dequantised weights (the golden blocks as a weight matrix)."""
     name, bb, be = {O.Q5_K: ("q5k", 176, 256), O.Q4_0: ("q40", 18, 32), O.Q5_0: ("q50", 22, 32),
-                    O.Q2_K: ("q2k", 84, 256), O.Q3_K: ("q3k", 110, 256)}[t]
+                    O.Q2_K: ("q2k", 84, 256), O.Q3_K: ("q3k", 110, 256), O.Q4_1: ("q41", 20, 32),
+                    O.Q5_1: ("q51", 24, 32)}[t]
     raw = GOLD[f"{name}_raw"]
     K = 1024
     N = raw.size // bb * be // K

@@ -240,8 +240,8 @@ TPTC_API int tptc_last_timing(const tptc_ctx* ctx, double* prefill_ms, double* d
 
 static bool type_ok(int t) {
     return t == TPTC_TYPE_Q2_K || t == TPTC_TYPE_Q3_K || t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q5_K ||
-           t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q4_0 || t == TPTC_TYPE_Q5_0 || t == TPTC_TYPE_Q8_0 ||
-           t == TPTC_TYPE_F16;
+           t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q4_0 || t == TPTC_TYPE_Q5_0 || t == TPTC_TYPE_Q4_1 ||
+           t == TPTC_TYPE_Q5_1 || t == TPTC_TYPE_Q8_0 || t == TPTC_TYPE_F16;
 }
 
 TPTC_API int tptc_dequant(int ggml_type, const void* d_blocks, int64_t n, float* d_out, void* stream) {
@@ -295,6 +295,8 @@ TPTC_API int tptc_matrix_create(int ggml_type, const void* raw, int raw_on_devic
     if (ggml_type == TPTC_TYPE_Q8_0) raw_row = (int64_t)K / 32 * 34;
     if (ggml_type == TPTC_TYPE_Q4_0) raw_row = (int64_t)K / 32 * 18;
     if (ggml_type == TPTC_TYPE_Q5_0) raw_row = (int64_t)K / 32 * 22;
+    if (ggml_type == TPTC_TYPE_Q4_1) raw_row = (int64_t)K / 32 * 20;
+    if (ggml_type == TPTC_TYPE_Q5_1) raw_row = (int64_t)K / 32 * 24;
     if (ggml_type == TPTC_TYPE_Q2_K) raw_row = (int64_t)K / 256 * 84;
     if (ggml_type == TPTC_TYPE_Q3_K) raw_row = (int64_t)K / 256 * 110;
     const size_t main_al = ((size_t)d.main_bytes() + 255) / 256 * 256;

@@ -45,6 +45,8 @@ int64_t raw_row_bytes(int type, int K) {
     case TPTC_TYPE_Q3_K: return (int64_t)K / QK_K * Q3K_BYTES;
     case TPTC_TYPE_Q4_0: return (int64_t)K / QK8_0 * Q40_BYTES;
     case TPTC_TYPE_Q5_0: return (int64_t)K / QK8_0 * Q50_BYTES;
+    case TPTC_TYPE_Q4_1: return (int64_t)K / QK8_0 * Q41_BYTES;
+    case TPTC_TYPE_Q5_1: return (int64_t)K / QK8_0 * Q51_BYTES;
     case TPTC_TYPE_F16: return (int64_t)K * 2;
     case TPTC_TYPE_F32: return (int64_t)K * 4;
     }
@@ -53,8 +55,8 @@ int64_t raw_row_bytes(int type, int K) {
 
 bool matrix_type_ok(int t) {
     return t == TPTC_TYPE_Q2_K || t == TPTC_TYPE_Q3_K || t == TPTC_TYPE_Q4_K || t == TPTC_TYPE_Q5_K ||
-           t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q4_0 || t == TPTC_TYPE_Q5_0 || t == TPTC_TYPE_Q8_0 ||
-           t == TPTC_TYPE_F16;
+           t == TPTC_TYPE_Q6_K || t == TPTC_TYPE_Q4_0 || t == TPTC_TYPE_Q5_0 || t == TPTC_TYPE_Q4_1 ||
+           t == TPTC_TYPE_Q5_1 || t == TPTC_TYPE_Q8_0 || t == TPTC_TYPE_F16;
 }
 
 // Streams host bytes into device memory through two pinned buffers (the reference uploads

@@ -580,7 +580,10 @@ __device__ __forceinline__ uint32_t spread4(uint32_t v) { return ((v & 0xfu) * 0
 // its high nibble with activation j + 16; Q5_0 adds bit j (j + 16) of qh as the 5th bit.
 // The block's integer sum is sum(q * x) - off * sum(x) (off = 8 or 16), candle's
 // sum((q - off) * x) exactly; its f32 contribution is candle's (sumi * d_w) * d_x.
-template <bool DOTS, bool Q5>
+// MIN (Q4_1 / Q5_1, (d, m) per block in the scale section): codes are unsigned, no offset, and
+// candle adds m_w * s_x, where its Q8_1 activation's s = f16(f16(sum(x)) * d_x) (its quants
+// and d equal Q8_0's, so the Q8_0 activation serves).
+template <bool DOTS, bool Q5, bool MIN = false>
 __device__ __forceinline__ float chunk_q40(const uint8_t* slot, const uint16_t* dsec, const Act& a, int c0, int cb,
                                            int lane, int32_t* isum_row) {
     float acc = 0.f;
@@ -624,6 +627,16 @@ __device__ __forceinline__ float chunk_q40(const uint8_t* slot, const uint16_t* 
         sx = __dp4a(ones, xh.y, sx);
         sx = __dp4a(ones, xh.z, sx);
         sx = __dp4a(ones, xh.w, sx);
+        if (MIN) {
+            if (DOTS) {
+                isum_row[b0 + b] = s;
+            } else {
+                const float dx = a.q80_d[b0 + b];
+                const float s81 = __half2float(__float2half_rn(__fmul_rn(__half2float(__float2half_rn((float)sx)), dx)));
+                acc += __fadd_rn(__fmul_rn(__fmul_rn((float)s, h2f(dsec[2 * b])), dx), __fmul_rn(h2f(dsec[2 * b + 1]), s81));
+            }
+            continue;
+        }
         const int sum = s - (Q5 ? 16 : 8) * sx;
         if (DOTS) isum_row[b0 + b] = sum;
         else acc += __fmul_rn(__fmul_rn((float)sum, h2f(dsec[b])), a.q80_d[b0 + b]);
@@ -1010,6 +1023,8 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
             return 0.f;
         case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q4_1: return chunk_q40<EPI == EPI_DOTS, false, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q5_1: return chunk_q40<EPI == EPI_DOTS, true, true>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
         default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
         }
@@ -1255,6 +1270,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             return 0.f;
         case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q4_1: return chunk_q40<EPI == EPI_DOTS, false, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q5_1: return chunk_q40<EPI == EPI_DOTS, true, true>(slot, dsec, a, c0, cb, lane, isum_row);
         case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
         default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
         }

@@ -15,8 +15,8 @@ __host__ __device__ inline int sb_main_bytes(int type) {
     case TPTC_TYPE_Q4_K: return 144;
     case TPTC_TYPE_Q5_K: return 176;
     case TPTC_TYPE_Q6_K: return 208;
-    case TPTC_TYPE_Q4_0: return 128;
-    case TPTC_TYPE_Q5_0: return 160;
+    case TPTC_TYPE_Q4_0: case TPTC_TYPE_Q4_1: return 128;
+    case TPTC_TYPE_Q5_0: case TPTC_TYPE_Q5_1: return 160;
     case TPTC_TYPE_Q8_0: return 256;
     }
     return 512;
@@ -27,13 +27,15 @@ __host__ __device__ inline int sb_d_bytes(int type) {
     case TPTC_TYPE_Q2_K: return 4;
     case TPTC_TYPE_Q3_K: return 14;
     case TPTC_TYPE_Q4_0: case TPTC_TYPE_Q5_0: case TPTC_TYPE_Q8_0: return 16;
+    case TPTC_TYPE_Q4_1: case TPTC_TYPE_Q5_1: return 32;
     }
     return 0;
 }
 __host__ __device__ inline int sb_bytes(int type) { return sb_main_bytes(type) + sb_d_bytes(type); }
 // The 32-element formats: eight blocks per super-block, activations quantised to Q8_0.
 __host__ __device__ inline bool type_q80_family(int type) {
-    return type == TPTC_TYPE_Q8_0 || type == TPTC_TYPE_Q4_0 || type == TPTC_TYPE_Q5_0;
+    return type == TPTC_TYPE_Q8_0 || type == TPTC_TYPE_Q4_0 || type == TPTC_TYPE_Q5_0 || type == TPTC_TYPE_Q4_1 ||
+           type == TPTC_TYPE_Q5_1;
 }
 __host__ __device__ inline int chunk_sb(int type) { return type == TPTC_TYPE_F16 ? 8 : 16; }
 
@@ -49,6 +51,7 @@ constexpr int kTileRows = 8;
 //   Q6_K  208 B: ql | qh | scales, plus its f16 d in the tile's scale section
 //   Q4_0  128 B: qs of eight 32-blocks (16 B each), plus their eight f16 d in the scale section
 //   Q5_0  160 B: qs of eight 32-blocks, then their eight 4-byte qh words; d as Q4_0
+//   Q4_1 / Q5_1: Q4_0's / Q5_0's main part, each block's f16 d and m in the scale section
 //   Q8_0  256 B: qs of eight 32-blocks, plus their eight f16 d in the scale section
 //   F16   512 B: 256 f16 values
 // Tiling: rows are grouped by 8 (N padded to Npad, zero rows) and each row is cut into
@@ -112,7 +115,7 @@ __host__ __device__ inline const uint8_t* dm_block(const DevMatrix& m, int prow,
 }
 
 // Scale-section entry of super-block `sb` of physical row `prow` (Q6_K: d; Q2_K: d, dmin;
-// Q3_K: scales[12] then d; Q4_0 / Q5_0 / Q8_0: the eight blocks' d).
+// Q3_K: scales[12] then d; Q4_0 / Q5_0 / Q8_0: the eight blocks' d; Q4_1 / Q5_1: their (d, m)).
 __host__ __device__ inline const uint16_t* dm_scales(const DevMatrix& m, int prow, int sb) {
     int cb, j;
     const uint8_t* t = dm_tile(m, prow, sb, cb, j);

@@ -121,6 +121,17 @@ __global__ void repack_kernel(const uint8_t* __restrict__ raw, int64_t raw_row, 
             for (int k = 0; k < 4; k++) dst[128 + 4 * j + k] = src[2 + k];
             dsc[j] = (uint16_t)(src[0] | (src[1] << 8));
         }
+    } else if (m.type == TPTC_TYPE_Q4_1 || m.type == TPTC_TYPE_Q5_1) {  // d m [qh] qs -> qs | [qh], (d, m)
+        const bool five = m.type == TPTC_TYPE_Q5_1;
+        uint16_t* dsc = const_cast<uint16_t*>(dm_scales(m, prow, sb));
+        for (int j = 0; j < 8; j++) {
+            const uint8_t* src = row + ((int64_t)sb * 8 + j) * (five ? Q51_BYTES : Q41_BYTES);
+            for (int k = 0; k < 16; k++) dst[16 * j + k] = src[(five ? 8 : 4) + k];
+            if (five)
+                for (int k = 0; k < 4; k++) dst[128 + 4 * j + k] = src[4 + k];
+            dsc[2 * j] = (uint16_t)(src[0] | (src[1] << 8));
+            dsc[2 * j + 1] = (uint16_t)(src[2] | (src[3] << 8));
+        }
     } else {
         const uint8_t* src = row + (int64_t)sb * 512;
         for (int k = 0; k < 512; k++) dst[k] = src[k];
@@ -189,7 +200,8 @@ __global__ void dequant_rows_f16_kernel(DevMatrix m, int row0, int rows, int phy
 #pragma unroll
         for (int b = 0; b < 32; b++) v[b] = __float2half_rn(__fmul_rn((float)q[b], d));
     } else {
-        // Q2_K, Q3_K, Q5_K, Q4_0, Q5_0: the element values of dm_elem (one group of 32, rounded to fp16)
+        // Q2_K, Q3_K, Q5_K, Q4_0, Q5_0, Q4_1, Q5_1: the element values of dm_elem (one group of
+        // 32, rounded to fp16)
 #pragma unroll 8
         for (int b = 0; b < 32; b++) v[b] = __float2half_rn(dm_elem(m, prow, k0 + b));
     }

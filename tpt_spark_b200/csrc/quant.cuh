@@ -230,6 +230,14 @@ __device__ __forceinline__ float dm_elem(const DevMatrix& m, int prow, int i) {
         const int q = q4_nibble(blk + 16 * j, l) | (q5_hbit(blk + 128 + 4 * j, l) << 4);
         return __fmul_rn(h2f(dm_scales(m, prow, sb)[j]), (float)(q - 16));
     }
+    case TPTC_TYPE_Q4_1:
+    case TPTC_TYPE_Q5_1: {
+        const int j = e / QK8_0, l = e % QK8_0;
+        int q = q4_nibble(blk + 16 * j, l);
+        if (m.type == TPTC_TYPE_Q5_1) q |= q5_hbit(blk + 128 + 4 * j, l) << 4;
+        const uint16_t* dm = dm_scales(m, prow, sb) + 2 * j;
+        return __fadd_rn(__fmul_rn(h2f(dm[0]), (float)q), h2f(dm[1]));
+    }
     }
     return h2f(reinterpret_cast<const uint16_t*>(blk)[e]);
 }

@@ -25,7 +25,7 @@
 #include <stdint.h>
 #include <string.h>
 
-enum { SY_F32 = 0, SY_F16 = 1, SY_Q4_0 = 2, SY_Q5_0 = 6, SY_Q8_0 = 8, SY_Q2_K = 10, SY_Q3_K = 11, SY_Q4_K = 12, SY_Q5_K = 13, SY_Q6_K = 14 };
+enum { SY_F32 = 0, SY_F16 = 1, SY_Q4_0 = 2, SY_Q4_1 = 3, SY_Q5_0 = 6, SY_Q5_1 = 7, SY_Q8_0 = 8, SY_Q2_K = 10, SY_Q3_K = 11, SY_Q4_K = 12, SY_Q5_K = 13, SY_Q6_K = 14 };
 
 static inline uint64_t splitmix64(uint64_t x) {
     x += 0x9E3779B97F4A7C15ull;
@@ -162,6 +162,32 @@ static void enc_q40_q50(const float* x, uint8_t* b, int five) {
         uint32_t qh = 0;
         for (int j = 0; j < 32; j++) qh |= (uint32_t)(q[j] >> 4) << j;
         memcpy(b + 2, &qh, 4);
+    }
+}
+
+/* Q4_1 / Q5_1 as gguf-py's quantize_blocks (gguf/quants.py :256-274, :335-355): d = (max -
+ * min) / 15 (31), m = min, q = trunc((x - min) / d + 0.5) clipped; layouts as Q4_0 / Q5_0 with
+ * m after d. */
+static void enc_q41_q51(const float* x, uint8_t* b, int five) {
+    float mn = x[0], mx = x[0];
+    for (int j = 1; j < 32; j++) {
+        mn = fminf(mn, x[j]);
+        mx = fmaxf(mx, x[j]);
+    }
+    const float d = (mx - mn) / (five ? 31.f : 15.f), id = d != 0.f ? 1.f / d : 0.f;
+    uint8_t q[32];
+    for (int j = 0; j < 32; j++) q[j] = (uint8_t)clampi((int)truncf((x[j] - mn) * id + 0.5f), 0, five ? 31 : 15);
+    const uint16_t dh = f2h(d), mh = f2h(mn);
+    b[0] = (uint8_t)(dh & 0xff);
+    b[1] = (uint8_t)(dh >> 8);
+    b[2] = (uint8_t)(mh & 0xff);
+    b[3] = (uint8_t)(mh >> 8);
+    uint8_t* qs = b + (five ? 8 : 4);
+    for (int j = 0; j < 16; j++) qs[j] = (uint8_t)((q[j] & 0x0f) | ((q[j + 16] & 0x0f) << 4));
+    if (five) {
+        uint32_t qh = 0;
+        for (int j = 0; j < 32; j++) qh |= (uint32_t)(q[j] >> 4) << j;
+        memcpy(b + 4, &qh, 4);
     }
 }
 
@@ -329,6 +355,8 @@ int64_t sy_type_bytes(int type, int64_t n) {
     case SY_Q5_0: return n / 32 * 22;
     case SY_Q5_K: return n / 256 * 176;
     case SY_Q2_K: return n / 256 * 84;
+    case SY_Q4_1: return n / 32 * 20;
+    case SY_Q5_1: return n / 32 * 24;
     case SY_Q3_K: return n / 256 * 110;
     }
     return -1;
@@ -374,6 +402,12 @@ int64_t sy_encode(int type, const float* x, int64_t n, uint8_t* out) {
 #pragma omp parallel for schedule(static)
         for (int64_t i = 0; i < nb; i++) enc_q5k(x + 256 * i, out + 176 * i);
         return nb * 176;
+    case SY_Q4_1:
+    case SY_Q5_1:
+        nb = n / 32;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < nb; i++) enc_q41_q51(x + 32 * i, out + (type == SY_Q5_1 ? 24 : 20) * i, type == SY_Q5_1);
+        return nb * (type == SY_Q5_1 ? 24 : 20);
     case SY_Q2_K:
         nb = n / 256;
 #pragma omp parallel for schedule(static)

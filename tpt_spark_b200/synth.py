@@ -26,11 +26,11 @@ import numpy as np
 from ._build import lib_path
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
-Q4_0, Q5_0, Q5_K, Q2_K, Q3_K = 2, 6, 13, 10, 11
+Q4_0, Q5_0, Q5_K, Q2_K, Q3_K, Q4_1, Q5_1 = 2, 6, 13, 10, 11, 3, 7
 BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q4_0: (32, 18),
-         Q5_0: (32, 22), Q5_K: (256, 176), Q2_K: (256, 84), Q3_K: (256, 110)}
+         Q5_0: (32, 22), Q5_K: (256, 176), Q2_K: (256, 84), Q3_K: (256, 110), Q4_1: (32, 20), Q5_1: (32, 24)}
 TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q4_0: "Q4_0", Q5_0: "Q5_0",
-              Q5_K: "Q5_K", Q2_K: "Q2_K", Q3_K: "Q3_K"}
+              Q5_K: "Q5_K", Q2_K: "Q2_K", Q3_K: "Q3_K", Q4_1: "Q4_1", Q5_1: "Q5_1"}
 ALIGN = 32
 
 
@@ -165,6 +165,11 @@ TINY: Dict[str, ModelConfig] = {
         "tiny_q2k", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=416,
         rope_base=10000.0, context_length=512, default_type=Q2_K,
         overrides=(("attn_v", Q3_K), ("ffn_down", Q3_K)), embd_type=Q2_K, output_type=Q4_K, norm_std=0.1),
+    # Q4_1 with Q5_1 attn_v / ffn_down / output (candle pairs both with Q8_1 activations)
+    "tiny_q4_1": ModelConfig(
+        "tiny_q4_1", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=320,
+        rope_base=10000.0, context_length=512, default_type=Q4_1,
+        overrides=(("attn_v", Q5_1), ("ffn_down", Q5_1)), embd_type=Q4_1, output_type=Q5_1, norm_std=0.1),
     # qwen2 (candle quantized_qwen2): q / k / v biases, RoPE on head halves, tied embeddings
     "tiny_qwen2": ModelConfig(
         "tiny_qwen2", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=384,
