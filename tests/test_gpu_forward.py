@@ -30,8 +30,15 @@ TIE_PRONE = {"tiny_q4km_tied"}
 GREEDY_TIE_PRONE = TIE_PRONE | {"tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2", "tiny_phi3", "tiny_q4_1"}
 
 
+# tiny_phi3: the oracle's own logits move by up to 0.026 over the first steps of PROMPT when
+# its RMSNorm sums in 4 interleaved lanes instead of sequentially (an equally valid f32
+# order, oracle.set_norm_lanes): one Q8 activation rounding flips, the floor any
+# reimplementation that sums in another order meets, and the GPU lands at that floor.
+FLOOR_ATOL = {"tiny_phi3": LOGIT_ATOL_TIES}
+
+
 def atol_for(name):
-    return LOGIT_ATOL_TIES if name in TIE_PRONE else LOGIT_ATOL
+    return LOGIT_ATOL_TIES if name in TIE_PRONE else FLOOR_ATOL.get(name, LOGIT_ATOL)
 PROMPT = [3, 141, 59, 26, 5, 358, 97, 93, 238, 46, 264, 33]
 
 
