@@ -57,6 +57,27 @@ __device__ __forceinline__ int unit_seg(const GemvParams& p, int u) {
 // Whether units u and u + grid are reduced together (sharing the activation slice): both
 // exist, same Q4_K / Q6_K weights, and the ring holds the pair plus at least one stage to
 // refill meanwhile.  Producer and consumers take the same decision.
+// Super-block byte sizes inside the kernels.  The narrow build (WIDE = false) knows four
+// formats and picks among them by selects; the wide build takes the switch over every format.
+// The paired path (unit_pair: Q4_K or Q6_K only) uses the narrow form in both builds.
+template <bool WIDE>
+__device__ __forceinline__ int k_sb_main(int t) {
+    if constexpr (WIDE) return sb_main_bytes(t);
+    constexpr int q4k = sb_main_bytes(TPTC_TYPE_Q4_K), q6k = sb_main_bytes(TPTC_TYPE_Q6_K),
+                  q80 = sb_main_bytes(TPTC_TYPE_Q8_0), f16 = sb_main_bytes(TPTC_TYPE_F16);
+    return t == TPTC_TYPE_Q4_K ? q4k : t == TPTC_TYPE_Q6_K ? q6k : t == TPTC_TYPE_Q8_0 ? q80 : f16;
+}
+template <bool WIDE>
+__device__ __forceinline__ int k_sb_d(int t) {
+    if constexpr (WIDE) return sb_d_bytes(t);
+    constexpr int q6k = sb_d_bytes(TPTC_TYPE_Q6_K), q80 = sb_d_bytes(TPTC_TYPE_Q8_0);
+    return t == TPTC_TYPE_Q6_K ? q6k : t == TPTC_TYPE_Q8_0 ? q80 : 0;
+}
+template <bool WIDE>
+__device__ __forceinline__ int k_sb_bytes(int t) {
+    return k_sb_main<WIDE>(t) + k_sb_d<WIDE>(t);
+}
+
 __device__ __forceinline__ bool unit_pair(const GemvParams& p, int u, int epi) {
     const int u2 = u + gridDim.x;
     if (epi == EPI_DOTS || u2 >= p.units || p.stages < 3) return false;
@@ -853,6 +874,7 @@ __device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, int* 
 // alternating when unit_pair holds, a single unit alone otherwise.  Weights do not depend on
 // any earlier kernel or phase, so this runs ahead of every wait the consumers do.  Returns
 // false once a wait for a free stage gave up (or the CTA aborted).
+template <bool WIDE>
 __device__ bool produce_units(const GemvParams& p, int epi, const Ring& r, int& s, int& lap, uint64_t policy,
                               volatile int* abort_flag) {
     const int nsb = p.K / QK_K;
@@ -862,7 +884,7 @@ __device__ bool produce_units(const GemvParams& p, int epi, const Ring& r, int& 
             const int c = two ? i >> 1 : i, k = two ? i & 1 : 0;
             const int uk = u + k * gridDim.x, s_ = unit_seg(p, uk);
             const DevMatrix& m = p.seg[s_].m;
-            const int sbb = sb_bytes(m.type);
+            const int sbb = k_sb_bytes<WIDE>(m.type);
             const int64_t tile0 = (int64_t)(uk - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
             if (lap > 0 && !wait_backoff_abort(&r.empty[s], (lap - 1) & 1, p.err, abort_flag)) return false;
             const int cb = min(p.cbs, nsb - c * p.cbs);
@@ -914,13 +936,87 @@ __device__ __forceinline__ void argbest_take(ArgBest& b, float v, int i) {
     }
 }
 
+// One row chunk of one unit on its own (DOTS test hook, mixed types, Q8_0, F16, and every
+// format beyond Q4_K / Q6_K).  Kernels built with WIDE = false carry only Q4_K, Q6_K, Q8_0
+// and F16: the other formats' code would raise the register pressure of the whole kernel
+// (more spills in the Q4_K / Q6_K loop), so a launch takes the WIDE build only when one of
+// its matrices needs it.
+template <int EPI, bool WIDE>
+__device__ __forceinline__ float single_chunk(const GemvParams& p, const Act& a, const DevMatrix& m,
+                                              const UnitRow& ur, const uint8_t* stage, int c0, int cb,
+                                              int lane, int warp) {
+    const int nsb = p.K / QK_K;
+    if (ur.seg < 0) return 0.f;
+    const int sbm = k_sb_main<WIDE>(m.type), sbd = k_sb_d<WIDE>(m.type);
+    const uint8_t* slot = stage + warp * cb * sbm;
+    const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
+    int32_t* isum_row = nullptr;
+    int32_t* msum_row = nullptr;
+    if (EPI == EPI_DOTS) {
+        const int per_row = type_q80_family(m.type) ? p.K / QK8_0 : nsb;
+        isum_row = p.isum + (int64_t)ur.row * per_row;
+        msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
+    }
+    if constexpr (WIDE) {
+        switch (m.type) {
+        case TPTC_TYPE_Q5_K:
+            if (EPI == EPI_DOTS) {
+                chunk_q5k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+                return q5k_half(slot, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q2_K:
+        case TPTC_TYPE_Q3_K:
+            if (EPI == EPI_DOTS) {
+                if (m.type == TPTC_TYPE_Q2_K) dots_q23k<TPTC_TYPE_Q2_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
+                else dots_q23k<TPTC_TYPE_Q3_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
+            } else if (lane < 2 * cb) {
+                XHalf xh;
+                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+                return m.type == TPTC_TYPE_Q2_K ? q2k_half(slot, dsec, xh, lane) : q3k_half(slot, dsec, xh, lane);
+            }
+            return 0.f;
+        case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q4_1: return chunk_q40<EPI == EPI_DOTS, false, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        case TPTC_TYPE_Q5_1: return chunk_q40<EPI == EPI_DOTS, true, true>(slot, dsec, a, c0, cb, lane, isum_row);
+        default: break;
+        }
+    }
+    switch (m.type) {
+    case TPTC_TYPE_Q4_K:
+        if (EPI == EPI_DOTS) {
+            chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
+        } else if (lane < 2 * cb) {
+            XHalf xh;
+            load_xhalf<false>(xh, a, c0, 2 * cb, lane);
+            return q4k_half(slot, xh, lane);
+        }
+        return 0.f;
+    case TPTC_TYPE_Q6_K:
+        if (EPI == EPI_DOTS) {
+            chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
+        } else if (lane < 2 * cb) {
+            XHalf xh;
+            load_xhalf<true>(xh, a, c0, 2 * cb, lane);
+            return q6k_half(slot, dsec, xh, lane);
+        }
+        return 0.f;
+    case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
+    default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
+    }
+}
+
 // Consumer warps: this CTA's units of GEMV p from the ring, one warp per tile row.  Units in
 // pairs (u, u + grid): for every chunk the producer filled the pair's two stages back to back
 // and a warp reduces its row of both in one pass; with the same weight type the two dot
 // products share the lane's activation slice (same columns).  Once a wait gives up the warps
 // skip the arithmetic but keep the loop's barriers (the gate|up pair barrier) and stage
 // releases, so every warp leaves together.  `best` (EPI_STORE): argmax of the rows written.
-template <int EPI>
+template <int EPI, bool WIDE>
 __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a, const Ring& r, int& s, int& lap,
                                               int& unit_no, float (&glu_up)[2][4], ArgBest* best,
                                               volatile int* abort_flag, bool& timed_out) {
@@ -971,63 +1067,7 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
     };
     // one row chunk of one unit on its own (DOTS test hook, mixed types, Q8_0, F16)
     auto single = [&](const DevMatrix& m, const UnitRow& ur, const uint8_t* stage, int c0, int cb) -> float {
-        if (ur.seg < 0) return 0.f;
-        const int sbm = sb_main_bytes(m.type), sbd = sb_d_bytes(m.type);
-        const uint8_t* slot = stage + warp * cb * sbm;
-        const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
-        int32_t* isum_row = nullptr;
-        int32_t* msum_row = nullptr;
-        if (EPI == EPI_DOTS) {
-            const int per_row = type_q80_family(m.type) ? p.K / QK8_0 : nsb;
-            isum_row = p.isum + (int64_t)ur.row * per_row;
-            msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
-        }
-        switch (m.type) {
-        case TPTC_TYPE_Q4_K:
-            if (EPI == EPI_DOTS) {
-                chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
-                return q4k_half(slot, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q6_K:
-            if (EPI == EPI_DOTS) {
-                chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
-                return q6k_half(slot, dsec, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q5_K:
-            if (EPI == EPI_DOTS) {
-                chunk_q5k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
-                return q5k_half(slot, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q2_K:
-        case TPTC_TYPE_Q3_K:
-            if (EPI == EPI_DOTS) {
-                if (m.type == TPTC_TYPE_Q2_K) dots_q23k<TPTC_TYPE_Q2_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
-                else dots_q23k<TPTC_TYPE_Q3_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
-                return m.type == TPTC_TYPE_Q2_K ? q2k_half(slot, dsec, xh, lane) : q3k_half(slot, dsec, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q4_1: return chunk_q40<EPI == EPI_DOTS, false, true>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q5_1: return chunk_q40<EPI == EPI_DOTS, true, true>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
-        default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
-        }
+        return single_chunk<EPI, WIDE>(p, a, m, ur, stage, c0, cb, lane, warp);
     };
     for (int u = blockIdx.x; u < p.units;) {
         const int u2 = u + gridDim.x;
@@ -1060,7 +1100,7 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
                 const uint8_t* stB = r.base + sb2 * r.stage_bytes;
                 if (two) {
                     if (lane < 2 * cb) {
-                        const int sbm = sb_main_bytes(ty), sbd = sb_d_bytes(ty);
+                        const int sbm = k_sb_main<false>(ty), sbd = k_sb_d<false>(ty);
                         XHalf xh;
                         if (ty == TPTC_TYPE_Q4_K) {
                             load_xhalf<false>(xh, a, c0, 2 * cb, lane);
@@ -1092,7 +1132,7 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
 // The standalone GEMV (one launch per projection), written out in one body: the ring
 // bookkeeping and the unit loop inline here measured faster than the shared
 // produce_units / consume_units the chain kernel uses.
-template <int EPI>
+template <int EPI, bool WIDE>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
@@ -1129,7 +1169,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                     {
                         const int uk = u + k * gridDim.x, s_ = unit_seg(p, uk);
                         const DevMatrix& m = p.seg[s_].m;
-                        const int sbb = sb_bytes(m.type);
+                        const int sbb = k_sb_bytes<WIDE>(m.type);
                         const int64_t tile0 = (int64_t)(uk - p.seg[s_].unit_begin) * kTileRows * m.main_row_bytes;
                         if (lap > 0 && !mbar_wait_backoff(&empty[s], (lap - 1) & 1, p.err)) return;
                         const int cb = min(p.cbs, nsb - c * p.cbs);
@@ -1218,63 +1258,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     };
     // one row chunk of one unit on its own (DOTS test hook, mixed types, Q8_0, F16)
     auto single = [&](const DevMatrix& m, const UnitRow& ur, const uint8_t* stage, int c0, int cb) -> float {
-        if (ur.seg < 0) return 0.f;
-        const int sbm = sb_main_bytes(m.type), sbd = sb_d_bytes(m.type);
-        const uint8_t* slot = stage + warp * cb * sbm;
-        const uint16_t* dsec = reinterpret_cast<const uint16_t*>(stage + kTileRows * cb * sbm + warp * cb * sbd);
-        int32_t* isum_row = nullptr;
-        int32_t* msum_row = nullptr;
-        if (EPI == EPI_DOTS) {
-            const int per_row = type_q80_family(m.type) ? p.K / QK8_0 : nsb;
-            isum_row = p.isum + (int64_t)ur.row * per_row;
-            msum_row = p.msum ? p.msum + (int64_t)ur.row * per_row : nullptr;
-        }
-        switch (m.type) {
-        case TPTC_TYPE_Q4_K:
-            if (EPI == EPI_DOTS) {
-                chunk_q4k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
-                return q4k_half(slot, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q6_K:
-            if (EPI == EPI_DOTS) {
-                chunk_q6k<true>(slot, dsec, a, c0, cb, lane, 0, 32, isum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
-                return q6k_half(slot, dsec, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q5_K:
-            if (EPI == EPI_DOTS) {
-                chunk_q5k<true>(slot, a, c0, cb, lane, 0, 32, isum_row, msum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<false>(xh, a, c0, 2 * cb, lane);
-                return q5k_half(slot, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q2_K:
-        case TPTC_TYPE_Q3_K:
-            if (EPI == EPI_DOTS) {
-                if (m.type == TPTC_TYPE_Q2_K) dots_q23k<TPTC_TYPE_Q2_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
-                else dots_q23k<TPTC_TYPE_Q3_K>(slot, dsec, a, c0, cb, lane, isum_row, msum_row);
-            } else if (lane < 2 * cb) {
-                XHalf xh;
-                load_xhalf<true>(xh, a, c0, 2 * cb, lane);
-                return m.type == TPTC_TYPE_Q2_K ? q2k_half(slot, dsec, xh, lane) : q3k_half(slot, dsec, xh, lane);
-            }
-            return 0.f;
-        case TPTC_TYPE_Q4_0: return chunk_q40<EPI == EPI_DOTS, false>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q5_0: return chunk_q40<EPI == EPI_DOTS, true>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q4_1: return chunk_q40<EPI == EPI_DOTS, false, true>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q5_1: return chunk_q40<EPI == EPI_DOTS, true, true>(slot, dsec, a, c0, cb, lane, isum_row);
-        case TPTC_TYPE_Q8_0: return chunk_q80<EPI == EPI_DOTS>(slot, dsec, a, c0, cb, lane, isum_row);
-        default: return chunk_f16(slot, a, c0, cb, lane, 0, 32);
-        }
+        return single_chunk<EPI, WIDE>(p, a, m, ur, stage, c0, cb, lane, warp);
     };
     for (int u = blockIdx.x; u < p.units;) {
         const int u2 = u + gridDim.x;
@@ -1308,7 +1292,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                 const uint8_t* stB = ring + sb2 * p.stage_bytes;
                 if (paired) {
                     if (lane < 2 * cb) {
-                        const int sbm = sb_main_bytes(ty), sbd = sb_d_bytes(ty);
+                        const int sbm = k_sb_main<false>(ty), sbd = k_sb_d<false>(ty);
                         XHalf xh;
                         if (ty == TPTC_TYPE_Q4_K) {
                             load_xhalf<false>(xh, a, c0, 2 * cb, lane);
@@ -1468,6 +1452,7 @@ __device__ void build_act_local(const GemvParams& p, uint8_t* act, float* red, c
     }
 }
 
+template <bool WIDE>
 __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_constant__ ChainParams c) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kGemvMaxStages], empty[kGemvMaxStages], actbar;
@@ -1494,7 +1479,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
             int s = 0, lap = 0;
             const uint64_t policy = l2_evict_first_policy();
             for (int ph = 0; ph < c.nph; ph++)
-                if (!produce_units(c.ph[ph], c.epi[ph], r, s, lap, policy, &abort_flag)) break;
+                if (!produce_units<WIDE>(c.ph[ph], c.epi[ph], r, s, lap, policy, &abort_flag)) break;
             drain_ring(r, s, lap, &abort_flag);
         }
         return;
@@ -1537,13 +1522,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
         const Act a = act_view(p.act, smem);
         switch (c.epi[ph]) {
         case EPI_STORE:
-            consume_units<EPI_STORE>(p, a, r, s, lap, unit_no, glu_up, &best, &abort_flag, timed_out);
+            consume_units<EPI_STORE, WIDE>(p, a, r, s, lap, unit_no, glu_up, &best, &abort_flag, timed_out);
             break;
         case EPI_RESID:
-            consume_units<EPI_RESID>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out);
+            consume_units<EPI_RESID, WIDE>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out);
             break;
-        case EPI_QKV: consume_units<EPI_QKV>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out); break;
-        default: consume_units<EPI_GLU>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out); break;
+        case EPI_QKV: consume_units<EPI_QKV, WIDE>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out); break;
+        default: consume_units<EPI_GLU, WIDE>(p, a, r, s, lap, unit_no, glu_up, nullptr, &abort_flag, timed_out); break;
         }
         // every warp's writes of this phase, then one arrival for the CTA
         if (ph == c.nph - 1 && c.out_tok && lane == 0) {
@@ -1638,6 +1623,21 @@ void gemv_prepare(GemvParams& p, int sm_count) {
 
 size_t gemv_smem(const GemvParams& p) { return (size_t)p.act.bytes + (size_t)p.stages * p.stage_bytes; }
 
+// True when a matrix of the launch has a format only the WIDE kernel build carries.
+static bool needs_wide(const GemvParams& p) {
+    for (int i = 0; i < p.nseg; i++) {
+        const int t = p.seg[i].m.type;
+        if (t != TPTC_TYPE_Q4_K && t != TPTC_TYPE_Q6_K && t != TPTC_TYPE_Q8_0 && t != TPTC_TYPE_F16) return true;
+    }
+    return false;
+}
+
+static bool chain_wide(const ChainParams& c) {
+    for (int i = 0; i < c.nph; i++)
+        if (needs_wide(c.ph[i])) return true;
+    return false;
+}
+
 template <int EPI>
 static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
@@ -1650,7 +1650,8 @@ static cudaError_t launch_epi(const GemvParams& p, cudaStream_t st, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<EPI>, p);
+    return needs_wide(p) ? cudaLaunchKernelEx(&cfg, gemv_kernel<EPI, true>, p)
+                         : cudaLaunchKernelEx(&cfg, gemv_kernel<EPI, false>, p);
 }
 
 cudaError_t gemv_launch(const GemvParams& p, int epi, cudaStream_t st, bool pdl) {
@@ -1701,7 +1702,8 @@ size_t chain_smem(const ChainParams& c) { return (size_t)c.act_bytes + (size_t)c
 
 bool chain_fits(const ChainParams& c, int sm_count) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_chain_kernel, kThreads, chain_smem(c)) != cudaSuccess)
+    const void* fn = chain_wide(c) ? (const void*)gemv_chain_kernel<true> : (const void*)gemv_chain_kernel<false>;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, chain_smem(c)) != cudaSuccess)
         return false;
     return n * sm_count >= c.grid;
 }
@@ -1720,19 +1722,25 @@ cudaError_t chain_launch(const ChainParams& c, cudaStream_t st, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, c);
+    return chain_wide(c) ? cudaLaunchKernelEx(&cfg, gemv_chain_kernel<true>, c)
+                         : cudaLaunchKernelEx(&cfg, gemv_chain_kernel<false>, c);
+}
+
+template <bool WIDE>
+static cudaError_t set_smem_attrs(int max_smem) {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(gemv_chain_kernel<WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_STORE, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_RESID, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_QKV, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_GLU, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
+    return cudaFuncSetAttribute(gemv_kernel<EPI_DOTS, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
 
 cudaError_t gemv_init_device() {
     const int max_smem = 200 * 1024;
-    cudaError_t e;
-    if ((e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<EPI_GLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem))) return e;
-    return cudaFuncSetAttribute(gemv_kernel<EPI_DOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    cudaError_t e = set_smem_attrs<false>(max_smem);
+    return e != cudaSuccess ? e : set_smem_attrs<true>(max_smem);
 }
 
 }  // namespace tptc

@@ -8,7 +8,7 @@ namespace tptc {
 
 // Bytes per 256-element super-block in the device layout (all of it, GGUF size), the part
 // before a tile's scale section, and its share of that section; super-blocks per chunk.
-__host__ __device__ inline int sb_main_bytes(int type) {
+__host__ __device__ constexpr int sb_main_bytes(int type) {
     switch (type) {
     case TPTC_TYPE_Q2_K: return 80;
     case TPTC_TYPE_Q3_K: return 96;
@@ -21,7 +21,7 @@ __host__ __device__ inline int sb_main_bytes(int type) {
     }
     return 512;
 }
-__host__ __device__ inline int sb_d_bytes(int type) {
+__host__ __device__ constexpr int sb_d_bytes(int type) {
     switch (type) {
     case TPTC_TYPE_Q6_K: return 2;
     case TPTC_TYPE_Q2_K: return 4;
@@ -31,7 +31,7 @@ __host__ __device__ inline int sb_d_bytes(int type) {
     }
     return 0;
 }
-__host__ __device__ inline int sb_bytes(int type) { return sb_main_bytes(type) + sb_d_bytes(type); }
+__host__ __device__ constexpr int sb_bytes(int type) { return sb_main_bytes(type) + sb_d_bytes(type); }
 // The 32-element formats: eight blocks per super-block, activations quantised to Q8_0.
 __host__ __device__ inline bool type_q80_family(int type) {
     return type == TPTC_TYPE_Q8_0 || type == TPTC_TYPE_Q4_0 || type == TPTC_TYPE_Q5_0 || type == TPTC_TYPE_Q4_1 ||
