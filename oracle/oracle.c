@@ -26,7 +26,14 @@
  *     BlockQ4K, BlockQ5K, BlockQ6K, BlockQ4_0, BlockQ5_0, BlockQ8_0);
  *   - the quantized_llama forward: RmsNorm, interleaved RoPE (rope_i) from an f32
  *     cos/sin table, f32 KV concatenation, causal softmax(QK^T/sqrt(d))V, SwiGLU MLP,
- *     residual adds, final norm and the output projection on the last position only.
+ *     residual adds, final norm and the output projection on the last position only;
+ *   - its mixture-of-experts block (MlpOrMoe::MoE, the Mixtral GGUFs): softmax routing over
+ *     every expert, the top n_used by a stable descending sort, weights renormalised over
+ *     them, outputs accumulated in expert order (moe_ffn below); the reference's wgpu path adds
+ *     stacked expert tensors and a shared expert (wgpu_loader.rs:151-173,
+ *     wgpu_engine.rs:781-864), taken over here;
+ *   - gemma's GEGLU (the reference's shaders/geglu.wgsl tanh form) and sqrt(dim) embedding
+ *     scale.
  * The reference's own wgpu path (engine/wgpu_engine.rs) is not followed: its Q4_K
  * nibble layout is wrong (shaders/dequant_q4k.wgsl:9-21) and run_forward_pass has no
  * residual connections (wgpu_engine.rs:443,474).
@@ -964,6 +971,18 @@ typedef struct {
      * the two halves of each head (candle_nn::rotary_emb::rope) instead of interleaved pairs. */
     const float** biases;
     int rope_neox;
+    /* gemma: GEGLU feed-forward (gelu in the tanh form of the reference's shaders/geglu.wgsl:24-25,
+     * times up) and embedding rows times embd_scale (sqrt(dim)); 0 and 1.0 for the others. */
+    int ffn_geglu;
+    float embd_scale;
+    /* Mixture of experts (candle quantized_llama MlpOrMoe::MoE), n_expert > 1: moe[l * S ...],
+     * S = 4 + 3 * n_expert, holds layer l's router ([n_expert][dim], F32 or F16; NULL makes the
+     * layer dense), then each expert's gate, up and down ([expert_ffn][dim], [expert_ffn][dim],
+     * [dim][expert_ffn]), then a shared expert's gate, up and down ([shared_ffn] rows; NULL when
+     * absent); moe_types the GGML types alike. */
+    int n_expert, n_expert_used, expert_ffn, shared_ffn;
+    const void** moe;
+    const int* moe_types;
 } or_model_desc;
 
 typedef struct {
@@ -976,6 +995,8 @@ typedef struct {
     float* kc;      /* [L, max_seq, n_kv, hd] f32 */
     float* vc;
     const float** b;  /* copy of desc->biases, or NULL */
+    const void** moe; /* copies of desc->moe / moe_types, or NULL */
+    int* moe_ty;
     int n_past;
 } or_model;
 
@@ -1011,6 +1032,15 @@ void* or_model_create(const or_model_desc* desc) {
         memcpy(m->b, desc->biases, sizeof(float*) * 3 * desc->n_layers);
     }
     m->d.biases = m->b;
+    if (desc->n_expert > 1 && desc->moe) {
+        size_t nm = (size_t)desc->n_layers * (4 + 3 * (size_t)desc->n_expert);
+        m->moe = (const void**)malloc(sizeof(void*) * nm);
+        m->moe_ty = (int*)malloc(sizeof(int) * nm);
+        memcpy(m->moe, desc->moe, sizeof(void*) * nm);
+        memcpy(m->moe_ty, desc->moe_types, sizeof(int) * nm);
+    }
+    m->d.moe = m->moe;
+    m->d.moe_types = m->moe_ty;
     size_t ne = (size_t)desc->vocab * desc->dim;
     m->embd = (float*)malloc(ne * sizeof(float));
     or_dequant(m->ty[0], m->t[0], (int64_t)ne, m->embd);
@@ -1029,6 +1059,7 @@ void or_model_destroy(void* p) {
     if (!m) return;
     free(m->t); free(m->ty); free(m->embd); free(m->cos_t); free(m->sin_t); free(m->kc); free(m->vc);
     free((void*)m->b);
+    free((void*)m->moe); free(m->moe_ty);
     free(m);
 }
 
@@ -1081,6 +1112,97 @@ static void add_bias(float* y, const float* b, int n, int w) {
         for (int i = 0; i < w; i++) y[(size_t)r * w + i] += b[i];
 }
 
+/* GEGLU's gate activation times up, the reference's shaders/geglu.wgsl:24-25 operation order:
+ * ((g * 0.5) * (1 + tanh(0.7978845608 * (g + ((0.044715 * g) * g) * g)))) * u. */
+static float gelu_tanh_mul(float g, float u) {
+    float g3 = 0.044715f * g * g * g;
+    float t = tanhf(0.7978845608f * (g + g3));
+    return g * 0.5f * (1.f + t) * u;
+}
+
+/* candle quantized_llama Mlp::forward for one row: down(act(gate(x)) * up(x)), the activation
+ * silu (candle_nn::ops::silu: x / (1 + exp(-x))) or GEGLU's tanh gelu. */
+static void mlp_row(int tg, const void* wg, int tu, const void* wu, int td, const void* wd, int rows, int dim,
+                    const float* x, int geglu, float* g, float* u, float* y) {
+    or_matmul(tg, wg, rows, dim, x, 1, g);
+    or_matmul(tu, wu, rows, dim, x, 1, u);
+    for (int i = 0; i < rows; i++) g[i] = geglu ? gelu_tanh_mul(g[i], u[i]) : g[i] / (1.f + expf(-g[i])) * u[i];
+    or_matmul(td, wd, dim, rows, g, 1, y);
+}
+
+/* candle quantized_llama MlpOrMoe::MoE::forward over n rows, then the residual add:
+ *   routing_weights = softmax_last_dim(router(x))          (max, exp(l - max), sum in order)
+ *   experts sorted by weight, descending, stable (sort_by on total_cmp): the first n_used
+ *   w_e = rw[e] / (sum of the chosen rw in that order)
+ *   ys = 0; for e ascending among the chosen: ys = ys + mlp_e(x) * w_e   (index_add)
+ * then a shared expert (the reference's wgpu_engine.rs:840-853, weight 1): ys = ys + mlp_s(x);
+ * x = ys + x. */
+/* Optional per-layer record of the last row's routing margin: the router-logit gap between
+ * the n_used-th and the next expert (NaN for dense layers).  Tests use it to tell a routing
+ * near-tie, where two correct evaluations may choose different experts, from an error. */
+static float* g_route = NULL;
+void or_set_route_trace(float* gaps) { g_route = gaps; }
+
+static void moe_ffn(const or_model* m, int l, const float* xn, int n, float* x) {
+    const or_model_desc* d = &m->d;
+    const int E = d->n_expert, K = d->n_expert_used, eff = d->expert_ffn, sffn = d->shared_ffn, dim = d->dim;
+    const size_t S = 4 + 3 * (size_t)E;
+    const void** T = m->moe + (size_t)l * S;
+    const int* Ty = m->moe_ty + (size_t)l * S;
+    const int hmax = eff > sffn ? eff : sffn;
+    float* lg = (float*)malloc(sizeof(float) * E);
+    float* rw = (float*)malloc(sizeof(float) * E);
+    int* order = (int*)malloc(sizeof(int) * (K > 0 ? K : 1));
+    char* taken = (char*)malloc((size_t)E);
+    float* g = (float*)malloc(sizeof(float) * hmax);
+    float* u = (float*)malloc(sizeof(float) * hmax);
+    float* y = (float*)malloc(sizeof(float) * dim);
+    float* ys = (float*)malloc(sizeof(float) * dim);
+    for (int i = 0; i < n; i++) {
+        const float* xi = xn + (size_t)i * dim;
+        or_matmul(Ty[0], T[0], E, dim, xi, 1, lg);
+        float mx = -INFINITY, sum = 0.f;
+        for (int e = 0; e < E; e++) if (lg[e] > mx) mx = lg[e];
+        for (int e = 0; e < E; e++) rw[e] = expf(lg[e] - mx);
+        for (int e = 0; e < E; e++) sum += rw[e];
+        for (int e = 0; e < E; e++) rw[e] /= sum;
+        memset(taken, 0, (size_t)E);
+        for (int k = 0; k < K; k++) {
+            int best = -1;
+            for (int e = 0; e < E; e++)
+                if (!taken[e] && (best < 0 || rw[e] > rw[best])) best = e;
+            order[k] = best;
+            taken[best] = 1;
+        }
+        float ssel = 0.f;
+        for (int k = 0; k < K; k++) ssel += rw[order[k]];
+        if (g_route && i == n - 1) {
+            float next = -INFINITY;
+            for (int e = 0; e < E; e++)
+                if (!taken[e] && lg[e] > next) next = lg[e];
+            float kth = INFINITY;
+            for (int k = 0; k < K; k++)
+                if (lg[order[k]] < kth) kth = lg[order[k]];
+            g_route[l] = K < E ? kth - next : INFINITY;
+        }
+        for (int j = 0; j < dim; j++) ys[j] = 0.f;
+        for (int e = 0; e < E; e++) {
+            if (!taken[e]) continue;
+            const float we = rw[e] / ssel;
+            mlp_row(Ty[1 + 3 * e], T[1 + 3 * e], Ty[2 + 3 * e], T[2 + 3 * e], Ty[3 + 3 * e], T[3 + 3 * e], eff, dim, xi,
+                    d->ffn_geglu, g, u, y);
+            for (int j = 0; j < dim; j++) ys[j] = ys[j] + y[j] * we;
+        }
+        if (T[1 + 3 * E]) {
+            mlp_row(Ty[1 + 3 * E], T[1 + 3 * E], Ty[2 + 3 * E], T[2 + 3 * E], Ty[3 + 3 * E], T[3 + 3 * E], sffn, dim, xi,
+                    d->ffn_geglu, g, u, y);
+            for (int j = 0; j < dim; j++) ys[j] = ys[j] + y[j];
+        }
+        for (int j = 0; j < dim; j++) x[(size_t)i * dim + j] = ys[j] + x[(size_t)i * dim + j];
+    }
+    free(lg); free(rw); free(order); free(taken); free(g); free(u); free(y); free(ys);
+}
+
 /* One forward call: tokens[0..n) at absolute positions pos..pos+n-1, attending the
  * cached positions [0, pos).  Writes the last position's logits [vocab] and, when
  * hidden_out is non-NULL, the final-normed hidden state of the last position [dim].
@@ -1103,6 +1225,8 @@ int or_forward(void* p, const uint32_t* tokens, int n, int pos, float* logits, f
     float* g = (float*)malloc(sizeof(float) * (size_t)n * ffn);
     float* u = (float*)malloc(sizeof(float) * (size_t)n * ffn);
     for (int i = 0; i < n; i++) memcpy(x + (size_t)i * dim, m->embd + (size_t)tokens[i] * dim, sizeof(float) * dim);
+    if (d->embd_scale != 0.f && d->embd_scale != 1.f)
+        for (size_t i = 0; i < (size_t)n * dim; i++) x[i] = x[i] * d->embd_scale;
     float scale = (float)(1.0 / sqrt((double)hd));
     int kv_len = pos + n;
     for (int l = 0; l < d->n_layers; l++) {
@@ -1169,14 +1293,18 @@ int or_forward(void* p, const uint32_t* tokens, int n, int pos, float* logits, f
         or_matmul(Ty[4], T[4], dim, qd, att, n, tmp);
         for (size_t i = 0; i < (size_t)n * dim; i++) x[i] = tmp[i] + x[i];
         for (int i = 0; i < n; i++) rms_norm(x + (size_t)i * dim, (const float*)T[5], dim, d->rms_eps, xn + (size_t)i * dim);
-        or_matmul(Ty[6], T[6], ffn, dim, xn, n, g);
-        or_matmul(Ty[7], T[7], ffn, dim, xn, n, u);
-        for (size_t i = 0; i < (size_t)n * ffn; i++) {
-            float a = g[i];
-            g[i] = a / (1.f + expf(-a)) * u[i];
+        if (m->moe && m->moe[(size_t)l * (4 + 3 * (size_t)d->n_expert)]) {
+            moe_ffn(m, l, xn, n, x);
+        } else {
+            or_matmul(Ty[6], T[6], ffn, dim, xn, n, g);
+            or_matmul(Ty[7], T[7], ffn, dim, xn, n, u);
+            for (size_t i = 0; i < (size_t)n * ffn; i++) {
+                float a = g[i];
+                g[i] = d->ffn_geglu ? gelu_tanh_mul(a, u[i]) : a / (1.f + expf(-a)) * u[i];
+            }
+            or_matmul(Ty[8], T[8], dim, ffn, g, n, tmp);
+            for (size_t i = 0; i < (size_t)n * dim; i++) x[i] = tmp[i] + x[i];
         }
-        or_matmul(Ty[8], T[8], dim, ffn, g, n, tmp);
-        for (size_t i = 0; i < (size_t)n * dim; i++) x[i] = tmp[i] + x[i];
         if (g_trace) memcpy(g_trace + (size_t)(3 * l + 2) * dim, x + (size_t)(n - 1) * dim, sizeof(float) * dim);
     }
     float* last = x + (size_t)(n - 1) * dim;

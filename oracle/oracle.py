@@ -37,7 +37,11 @@ class _Desc(ctypes.Structure):
                 ("vocab", ctypes.c_int), ("max_seq", ctypes.c_int), ("rope_base", ctypes.c_float),
                 ("rms_eps", ctypes.c_float), ("rope_scale", ctypes.c_float),
                 ("tensors", ctypes.POINTER(ctypes.c_void_p)), ("types", ctypes.POINTER(ctypes.c_int)),
-                ("biases", ctypes.POINTER(ctypes.c_void_p)), ("rope_neox", ctypes.c_int)]
+                ("biases", ctypes.POINTER(ctypes.c_void_p)), ("rope_neox", ctypes.c_int),
+                ("ffn_geglu", ctypes.c_int), ("embd_scale", ctypes.c_float),
+                ("n_expert", ctypes.c_int), ("n_expert_used", ctypes.c_int), ("expert_ffn", ctypes.c_int),
+                ("shared_ffn", ctypes.c_int), ("moe", ctypes.POINTER(ctypes.c_void_p)),
+                ("moe_types", ctypes.POINTER(ctypes.c_int))]
 
 
 _L = None
@@ -74,6 +78,8 @@ def lib():
         L.or_repeat_penalty.argtypes = [vp, i32, vp, i32, ctypes.c_float]
         L.or_set_trace.restype = None
         L.or_set_trace.argtypes = [vp]
+        L.or_set_route_trace.restype = None
+        L.or_set_route_trace.argtypes = [vp]
         L.or_set_threads.restype = None
         L.or_set_threads.argtypes = [i32]
         L.or_set_norm_lanes.restype = None
@@ -169,9 +175,11 @@ def repeat_penalty(logits: np.ndarray, seen: Sequence[int], penalty: float) -> n
 
 
 class Model:
-    """candle quantized_llama (architectures llama / mistral), quantized_qwen2 (qwen2: q / k / v
-    biases, RoPE on head halves) or quantized_phi3 (phi3: fused attn_qkv and ffn_up, RoPE on head
-    halves) restated on CPU over a GGUF file (read with gguf-py)."""
+    """candle quantized_llama (architectures llama / mistral, with its mixture-of-experts block
+    when the file has experts), quantized_qwen2 (qwen2: q / k / v biases, RoPE on head halves) or
+    quantized_phi3 (phi3: fused attn_qkv and ffn_up, RoPE on head halves), or gemma (GEGLU,
+    embeddings times sqrt(dim), RoPE on head halves) restated on CPU over a GGUF file (read with
+    gguf-py)."""
 
     def __init__(self, path: str, max_seq: Optional[int] = None):
         import gguf
@@ -216,10 +224,53 @@ class Model:
                 t = tensors[p + "attn_qkv.weight"]
                 for n, (r0, r1) in (("attn_q", (0, nq)), ("attn_k", (nq, nq + nkv)), ("attn_v", (nq + nkv, nq + 2 * nkv))):
                     blocks[p + n + ".weight"] = (np.ascontiguousarray(t.data[r0:r1]), int(t.tensor_type))
-            if p + "ffn_gate.weight" not in tensors:
+            if p + "ffn_gate.weight" not in tensors and p + "ffn_up.weight" in tensors:
                 t = tensors[p + "ffn_up.weight"]
                 blocks[p + "ffn_gate.weight"] = (np.ascontiguousarray(t.data[:self.ffn]), int(t.tensor_type))
                 blocks[p + "ffn_up.weight"] = (np.ascontiguousarray(t.data[self.ffn:]), int(t.tensor_type))
+
+        # mixture of experts: layers with a router; experts stacked (ffn_*_exps, [E][rows][K]) or
+        # one tensor each (ffn_*.E); an optional shared expert (ffn_*_shexp)
+        n_exp = field(f"{arch}.expert_count", 0) or 0
+        self.n_expert = n_exp if n_exp > 1 else 0
+        self.n_expert_used = (field(f"{arch}.expert_used_count", 2) or 0) if self.n_expert else 0
+        self.expert_ffn = field(f"{arch}.expert_feed_forward_length", self.ffn) if self.n_expert else 0
+        self.shared_ffn = 0
+        moe_arrays, moe_types = [], []
+        if self.n_expert:
+            E = self.n_expert
+            for i in range(self.n_layers):
+                p = f"blk.{i}."
+                if p + "ffn_gate_inp.weight" not in tensors:
+                    moe_arrays += [None] * (4 + 3 * E)
+                    moe_types += [0] * (4 + 3 * E)
+                    continue
+                rt = tensors[p + "ffn_gate_inp.weight"]
+                moe_arrays.append(np.ascontiguousarray(rt.data))
+                moe_types.append(int(rt.tensor_type))
+                for e in range(E):
+                    for stem in ("ffn_gate", "ffn_up", "ffn_down"):
+                        if p + stem + "_exps.weight" in tensors:
+                            t = tensors[p + stem + "_exps.weight"]
+                            moe_arrays.append(np.ascontiguousarray(t.data[e]))
+                        else:
+                            t = tensors[f"{p}{stem}.{e}.weight"]
+                            moe_arrays.append(np.ascontiguousarray(t.data))
+                        moe_types.append(int(t.tensor_type))
+                for stem in ("ffn_gate", "ffn_up", "ffn_down"):
+                    n = p + stem + "_shexp.weight"
+                    if n in tensors:
+                        moe_arrays.append(np.ascontiguousarray(tensors[n].data))
+                        moe_types.append(int(tensors[n].tensor_type))
+                        if stem == "ffn_gate":
+                            self.shared_ffn = int(tensors[n].shape[1])
+                    else:
+                        moe_arrays.append(None)
+                        moe_types.append(0)
+                # a MoE layer has no dense ffn tensors; its dense slots hold the router, unread
+                router = moe_arrays[-(4 + 3 * E)], moe_types[-(4 + 3 * E)]
+                for stem in ("ffn_gate", "ffn_up", "ffn_down"):
+                    blocks.setdefault(p + stem + ".weight", router)
 
         def get(n):
             return blocks[n] if n in blocks else (np.ascontiguousarray(tensors[n].data), int(tensors[n].tensor_type))
@@ -239,8 +290,19 @@ class Model:
         d = _Desc(self.n_layers, self.dim, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.vocab,
                   self.max_seq, self.rope_base, self.rms_eps, 1.0, ptrs, tys,
                   ctypes.cast(barr, ctypes.POINTER(ctypes.c_void_p)) if barr is not None else None,
-                  1 if arch in ("qwen2", "phi3") else 0)
-        self._keep = (ptrs, tys, barr)
+                  1 if arch in ("qwen2", "phi3", "gemma") else 0)
+        d.ffn_geglu = 1 if arch == "gemma" else 0
+        d.embd_scale = float(np.float32(np.sqrt(np.float32(self.dim)))) if arch == "gemma" else 1.0
+        marr = mtys = None
+        if self.n_expert:
+            self._moe = moe_arrays
+            marr = (ctypes.c_void_p * len(moe_arrays))(*[a.ctypes.data if a is not None else None for a in moe_arrays])
+            mtys = (ctypes.c_int * len(moe_types))(*moe_types)
+            d.n_expert, d.n_expert_used = self.n_expert, self.n_expert_used
+            d.expert_ffn, d.shared_ffn = self.expert_ffn, self.shared_ffn
+            d.moe = ctypes.cast(marr, ctypes.POINTER(ctypes.c_void_p))
+            d.moe_types = ctypes.cast(mtys, ctypes.POINTER(ctypes.c_int))
+        self._keep = (ptrs, tys, barr, marr, mtys)
         self.h = lib().or_model_create(ctypes.byref(d))
 
     def forward(self, tokens: Sequence[int], pos: int, want_hidden: bool = False):
@@ -251,6 +313,19 @@ class Model:
         if rc != 0:
             raise ValueError("oracle forward rejected the input")
         return (logits, hid) if want_hidden else logits
+
+    def forward_route(self, tokens: Sequence[int], pos: int):
+        """forward() that also returns, per layer, the last position's routing margin: the
+        router-logit gap between the last chosen expert and the best one left out (NaN for
+        dense layers).  A small margin is a routing near-tie: evaluations that differ in the
+        last bits may choose different experts there."""
+        gaps = np.full(self.n_layers, np.nan, np.float32)
+        lib().or_set_route_trace(_p(gaps))
+        try:
+            logits = self.forward(tokens, pos)
+        finally:
+            lib().or_set_route_trace(None)
+        return logits, gaps
 
     def forward_trace(self, tokens: Sequence[int], pos: int):
         """forward() that also returns the per-layer trace [3 * n_layers, dim] of the last

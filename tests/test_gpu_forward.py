@@ -25,9 +25,11 @@ TIE_PRONE = {"tiny_q4km_tied"}
 # Greedy paths that pass through near-ties of the oracle's own top two logits (measured on the
 # oracle: tiny_q5km 0.046 at step 31 and 3.2e-4 at step 10, tiny_q4_0 2.3e-5 at step 60,
 # tiny_q2k 9.3e-5 at step 19, tiny_qwen2 1.8e-3 at step 6, tiny_phi3 4.5e-4 at step 24,
-# tiny_q4_1 3.4e-3 at step 11): a difference within the logit tolerance can pick the other
-# token there, so these sequences may part only at such a step.
-GREEDY_TIE_PRONE = TIE_PRONE | {"tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2", "tiny_phi3", "tiny_q4_1"}
+# tiny_q4_1 3.4e-3 at step 11, tiny_mixtral 9.6e-4 at step 41, tiny_moe 3.7e-4 at step 19):
+# a difference within the logit tolerance can pick the other token there, so these sequences
+# may part only at such a step.
+GREEDY_TIE_PRONE = TIE_PRONE | {"tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2", "tiny_phi3", "tiny_q4_1",
+                                "tiny_mixtral", "tiny_moe"}
 
 
 # tiny_phi3: the oracle's own logits move by up to 0.026 over the first steps of PROMPT when
@@ -39,6 +41,25 @@ FLOOR_ATOL = {"tiny_phi3": LOGIT_ATOL_TIES}
 
 def atol_for(name):
     return LOGIT_ATOL_TIES if name in TIE_PRONE else FLOOR_ATOL.get(name, LOGIT_ATOL)
+
+
+# Mixture of experts: the expert choice is discontinuous in the router logits.  Where the
+# oracle's gap between the last chosen expert and the best one left out is within the two
+# paths' numerical difference (the hidden states differ by about 1e-3), the GPU may choose the
+# other expert and the logits jump (tiny_mixtral with a router of std 0.05: 0.098 at a gap of
+# 1.2e-3; with the 0.2 router of the test models the smallest gaps on the 64-step paths are
+# 9.9e-3 at step 21 and, for tiny_moe, 3.9e-4 at step 44).  Such a step ends a comparison; it is accepted only after ROUTE_MIN_STEPS strict
+# steps and only where the oracle reports a gap below ROUTE_TIE at that step or before.
+ROUTE_TIE = 1e-2
+ROUTE_MIN_STEPS = 16
+
+
+def oracle_step(ref, tokens, pos):
+    """Oracle logits and its smallest routing margin over the layers (inf without experts)."""
+    if not getattr(ref, "n_expert", 0):
+        return ref.forward(tokens, pos), float("inf")
+    lo, gaps = ref.forward_route(tokens, pos)
+    return lo, float(np.nanmin(gaps))
 PROMPT = [3, 141, 59, 26, 5, 358, 97, 93, 238, 46, 264, 33]
 
 
@@ -70,7 +91,7 @@ def engines_f16kv(tiny_models, cuda_device):
 
 
 MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2",
-          "tiny_phi3", "tiny_q4_1"]
+          "tiny_phi3", "tiny_q4_1", "tiny_mixtral", "tiny_moe", "tiny_gemma"]
 
 
 @pytest.mark.parametrize("name", MODELS)
@@ -98,13 +119,18 @@ def test_teacher_forced_logits_and_argmax(engines, tiny_models, name):
     np.testing.assert_allclose(lg, lo, rtol=0, atol=atol)
     pos = len(prompt)
     worst = 0.0
+    route_tie = False
     for step in range(64):
         tok = O.argmax(lo)
         g_logits, g_tok = e.decode(tok, pos)
-        lo = ref.forward([tok], pos)
+        lo, rgap = oracle_step(ref, [tok], pos)
+        route_tie = route_tie or rgap <= ROUTE_TIE
         top2 = np.sort(lo)[-2:]
         margin = float(top2[1] - top2[0])  # oracle's top-2 gap for this step
         diff = float(np.abs(g_logits - lo).max())
+        if diff > atol and route_tie and step >= ROUTE_MIN_STEPS:
+            print(f"{name}: routing near-tie (margin {rgap:.1e}) at step {step}, diff {diff:.2e}: stop")
+            break
         worst = max(worst, diff)
         assert diff <= atol, f"step {step}"
         # an argmax may only differ where the oracle's own top-2 gap is within the
@@ -126,11 +152,16 @@ def test_fp16_kv_logits_within_tolerance(engines_f16kv, tiny_models, name):
     lo = ref.forward(prompt, 0)
     worst = float(np.abs(lg - lo).max())
     pos = len(prompt)
+    route_tie = False
     for step in range(32):
         tok = O.argmax(lo)
         g_logits, _ = e.decode(tok, pos)
-        lo = ref.forward([tok], pos)
-        worst = max(worst, float(np.abs(g_logits - lo).max()))
+        lo, rgap = oracle_step(ref, [tok], pos)
+        route_tie = route_tie or rgap <= ROUTE_TIE
+        diff = float(np.abs(g_logits - lo).max())
+        if diff > LOGIT_ATOL_F16KV and route_tie and step >= ROUTE_MIN_STEPS:
+            break
+        worst = max(worst, diff)
         pos += 1
     print(f"{name} fp16 KV: max |logit diff| over 32 steps = {worst:.2e}")
     assert worst <= LOGIT_ATOL_F16KV
@@ -149,11 +180,20 @@ def test_greedy_64_identical(engines, tiny_models, name):
     if name not in GREEDY_TIE_PRONE:
         assert got == want
         return
-    # tie-prone model: the sequences may part only where the oracle itself is near a tie
+    # tie-prone model: the sequences may part only where the oracle itself is near a tie (of
+    # its top two logits, or, with experts, of its routing at that step or before)
     if got != want:
         k = next(i for i, (a, b) in enumerate(zip(got, want)) if a != b)
         lo = ref.__class__(tiny_models[name]).forward(prompt + want[:k], 0) if k else ref.forward(prompt, 0)
         top2 = np.sort(lo)[-2:]
+        if top2[1] - top2[0] > 2 * LOGIT_ATOL_TIES and getattr(ref, "n_expert", 0):
+            walk = ref.__class__(tiny_models[name])
+            _, gap = oracle_step(walk, prompt, 0)
+            for i in range(k):
+                _, g = oracle_step(walk, [want[i]], len(prompt) + i)
+                gap = min(gap, g)
+            assert k >= ROUTE_MIN_STEPS and gap <= ROUTE_TIE, f"diverged at step {k}, routing margin {gap}"
+            return
         assert top2[1] - top2[0] <= 2 * LOGIT_ATOL_TIES, f"diverged at step {k} with margin {top2[1] - top2[0]}"
 
 

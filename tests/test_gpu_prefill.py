@@ -21,7 +21,10 @@ from tpt_spark_b200._lib import EngineError  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2",
-          "tiny_phi3", "tiny_q4_1"]
+          "tiny_phi3", "tiny_q4_1", "tiny_gemma", "tiny_mixtral", "tiny_moe"]
+# mixture-of-experts models prefill position by position through the decode graph (8-bit
+# activations, the oracle's semantics), so the fp16-operand float reference does not apply
+BATCHED = [n for n in MODELS if n not in ("tiny_mixtral", "tiny_moe")]
 
 # fp16 operands (11-bit significands) against a float64 forward: relative error of a few
 # 2^-11 per layer on the hidden state, times the logit scale of the tiny models (|logit| < 3)
@@ -119,7 +122,9 @@ def float_prefill_logits(ref, tokens):
     def rms(x, g):
         return x / np.sqrt((x * x).mean(-1, keepdims=True) + ref.rms_eps) * g
 
-    neox = getattr(ref, "arch", "llama") in ("qwen2", "phi3")
+    arch = getattr(ref, "arch", "llama")
+    neox = arch in ("qwen2", "phi3", "gemma")
+    geglu = arch == "gemma"  # GEGLU and embeddings times sqrt(dim)
 
     def rope(x, n):  # [T, n*hd]: interleaved pairs (rope_i), or the head's two halves (qwen2)
         c, s = cos[:, None, :], sin[:, None, :]
@@ -140,6 +145,8 @@ def float_prefill_logits(ref, tokens):
         return 0.0 if b is None else b.astype(np.float64)
 
     x = w["emb"][np.asarray(tokens)]
+    if geglu:
+        x = x * np.float64(np.float32(np.sqrt(np.float32(D))))
     mask = np.triu(np.full((T, T), -np.inf), 1)
     for li, L in enumerate(w["layers"]):
         xn = rms(x, L["attn_norm"])
@@ -154,7 +161,8 @@ def float_prefill_logits(ref, tokens):
         x = x + att.reshape(T, H * hd) @ L["o"].T
         xn = rms(x, L["ffn_norm"])
         gt, up = xn @ L["gate"].T, xn @ L["up"].T
-        x = x + (gt / (1 + np.exp(-gt)) * up) @ L["down"].T
+        act = gt * 0.5 * (1 + np.tanh(0.7978845608 * (gt + 0.044715 * gt ** 3))) if geglu else gt / (1 + np.exp(-gt))
+        x = x + (act * up) @ L["down"].T
     last = rms(x[-1:], w["out_norm"]).astype(np.float32)
     out_i = 2
     return O.matmul(ref._types[out_i], ref._arrays[out_i], ref.vocab, D, last)[0]
@@ -179,7 +187,7 @@ def _prompt(ref, n, seed):
     return [int(t) for t in np.random.default_rng(seed).integers(0, ref.vocab, n)]
 
 
-@pytest.mark.parametrize("name", MODELS)
+@pytest.mark.parametrize("name", BATCHED)
 def test_batched_prefill_matches_float_reference(engines_f16, tiny_models, name):
     e = engines_f16[name]
     ref = O.Model(tiny_models[name])
@@ -204,11 +212,18 @@ def test_batched_prefill_then_decode_against_oracle(engines_f16, tiny_models, na
     lo = ref.forward(prompt, 0)
     worst = float(np.abs(lg - lo).max())
     pos = len(prompt)
-    for _ in range(32):
+    route_tie = False
+    for step in range(32):
         tok = O.argmax(lo)
         g_logits, g_tok = e.decode(tok, pos)
-        lo = ref.forward([tok], pos)
+        if ref.n_expert:  # routing near-ties end the comparison (tests/test_gpu_forward.py)
+            lo, gaps = ref.forward_route([tok], pos)
+            route_tie = route_tie or float(np.nanmin(gaps)) <= 1e-2
+        else:
+            lo = ref.forward([tok], pos)
         d = float(np.abs(g_logits - lo).max())
+        if d > LOGIT_ATOL_ORACLE and route_tie and step >= 16:
+            break
         worst = max(worst, d)
         top2 = np.sort(lo)[-2:]
         if top2[1] - top2[0] > 2 * d:

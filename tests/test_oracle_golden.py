@@ -237,7 +237,7 @@ def test_argmax_ties_last_and_repeat_penalty():
     np.testing.assert_array_equal(O.repeat_penalty(lg, [1], 1.0), lg)
 
 
-@pytest.mark.parametrize("name", ["tiny_q4km", "tiny_qwen2", "tiny_phi3"])
+@pytest.mark.parametrize("name", ["tiny_q4km", "tiny_qwen2", "tiny_phi3", "tiny_mixtral", "tiny_moe", "tiny_gemma"])
 def test_forward_prefill_equals_incremental(tmp_path, name):
     """candle's batched prefill and one-token steps give the same last-position logits."""
     from tpt_spark_b200 import synth
@@ -342,3 +342,125 @@ def test_tiny_phi3_reordering_floor(tmp_path):
     finally:
         O.set_norm_lanes(1)
     assert worst > 2e-2
+
+
+# ---- mixture of experts and GEGLU: the C restatement against a second one in numpy
+
+def _libm():
+    import ctypes
+
+    m = ctypes.CDLL("libm.so.6")
+    for fn in ("expf", "tanhf"):
+        getattr(m, fn).restype = ctypes.c_float
+        getattr(m, fn).argtypes = [ctypes.c_float]
+    return m
+
+
+def _seq_sum(a):
+    s = np.float32(0.0)
+    for v in np.asarray(a, np.float32):
+        s = np.float32(s + v)
+    return s
+
+
+def _rms_norm(x, w, eps):
+    m = np.sqrt(np.float32(_seq_sum(x * x) / np.float32(x.size) + np.float32(eps)))
+    return (x / m * w).astype(np.float32)
+
+
+def _mlp(reader, names, x, rows, geglu, expert=None):
+    """candle Mlp::forward on one row: down(act(gate(x)) * up(x)) with QMatMul semantics."""
+    libm = _libm()
+    dim = x.size
+    out = []
+    for n in names[:2]:
+        t = reader[n]
+        w = t.data[expert] if expert is not None else t.data
+        out.append(O.matmul(int(t.tensor_type), np.ascontiguousarray(w), rows, dim, x)[0])
+    g, u = out
+    h = np.empty(rows, np.float32)
+    for i in range(rows):
+        gi, ui = np.float32(g[i]), np.float32(u[i])
+        if geglu:
+            g3 = np.float32(np.float32(np.float32(np.float32(0.044715) * gi) * gi) * gi)
+            t_ = np.float32(libm.tanhf(float(np.float32(np.float32(0.7978845608) * np.float32(gi + g3)))))
+            h[i] = np.float32(np.float32(np.float32(gi * np.float32(0.5)) * np.float32(np.float32(1.0) + t_)) * ui)
+        else:
+            h[i] = np.float32(np.float32(gi / np.float32(np.float32(1.0) + np.float32(libm.expf(float(-gi))))) * ui)
+    t = reader[names[2]]
+    w = t.data[expert] if expert is not None else t.data
+    return O.matmul(int(t.tensor_type), np.ascontiguousarray(w), dim, rows, h)[0]
+
+
+def _layer_ffn_input(m, tokens, layer):
+    """(residual after layer `layer`'s attention, the oracle's residual after the layer) for the
+    last of `tokens`, from the oracle's per-layer trace and its o projection."""
+    logits, tr = m.forward_trace(tokens, 0)
+    R = {t.name: t for t in m.reader.tensors}
+    x_prev = tr[3 * (layer - 1) + 2]
+    att = tr[3 * layer + 1]
+    wo = R[f"blk.{layer}.attn_output.weight"]
+    o = O.matmul(int(wo.tensor_type), np.ascontiguousarray(wo.data), m.dim, m.dim, att)[0]
+    return (o + x_prev).astype(np.float32), tr[3 * layer + 2], R
+
+
+@pytest.mark.parametrize("name", ["tiny_mixtral", "tiny_moe"])
+def test_moe_oracle_matches_restatement(tmp_path, name):
+    """candle MlpOrMoe::MoE restated a second time in numpy on the oracle's primitives (router
+    matmul, softmax with glibc expf, stable descending sort, renormalised weights, index_add in
+    expert order, shared expert, residual add) gives the oracle's residual bit for bit."""
+    from tpt_spark_b200 import synth
+
+    cfg = synth.TINY[name]
+    p = str(tmp_path / "m.gguf")
+    synth.write_gguf(p, cfg, seed=2)
+    m = O.Model(p, max_seq=64)
+    libm = _libm()
+    layer = 1
+    x_mid, want, R = _layer_ffn_input(m, [11, 200, 45, 3], layer)
+    pre = f"blk.{layer}."
+    xn = _rms_norm(x_mid, np.asarray(R[pre + "ffn_norm.weight"].data, np.float32), m.rms_eps)
+    rt = R[pre + "ffn_gate_inp.weight"]
+    E, K = cfg.n_expert, cfg.n_expert_used
+    lg = O.matmul(int(rt.tensor_type), np.ascontiguousarray(rt.data), E, m.dim, xn)[0]
+    mx = lg.max()
+    rw = np.array([libm.expf(float(np.float32(v - mx))) for v in lg], np.float32)
+    rw = (rw / _seq_sum(rw)).astype(np.float32)
+    order = np.argsort(-rw, kind="stable")[:K]
+    ssel = _seq_sum(rw[order])
+    ys = np.zeros(m.dim, np.float32)
+    stacked = pre + "ffn_gate_exps.weight" in R
+    for e in sorted(order.tolist()):
+        names = ([pre + s + "_exps.weight" for s in ("ffn_gate", "ffn_up", "ffn_down")] if stacked else
+                 [f"{pre}{s}.{e}.weight" for s in ("ffn_gate", "ffn_up", "ffn_down")])
+        y = _mlp(R, names, xn, cfg.expert_ffn, False, expert=e if stacked else None)
+        ys = (ys + y * np.float32(rw[e] / ssel)).astype(np.float32)
+    if cfg.shared_ffn:
+        y = _mlp(R, [pre + s + "_shexp.weight" for s in ("ffn_gate", "ffn_up", "ffn_down")], xn, cfg.shared_ffn, False)
+        ys = (ys + y).astype(np.float32)
+    got = (ys + x_mid).astype(np.float32)
+    np.testing.assert_array_equal(bits(got), bits(want))
+    assert len(set(order.tolist())) == K
+
+
+def test_gemma_oracle_matches_restatement(tmp_path):
+    """gemma's dense block (GEGLU with glibc tanhf in geglu.wgsl's operation order) restated in
+    numpy gives the oracle's residual bit for bit; the embeddings carry the sqrt(dim) factor."""
+    from tpt_spark_b200 import synth
+
+    cfg = synth.TINY["tiny_gemma"]
+    p = str(tmp_path / "g.gguf")
+    synth.write_gguf(p, cfg, seed=2)
+    m = O.Model(p, max_seq=64)
+    layer = 1
+    x_mid, want, R = _layer_ffn_input(m, [11, 200, 45, 3], layer)
+    pre = f"blk.{layer}."
+    xn = _rms_norm(x_mid, np.asarray(R[pre + "ffn_norm.weight"].data, np.float32), m.rms_eps)
+    y = _mlp(R, [pre + s + ".weight" for s in ("ffn_gate", "ffn_up", "ffn_down")], xn, cfg.ffn, True)
+    np.testing.assert_array_equal(bits((y + x_mid).astype(np.float32)), bits(want))
+    # the first layer's input is the embedding row times sqrt(dim)
+    import dataclasses
+
+    p1 = str(tmp_path / "l.gguf")
+    synth.write_gguf(p1, dataclasses.replace(cfg, arch="llama"), seed=2)
+    assert np.abs(O.Model(p1, max_seq=64).forward([7], 0) - m.forward([7], 0)).max() > 1e-3

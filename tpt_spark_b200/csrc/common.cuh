@@ -143,6 +143,14 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
 }
 
 // Programmatic dependent launch: wait for the producing grid / let the next grid start.
+// GEGLU's gate activation times up: gelu(g) = g * 0.5 * (1 + tanh(0.7978845608 * (g + 0.044715 g^3))),
+// the tanh form and operation order of the reference's shaders/geglu.wgsl:24-25, unfused.
+__device__ __forceinline__ float gelu_tanh_mul(float g, float u) {
+    const float g3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g);
+    const float t = tanhf(__fmul_rn(0.7978845608f, __fadd_rn(g, g3)));
+    return __fmul_rn(__fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.f, t)), u);
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -8,6 +8,7 @@
 #include <chrono>
 
 #include "kernels.h"
+#include "moe.h"
 #include "prefill.h"
 #include "tp.h"
 
@@ -211,13 +212,18 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
     // the reference runs it on its wgpu path, wgpu_loader.rs:270, bias_add.wgsl).
     // phi3 (candle quantized_phi3): one fused attn_qkv tensor (rows q | k | v, the reference's
     // wgpu_engine.rs:385-397) and one fused ffn_up tensor (rows gate | up), RoPE on head halves.
+    // gemma (the reference's arch table gives it GEGLU and a tied lm_head, wgpu_loader.rs:220,270)
+    // follows its model definition: GEGLU with the tanh gelu, embeddings scaled by sqrt(dim),
+    // RoPE on head halves; its GGUF norm gains already carry the +1.  gemma2 / gemma3 add
+    // post-norms and logit soft-capping, which this forward pass does not have.
     ModelMeta m;
     f.get_str("general.architecture", m.architecture);
     if (m.architecture != "llama" && m.architecture != "mistral" && m.architecture != "qwen2" &&
-        m.architecture != "phi3")
+        m.architecture != "phi3" && m.architecture != "gemma")
         return err(TPTC_ERR_UNSUPPORTED, "Architecture '" + m.architecture +
-                                             "' is not yet supported. Supported: llama, mistral, qwen2, phi3.");
-    m.rope_neox = m.architecture == "qwen2" || m.architecture == "phi3";
+                                             "' is not yet supported. Supported: llama, mistral, qwen2, phi3, gemma.");
+    m.rope_neox = m.architecture == "qwen2" || m.architecture == "phi3" || m.architecture == "gemma";
+    m.geglu = m.architecture == "gemma";
     f.get_str("general.name", m.name);
     const std::string a = m.architecture;
     uint64_t u;
@@ -251,6 +257,23 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
     if (m.head_dim != 64 && m.head_dim != 96 && m.head_dim != 128)
         return err(TPTC_ERR_UNSUPPORTED, "head_dim must be 64, 96 or 128");
     if (m.dim % QK_K || m.ffn % QK_K) return err(TPTC_ERR_UNSUPPORTED, "embedding/ffn sizes must be multiples of 256");
+    if (m.geglu) m.embd_scale = sqrtf((float)m.dim);
+    // mixture of experts (wgpu_loader.rs:367-377: expert_used_count defaults to 2 when absent)
+    m.n_expert = getu("expert_count", 0);
+    if (m.n_expert > 1) {
+        m.n_expert_used = getu("expert_used_count", 2);
+        m.expert_ffn = getu("expert_feed_forward_length", m.ffn);
+        if (m.n_expert > kMoeMaxExperts || m.n_expert_used < 1 || m.n_expert_used > kMoeMaxUsed ||
+            m.n_expert_used > m.n_expert)
+            return err(TPTC_ERR_UNSUPPORTED, "expert_count / expert_used_count out of range (at most " +
+                                                 std::to_string(kMoeMaxExperts) + " experts, " +
+                                                 std::to_string(kMoeMaxUsed) + " chosen per token)");
+        if (m.expert_ffn % QK_K || m.dim > kMoeMaxDim)
+            return err(TPTC_ERR_UNSUPPORTED, "expert feed-forward size must be a multiple of 256");
+        if (tp_size_ > 1) return err(TPTC_ERR_UNSUPPORTED, "mixture-of-experts models run on one GPU (tp_size 1)");
+    } else {
+        m.n_expert = 0;
+    }
     int sh[7][4];
     for (int w = 0; w < 7; w++)
         if (!tp_shard(w, m.n_heads, m.n_kv_heads, m.head_dim, m.dim, m.ffn, tp_rank_, tp_size_, sh[w][0], sh[w][1],
@@ -280,6 +303,10 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         float** vec;
         int first_row;       // logical row of r0 in `mat`
         int glu_rows;        // > 0: `mat` is a fused gate|up matrix of this many rows
+        int expert = -1;     // >= 0: this expert's [N x K] slice of a stacked [n_stack][N][K] tensor
+        int n_stack = 0;
+        const void** raw = nullptr;  // F32 / F16 rows copied as they are (the MoE router)
+        int* raw_type = nullptr;
     };
     std::vector<Plan> plans;
     layers_.assign(m.n_layers, LayerWeights{});
@@ -315,14 +342,55 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         }
         W(TPTC_SHARD_O, "attn_output.weight", m.dim, m.n_heads * hd, &L.o, 0, 0);
         plans.push_back({p + "ffn_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &L.ffn_norm, 0, 0});
-        if (m.fused_gate_up) {  // ffn_up rows [0, ffn) gate, [ffn, 2 ffn) up
+        L.moe = m.n_expert > 1 && f.find(p + "ffn_gate_inp.weight") != nullptr;
+        if (L.moe) {
+            // router [n_expert][dim]; the experts stacked (ffn_*_exps, llama.cpp's layout, split per
+            // expert as wgpu_loader.rs:151-173 does) or one tensor each (ffn_*.E, candle's
+            // quantized_llama names); gate|up of every expert first, then every down, so each
+            // group lands at a uniform stride in the arena
+            Plan rp{p + "ffn_gate_inp.weight", m.n_expert, m.dim, 0, m.n_expert, 0, m.dim, nullptr, nullptr, 0, 0};
+            rp.raw = &L.router;
+            rp.raw_type = &L.router_type;
+            plans.push_back(rp);
+            const int E = m.n_expert, eff = m.expert_ffn;
+            const bool stacked = f.find(p + "ffn_gate_exps.weight") != nullptr;
+            L.eglu_all.assign(E, DevMatrix{});
+            L.edown_all.assign(E, DevMatrix{});
+            auto X = [&](const char* stem, int e, int N, int K, DevMatrix* mat, int first_row, int glu_rows) {
+                Plan q{stacked ? p + stem + "_exps.weight" : p + stem + "." + std::to_string(e) + ".weight",
+                       N, K, 0, N, 0, K, mat, nullptr, first_row, glu_rows};
+                if (stacked) {
+                    q.expert = e;
+                    q.n_stack = E;
+                }
+                plans.push_back(q);
+            };
+            for (int e = 0; e < E; e++) {
+                X("ffn_gate", e, eff, m.dim, &L.eglu_all[e], 0, 2 * eff);
+                X("ffn_up", e, eff, m.dim, &L.eglu_all[e], eff, 2 * eff);
+            }
+            for (int e = 0; e < E; e++) X("ffn_down", e, m.dim, eff, &L.edown_all[e], 0, 0);
+            // an always-on shared expert (the reference's wgpu_engine.rs:840-853)
+            if (const GgufTensor* sg = f.find(p + "ffn_gate_shexp.weight")) {
+                const int sffn = sg->ne.size() == 2 ? (int)sg->ne[1] : 0;
+                if (sffn <= 0 || sffn % QK_K)
+                    return err(TPTC_ERR_UNSUPPORTED, "shared expert rows must be a multiple of 256");
+                if (meta_.shared_ffn && meta_.shared_ffn != sffn)
+                    return err(TPTC_ERR_UNSUPPORTED, "shared experts of different sizes");
+                meta_.shared_ffn = sffn;
+                L.shexp = true;
+                plans.push_back({p + "ffn_gate_shexp.weight", sffn, m.dim, 0, sffn, 0, m.dim, &L.glu, nullptr, 0, 2 * sffn});
+                plans.push_back({p + "ffn_up_shexp.weight", sffn, m.dim, 0, sffn, 0, m.dim, &L.glu, nullptr, sffn, 2 * sffn});
+                plans.push_back({p + "ffn_down_shexp.weight", m.dim, sffn, 0, m.dim, 0, sffn, &L.down, nullptr, 0, 0});
+            }
+        } else if (m.fused_gate_up) {  // ffn_up rows [0, ffn) gate, [ffn, 2 ffn) up
             W(TPTC_SHARD_GATE, "ffn_up.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l, 0, 2 * m.ffn);
             W(TPTC_SHARD_UP, "ffn_up.weight", m.ffn, m.dim, &L.glu, ffn_l, 2 * ffn_l, m.ffn, 2 * m.ffn);
         } else {
             W(TPTC_SHARD_GATE, "ffn_gate.weight", m.ffn, m.dim, &L.glu, 0, 2 * ffn_l);
             W(TPTC_SHARD_UP, "ffn_up.weight", m.ffn, m.dim, &L.glu, ffn_l, 2 * ffn_l);
         }
-        W(TPTC_SHARD_DOWN, "ffn_down.weight", m.dim, m.ffn, &L.down, 0, 0);
+        if (!L.moe) W(TPTC_SHARD_DOWN, "ffn_down.weight", m.dim, m.ffn, &L.down, 0, 0);
     }
     plans.push_back({"output_norm.weight", 1, m.dim, 0, 1, 0, m.dim, nullptr, &out_norm_, 0, 0});
     // lm_head: vocab-parallel under tensor parallelism when the vocabulary splits evenly (each
@@ -348,11 +416,21 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         const GgufTensor* t = f.find(p.name);
         if (!t) return err(TPTC_ERR_FORMAT, "missing tensor '" + p.name + "'");
         tens[i] = t;
-        const bool vec = p.mat == nullptr;
+        const bool vec = p.mat == nullptr && p.raw == nullptr;
         const uint64_t want0 = (uint64_t)p.K, want1 = (uint64_t)p.N;
         bool shape_ok = vec ? (t->ne.size() == 1 && t->ne[0] == want0)
-                            : (t->ne.size() == 2 && t->ne[0] == want0 && t->ne[1] == want1);
+                        : p.n_stack ? (t->ne.size() == 3 && t->ne[0] == want0 && t->ne[1] == want1 &&
+                                       t->ne[2] == (uint64_t)p.n_stack)
+                                    : (t->ne.size() == 2 && t->ne[0] == want0 && t->ne[1] == want1);
         if (!shape_ok) return err(TPTC_ERR_FORMAT, "tensor '" + p.name + "' has an unexpected shape");
+        if (p.raw) {  // the MoE router: f32 or f16 rows, used as they are (candle dequantises to f32)
+            if (t->type != TPTC_TYPE_F32 && t->type != TPTC_TYPE_F16)
+                return err(TPTC_ERR_UNSUPPORTED, "router tensor '" + p.name + "' must be F32 or F16");
+            *p.raw_type = (int)t->type;
+            offs[i] = off;
+            off = align_up(off + (size_t)p.N * p.K * (t->type == TPTC_TYPE_F32 ? 4 : 2), 256);
+            continue;
+        }
         if (vec) {
             if (t->type != TPTC_TYPE_F32) return err(TPTC_ERR_UNSUPPORTED, "vector tensor '" + p.name + "' must be F32");
             offs[i] = off;
@@ -388,7 +466,15 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
         Plan& p = plans[i];
         const GgufTensor* t = tens[i];
         const uint8_t* src = f.tensor_data(*t);
-        if (!p.mat) {
+        if (p.raw) {
+            const int64_t rb = (int64_t)p.K * (*p.raw_type == TPTC_TYPE_F32 ? 4 : 2);
+            *p.raw = arena_ + offs[i];
+            DevMatrix tmp;
+            tmp.type = TPTC_TYPE_F32;  // copied as is
+            tmp.main = arena_ + offs[i];
+            RET_IF(upload_rows(sg, src, rb, 0, p.N, 0, rb, tmp, 0));
+            weight_bytes_ += (uint64_t)p.N * rb;
+        } else if (!p.mat) {
             *p.vec = reinterpret_cast<float*>(arena_ + offs[i]);
             DevMatrix tmp;
             tmp.type = TPTC_TYPE_F32;
@@ -402,12 +488,29 @@ Status Engine::load(const std::string& path, tptc_progress_cb cb, void* user) {
             }
             const int64_t rrb = raw_row_bytes(d.type, p.K);
             const int64_t c0 = raw_row_bytes(d.type, p.k0), c1 = raw_row_bytes(d.type, p.k1);
+            if (p.expert >= 0) src += (int64_t)p.expert * p.N * rrb;  // this expert's slice of the stack
             RET_IF(upload_rows(sg, src, rrb, p.r0, p.r1, c0, c1, d, p.first_row));
             weight_bytes_ += (uint64_t)(p.r1 - p.r0) * d.main_row_bytes;
         }
         if (cb) cb((uint32_t)(i + 1), (uint32_t)plans.size(), user);
     }
     if (m.tied && !head_sliced) output_ = embd_;
+    // every expert of a layer: one type and shape, at a uniform stride (the GEMVs address
+    // expert e as expert 0's matrix plus e strides)
+    for (LayerWeights& L : layers_) {
+        if (!L.moe) continue;
+        auto stack = [&](const std::vector<DevMatrix>& all, DevMatrix& first, int64_t& stride) -> bool {
+            first = all[0];
+            stride = all.size() > 1 ? (int64_t)(all[1].main - all[0].main) : 0;
+            for (size_t e = 1; e < all.size(); e++)
+                if (all[e].type != first.type || all[e].N != first.N || all[e].K != first.K ||
+                    all[e].main != first.main + (int64_t)e * stride)
+                    return false;
+            return true;
+        };
+        if (!stack(L.eglu_all, L.eglu, L.eglu_stride) || !stack(L.edown_all, L.edown, L.edown_stride))
+            return err(TPTC_ERR_UNSUPPORTED, "the experts of a layer must share one GGML type per projection");
+    }
     CU(cudaStreamSynchronize(stream_));
     RET_IF(alloc_runtime());
     loaded_ = true;
@@ -432,12 +535,19 @@ Status Engine::alloc_runtime() {
     const size_t o_x = take((size_t)m.dim * 4), o_x2 = take((size_t)m.dim * 4);
     const size_t o_q = take((size_t)n_heads_l_ * hd * 4), o_att = take((size_t)n_heads_l_ * hd * 4);
     const size_t o_qr = take((size_t)n_heads_l_ * hd * 4), o_kr = take((size_t)n_kv_l_ * hd * 4);
-    const size_t o_h = take((size_t)2 * (m.ffn / tp_size_) * 4), o_lg = take((size_t)m.vocab * 4);
+    // h: [2 ffn_l] (gate|up products); under MoE the selected experts' products side by side,
+    // then the shared expert's
+    const size_t h_floats = std::max((size_t)2 * (m.ffn / tp_size_),
+                                     (size_t)m.n_expert_used * m.expert_ffn + (size_t)m.shared_ffn);
+    const size_t o_h = take(h_floats * 4), o_lg = take((size_t)m.vocab * 4);
+    const size_t o_mlg = take((size_t)std::max(1, m.n_expert) * 4), o_msel = take((size_t)kMoeMaxUsed * 4);
+    const size_t o_mw = take((size_t)kMoeMaxUsed * 4), o_macc = take((size_t)m.dim * 4);
     const size_t o_ti = take(64), o_to = take(64), o_pos = take(64), o_err = take(64), o_step = take(64);
     const size_t o_hist = take((size_t)max_seq_ * 4 + 64);
     const size_t o_part = take(attn_decode_partial_floats(n_heads_l_, n_kv_l_, hd, attn_splits_) * 4);
     const size_t o_cnt = take((size_t)n_kv_l_ * 4);
-    const int k_max = std::max(m.dim, std::max(m.ffn / tp_size_, n_heads_l_ * hd));
+    const int k_max = std::max(std::max(m.dim, std::max(m.ffn / tp_size_, n_heads_l_ * hd)),
+                               std::max(m.expert_ffn, m.shared_ffn));
     const size_t o_act = take(gemv_act_bytes_max(k_max));
     const size_t o_cbar = take((size_t)(L + 1) * kChainMaxPhases * 4);
     const size_t o_bval = take((size_t)2 * sm_count_ * 4), o_bidx = take((size_t)2 * sm_count_ * 4);
@@ -461,6 +571,10 @@ Status Engine::alloc_runtime() {
     qrot_ = reinterpret_cast<float*>(rt_ + o_qr);
     kraw_ = reinterpret_cast<float*>(rt_ + o_kr);
     h_ = reinterpret_cast<float*>(rt_ + o_h);
+    moe_logits_ = reinterpret_cast<float*>(rt_ + o_mlg);
+    moe_sel_ = reinterpret_cast<int*>(rt_ + o_msel);
+    moe_w_ = reinterpret_cast<float*>(rt_ + o_mw);
+    moe_acc_ = reinterpret_cast<float*>(rt_ + o_macc);
     logits_ = reinterpret_cast<float*>(rt_ + o_lg);
     tok_in_ = reinterpret_cast<uint32_t*>(rt_ + o_ti);
     tok_out_ = reinterpret_cast<uint32_t*>(rt_ + o_to);
@@ -577,8 +691,85 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         if (link) gather(p, 0, 2 * l, x_, x2_);
         p.norm_w = layers_[l].ffn_norm;
         p.out = h_;
+        p.glu_act = m.geglu ? 1 : 0;
         gemv_prepare(p, sm_count_);
         return p;
+    };
+    // Mixture-of-experts feed-forward of layer l (candle MlpOrMoe::MoE): routing on the device,
+    // gate|up of the selected experts (up to three per launch, one activation build), then one
+    // down launch per expert accumulating the weighted sum, the last adding it to x; a shared
+    // expert runs after the routed ones with weight 1.
+    auto enqueue_moe = [&](int l) -> Status {
+        const LayerWeights& W = layers_[l];
+        const int K = m.n_expert_used, eff = m.expert_ffn;
+        MoeRouteParams r = {};
+        r.x = x_;
+        r.norm_w = W.ffn_norm;
+        r.eps = m.rms_eps;
+        r.router = W.router;
+        r.router_f16 = W.router_type == TPTC_TYPE_F16 ? 1 : 0;
+        r.dim = m.dim;
+        r.n_expert = m.n_expert;
+        r.n_used = K;
+        r.logits = moe_logits_;
+        r.sel = moe_sel_;
+        r.w = moe_w_;
+        CU(launch_moe_route(r, st, pdl_));
+        bool act_ready = false;
+        for (int k0 = 0; k0 < K; k0 += kGemvMaxSeg) {
+            GemvParams g = base(m.dim);
+            g.nseg = std::min(kGemvMaxSeg, K - k0);
+            for (int i = 0; i < g.nseg; i++) {
+                g.seg[i] = GemvSeg{W.eglu, 0};
+                g.seg[i].out_off = (k0 + i) * eff;
+                g.seg[i].sel = k0 + i;
+            }
+            g.moe_sel = moe_sel_;
+            g.moe_stride = W.eglu_stride;
+            g.moe_nexp = m.n_expert;
+            g.x = x_;
+            g.norm_w = W.ffn_norm;
+            g.out = h_;
+            g.glu_act = m.geglu ? 1 : 0;
+            g.act_prepared = act_ready ? 1 : 0;  // the first launch's activation is still in act_
+            gemv_prepare(g, sm_count_);
+            CU(gemv_launch(g, EPI_GLU, st, pdl_));
+            act_ready = true;
+        }
+        if (W.shexp) {
+            GemvParams g = base(m.dim);
+            g.seg[0] = GemvSeg{W.glu, 0};
+            g.seg[0].out_off = K * eff;
+            g.x = x_;
+            g.norm_w = W.ffn_norm;
+            g.out = h_;
+            g.glu_act = m.geglu ? 1 : 0;
+            g.act_prepared = W.glu.type == W.eglu.type ? 1 : 0;  // same layout as the experts' activation
+            gemv_prepare(g, sm_count_);
+            CU(gemv_launch(g, EPI_GLU, st, pdl_));
+        }
+        for (int k = 0; k <= K; k++) {
+            if (k == K && !W.shexp) break;
+            const bool shared = k == K;
+            GemvParams d = base(shared ? m.shared_ffn : eff);
+            d.seg[0] = GemvSeg{shared ? W.down : W.edown, 0};
+            if (!shared) {
+                d.seg[0].sel = k;
+                d.moe_sel = moe_sel_;
+                d.moe_stride = W.edown_stride;
+                d.moe_nexp = m.n_expert;
+            }
+            d.x = h_ + (size_t)k * eff;
+            d.out = x_;
+            d.moe_acc = moe_acc_;
+            d.moe_w = moe_w_;
+            d.moe_slot = shared ? -1 : k;
+            d.moe_first = k == 0 ? 1 : 0;
+            d.moe_last = (shared || (k == K - 1 && !W.shexp)) ? 1 : 0;
+            gemv_prepare(d, sm_count_);
+            CU(gemv_launch(d, EPI_RESID, st, pdl_));
+        }
+        return {};
     };
     auto down_params = [&](int l) {
         GemvParams p = base(m.ffn / tp_size_);
@@ -646,7 +837,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         return {};
     };
 
-    bool use_chain = chain_ && !tp_;
+    bool use_chain = chain_ && !tp_ && m.n_expert == 0;
     if (use_chain) {  // the chains with the largest activation / stage (the widest layer, the head)
         ChainParams t = {};
         t.ph[0] = o_params(L - 1);
@@ -660,7 +851,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         chain_prepare(t, sm_count_);
         use_chain = use_chain && chain_fits(t, sm_count_);
     }
-    CU(launch_embed_row(embd_, tok_in_, x_, st, false, link ? step_ : nullptr));
+    CU(launch_embed_row(embd_, tok_in_, x_, st, false, link ? step_ : nullptr, m.embd_scale));
     if (use_chain) {
         // GEMV chains: [q|k|v(0)], then per layer attention(l) and one chain
         // [o(l), gate|up(l), down(l), q|k|v(l+1) or lm_head + argmax]
@@ -712,10 +903,14 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         const AttnDecodeParams a = attn_params(l, o);
         CU(launch_attn_decode(a, st, pdl_));
         CU(gemv_launch(o, EPI_RESID, st, pdl_));  // under TP: scatter to every rank's inbox
-        GemvParams g = glu_params(l);
-        CU(gemv_launch(g, EPI_GLU, st, pdl_));
-        GemvParams d = down_params(l);
-        CU(gemv_launch(d, EPI_RESID, st, pdl_));
+        if (layers_[l].moe) {
+            RET_IF(enqueue_moe(l));
+        } else {
+            GemvParams g = glu_params(l);
+            CU(gemv_launch(g, EPI_GLU, st, pdl_));
+            GemvParams d = down_params(l);
+            CU(gemv_launch(d, EPI_RESID, st, pdl_));
+        }
         RET_IF(trace_layer(l));
     }
     GemvParams h = head_params();

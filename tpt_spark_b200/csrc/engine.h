@@ -28,6 +28,11 @@ struct ModelMeta {
     bool qkv_bias = false;   // qwen2: f32 attn_q / attn_k / attn_v biases
     bool fused_qkv = false;      // phi3: one attn_qkv tensor, rows q | k | v
     bool fused_gate_up = false;  // phi3: one ffn_up tensor, rows gate | up
+    bool geglu = false;          // gemma: GEGLU feed-forward (tanh-form gelu(gate) * up)
+    float embd_scale = 1.f;      // gemma: embedding rows times sqrt(dim)
+    // mixture of experts (wgpu_loader.rs:367-377): experts per MoE layer, chosen per token,
+    // rows of each expert's gate / up (and down's K); shared-expert rows (0: none)
+    int n_expert = 0, n_expert_used = 0, expert_ffn = 0, shared_ffn = 0;
 };
 
 struct LayerWeights {
@@ -38,6 +43,17 @@ struct LayerWeights {
     float* bq = nullptr;  // this rank's rows of the q / k / v biases (qwen2), or nullptr
     float* bk = nullptr;
     float* bv = nullptr;
+    // mixture of experts (a layer with blk.N.ffn_gate_inp.weight): the router's raw rows
+    // [n_expert][dim] (F32 or F16); every expert's gate|up and down matrix in the device layout,
+    // expert e at eglu.main + e * eglu_stride (edown likewise); an optional shared expert in
+    // glu / down (the dense layer's matrices)
+    bool moe = false;
+    const void* router = nullptr;
+    int router_type = 0;
+    DevMatrix eglu, edown;
+    int64_t eglu_stride = 0, edown_stride = 0;
+    bool shexp = false;
+    std::vector<DevMatrix> eglu_all, edown_all;  // per expert (load-time bookkeeping)
 };
 
 struct Tp;  // tensor-parallel communicator (tp.cpp)
@@ -156,7 +172,11 @@ class Engine {
     float* qrot_ = nullptr;     // [n_heads_l * hd] q after RoPE (written by attention, for traces)
     float* kraw_ = nullptr;     // [n_kv_l * hd] this step's k before RoPE
     float* attn_ = nullptr;     // [n_heads_l * hd]
-    float* h_ = nullptr;        // [2 * ffn_l]: gate rows then up rows
+    float* h_ = nullptr;        // [2 * ffn_l]: gate rows then up rows; MoE: the selected experts' and the shared expert's products
+    float* moe_logits_ = nullptr;  // [n_expert] router logits
+    int* moe_sel_ = nullptr;       // [n_expert_used] selected experts, ascending
+    float* moe_w_ = nullptr;       // [n_expert_used] their routing weights
+    float* moe_acc_ = nullptr;     // [dim] weighted sum of the experts' outputs
     float* logits_ = nullptr;   // [vocab]
     uint32_t* tok_in_ = nullptr;
     uint32_t* tok_out_ = nullptr;

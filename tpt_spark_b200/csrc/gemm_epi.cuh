@@ -1,15 +1,17 @@
 // gemm_epi.cuh -- epilogue of the tcgen05 prefill GEMMs (gemm_tc.cu, gemm_q.cu): 32 f32
 // accumulator columns of one row of C written as a plain store, a residual add, or the fused
-// gate|up SiLU product in fp16.
+// gate|up SiLU (or GEGLU) product in fp16.
 #pragma once
 
 #include <cuda_fp16.h>
 
+#include "common.cuh"
 #include "prefill.h"
 
 namespace tptc {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fmul_rn(__fdiv_rn(g, 1.f + expf(-g)), u); }
+__device__ __forceinline__ float glu_mul(int geglu, float g, float u) { return geglu ? gelu_tanh_mul(g, u) : silu_mul(g, u); }
 
 // Epilogue of 32 accumulator columns (col .. col + 31) of one row.
 template <int EPI>
@@ -57,7 +59,7 @@ __device__ __forceinline__ void store_cols(const GemmTcParams& p, int row, int c
             for (int t = 0; t < 4; t++)
 #pragma unroll
                 for (int i = 0; i < 4; i++)
-                    o[4 * t + i] = __float2half_rn(silu_mul(__uint_as_float(r[8 * t + i]), __uint_as_float(r[8 * t + 4 + i])));
+                    o[4 * t + i] = __float2half_rn(glu_mul(p.geglu, __uint_as_float(r[8 * t + i]), __uint_as_float(r[8 * t + 4 + i])));
             reinterpret_cast<uint4*>(h)[0] = reinterpret_cast<const uint4*>(o)[0];
             reinterpret_cast<uint4*>(h)[1] = reinterpret_cast<const uint4*>(o)[1];
         } else {
@@ -67,7 +69,7 @@ __device__ __forceinline__ void store_cols(const GemmTcParams& p, int row, int c
                 for (int i = 0; i < 4; i++)
                     if (col + 8 * t + 4 + i < p.N)
                         h[4 * t + i] =
-                            __float2half_rn(silu_mul(__uint_as_float(r[8 * t + i]), __uint_as_float(r[8 * t + 4 + i])));
+                            __float2half_rn(glu_mul(p.geglu, __uint_as_float(r[8 * t + i]), __uint_as_float(r[8 * t + 4 + i])));
         }
     }
 }

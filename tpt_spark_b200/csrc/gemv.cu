@@ -54,6 +54,30 @@ __device__ __forceinline__ int unit_seg(const GemvParams& p, int u) {
     return s;
 }
 
+// Byte offsets of the segments' weights from m.main: 0, or for an expert segment the
+// selected expert's place in the stack.  The index is written by the previous kernel (the
+// routing kernel), so a launch with experts waits for it first; the producer lane calls this
+// once and keeps the offsets in registers (seg_off picks one by selects, no local array).
+static_assert(kGemvMaxSeg == 3, "seg_off selects among three segments");
+struct SegOff {
+    int64_t o0 = 0, o1 = 0, o2 = 0;
+};
+__device__ __forceinline__ SegOff expert_offsets(const GemvParams& p) {
+    SegOff r;
+    if (!p.moe_sel) return r;
+    pdl_wait();
+    auto off = [&](int s) -> int64_t {
+        if (s >= p.nseg || p.seg[s].sel < 0) return 0;
+        const int e = min(max(__ldcg(p.moe_sel + p.seg[s].sel), 0), p.moe_nexp - 1);
+        return (int64_t)e * p.moe_stride;
+    };
+    r.o0 = off(0);
+    r.o1 = off(1);
+    r.o2 = off(2);
+    return r;
+}
+__device__ __forceinline__ int64_t seg_off(const SegOff& r, int s) { return s == 0 ? r.o0 : s == 1 ? r.o1 : r.o2; }
+
 // Whether units u and u + grid are reduced together (sharing the activation slice): both
 // exist, same Q4_K / Q6_K weights, and the ring holds the pair plus at least one stage to
 // refill meanwhile.  Producer and consumers take the same decision.
@@ -93,12 +117,12 @@ __device__ __forceinline__ UnitRow unit_row(const GemvParams& p, int u, int r) {
     ur.seg = s;
     if (m.glu) {
         const int half = m.N / 2, pr = 4 * t + (r & 3);
-        ur.out = pr;
+        ur.out = pr + p.seg[s].out_off;
         ur.row = r < 4 ? pr : half + pr;
         if (pr >= half) ur.seg = -1;
     } else {
         ur.row = t * kTileRows + r;
-        ur.out = ur.row;
+        ur.out = ur.row + p.seg[s].out_off;
         if (ur.row >= m.N) ur.seg = -1;
     }
     return ur;
@@ -872,12 +896,14 @@ __device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, int* 
 // Producer lane: the weight tiles of this CTA's units of GEMV p, one bulk copy per stage,
 // in the order the consumers take them -- units in pairs (u, u + grid) chunk by chunk
 // alternating when unit_pair holds, a single unit alone otherwise.  Weights do not depend on
-// any earlier kernel or phase, so this runs ahead of every wait the consumers do.  Returns
+// any earlier kernel or phase, so this runs ahead of every wait the consumers do (expert
+// weights excepted: which expert is read depends on the routing kernel).  Returns
 // false once a wait for a free stage gave up (or the CTA aborted).
 template <bool WIDE>
 __device__ bool produce_units(const GemvParams& p, int epi, const Ring& r, int& s, int& lap, uint64_t policy,
                               volatile int* abort_flag) {
     const int nsb = p.K / QK_K;
+    const SegOff eo = expert_offsets(p);
     for (int u = blockIdx.x; u < p.units;) {
         const bool two = unit_pair(p, u, epi);
         for (int i = 0; i < (two ? 2 : 1) * p.nchunks; i++) {
@@ -890,7 +916,7 @@ __device__ bool produce_units(const GemvParams& p, int epi, const Ring& r, int& 
             const int cb = min(p.cbs, nsb - c * p.cbs);
             const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
             mbar_expect_tx(&r.full[s], bytes);
-            bulk_g2s(r.base + s * r.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
+            bulk_g2s(r.base + s * r.stage_bytes, m.main + seg_off(eo, s_) + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
                      &r.full[s], policy);
             if (++s == r.S) {
                 s = 0;
@@ -921,6 +947,16 @@ __device__ __forceinline__ Act act_view(const ActLayout& L, const uint8_t* smem)
     a.q80 = L.q80 >= 0 ? reinterpret_cast<const int8_t*>(smem + L.q80) : nullptr;
     a.q80_d = L.q80 >= 0 ? reinterpret_cast<const float*>(smem + L.q80_d) : nullptr;
     return a;
+}
+
+// EPI_RESID of a mixture-of-experts down projection, candle's MlpOrMoe::MoE order: ys starts
+// at zero, each selected expert in ascending expert order adds its output times its routing
+// weight (index_add of broadcast_mul), a shared expert adds its output, then x = ys + x.
+__device__ __forceinline__ void moe_resid(const GemvParams& p, int row, float y) {
+    const float a = __fmul_rn(y, p.moe_slot >= 0 ? __ldcg(p.moe_w + p.moe_slot) : 1.f);
+    const float acc = p.moe_first ? a : __fadd_rn(__ldcg(p.moe_acc + row), a);
+    if (p.moe_last) p.out[row] = __fadd_rn(acc, __ldcg(p.out + row));
+    else p.moe_acc[row] = acc;
 }
 
 // Running greedy pick of the rows a warp wrote (lane 0): candle sample_argmax keeps the last
@@ -1033,7 +1069,8 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
             if (warp >= 4 && lane == 0) glu_up[buf][warp - 4] = y;
             pair_sync(warp & 3);
             if (warp < 4 && lane == 0 && ur.seg >= 0 && !timed_out)
-                p.out[ur.out] = __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
+                p.out[ur.out] = p.glu_act ? gelu_tanh_mul(y, glu_up[buf][warp])
+                                          : __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
             unit_no++;
             return;
         }
@@ -1047,6 +1084,8 @@ __device__ __forceinline__ void consume_units(const GemvParams& p, const Act& a,
                 const size_t at = ((size_t)p.tp_slot * t.size + t.rank) * t.dim + ur.out;
                 const unsigned long long w = ((unsigned long long)tp_epoch(p) << 32) | __float_as_uint(y);
                 for (int r = 0; r < t.size; r++) st_volatile_u64(t.inbox[r] + at, w);
+            } else if (p.moe_acc) {
+                moe_resid(p, ur.out, y);
             } else {
                 p.out[ur.out] = __ldcg(p.out + ur.out) + y;
             }
@@ -1160,6 +1199,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         if (lane == 0) {
             const uint64_t policy = l2_evict_first_policy();
             int s = 0, lap = 0;  // ring stage and how many times the ring has wrapped
+            const SegOff eo = expert_offsets(p);
             // units in pairs (u, u + grid), chunk by chunk: the order the consumers take them
             for (int u = blockIdx.x; u < p.units;) {
                 const bool two = unit_pair(p, u, EPI);
@@ -1175,7 +1215,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                         const int cb = min(p.cbs, nsb - c * p.cbs);
                         const uint32_t bytes = (uint32_t)(kTileRows * cb * sbb);
                         mbar_expect_tx(&full[s], bytes);
-                        bulk_g2s(ring + s * p.stage_bytes, m.main + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
+                        bulk_g2s(ring + s * p.stage_bytes, m.main + seg_off(eo, s_) + tile0 + (int64_t)c * kTileRows * p.cbs * sbb, bytes,
                                  &full[s], policy);
                         if (++s == S) {
                             s = 0;
@@ -1225,7 +1265,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             if (warp >= 4 && lane == 0) glu_up[buf][warp - 4] = y;
             pair_sync(warp & 3);
             if (warp < 4 && lane == 0 && ur.seg >= 0)
-                p.out[ur.out] = __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
+                p.out[ur.out] = p.glu_act ? gelu_tanh_mul(y, glu_up[buf][warp])
+                                          : __fmul_rn(__fdiv_rn(y, 1.f + expf(-y)), glu_up[buf][warp]);
             unit_no++;
             return;
         }
@@ -1238,6 +1279,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
                 const size_t at = ((size_t)p.tp_slot * t.size + t.rank) * t.dim + ur.out;
                 const unsigned long long w = ((unsigned long long)tp_epoch(p) << 32) | __float_as_uint(y);
                 for (int r = 0; r < t.size; r++) st_volatile_u64(t.inbox[r] + at, w);
+            } else if (p.moe_acc) {
+                moe_resid(p, ur.out, y);
             } else {
                 p.out[ur.out] += y;
             }

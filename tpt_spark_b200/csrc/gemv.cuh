@@ -184,7 +184,9 @@ __host__ __device__ inline size_t tp_argmax_offset(int size, int dim) { return (
 
 struct GemvSeg {
     DevMatrix m;
-    int unit_begin;  // filled by gemv_prepare
+    int unit_begin;    // filled by gemv_prepare
+    int out_off = 0;   // EPI_GLU / EPI_RESID: added to the output row (several gate|up segments into one buffer)
+    int sel = -1;      // >= 0: mixture-of-experts weights, expert moe_sel[sel] of the stack m.main points at
 };
 
 struct GemvParams {
@@ -194,6 +196,7 @@ struct GemvParams {
     const float* x;       // input activation [K] (f32)
     const float* norm_w;  // RMSNorm gain [K] or nullptr (no norm)
     int glu_in;           // 1: x holds [gate | up] (2K floats); the input is silu(gate) * up
+    int glu_act;          // EPI_GLU: 0 silu(gate) * up, 1 GEGLU's tanh-form gelu(gate) * up
     float eps;
     float* out;
     // EPI_QKV
@@ -204,6 +207,19 @@ struct GemvParams {
     int hd;
     int max_seq;
     const float* bias[kGemvMaxSeg];  // optional per-segment row biases (qwen2 q / k / v), added in f32
+    // mixture of experts.  Segments with sel >= 0 read expert moe_sel[sel] (device, written by
+    // the routing kernel; clamped to [0, moe_nexp)) at m.main + expert * moe_stride; the
+    // producer waits for the previous kernel before it reads the index.  EPI_RESID with moe_acc
+    // set accumulates candle's weighted sum instead of adding to out: a = y * moe_w[moe_slot]
+    // (weight 1 for moe_slot < 0, a shared expert), acc = moe_first ? a : acc + a, and with
+    // moe_last out[row] = acc + out[row] (the residual add) instead of storing acc.
+    const int* moe_sel;
+    int64_t moe_stride;
+    int moe_nexp;
+    const float* moe_w;
+    int moe_slot;
+    int moe_first, moe_last;
+    float* moe_acc;
     // EPI_DOTS
     int32_t* isum;
     int32_t* msum;

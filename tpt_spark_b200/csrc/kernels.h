@@ -74,10 +74,11 @@ cudaError_t attn_noalloc_scratch(int device, cudaStream_t st, uint8_t** out);
 cudaError_t attn_noalloc_status(int device, cudaStream_t st, int* code);
 
 // misc.cu
-// x[dim] = dequantised row `tok` of token_embd (device layout), token read from *tok_ptr.
+// x[dim] = dequantised row `tok` of token_embd (device layout), token read from *tok_ptr,
+// times `scale` (gemma's sqrt(dim); 1 leaves the row as it is).
 // `step` (optional): a counter the kernel increments once (the decode step, for TpLink epochs).
 cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl,
-                             int* step = nullptr);
+                             int* step = nullptr, float scale = 1.f);
 // argmax over logits[n] (ties -> highest index, candle sample_argmax); writes *out_tok;
 // when next_tok/pos are non-null also stores the token as the next step's input and
 // increments *pos (device-chained greedy decode).

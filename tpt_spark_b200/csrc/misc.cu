@@ -2,6 +2,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "moe.h"
 #include "quant.cuh"
 
 namespace tptc {
@@ -15,13 +16,16 @@ namespace {
 // dequantised on the fly (bit-identical values) into the residual stream x.
 // Replaces the reference's whole-table dequant + row copy (wgpu_engine.rs:235-242,364-368).
 __global__ void embed_row_kernel(DevMatrix emb, const uint32_t* __restrict__ tok_ptr, float* __restrict__ x,
-                                 int* step) {
+                                 int* step, float scale) {
     pdl_wait();
     pdl_launch_dependents();
     if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;  // opens a decode step (TpLink epochs)
     const int row = (int)*tok_ptr;  // token_embd is never a fused gate|up matrix: phys row = row
     const int K = emb.K;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) x[i] = dm_elem(emb, row, i);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K; i += gridDim.x * blockDim.x) {
+        const float v = dm_elem(emb, row, i);
+        x[i] = scale == 1.f ? v : __fmul_rn(v, scale);
+    }
 }
 
 // Greedy pick, candle LogitsProcessor::sample_argmax: Iterator::max_by(f32::total_cmp)
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(1024) argmax_tp_kernel(const float* __restrict
 }  // namespace
 
 cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, float* x, cudaStream_t st, bool pdl,
-                             int* step) {
+                             int* step, float scale) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::max(1, std::min(16, emb.K / 256)));
     cfg.blockDim = dim3(256);
@@ -172,7 +176,7 @@ cudaError_t launch_embed_row(const DevMatrix& emb, const uint32_t* tok_ptr, floa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, embed_row_kernel, emb, tok_ptr, x, step);
+    return cudaLaunchKernelEx(&cfg, embed_row_kernel, emb, tok_ptr, x, step, scale);
 }
 
 cudaError_t launch_argmax(const float* logits, int n, uint32_t* out_tok, uint32_t* next_tok, int* pos,
@@ -205,6 +209,8 @@ cudaError_t launch_argmax_tp(const float* logits, int n, int row0, const TpLink*
 
 cudaError_t kernels_init_device() {
     cudaError_t e = gemv_init_device();
+    if (e != cudaSuccess) return e;
+    e = moe_init_device();
     if (e != cudaSuccess) return e;
     e = attn_init_device();
     if (e != cudaSuccess) return e;

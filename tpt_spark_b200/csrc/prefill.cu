@@ -31,10 +31,13 @@ namespace {
     } while (0)
 
 // x[t][:] = dequantised row ids[t] of token_embd (device layout); one CTA per token.
-__global__ void embed_rows_kernel(DevMatrix emb, const uint32_t* __restrict__ ids, float* __restrict__ x) {
+__global__ void embed_rows_kernel(DevMatrix emb, const uint32_t* __restrict__ ids, float* __restrict__ x, float scale) {
     const int t = blockIdx.x, row = (int)ids[t], K = emb.K;
     float* xr = x + (size_t)t * K;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) xr[i] = dm_elem(emb, row, i);
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float v = dm_elem(emb, row, i);
+        xr[i] = scale == 1.f ? v : __fmul_rn(v, scale);
+    }
 }
 
 // out[t][:] = fp16(x[t] / sqrt(mean(x[t]^2) + eps) * w) (candle rms_norm: x / m * alpha);
@@ -200,7 +203,7 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         cudaError_t e = launch_dequant_rows_f16(w, 0, g.N, pf_w_, st, w.glu != 0);
         return e != cudaSuccess ? e : gemm_tc(epi, a, g.K, pf_w_, g.K, g, st, false);
     };
-    embed_rows_kernel<<<T, 256, 0, st>>>(embd_, pf_ids_, pf_x_);
+    embed_rows_kernel<<<T, 256, 0, st>>>(embd_, pf_ids_, pf_x_, m.embd_scale);
     TPTC_CUDA_RET(cudaGetLastError());
     for (int l = 0; l < m.n_layers; l++) {
         const LayerWeights& L = layers_[l];
@@ -270,6 +273,7 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         gg.h = pf_h_;
         gg.ldh = ffn_l;
         gg.err = err_;
+        gg.geglu = m.geglu ? 1 : 0;
         TPTC_CUDA_RET(matmul(GEMM_GLU, pf_xn_, L.glu, gg));
         g.N = dim;
         g.K = ffn_l;
@@ -287,7 +291,9 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
 }
 
 bool Engine::prefill_uses_gemm(int n) const {
-    if (kv_f32_ || prefill_gemm_min_ <= 0 || n < prefill_gemm_min_) return false;
+    // mixture-of-experts models prefill position by position through the decode graph (the
+    // experts are chosen per token on the device)
+    if (kv_f32_ || prefill_gemm_min_ <= 0 || n < prefill_gemm_min_ || meta_.n_expert > 0) return false;
     const ModelMeta& m = meta_;
     const int ffn_l = m.ffn / tp_size_;
     // GEMM operands: K a multiple of 64, the gate|up tile order whole 8-row groups

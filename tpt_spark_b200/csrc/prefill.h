@@ -23,7 +23,8 @@ struct GemmTcParams {
     int ldc;
     __half* h;  // GEMM_GLU, leading dimension ldh
     int ldh;
-    int* err;  // bounded waits that give up set TPTC_ERR_TIMEOUT here
+    int* err;   // bounded waits that give up set TPTC_ERR_TIMEOUT here
+    int geglu;  // GEMM_GLU: 0 silu(gate) * up, 1 GEGLU's tanh-form gelu(gate) * up
 };
 // A and B 16-byte aligned, lda / ldb multiples of 8 elements, K a multiple of 64.
 cudaError_t gemm_tc(int epi, const __half* a, int lda, const __half* b, int ldb, const GemmTcParams& p,

@@ -65,14 +65,32 @@ class ModelConfig:
                             # "phi3" stores attn_qkv (rows q | k | v) and ffn_up (rows gate | up) fused
     qkv_bias: bool = False  # f32 attn_q / attn_k / attn_v biases, N(0, bias_std)
     bias_std: float = 0.1
+    # mixture of experts: n_expert > 1 makes the layers in moe_layers (None: all) MoE layers
+    # with a router (ffn_gate_inp, router_type) and n_expert experts of expert_ffn rows, stored
+    # stacked (ffn_*_exps, llama.cpp) or one tensor each (ffn_*.E, candle's names), plus a
+    # shared expert of shared_ffn rows when > 0
+    n_expert: int = 0
+    n_expert_used: int = 0
+    expert_ffn: int = 0
+    moe_layers: Optional[Tuple[int, ...]] = None
+    stacked_experts: bool = True
+    shared_ffn: int = 0
+    router_type: int = F32
+    router_std: float = 0.02
 
     @property
     def head_dim(self) -> int:
         return self.dim // self.n_heads
 
+    def is_moe_layer(self, i: int) -> bool:
+        return self.n_expert > 1 and (self.moe_layers is None or i in self.moe_layers)
+
     def type_of(self, kind: str) -> int:
         if kind.endswith("norm") or kind == "bias":
             return F32
+        if kind == "ffn_gate_inp":
+            return self.router_type
+        kind = kind.replace("_exps", "").replace("_shexp", "")  # experts take the dense kinds' types
         if kind == "token_embd":
             return self.embd_type if self.embd_type is not None else self.default_type
         if kind == "output":
@@ -100,12 +118,30 @@ class ModelConfig:
                         (p + "attn_v.bias", "bias", [self.n_kv_heads * hd])]
             out += [(p + "attn_output.weight", "attn_output", [self.n_heads * hd, d]),
                     (p + "ffn_norm.weight", "ffn_norm", [d])]
-            if self.arch == "phi3":
+            if self.is_moe_layer(i):
+                E, ef = self.n_expert, self.expert_ffn
+                out += [(p + "ffn_gate_inp.weight", "ffn_gate_inp", [d, E])]
+                if self.stacked_experts:
+                    out += [(p + "ffn_gate_exps.weight", "ffn_gate_exps", [d, ef, E]),
+                            (p + "ffn_up_exps.weight", "ffn_up_exps", [d, ef, E]),
+                            (p + "ffn_down_exps.weight", "ffn_down_exps", [ef, d, E])]
+                else:
+                    for e in range(E):
+                        out += [(p + f"ffn_gate.{e}.weight", "ffn_gate", [d, ef]),
+                                (p + f"ffn_up.{e}.weight", "ffn_up", [d, ef]),
+                                (p + f"ffn_down.{e}.weight", "ffn_down", [ef, d])]
+                if self.shared_ffn:
+                    sf = self.shared_ffn
+                    out += [(p + "ffn_gate_shexp.weight", "ffn_gate_shexp", [d, sf]),
+                            (p + "ffn_up_shexp.weight", "ffn_up_shexp", [d, sf]),
+                            (p + "ffn_down_shexp.weight", "ffn_down_shexp", [sf, d])]
+            elif self.arch == "phi3":
                 out += [(p + "ffn_up.weight", "ffn_up", [d, 2 * self.ffn])]
             else:
                 out += [(p + "ffn_gate.weight", "ffn_gate", [d, self.ffn]),
                         (p + "ffn_up.weight", "ffn_up", [d, self.ffn])]
-            out += [(p + "ffn_down.weight", "ffn_down", [self.ffn, d])]
+            if not self.is_moe_layer(i):
+                out += [(p + "ffn_down.weight", "ffn_down", [self.ffn, d])]
         out.append(("output_norm.weight", "output_norm", [d]))
         if not self.tied:
             out.append(("output.weight", "output", [d, self.vocab]))
@@ -180,6 +216,24 @@ TINY: Dict[str, ModelConfig] = {
         "tiny_phi3", dim=768, n_layers=2, n_heads=8, n_kv_heads=8, ffn=512, vocab=352,
         rope_base=10000.0, context_length=512, default_type=Q4_K, embd_type=Q4_K, output_type=Q6_K,
         norm_std=0.1, arch="phi3"),
+    # mixture of experts, candle's per-expert tensor names (ffn_gate.E): Mixtral's layout in
+    # miniature (4 experts, 2 per token, Q4_K_M mix with Q6_K downs, f32 router)
+    "tiny_mixtral": ModelConfig(
+        "tiny_mixtral", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=384,
+        rope_base=1000000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K, output_type=Q6_K,
+        norm_std=0.1, n_expert=4, n_expert_used=2, expert_ffn=512, stacked_experts=False, router_std=0.2),
+    # llama.cpp's stacked experts (ffn_*_exps): 8 experts, 4 per token (two gate|up launches),
+    # a shared expert, an f16 router, Q5_K weights; layer 0 dense, layer 1 MoE
+    "tiny_moe": ModelConfig(
+        "tiny_moe", dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn=512, vocab=352,
+        rope_base=10000.0, context_length=512, default_type=Q5_K, overrides=(("ffn_down", Q6_K),),
+        embd_type=Q5_K, output_type=Q6_K, norm_std=0.1, n_expert=8, n_expert_used=4, expert_ffn=256,
+        moe_layers=(1,), shared_ffn=512, router_type=F16, router_std=0.2),
+    # gemma: GEGLU, embeddings times sqrt(dim), RoPE on head halves, tied embeddings
+    "tiny_gemma": ModelConfig(
+        "tiny_gemma", dim=256, n_layers=2, n_heads=4, n_kv_heads=4, ffn=512, vocab=320,
+        rope_base=10000.0, context_length=512, tied=True, overrides=Q4_K_M, embd_type=Q4_K,
+        norm_std=0.1, arch="gemma"),
     "tiny_tp_q4km": ModelConfig(
         "tiny_tp_q4km", dim=512, n_layers=2, n_heads=8, n_kv_heads=4, ffn=1024, vocab=384,
         rope_base=10000.0, context_length=512, overrides=Q4_K_M, embd_type=Q4_K,
@@ -277,7 +331,9 @@ def metadata(cfg: ModelConfig) -> List[bytes]:
         _kv(f"{a}.rope.freq_base", 6, cfg.rope_base),
         _kv(f"{a}.attention.layer_norm_rms_epsilon", 6, cfg.rms_eps),
         _kv(f"{a}.vocab_size", 4, cfg.vocab),
-    ]
+    ] + ([_kv(f"{a}.expert_count", 4, cfg.n_expert),
+          _kv(f"{a}.expert_used_count", 4, cfg.n_expert_used),
+          _kv(f"{a}.expert_feed_forward_length", 4, cfg.expert_ffn)] if cfg.n_expert > 1 else [])
 
 
 def write_gguf(path: str, cfg: ModelConfig, seed: int = 0,
@@ -309,6 +365,8 @@ def write_gguf(path: str, cfg: ModelConfig, seed: int = 0,
                 std, mean = cfg.norm_std, 1.0
             elif kind == "bias":
                 std, mean = cfg.bias_std, 0.0
+            elif kind == "ffn_gate_inp":
+                std, mean = cfg.router_std, 0.0
             else:
                 std, mean = cfg.weight_std, 0.0
             s = tensor_seed(name, seed)
