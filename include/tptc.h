@@ -154,9 +154,12 @@ TPTC_API int tptc_set_tp_wait_polls(tptc_ctx* ctx, uint32_t polls);
 /* LlmEngine::load (mod.rs:66-70) -> load_gguf_to_vram (wgpu_loader.rs:87-201): mmap the
  * file, parse GGUF v3, check bounds, stream every tensor through pinned staging with
  * cudaMemcpyAsync, repack to the device layout, build the KV cache and rope table.
- * Architectures llama, mistral, qwen2 (q / k / v biases, RoPE on head halves) and phi3 (fused
- * attn_qkv and ffn_up, RoPE on head halves); weight types
- * F16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K; anything else
+ * Architectures llama, mistral, qwen2 (q / k / v biases, RoPE on head halves), phi3 (fused
+ * attn_qkv and ffn_up, RoPE on head halves) and gemma (GEGLU, embeddings times sqrt(dim)); a
+ * model with {arch}.expert_count > 1 has mixture-of-experts layers wherever
+ * blk.N.ffn_gate_inp.weight exists (experts stacked as ffn_*_exps or one tensor each as
+ * ffn_*.E, an optional shared expert ffn_*_shexp, an F32 / F16 router; one GPU only); weight
+ * types F16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K; anything else
  * TPTC_ERR_UNSUPPORTED. */
 TPTC_API int tptc_load_gguf(tptc_ctx* ctx, const char* path, tptc_progress_cb progress, void* user);
 /* LlmEngine::unload / is_loaded / model_info (mod.rs:71-73, wgpu_engine.rs:126-147). */
