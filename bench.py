@@ -76,7 +76,15 @@ def parse():
     return ap.parse_args()
 
 
-PROMPT_LEN = {"c2_llama1b_q4km": 128, "c3_mistral7b_q8_0": 2048, "c4_phi3mini_f16": 1024, "c5_llama8b_q4km": 8192}
+PROMPT_LEN = {"c2_llama1b_q4km": 128, "c3_mistral7b_q8_0": 2048, "c4_phi3mini_f16": 1024, "c5_llama8b_q4km": 8192,
+              "mixtral8x7b_l4_q4km": 512}
+
+
+def workload(name):
+    """A benchmark configuration (synth.CONFIGS) or a further workload (synth.WORKLOADS)."""
+    from tpt_spark_b200 import synth
+
+    return synth.CONFIGS.get(name) or synth.WORKLOADS[name]
 DECODE_LEN = {"c2_llama1b_q4km": 256, "c3_mistral7b_q8_0": 512, "c4_phi3mini_f16": 256, "c5_llama8b_q4km": 1024}
 
 
@@ -226,8 +234,9 @@ class Clocks:
 
 def decode_bytes(cfg, kv_len_mean):
     """Algorithmic HBM bytes of one decode step: every weight matrix once (token_embd: one row
-    unless it is also the output projection), norm gains, and the fp16 K and V of the
-    kv_len positions attended to."""
+    unless it is also the output projection; of a mixture-of-experts layer the router and the
+    n_expert_used chosen experts), norm gains, and the fp16 K and V of the kv_len positions
+    attended to."""
     from tpt_spark_b200 import synth
 
     tot = 0
@@ -236,6 +245,10 @@ def decode_bytes(cfg, kv_len_mean):
         b = synth.type_bytes(cfg.type_of(kind), n)
         if kind == "token_embd":
             tot += b if cfg.tied else b // ne[1]
+        elif kind.endswith("_exps"):  # [E][rows][K]: the chosen experts' slices
+            tot += b * cfg.n_expert_used
+        elif cfg.n_expert > 1 and ".ffn_" in name and name.split(".")[2].isdigit():  # ffn_*.E
+            tot += b * cfg.n_expert_used // cfg.n_expert
         else:
             tot += b
     tot += int(2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * kv_len_mean)
@@ -352,7 +365,7 @@ def cpu_baseline(path, cfg, decode_pos, max_decode_s=20.0, prefill_tokens=64, ma
 def run_reference(args, dist):
     from tpt_spark_b200 import synth
 
-    cfg = synth.CONFIGS[args.workload]
+    cfg = workload(args.workload)
     if dist.rank != 0:
         return
     path = model_file(cfg, args.model_dir, args.seed, _Solo())
@@ -386,7 +399,7 @@ def run_ours(args, dist):
     from tpt_spark_b200 import synth
     from tpt_spark_b200.engine import CudaEngine
 
-    cfg = synth.CONFIGS[args.workload]
+    cfg = workload(args.workload)
     torch.cuda.set_device(dist.local)
     path = model_file(cfg, args.model_dir, args.seed, dist)
     P = args.prompt if args.prompt is not None else PROMPT_LEN[cfg.name]
@@ -539,6 +552,11 @@ def run_ours(args, dist):
         "clocks": clk.summary(),
         "gpu_launches": launches_per_step * args.steps,
     }
+    if cfg.n_expert > 1:  # experts chosen per token: the prompt runs position by position
+        line["prefill"]["path"] = "position by position through the decode graph (mixture of experts)"
+        line["prefill"]["roofline"] = None
+        line["config"]["experts"] = f"{cfg.n_expert_used} of {cfg.n_expert} per token"
+        line["config"]["l2"] = f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB of weights per step)"
     eng.close()
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(path, cfg, decode_pos=kv_start)

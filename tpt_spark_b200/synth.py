@@ -168,6 +168,16 @@ CONFIGS: Dict[str, ModelConfig] = {
         embd_type=Q4_K, output_type=Q6_K),
 }
 
+# Further bench workloads (bench.py --workload): Mixtral 8x7B's layer shape for the
+# mixture-of-experts decode path, 4 of its 32 layers (8 experts of 14336 rows, 2 per token,
+# llama.cpp's stacked expert tensors, Q4_K_M mix, f32 router).
+WORKLOADS: Dict[str, ModelConfig] = {
+    "mixtral8x7b_l4_q4km": ModelConfig(
+        "mixtral8x7b_l4_q4km", dim=4096, n_layers=4, n_heads=32, n_kv_heads=8, ffn=14336, vocab=32000,
+        rope_base=1000000.0, context_length=4096, overrides=Q4_K_M, embd_type=Q4_K, output_type=Q6_K,
+        n_expert=8, n_expert_used=2, expert_ffn=14336),
+}
+
 # Small models with the same code paths, for parity tests that the CPU oracle finishes
 # in seconds.
 TINY: Dict[str, ModelConfig] = {
