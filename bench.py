@@ -260,7 +260,11 @@ def prefill_flops(cfg, P):
     attention (QK^T and PV over positions 0..t for token t), lm_head on the last token."""
     d, hd, L = cfg.dim, cfg.head_dim, cfg.n_layers
     nq, nk = cfg.n_heads * hd, cfg.n_kv_heads * hd
-    linear = 2.0 * P * L * (d * (nq + 2 * nk) + nq * d + 3 * d * cfg.ffn)
+    ffn = [3 * d * cfg.ffn] * L
+    for i in range(L):  # a mixture-of-experts layer: the chosen experts, the shared one, the router
+        if cfg.is_moe_layer(i):
+            ffn[i] = 3 * d * (cfg.expert_ffn * cfg.n_expert_used + cfg.shared_ffn) + d * cfg.n_expert
+    linear = 2.0 * P * (L * (d * (nq + 2 * nk) + nq * d) + sum(ffn))
     attn = 4.0 * L * cfg.n_heads * hd * P * (P + 1) / 2
     return linear + attn + 2.0 * d * cfg.vocab
 
@@ -552,9 +556,9 @@ def run_ours(args, dist):
         "clocks": clk.summary(),
         "gpu_launches": launches_per_step * args.steps,
     }
-    if cfg.n_expert > 1:  # experts chosen per token: the prompt runs position by position
-        line["prefill"]["path"] = "position by position through the decode graph (mixture of experts)"
-        line["prefill"]["roofline"] = None
+    if cfg.n_expert > 1:
+        line["prefill"]["path"] = ("tokens routed on the device, grouped by expert on the host once per layer, each "
+                                   "expert's rows through the tcgen05 GEMMs, combined in candle's order")
         line["config"]["experts"] = f"{cfg.n_expert_used} of {cfg.n_expert} per token"
         line["config"]["l2"] = f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB of weights per step)"
     eng.close()

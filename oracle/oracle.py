@@ -296,6 +296,7 @@ class Model:
         marr = mtys = None
         if self.n_expert:
             self._moe = moe_arrays
+            self._moe_types = moe_types
             marr = (ctypes.c_void_p * len(moe_arrays))(*[a.ctypes.data if a is not None else None for a in moe_arrays])
             mtys = (ctypes.c_int * len(moe_types))(*moe_types)
             d.n_expert, d.n_expert_used = self.n_expert, self.n_expert_used

@@ -22,9 +22,7 @@ pytestmark = pytest.mark.gpu
 
 MODELS = ["tiny_q4km", "tiny_q4km_tied", "tiny_q8_0", "tiny_f16", "tiny_q5km", "tiny_q4_0", "tiny_q2k", "tiny_qwen2",
           "tiny_phi3", "tiny_q4_1", "tiny_gemma", "tiny_mixtral", "tiny_moe"]
-# mixture-of-experts models prefill position by position through the decode graph (8-bit
-# activations, the oracle's semantics), so the fp16-operand float reference does not apply
-BATCHED = [n for n in MODELS if n not in ("tiny_mixtral", "tiny_moe")]
+BATCHED = MODELS
 
 # fp16 operands (11-bit significands) against a float64 forward: relative error of a few
 # 2^-11 per layer on the hidden state, times the logit scale of the tiny models (|logit| < 3)
@@ -97,15 +95,34 @@ def _weights(ref):
         return O.dequant(tys[i], arrs[i], N * Kd).reshape(N, Kd).astype(np.float64)
 
     w = {"emb": mat(0, ref.vocab, D), "out_norm": np.asarray(arrs[1], np.float32).astype(np.float64)}
+    E = getattr(ref, "n_expert", 0)
+    S = 4 + 3 * E
+
+    def moe_mat(a, t, N, Kd):
+        if t in (O.F32, O.F16):  # the router: rows as stored
+            return np.asarray(a).view(np.float32 if t == O.F32 else np.float16).reshape(N, Kd).astype(np.float64)
+        return O.dequant(t, a, N * Kd).reshape(N, Kd).astype(np.float64)
+
     layers = []
     for l in range(ref.n_layers):
         b = 3 + 9 * l
-        layers.append(dict(
+        L = dict(
             attn_norm=np.asarray(arrs[b], np.float32).astype(np.float64),
             q=mat(b + 1, ref.n_heads * hd, D), k=mat(b + 2, ref.n_kv_heads * hd, D),
             v=mat(b + 3, ref.n_kv_heads * hd, D), o=mat(b + 4, D, ref.n_heads * hd),
-            ffn_norm=np.asarray(arrs[b + 5], np.float32).astype(np.float64),
-            gate=mat(b + 6, F, D), up=mat(b + 7, F, D), down=mat(b + 8, D, F)))
+            ffn_norm=np.asarray(arrs[b + 5], np.float32).astype(np.float64))
+        moe = ref._moe[l * S: (l + 1) * S] if E else None
+        if moe is not None and moe[0] is not None:  # router, experts (gate, up, down), shared expert
+            mtys = ref._moe_types[l * S: (l + 1) * S]
+            ef, sf = ref.expert_ffn, ref.shared_ffn
+            L["router"] = moe_mat(moe[0], mtys[0], E, D)
+            L["experts"] = [(moe_mat(moe[1 + 3 * e], mtys[1 + 3 * e], ef, D), moe_mat(moe[2 + 3 * e], mtys[2 + 3 * e], ef, D),
+                             moe_mat(moe[3 + 3 * e], mtys[3 + 3 * e], D, ef)) for e in range(E)]
+            L["shared"] = ((moe_mat(moe[1 + 3 * E], mtys[1 + 3 * E], sf, D), moe_mat(moe[2 + 3 * E], mtys[2 + 3 * E], sf, D),
+                            moe_mat(moe[3 + 3 * E], mtys[3 + 3 * E], D, sf)) if moe[1 + 3 * E] is not None else None)
+        else:
+            L.update(gate=mat(b + 6, F, D), up=mat(b + 7, F, D), down=mat(b + 8, D, F))
+        layers.append(L)
     w["layers"] = layers
     return w
 
@@ -160,9 +177,26 @@ def float_prefill_logits(ref, tokens):
             att[:, h] = (p / p.sum(-1, keepdims=True)) @ v[:, h // G]
         x = x + att.reshape(T, H * hd) @ L["o"].T
         xn = rms(x, L["ffn_norm"])
-        gt, up = xn @ L["gate"].T, xn @ L["up"].T
-        act = gt * 0.5 * (1 + np.tanh(0.7978845608 * (gt + 0.044715 * gt ** 3))) if geglu else gt / (1 + np.exp(-gt))
-        x = x + (act * up) @ L["down"].T
+
+        def mlp(z, g_, u_, d_):
+            gt, up = z @ g_.T, z @ u_.T
+            act = gt * 0.5 * (1 + np.tanh(0.7978845608 * (gt + 0.044715 * gt ** 3))) if geglu else gt / (1 + np.exp(-gt))
+            return (act * up) @ d_.T
+
+        if "router" in L:  # candle MlpOrMoe::MoE: softmax routing, stable top-k, renormalised
+            lg = xn @ L["router"].T
+            rw = np.exp(lg - lg.max(-1, keepdims=True))
+            rw /= rw.sum(-1, keepdims=True)
+            y = np.zeros_like(x)
+            for t in range(T):
+                top = np.argsort(-rw[t], kind="stable")[:ref.n_expert_used]
+                for e in sorted(top.tolist()):
+                    y[t] += mlp(xn[t:t + 1], *L["experts"][e])[0] * (rw[t, e] / rw[t, top].sum())
+            if L["shared"] is not None:
+                y += mlp(xn, *L["shared"])
+            x = x + y
+        else:
+            x = x + mlp(xn, L["gate"], L["up"], L["down"])
     last = rms(x[-1:], w["out_norm"]).astype(np.float32)
     out_i = 2
     return O.matmul(ref._types[out_i], ref._arrays[out_i], ref.vocab, D, last)[0]

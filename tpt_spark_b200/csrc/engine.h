@@ -210,6 +210,18 @@ class Engine {
     __half* pf_h_ = nullptr;      // [T][ffn] silu(gate) * up
     __half* pf_w_ = nullptr;      // one layer matrix as dense fp16 (GEMM B operand)
     float* pf_part_ = nullptr;    // [T][dim] row-parallel partial sums (tensor parallel)
+    // mixture of experts: the chunk's routing ([T][n_used] experts, ascending, and weights),
+    // the chosen (token, expert) rows grouped by expert: token of each row, row of each
+    // choice, gathered activations, gate|up products and down outputs; the shared expert's
+    int* pf_rsel_ = nullptr;
+    float* pf_rw_ = nullptr;
+    int* pf_gidx_ = nullptr;
+    int* pf_rowof_ = nullptr;
+    __half* pf_ga_ = nullptr;
+    __half* pf_gh_ = nullptr;
+    float* pf_gy_ = nullptr;
+    __half* pf_sh_h_ = nullptr;
+    float* pf_sh_y_ = nullptr;
 
     // pinned host staging
     uint32_t* h_tok_ = nullptr;

@@ -1,4 +1,5 @@
-// moe.cu -- mixture-of-experts routing for the decode step.
+// moe.cu -- mixture-of-experts routing (decode and batched prefill) and the batched
+// prefill's row gather and combine.
 //
 // Semantics: candle quantized_llama MlpOrMoe::MoE (the forward of Mixtral-style GGUFs, which
 // the reference's candle engine loads through ModelWeights::from_gguf): router logits of the
@@ -13,6 +14,10 @@
 //                      which candle dequantises to f32 and multiplies in f32)
 //   moe_select_kernel  one warp: softmax, top n_used, renormalised weights, written in
 //                      ascending expert order (sel[k], w[k]) for the expert GEMVs
+// The batched prefill routes every token of a chunk in one launch (moe_route_rows_kernel: the
+// same norm, logits and selection per token), gathers each expert's rows
+// (gather_rows_f16_kernel) for the GEMMs, and adds the experts' outputs back in candle's order
+// (moe_combine_rows_kernel).
 #include "common.cuh"
 #include "moe.h"
 
@@ -21,26 +26,25 @@ namespace {
 
 constexpr int kRouterWarps = 8;
 
-__global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const MoeRouteParams p) {
-    extern __shared__ __align__(16) float xn[];
-    __shared__ float red[kRouterWarps];
-    pdl_wait();
-    pdl_launch_dependents();
+// xn[0, dim) = x / sqrt(sum(x^2) / dim + eps) * w (candle_nn::ops::rms_norm) by the whole CTA
+// (kRouterWarps warps); `red` holds kRouterWarps floats.  Ends with a barrier.
+__device__ __forceinline__ void norm_row(const float* x, const float* w, int dim, float eps, float* xn, float* red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int dim = p.dim;
-    // candle_nn::ops::rms_norm: m = sqrt(sum(x^2) / dim + eps); xn = x / m * w
     float ss = 0.f;
-    for (int i = tid; i < dim; i += blockDim.x) ss = __fmaf_rn(p.x[i], p.x[i], ss);
+    for (int i = tid; i < dim; i += blockDim.x) ss = __fmaf_rn(x[i], x[i], ss);
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
     float tot = 0.f;
-    for (int w = 0; w < kRouterWarps; w++) tot += red[w];
-    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)dim), p.eps));
-    for (int i = tid; i < dim; i += blockDim.x) xn[i] = __fmul_rn(__fdiv_rn(p.x[i], m), p.norm_w[i]);
+    for (int k = 0; k < kRouterWarps; k++) tot += red[k];
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)dim), eps));
+    for (int i = tid; i < dim; i += blockDim.x) xn[i] = __fmul_rn(__fdiv_rn(x[i], m), w[i]);
     __syncthreads();
-    const int e = blockIdx.x * kRouterWarps + warp;
-    if (e >= p.n_expert) return;
+}
+
+// Router logit of expert e (one warp; the result in every lane): dot(router row e, xn).
+__device__ __forceinline__ float router_logit(const MoeRouteParams& p, int e, const float* xn, int lane) {
+    const int dim = p.dim;
     float acc = 0.f;
     if (p.router_f16) {
         const __half* row = static_cast<const __half*>(p.router) + (size_t)e * dim;
@@ -66,7 +70,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const Moe
         }
     }
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) p.logits[e] = acc;
+    return acc;
 }
 
 // (value, index) of the better of two routing weights: larger weight, then lower index.
@@ -74,35 +78,39 @@ __device__ __forceinline__ bool route_better(float v, int i, float bv, int bi) {
     return i >= 0 && (bi < 0 || v > bv || (v == bv && i < bi));
 }
 
-__global__ void __launch_bounds__(32) moe_select_kernel(const MoeRouteParams p) {
-    __shared__ float rw[kMoeMaxExperts];
-    __shared__ unsigned char taken[kMoeMaxExperts];
-    __shared__ int order[kMoeMaxUsed];
-    pdl_wait();
-    pdl_launch_dependents();
-    const int lane = threadIdx.x, E = p.n_expert, K = p.n_used;
-    // softmax_last_dim: max, exp(l - max), the sum in index order, then each divided by it
+struct SelectScratch {
+    float rw[kMoeMaxExperts];
+    unsigned char taken[kMoeMaxExperts];
+    int order[kMoeMaxUsed];
+};
+
+// One warp: softmax over logits[0, E) (max, exp(l - max), the sum in index order, each divided
+// by it), the K largest (stable descending order: ties to the lower index), their weights
+// divided by the sum of the chosen ones in that order; sel / w written in ascending expert
+// order.  `logits` is global memory written by the previous kernel (read after its wait) or
+// shared memory: plain loads.
+__device__ __forceinline__ void select_topk(const float* logits, int E, int K, int* sel, float* w, SelectScratch& s) {
+    const int lane = threadIdx.x & 31;
     float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, __ldcg(p.logits + e));
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, logits[e]);
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     for (int e = lane; e < E; e += 32) {
-        rw[e] = expf(__fsub_rn(__ldcg(p.logits + e), mx));
-        taken[e] = 0;
+        s.rw[e] = expf(__fsub_rn(logits[e], mx));
+        s.taken[e] = 0;
     }
     __syncwarp();
     float sum = 0.f;
     if (lane == 0)
-        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, rw[e]);
+        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, s.rw[e]);
     sum = __shfl_sync(0xffffffffu, sum, 0);
-    for (int e = lane; e < E; e += 32) rw[e] = __fdiv_rn(rw[e], sum);
+    for (int e = lane; e < E; e += 32) s.rw[e] = __fdiv_rn(s.rw[e], sum);
     __syncwarp();
-    // the K largest, one per round (stable descending order: ties to the lower index)
     for (int k = 0; k < K; k++) {
         float bv = -INFINITY;
         int bi = -1;
         for (int e = lane; e < E; e += 32)
-            if (!taken[e] && route_better(rw[e], e, bv, bi)) {
-                bv = rw[e];
+            if (!s.taken[e] && route_better(s.rw[e], e, bv, bi)) {
+                bv = s.rw[e];
                 bi = e;
             }
         for (int o = 16; o; o >>= 1) {
@@ -114,18 +122,17 @@ __global__ void __launch_bounds__(32) moe_select_kernel(const MoeRouteParams p) 
             }
         }
         if (lane == 0) {
-            order[k] = bi;
-            taken[bi] = 1;
+            s.order[k] = bi;
+            s.taken[bi] = 1;
         }
         __syncwarp();
     }
     if (lane == 0) {
-        float s = 0.f;  // the selected weights' sum in selection order
-        for (int k = 0; k < K; k++) s = __fadd_rn(s, rw[order[k]]);
-        // ascending expert order (the order candle accumulates the experts in)
+        float tot = 0.f;  // the selected weights' sum in selection order
+        for (int k = 0; k < K; k++) tot = __fadd_rn(tot, s.rw[s.order[k]]);
         int ids[kMoeMaxUsed];
-        for (int k = 0; k < K; k++) {
-            int v = order[k], j = k;
+        for (int k = 0; k < K; k++) {  // ascending expert order
+            int v = s.order[k], j = k;
             while (j > 0 && ids[j - 1] > v) {
                 ids[j] = ids[j - 1];
                 j--;
@@ -133,9 +140,72 @@ __global__ void __launch_bounds__(32) moe_select_kernel(const MoeRouteParams p) 
             ids[j] = v;
         }
         for (int k = 0; k < K; k++) {
-            p.sel[k] = ids[k];
-            p.w[k] = __fdiv_rn(rw[ids[k]], s);
+            sel[k] = ids[k];
+            w[k] = __fdiv_rn(s.rw[ids[k]], tot);
         }
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const MoeRouteParams p) {
+    extern __shared__ __align__(16) float xn[];
+    __shared__ float red[kRouterWarps];
+    pdl_wait();
+    pdl_launch_dependents();
+    norm_row(p.x, p.norm_w, p.dim, p.eps, xn, red);
+    const int lane = threadIdx.x & 31, e = blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
+    if (e >= p.n_expert) return;
+    const float v = router_logit(p, e, xn, lane);
+    if (lane == 0) p.logits[e] = v;
+}
+
+__global__ void __launch_bounds__(32) moe_select_kernel(const MoeRouteParams p) {
+    __shared__ SelectScratch s;
+    pdl_wait();
+    pdl_launch_dependents();
+    select_topk(p.logits, p.n_expert, p.n_used, p.sel, p.w, s);
+}
+
+// Every token of a prefill chunk: x, sel and w are [T] rows of dim, n_used and n_used.
+__global__ void __launch_bounds__(kRouterWarps * 32) moe_route_rows_kernel(const MoeRouteParams p) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float red[kRouterWarps];
+    __shared__ SelectScratch s;
+    float* xn = sm;
+    float* lg = sm + p.dim;
+    const size_t t = blockIdx.x;
+    norm_row(p.x + t * p.dim, p.norm_w, p.dim, p.eps, xn, red);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int e = warp; e < p.n_expert; e += kRouterWarps) {
+        const float v = router_logit(p, e, xn, lane);
+        if (lane == 0) lg[e] = v;
+    }
+    __syncthreads();
+    if (warp == 0) select_topk(lg, p.n_expert, p.n_used, p.sel + t * p.n_used, p.w + t * p.n_used, s);
+}
+
+// dst[r][0, dim) = src[idx[r]][0, dim) (fp16 rows, dim a multiple of 8); one CTA per row.
+__global__ void __launch_bounds__(128) gather_rows_f16_kernel(const __half* src, const int* idx, int dim, __half* dst) {
+    const size_t r = blockIdx.x;
+    const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)idx[r] * dim);
+    uint4* d = reinterpret_cast<uint4*>(dst + r * dim);
+    for (int i = threadIdx.x; i < dim / 8; i += blockDim.x) d[i] = s[i];
+}
+
+// x[t] = ys + x[t] with ys = the token's chosen experts' rows y[row_of[t][k]] times w[t][k],
+// added in ascending expert order from zero, then the shared expert's row (candle
+// MlpOrMoe::MoE's index_add order, as the decode path's down GEMVs add them).
+__global__ void __launch_bounds__(256) moe_combine_rows_kernel(float* x, const float* y, const int* row_of,
+                                                              const float* w, int K, const float* shared_y, int dim) {
+    const size_t t = blockIdx.x;
+    for (int j = threadIdx.x; j < dim; j += blockDim.x) {
+        float ys = 0.f;
+        for (int k = 0; k < K; k++) {
+            const float a = __fmul_rn(y[(size_t)row_of[t * K + k] * dim + j], w[t * K + k]);
+            ys = k == 0 ? a : __fadd_rn(ys, a);
+        }
+        if (shared_y) ys = __fadd_rn(ys, shared_y[t * dim + j]);
+        x[t * dim + j] = __fadd_rn(ys, x[t * dim + j]);
     }
 }
 
@@ -152,12 +222,15 @@ cudaLaunchConfig_t route_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st
     return cfg;
 }
 
+bool route_params_ok(const MoeRouteParams& p) {
+    return p.n_expert >= 2 && p.n_expert <= kMoeMaxExperts && p.n_used >= 1 && p.n_used <= kMoeMaxUsed &&
+           p.n_used <= p.n_expert && p.dim % 128 == 0 && p.dim <= kMoeMaxDim;
+}
+
 }  // namespace
 
 cudaError_t launch_moe_route(const MoeRouteParams& p, cudaStream_t st, bool pdl) {
-    if (p.n_expert < 2 || p.n_expert > kMoeMaxExperts || p.n_used < 1 || p.n_used > kMoeMaxUsed ||
-        p.n_used > p.n_expert || p.dim % 128 || p.dim > kMoeMaxDim)
-        return cudaErrorInvalidValue;
+    if (!route_params_ok(p)) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = route_cfg(dim3((p.n_expert + kRouterWarps - 1) / kRouterWarps), dim3(kRouterWarps * 32),
                                        (size_t)p.dim * 4, st, pdl, attr);
@@ -167,8 +240,30 @@ cudaError_t launch_moe_route(const MoeRouteParams& p, cudaStream_t st, bool pdl)
     return cudaLaunchKernelEx(&cfg, moe_select_kernel, p);
 }
 
+cudaError_t launch_moe_route_rows(const MoeRouteParams& p, int T, cudaStream_t st) {
+    if (!route_params_ok(p) || T < 1) return cudaErrorInvalidValue;
+    moe_route_rows_kernel<<<T, kRouterWarps * 32, (size_t)(p.dim + p.n_expert) * 4, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows_f16(const __half* src, const int* idx, int rows, int dim, __half* dst, cudaStream_t st) {
+    if (rows < 1 || dim % 8) return rows == 0 ? cudaSuccess : cudaErrorInvalidValue;
+    gather_rows_f16_kernel<<<rows, 128, 0, st>>>(src, idx, dim, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine_rows(float* x, const float* y, const int* row_of, const float* w, int K,
+                                    const float* shared_y, int T, int dim, cudaStream_t st) {
+    if (T < 1) return cudaSuccess;
+    moe_combine_rows_kernel<<<T, 256, 0, st>>>(x, y, row_of, w, K, shared_y, dim);
+    return cudaGetLastError();
+}
+
 cudaError_t moe_init_device() {
-    return cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMoeMaxDim * 4);
+    cudaError_t e = cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMoeMaxDim * 4);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(moe_route_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (kMoeMaxDim + kMoeMaxExperts) * 4);
 }
 
 }  // namespace tptc

@@ -25,6 +25,14 @@ struct MoeRouteParams {
 // Router logits and the top-n_used selection: two launches (a grid over the experts, then
 // one warp), both after the previous kernel (programmatic dependent launch when pdl).
 cudaError_t launch_moe_route(const MoeRouteParams& p, cudaStream_t st, bool pdl);
+// Batched prefill: the same routing for T tokens (x, sel and w hold T rows), one launch.
+cudaError_t launch_moe_route_rows(const MoeRouteParams& p, int T, cudaStream_t st);
+// dst[r] = src[idx[r]] for r < rows (fp16 rows of dim elements, dim a multiple of 8).
+cudaError_t launch_gather_rows_f16(const __half* src, const int* idx, int rows, int dim, __half* dst, cudaStream_t st);
+// x[t] = (sum over k of y[row_of[t K + k]] * w[t K + k], in k order, then + shared_y[t]) + x[t]
+// for t < T (f32 rows of dim; shared_y may be null).
+cudaError_t launch_moe_combine_rows(float* x, const float* y, const int* row_of, const float* w, int K,
+                                    const float* shared_y, int T, int dim, cudaStream_t st);
 cudaError_t moe_init_device();
 
 }  // namespace tptc

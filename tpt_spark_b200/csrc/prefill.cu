@@ -16,6 +16,7 @@
 
 #include "engine.h"
 #include "kernels.h"
+#include "moe.h"
 #include "prefill.h"
 #include "quant.cuh"
 #include "tp.h"
@@ -141,8 +142,9 @@ Status Engine::prefill_buffers(int chunk) {
     const int hd = m.head_dim, ffn_l = m.ffn / tp_size_;
     const size_t nq = (size_t)n_heads_l_ * hd, nqkv = nq + 2 * (size_t)n_kv_l_ * hd;
     const size_t T = (size_t)chunk;
+    const size_t eff = (size_t)m.expert_ffn, sffn = (size_t)m.shared_ffn, TK = T * (size_t)m.n_expert_used;
     const size_t w_elems = std::max({nqkv * m.dim, (size_t)2 * ffn_l * m.dim, (size_t)m.dim * ffn_l,
-                                     (size_t)m.dim * nq});
+                                     (size_t)m.dim * nq, 2 * eff * m.dim, 2 * sffn * m.dim});
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -155,6 +157,12 @@ Status Engine::prefill_buffers(int chunk) {
     // row-parallel partial sums under tensor parallelism (the decode step's own partial
     // buffer is baked into its graph and is not resized here)
     const size_t o_part = tp_ ? take(T * m.dim * 4) : 0;
+    const bool moe = m.n_expert > 0;
+    const size_t o_rsel = moe ? take(TK * 4) : 0, o_rw = moe ? take(TK * 4) : 0;
+    const size_t o_gidx = moe ? take(TK * 4) : 0, o_rowof = moe ? take(TK * 4) : 0;
+    const size_t o_ga = moe ? take(TK * m.dim * 2) : 0, o_gh = moe ? take(TK * eff * 2) : 0;
+    const size_t o_gy = moe ? take(TK * m.dim * 4) : 0;
+    const size_t o_shh = sffn ? take(T * sffn * 2) : 0, o_shy = sffn ? take(T * m.dim * 4) : 0;
     if (pf_) {
         TPTC_CUDA_RET(cudaStreamSynchronize(stream_));
         cudaFree(pf_);
@@ -179,6 +187,15 @@ Status Engine::prefill_buffers(int chunk) {
     pf_h_ = reinterpret_cast<__half*>(pf_ + o_h);
     pf_w_ = reinterpret_cast<__half*>(pf_ + o_w);
     pf_part_ = tp_ ? reinterpret_cast<float*>(pf_ + o_part) : nullptr;
+    pf_rsel_ = moe ? reinterpret_cast<int*>(pf_ + o_rsel) : nullptr;
+    pf_rw_ = moe ? reinterpret_cast<float*>(pf_ + o_rw) : nullptr;
+    pf_gidx_ = moe ? reinterpret_cast<int*>(pf_ + o_gidx) : nullptr;
+    pf_rowof_ = moe ? reinterpret_cast<int*>(pf_ + o_rowof) : nullptr;
+    pf_ga_ = moe ? reinterpret_cast<__half*>(pf_ + o_ga) : nullptr;
+    pf_gh_ = moe ? reinterpret_cast<__half*>(pf_ + o_gh) : nullptr;
+    pf_gy_ = moe ? reinterpret_cast<float*>(pf_ + o_gy) : nullptr;
+    pf_sh_h_ = sffn ? reinterpret_cast<__half*>(pf_ + o_shh) : nullptr;
+    pf_sh_y_ = sffn ? reinterpret_cast<float*>(pf_ + o_shy) : nullptr;
     return {};
 }
 
@@ -194,12 +211,12 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
     // (TPTC_FUSED_ALWAYS); otherwise it is expanded to fp16 in pf_w_ first (one pass over the
     // matrix) and contracted by gemm_tc.  A gate|up matrix is used in its physical row order
     // (4 gate rows, then the 4 matching up rows), which the GLU epilogue expects.
-    auto fused = [&](const DevMatrix& w) {
+    auto fused = [&](const DevMatrix& w, int M) {
         if (prefill_fused_ == TPTC_FUSED_NEVER || !gemm_q_supported(w)) return false;
-        return prefill_fused_ == TPTC_FUSED_ALWAYS || gemm_q_preferred(w, T, w.N, sm_count_);
+        return prefill_fused_ == TPTC_FUSED_ALWAYS || gemm_q_preferred(w, M, w.N, sm_count_);
     };
     auto matmul = [&](int epi, const __half* a, const DevMatrix& w, const GemmTcParams& g) -> cudaError_t {
-        if (fused(w)) return gemm_q(epi, a, g.K, w, g, st, false);
+        if (fused(w, g.M)) return gemm_q(epi, a, g.K, w, g, st, false);
         cudaError_t e = launch_dequant_rows_f16(w, 0, g.N, pf_w_, st, w.glu != 0);
         return e != cudaSuccess ? e : gemm_tc(epi, a, g.K, pf_w_, g.K, g, st, false);
     };
@@ -219,7 +236,7 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         g.c = pf_qkv_;
         g.ldc = nqkv;
         g.err = err_;
-        if (fused(L.q) && fused(L.k) && fused(L.v)) {  // three GEMMs into the column ranges
+        if (fused(L.q, T) && fused(L.k, T) && fused(L.v, T)) {  // three GEMMs into the column ranges
             GemmTcParams gq = g;
             gq.N = nq;
             TPTC_CUDA_RET(gemm_q(GEMM_STORE, pf_xn_, dim, L.q, gq, st, false));
@@ -266,6 +283,89 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
         // feed-forward block: gate|up in the device tile order, silu(gate) * up in the epilogue
         rmsnorm_f16_kernel<<<T, 256, 0, st>>>(pf_x_, L.ffn_norm, dim, m.rms_eps, pf_xn_);
         TPTC_CUDA_RET(cudaGetLastError());
+        if (L.moe) {
+            // Mixture of experts: every token routed on the device (the decode path's routing);
+            // the choices come to the host once per layer to group the chosen (token, expert)
+            // rows by expert; each expert's rows then go through the same GEMMs as a dense
+            // layer, and the combine kernel adds the outputs back in candle's order.
+            const int E = m.n_expert, K = m.n_expert_used, eff = m.expert_ffn, TK = T * K;
+            MoeRouteParams r = {};
+            r.x = pf_x_;
+            r.norm_w = L.ffn_norm;
+            r.eps = m.rms_eps;
+            r.router = L.router;
+            r.router_f16 = L.router_type == TPTC_TYPE_F16 ? 1 : 0;
+            r.dim = dim;
+            r.n_expert = E;
+            r.n_used = K;
+            r.sel = pf_rsel_;
+            r.w = pf_rw_;
+            TPTC_CUDA_RET(launch_moe_route_rows(r, T, st));
+            std::vector<int> sel((size_t)TK), cnt(E, 0), off(E + 1, 0), gidx((size_t)TK), rowof((size_t)TK);
+            TPTC_CUDA_RET(cudaMemcpyAsync(sel.data(), pf_rsel_, (size_t)TK * 4, cudaMemcpyDeviceToHost, st));
+            TPTC_CUDA_RET(cudaStreamSynchronize(st));
+            for (int i = 0; i < TK; i++) {
+                if (sel[i] < 0 || sel[i] >= E) return Status{TPTC_ERR_CUDA, "expert routing out of range"};
+                cnt[sel[i]]++;
+            }
+            for (int e = 0; e < E; e++) off[e + 1] = off[e] + cnt[e];
+            std::vector<int> fill(off.begin(), off.end() - 1);
+            for (int t = 0; t < T; t++)
+                for (int k = 0; k < K; k++) {
+                    const int row = fill[sel[(size_t)t * K + k]]++;
+                    gidx[row] = t;
+                    rowof[(size_t)t * K + k] = row;
+                }
+            TPTC_CUDA_RET(cudaMemcpyAsync(pf_gidx_, gidx.data(), (size_t)TK * 4, cudaMemcpyHostToDevice, st));
+            TPTC_CUDA_RET(cudaMemcpyAsync(pf_rowof_, rowof.data(), (size_t)TK * 4, cudaMemcpyHostToDevice, st));
+            TPTC_CUDA_RET(launch_gather_rows_f16(pf_xn_, pf_gidx_, TK, dim, pf_ga_, st));
+            for (int e = 0; e < E; e++) {
+                if (!cnt[e]) continue;
+                DevMatrix wg = L.eglu, wd = L.edown;
+                wg.main += (int64_t)e * L.eglu_stride;
+                wd.main += (int64_t)e * L.edown_stride;
+                GemmTcParams ge = {};
+                ge.M = cnt[e];
+                ge.N = 2 * eff;
+                ge.K = dim;
+                ge.h = pf_gh_ + (size_t)off[e] * eff;
+                ge.ldh = eff;
+                ge.err = err_;
+                ge.geglu = m.geglu ? 1 : 0;
+                TPTC_CUDA_RET(matmul(GEMM_GLU, pf_ga_ + (size_t)off[e] * dim, wg, ge));
+                GemmTcParams gd = {};
+                gd.M = cnt[e];
+                gd.N = dim;
+                gd.K = eff;
+                gd.c = pf_gy_ + (size_t)off[e] * dim;
+                gd.ldc = dim;
+                gd.err = err_;
+                TPTC_CUDA_RET(matmul(GEMM_STORE, pf_gh_ + (size_t)off[e] * eff, wd, gd));
+            }
+            if (L.shexp) {  // the shared expert on every token
+                const int sffn = m.shared_ffn;
+                GemmTcParams gs = {};
+                gs.M = T;
+                gs.N = 2 * sffn;
+                gs.K = dim;
+                gs.h = pf_sh_h_;
+                gs.ldh = sffn;
+                gs.err = err_;
+                gs.geglu = m.geglu ? 1 : 0;
+                TPTC_CUDA_RET(matmul(GEMM_GLU, pf_xn_, L.glu, gs));
+                GemmTcParams gd = {};
+                gd.M = T;
+                gd.N = dim;
+                gd.K = sffn;
+                gd.c = pf_sh_y_;
+                gd.ldc = dim;
+                gd.err = err_;
+                TPTC_CUDA_RET(matmul(GEMM_STORE, pf_sh_h_, L.down, gd));
+            }
+            TPTC_CUDA_RET(launch_moe_combine_rows(pf_x_, pf_gy_, pf_rowof_, pf_rw_, K, L.shexp ? pf_sh_y_ : nullptr,
+                                                  T, dim, st));
+            continue;
+        }
         GemmTcParams gg = {};
         gg.M = T;
         gg.N = 2 * ffn_l;
@@ -291,9 +391,7 @@ Status Engine::enqueue_prefill_chunk(int T, int start) {
 }
 
 bool Engine::prefill_uses_gemm(int n) const {
-    // mixture-of-experts models prefill position by position through the decode graph (the
-    // experts are chosen per token on the device)
-    if (kv_f32_ || prefill_gemm_min_ <= 0 || n < prefill_gemm_min_ || meta_.n_expert > 0) return false;
+    if (kv_f32_ || prefill_gemm_min_ <= 0 || n < prefill_gemm_min_) return false;
     const ModelMeta& m = meta_;
     const int ffn_l = m.ffn / tp_size_;
     // GEMM operands: K a multiple of 64, the gate|up tile order whole 8-row groups
