@@ -147,16 +147,62 @@ __device__ __forceinline__ void select_topk(const float* logits, int E, int K, i
     __syncwarp();
 }
 
+// Four consecutive router weights of row `row` from element i, as f32.
+__device__ __forceinline__ float4 router_quad(const MoeRouteParams& p, int row, int i) {
+    if (p.router_f16) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p.router) + (size_t)row * p.dim + i);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(p.router) + (size_t)row * p.dim + i);
+}
+
+// One CTA per expert: the expert's router row is loaded into registers before the wait for
+// the previous kernel (weights do not depend on it), the CTA normalises x after it, and its
+// threads split the dot product (a fixed-order block reduction).
+constexpr int kRouterPre = 4;  // float4 quads of the row each thread holds (dim <= 4096 in registers)
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const MoeRouteParams p) {
     extern __shared__ __align__(16) float xn[];
     __shared__ float red[kRouterWarps];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, e = blockIdx.x, nt = blockDim.x;
+    float4 wq[kRouterPre];
+#pragma unroll
+    for (int j = 0; j < kRouterPre; j++) {
+        const int i = (j * nt + tid) * 4;
+        wq[j] = i < p.dim ? router_quad(p, e, i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     pdl_wait();
     pdl_launch_dependents();
     norm_row(p.x, p.norm_w, p.dim, p.eps, xn, red);
-    const int lane = threadIdx.x & 31, e = blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
-    if (e >= p.n_expert) return;
-    const float v = router_logit(p, e, xn, lane);
-    if (lane == 0) p.logits[e] = v;
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRouterPre; j++) {
+        const int i = (j * nt + tid) * 4;
+        if (i < p.dim) {
+            const float4 v = *reinterpret_cast<const float4*>(xn + i);
+            acc = __fmaf_rn(wq[j].x, v.x, acc);
+            acc = __fmaf_rn(wq[j].y, v.y, acc);
+            acc = __fmaf_rn(wq[j].z, v.z, acc);
+            acc = __fmaf_rn(wq[j].w, v.w, acc);
+        }
+    }
+    for (int i = (kRouterPre * nt + tid) * 4; i < p.dim; i += nt * 4) {  // rows beyond dim 4096
+        const float4 w4 = router_quad(p, e, i), v = *reinterpret_cast<const float4*>(xn + i);
+        acc = __fmaf_rn(w4.x, v.x, acc);
+        acc = __fmaf_rn(w4.y, v.y, acc);
+        acc = __fmaf_rn(w4.z, v.z, acc);
+        acc = __fmaf_rn(w4.w, v.w, acc);
+    }
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    __syncthreads();  // red is free again (norm_row's readers are past its last barrier)
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (tid == 0) {
+        float tot = 0.f;
+        for (int k = 0; k < kRouterWarps; k++) tot += red[k];
+        p.logits[e] = tot;
+    }
 }
 
 __global__ void __launch_bounds__(32) moe_select_kernel(const MoeRouteParams p) {
@@ -232,8 +278,7 @@ bool route_params_ok(const MoeRouteParams& p) {
 cudaError_t launch_moe_route(const MoeRouteParams& p, cudaStream_t st, bool pdl) {
     if (!route_params_ok(p)) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = route_cfg(dim3((p.n_expert + kRouterWarps - 1) / kRouterWarps), dim3(kRouterWarps * 32),
-                                       (size_t)p.dim * 4, st, pdl, attr);
+    cudaLaunchConfig_t cfg = route_cfg(dim3(p.n_expert), dim3(kRouterWarps * 32), (size_t)p.dim * 4, st, pdl, attr);
     cudaError_t e = cudaLaunchKernelEx(&cfg, moe_router_kernel, p);
     if (e != cudaSuccess) return e;
     cfg = route_cfg(dim3(1), dim3(32), 0, st, pdl, attr);
