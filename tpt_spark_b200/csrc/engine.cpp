@@ -541,7 +541,7 @@ Status Engine::alloc_runtime() {
                                      (size_t)m.n_expert_used * m.expert_ffn + (size_t)m.shared_ffn);
     const size_t o_h = take(h_floats * 4), o_lg = take((size_t)m.vocab * 4);
     const size_t o_mlg = take((size_t)std::max(1, m.n_expert) * 4), o_msel = take((size_t)kMoeMaxUsed * 4);
-    const size_t o_mw = take((size_t)kMoeMaxUsed * 4), o_macc = take((size_t)m.dim * 4);
+    const size_t o_mw = take((size_t)kMoeMaxUsed * 4), o_macc = take((size_t)m.dim * 4), o_mcnt = take(64);
     const size_t o_ti = take(64), o_to = take(64), o_pos = take(64), o_err = take(64), o_step = take(64);
     const size_t o_hist = take((size_t)max_seq_ * 4 + 64);
     const size_t o_part = take(attn_decode_partial_floats(n_heads_l_, n_kv_l_, hd, attn_splits_) * 4);
@@ -575,6 +575,7 @@ Status Engine::alloc_runtime() {
     moe_sel_ = reinterpret_cast<int*>(rt_ + o_msel);
     moe_w_ = reinterpret_cast<float*>(rt_ + o_mw);
     moe_acc_ = reinterpret_cast<float*>(rt_ + o_macc);
+    moe_count_ = reinterpret_cast<int*>(rt_ + o_mcnt);
     logits_ = reinterpret_cast<float*>(rt_ + o_lg);
     tok_in_ = reinterpret_cast<uint32_t*>(rt_ + o_ti);
     tok_out_ = reinterpret_cast<uint32_t*>(rt_ + o_to);
@@ -714,6 +715,7 @@ Status Engine::enqueue_decode(cudaStream_t st, bool chained, float* trace) {
         r.logits = moe_logits_;
         r.sel = moe_sel_;
         r.w = moe_w_;
+        r.count = moe_count_;
         CU(launch_moe_route(r, st, pdl_));
         bool act_ready = false;
         for (int k0 = 0; k0 < K; k0 += kGemvMaxSeg) {

@@ -177,6 +177,7 @@ class Engine {
     int* moe_sel_ = nullptr;       // [n_expert_used] selected experts, ascending
     float* moe_w_ = nullptr;       // [n_expert_used] their routing weights
     float* moe_acc_ = nullptr;     // [dim] weighted sum of the experts' outputs
+    int* moe_count_ = nullptr;     // routing kernel's ticket (kept at zero between launches)
     float* logits_ = nullptr;   // [vocab]
     uint32_t* tok_in_ = nullptr;
     uint32_t* tok_out_ = nullptr;

@@ -12,8 +12,9 @@
 //   moe_router_kernel  RMSNorm of the residual stream with the ffn_norm gain, then one warp
 //                      per expert: logit[e] = dot(router row e, xn) in f32 (F32 or F16 rows,
 //                      which candle dequantises to f32 and multiplies in f32)
-//   moe_select_kernel  one warp: softmax, top n_used, renormalised weights, written in
-//                      ascending expert order (sel[k], w[k]) for the expert GEMVs
+//                      the last CTA to finish (a ticket) then, with one warp: softmax,
+//                      top n_used, renormalised weights, written in ascending expert order
+//                      (sel[k], w[k]) for the expert GEMVs
 // The batched prefill routes every token of a chunk in one launch (moe_route_rows_kernel: the
 // same norm, logits and selection per token), gathers each expert's rows
 // (gather_rows_f16_kernel) for the GEMMs, and adds the experts' outputs back in candle's order
@@ -160,11 +161,15 @@ __device__ __forceinline__ float4 router_quad(const MoeRouteParams& p, int row, 
 
 // One CTA per expert: the expert's router row is loaded into registers before the wait for
 // the previous kernel (weights do not depend on it), the CTA normalises x after it, and its
-// threads split the dot product (a fixed-order block reduction).
+// threads split the dot product (a fixed-order block reduction).  The last CTA to write its
+// logit (a ticket on p.count, which it resets) selects the experts with one warp.
 constexpr int kRouterPre = 4;  // float4 quads of the row each thread holds (dim <= 4096 in registers)
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const MoeRouteParams p) {
     extern __shared__ __align__(16) float xn[];
     __shared__ float red[kRouterWarps];
+    __shared__ float lg[kMoeMaxExperts];
+    __shared__ SelectScratch s;
+    __shared__ int last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, e = blockIdx.x, nt = blockDim.x;
     float4 wq[kRouterPre];
 #pragma unroll
@@ -202,14 +207,16 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const Moe
         float tot = 0.f;
         for (int k = 0; k < kRouterWarps; k++) tot += red[k];
         p.logits[e] = tot;
+        __threadfence();  // the logit before the ticket
+        last = atomicAdd(p.count, 1) == p.n_expert - 1;
     }
-}
-
-__global__ void __launch_bounds__(32) moe_select_kernel(const MoeRouteParams p) {
-    __shared__ SelectScratch s;
-    pdl_wait();
-    pdl_launch_dependents();
-    select_topk(p.logits, p.n_expert, p.n_used, p.sel, p.w, s);
+    __syncthreads();
+    if (!last || warp != 0) return;
+    __threadfence();  // every other CTA's logit is visible after its ticket
+    for (int i = lane; i < p.n_expert; i += 32) lg[i] = __ldcg(p.logits + i);
+    __syncwarp();
+    select_topk(lg, p.n_expert, p.n_used, p.sel, p.w, s);
+    if (lane == 0) *p.count = 0;  // for the next launch
 }
 
 // Every token of a prefill chunk: x, sel and w are [T] rows of dim, n_used and n_used.
@@ -278,11 +285,9 @@ bool route_params_ok(const MoeRouteParams& p) {
 cudaError_t launch_moe_route(const MoeRouteParams& p, cudaStream_t st, bool pdl) {
     if (!route_params_ok(p)) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
+    if (!p.count) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = route_cfg(dim3(p.n_expert), dim3(kRouterWarps * 32), (size_t)p.dim * 4, st, pdl, attr);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_router_kernel, p);
-    if (e != cudaSuccess) return e;
-    cfg = route_cfg(dim3(1), dim3(32), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, moe_select_kernel, p);
+    return cudaLaunchKernelEx(&cfg, moe_router_kernel, p);
 }
 
 cudaError_t launch_moe_route_rows(const MoeRouteParams& p, int T, cudaStream_t st) {

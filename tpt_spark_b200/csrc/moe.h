@@ -20,10 +20,11 @@ struct MoeRouteParams {
     float* logits;  // [n_expert] scratch
     int* sel;       // [n_used] out: selected experts, ascending
     float* w;       // [n_used] out: their renormalised routing weights
+    int* count;     // decode: a zeroed counter (the routing kernel leaves it zeroed)
 };
 
-// Router logits and the top-n_used selection: two launches (a grid over the experts, then
-// one warp), both after the previous kernel (programmatic dependent launch when pdl).
+// Router logits and the top-n_used selection in one launch (a CTA per expert; the last one
+// selects), after the previous kernel (programmatic dependent launch when pdl).
 cudaError_t launch_moe_route(const MoeRouteParams& p, cudaStream_t st, bool pdl);
 // Batched prefill: the same routing for T tokens (x, sel and w hold T rows), one launch.
 cudaError_t launch_moe_route_rows(const MoeRouteParams& p, int T, cudaStream_t st);
