@@ -505,7 +505,15 @@ TPTC_API int tptc_sample(const float* d_logits, int vocab, int* d_counts, float 
     s.scratch = d_scratch;
     s.out_tok = d_out_tok;
     s.dbg = reinterpret_cast<unsigned long long*>(d_dbg);
-    cudaError_t e = tptc::launch_sample(s, static_cast<cudaStream_t>(stream), false);
+    // the kernels' work area, stream-ordered (this entry takes only the caller's buffers)
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void* work = nullptr;
+    cudaError_t e = cudaMallocAsync(&work, tptc::kSampleWorkBytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "sample");
+    s.work = static_cast<unsigned char*>(work);
+    e = tptc::launch_sample(s, st, false);
+    const cudaError_t ef = cudaFreeAsync(work, st);
+    if (e == cudaSuccess) e = ef;
     return e == cudaSuccess ? TPTC_OK : cuda_fail(e, "sample");
 }
 

@@ -552,6 +552,7 @@ Status Engine::alloc_runtime() {
     const size_t o_cbar = take((size_t)(L + 1) * kChainMaxPhases * 4);
     const size_t o_bval = take((size_t)2 * sm_count_ * 4), o_bidx = take((size_t)2 * sm_count_ * 4);
     const size_t o_scnt = take((size_t)m.vocab * 4), o_sscr = take((size_t)m.vocab * 4), o_sstep = take(64);
+    const size_t o_swork = take(kSampleWorkBytes);
     rt_size_ = off;
     cudaError_t ce = cudaMalloc(&rt_, rt_size_);
     if (ce != cudaSuccess) {
@@ -591,6 +592,7 @@ Status Engine::alloc_runtime() {
     best_idx_ = reinterpret_cast<int*>(rt_ + o_bidx);
     sample_counts_ = reinterpret_cast<int*>(rt_ + o_scnt);
     sample_scratch_ = reinterpret_cast<float*>(rt_ + o_sscr);
+    sample_work_ = rt_ + o_swork;
     sample_step_ = reinterpret_cast<int*>(rt_ + o_sstep);
 
     // candle quantized_llama precomput_freqs_cis: theta_i = 1/base^(2i/hd) (f32 powf),
@@ -1039,6 +1041,7 @@ Status Engine::enqueue_sample(const tptc_infer_params& p) {
     s.seed = p.seed;
     s.step = sample_step_;
     s.scratch = sample_scratch_;
+    s.work = sample_work_;
     s.out_tok = tok_out_;
     CU(launch_sample(s, stream_, false));
     CU(cudaMemcpyAsync(h_tok_ + 1, tok_out_, 4, cudaMemcpyDeviceToHost, stream_));

@@ -189,6 +189,7 @@ class Engine {
     int* chain_bar_ = nullptr;     // [L + 1][kChainMaxPhases] chain arrival counters
     int* sample_counts_ = nullptr;     // [vocab] context token counts (repeat penalty)
     float* sample_scratch_ = nullptr;  // [vocab]
+    unsigned char* sample_work_ = nullptr;  // kSampleWorkBytes (the sampling kernels' histograms and partials)
     int* sample_step_ = nullptr;       // draws so far in this inference
     float* best_val_ = nullptr;    // [2 * SMs] per-CTA argmax partials of the lm_head chain
     int* best_idx_ = nullptr;

@@ -108,7 +108,10 @@ struct SampleParams {
     int* pos;
     uint32_t* history;
     unsigned long long* dbg;  // optional [3]: cut pattern, kept mass, total mass (2^-40 units)
+    unsigned char* work;      // kSampleWorkBytes of device memory (histograms, per-CTA partials)
 };
+constexpr size_t kSampleWorkBytes = 36 * 1024;
+// Vocabularies up to 262144 tokens (256 CTAs of 1024).
 cudaError_t launch_sample(const SampleParams& p, cudaStream_t st, bool pdl);
 
 cudaError_t kernels_init_device();
