@@ -249,7 +249,8 @@ TPTC_API int tptc_matrix_dequant_f16(const tptc_matrix* m, void* d_out, void* st
 TPTC_API int tptc_block_dots(const tptc_matrix* m, const float* d_x, int32_t* d_isum, int32_t* d_msum,
                              void* stream);
 
-/* The engine's next-token selection on the device (infer's sampling step), as a kernel:
+/* The engine's next-token selection on the device (infer's sampling step), as kernels on
+ * `stream` (their 36 KB work area is allocated and freed stream-ordered for the call):
  * logits[vocab] with the repeat penalty applied once per context occurrence (counts[vocab],
  * candle_engine.rs:87-101; the picked token's count is incremented), then argmax when
  * temperature is below 1e-7 (ties to the highest index), else softmax(x / temperature), the top-p
