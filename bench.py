@@ -247,7 +247,7 @@ def decode_bytes(cfg, kv_len_mean):
             tot += b if cfg.tied else b // ne[1]
         elif kind.endswith("_exps"):  # [E][rows][K]: the chosen experts' slices
             tot += b * cfg.n_expert_used
-        elif cfg.n_expert > 1 and ".ffn_" in name and name.split(".")[2].isdigit():  # ffn_*.E
+        elif cfg.n_expert > 1 and ".ffn_" in name and name.split(".")[3].isdigit():  # blk.N.ffn_*.E.weight
             tot += b * cfg.n_expert_used // cfg.n_expert
         else:
             tot += b

@@ -67,3 +67,63 @@ def test_normal_draw_is_stable():
     b = synth.normal(1234, 500, 1.0, start=500)
     np.testing.assert_array_equal(a[500:], b)
     assert abs(a.mean()) < 0.15 and abs(a.std() - 1) < 0.1
+
+
+def test_moe_models_roundtrip_and_bench_accounting(tiny_models):
+    """The mixture-of-experts writers: expert metadata, stacked ([E][rows][K]) and per-expert
+    tensors and the router read back by gguf-py; bench.py counts the chosen experts' bytes
+    per decode step and their FLOPs per prefilled token, the dense configurations unchanged."""
+    import os
+    import sys
+
+    import gguf
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    for name in ("tiny_mixtral", "tiny_moe"):
+        cfg = synth.TINY[name]
+        r = gguf.GGUFReader(tiny_models[name])
+        t = {x.name: x for x in r.tensors}
+        f = r.fields
+        assert f["llama.expert_count"].parts[-1][0] == cfg.n_expert
+        assert f["llama.expert_used_count"].parts[-1][0] == cfg.n_expert_used
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            if not cfg.is_moe_layer(i):
+                assert p + "ffn_gate.weight" in t and p + "ffn_gate_inp.weight" not in t
+                continue
+            assert list(t[p + "ffn_gate_inp.weight"].shape) == [cfg.dim, cfg.n_expert]
+            assert int(t[p + "ffn_gate_inp.weight"].tensor_type) == cfg.router_type
+            if cfg.stacked_experts:
+                assert list(t[p + "ffn_down_exps.weight"].shape) == [cfg.expert_ffn, cfg.dim, cfg.n_expert]
+            else:
+                assert list(t[p + f"ffn_up.{cfg.n_expert - 1}.weight"].shape) == [cfg.dim, cfg.expert_ffn]
+            assert (p + "ffn_gate_shexp.weight" in t) == bool(cfg.shared_ffn)
+
+    # decode bytes: one of each dense tensor, the router and n_used of n_expert experts
+    def layer_bytes(cfg, i):
+        tb = synth.type_bytes
+        d, ef = cfg.dim, cfg.expert_ffn
+        router = tb(cfg.type_of("ffn_gate_inp"), d * cfg.n_expert)
+        experts = cfg.n_expert_used * (2 * tb(cfg.type_of("ffn_gate"), d * ef) + tb(cfg.type_of("ffn_down"), d * ef))
+        return router + experts
+
+    for name in ("tiny_mixtral", "tiny_moe"):
+        cfg = synth.TINY[name]
+        dense = __import__("dataclasses").replace(cfg, n_expert=0, n_expert_used=0, expert_ffn=0, moe_layers=None,
+                                                   shared_ffn=0)
+        moe_part = sum(layer_bytes(cfg, i) for i in range(cfg.n_layers) if cfg.is_moe_layer(i))
+        dense_ffn = sum(2 * synth.type_bytes(dense.type_of("ffn_gate"), cfg.dim * cfg.ffn)
+                        + synth.type_bytes(dense.type_of("ffn_down"), cfg.dim * cfg.ffn)
+                        for i in range(cfg.n_layers) if cfg.is_moe_layer(i))
+        shared = sum(2 * synth.type_bytes(cfg.type_of("ffn_gate"), cfg.dim * cfg.shared_ffn)
+                     + synth.type_bytes(cfg.type_of("ffn_down"), cfg.dim * cfg.shared_ffn)
+                     for i in range(cfg.n_layers) if cfg.is_moe_layer(i))
+        assert bench.decode_bytes(cfg, 100) == bench.decode_bytes(dense, 100) - dense_ffn + moe_part + shared
+    # prefill FLOPs: per token 2 * 3 * dim * expert_ffn per chosen expert (+ router, shared)
+    w = synth.WORKLOADS["mixtral8x7b_l4_q4km"]
+    dense = __import__("dataclasses").replace(w, n_expert=0, n_expert_used=0, expert_ffn=0)
+    moe_minus_dense = 2.0 * 512 * w.n_layers * (3 * w.dim * w.expert_ffn * (w.n_expert_used - 1) + w.dim * w.n_expert)
+    assert bench.prefill_flops(w, 512) == bench.prefill_flops(dense, 512) + moe_minus_dense
+    assert bench.decode_bytes(synth.CONFIGS["c5_llama8b_q4km"], 8704.5) == 6017837312
